@@ -1,0 +1,353 @@
+"""Benchmark of the B200 VNN hot path on BASELINE config 0 (62x62 ALU train step).
+
+``python bench.py --gpus N --steps K --warmup W [--impl b200|reference]``
+
+* ``--impl b200`` (default): every rank trains the ALU chip (K=23x13, M=16, d=4,
+  continuous Codd, MSE, SGD lr=1e-2) on its own 128-sample batches; gradients are
+  all-reduced with NCCL (data parallel, weak scaling: global batch = 128*N).  Prints ONE
+  JSON line on rank 0: device-resident throughput (``value``), the end-to-end figure through
+  the public ``VNNTrainStep`` API with pinned host batches (``e2e``), the fused-kernel
+  roofline against a live-measured FP32 FFMA peak, the clocks seen during the timed region
+  and a CPU baseline (the torch-CPU port of the same algorithm, rank 0, N=1 only).
+* ``--impl reference``: the reference's JAX path cannot be installed here, so rank 0 times
+  the CPU port of the reference algorithm (``oracle/torch_port.py``, float32, all host
+  threads) on the same workload; other ranks exit.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "neurocell-v2_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+BATCH = 128
+SEED = 0            # config index 0 -> seeds 0 (params), 1 (filters), 2 (inputs)
+LR = 1e-2
+WORKLOAD = "BASELINE config 0: 62x62 ALU VNN train step (fwd+bwd+SGD)"
+
+
+def alu_flops_per_sample(train: bool = True) -> float:
+    """Effective direct-convolution FLOPs per sample: 2*M*P*K per pass; a train step makes
+    d forward passes, d filter-gradient passes and d-1 field-adjoint passes."""
+    M, P, K, d = 16, 40 * 50, 23 * 13, 4
+    per_pass = 2.0 * M * P * K
+    return per_pass * ((3 * d - 1) if train else d)
+
+
+# ---------------------------------------------------------------------------------------
+def make_problem(rank: int, n_batches: int, batch: int):
+    from oracle import vnn_oracle as O   # seeded synthetic ALU data (datasets.py:77-130)
+    rng_p = np.random.default_rng(SEED * 1000 + 0)
+    rng_f = np.random.default_rng(SEED * 1000 + 1)
+    rng_x = np.random.default_rng([SEED * 1000 + 2, rank])
+    cell = rng_p.normal(0, 0.1, (3, 62, 62)).astype(np.float32)
+    filt = (rng_f.normal(0, 1, (16, 1, 23, 13)) / np.sqrt(23 * 13)).astype(np.float32)
+    xs, ys = [], []
+    for _ in range(n_batches):
+        x, y, _ = O.alu_batch(rng_x, batch, noise=0.0)
+        xs.append(x)
+        ys.append(y)
+    return cell, filt, np.stack(xs), np.stack(ys)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.rows = []
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(gpu_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def fp32_peak_tflops(device) -> float:
+    """Live FP32 FFMA peak of this GPU (best of 3 probe launches, CUDA events)."""
+    import ctypes
+    from neurocell_b200 import _lib
+    lib = _lib.load()
+    sink = torch.zeros(1, device=device)
+    flops = ctypes.c_double(0)
+    st = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    best = 0.0
+    for it in (2000, 20000, 20000, 20000):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        _lib.check(lib.nc_fp32_peak_probe(it, ctypes.byref(flops), ctypes.c_void_p(sink.data_ptr()), st),
+                   "nc_fp32_peak_probe")
+        e1.record()
+        torch.cuda.synchronize()
+        if it == 20000:
+            best = max(best, flops.value / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+    return best
+
+
+def cpu_baseline(steps_budget_s: float = 12.0) -> dict:
+    """The torch-CPU port of the reference algorithm (float32, all host threads), timed on a
+    bounded sample: full 128-sample train steps until the time budget is spent."""
+    from oracle import torch_port as T
+    from oracle import vnn_oracle as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cell, filt, xs, ys = make_problem(0, 1, BATCH)
+    g = O.alu_geometry()
+    x, y = xs[0], ys[0]
+    ports = [x[:, 0], x[:, 1], x[:, 2]]
+    for _ in range(2):
+        T.value_and_grad(g, O.Config(), cell, filt, ports, y, dtype=torch.float32)
+    times = []
+    t_end = time.perf_counter() + steps_budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        T.value_and_grad(g, O.Config(), cell, filt, ports, y, dtype=torch.float32)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": BATCH / med, "unit": "samples/s", "cores": threads, "kind": "port",
+            "ms_per_step": med * 1e3,
+            "sample": f"{len(times)} full B={BATCH} train steps (fwd+autograd bwd, float32) of "
+                      f"oracle/torch_port.py on {threads} host threads, median"}
+
+
+# ---------------------------------------------------------------------------------------
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import torch_port as T
+    from oracle import vnn_oracle as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cell, filt, xs, ys = make_problem(0, 1, BATCH)
+    g = O.alu_geometry()
+    ports = [xs[0][:, 0], xs[0][:, 1], xs[0][:, 2]]
+    for _ in range(args.warmup):
+        T.value_and_grad(g, O.Config(), cell, filt, ports, ys[0], dtype=torch.float32)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        T.value_and_grad(g, O.Config(), cell, filt, ports, ys[0], dtype=torch.float32)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(times)
+    val = BATCH / (ms * 1e-3)
+    line = {
+        "impl": "reference", "metric": "train samples/s (62x62 ALU VNN, B=128)", "value": val,
+        "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded numpy ALU batches)",
+        "config": {"workload": WORKLOAD, "per_gpu_batch": BATCH, "global_batch": BATCH,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "samples/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} full B={BATCH} train steps of oracle/torch_port.py "
+                                   "(the reference's JAX CPU path is not installable here)"},
+        "e2e": {"value": val, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args) -> None:
+    import ctypes
+    import torch.distributed as dist
+    import neurocell_b200 as nc
+    from neurocell_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+        pg = dist.group.WORLD
+    lib = _lib.load()
+
+    nb = 8
+    cell, filt, xs, ys = make_problem(rank, nb, BATCH)
+    topo = nc.ChipTopology2D.alu_chip()
+    params = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
+    runner = nc.trainer.VNNTrainStep(topo, params, BATCH, lr=LR, in_shapes=((8, 1),) * 3,
+                                     process_group=pg)
+    x_dev = torch.tensor(xs.reshape(nb, BATCH, -1), device=dev)
+    y_dev = torch.tensor(ys, device=dev)
+    if world == 1 and not args.no_graph:
+        runner.load_batch(x_dev[0], y_dev[0])
+        runner.capture()
+    l2_flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if pg is not None:
+            dist.barrier()
+
+    # ---- warm-up
+    for i in range(args.warmup):
+        runner.step(x_dev[i % nb], y_dev[i % nb])
+    torch.cuda.synchronize()
+
+    # ---- timed region: device-resident batches, L2 flushed before every step
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    kev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        runner.load_batch(x_dev[i % nb], y_dev[i % nb])
+        l2_flush.fill_(float(i))
+        if runner.graph is None:
+            lib.nc_set_profile_events(*(ctypes.c_void_p(e.cuda_event) for e in kev[i]))
+        ev[i][0].record()
+        runner.step()
+        ev[i][1].record()
+    lib.nc_set_profile_events(None, None, None, None)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    ms = statistics.mean(step_ms)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if pg is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = BATCH * world / (ms_max * 1e-3)
+
+    # ---- fused-kernel durations (profile events; eager replays when the step is a graph)
+    if runner.graph is not None:
+        for i in range(min(K, 10)):
+            runner.load_batch(x_dev[i % nb], y_dev[i % nb])
+            l2_flush.fill_(float(i))
+            lib.nc_set_profile_events(*(ctypes.c_void_p(e.cuda_event) for e in kev[i]))
+            runner._launch()
+        lib.nc_set_profile_events(None, None, None, None)
+        torch.cuda.synchronize()
+        kev = kev[:min(K, 10)]
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in kev)
+    bwd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in kev)
+
+    # ---- end to end through the public API: pinned host batches, H2D + step + D2H loss
+    x_host = torch.tensor(xs.reshape(nb, BATCH, -1)).pin_memory()
+    y_host = torch.tensor(ys).pin_memory()
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    eev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        l2_flush.fill_(float(i))
+        eev[i][0].record()
+        loss = runner.step(x_host[i % nb], y_host[i % nb])
+        loss_host.copy_(loss, non_blocking=True)
+        eev[i][1].record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = statistics.mean(a.elapsed_time(b) for a, b in eev)
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if pg is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    h2d = x_host[0].numel() * 4 + y_host[0].numel() * 4
+
+    peak = fp32_peak_tflops(dev)
+    flops_fwd = BATCH * 2.0 * 16 * 2000 * 299 * 4            # d forward passes
+    flops_bwd = BATCH * 2.0 * 16 * 2000 * 299 * 7            # d dG + (d-1) dX passes
+    dom = "vnn_fused_bwd_kernel" if bwd_ms >= fwd_ms else "vnn_fused_fwd_kernel"
+    ach = (flops_bwd / (bwd_ms * 1e-3) if dom == "vnn_fused_bwd_kernel" else flops_fwd / (fwd_ms * 1e-3)) / 1e12
+
+    if rank == 0:
+        line = {
+            "metric": "train samples/s (62x62 ALU VNN, B=128 per GPU)", "value": value,
+            "unit": "samples/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
+            "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded numpy ALU batches, random-init params as BASELINE config 0)",
+            "config": {"workload": WORKLOAD, "grid": [62, 62], "roi": [40, 50], "kernel": [23, 13],
+                       "M": 16, "depth": 4, "codd_mode": "continuous", "loss": "mse",
+                       "optimizer": "sgd(1e-2)", "per_gpu_batch": BATCH, "global_batch": BATCH * world,
+                       "parallelism": f"dp{world}", "l2": "flushed (256 MB write) before every timed step",
+                       "cuda_graph": runner.graph is not None},
+            "e2e": {"value": BATCH * world / (e2e_ms * 1e-3), "unit": "samples/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms},
+            "gpu_launches": runner.launches_per_step() * K,
+            "kernels_ms": {"vnn_fused_fwd_kernel": fwd_ms, "vnn_fused_bwd_kernel": bwd_ms},
+            "roofline": {"bound": "fp32", "kernel": dom, "achieved": ach, "peak": peak,
+                         "unit": "TFLOP/s", "frac": ach / peak if peak else None,
+                         "peak_source": "live FFMA probe (nc_fp32_peak_probe); MEASURED_PEAKS.json has no FP32 figure",
+                         "traffic": None},
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "b200":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,186 @@
+/*
+ * neurocell_b200.h -- C ABI of the B200-native VNN propagation hot path.
+ *
+ * One shared library, libneurocell_b200.so, built for sm_100a.  Every entry point takes
+ * plain pointers, sizes and a cudaStream_t (passed as void*), returns an nc_status, and
+ * never allocates device memory: the caller owns the plan buffer, the workspace, the
+ * parameters, inputs, outputs and gradients.  All work is stream-ordered; no entry point
+ * synchronises the host except nc_plan_build (which copies host tables to the device).
+ *
+ * Interfaces replaced (paths relative to the shakes76/neurocell-v2 project root):
+ *   nc_vnn_forward   -> neurocell/propagator.py:209-734  propagate_vnn_2d(...) forward
+ *                       (d-step loop, border hoist, hidden and output-port epilogues) and
+ *                       neurocell/params.py:220-322 precompute_step_params (+ Codd 31-80)
+ *   nc_vnn_backward  -> the custom_vjp backward rules of the same path:
+ *                       neurocell/kernels_pallas.py:1067-1069 (ROI epilogue vjp),
+ *                       :1378-1504 (sparse output-port vjp), :1623-1628 and
+ *                       neurocell/kernels_greens.py:316-400 (convolution dX / dG vjp),
+ *                       plus the XLA autodiff of params.py:220-322
+ *   nc_codd_states   -> neurocell/params.py:31-80 compute_codd_state_probs
+ *                       (VonNeumannNetwork.effective_states, neurocell/model.py:160-183)
+ *   nc_mse_loss      -> neurocell/trainer.py:57-61 default_mse_loss (value and gradient)
+ *   nc_softmax_ce_loss -> optax.softmax_cross_entropy_with_integer_labels(...).mean()
+ *                       as used by the reference's classification drivers
+ *   nc_sgd_update    -> optax.sgd update + apply_updates inside trainer.py:101-106
+ */
+#ifndef NEUROCELL_B200_H_
+#define NEUROCELL_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NC_ABI_VERSION 1
+
+typedef enum nc_status {
+  NC_OK = 0,
+  NC_ERR_INVALID = 1,      /* bad topology, sizes, pointers or enum values        */
+  NC_ERR_WORKSPACE = 2,    /* workspace or plan buffer too small / misaligned     */
+  NC_ERR_UNSUPPORTED = 3,  /* valid reference configuration not built here        */
+  NC_ERR_CUDA = 4,         /* a CUDA runtime call failed; see nc_last_error()     */
+} nc_status;
+
+typedef enum nc_padding { NC_PAD_VALID = 0, NC_PAD_SAME = 1, NC_PAD_CIRCULAR = 2 } nc_padding;
+
+/* Activation ids (neurocell/kernels_pallas.py:76-156). NC_ACT_NONE is `None` (identity). */
+typedef enum nc_activation {
+  NC_ACT_NONE = 0,
+  NC_ACT_TANH = 1,
+  NC_ACT_SIGMOID = 2,
+  NC_ACT_RELU = 3,
+  NC_ACT_LEAKY_RELU = 4,
+  NC_ACT_GELU = 5, /* tanh approximation */
+} nc_activation;
+
+/* Codd modes (neurocell/params.py:23-28). */
+typedef enum nc_codd_mode {
+  NC_CODD_CONTINUOUS = 0,
+  NC_CODD_ANNEALED = 1,
+  NC_CODD_STE_BINARY = 2,
+  NC_CODD_STE_TERNARY = 3,
+} nc_codd_mode;
+
+/*
+ * Static geometry and options of one network: the POD image of ChipTopology2D
+ * (neurocell/topology.py:109-135) plus the model options of VonNeumannNetwork
+ * (neurocell/model.py:38-52).  Port tables live in the plan buffer (nc_plan_build).
+ */
+typedef struct nc_topo {
+  int32_t H, W;            /* grid_shape                                             */
+  int32_t kh, kw;          /* kernel_size, both odd                                  */
+  int32_t M;               /* directions                                             */
+  int32_t depth;           /* d >= 1                                                 */
+  int32_t padding;         /* nc_padding                                             */
+  int32_t n_in;            /* input values per sample (sum over input ports)         */
+  int32_t n_out;           /* output cells per sample (out_h * out_w)                */
+  int32_t act;             /* nc_activation of hidden steps                          */
+  int32_t final_act;       /* nc_activation of the output step (NC_ACT_NONE = None)  */
+  float act_slope;         /* leaky_relu negative slope of `act`                     */
+  float final_act_slope;   /* leaky_relu negative slope of `final_act`               */
+  int32_t norm;            /* spatial standardisation on (1) / off (0)               */
+  int32_t hard_pin_io;     /* params.py:55-79                                        */
+  int32_t gated_filters;   /* propagator.py:262-264: filters -> sigmoid(filters)     */
+} nc_topo;
+
+/* Per-call Codd options (traced scalars in the reference, trainer.py:285-302). */
+typedef struct nc_codd {
+  int32_t mode;            /* nc_codd_mode */
+  float temperature;       /* tau, clamped to >= 1e-4 as params.py:63 */
+  float active_threshold;  /* ste_ternary role-2 threshold (default 0.6) */
+} nc_codd;
+
+/* ---- plan: device copy of the static port tables and masks -------------------------- */
+
+/* Bytes of the device plan buffer for `topo` (256-byte aligned buffer required). */
+size_t nc_plan_bytes(const nc_topo* topo);
+
+/*
+ * Copies the host tables into the caller's device buffer `d_plan` (stream-ordered).
+ *   in_index[n_in]    flat grid index r*W+c of each input value, -1 to drop it
+ *                     (neurocell/propagator.py:103-191 injection order)
+ *   out_index[n_out]  flat grid index r*W+c of each output cell, all inside the ROI and
+ *                     pairwise distinct (neurocell/epilogue.py:82-128 gather order)
+ *   io_mask[H*W]      io_state_mask      (neurocell/topology.py:241-253), 0/1 bytes
+ *   out_w_mask[H*W]   out_weight_mask    (neurocell/topology.py:245-253), 0/1 bytes
+ */
+nc_status nc_plan_build(const nc_topo* topo, const int32_t* in_index, const int32_t* out_index,
+                        const uint8_t* io_mask, const uint8_t* out_w_mask, void* d_plan,
+                        size_t plan_bytes, void* stream);
+
+/* ---- forward / backward ---------------------------------------------------------------- */
+
+#define NC_FLAG_TRAIN 1u   /* forward saves what nc_vnn_backward needs */
+
+/* Workspace bytes for `batch` samples (flags: NC_FLAG_TRAIN or 0). */
+size_t nc_workspace_bytes(const nc_topo* topo, int32_t batch, uint32_t flags);
+
+/*
+ * Forward propagation (propagate_vnn_2d, return_universe=False):
+ *   cell_params (3,H,W) = [W, B, S_raw]; filters (M,1,kh,kw) OIHW; inputs (batch, n_in)
+ *   out (batch, n_out).  With NC_FLAG_TRAIN the workspace keeps the residuals for one
+ *   following nc_vnn_backward call with the same arguments.
+ */
+nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                         const float* filters, const float* inputs, int32_t batch,
+                         const nc_codd* codd, uint32_t flags, float* out, void* d_ws,
+                         size_t ws_bytes, void* stream);
+
+/*
+ * Vector-Jacobian product of nc_vnn_forward w.r.t. the parameters:
+ *   g_out (batch, n_out) -> g_cell_params (3,H,W), g_filters (M,1,kh,kw)  (overwritten).
+ * Deterministic: no floating-point atomics; the batch reduction order is fixed.
+ */
+nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                          const float* filters, const float* inputs, int32_t batch,
+                          const nc_codd* codd, const float* g_out, float* g_cell_params,
+                          float* g_filters, void* d_ws, size_t ws_bytes, void* stream);
+
+/* Effective Codd states s_prob (H,W) (params.py:31-80); d_plan supplies io_mask. */
+nc_status nc_codd_states(const nc_topo* topo, const void* d_plan, const float* states_raw,
+                         const nc_codd* codd, float* s_prob, void* stream);
+
+/* ---- losses and update ----------------------------------------------------------------- */
+
+/* MSE over batch*n values: loss[0] = mean((out-y)^2); g_out = d loss / d out. */
+nc_status nc_mse_loss(const float* out, const float* targets, int32_t batch, int32_t n,
+                      float* loss, float* g_out, void* stream);
+
+/* Mean softmax cross-entropy over `batch` rows of `n` logits with int32 labels. */
+nc_status nc_softmax_ce_loss(const float* logits, const int32_t* labels, int32_t batch,
+                             int32_t n, float* loss, float* g_logits, void* stream);
+
+/* In-place SGD: params[i] -= lr * grads[i]  (lr read from host scalar). */
+nc_status nc_sgd_update(float* params, const float* grads, int64_t n, float lr, void* stream);
+
+/* ---- measurement ----------------------------------------------------------------------- */
+
+/*
+ * Profiling hook (no reference counterpart): when non-null, nc_vnn_forward records
+ * `fwd_start`/`fwd_stop` (cudaEvent_t) on its stream immediately around its fused
+ * propagation kernel, and nc_vnn_backward records `bwd_start`/`bwd_stop` around its fused
+ * adjoint kernel.  Applies to calls made from the calling host thread; pass nulls to stop.
+ */
+void nc_set_profile_events(void* fwd_start, void* fwd_stop, void* bwd_start, void* bwd_stop);
+
+/*
+ * FP32 FFMA throughput probe (no reference counterpart): launches a dependent-chain FFMA
+ * loop on every SM of the current device and writes the FLOPs it performs to *flops.
+ * Time it with CUDA events on `stream` to obtain the device's FP32-pipe peak.
+ */
+nc_status nc_fp32_peak_probe(int32_t iters, double* flops, float* sink, void* stream);
+
+/* ---- misc ------------------------------------------------------------------------------ */
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* nc_last_error(void);
+
+/* NC_ABI_VERSION of the loaded library. */
+int32_t nc_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NEUROCELL_B200_H_ */

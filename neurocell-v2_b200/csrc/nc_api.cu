@@ -1,0 +1,416 @@
+// nc_api.cu -- the extern "C" entry points declared in include/neurocell_b200.h.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <cuda_runtime.h>
+
+#include "nc_errors.h"
+#include "nc_internal.h"
+#include "nc_kernels.cuh"
+
+namespace nc {
+
+// kernels (nc_fused.cu, nc_aux.cu)
+__global__ void vnn_fused_fwd_kernel(FwdArgs a);
+__global__ void vnn_fused_bwd_kernel(BwdArgs a);
+__global__ void prestep_kernel(Geo g, StepParams sp, const float* cell, const float* filters,
+                               const uint8_t* io, const uint8_t* owm, nc_codd codd);
+__global__ void codd_kernel(int HW, const float* s_raw, const uint8_t* io, int hard_pin,
+                            nc_codd codd, float* out);
+__global__ void batch_sum_kernel(const float* in, size_t stride, int n, int batch, float* out);
+__global__ void border_grad_kernel(Geo g, const float* G, const float* gdelta, float* gborder);
+__global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* cell, const float* filters,
+                                   const uint8_t* owm, const float* gsum, const float* gborder,
+                                   const float* gdsum, float* gcell, float* gfilt);
+__global__ void mse_kernel(const float* o, const float* y, int n, float* loss, float* g);
+__global__ void softmax_ce_kernel(const float* x, const int32_t* lab, int batch, int n,
+                                  float* loss, float* g);
+__global__ void sgd_kernel(float* p, const float* gr, int64_t n, float lr);
+
+static thread_local char g_err[1024];
+
+struct ProfileEvents {
+  cudaEvent_t fs = nullptr, fe = nullptr, bs = nullptr, be = nullptr;
+};
+static thread_local ProfileEvents g_prof;
+
+__global__ void fp32_peak_kernel(int iters, float* sink);
+
+nc_status set_error(nc_status st, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return st;
+}
+
+nc_status cuda_error(cudaError_t e, const char* what) {
+  return set_error(NC_ERR_CUDA, "%s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+void clear_error() { g_err[0] = 0; }
+
+static inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+template <typename T>
+static inline T* at(void* base, size_t off) {
+  return off == SIZE_MAX ? nullptr : reinterpret_cast<T*>(static_cast<char*>(base) + off);
+}
+template <typename T>
+static inline const T* at(const void* base, size_t off) {
+  return off == SIZE_MAX ? nullptr : reinterpret_cast<const T*>(static_cast<const char*>(base) + off);
+}
+
+static nc_status check_codd(const nc_codd* c) {
+  if (!c) return set_error(NC_ERR_INVALID, "codd options pointer is null");
+  if (c->mode < NC_CODD_CONTINUOUS || c->mode > NC_CODD_STE_TERNARY)
+    return set_error(NC_ERR_INVALID,
+                     "Unsupported codd_mode id %d; choose from (continuous, annealed, ste_binary, ste_ternary)",
+                     c->mode);
+  return NC_OK;
+}
+
+static nc_status check_ptr(const void* p, const char* name) {
+  if (!p) return set_error(NC_ERR_INVALID, "%s is null", name);
+  if (reinterpret_cast<uintptr_t>(p) % 4 != 0) return set_error(NC_ERR_INVALID, "%s is not 4-byte aligned", name);
+  return NC_OK;
+}
+
+static StepParams step_params(void* ws, const WsLayout& L) {
+  StepParams sp;
+  sp.weff = at<float>(ws, L.weff);
+  sp.seff = at<float>(ws, L.seff);
+  sp.broi = at<float>(ws, L.broi);
+  sp.border = at<float>(ws, L.border);
+  sp.sprob = at<float>(ws, L.sprob);
+  sp.dsprob = at<float>(ws, L.dsprob);
+  sp.wpinned = at<float>(ws, L.wpinned);
+  sp.geff = at<float>(ws, L.geff);
+  return sp;
+}
+
+static size_t fused_smem_bytes(const Geo& g, bool g_smem, bool f_smem, bool big_smem) {
+  size_t n = 2 * (size_t)g.M + 32;
+  if (g_smem) n += (size_t)g.M * g.K;
+  if (f_smem) n += (size_t)g.F_elems;
+  if (big_smem) n += (size_t)g.M * g.P;
+  return n * sizeof(float);
+}
+
+static bool g_fits(const Geo& g) {
+  return sizeof(float) * ((size_t)g.M * g.K + 4 * (size_t)g.M + 128) <= kSmemBudget;
+}
+
+static nc_status set_smem_attr(const void* fn, size_t bytes) {
+  if (bytes <= 48 * 1024) return NC_OK;
+  NC_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return NC_OK;
+}
+
+static nc_status launch_check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, what);
+  return NC_OK;
+}
+
+struct Prepared {
+  Geo g;
+  WsLayout L;
+  bool gs, fs, zs, gzs;
+  StepParams sp;
+  const int32_t* in_index;
+  const int32_t* out_index;
+  const uint8_t* io;
+  const uint8_t* owm;
+};
+
+static nc_status prepare(const nc_topo* topo, const void* plan, int32_t batch, uint32_t flags,
+                         void* ws, size_t ws_bytes, Prepared* pr) {
+  NC_CHECK(make_geo(topo, &pr->g));
+  if (batch <= 0) return set_error(NC_ERR_INVALID, "batch must be >= 1, got %d", batch);
+  if (!plan) return set_error(NC_ERR_INVALID, "plan buffer is null");
+  if (!ws) return set_error(NC_ERR_INVALID, "workspace is null");
+  if (reinterpret_cast<uintptr_t>(ws) % 256 != 0 || reinterpret_cast<uintptr_t>(plan) % 256 != 0)
+    return set_error(NC_ERR_WORKSPACE, "workspace and plan buffers must be 256-byte aligned");
+  pr->L = ws_layout(pr->g, batch, flags, &pr->fs, &pr->zs, &pr->gzs);
+  pr->gs = g_fits(pr->g);
+  if (ws_bytes < pr->L.total)
+    return set_error(NC_ERR_WORKSPACE, "workspace too small: %zu bytes given, %zu required", ws_bytes,
+                     pr->L.total);
+  pr->sp = step_params(ws, pr->L);
+  const PlanLayout PL = plan_layout(topo);
+  pr->in_index = at<int32_t>(plan, PL.in_index);
+  pr->out_index = at<int32_t>(plan, PL.out_index);
+  pr->io = at<uint8_t>(plan, PL.io_mask);
+  pr->owm = at<uint8_t>(plan, PL.out_w_mask);
+  return NC_OK;
+}
+
+static nc_status launch_prestep(const Prepared& pr, const float* cell, const float* filters,
+                                const nc_codd* codd, cudaStream_t st) {
+  const int HW = pr.g.H * pr.g.W;
+  const int nthreads = 256;
+  const int nblocks = (HW + nthreads - 1) / nthreads;
+  prestep_kernel<<<nblocks, nthreads, 0, st>>>(pr.g, pr.sp, cell, filters, pr.io, pr.owm, *codd);
+  return launch_check("prestep_kernel launch");
+}
+
+}  // namespace nc
+
+using namespace nc;
+
+extern "C" {
+
+int32_t nc_abi_version(void) { return NC_ABI_VERSION; }
+
+const char* nc_last_error(void) { return g_err; }
+
+size_t nc_plan_bytes(const nc_topo* topo) {
+  Geo g;
+  if (make_geo(topo, &g) != NC_OK) return 0;
+  return plan_layout(topo).total;
+}
+
+nc_status nc_plan_build(const nc_topo* topo, const int32_t* in_index, const int32_t* out_index,
+                        const uint8_t* io_mask, const uint8_t* out_w_mask, void* d_plan,
+                        size_t plan_bytes, void* stream) {
+  Geo g;
+  NC_CHECK(make_geo(topo, &g));
+  const PlanLayout PL = plan_layout(topo);
+  if (!d_plan) return set_error(NC_ERR_INVALID, "plan buffer is null");
+  if (reinterpret_cast<uintptr_t>(d_plan) % 256 != 0)
+    return set_error(NC_ERR_WORKSPACE, "plan buffer must be 256-byte aligned");
+  if (plan_bytes < PL.total)
+    return set_error(NC_ERR_WORKSPACE, "plan buffer too small: %zu < %zu", plan_bytes, PL.total);
+  if ((g.n_in > 0 && !in_index) || !out_index || !io_mask || !out_w_mask)
+    return set_error(NC_ERR_INVALID, "null plan table");
+  const int HW = g.H * g.W;
+  for (int j = 0; j < g.n_in; ++j)
+    if (in_index[j] >= HW || in_index[j] < -1)
+      return set_error(NC_ERR_INVALID, "input index %d out of grid (value %d)", j, in_index[j]);
+  for (int j = 0; j < g.n_out; ++j) {
+    const int idx = out_index[j];
+    if (idx < 0 || idx >= HW) return set_error(NC_ERR_INVALID, "output index %d out of grid", j);
+    const int r = idx / g.W - g.pad_h, c = idx % g.W - g.pad_w;
+    if (r < 0 || r >= g.roi_h || c < 0 || c >= g.roi_w)
+      return set_error(NC_ERR_UNSUPPORTED,
+                       "output cell (%d, %d) lies outside the active ROI; border outputs are not built",
+                       idx / g.W, idx % g.W);
+    for (int k = 0; k < j; ++k)
+      if (out_index[k] == idx) return set_error(NC_ERR_UNSUPPORTED, "duplicate output cell %d", idx);
+  }
+  cudaStream_t st = as_stream(stream);
+  char* base = static_cast<char*>(d_plan);
+  if (g.n_in > 0)
+    NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.in_index, in_index, sizeof(int32_t) * g.n_in,
+                                  cudaMemcpyHostToDevice, st));
+  NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.out_index, out_index, sizeof(int32_t) * g.n_out,
+                                cudaMemcpyHostToDevice, st));
+  NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.io_mask, io_mask, (size_t)HW, cudaMemcpyHostToDevice, st));
+  NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.out_w_mask, out_w_mask, (size_t)HW, cudaMemcpyHostToDevice, st));
+  NC_CUDA_CHECK(cudaStreamSynchronize(st));   // host tables may be freed after return
+  return NC_OK;
+}
+
+size_t nc_workspace_bytes(const nc_topo* topo, int32_t batch, uint32_t flags) {
+  Geo g;
+  if (make_geo(topo, &g) != NC_OK || batch <= 0) return 0;
+  return ws_layout(g, batch, flags, nullptr, nullptr, nullptr).total;
+}
+
+nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                         const float* filters, const float* inputs, int32_t batch,
+                         const nc_codd* codd, uint32_t flags, float* out, void* d_ws,
+                         size_t ws_bytes, void* stream) {
+  Prepared pr;
+  NC_CHECK(prepare(topo, d_plan, batch, flags, d_ws, ws_bytes, &pr));
+  NC_CHECK(check_codd(codd));
+  NC_CHECK(check_ptr(cell_params, "cell_params"));
+  NC_CHECK(check_ptr(filters, "filters"));
+  NC_CHECK(check_ptr(out, "out"));
+  if (pr.g.n_in > 0) NC_CHECK(check_ptr(inputs, "inputs"));
+  cudaStream_t st = as_stream(stream);
+  NC_CHECK(launch_prestep(pr, cell_params, filters, codd, st));
+
+  const bool train = (flags & NC_FLAG_TRAIN) != 0;
+  FwdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.g = pr.g;
+  a.sp = pr.sp;
+  a.in_index = pr.in_index;
+  a.out_index = pr.out_index;
+  a.inputs = inputs;
+  a.out = out;
+  a.xsave = at<float>(d_ws, pr.L.xsave);
+  a.zhat = at<float>(d_ws, pr.L.zhat);
+  a.rstd = at<float>(d_ws, pr.L.rstd);
+  a.fscr = at<float>(d_ws, pr.L.fscr);
+  a.zscr = at<float>(d_ws, pr.L.zscr);
+  a.train = train ? 1 : 0;
+  a.g_smem = pr.gs ? 1 : 0;
+  a.f_smem = (pr.gs && pr.fs) ? 1 : 0;
+  a.z_smem = (a.f_smem && pr.zs) ? 1 : 0;
+  a.batch = batch;
+  if (!a.f_smem && !a.fscr)
+    return set_error(NC_ERR_UNSUPPORTED, "field does not fit on chip and no scratch was laid out");
+  if (!a.z_smem && !train && !a.zscr)
+    return set_error(NC_ERR_UNSUPPORTED, "planes do not fit on chip and no scratch was laid out");
+  const size_t smem = fused_smem_bytes(pr.g, a.g_smem, a.f_smem, a.z_smem);
+  NC_CHECK(set_smem_attr((const void*)vnn_fused_fwd_kernel, smem));
+  if (g_prof.fs) NC_CUDA_CHECK(cudaEventRecord(g_prof.fs, st));
+  vnn_fused_fwd_kernel<<<batch, kFusedThreads, smem, st>>>(a);
+  NC_CHECK(launch_check("vnn_fused_fwd_kernel launch"));
+  if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
+  clear_error();
+  return NC_OK;
+}
+
+nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                          const float* filters, const float* inputs, int32_t batch,
+                          const nc_codd* codd, const float* g_out, float* g_cell_params,
+                          float* g_filters, void* d_ws, size_t ws_bytes, void* stream) {
+  Prepared pr;
+  NC_CHECK(prepare(topo, d_plan, batch, NC_FLAG_TRAIN, d_ws, ws_bytes, &pr));
+  NC_CHECK(check_codd(codd));
+  NC_CHECK(check_ptr(cell_params, "cell_params"));
+  NC_CHECK(check_ptr(filters, "filters"));
+  NC_CHECK(check_ptr(g_out, "g_out"));
+  NC_CHECK(check_ptr(g_cell_params, "g_cell_params"));
+  NC_CHECK(check_ptr(g_filters, "g_filters"));
+  if (pr.g.n_in > 0) NC_CHECK(check_ptr(inputs, "inputs"));
+  cudaStream_t st = as_stream(stream);
+  const Geo& g = pr.g;
+  const WsLayout& L = pr.L;
+
+  BwdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.g = g;
+  a.sp = pr.sp;
+  a.in_index = pr.in_index;
+  a.out_index = pr.out_index;
+  a.inputs = inputs;
+  a.gout = g_out;
+  a.xsave = at<float>(d_ws, L.xsave);
+  a.zhat = at<float>(d_ws, L.zhat);
+  a.rstd = at<float>(d_ws, L.rstd);
+  a.fscr = at<float>(d_ws, L.fscr);
+  a.gzscr = at<float>(d_ws, L.gzscr);
+  a.gpix = at<float>(d_ws, L.gpix);
+  a.gdpart = at<float>(d_ws, L.gdpart);
+  a.gdelta = at<float>(d_ws, L.gdelta);
+  a.g_smem = pr.gs ? 1 : 0;
+  a.f_smem = (pr.gs && pr.fs) ? 1 : 0;
+  a.gz_smem = (a.f_smem && pr.gzs) ? 1 : 0;
+  a.batch = batch;
+  if (!a.f_smem && !a.fscr)
+    return set_error(NC_ERR_UNSUPPORTED, "field does not fit on chip and no scratch was laid out");
+  if (!a.gz_smem && !a.gzscr)
+    return set_error(NC_ERR_UNSUPPORTED, "plane gradients do not fit on chip and no scratch was laid out");
+  const size_t smem = fused_smem_bytes(g, a.g_smem, a.f_smem, a.gz_smem);
+  NC_CHECK(set_smem_attr((const void*)vnn_fused_bwd_kernel, smem));
+  if (g_prof.bs) NC_CUDA_CHECK(cudaEventRecord(g_prof.bs, st));
+  vnn_fused_bwd_kernel<<<batch, kFusedThreads, smem, st>>>(a);
+  NC_CHECK(launch_check("vnn_fused_bwd_kernel launch"));
+  if (g_prof.be) NC_CUDA_CHECK(cudaEventRecord(g_prof.be, st));
+
+  // batch reductions (fixed order -> deterministic)
+  float* gsum = at<float>(d_ws, L.gsum);
+  float* gdsum = at<float>(d_ws, L.gdsum);
+  const int P3 = 3 * g.P, MK = g.M * g.K;
+  batch_sum_kernel<<<(P3 + 255) / 256, 256, 0, st>>>(a.gpix, (size_t)P3, P3, batch, gsum);
+  NC_CHECK(launch_check("batch_sum_kernel(pixels) launch"));
+  batch_sum_kernel<<<(MK + 255) / 256, 256, 0, st>>>(a.gdpart, (size_t)MK, MK, batch, gdsum);
+  NC_CHECK(launch_check("batch_sum_kernel(filters) launch"));
+  float* gborder = nullptr;
+  const int HW = g.H * g.W;
+  if (a.gdelta) {
+    float* gdeltasum = at<float>(d_ws, L.gdeltasum);
+    const int MP = g.M * g.P;
+    batch_sum_kernel<<<(MP + 255) / 256, 256, 0, st>>>(a.gdelta, (size_t)MP, MP, batch, gdeltasum);
+    NC_CHECK(launch_check("batch_sum_kernel(delta) launch"));
+    gborder = at<float>(d_ws, L.gborder);
+    border_grad_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp.geff, gdeltasum, gborder);
+    NC_CHECK(launch_check("border_grad_kernel launch"));
+  }
+  prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, gsum,
+                                                       gborder, gdsum, g_cell_params, g_filters);
+  NC_CHECK(launch_check("prestep_bwd_kernel launch"));
+  clear_error();
+  return NC_OK;
+}
+
+nc_status nc_codd_states(const nc_topo* topo, const void* d_plan, const float* states_raw,
+                         const nc_codd* codd, float* s_prob, void* stream) {
+  Geo g;
+  NC_CHECK(make_geo(topo, &g));
+  NC_CHECK(check_codd(codd));
+  if (!d_plan) return set_error(NC_ERR_INVALID, "plan buffer is null");
+  NC_CHECK(check_ptr(states_raw, "states_raw"));
+  NC_CHECK(check_ptr(s_prob, "s_prob"));
+  const PlanLayout PL = plan_layout(topo);
+  const int HW = g.H * g.W;
+  codd_kernel<<<(HW + 255) / 256, 256, 0, as_stream(stream)>>>(
+      HW, states_raw, at<uint8_t>(d_plan, PL.io_mask), g.hard_pin, *codd, s_prob);
+  NC_CHECK(launch_check("codd_kernel launch"));
+  clear_error();
+  return NC_OK;
+}
+
+nc_status nc_mse_loss(const float* out, const float* targets, int32_t batch, int32_t n, float* loss,
+                      float* g_out, void* stream) {
+  if (batch <= 0 || n <= 0) return set_error(NC_ERR_INVALID, "bad loss shape (%d, %d)", batch, n);
+  NC_CHECK(check_ptr(out, "out"));
+  NC_CHECK(check_ptr(targets, "targets"));
+  const int64_t total = (int64_t)batch * n;
+  if (total > 0x7fffffff) return set_error(NC_ERR_INVALID, "loss too large");
+  mse_kernel<<<1, 1024, 0, as_stream(stream)>>>(out, targets, (int)total, loss, g_out);
+  NC_CHECK(launch_check("mse_kernel launch"));
+  clear_error();
+  return NC_OK;
+}
+
+nc_status nc_softmax_ce_loss(const float* logits, const int32_t* labels, int32_t batch, int32_t n,
+                             float* loss, float* g_logits, void* stream) {
+  if (batch <= 0 || n <= 0) return set_error(NC_ERR_INVALID, "bad loss shape (%d, %d)", batch, n);
+  NC_CHECK(check_ptr(logits, "logits"));
+  NC_CHECK(check_ptr(labels, "labels"));
+  softmax_ce_kernel<<<1, 1024, 0, as_stream(stream)>>>(logits, labels, batch, n, loss, g_logits);
+  NC_CHECK(launch_check("softmax_ce_kernel launch"));
+  clear_error();
+  return NC_OK;
+}
+
+nc_status nc_sgd_update(float* params, const float* grads, int64_t n, float lr, void* stream) {
+  if (n <= 0) return set_error(NC_ERR_INVALID, "bad parameter count %lld", (long long)n);
+  NC_CHECK(check_ptr(params, "params"));
+  NC_CHECK(check_ptr(grads, "grads"));
+  const int64_t blocks64 = (n + 255) / 256;
+  const int blocks = (int)(blocks64 < 4096 ? blocks64 : 4096);
+  sgd_kernel<<<blocks, 256, 0, as_stream(stream)>>>(params, grads, n, lr);
+  NC_CHECK(launch_check("sgd_kernel launch"));
+  clear_error();
+  return NC_OK;
+}
+
+void nc_set_profile_events(void* fwd_start, void* fwd_stop, void* bwd_start, void* bwd_stop) {
+  g_prof.fs = reinterpret_cast<cudaEvent_t>(fwd_start);
+  g_prof.fe = reinterpret_cast<cudaEvent_t>(fwd_stop);
+  g_prof.bs = reinterpret_cast<cudaEvent_t>(bwd_start);
+  g_prof.be = reinterpret_cast<cudaEvent_t>(bwd_stop);
+}
+
+nc_status nc_fp32_peak_probe(int32_t iters, double* flops, float* sink, void* stream) {
+  if (iters <= 0 || !flops || !sink) return set_error(NC_ERR_INVALID, "bad probe arguments");
+  int dev = 0, sms = 0;
+  NC_CUDA_CHECK(cudaGetDevice(&dev));
+  NC_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int blocks = sms * 4, threads = 256;
+  fp32_peak_kernel<<<blocks, threads, 0, as_stream(stream)>>>(iters, sink);
+  NC_CHECK(launch_check("fp32_peak_kernel launch"));
+  *flops = 2.0 * 16.0 * (double)iters * (double)blocks * (double)threads;
+  clear_error();
+  return NC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,426 @@
+// nc_fused.cu -- per-sample fused forward and backward of the VNN d-step loop (sm_100a).
+//
+// One CTA owns one sample for the whole propagation: its padded cell field F, the M
+// response planes z and (in backward) the plane gradients stay in shared memory across
+// all d steps whenever they fit, so HBM only sees the inputs, the outputs and the
+// training residuals.  The Green's convolution is a direct FP32 cross-correlation
+// (neurocell/kernels_greens.py:177-217 semantics); the epilogues follow
+// neurocell/epilogue.py:28-56 and :82-128 with the centred two-pass variance of
+// neurocell/kernels_pallas.py:202-205.
+#include <cuda_runtime.h>
+
+#include "nc_common.cuh"
+#include "nc_kernels.cuh"
+
+namespace nc {
+
+// ---------------------------------------------------------------------------------------
+// field construction
+// ---------------------------------------------------------------------------------------
+
+// Fill the halo of F with the wrapped interior (CIRCULAR mode, propagator.py:284-341).
+__device__ void field_wrap_ring(const Geo& g, float* F, int tid, int nt) {
+  const int n = g.Fh * g.Fw;
+  for (int i = tid; i < n; i += nt) {
+    const int fr = i / g.Fw, fc = i - fr * g.Fw;
+    const int r = fr - g.oh, c = fc - g.ow;
+    if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) continue;
+    int sr = r % g.roi_h; if (sr < 0) sr += g.roi_h;
+    int sc = c % g.roi_w; if (sc < 0) sc += g.roi_w;
+    F[fr * g.Fs + fc] = F[(sr + g.oh) * g.Fs + sc + g.ow];
+  }
+}
+
+// Step t=0 field: zeros with the sample's inputs scattered in (propagator.py:103-191).
+__device__ void field_inject(const Geo& g, float* F, const int32_t* in_index,
+                             const float* inp, int tid, int nt) {
+  for (int i = tid; i < g.F_elems; i += nt) F[i] = 0.0f;
+  __syncthreads();
+  for (int j = tid; j < g.n_in; j += nt) {
+    const int idx = in_index[j];
+    if (idx < 0) continue;
+    const int r = idx / g.W, c = idx - (idx / g.W) * g.W;
+    F[(r + g.gr) * g.Fs + c + g.gc] = inp[j];
+  }
+  __syncthreads();
+  if (g.padding == NC_PAD_CIRCULAR) {
+    field_wrap_ring(g, F, tid, nt);
+    __syncthreads();
+  }
+}
+
+// VALID ring for steps t>=1: the static border template border_2d (propagator.py:354-371).
+__device__ void field_border_ring(const Geo& g, float* F, const float* border, int tid, int nt) {
+  const int n = g.Fh * g.Fw;   // VALID: F == grid
+  for (int i = tid; i < n; i += nt) {
+    const int fr = i / g.Fw, fc = i - fr * g.Fw;
+    const int r = fr - g.oh, c = fc - g.ow;
+    if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) continue;
+    F[fr * g.Fs + fc] = border[fr * g.W + fc];
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Green's convolution: Z[m, r, c] = sum_{u,v} G[m,u,v] F[r+u, c+v]
+// ---------------------------------------------------------------------------------------
+__device__ void conv_fwd(const Geo& g, const float* F, const float* G, float* Z, int tid, int nt) {
+  const int ns = (g.roi_w + 3) >> 2;
+  const int items = g.M * g.roi_h * ns;
+  for (int it = tid; it < items; it += nt) {
+    const int s = it % ns;
+    const int rest = it / ns;
+    const int r = rest % g.roi_h;
+    const int m = rest / g.roi_h;
+    const int c0 = s << 2;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    const float* Gm = G + (size_t)m * g.K;
+    for (int u = 0; u < g.kh; ++u) {
+      const float* fr = F + (r + u) * g.Fs + c0;
+      const float* gr = Gm + u * g.kw;
+      for (int v = 0; v < g.kw; ++v) {
+        const float w = gr[v];
+        a0 = fmaf(w, fr[v], a0);
+        a1 = fmaf(w, fr[v + 1], a1);
+        a2 = fmaf(w, fr[v + 2], a2);
+        a3 = fmaf(w, fr[v + 3], a3);
+      }
+    }
+    float* zr = Z + (size_t)m * g.P + r * g.roi_w + c0;
+    zr[0] = a0;
+    if (c0 + 1 < g.roi_w) zr[1] = a1;
+    if (c0 + 2 < g.roi_w) zr[2] = a2;
+    if (c0 + 3 < g.roi_w) zr[3] = a3;
+  }
+}
+
+// Per-plane mean and 1/sqrt(var + eps), centred two-pass (kernels_pallas.py:200-205).
+__device__ void plane_stats(const Geo& g, const float* Z, float* s_mean, float* s_rstd,
+                            int tid, int nt) {
+  const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
+  const float inv_n = 1.0f / (float)g.P;
+  for (int m = warp; m < g.M; m += nw) {
+    if (!g.norm) {
+      if (lane == 0) { s_mean[m] = 0.f; s_rstd[m] = 1.f; }
+      continue;
+    }
+    const float* z = Z + (size_t)m * g.P;
+    float s = 0.f;
+    for (int p = lane; p < g.P; p += 32) s += z[p];
+    const float mean = warp_sum(s) * inv_n;
+    float v = 0.f;
+    for (int p = lane; p < g.P; p += 32) {
+      const float dz = z[p] - mean;
+      v = fmaf(dz, dz, v);
+    }
+    const float var = warp_sum(v) * inv_n;
+    if (lane == 0) {
+      s_mean[m] = mean;
+      s_rstd[m] = 1.0f / sqrtf(var + kNormEps);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kFusedThreads, 1) vnn_fused_fwd_kernel(FwdArgs a) {
+  extern __shared__ float smem[];
+  const Geo& g = a.g;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int b = blockIdx.x;
+  const size_t P = (size_t)g.P, M = (size_t)g.M;
+
+  // shared layout: [G (M*K)] [mean M] [rstd M] [pad] [F] [Z]
+  float* cur = smem;
+  float* Gs = a.g_smem ? cur : a.sp.geff;
+  if (a.g_smem) cur += M * g.K;
+  float* s_mean = cur;
+  float* s_rstd = cur + M;
+  cur += 2 * M + 32;
+  float* F = a.f_smem ? cur : a.fscr + (size_t)b * g.F_elems;
+  if (a.f_smem) cur += g.F_elems;
+  float* Zs = a.z_smem ? cur : nullptr;
+
+  if (a.g_smem)
+    for (int i = tid; i < (int)(M * g.K); i += nt) Gs[i] = a.sp.geff[i];
+  field_inject(g, F, a.in_index, a.inputs + (size_t)b * g.n_in, tid, nt);
+
+  for (int t = 0; t < g.d; ++t) {
+    float* ZH = a.train ? a.zhat + ((size_t)b * g.d + t) * M * P : nullptr;
+    float* Z = Zs ? Zs : (a.train ? ZH : a.zscr + (size_t)b * M * P);
+    conv_fwd(g, F, Gs, Z, tid, nt);
+    __syncthreads();
+    plane_stats(g, Z, s_mean, s_rstd, tid, nt);
+    __syncthreads();
+    if (a.train)
+      for (int m = tid; m < g.M; m += nt) a.rstd[((size_t)b * g.d + t) * M + m] = s_rstd[m];
+
+    if (t < g.d - 1) {
+      // hidden-step epilogue (epilogue.py:28-56) -> new ROI field inside F
+      float* xs = a.train ? a.xsave + ((size_t)b * (g.d - 1) + t) * P : nullptr;
+      for (int p = tid; p < g.P; p += nt) {
+        const float bb = a.sp.broi[p];
+        float lin = 0.f, act = 0.f;
+        for (int m = 0; m < g.M; ++m) {
+          const float zh = (Z[m * P + p] - s_mean[m]) * s_rstd[m];
+          if (ZH) ZH[m * P + p] = zh;
+          lin += zh;
+          if (g.act != NC_ACT_NONE) act += act_fwd(g.act, zh + bb, g.slope);
+        }
+        if (g.act == NC_ACT_NONE) act = lin + (float)g.M * bb;
+        const float xn = a.sp.weff[p] * lin + a.sp.seff[p] * act;
+        const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+        F[(r + g.oh) * g.Fs + c + g.ow] = xn;
+        if (xs) xs[p] = xn;
+      }
+      __syncthreads();
+      if (t == 0 && g.padding == NC_PAD_VALID) {
+        field_border_ring(g, F, a.sp.border, tid, nt);
+        __syncthreads();
+      }
+      if (g.padding == NC_PAD_CIRCULAR) {
+        field_wrap_ring(g, F, tid, nt);
+        __syncthreads();
+      }
+    } else {
+      // output step (epilogue.py:82-128): standardise with full-plane statistics,
+      // gather the port cells, factored Codd gating.
+      bool normalized = false;
+      if (a.train) {
+        for (int i = tid; i < (int)(M * P); i += nt) {
+          const int m = i / g.P;
+          ZH[i] = (Z[i] - s_mean[m]) * s_rstd[m];
+        }
+        __syncthreads();
+        normalized = true;
+      }
+      const float* Zr = normalized ? ZH : Z;
+      for (int j = tid; j < g.n_out; j += nt) {
+        const int idx = a.out_index[j];
+        const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
+        const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+        const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];
+        float lin = 0.f, act = 0.f;
+        for (int m = 0; m < g.M; ++m) {
+          const float zh = normalized ? Zr[m * P + p] : (Zr[m * P + p] - s_mean[m]) * s_rstd[m];
+          lin += zh;
+          if (g.fact != NC_ACT_NONE) act += act_fwd(g.fact, zh + bo, g.fslope);
+        }
+        float o;
+        if (g.fact == NC_ACT_NONE) {
+          o = (wo + so) * lin + ((float)g.M * so * bo);
+        } else {
+          o = act_fwd(g.fact, wo * lin + so * act, g.fslope);
+        }
+        a.out[(size_t)b * g.n_out + j] = o;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------------------
+
+// In-place standardisation adjoint: GZ <- rstd * (GZ - mean(GZ) - zh * mean(GZ*zh)).
+__device__ void norm_bwd(const Geo& g, float* GZ, const float* ZH, const float* rstd_t,
+                         int tid, int nt) {
+  if (!g.norm) return;
+  const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
+  const float inv_n = 1.0f / (float)g.P;
+  const size_t P = (size_t)g.P;
+  for (int m = warp; m < g.M; m += nw) {
+    float* gz = GZ + m * P;
+    const float* zh = ZH + m * P;
+    float s1 = 0.f, s2 = 0.f;
+    for (int p = lane; p < g.P; p += 32) {
+      const float v = gz[p];
+      s1 += v;
+      s2 = fmaf(v, zh[p], s2);
+    }
+    const float c1 = warp_sum(s1) * inv_n;
+    const float c2 = warp_sum(s2) * inv_n;
+    const float rs = rstd_t[m];
+    for (int p = lane; p < g.P; p += 32) gz[p] = rs * (gz[p] - c1 - zh[p] * c2);
+  }
+}
+
+// Filter-gradient partial: dG[m,u,v] (+)= sum_{r,c} GZ[m,r,c] F[r+u, c+v].
+__device__ void conv_dg(const Geo& g, const float* F, const float* GZ, float* dg, bool accumulate,
+                        int tid, int nt) {
+  const int items = g.M * g.K;
+  for (int it = tid; it < items; it += nt) {
+    const int m = it / g.K, k = it - (it / g.K) * g.K;
+    const int u = k / g.kw, v = k - (k / g.kw) * g.kw;
+    const float* gz = GZ + (size_t)m * g.P;
+    float acc = 0.f;
+    for (int r = 0; r < g.roi_h; ++r) {
+      const float* fr = F + (r + u) * g.Fs + v;
+      const float* gr = gz + r * g.roi_w;
+      for (int c = 0; c < g.roi_w; ++c) acc = fmaf(gr[c], fr[c], acc);
+    }
+    dg[it] = accumulate ? dg[it] + acc : acc;
+  }
+}
+
+// Field adjoint on the ROI: GY[r',c'] = sum_m sum_{u,v} G[m,u,v] GZ[m, r'+oh-u, c'+ow-v]
+// (zero outside the ROI, wrapped for CIRCULAR).
+__device__ void conv_dx(const Geo& g, const float* G, const float* GZ, float* GY, int tid, int nt) {
+  const size_t P = (size_t)g.P;
+  for (int q = tid; q < g.P; q += nt) {
+    const int r = q / g.roi_w, c = q - (q / g.roi_w) * g.roi_w;
+    float acc = 0.f;
+    if (g.padding == NC_PAD_CIRCULAR) {
+      for (int m = 0; m < g.M; ++m) {
+        const float* gz = GZ + m * P;
+        const float* Gm = G + (size_t)m * g.K;
+        for (int u = 0; u < g.kh; ++u) {
+          int rr = (r + g.oh - u) % g.roi_h; if (rr < 0) rr += g.roi_h;
+          for (int v = 0; v < g.kw; ++v) {
+            int cc = (c + g.ow - v) % g.roi_w; if (cc < 0) cc += g.roi_w;
+            acc = fmaf(Gm[u * g.kw + v], gz[rr * g.roi_w + cc], acc);
+          }
+        }
+      }
+    } else {
+      const int u_lo = max(0, r + g.oh - g.roi_h + 1), u_hi = min(g.kh - 1, r + g.oh);
+      const int v_lo = max(0, c + g.ow - g.roi_w + 1), v_hi = min(g.kw - 1, c + g.ow);
+      for (int m = 0; m < g.M; ++m) {
+        const float* gz = GZ + m * P;
+        const float* Gm = G + (size_t)m * g.K;
+        for (int u = u_lo; u <= u_hi; ++u) {
+          const float* grow = gz + (r + g.oh - u) * g.roi_w + (c + g.ow);
+          const float* wrow = Gm + u * g.kw;
+          for (int v = v_lo; v <= v_hi; ++v) acc = fmaf(wrow[v], grow[-v], acc);
+        }
+      }
+    }
+    GY[q] = acc;
+  }
+}
+
+__global__ void __launch_bounds__(kFusedThreads, 1) vnn_fused_bwd_kernel(BwdArgs a) {
+  extern __shared__ float smem[];
+  const Geo& g = a.g;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int b = blockIdx.x;
+  const size_t P = (size_t)g.P, M = (size_t)g.M;
+
+  // shared layout: [G (M*K)] [rstd M] [pad] [F] [GZ]
+  float* cur = smem;
+  float* Gs = a.g_smem ? cur : a.sp.geff;
+  if (a.g_smem) cur += M * g.K;
+  float* s_rstd = cur;
+  cur += 2 * M + 32;
+  float* F = a.f_smem ? cur : a.fscr + (size_t)b * g.F_elems;
+  if (a.f_smem) cur += g.F_elems;
+  float* GZ = a.gz_smem ? cur : a.gzscr + (size_t)b * M * P;
+  float* gp0 = a.gpix + (size_t)b * 3 * P;   // g w_eff partial
+  float* gp1 = gp0 + P;                      // g s_eff partial
+  float* gp2 = gp1 + P;                      // g b_roi partial
+  float* GY = a.gpix + (size_t)a.batch * 3 * P + (size_t)b * P;
+  float* dg = a.gdpart + (size_t)b * M * g.K;
+  float* gdel = a.gdelta ? a.gdelta + (size_t)b * M * P : nullptr;
+
+  if (a.g_smem)
+    for (int i = tid; i < (int)(M * g.K); i += nt) Gs[i] = a.sp.geff[i];
+  for (int p = tid; p < g.P; p += nt) { gp0[p] = 0.f; gp1[p] = 0.f; gp2[p] = 0.f; }
+  for (int i = tid; i < (int)(M * P); i += nt) GZ[i] = 0.f;
+  // F for t >= 1: zero halo (SAME), border template (VALID); interior filled per step
+  for (int i = tid; i < g.F_elems; i += nt) F[i] = 0.f;
+  __syncthreads();
+  if (g.padding == NC_PAD_VALID && g.d > 1) field_border_ring(g, F, a.sp.border, tid, nt);
+
+  // ---- output step (t = d-1): sparse port adjoint (kernels_pallas.py:1107-1179) --------
+  {
+    const int t = g.d - 1;
+    const float* ZH = a.zhat + ((size_t)b * g.d + t) * M * P;
+    for (int m = tid; m < g.M; m += nt) s_rstd[m] = a.rstd[((size_t)b * g.d + t) * M + m];
+    for (int j = tid; j < g.n_out; j += nt) {
+      const int idx = a.out_index[j];
+      const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
+      const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+      const float go = a.gout[(size_t)b * g.n_out + j];
+      const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];
+      float lin = 0.f;
+      for (int m = 0; m < g.M; ++m) lin += ZH[m * P + p];
+      if (g.fact == NC_ACT_NONE) {
+        gp0[p] += go * lin;
+        gp1[p] += go * (lin + (float)g.M * bo);
+        gp2[p] += go * (float)g.M * so;
+        const float gzh = (wo + so) * go;
+        for (int m = 0; m < g.M; ++m) GZ[m * P + p] = gzh;
+      } else {
+        float act = 0.f;
+        for (int m = 0; m < g.M; ++m) act += act_fwd(g.fact, ZH[m * P + p] + bo, g.fslope);
+        float dpre;
+        act_fwd_deriv(g.fact, wo * lin + so * act, g.fslope, &dpre);
+        const float gpre = go * dpre;
+        gp0[p] += gpre * lin;
+        gp1[p] += gpre * act;
+        float db = 0.f;
+        for (int m = 0; m < g.M; ++m) {
+          float dd;
+          act_fwd_deriv(g.fact, ZH[m * P + p] + bo, g.fslope, &dd);
+          GZ[m * P + p] = gpre * (wo + so * dd);
+          db += gpre * so * dd;
+        }
+        gp2[p] += db;
+      }
+    }
+    __syncthreads();
+    norm_bwd(g, GZ, ZH, s_rstd, tid, nt);
+    __syncthreads();
+  }
+
+  for (int t = g.d - 1; t >= 0; --t) {
+    // GZ holds the plane gradients of step t
+    if (gdel && t >= 1) {
+      for (int i = tid; i < (int)(M * P); i += nt) gdel[i] = (t == g.d - 1) ? GZ[i] : gdel[i] + GZ[i];
+    }
+    if (t == 0) {
+      field_inject(g, F, a.in_index, a.inputs + (size_t)b * g.n_in, tid, nt);
+    } else {
+      const float* xs = a.xsave + ((size_t)b * (g.d - 1) + (t - 1)) * P;
+      for (int p = tid; p < g.P; p += nt) {
+        const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+        F[(r + g.oh) * g.Fs + c + g.ow] = xs[p];
+      }
+      __syncthreads();
+      if (g.padding == NC_PAD_CIRCULAR) {
+        field_wrap_ring(g, F, tid, nt);
+        __syncthreads();
+      }
+    }
+    conv_dg(g, F, GZ, dg, t != g.d - 1, tid, nt);
+    if (t == 0) break;
+    conv_dx(g, Gs, GZ, GY, tid, nt);
+    __syncthreads();
+
+    // hidden epilogue adjoint of step t-1 (kernels_pallas.py:221-291)
+    const float* ZH = a.zhat + ((size_t)b * g.d + (t - 1)) * M * P;
+    for (int m = tid; m < g.M; m += nt) s_rstd[m] = a.rstd[((size_t)b * g.d + (t - 1)) * M + m];
+    for (int p = tid; p < g.P; p += nt) {
+      const float gy = GY[p];
+      const float bb = a.sp.broi[p], we = a.sp.weff[p], se = a.sp.seff[p];
+      float lin = 0.f, act = 0.f, dsum = 0.f;
+      for (int m = 0; m < g.M; ++m) {
+        const float zh = ZH[m * P + p];
+        float dd;
+        const float av = act_fwd_deriv(g.act, zh + bb, g.slope, &dd);
+        lin += zh;
+        act += av;
+        dsum += dd;
+        GZ[m * P + p] = we * gy + se * gy * dd;
+      }
+      gp0[p] += gy * lin;
+      gp1[p] += gy * act;
+      gp2[p] += se * gy * dsum;
+    }
+    __syncthreads();
+    norm_bwd(g, GZ, ZH, s_rstd, tid, nt);
+    __syncthreads();
+  }
+}
+
+}  // namespace nc

@@ -1,0 +1,56 @@
+// nc_internal.h -- host/device shared geometry and workspace layout.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "neurocell_b200.h"
+
+namespace nc {
+
+// Derived geometry passed by value to every kernel.
+//
+// The per-sample "field" F is the padded plane the Green's convolution reads:
+//   VALID:        F is the full H x W grid; the ROI is its interior at (pad_h, pad_w).
+//   SAME/CIRCULAR: F is the ROI (== grid) with a ((kh-1)/2, (kw-1)/2) halo that holds
+//                 zeros (SAME) or the wrapped interior (CIRCULAR).
+// conv_VALID(F, G) then equals conv_SAME(roi, G) + Delta_border of the reference
+// (neurocell/propagator.py:1-12 identity) when F's ring holds border_2d.
+struct Geo {
+  int H, W, kh, kw, K, M, d, padding;
+  int pad_h, pad_w;        // grid -> ROI offset (topology.pad_h / pad_w)
+  int roi_h, roi_w, P;     // ROI size and pixel count
+  int Fh, Fw, Fs;          // field height, width, row stride (floats)
+  int oh, ow;              // ROI origin inside F
+  int gr, gc;              // grid origin inside F (VALID: 0,0; else oh,ow)
+  int n_in, n_out;
+  int act, fact;
+  float slope, fslope;
+  int norm, hard_pin, gated;
+  int F_elems;             // floats of one field buffer (incl. slack rows)
+};
+
+nc_status make_geo(const nc_topo* t, Geo* g);
+
+// Offsets (bytes) of the plan buffer sections.
+struct PlanLayout {
+  size_t in_index, out_index, io_mask, out_w_mask, total;
+};
+PlanLayout plan_layout(const nc_topo* t);
+
+// Offsets (bytes) of the workspace sections; 0-sized sections have offset SIZE_MAX.
+struct WsLayout {
+  // step parameters (pre-step fusion output)
+  size_t weff, seff, broi, border, sprob, dsprob, wpinned, geff;
+  // forward residuals (train)
+  size_t xsave, zhat, rstd;
+  // scratch when on-chip buffers do not fit
+  size_t fscr, zscr, gzscr;
+  // backward partials and reductions
+  size_t gpix, gdpart, gdelta, gsum, gdsum, gdeltasum, gborder;
+  size_t total;
+};
+WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* z_smem,
+                   bool* gz_smem);
+
+}  // namespace nc

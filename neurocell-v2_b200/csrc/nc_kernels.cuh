@@ -1,0 +1,56 @@
+// nc_kernels.cuh -- argument blocks of the VNN kernels.
+#pragma once
+
+#include "nc_internal.h"
+
+namespace nc {
+
+constexpr int kFusedThreads = 512;
+
+struct StepParams {           // pre-step fusion output (neurocell/params.py:104-135)
+  float* weff;                // (P)  (1/M) * W_pinned * (1 - s)      on the ROI
+  float* seff;                // (P)  (1/M) * s                       on the ROI
+  float* broi;                // (P)  B                               on the ROI
+  float* border;              // (H*W) act(B) * s  (VALID ring values)
+  float* sprob;               // (H*W) s_prob
+  float* dsprob;              // (H*W) d s_prob / d S_raw (surrogate)
+  float* wpinned;             // (H*W) W with the output port pinned to 1
+  float* geff;                // (M*K) filters (sigmoid-gated when requested)
+};
+
+struct FwdArgs {
+  Geo g;
+  StepParams sp;
+  const int32_t* in_index;    // (n_in) flat grid index, -1 = dropped
+  const int32_t* out_index;   // (n_out) flat grid index
+  const float* inputs;        // (B, n_in)
+  float* out;                 // (B, n_out)
+  float* xsave;               // train: (B, d-1, P) field interior entering step t>=1
+  float* zhat;                // train: (B, d, M, P) standardised planes
+  float* rstd;                // train: (B, d, M)
+  float* fscr;                // (B, F_elems) field scratch when F is not on-chip
+  float* zscr;                // (B, M, P) plane scratch when z is not on-chip (inference)
+  int train, g_smem, f_smem, z_smem;
+  int batch;
+};
+
+struct BwdArgs {
+  Geo g;
+  StepParams sp;
+  const int32_t* in_index;
+  const int32_t* out_index;
+  const float* inputs;
+  const float* gout;          // (B, n_out)
+  const float* xsave;
+  const float* zhat;
+  const float* rstd;
+  float* fscr;
+  float* gzscr;               // (B, M, P) when gz is not on-chip
+  float* gpix;                // (B, 3, P) per-sample partials + (B, P) dX plane after them
+  float* gdpart;              // (B, M*K) per-sample filter-gradient partials
+  float* gdelta;              // (B, M, P) per-sample sum over t>=1 of gz (VALID, d>1)
+  int g_smem, f_smem, gz_smem;
+  int batch;
+};
+
+}  // namespace nc

@@ -1,0 +1,112 @@
+// nc_layout.cu -- geometry derivation, validation and buffer layouts (host code).
+#include <stdio.h>
+#include <string.h>
+
+#include "nc_internal.h"
+#include "nc_errors.h"
+
+namespace nc {
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+nc_status make_geo(const nc_topo* t, Geo* g) {
+  if (!t) return set_error(NC_ERR_INVALID, "topology pointer is null");
+  if (t->H <= 0 || t->W <= 0) return set_error(NC_ERR_INVALID, "grid must be positive, got %dx%d", t->H, t->W);
+  if (t->kh <= 0 || t->kw <= 0 || (t->kh % 2) == 0 || (t->kw % 2) == 0)
+    return set_error(NC_ERR_INVALID, "Green's function kernel_size must be odd, got (%d, %d)", t->kh, t->kw);
+  if (t->M <= 0) return set_error(NC_ERR_INVALID, "directions must be >= 1, got %d", t->M);
+  if (t->depth <= 0) return set_error(NC_ERR_INVALID, "depth must be >= 1, got %d", t->depth);
+  if (t->padding < NC_PAD_VALID || t->padding > NC_PAD_CIRCULAR)
+    return set_error(NC_ERR_INVALID, "unsupported padding_mode id %d", t->padding);
+  if (t->act < NC_ACT_NONE || t->act > NC_ACT_GELU || t->final_act < NC_ACT_NONE || t->final_act > NC_ACT_GELU)
+    return set_error(NC_ERR_INVALID, "unsupported activation id (%d, %d)", t->act, t->final_act);
+  if (t->n_in < 0 || t->n_out <= 0) return set_error(NC_ERR_INVALID, "bad port sizes n_in=%d n_out=%d", t->n_in, t->n_out);
+  memset(g, 0, sizeof(*g));
+  g->H = t->H; g->W = t->W; g->kh = t->kh; g->kw = t->kw; g->K = t->kh * t->kw;
+  g->M = t->M; g->d = t->depth; g->padding = t->padding;
+  if (t->padding == NC_PAD_VALID) {
+    g->pad_h = (t->kh - 1) / 2;
+    g->pad_w = (t->kw - 1) / 2;
+  }
+  g->roi_h = t->H - 2 * g->pad_h;
+  g->roi_w = t->W - 2 * g->pad_w;
+  if (g->roi_h <= 0 || g->roi_w <= 0)
+    return set_error(NC_ERR_INVALID, "grid (%d, %d) is too small for kernel (%d, %d)", t->H, t->W, t->kh, t->kw);
+  g->P = g->roi_h * g->roi_w;
+  g->Fh = g->roi_h + t->kh - 1;
+  g->Fw = g->roi_w + t->kw - 1;
+  g->Fs = ((g->Fw + 4) + 3) & ~3;   // >= 4 floats of slack per row for strip over-reads
+  g->oh = (t->kh - 1) / 2;
+  g->ow = (t->kw - 1) / 2;
+  if (t->padding == NC_PAD_VALID) { g->gr = 0; g->gc = 0; } else { g->gr = g->oh; g->gc = g->ow; }
+  g->n_in = t->n_in; g->n_out = t->n_out;
+  g->act = t->act; g->fact = t->final_act;
+  g->slope = t->act_slope; g->fslope = t->final_act_slope;
+  g->norm = t->norm ? 1 : 0; g->hard_pin = t->hard_pin_io ? 1 : 0; g->gated = t->gated_filters ? 1 : 0;
+  g->F_elems = (g->Fh + 1) * g->Fs;   // one slack row
+  const double total_px = (double)g->M * (double)g->P;
+  if (total_px > 2.0e9) return set_error(NC_ERR_UNSUPPORTED, "plane too large (%g values)", total_px);
+  return NC_OK;
+}
+
+PlanLayout plan_layout(const nc_topo* t) {
+  PlanLayout L;
+  size_t o = 0;
+  L.in_index = o; o = align256(o + sizeof(int32_t) * (size_t)(t->n_in > 0 ? t->n_in : 1));
+  L.out_index = o; o = align256(o + sizeof(int32_t) * (size_t)t->n_out);
+  L.io_mask = o; o = align256(o + (size_t)t->H * t->W);
+  L.out_w_mask = o; o = align256(o + (size_t)t->H * t->W);
+  L.total = o;
+  return L;
+}
+
+WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* z_smem,
+                   bool* gz_smem) {
+  const bool train = (flags & NC_FLAG_TRAIN) != 0;
+  const size_t B = (size_t)batch, P = (size_t)g.P, M = (size_t)g.M, HW = (size_t)g.H * g.W;
+  const size_t fl = sizeof(float);
+  // on-chip policy (fixed budget so workspace sizes do not depend on the device)
+  const size_t budget = kSmemBudget;
+  const size_t base = fl * ((size_t)g.M * g.K + 4 * (size_t)g.M + 128);
+  const size_t fbytes = fl * (size_t)g.F_elems;
+  const bool fs = base + fbytes <= budget;
+  const bool zs = fs && base + fbytes + fl * M * P <= budget;
+  const bool gzs = fs && base + fbytes + fl * M * P <= budget;
+  if (f_smem) *f_smem = fs;
+  if (z_smem) *z_smem = zs;
+  if (gz_smem) *gz_smem = gzs;
+
+  WsLayout L;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t r = o; o = align256(o + (bytes ? bytes : 1)); return r; };
+  L.weff = take(fl * P);
+  L.seff = take(fl * P);
+  L.broi = take(fl * P);
+  L.border = take(fl * HW);
+  L.sprob = take(fl * HW);
+  L.dsprob = take(fl * HW);
+  L.wpinned = take(fl * HW);
+  L.geff = take(fl * M * g.K);
+  const size_t dm1 = (size_t)(g.d > 1 ? g.d - 1 : 0);
+  L.xsave = train ? take(fl * B * (dm1 ? dm1 : 1) * P) : SIZE_MAX;
+  L.zhat = train ? take(fl * B * g.d * M * P) : SIZE_MAX;
+  L.rstd = train ? take(fl * B * g.d * M) : SIZE_MAX;
+  L.fscr = fs ? SIZE_MAX : take(fl * B * g.F_elems);
+  L.zscr = (!train && !zs) ? take(fl * B * M * P) : SIZE_MAX;
+  if (train) {
+    L.gzscr = gzs ? SIZE_MAX : take(fl * B * M * P);
+    L.gpix = take(fl * B * 3 * P + fl * B * P);   // 3 partial planes + dX output plane
+    L.gdpart = take(fl * B * M * g.K);
+    L.gdelta = (g.padding == NC_PAD_VALID && g.d > 1) ? take(fl * B * M * P) : SIZE_MAX;
+    L.gsum = take(fl * 3 * P);
+    L.gdsum = take(fl * M * g.K);
+    L.gdeltasum = (g.padding == NC_PAD_VALID && g.d > 1) ? take(fl * M * P) : SIZE_MAX;
+    L.gborder = take(fl * HW);
+  } else {
+    L.gzscr = L.gpix = L.gdpart = L.gdelta = L.gsum = L.gdsum = L.gdeltasum = L.gborder = SIZE_MAX;
+  }
+  L.total = o;
+  return L;
+}
+
+}  // namespace nc

@@ -1,0 +1,225 @@
+"""Minimal training / evaluation engine around the B200 propagation path.
+
+Mirrors the parts of ``neurocell/trainer.py`` that drive the hot path:
+``compute_annealed_temperature`` (trainer.py:23-46), ``default_mse_loss`` (57-61),
+``packbits_u8_on_device`` (49-54) and a ``VNNTrainer`` whose ``train_step`` is
+value_and_grad + SGD (trainer.py:101-106 with optax.sgd).  Optimizers other than SGD,
+``lax.scan`` epochs and adaptive caches are not part of the B200 hot path.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import ops
+from .params import VNNParams
+
+
+def compute_annealed_temperature(epoch: int, total_epochs: int, init_temp: float = 1.0,
+                                 final_temp: float = 0.1, schedule: str = "exponential") -> float:
+    if total_epochs <= 1:
+        return float(final_temp)
+    progress = min(1.0, max(0.0, float(epoch) / float(total_epochs - 1)))
+    if schedule == "exponential":
+        return float(init_temp * ((final_temp / init_temp) ** progress))
+    if schedule == "cosine":
+        return float(final_temp + (init_temp - final_temp) * 0.5 * (1.0 + math.cos(math.pi * progress)))
+    if schedule == "linear":
+        return float(init_temp + (final_temp - init_temp) * progress)
+    raise ValueError(
+        f"Unsupported temperature schedule '{schedule}'; choose from ('exponential', 'cosine', 'linear').")
+
+
+def default_mse_loss(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+    """Mean squared error (trainer.py:57-61), evaluated by the CUDA library."""
+    return ops.mse_loss(logits, targets)
+
+
+def softmax_cross_entropy_loss(logits: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+    return ops.softmax_ce_loss(logits, labels)
+
+
+BIT_WEIGHTS_U8 = (128, 64, 32, 16, 8, 4, 2, 1)
+
+
+def packbits_u8_on_device(bits: torch.Tensor) -> torch.Tensor:
+    w = torch.tensor(BIT_WEIGHTS_U8, dtype=torch.int32, device=bits.device)
+    return (bits.to(torch.int32) * w).sum(-1, keepdim=True).to(torch.uint8)
+
+
+class VNNTrainStep:
+    """One fused training step over static device buffers: forward, loss, backward,
+    optional data-parallel gradient all-reduce, SGD update.
+
+    Parameters live in one packed device buffer ``[cell_params (3HW) | filters (MK)]`` and
+    gradients in a second one, so the data-parallel exchange is a single all-reduce of
+    3HW+MK floats (16,316 for the ALU chip).  ``step(x, y)`` copies the batch into the
+    static input buffers (host tensors: from pinned memory, asynchronously) and returns the
+    device loss.  ``capture()`` records the launch sequence into a CUDA graph (single
+    process only).  Every launch goes through ``libneurocell_b200.so``.
+    """
+
+    def __init__(self, topology, params: VNNParams, batch_size: int, lr: float = 1e-2,
+                 loss: str = "mse", activate=torch.tanh, final_activate=None, norm: bool = True,
+                 hard_pin_io: bool = False, gated_filters: bool = False,
+                 codd_mode: str = "continuous", state_temperature: float = 1.0,
+                 active_threshold: float = 0.6, in_shapes=None, process_group=None):
+        import ctypes
+        from . import _lib
+        from .params import check_codd_mode
+        check_codd_mode(codd_mode)
+        if loss not in ("mse", "ce"):
+            raise ValueError(f"Unsupported loss '{loss}'; choose from ('mse', 'ce').")
+        dev = params.cell_params.device
+        ops._require_cuda(params.cell_params, "params.cell_params")
+        act, slope = ops.resolve_activation(activate)
+        fact, fslope = ops.resolve_activation(final_activate)
+        if in_shapes is None:
+            in_shapes = tuple(tuple(p.size) if not hasattr(p, "num_points") else (p.num_points,)
+                              for p in topology.in_ports)
+        self.plan = ops.get_plan(topology, tuple(in_shapes), dev, act, slope, fact, fslope, norm,
+                                 hard_pin_io, gated_filters)
+        self.lib = _lib.load()
+        self._lib = _lib
+        self.ctypes = ctypes
+        self.device = dev
+        self.B = int(batch_size)
+        self.lr = float(lr)
+        self.loss_kind = loss
+        self.pg = process_group
+        self.world = 1
+        if process_group is not None:
+            import torch.distributed as dist
+            self.world = dist.get_world_size(process_group)
+        H, W = topology.grid_shape
+        self.n_cell = 3 * H * W
+        self.n_filt = int(params.greens_filters.numel())
+        self.flat = torch.empty(self.n_cell + self.n_filt, dtype=torch.float32, device=dev)
+        self.flat[: self.n_cell].copy_(params.cell_params.reshape(-1))
+        self.flat[self.n_cell:].copy_(params.greens_filters.reshape(-1))
+        self.grads = torch.zeros_like(self.flat)
+        self.params = VNNParams(self.flat[: self.n_cell].view(params.cell_params.shape),
+                                self.flat[self.n_cell:].view(params.greens_filters.shape))
+        self.ws_bytes = self.lib.nc_workspace_bytes(ctypes.byref(self.plan.topo), self.B,
+                                                    _lib.NC_FLAG_TRAIN)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+        self.x = torch.zeros((self.B, self.plan.n_in), dtype=torch.float32, device=dev)
+        if loss == "mse":
+            self.y = torch.zeros((self.B, self.plan.n_out), dtype=torch.float32, device=dev)
+        else:
+            self.y = torch.zeros((self.B,), dtype=torch.int32, device=dev)
+        self.out = torch.empty((self.B, self.plan.n_out), dtype=torch.float32, device=dev)
+        self.g_out = torch.empty_like(self.out)
+        self.loss = torch.zeros((), dtype=torch.float32, device=dev)
+        self.codd = ops._codd(codd_mode, state_temperature, active_threshold)
+        self.graph = None
+
+    # number of library kernel launches per step (for the bench's launch count)
+    def launches_per_step(self) -> int:
+        t = self.plan.topo
+        bwd = 1 + 2 + (2 if (t.padding == 0 and t.depth > 1) else 0) + 1
+        return 2 + 1 + bwd + 1
+
+    def set_temperature(self, tau: float) -> None:
+        self.codd.temperature = float(tau)
+
+    def _launch(self) -> None:
+        c, lib, P = self.ctypes, self.lib, ops._ptr
+        st = ops._stream(self.device)
+        t = c.byref(self.plan.topo)
+        cell = self.flat.data_ptr()
+        filt = cell + 4 * self.n_cell
+        gcell = self.grads.data_ptr()
+        gfilt = gcell + 4 * self.n_cell
+        self._lib.check(lib.nc_vnn_forward(t, P(self.plan.buf), c.c_void_p(cell), c.c_void_p(filt),
+                                           P(self.x), self.B, c.byref(self.codd),
+                                           self._lib.NC_FLAG_TRAIN, P(self.out), P(self.ws),
+                                           self.ws_bytes, st), "nc_vnn_forward")
+        if self.loss_kind == "mse":
+            self._lib.check(lib.nc_mse_loss(P(self.out), P(self.y), self.B, self.plan.n_out,
+                                            P(self.loss), P(self.g_out), st), "nc_mse_loss")
+        else:
+            self._lib.check(lib.nc_softmax_ce_loss(P(self.out), P(self.y), self.B, self.plan.n_out,
+                                                   P(self.loss), P(self.g_out), st),
+                            "nc_softmax_ce_loss")
+        self._lib.check(lib.nc_vnn_backward(t, P(self.plan.buf), c.c_void_p(cell), c.c_void_p(filt),
+                                            P(self.x), self.B, c.byref(self.codd), P(self.g_out),
+                                            c.c_void_p(gcell), c.c_void_p(gfilt), P(self.ws),
+                                            self.ws_bytes, st), "nc_vnn_backward")
+        lr = self.lr
+        if self.pg is not None:
+            import torch.distributed as dist
+            dist.all_reduce(self.grads, group=self.pg)
+            lr = self.lr / self.world       # mean of the per-rank mean-loss gradients
+        self._lib.check(lib.nc_sgd_update(c.c_void_p(cell), c.c_void_p(gcell),
+                                          self.n_cell + self.n_filt, lr, st), "nc_sgd_update")
+
+    def load_batch(self, x: torch.Tensor, y: torch.Tensor) -> None:
+        self.x.copy_(x.reshape(self.B, -1), non_blocking=True)
+        self.y.copy_(y.reshape(self.y.shape), non_blocking=True)
+
+    def step(self, x: torch.Tensor | None = None, y: torch.Tensor | None = None) -> torch.Tensor:
+        if x is not None:
+            self.load_batch(x, y)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._launch()
+        return self.loss
+
+    def capture(self) -> None:
+        if self.pg is not None:
+            raise NotImplementedError("graph capture is single-process only")
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        saved = self.flat.clone()
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._launch()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._launch()
+        self.flat.copy_(saved)             # warm-up and capture must not move the parameters
+        self.graph = g
+
+
+class VNNTrainer:
+    """value_and_grad + SGD over ``apply_fn`` (trainer.py:71-106, optimizer = SGD(lr))."""
+
+    def __init__(self, apply_fn, lr: float = 1e-2, batch_size: int = 128, loss_fn=None):
+        self.apply_fn = apply_fn
+        self.lr = float(lr)
+        self.batch_size = batch_size
+        self.loss_fn = loss_fn or default_mse_loss
+
+    def value_and_grad(self, params: VNNParams, batch_x, batch_y, **apply_kw):
+        cp = params.cell_params.detach().requires_grad_(True)
+        fl = params.greens_filters.detach().requires_grad_(True)
+        out = self.apply_fn(VNNParams(cp, fl), batch_x, **apply_kw)
+        loss = self.loss_fn(out, batch_y)
+        g_cp, g_fl = torch.autograd.grad(loss, (cp, fl))
+        return loss.detach(), VNNParams(g_cp, g_fl)
+
+    def train_step(self, params: VNNParams, batch_x, batch_y, **apply_kw):
+        """Returns ``(new_params, loss)``; the update runs in place on ``params``' storage."""
+        loss, grads = self.value_and_grad(params, batch_x, batch_y, **apply_kw)
+        with torch.no_grad():
+            ops.sgd_(params.cell_params, grads.cell_params, self.lr)
+            ops.sgd_(params.greens_filters, grads.greens_filters, self.lr)
+        return params, loss
+
+    @torch.no_grad()
+    def evaluate_packed(self, params: VNNParams, x_batches, y_packed_batches, **apply_kw):
+        """Packed 8-bit exact-match accuracy (trainer.py:122-138)."""
+        acc = 0.0
+        preds = []
+        for bx, by in zip(x_batches, y_packed_batches):
+            logits = self.apply_fn(params, bx, **apply_kw)
+            if logits.ndim == 3 and logits.shape[-1] == 1:
+                logits = logits[..., 0]
+            p = packbits_u8_on_device(torch.round(logits).clamp(0, 255).to(torch.uint8))
+            acc += float((p.reshape(by.shape) == by).float().mean())
+            preds.append(p)
+        return acc / max(1, len(preds)), preds

@@ -1,0 +1,229 @@
+"""GPU parity tests: the CUDA path (through the C ABI) against the float64 oracle.
+
+Tolerance (north_star): relative L2 <= 1e-5 for outputs, loss and both parameter
+gradients; discrete ste_ternary states must match exactly.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import neurocell_b200 as nc
+from oracle import vnn_oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+ACT = {None: None, "tanh": torch.tanh, "sigmoid": torch.sigmoid, "relu": torch.relu,
+       "leaky_relu": "leaky_relu", "gelu": "gelu", "identity": "identity"}
+
+
+def _rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _to_nc_port(p):
+    if isinstance(p, O.CoordPort):
+        return nc.CoordinatePortSpec(p.coords, p.name)
+    return nc.PortSpec(p.offset, p.size, p.name)
+
+
+def _nc_topo(g: O.Geometry):
+    return nc.ChipTopology2D.create(g.grid_shape, g.kernel_size, g.directions, g.depth,
+                                    tuple(_to_nc_port(p) for p in g.in_ports),
+                                    _to_nc_port(g.out_port), padding_mode=g.padding_mode)
+
+
+def run_gpu(geom, cfg, cell, filt, inputs, targets, loss="mse", train=True):
+    topo = _nc_topo(geom)
+    dev = torch.device("cuda:0")
+    cp = torch.tensor(cell, dtype=torch.float32, device=dev, requires_grad=train)
+    fl = torch.tensor(filt, dtype=torch.float32, device=dev, requires_grad=train)
+    if isinstance(inputs, (list, tuple)):
+        xin = [torch.tensor(np.asarray(a), dtype=torch.float32, device=dev) for a in inputs]
+    else:
+        xin = torch.tensor(inputs, dtype=torch.float32, device=dev)
+    out = nc.propagate_vnn_2d(
+        nc.VNNParams(cp, fl), xin, topo, activate=ACT[cfg.activate],
+        final_activate=ACT[cfg.final_activate], norm=cfg.norm, gated_filters=cfg.gated_filters,
+        hard_pin_io=cfg.hard_pin_io, codd_mode=cfg.codd_mode,
+        state_temperature=cfg.state_temperature, active_threshold=cfg.active_threshold)
+    if not train:
+        return out.detach().cpu().numpy(), None, None, None
+    y = torch.tensor(np.asarray(targets), device=dev)
+    L = nc.ops.mse_loss(out, y.float()) if loss == "mse" else nc.ops.softmax_ce_loss(out, y)
+    L.backward()
+    torch.cuda.synchronize()
+    return (out.detach().cpu().numpy(), float(L), cp.grad.cpu().numpy(), fl.grad.cpu().numpy())
+
+
+def run_oracle(geom, cfg, cell, filt, inputs, targets, loss="mse"):
+    out, tape = O.forward(cell, filt, inputs, geom, cfg)
+    lval, gout = O.mse_loss(out, targets) if loss == "mse" else O.softmax_ce_loss(out, targets)
+    gc, gf = O.backward(gout, tape, geom, cfg)
+    return out, lval, gc, gf
+
+
+def check_case(geom, cfg, cell, filt, inputs, targets, loss="mse", tol=TOL):
+    o_g, l_g, gc_g, gf_g = run_gpu(geom, cfg, cell, filt, inputs, targets, loss)
+    o_r, l_r, gc_r, gf_r = run_oracle(geom, cfg, cell, filt, inputs, targets, loss)
+    errs = dict(out=_rel(o_g, o_r), loss=abs(l_g - l_r) / max(abs(l_r), 1e-30),
+                g_cell=_rel(gc_g, gc_r), g_filters=_rel(gf_g, gf_r))
+    bad = {k: v for k, v in errs.items() if not v <= tol}
+    assert not bad, f"parity failure {bad} (all: {errs})"
+    return errs
+
+
+def alu_problem(B, seed, codd="continuous", tau=1.0, s_uniform=False):
+    """Config-0 synthetic distribution: W,B,S ~ N(0,0.1); filters ~ N(0, 1/sqrt(299))."""
+    rng = np.random.default_rng(seed)
+    geom = O.alu_geometry()
+    cell = rng.normal(0, 0.1, (3, 62, 62)).astype(np.float32)
+    if s_uniform:
+        u = rng.uniform(1e-6, 1 - 1e-6, (62, 62))
+        cell[2] = np.log(u / (1 - u)).astype(np.float32)
+    filt = (rng.normal(0, 1, (16, 1, 23, 13)) / np.sqrt(299)).astype(np.float32)
+    x, y, _ = O.alu_batch(rng, B, noise=0.0)
+    return geom, O.Config(codd_mode=codd, state_temperature=tau), cell, filt, x, y
+
+
+def random_problem(geom, B, seed, pscale=0.3, fscale=None, loss="mse"):
+    rng = np.random.default_rng(seed)
+    H, W = geom.grid_shape
+    kh, kw = geom.kernel_size
+    cell = rng.normal(0, pscale, (3, H, W)).astype(np.float32)
+    fscale = fscale if fscale is not None else 1.0 / np.sqrt(kh * kw)
+    filt = rng.normal(0, fscale, (geom.directions, 1, kh, kw)).astype(np.float32)
+    ins = [rng.normal(size=(B,) + tuple(p.size)).astype(np.float32) for p in geom.in_ports]
+    n_out = int(np.prod(geom.out_port.size))
+    y = (rng.normal(size=(B, n_out)).astype(np.float32) if loss == "mse"
+         else rng.integers(0, n_out, size=B).astype(np.int32))
+    return cell, filt, ins, y
+
+
+# ---- BASELINE config 0 shape: ALU train step ------------------------------------------
+@pytest.mark.parametrize("codd,tau", [("continuous", 1.0), ("annealed", 0.4),
+                                      ("ste_binary", 0.3), ("ste_ternary", 0.3)])
+def test_alu_train_step_parity(codd, tau):
+    geom, cfg, cell, filt, x, y = alu_problem(16, 100, codd, tau)
+    check_case(geom, cfg, cell, filt, x, y)
+
+
+def test_alu_train_step_parity_full_batch():
+    geom, cfg, cell, filt, x, y = alu_problem(128, 7)
+    check_case(geom, cfg, cell, filt, x, y)
+
+
+# ---- BASELINE config 1 shape: ALU inference, ste_ternary, sigma(S) uniform --------------
+def test_alu_inference_ste_ternary_and_exact_roles():
+    geom, cfg, cell, filt, x, y = alu_problem(256, 11, "ste_ternary", 1.0, s_uniform=True)
+    o_g, *_ = run_gpu(geom, cfg, cell, filt, x, y, train=False)
+    o_r, _ = O.forward(cell, filt, x, geom, cfg)
+    assert _rel(o_g, o_r) <= TOL
+    topo = _nc_topo(geom)
+    s_gpu = nc.compute_codd_state_probs(torch.tensor(cell[2], device="cuda"), topo.io_state_mask,
+                                        codd_mode="ste_ternary", state_temperature=1.0,
+                                        active_threshold=0.6).cpu().numpy()
+    s_ref, _ = O.codd_state_probs(cell[2], geom.io_state_mask, codd_mode="ste_ternary")
+    assert np.array_equal(s_gpu, s_ref.astype(np.float32))      # exact discrete roles
+    assert set(np.unique(s_gpu)).issubset({0.0, 0.5, 1.0})
+
+
+def test_ste_ternary_zero_threshold_gap():
+    """Outputs with raw states equal outputs with their thresholded roles, bit for bit
+    (tests/unit_milestone8_pallas_and_codd.py:235-252)."""
+    geom, cfg, cell, filt, x, y = alu_problem(32, 12, "ste_ternary", 0.25, s_uniform=True)
+    o1, *_ = run_gpu(geom, cfg, cell, filt, x, y, train=False)
+    roles = O.threshold_states(cell[2], 0.6)
+    cell2 = cell.copy()
+    cell2[2] = np.where(roles >= 2.0, 1.0, np.where(roles > 0.0, 0.3, -1.0))
+    o2, *_ = run_gpu(geom, cfg, cell2, filt, x, y, train=False)
+    assert np.array_equal(o1, o2)
+
+
+# ---- BASELINE config 2 shape (SAME, K=31^2, M=16), reduced grid -------------------------
+def test_same_mode_large_kernel_parity():
+    geom = O.make_geometry(48, (31, 31), 16, 3, (O.CoordPort(tuple((r, 12) for r in range(16, 32))),),
+                           O.CoordPort(tuple((r, 36) for r in range(20, 28))), padding_mode="SAME")
+    cell, filt, ins, y = random_problem(geom, 2, 21)
+    check_case(geom, O.Config(), cell, filt, ins, y)
+
+
+# ---- BASELINE config 3 shape (96^2, K=15^2, border inputs, CE); planes exceed smem -----
+def test_image_classifier_shape_parity():
+    ports = (O.RectPort((0, 32), (32, 32)), O.RectPort((32, 32), (32, 32)), O.RectPort((64, 32), (32, 32)))
+    out = O.CoordPort(tuple((r, 80) for r in range(43, 53)))
+    geom = O.make_geometry(96, (15, 15), 16, 3, ports, out)
+    assert not geom.in_in_roi
+    cell, filt, ins, y = random_problem(geom, 3, 31, loss="ce")
+    check_case(geom, O.Config(), cell, filt, ins, y, loss="ce")
+
+
+# ---- BASELINE config 4 shape (VALID, K=63^2, M=32, annealed), reduced grid --------------
+def test_large_kernel_many_directions_parity():
+    geom = O.make_geometry(96, (63, 63), 32, 2, (O.CoordPort(tuple((r, 40) for r in range(40, 56))),),
+                           O.CoordPort(tuple((r, 56) for r in range(40, 56))))
+    cell, filt, ins, y = random_problem(geom, 2, 41)
+    check_case(geom, O.Config(codd_mode="annealed", state_temperature=0.5), cell, filt, ins, y)
+
+
+# ---- modes and options ------------------------------------------------------------------
+@pytest.mark.parametrize("mode", ["VALID", "SAME", "CIRCULAR"])
+@pytest.mark.parametrize("cfg", [
+    O.Config(),
+    O.Config(activate="gelu", final_activate="tanh"),
+    O.Config(activate="leaky_relu", final_activate="sigmoid", gated_filters=True),
+    O.Config(activate="relu", norm=False, hard_pin_io=True),
+    O.Config(activate=None, codd_mode="ste_binary", state_temperature=0.5),
+])
+def test_modes_and_options_parity(mode, cfg):
+    geom = O.make_geometry((20, 22), (5, 3), 4, 3, (O.RectPort((6, 5), (4, 1)),),
+                           O.RectPort((6, 14), (4, 1)), padding_mode=mode)
+    cell, filt, ins, y = random_problem(geom, 5, 51)
+    check_case(geom, cfg, cell, filt, ins, y)
+
+
+@pytest.mark.parametrize("depth", [1, 2, 5])
+def test_depth_and_border_inputs_parity(depth):
+    geom = O.make_geometry((24, 24), (7, 5), 6, depth,
+                           (O.RectPort((0, 4), (6, 6)), O.CoordPort(((12, 12), (13, 9)))),
+                           O.CoordPort(((10, 18), (11, 18), (14, 6))))
+    cell, filt, ins, y = random_problem(geom, 4, 61 + depth)
+    check_case(geom, O.Config(), cell, filt, ins, y)
+
+
+def test_backward_is_deterministic():
+    geom, cfg, cell, filt, x, y = alu_problem(32, 5)
+    a = run_gpu(geom, cfg, cell, filt, x, y)
+    b = run_gpu(geom, cfg, cell, filt, x, y)
+    for u, v in zip(a, b):
+        assert np.array_equal(np.asarray(u), np.asarray(v))
+
+
+# ---- functional known answer: the reference's trained checkpoint ------------------------
+def test_trained_checkpoint_accuracy_on_gpu():
+    params = nc.VonNeumannNetwork.load_checkpoint(os.path.join(GOLDEN, "alu_trained_cells.npz"))
+    with np.load(os.path.join(GOLDEN, "alu_trained_eval.npz")) as d:
+        x, packed, out_ref = d["inputs"], d["packed"], d["out_f64"]
+    model = nc.VonNeumannNetwork(nc.ChipTopology2D.alu_chip(), codd_mode="ste_ternary",
+                                 state_temperature=0.2)
+    with torch.no_grad():
+        out = model.apply(params, torch.tensor(x, device="cuda")).cpu().numpy()
+    assert _rel(out, out_ref) <= TOL
+    pred = np.packbits(np.clip(np.round(out[:, :, 0]), 0, 255).astype(np.uint8), axis=1)[:, 0]
+    assert float((pred == packed).mean()) >= 0.97
+
+
+def test_sgd_step_matches_oracle():
+    geom, cfg, cell, filt, x, y = alu_problem(16, 9)
+    topo = _nc_topo(geom)
+    p = nc.VNNParams(torch.tensor(cell, device="cuda"), torch.tensor(filt, device="cuda"))
+    tr = nc.VNNTrainer(lambda prm, bx: nc.propagate_vnn_2d(prm, bx, topo), lr=1e-2)
+    _, loss = tr.train_step(p, torch.tensor(x, device="cuda"), torch.tensor(y, device="cuda"))
+    lval, new_cell, new_filt, _, _ = O.train_step(cell, filt, x, y, geom, O.Config(), lr=1e-2)
+    assert abs(float(loss) - lval) / lval <= TOL
+    assert _rel(p.cell_params.cpu().numpy() - cell, new_cell - cell) <= TOL
+    assert _rel(p.greens_filters.cpu().numpy() - filt, new_filt - filt) <= TOL
