@@ -238,6 +238,10 @@ def run_b200(args) -> None:
     K = args.steps
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     kev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    for row in kev:            # torch creates the CUDA event on first record
+        for e in row:
+            e.record()
+    torch.cuda.synchronize()
     clocks = ClockSampler(local)
     barrier()
     torch.cuda.synchronize()
