@@ -138,6 +138,27 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
                           const nc_codd* codd, const float* g_out, float* g_cell_params,
                           float* g_filters, void* d_ws, size_t ws_bytes, void* stream);
 
+/*
+ * nc_vnn_forward_static -- no counterpart in the reference.  Inference forward (flags 0)
+ * that takes no workspace: its scratch is a static device array of
+ * NC_STATIC_SCRATCH_BYTES inside this library, held on every GPU that loads the library
+ * until the process exits.  It is for callers that cannot call cudaMalloc: an XLA FFI
+ * custom call whose framework already owns nearly all device memory, code running while a
+ * stream is being captured, hosts that forbid allocation after start-up.  The caller
+ * still allocates the plan, parameters, inputs and outputs.
+ *   - Returns NC_ERR_WORKSPACE when nc_workspace_bytes(topo, batch, 0) exceeds the limit.
+ *   - The first call on a device resolves the array's device address (with that device
+ *     current); make that first call before any stream capture.
+ *   - All calls share the one array, which keeps the previous call's contents; nothing in
+ *     it has to start at zero.  Calls that overlap on the GPU (other streams, concurrent
+ *     graph replays) race on it and must be serialised by the caller.
+ *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library routine.
+ */
+#define NC_STATIC_SCRATCH_BYTES (8u * 1024u * 1024u)
+nc_status nc_vnn_forward_static(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                                const float* filters, const float* inputs, int32_t batch,
+                                const nc_codd* codd, float* out, void* stream);
+
 /* Effective Codd states s_prob (H,W) (params.py:31-80); d_plan supplies io_mask. */
 nc_status nc_codd_states(const nc_topo* topo, const void* d_plan, const float* states_raw,
                          const nc_codd* codd, float* s_prob, void* stream);

@@ -25,7 +25,7 @@ EXPORTED = (
     "nc_plan_bytes", "nc_plan_build", "nc_workspace_bytes", "nc_vnn_forward",
     "nc_vnn_backward", "nc_codd_states", "nc_mse_loss", "nc_softmax_ce_loss",
     "nc_sgd_update", "nc_last_error", "nc_abi_version", "nc_set_profile_events",
-    "nc_fp32_peak_probe",
+    "nc_fp32_peak_probe", "nc_vnn_forward_static",
 )
 
 
@@ -63,6 +63,7 @@ _SIGS = {
     "nc_mse_loss": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp]),
     "nc_softmax_ce_loss": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp]),
     "nc_sgd_update": (_i32, [_vp, _vp, _i64, _f32, _vp]),
+    "nc_vnn_forward_static": (_i32, [_TP, _vp, _vp, _vp, _vp, _i32, _CP, _vp, _vp]),
     "nc_set_profile_events": (None, [_vp, _vp, _vp, _vp]),
     "nc_fp32_peak_probe": (_i32, [_i32, ctypes.POINTER(ctypes.c_double), _vp, _vp]),
     "nc_last_error": (ctypes.c_char_p, []),
