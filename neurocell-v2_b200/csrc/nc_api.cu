@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include "nc_errors.h"
+#include "nc_fast.cuh"
 #include "nc_internal.h"
 #include "nc_kernels.cuh"
 
@@ -256,11 +257,16 @@ nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* c
     return set_error(NC_ERR_UNSUPPORTED, "field does not fit on chip and no scratch was laid out");
   if (!a.z_smem && !train && !a.zscr)
     return set_error(NC_ERR_UNSUPPORTED, "planes do not fit on chip and no scratch was laid out");
-  const size_t smem = fused_smem_bytes(pr.g, a.g_smem, a.f_smem, a.z_smem);
-  NC_CHECK(set_smem_attr((const void*)vnn_fused_fwd_kernel, smem));
+  const FastKernels fk = fast_kernels(pr.g);
+  const void* fn = fk.fwd ? fk.fwd : (const void*)vnn_fused_fwd_kernel;
+  const size_t smem = fk.fwd ? fk.fwd_smem : fused_smem_bytes(pr.g, a.g_smem, a.f_smem, a.z_smem);
+  NC_CHECK(set_smem_attr(fn, smem));
   if (g_prof.fs) NC_CUDA_CHECK(cudaEventRecord(g_prof.fs, st));
-  vnn_fused_fwd_kernel<<<batch, kFusedThreads, smem, st>>>(a);
-  NC_CHECK(launch_check("vnn_fused_fwd_kernel launch"));
+  {
+    void* args[] = {&a};
+    NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(batch), dim3(kFusedThreads), args, smem, st));
+  }
+  NC_CHECK(launch_check("fused forward kernel launch"));
   if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
   clear_error();
   return NC_OK;
@@ -307,11 +313,19 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
     return set_error(NC_ERR_UNSUPPORTED, "field does not fit on chip and no scratch was laid out");
   if (!a.gz_smem && !a.gzscr)
     return set_error(NC_ERR_UNSUPPORTED, "plane gradients do not fit on chip and no scratch was laid out");
-  const size_t smem = fused_smem_bytes(g, a.g_smem, a.f_smem, a.gz_smem);
-  NC_CHECK(set_smem_attr((const void*)vnn_fused_bwd_kernel, smem));
+  const FastKernels fk = fast_kernels(g);
+  const void* fn = fk.bwd ? fk.bwd : (const void*)vnn_fused_bwd_kernel;
+  const size_t smem = fk.bwd ? fk.bwd_smem : fused_smem_bytes(g, a.g_smem, a.f_smem, a.gz_smem);
+  NC_CHECK(set_smem_attr(fn, smem));
   if (g_prof.bs) NC_CUDA_CHECK(cudaEventRecord(g_prof.bs, st));
-  vnn_fused_bwd_kernel<<<batch, kFusedThreads, smem, st>>>(a);
-  NC_CHECK(launch_check("vnn_fused_bwd_kernel launch"));
+  {
+    FastBwdLayout bl = fk.bl;
+    void* args_fast[] = {&a, &bl};
+    void* args_v1[] = {&a};
+    NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(batch), dim3(kFusedThreads), fk.bwd ? args_fast : args_v1,
+                                   smem, st));
+  }
+  NC_CHECK(launch_check("fused backward kernel launch"));
   if (g_prof.be) NC_CUDA_CHECK(cudaEventRecord(g_prof.be, st));
 
   // batch reductions (fixed order -> deterministic)
@@ -330,7 +344,7 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
     batch_sum_kernel<<<(MP + 255) / 256, 256, 0, st>>>(a.gdelta, (size_t)MP, MP, batch, gdeltasum);
     NC_CHECK(launch_check("batch_sum_kernel(delta) launch"));
     gborder = at<float>(d_ws, L.gborder);
-    border_grad_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp.geff, gdeltasum, gborder);
+    border_grad_kernel<<<(HW + 7) / 8, 256, 0, st>>>(g, pr.sp.geff, gdeltasum, gborder);
     NC_CHECK(launch_check("border_grad_kernel launch"));
   }
   prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, gsum,

@@ -55,6 +55,7 @@ __global__ void batch_sum_kernel(const float* __restrict__ in, size_t stride, in
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float acc = 0.f;
+#pragma unroll 8
   for (int b = 0; b < batch; ++b) acc += in[(size_t)b * stride + i];
   out[i] = acc;
 }
@@ -62,29 +63,36 @@ __global__ void batch_sum_kernel(const float* __restrict__ in, size_t stride, in
 // Border-template adjoint (VALID): the transposed Green's convolution of
 // gdelta = sum_b sum_{t>=1} gz evaluated on the dead ring of the grid
 // (adjoint of propagator.py:354-371).  Interior cells get 0.
+// One warp per grid cell: lanes split the (m, u, v) taps, then a fixed-order shuffle sum.
 __global__ void border_grad_kernel(Geo g, const float* __restrict__ G,
                                    const float* __restrict__ gdelta, float* __restrict__ gborder) {
   const int HW = g.H * g.W;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (i >= HW) return;
   const int fr = i / g.W, fc = i - (i / g.W) * g.W;
   const int r = fr - g.pad_h, c = fc - g.pad_w;
   if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) {
-    gborder[i] = 0.f;
+    if (lane == 0) gborder[i] = 0.f;
     return;
   }
   // dF[fr, fc] = sum_m sum_{u,v} G[m,u,v] gdelta[m, fr-u, fc-v]
   const int u_lo = max(0, fr - g.roi_h + 1), u_hi = min(g.kh - 1, fr);
   const int v_lo = max(0, fc - g.roi_w + 1), v_hi = min(g.kw - 1, fc);
+  const int nu = u_hi - u_lo + 1, nv = v_hi - v_lo + 1;
   float acc = 0.f;
-  for (int m = 0; m < g.M; ++m) {
-    const float* gd = gdelta + (size_t)m * g.P;
-    const float* Gm = G + (size_t)m * g.K;
-    for (int u = u_lo; u <= u_hi; ++u)
-      for (int v = v_lo; v <= v_hi; ++v)
-        acc = fmaf(Gm[u * g.kw + v], gd[(fr - u) * g.roi_w + (fc - v)], acc);
+  if (nu > 0 && nv > 0) {
+    const int ntap = g.M * nu * nv;
+    for (int q = lane; q < ntap; q += 32) {
+      const int m = q / (nu * nv);
+      const int rem = q - m * nu * nv;
+      const int u = u_lo + rem / nv, v = v_lo + rem % nv;
+      acc = fmaf(G[(size_t)m * g.K + u * g.kw + v],
+                 gdelta[(size_t)m * g.P + (fr - u) * g.roi_w + (fc - v)], acc);
+    }
   }
-  gborder[i] = acc;
+  acc = warp_sum(acc);
+  if (lane == 0) gborder[i] = acc;
 }
 
 // Pre-step adjoint: chain the ROI partials and the border gradient back to (W, B, S_raw)
