@@ -20,6 +20,26 @@ __global__ void prestep_kernel(Geo g, StepParams sp, const float* cell, const fl
 __global__ void codd_kernel(int HW, const float* s_raw, const uint8_t* io, int hard_pin,
                             nc_codd codd, float* out);
 __global__ void batch_sum_kernel(const float* in, size_t stride, int n, int batch, float* out);
+__global__ void batch_step_sum4_kernel(const float* in, int batch, int d, int t0, size_t slot, int n,
+                                       int bc, float* part);
+__global__ void rows_sum_kernel(const float* part, int rows, int n, float* out);
+
+// out[i] = sum_b sum_{t0<=t<d} in[(b*d+t)*slot + i] in two deterministic stages over
+// kRedChunks sample chunks (n, slot multiples of 4; `scratch` holds kRedChunks*n floats).
+static nc_status batch_step_sum(const float* in, int batch, int d, int t0, size_t slot, int n,
+                                float* out, float* scratch, cudaStream_t st) {
+  const int chunks = batch < kRedChunks ? batch : kRedChunks;
+  const int bc = (batch + chunks - 1) / chunks;
+  const int n4 = n / 4;
+  dim3 grid((n4 + 255) / 256, chunks);
+  batch_step_sum4_kernel<<<grid, 256, 0, st>>>(in, batch, d, t0, slot, n, bc, scratch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "batch_step_sum4_kernel launch");
+  rows_sum_kernel<<<(n + 255) / 256, 256, 0, st>>>(scratch, chunks, n, out);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "rows_sum_kernel launch");
+  return NC_OK;
+}
 __global__ void border_grad_kernel(Geo g, const float* G, const float* gdelta, float* gborder);
 __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* cell, const float* filters,
                                    const uint8_t* owm, const float* gsum, const float* gborder,
@@ -264,7 +284,8 @@ nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* c
   if (g_prof.fs) NC_CUDA_CHECK(cudaEventRecord(g_prof.fs, st));
   {
     void* args[] = {&a};
-    NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(batch), dim3(kFusedThreads), args, smem, st));
+    const int threads = fk.fwd ? fk.fwd_threads : kFusedThreads;
+    NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(batch), dim3(threads), args, smem, st));
   }
   NC_CHECK(launch_check("fused forward kernel launch"));
   if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
@@ -332,17 +353,28 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
   float* gsum = at<float>(d_ws, L.gsum);
   float* gdsum = at<float>(d_ws, L.gdsum);
   const int P3 = 3 * g.P, MK = g.M * g.K;
-  batch_sum_kernel<<<(P3 + 255) / 256, 256, 0, st>>>(a.gpix, (size_t)P3, P3, batch, gsum);
-  NC_CHECK(launch_check("batch_sum_kernel(pixels) launch"));
+  const int MP = g.M * g.P;
+  float* redscr = at<float>(d_ws, L.redscr);
+  if (fk.bwd) {
+    // specialised kernel: per-step pixel partials (B, d, 3, P)
+    NC_CHECK(batch_step_sum(a.gpix, batch, g.d, 0, (size_t)P3, P3, gsum, redscr, st));
+  } else {
+    batch_sum_kernel<<<(P3 + 255) / 256, 256, 0, st>>>(a.gpix, (size_t)P3, P3, batch, gsum);
+    NC_CHECK(launch_check("pixel-partial reduction launch"));
+  }
   batch_sum_kernel<<<(MK + 255) / 256, 256, 0, st>>>(a.gdpart, (size_t)MK, MK, batch, gdsum);
   NC_CHECK(launch_check("batch_sum_kernel(filters) launch"));
   float* gborder = nullptr;
   const int HW = g.H * g.W;
   if (a.gdelta) {
     float* gdeltasum = at<float>(d_ws, L.gdeltasum);
-    const int MP = g.M * g.P;
-    batch_sum_kernel<<<(MP + 255) / 256, 256, 0, st>>>(a.gdelta, (size_t)MP, MP, batch, gdeltasum);
-    NC_CHECK(launch_check("batch_sum_kernel(delta) launch"));
+    if (fk.bwd) {
+      // specialised kernel: gz of steps t >= 1 overwrote the standardised planes (B, d, M, P)
+      NC_CHECK(batch_step_sum(a.zhat, batch, g.d, 1, (size_t)MP, MP, gdeltasum, redscr, st));
+    } else {
+      batch_sum_kernel<<<(MP + 255) / 256, 256, 0, st>>>(a.gdelta, (size_t)MP, MP, batch, gdeltasum);
+      NC_CHECK(launch_check("border-gradient reduction launch"));
+    }
     gborder = at<float>(d_ws, L.gborder);
     border_grad_kernel<<<(HW + 7) / 8, 256, 0, st>>>(g, pr.sp.geff, gdeltasum, gborder);
     NC_CHECK(launch_check("border_grad_kernel launch"));

@@ -60,6 +60,34 @@ __global__ void batch_sum_kernel(const float* __restrict__ in, size_t stride, in
   out[i] = acc;
 }
 
+// Stage 1 of out[i] = sum_b sum_{t0 <= t < d} in[(b*d + t)*slot + i]: block row y sums the
+// samples [y*bc, (y+1)*bc) for 4 consecutive i (float4) into part[y][i].  n and slot are
+// multiples of 4 and the buffers 16-byte aligned.  Stage 2 adds the rows in order.
+__global__ void batch_step_sum4_kernel(const float* __restrict__ in, int batch, int d, int t0,
+                                       size_t slot, int n, int bc, float* __restrict__ part) {
+  const int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const int b0 = blockIdx.y * bc, b1 = min(batch, b0 + bc);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int b = b0; b < b1; ++b) {
+    const float* row = in + (size_t)b * d * slot + i;
+#pragma unroll 4
+    for (int t = t0; t < d; ++t) {
+      const float4 v = *reinterpret_cast<const float4*>(row + (size_t)t * slot);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+  }
+  *reinterpret_cast<float4*>(part + (size_t)blockIdx.y * n + i) = acc;
+}
+
+__global__ void rows_sum_kernel(const float* __restrict__ part, int rows, int n, float* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float acc = 0.f;
+  for (int r = 0; r < rows; ++r) acc += part[(size_t)r * n + i];
+  out[i] = acc;
+}
+
 // Border-template adjoint (VALID): the transposed Green's convolution of
 // gdelta = sum_b sum_{t>=1} gz evaluated on the dead ring of the grid
 // (adjoint of propagator.py:354-371).  Interior cells get 0.

@@ -25,259 +25,13 @@
 
 #include "nc_common.cuh"
 #include "nc_fast.cuh"
+#include "nc_fast_dev.cuh"
 #include "nc_kernels.cuh"
 
 namespace nc {
 namespace fast {
 
 using namespace fastc;
-constexpr int NT = kFusedThreads;   // 512
-
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-__device__ __forceinline__ float2 dup2(float x) { return make_float2(x, x); }
-
-// out[m] = scale * sum over the CTA of v[m], m < 16.
-__device__ __forceinline__ void sum16_block(float (&v)[M], float* red, float* out, float scale) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int m = 0; m < M; ++m) v[m] = warp_sum(v[m]);
-  if (lane == 0) {
-#pragma unroll
-    for (int m = 0; m < M; ++m) red[warp * M + m] = v[m];
-  }
-  __syncthreads();
-  if (threadIdx.x < M) {
-    float s = 0.f;
-    for (int w = 0; w < NW; ++w) s += red[w * M + threadIdx.x];
-    out[threadIdx.x] = s * scale;
-  }
-  __syncthreads();
-}
-
-// Step t=0 field (zeros + the sample's inputs), row stride `fs`, `rows` rows.
-__device__ void inject(const Geo& g, float* F, int fs, int rows, const int32_t* in_index,
-                       const float* inp) {
-  for (int i = threadIdx.x; i < rows * fs; i += NT) F[i] = 0.f;
-  __syncthreads();
-  for (int j = threadIdx.x; j < g.n_in; j += NT) {
-    const int idx = in_index[j];
-    if (idx < 0) continue;
-    const int r = idx / g.W, c = idx - (idx / g.W) * g.W;
-    F[(r + g.gr) * fs + c + g.gc] = inp[j];
-  }
-  __syncthreads();
-}
-
-__device__ void wrap_ring(const Geo& g, float* F, int fs) {
-  const int n = g.Fh * g.Fw;
-  for (int i = threadIdx.x; i < n; i += NT) {
-    const int fr = i / g.Fw, fc = i - fr * g.Fw;
-    const int r = fr - g.oh, c = fc - g.ow;
-    if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) continue;
-    int sr = r % g.roi_h; if (sr < 0) sr += g.roi_h;
-    int sc = c % g.roi_w; if (sc < 0) sc += g.roi_w;
-    F[fr * fs + fc] = F[(sr + g.oh) * fs + sc + g.ow];
-  }
-}
-
-__device__ void border_ring(const Geo& g, float* F, int fs, const float* border) {
-  const int n = g.Fh * g.Fw;
-  for (int i = threadIdx.x; i < n; i += NT) {
-    const int fr = i / g.Fw, fc = i - fr * g.Fw;
-    const int r = fr - g.oh, c = fc - g.ow;
-    if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) continue;
-    F[fr * fs + fc] = border[fr * g.W + fc];
-  }
-}
-
-__device__ __forceinline__ int out_pixel(const Geo& g, int idx) {
-  const int r = idx / g.W, c = idx - (idx / g.W) * g.W;
-  return (r - g.pad_h) * g.roi_w + (c - g.pad_w);
-}
-
-// ---------------------------------------------------------------------------------------
-// forward
-// ---------------------------------------------------------------------------------------
-template <int KH, int KW>
-__global__ void __launch_bounds__(NT, 1) fwd_kernel(FwdArgs a) {
-  constexpr int K = KH * KW;
-  extern __shared__ __align__(16) float sm[];
-  const Geo& g = a.g;
-  const int tid = threadIdx.x;
-  const int b = blockIdx.x;
-  const int P = g.P, RW = g.roi_w, ROWS = g.roi_h;
-  const int FS = g.Fw;
-  const int FROWS = g.Fh + RH;
-  float* Gt = sm;                                   // [k][m]
-  float* F = Gt + K * M;                            // FROWS x FS
-  int* pmap = reinterpret_cast<int*>(F + FROWS * FS);
-  float* red = reinterpret_cast<float*>(pmap + P);  // NW * M
-  float* s_mean = red + NW * M;
-  float* s_rstd = s_mean + M;
-
-  for (int i = tid; i < K * M; i += NT) {
-    const int k = i / M, m = i - k * M;
-    Gt[i] = a.sp.geff[m * K + k];
-  }
-  for (int p = tid; p < P; p += NT) pmap[p] = -1;
-  inject(g, F, FS, FROWS, a.in_index, a.inputs + (size_t)b * g.n_in);
-  for (int j = tid; j < g.n_out; j += NT) pmap[out_pixel(g, a.out_index[j])] = j;
-  if (g.padding == NC_PAD_CIRCULAR) wrap_ring(g, F, FS);
-  __syncthreads();
-
-  const int nstrip = (ROWS + RH - 1) / RH;
-  const bool active = tid < nstrip * RW;
-  const int s = active ? tid / RW : 0;
-  const int c = active ? tid - s * RW : 0;
-  const int r0 = s * RH;
-  bool pv[RH];
-#pragma unroll
-  for (int i = 0; i < RH; ++i) pv[i] = active && (r0 + i < ROWS);
-  const float inv_p = 1.0f / (float)P;
-
-  for (int t = 0; t < g.d; ++t) {
-    float2 acc[MP][RH];   // acc[q][i] = (z[2q], z[2q+1]) at row r0+i
-#pragma unroll
-    for (int q = 0; q < MP; ++q)
-#pragma unroll
-      for (int i = 0; i < RH; ++i) acc[q][i] = make_float2(0.f, 0.f);
-
-    if (active) {
-      // one kernel-row tap: the window slot of field row r0+u+i is (u+i) % RH; row
-      // r0+u+RH replaces row r0+u after use
-      auto tap = [&](const float* grow, float2 (&w)[RH], int du, const float* next) {
-        const float4* gp = reinterpret_cast<const float4*>(grow);
-#pragma unroll
-        for (int q4 = 0; q4 < M / 4; ++q4) {
-          const float4 gg = gp[q4];
-          const float2 g01 = make_float2(gg.x, gg.y), g23 = make_float2(gg.z, gg.w);
-#pragma unroll
-          for (int i = 0; i < RH; ++i) {
-            const float2 x = w[(du + i) % RH];
-            acc[2 * q4][i] = ffma2(g01, x, acc[2 * q4][i]);
-            acc[2 * q4 + 1][i] = ffma2(g23, x, acc[2 * q4 + 1][i]);
-          }
-        }
-        if (next) w[du % RH] = dup2(*next);
-      };
-      constexpr int KHC = (KH / RH) * RH;   // kernel rows handled in unrolled chunks of RH
-#pragma unroll 1
-      for (int v = 0; v < KW; ++v) {
-        const float* col = F + r0 * FS + c + v;
-        float2 w[RH];
-#pragma unroll
-        for (int i = 0; i < RH; ++i) w[i] = dup2(col[i * FS]);
-#pragma unroll 1
-        for (int u0 = 0; u0 < KHC; u0 += RH) {
-#pragma unroll
-          for (int du = 0; du < RH; ++du) {
-            const int u = u0 + du;
-            tap(Gt + (u * KW + v) * M, w, du, col + (u + RH) * FS);
-          }
-        }
-#pragma unroll
-        for (int du = 0; du < KH - KHC; ++du) {
-          const int u = KHC + du;
-          tap(Gt + (u * KW + v) * M, w, du, (u + 1 < KH) ? col + (u + RH) * FS : nullptr);
-        }
-      }
-    }
-
-    // plane statistics (centred two-pass, kernels_pallas.py:200-205)
-    if (g.norm) {
-      float part[M];
-#pragma unroll
-      for (int q = 0; q < MP; ++q) {
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int i = 0; i < RH; ++i) {
-          s0 += pv[i] ? acc[q][i].x : 0.f;
-          s1 += pv[i] ? acc[q][i].y : 0.f;
-        }
-        part[2 * q] = s0;
-        part[2 * q + 1] = s1;
-      }
-      sum16_block(part, red, s_mean, inv_p);
-#pragma unroll
-      for (int q = 0; q < MP; ++q) {
-        const float mu0 = s_mean[2 * q], mu1 = s_mean[2 * q + 1];
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int i = 0; i < RH; ++i) {
-          const float d0 = acc[q][i].x - mu0, d1 = acc[q][i].y - mu1;
-          s0 += pv[i] ? d0 * d0 : 0.f;
-          s1 += pv[i] ? d1 * d1 : 0.f;
-        }
-        part[2 * q] = s0;
-        part[2 * q + 1] = s1;
-      }
-      sum16_block(part, red, s_rstd, inv_p);
-      if (tid < M) s_rstd[tid] = 1.0f / sqrtf(s_rstd[tid] + kNormEps);
-      __syncthreads();
-    } else {
-      if (tid < M) { s_mean[tid] = 0.f; s_rstd[tid] = 1.f; }
-      __syncthreads();
-    }
-    if (a.train && tid < M) a.rstd[((size_t)b * g.d + t) * M + tid] = s_rstd[tid];
-
-    float* ZH = a.train ? a.zhat + ((size_t)b * g.d + t) * (size_t)M * P : nullptr;
-    if (t < g.d - 1) {
-      float* xs = a.train ? a.xsave + ((size_t)b * (g.d - 1) + t) * P : nullptr;
-#pragma unroll
-      for (int i = 0; i < RH; ++i) {
-        if (!pv[i]) continue;
-        const int p = (r0 + i) * RW + c;
-        const float bb = a.sp.broi[p];
-        float lin = 0.f, act = 0.f;
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const float z = (m & 1) ? acc[m >> 1][i].y : acc[m >> 1][i].x;
-          const float zh = (z - s_mean[m]) * s_rstd[m];
-          if (ZH) ZH[(size_t)m * P + p] = zh;
-          lin += zh;
-          if (g.act != NC_ACT_NONE) act += act_fwd(g.act, zh + bb, g.slope);
-        }
-        if (g.act == NC_ACT_NONE) act = lin + (float)M * bb;
-        const float xn = a.sp.weff[p] * lin + a.sp.seff[p] * act;
-        F[(r0 + i + g.oh) * FS + c + g.ow] = xn;
-        if (xs) xs[p] = xn;
-      }
-      __syncthreads();
-      if (t == 0 && g.padding == NC_PAD_VALID) {
-        border_ring(g, F, FS, a.sp.border);
-        __syncthreads();
-      }
-      if (g.padding == NC_PAD_CIRCULAR) {
-        wrap_ring(g, F, FS);
-        __syncthreads();
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < RH; ++i) {
-        if (!pv[i]) continue;
-        const int p = (r0 + i) * RW + c;
-        const int j = pmap[p];
-        if (!ZH && j < 0) continue;
-        const float bo = a.sp.broi[p];
-        float lin = 0.f, act = 0.f;
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const float z = (m & 1) ? acc[m >> 1][i].y : acc[m >> 1][i].x;
-          const float zh = (z - s_mean[m]) * s_rstd[m];
-          if (ZH) ZH[(size_t)m * P + p] = zh;
-          lin += zh;
-          if (g.fact != NC_ACT_NONE) act += act_fwd(g.fact, zh + bo, g.fslope);
-        }
-        if (j >= 0) {
-          const float wo = a.sp.weff[p], so = a.sp.seff[p];
-          const float o = (g.fact == NC_ACT_NONE) ? (wo + so) * lin + ((float)M * so * bo)
-                                                  : act_fwd(g.fact, wo * lin + so * act, g.fslope);
-          a.out[(size_t)b * g.n_out + j] = o;
-        }
-      }
-    }
-  }
-}
 
 // ---------------------------------------------------------------------------------------
 // backward
@@ -318,112 +72,105 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(BwdArgs a, FastBwdLayout L) 
   __syncthreads();
   if (g.padding == NC_PAD_VALID && g.d > 1) border_ring(g, F, FS, a.sp.border);
 
-  const int nstrip = (ROWS + RH - 1) / RH;
-  const bool active = tid < nstrip * RW;
-  const int s = active ? tid / RW : 0;
-  const int c = active ? tid - s * RW : 0;
-  const int r0 = s * RH;
   const float inv_p = 1.0f / (float)P;
-  // per-pixel partials of g w_eff, g s_eff, g b_roi accumulate in this sample's gpix slice
-  float* gp0 = a.gpix + (size_t)b * 3 * P;
-  float* gp1 = gp0 + P;
-  float* gp2 = gp1 + P;
-#pragma unroll 1
-  for (int i = 0; i < RH; ++i) {
-    if (!(active && r0 + i < ROWS)) continue;
-    const int p = (r0 + i) * RW + c;
-    gp0[p] = 0.f;
-    gp1[p] = 0.f;
-    gp2[p] = 0.f;
-  }
   float* dg = a.gdpart + (size_t)b * M * K;
-  float* gdel = a.gdelta ? a.gdelta + (size_t)b * M * P : nullptr;
+  // VALID with d > 1: the plane gradients of steps t >= 1 overwrite the standardised planes
+  // they were computed from (store only, no read-modify-write); a batch-and-step reduction
+  // sums them afterwards for the border-template adjoint
+  const bool keep_gz = a.gdelta != nullptr;
 
   for (int t = g.d - 1; t >= 0; --t) {
+    NC_PHASE_MARK(t, 0);
     // ---- phase A: plane gradients of step t into GZ ---------------------------------------
-    const float* ZH = a.zhat + ((size_t)b * g.d + t) * (size_t)M * P;
+    // thread <-> pixel, all 16 directions: plane loads and stores are coalesced along the
+    // pixel index; per-pixel sums over directions stay in the thread
+    float* ZH = a.zhat + ((size_t)b * g.d + t) * (size_t)M * P;
     if (tid < M) s_rstd[tid] = a.rstd[((size_t)b * g.d + t) * M + tid];
-    auto ZV = [&](int m, int p) { return __ldg(ZH + (size_t)m * P + p); };
+    float* gpp = a.gpix + ((size_t)b * g.d + t) * 3 * P;   // this step's pixel partials
     float c1p[M], c2p[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) { c1p[m] = 0.f; c2p[m] = 0.f; }
+    auto store_gz = [&](int p, const float (&gzh)[M], const float (&z)[M]) {
+      const int r = p / RW, cc = p - r * RW;
+      float2* gzp = GZ + r * RS + OW + cc;
+#pragma unroll
+      for (int q = 0; q < MP; ++q) gzp[q * PS] = make_float2(gzh[2 * q], gzh[2 * q + 1]);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        c1p[m] += gzh[m];
+        c2p[m] = fmaf(gzh[m], z[m], c2p[m]);
+      }
+    };
+    if (t == g.d - 1) {
+      // output step: only port cells carry a gradient (kernels_pallas.py:1107-1179)
+      for (int i = tid; i < 3 * P; i += NT) gpp[i] = 0.f;
+      __syncthreads();
 #pragma unroll 1
-    for (int i = 0; i < RH; ++i) {
-      if (!(active && r0 + i < ROWS)) continue;
-      const int p = (r0 + i) * RW + c;
-      float2* gzp = GZ + (r0 + i) * RS + OW + c;
-      float gzh[M];
-      bool any = true;
-      if (t == g.d - 1) {
-        // output step: only port cells carry a gradient (kernels_pallas.py:1107-1179)
-        int j = -1;
-        for (int q = 0; q < g.n_out; ++q)
-          if (out_pixel(g, a.out_index[q]) == p) { j = q; break; }
-        any = j >= 0;
-        if (any) {
-          const float go = a.gout[(size_t)b * g.n_out + j];
-          const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];
-          float lin = 0.f;
+      for (int j = tid; j < g.n_out; j += NT) {
+        const int p = out_pixel(g, a.out_index[j]);
+        float z[M], gzh[M];
 #pragma unroll
-          for (int m = 0; m < M; ++m) lin += ZV(m, p);
-          if (g.fact == NC_ACT_NONE) {
-            gp0[p] += go * lin;
-            gp1[p] += go * (lin + (float)M * bo);
-            gp2[p] += go * (float)M * so;
+        for (int m = 0; m < M; ++m) z[m] = ZH[(size_t)m * P + p];
+        const float go = a.gout[(size_t)b * g.n_out + j];
+        const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];
+        float lin = 0.f;
 #pragma unroll
-            for (int m = 0; m < M; ++m) gzh[m] = (wo + so) * go;
-          } else {
-            float act = 0.f;
-#pragma unroll 2
-            for (int m = 0; m < M; ++m) act += act_fwd(g.fact, ZV(m, p) + bo, g.fslope);
-            float dpre;
-            act_fwd_deriv(g.fact, wo * lin + so * act, g.fslope, &dpre);
-            const float gpre = go * dpre;
-            gp0[p] += gpre * lin;
-            gp1[p] += gpre * act;
-            float db = 0.f;
+        for (int m = 0; m < M; ++m) lin += z[m];
+        if (g.fact == NC_ACT_NONE) {
+          gpp[p] = go * lin;
+          gpp[P + p] = go * (lin + (float)M * bo);
+          gpp[2 * P + p] = go * (float)M * so;
 #pragma unroll
-            for (int m = 0; m < M; ++m) {
-              float dd;
-              act_fwd_deriv(g.fact, ZV(m, p) + bo, g.fslope, &dd);
-              gzh[m] = gpre * (wo + so * dd);
-              db += gpre * so * dd;
-            }
-            gp2[p] += db;
+          for (int m = 0; m < M; ++m) gzh[m] = (wo + so) * go;
+        } else {
+          float act = 0.f;
+#pragma unroll
+          for (int m = 0; m < M; ++m) act += act_fwd(g.fact, z[m] + bo, g.fslope);
+          float dpre;
+          act_fwd_deriv(g.fact, wo * lin + so * act, g.fslope, &dpre);
+          const float gpre = go * dpre;
+          float db = 0.f;
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            float dd;
+            act_fwd_deriv(g.fact, z[m] + bo, g.fslope, &dd);
+            gzh[m] = gpre * (wo + so * dd);
+            db += gpre * so * dd;
           }
+          gpp[p] = gpre * lin;
+          gpp[P + p] = gpre * act;
+          gpp[2 * P + p] = db;
         }
-      } else {
-        // hidden step t (kernels_pallas.py:221-291); GY holds d loss / d field_{t+1}
+        store_gz(p, gzh, z);
+      }
+    } else {
+      // hidden step t (kernels_pallas.py:221-291); GY holds d loss / d field_{t+1}
+#pragma unroll 1
+      for (int p = tid; p < P; p += NT) {
+        float z[M], gzh[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) z[m] = ZH[(size_t)m * P + p];
         const float gy = GY[p];
         const float bb = a.sp.broi[p], we = a.sp.weff[p], se = a.sp.seff[p];
         float lin = 0.f, act = 0.f, dsum = 0.f;
 #pragma unroll
         for (int m = 0; m < M; ++m) {
           float dd;
-          const float zv = ZV(m, p);
-          const float av = act_fwd_deriv(g.act, zv + bb, g.slope, &dd);
-          lin += zv;
+          const float av = act_fwd_deriv(g.act, z[m] + bb, g.slope, &dd);
+          lin += z[m];
           act += av;
           dsum += dd;
           gzh[m] = we * gy + se * gy * dd;
         }
-        gp0[p] += gy * lin;
-        gp1[p] += gy * act;
-        gp2[p] += se * gy * dsum;
-      }
-      if (any) {
-#pragma unroll
-        for (int q = 0; q < MP; ++q) gzp[q * PS] = make_float2(gzh[2 * q], gzh[2 * q + 1]);
-        if (g.norm) {
-#pragma unroll
-          for (int m = 0; m < M; ++m) {
-            c1p[m] += gzh[m];
-            c2p[m] = fmaf(gzh[m], ZV(m, p), c2p[m]);
-          }
-        }
+        gpp[p] = gy * lin;
+        gpp[P + p] = gy * act;
+        gpp[2 * P + p] = se * gy * dsum;
+        store_gz(p, gzh, z);
       }
     }
+    NC_PHASE_MARK(t, 4);
     if (g.norm) {
+      // c1 = mean(g zhat), c2 = mean(g zhat * zhat) per plane
 #pragma unroll
       for (int m = 0; m < M; ++m) {
         const float s1 = warp_sum(c1p[m]);
@@ -441,38 +188,38 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(BwdArgs a, FastBwdLayout L) 
         else s_c2[tid - M] = sacc * inv_p;
       }
       __syncthreads();
+    }
+    NC_PHASE_MARK(t, 5);
+    // standardisation adjoint GZ <- rstd (GZ - c1 - zhat c2); keep gz for the border adjoint
+    if (g.norm || (keep_gz && t >= 1)) {
+      if (!g.norm) __syncthreads();
 #pragma unroll 1
-      for (int i = 0; i < RH; ++i) {
-        if (!(active && r0 + i < ROWS)) continue;
-        const int p = (r0 + i) * RW + c;
-        float2* gzp = GZ + (r0 + i) * RS + OW + c;
-#pragma unroll 2
+      for (int p = tid; p < P; p += NT) {
+        const int r = p / RW, cc = p - r * RW;
+        float2* gzp = GZ + r * RS + OW + cc;
+        float z[M];
+        if (g.norm) {
+#pragma unroll
+          for (int m = 0; m < M; ++m) z[m] = ZH[(size_t)m * P + p];
+        }
+#pragma unroll
         for (int q = 0; q < MP; ++q) {
           float2 v = gzp[q * PS];
-          v.x = s_rstd[2 * q] * (v.x - s_c1[2 * q] - ZV(2 * q, p) * s_c2[2 * q]);
-          v.y = s_rstd[2 * q + 1] * (v.y - s_c1[2 * q + 1] - ZV(2 * q + 1, p) * s_c2[2 * q + 1]);
-          gzp[q * PS] = v;
-        }
-      }
-    }
-    if (gdel && t >= 1) {
-#pragma unroll 1
-      for (int i = 0; i < RH; ++i) {
-        if (!(active && r0 + i < ROWS)) continue;
-        const int p = (r0 + i) * RW + c;
-        const float2* gzp = GZ + (r0 + i) * RS + OW + c;
-#pragma unroll 2
-        for (int q = 0; q < MP; ++q) {
-          const float2 v = gzp[q * PS];
-          float* d0 = gdel + (size_t)(2 * q) * P + p;
-          float* d1 = d0 + P;
-          *d0 = (t == g.d - 1) ? v.x : *d0 + v.x;
-          *d1 = (t == g.d - 1) ? v.y : *d1 + v.y;
+          if (g.norm) {
+            v.x = s_rstd[2 * q] * (v.x - s_c1[2 * q] - z[2 * q] * s_c2[2 * q]);
+            v.y = s_rstd[2 * q + 1] * (v.y - s_c1[2 * q + 1] - z[2 * q + 1] * s_c2[2 * q + 1]);
+            gzp[q * PS] = v;
+          }
+          if (keep_gz && t >= 1) {
+            ZH[(size_t)(2 * q) * P + p] = v.x;
+            ZH[(size_t)(2 * q + 1) * P + p] = v.y;
+          }
         }
       }
     }
     // ---- field entering step t -----------------------------------------------------------
     __syncthreads();
+    NC_PHASE_MARK(t, 1);
     if (t == 0) {
       inject(g, F, FS, g.Fh + 2, a.in_index, a.inputs + (size_t)b * g.n_in);
       if (g.padding == NC_PAD_CIRCULAR) wrap_ring(g, F, FS);
@@ -488,6 +235,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(BwdArgs a, FastBwdLayout L) 
       }
     }
     __syncthreads();
+    NC_PHASE_MARK(t, 2);
 
     // ---- phase B: dG[m,u,v] += sum_{r,c} GZ[m,r,c] F[r+u, c+v]   (warps 0 .. NUP-1) -----
     if (warp < NUP) {
@@ -552,6 +300,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(BwdArgs a, FastBwdLayout L) 
         }
       }
     }
+    NC_WARP_MARK(t, 0);
 
     // ---- phase C: GY[r,c] = sum_m sum_{u,v} G[m,u,v] GZ[m, r+oh-u, c+ow-v]   (t >= 1) ----
     if (t >= 1) {
@@ -598,7 +347,9 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(BwdArgs a, FastBwdLayout L) 
         }
       }
     }
+    NC_WARP_MARK(t, 1);
     __syncthreads();
+    NC_PHASE_MARK(t, 3);
   }
 }
 
@@ -609,21 +360,15 @@ template <int KH, int KW>
 struct Inst {
   static bool fits(const Geo& g) {
     if (g.M != M || g.kh != KH || g.kw != KW) return false;
-    if (((g.roi_h + RH - 1) / RH) * g.roi_w > NT) return false;
+    if (((g.roi_h + RH - 1) / RH) * g.roi_w > NT) return false;   // backward mapping
     if ((KH + 1) / 2 > NW) return false;
-    return fast_fwd_smem_bytes(g, KH, KW) <= kFastSmemMax &&
-           fast_bwd_layout(g, KH, KW).bytes <= kFastSmemMax;
+    if (g.P % 4 != 0) return false;   // float4 batch reductions of the per-step partials
+    const FastFwd f = fast_fwd_select(g);
+    return f.fn && f.smem <= kFastSmemMax && fast_bwd_layout(g, KH, KW).bytes <= kFastSmemMax;
   }
 };
 
 }  // namespace fast
-
-size_t fast_fwd_smem_bytes(const Geo& g, int kh, int kw) {
-  const size_t K = (size_t)kh * kw;
-  size_t n = K * fastc::M + (size_t)(g.Fh + fastc::RH) * g.Fw + (size_t)g.P /*pmap*/ +
-             (size_t)fastc::NW * fastc::M + 2 * fastc::M;
-  return n * sizeof(float);
-}
 
 // Number of distinct values among {x_i mod m}.
 static int distinct_mod(const long* x, int n, long m) {
@@ -686,9 +431,11 @@ FastKernels fast_kernels(const Geo& g) {
   FastKernels k{};
 #define NC_FAST_INST(KH_, KW_)                                                        \
   if (fast::Inst<KH_, KW_>::fits(g)) {                                                \
-    k.fwd = (const void*)fast::fwd_kernel<KH_, KW_>;                                  \
+    const FastFwd f = fast_fwd_select(g);                                             \
+    k.fwd = f.fn;                                                                     \
+    k.fwd_smem = f.smem;                                                              \
+    k.fwd_threads = f.threads;                                                        \
     k.bwd = (const void*)fast::bwd_kernel<KH_, KW_>;                                  \
-    k.fwd_smem = fast_fwd_smem_bytes(g, KH_, KW_);                                     \
     k.bl = fast_bwd_layout(g, KH_, KW_);                                               \
     k.bwd_smem = k.bl.bytes;                                                          \
     return k;                                                                         \
@@ -699,3 +446,12 @@ FastKernels fast_kernels(const Geo& g) {
 }
 
 }  // namespace nc
+
+#if NC_PHASE_TIMING
+// Debug builds only: copies the phase clocks of CTA 0 ([8][4] then [8][32][2]) to `out`.
+extern "C" int nc_debug_phase_times(long long* out) {
+  if (cudaMemcpyFromSymbol(out, nc::fast::g_nc_phase, sizeof(long long) * 64) != cudaSuccess) return 1;
+  if (cudaMemcpyFromSymbol(out + 64, nc::fast::g_nc_warp, sizeof(long long) * 512) != cudaSuccess) return 1;
+  return 0;
+}
+#endif

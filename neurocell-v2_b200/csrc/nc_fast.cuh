@@ -34,10 +34,17 @@ struct FastKernels {
   const void* fwd;
   const void* bwd;
   size_t fwd_smem, bwd_smem;
+  int fwd_threads;
   FastBwdLayout bl;
 };
 
-size_t fast_fwd_smem_bytes(const Geo& g, int kh, int kw);
+// Specialised forward for this geometry (fn == nullptr when none applies).
+struct FastFwd {
+  const void* fn;
+  size_t smem;
+  int threads;
+};
+FastFwd fast_fwd_select(const Geo& g);
 FastBwdLayout fast_bwd_layout(const Geo& g, int kh, int kw);
 FastKernels fast_kernels(const Geo& g);
 

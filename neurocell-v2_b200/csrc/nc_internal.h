@@ -48,8 +48,12 @@ struct WsLayout {
   size_t fscr, zscr, gzscr;
   // backward partials and reductions
   size_t gpix, gdpart, gdelta, gsum, gdsum, gdeltasum, gborder;
+  size_t redscr;          // partial rows of the two-stage batch reductions
   size_t total;
 };
+
+// Sample chunks of the two-stage batch-and-step reductions.
+constexpr int kRedChunks = 16;
 WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* z_smem,
                    bool* gz_smem);
 

@@ -42,7 +42,7 @@ struct BwdArgs {
   const float* inputs;
   const float* gout;          // (B, n_out)
   const float* xsave;
-  const float* zhat;
+  float* zhat;                // the specialised kernels overwrite consumed planes with gz
   const float* rstd;
   float* fscr;
   float* gzscr;               // (B, M, P) when gz is not on-chip

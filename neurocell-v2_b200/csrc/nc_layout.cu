@@ -95,15 +95,19 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
   L.zscr = (!train && !zs) ? take(fl * B * M * P) : SIZE_MAX;
   if (train) {
     L.gzscr = gzs ? SIZE_MAX : take(fl * B * M * P);
-    L.gpix = take(fl * B * 3 * P + fl * B * P);   // 3 partial planes + dX output plane
+    // per-sample pixel partials: (B, d, 3, P) per-step slots (specialised kernels) or
+    // (B, 3, P) followed by a (B, P) field-adjoint plane (generic kernels)
+    L.gpix = take(fl * B * (3 * (size_t)g.d + 1) * P);
     L.gdpart = take(fl * B * M * g.K);
     L.gdelta = (g.padding == NC_PAD_VALID && g.d > 1) ? take(fl * B * M * P) : SIZE_MAX;
     L.gsum = take(fl * 3 * P);
     L.gdsum = take(fl * M * g.K);
     L.gdeltasum = (g.padding == NC_PAD_VALID && g.d > 1) ? take(fl * M * P) : SIZE_MAX;
     L.gborder = take(fl * HW);
+    L.redscr = take(fl * kRedChunks * (3 * P > M * P ? 3 * P : M * P));
   } else {
     L.gzscr = L.gpix = L.gdpart = L.gdelta = L.gsum = L.gdsum = L.gdeltasum = L.gborder = SIZE_MAX;
+    L.redscr = SIZE_MAX;
   }
   L.total = o;
   return L;
