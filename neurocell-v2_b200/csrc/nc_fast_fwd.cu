@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(FwdCfg<KH, KW, MT>::NTF, 1) fwd_kernel_mt(FwdA
   const int m0 = MT * h;
 
   for (int t = 0; t < g.d; ++t) {
+    NC_PHASE_MARK(t, 0);
     float acc[MT][FR];   // acc[k][i] = z[m0+k] at row r0+i
 #pragma unroll
     for (int k = 0; k < MT; ++k)
@@ -118,6 +119,7 @@ __global__ void __launch_bounds__(FwdCfg<KH, KW, MT>::NTF, 1) fwd_kernel_mt(FwdA
       }
     }
 
+    NC_PHASE_MARK(t, 1);
     // plane statistics (centred two-pass); lanes congruent mod LP share a direction group
     auto reduce_group = [&](float (&part)[MT], float* out) {
 #pragma unroll
@@ -169,6 +171,7 @@ __global__ void __launch_bounds__(FwdCfg<KH, KW, MT>::NTF, 1) fwd_kernel_mt(FwdA
     }
     if (a.train && tid < M) a.rstd[((size_t)b * g.d + t) * M + tid] = s_rstd[tid];
 
+    NC_PHASE_MARK(t, 2);
     float* ZH = a.train ? a.zhat + ((size_t)b * g.d + t) * (size_t)M * P : nullptr;
     const bool last = (t == g.d - 1);
     const int fact = last ? g.fact : g.act;
@@ -223,6 +226,7 @@ __global__ void __launch_bounds__(FwdCfg<KH, KW, MT>::NTF, 1) fwd_kernel_mt(FwdA
         __syncthreads();
       }
     }
+    NC_PHASE_MARK(t, 3);
   }
 }
 
@@ -250,3 +254,10 @@ FastFwd fast_fwd_select(const Geo& g) {
 }
 
 }  // namespace nc
+
+#if NC_PHASE_TIMING
+// Debug builds only: the forward kernel's phase clocks of CTA 0 ([8][8]).
+extern "C" int nc_debug_fwd_phase_times(long long* out) {
+  return cudaMemcpyFromSymbol(out, nc::fast::g_nc_phase, sizeof(long long) * 64) == cudaSuccess ? 0 : 1;
+}
+#endif

@@ -48,6 +48,21 @@ def packbits_u8_on_device(bits: torch.Tensor) -> torch.Tensor:
     return (bits.to(torch.int32) * w).sum(-1, keepdim=True).to(torch.uint8)
 
 
+def allreduce_mean_(flat: torch.Tensor, process_group=None) -> int:
+    """Data-parallel gradient exchange: sums ``flat`` over the ranks of ``process_group`` in
+    place (one collective over the packed [g_cell | g_filters] buffer) and returns the world
+    size, so the caller scales the update by 1/world.  Every rank computed the gradient of
+    its own mean loss over an equal-sized shard, so (sum over ranks) / world is the gradient
+    of the mean loss over the global batch.  No-op for a single process."""
+    if process_group is None:
+        return 1
+    import torch.distributed as dist
+    world = dist.get_world_size(process_group)
+    if world > 1:
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=process_group)
+    return world
+
+
 class VNNTrainStep:
     """One fused training step over static device buffers: forward, loss, backward,
     optional data-parallel gradient all-reduce, SGD update.
@@ -147,11 +162,8 @@ class VNNTrainStep:
                                             P(self.x), self.B, c.byref(self.codd), P(self.g_out),
                                             c.c_void_p(gcell), c.c_void_p(gfilt), P(self.ws),
                                             self.ws_bytes, st), "nc_vnn_backward")
-        lr = self.lr
-        if self.pg is not None:
-            import torch.distributed as dist
-            dist.all_reduce(self.grads, group=self.pg)
-            lr = self.lr / self.world       # mean of the per-rank mean-loss gradients
+        world = allreduce_mean_(self.grads, self.pg)
+        lr = self.lr / world                # mean of the per-rank mean-loss gradients
         self._lib.check(lib.nc_sgd_update(c.c_void_p(cell), c.c_void_p(gcell),
                                           self.n_cell + self.n_filt, lr, st), "nc_sgd_update")
 

@@ -1,0 +1,78 @@
+"""Data parallelism on 2 GPUs with NCCL: two ranks each run the fused train step on half of
+an ALU batch; the all-reduced gradient equals the single-GPU gradient of the whole batch
+(relative L2 <= 1e-5) and both ranks end with identical parameters.  Skips on boxes with
+fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _problem(B):
+    from oracle import vnn_oracle as O
+    rng = np.random.default_rng(123)
+    cell = rng.normal(0, 0.1, (3, 62, 62)).astype(np.float32)
+    filt = (rng.normal(0, 1, (16, 1, 23, 13)) / np.sqrt(299)).astype(np.float32)
+    x, y, _ = O.alu_batch(rng, B, noise=0.0)
+    return cell, filt, x.reshape(B, -1), y
+
+
+def _rank_main(rank, world, port, out_dir):
+    import sys
+    from datetime import timedelta
+    import torch.distributed as dist
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "neurocell-v2_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        import neurocell_b200 as nc
+        cell, filt, x, y = _problem(64)
+        shard = slice(rank * 32, rank * 32 + 32)
+        topo = nc.ChipTopology2D.alu_chip()
+        p = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
+        st = nc.trainer.VNNTrainStep(topo, p, 32, lr=1e-2, in_shapes=((8, 1),) * 3,
+                                     process_group=dist.group.WORLD)
+        st.step(torch.tensor(x[shard], device=dev), torch.tensor(y[shard], device=dev))
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"grads{rank}.npy"), st.grads.cpu().numpy())
+        np.save(os.path.join(out_dir, f"params{rank}.npy"), st.flat.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_data_parallel_step_matches_full_batch(tmp_path):
+    import torch.multiprocessing as mp
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    import neurocell_b200 as nc
+    cell, filt, x, y = _problem(64)
+    dev = torch.device("cuda", 0)
+    p = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
+    st = nc.trainer.VNNTrainStep(nc.ChipTopology2D.alu_chip(), p, 64, lr=1e-2,
+                                 in_shapes=((8, 1),) * 3)
+    st.step(torch.tensor(x, device=dev), torch.tensor(y, device=dev))
+    torch.cuda.synchronize()
+    full = st.grads.cpu().numpy()
+    g0 = np.load(tmp_path / "grads0.npy") / 2.0
+    g1 = np.load(tmp_path / "grads1.npy") / 2.0
+    assert np.array_equal(g0, g1)                       # every rank holds the same sum
+    assert np.linalg.norm(g0 - full) / np.linalg.norm(full) <= 1e-5
+    p0, p1 = np.load(tmp_path / "params0.npy"), np.load(tmp_path / "params1.npy")
+    assert np.array_equal(p0, p1)
+    assert np.linalg.norm(p0 - st.flat.cpu().numpy()) / np.linalg.norm(p0) <= 1e-6
