@@ -220,9 +220,9 @@ def run_b200(args) -> None:
                                      process_group=pg)
     x_dev = torch.tensor(xs.reshape(nb, BATCH, -1), device=dev)
     y_dev = torch.tensor(ys, device=dev)
-    if world == 1 and not args.no_graph:
+    if not args.no_graph:
         runner.load_batch(x_dev[0], y_dev[0])
-        runner.capture()
+        runner.capture()            # the NCCL all-reduce is captured too when world > 1
     l2_flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def barrier():
@@ -331,6 +331,8 @@ def run_b200(args) -> None:
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
+    runner.release()                # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
     if pg is not None:
         dist.barrier()
         dist.destroy_process_group()

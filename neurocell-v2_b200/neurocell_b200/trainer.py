@@ -181,8 +181,8 @@ class VNNTrainStep:
         return self.loss
 
     def capture(self) -> None:
-        if self.pg is not None:
-            raise NotImplementedError("graph capture is single-process only")
+        """Records one step into a CUDA graph (the NCCL all-reduce included when data
+        parallel; call ``release()`` before destroying the process group)."""
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         saved = self.flat.clone()
@@ -195,6 +195,10 @@ class VNNTrainStep:
             self._launch()
         self.flat.copy_(saved)             # warm-up and capture must not move the parameters
         self.graph = g
+
+    def release(self) -> None:
+        """Drops the captured graph (required before destroy_process_group)."""
+        self.graph = None
 
 
 class VNNTrainer:
