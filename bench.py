@@ -217,12 +217,12 @@ def run_b200(args) -> None:
     topo = nc.ChipTopology2D.alu_chip()
     params = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
     runner = nc.trainer.VNNTrainStep(topo, params, BATCH, lr=LR, in_shapes=((8, 1),) * 3,
-                                     process_group=pg)
+                                     process_group=pg, exchange=args.exchange)
     x_dev = torch.tensor(xs.reshape(nb, BATCH, -1), device=dev)
     y_dev = torch.tensor(ys, device=dev)
     if not args.no_graph:
         runner.load_batch(x_dev[0], y_dev[0])
-        runner.capture()            # the NCCL all-reduce is captured too when world > 1
+        runner.capture()            # the gradient exchange is captured too when world > 1
     l2_flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def barrier():
@@ -298,6 +298,12 @@ def run_b200(args) -> None:
     if pg is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
+    bad = torch.tensor([runner.exchange_status()], dtype=torch.int32, device=dev)
+    if pg is not None:
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)    # every rank takes the same exit
+    if int(bad.item()) != 0:
+        runner.graph = None
+        raise RuntimeError("NVLink gradient exchange: a peer timed out during the run")
     h2d = x_host[0].numel() * 4 + y_host[0].numel() * 4
 
     peak = fp32_peak_tflops(dev)
@@ -317,7 +323,8 @@ def run_b200(args) -> None:
                        "M": 16, "depth": 4, "codd_mode": "continuous", "loss": "mse",
                        "optimizer": "sgd(1e-2)", "per_gpu_batch": BATCH, "global_batch": BATCH * world,
                        "parallelism": f"dp{world}", "l2": "flushed (256 MB write) before every timed step",
-                       "cuda_graph": runner.graph is not None},
+                       "cuda_graph": runner.graph is not None,
+                       "grad_exchange": (args.exchange if world > 1 else "none")},
             "e2e": {"value": BATCH * world / (e2e_ms * 1e-3), "unit": "samples/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms},
             "gpu_launches": runner.launches_per_step() * K,
@@ -331,7 +338,7 @@ def run_b200(args) -> None:
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
-    runner.release()                # graphs holding NCCL calls go before the process group
+    runner.release()                # graphs holding NCCL calls and the IPC maps go first
     torch.cuda.synchronize()
     if pg is not None:
         dist.barrier()
@@ -346,6 +353,8 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--exchange", choices=("nccl", "nvlink"), default="nccl",
+                    help="data-parallel gradient exchange for --gpus > 1")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3

@@ -176,6 +176,46 @@ nc_status nc_softmax_ce_loss(const float* logits, const int32_t* labels, int32_t
 /* In-place SGD: params[i] -= lr * grads[i]  (lr read from host scalar). */
 nc_status nc_sgd_update(float* params, const float* grads, int64_t n, float lr, void* stream);
 
+/* ---- data-parallel gradient exchange over NVLink ---------------------------------------- */
+/*
+ * No counterpart in the reference (it has no multi-GPU code; the north star asks for the
+ * ~16k-parameter gradient to be all-reduced across 1/2/4/8 GPUs).  nc_dp_allreduce_sgd
+ * fuses the cross-GPU gradient sum with the SGD update in one kernel: every rank copies
+ * its packed gradient into its slot of a double-buffered shared buffer, raises per-slice
+ * flags, waits (bounded) for the same slices of all peers, sums them in rank order with
+ * peer loads over NVLink (bitwise identical on every rank) and updates its parameters.
+ * Set-up: nc_dp_alloc on every rank, exchange nc_ipc_get handles (e.g. all_gather), open
+ * the peers' buffers with nc_ipc_open, zero-initialised state from nc_dp_alloc.
+ * Step counters live on the device, so the call can be captured in a CUDA graph.
+ */
+#define NC_DP_MAX_RANKS 8
+#define NC_IPC_HANDLE_BYTES 64
+
+/* Device bytes of the shared exchange buffer for n parameters. */
+size_t nc_dp_shared_bytes(int64_t n);
+/* Device bytes of the private per-rank state (step counters, status word). */
+size_t nc_dp_state_bytes(void);
+/* Set-up time allocations (cudaMalloc + zero fill); not for the hot path. */
+nc_status nc_dp_alloc(size_t bytes, void** d_ptr);
+nc_status nc_dp_free(void* d_ptr);
+/* CUDA IPC of a buffer from nc_dp_alloc: handle_out receives NC_IPC_HANDLE_BYTES bytes. */
+nc_status nc_ipc_get(void* d_ptr, void* handle_out);
+nc_status nc_ipc_open(const void* handle, void** d_peer_ptr);
+nc_status nc_ipc_close(void* d_peer_ptr);
+
+/*
+ * grads[n] (this rank's gradient of its mean loss) -> grads[n] = sum over ranks,
+ * params[n] -= lr / world * grads[n].  peers[world] are the shared buffers of all ranks
+ * (this rank's own at index rank).  A peer that does not arrive within max_wait_iters
+ * polls makes the kernel skip the update and set the status word; read it with
+ * nc_dp_status (0 = ok, 1 = a peer timed out).
+ */
+nc_status nc_dp_allreduce_sgd(void* const* peers, int32_t world, int32_t rank, void* d_state,
+                              float* grads, float* params, int64_t n, float lr,
+                              int32_t max_wait_iters, void* stream);
+/* Copies the device status word of d_state to *status (synchronises the stream). */
+nc_status nc_dp_status(const void* d_state, int32_t* status, void* stream);
+
 /* ---- measurement ----------------------------------------------------------------------- */
 
 /*
@@ -200,6 +240,10 @@ const char* nc_last_error(void);
 
 /* NC_ABI_VERSION of the loaded library. */
 int32_t nc_abi_version(void);
+
+/* Number of kernels this library has launched in the process so far (all host threads;
+ * launches recorded into a CUDA graph count once, at capture). */
+uint64_t nc_launch_count(void);
 
 #ifdef __cplusplus
 }

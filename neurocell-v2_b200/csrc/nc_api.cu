@@ -2,6 +2,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
+#include <atomic>
 
 #include <cuda_runtime.h>
 
@@ -35,9 +36,11 @@ static nc_status batch_step_sum(const float* in, int batch, int d, int t0, size_
   batch_step_sum4_kernel<<<grid, 256, 0, st>>>(in, batch, d, t0, slot, n, bc, scratch);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "batch_step_sum4_kernel launch");
+  note_launch();
   rows_sum_kernel<<<(n + 255) / 256, 256, 0, st>>>(scratch, chunks, n, out);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "rows_sum_kernel launch");
+  note_launch();
   return NC_OK;
 }
 __global__ void border_grad_kernel(Geo g, const float* G, const float* gdelta, float* gborder);
@@ -71,6 +74,9 @@ nc_status cuda_error(cudaError_t e, const char* what) {
 }
 
 void clear_error() { g_err[0] = 0; }
+
+static std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 static inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
@@ -132,6 +138,7 @@ static nc_status set_smem_attr(const void* fn, size_t bytes) {
 static nc_status launch_check(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, what);
+  note_launch();
   return NC_OK;
 }
 
@@ -184,6 +191,8 @@ using namespace nc;
 extern "C" {
 
 int32_t nc_abi_version(void) { return NC_ABI_VERSION; }
+
+uint64_t nc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* nc_last_error(void) { return g_err; }
 

@@ -13,6 +13,8 @@ constexpr size_t kSmemBudget = 225 * 1024;
 nc_status set_error(nc_status st, const char* fmt, ...);
 nc_status cuda_error(cudaError_t e, const char* what);
 void clear_error();
+// Counts one successful kernel launch (reported by nc_launch_count).
+void note_launch();
 
 }  // namespace nc
 

@@ -25,8 +25,12 @@ EXPORTED = (
     "nc_plan_bytes", "nc_plan_build", "nc_workspace_bytes", "nc_vnn_forward",
     "nc_vnn_backward", "nc_codd_states", "nc_mse_loss", "nc_softmax_ce_loss",
     "nc_sgd_update", "nc_last_error", "nc_abi_version", "nc_set_profile_events",
-    "nc_fp32_peak_probe", "nc_vnn_forward_static",
+    "nc_fp32_peak_probe", "nc_vnn_forward_static", "nc_dp_shared_bytes", "nc_dp_state_bytes",
+    "nc_dp_alloc", "nc_dp_free", "nc_ipc_get", "nc_ipc_open", "nc_ipc_close",
+    "nc_dp_allreduce_sgd", "nc_dp_status", "nc_launch_count",
 )
+NC_DP_MAX_RANKS = 8
+NC_IPC_HANDLE_BYTES = 64
 
 
 class NcTopo(ctypes.Structure):
@@ -66,8 +70,19 @@ _SIGS = {
     "nc_vnn_forward_static": (_i32, [_TP, _vp, _vp, _vp, _vp, _i32, _CP, _vp, _vp]),
     "nc_set_profile_events": (None, [_vp, _vp, _vp, _vp]),
     "nc_fp32_peak_probe": (_i32, [_i32, ctypes.POINTER(ctypes.c_double), _vp, _vp]),
+    "nc_dp_shared_bytes": (_sz, [_i64]),
+    "nc_dp_state_bytes": (_sz, []),
+    "nc_dp_alloc": (_i32, [_sz, ctypes.POINTER(_vp)]),
+    "nc_dp_free": (_i32, [_vp]),
+    "nc_ipc_get": (_i32, [_vp, _vp]),
+    "nc_ipc_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "nc_ipc_close": (_i32, [_vp]),
+    "nc_dp_allreduce_sgd": (_i32, [ctypes.POINTER(_vp), _i32, _i32, _vp, _vp, _vp, _i64, _f32,
+                                   _i32, _vp]),
+    "nc_dp_status": (_i32, [_vp, ctypes.POINTER(_i32), _vp]),
     "nc_last_error": (ctypes.c_char_p, []),
     "nc_abi_version": (_i32, []),
+    "nc_launch_count": (ctypes.c_uint64, []),
 }
 
 _lib = None

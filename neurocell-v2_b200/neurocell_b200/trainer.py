@@ -63,29 +63,128 @@ def allreduce_mean_(flat: torch.Tensor, process_group=None) -> int:
     return world
 
 
+class NVLinkExchange:
+    """Gradient sum over the ranks of a process group fused with the SGD update, one kernel
+    over NVLink peer memory (``nc_dp_allreduce_sgd``).
+
+    Each rank allocates a double-buffered exchange buffer, the ranks swap CUDA IPC handles
+    with one ``all_gather_object`` and map each other's buffers.  Every step each rank's
+    kernel publishes its gradient, waits (bounded by ``max_wait_iters`` polls) for the same
+    slices of all peers, sums them in rank order (bitwise the same on every rank) and applies
+    ``params -= lr / world * sum``.  One process per GPU; ranks on one GPU are rejected,
+    because kernels that wait on one another cannot share a device.  ``close()`` unmaps and
+    frees the buffers (collective: every rank calls it).
+    """
+
+    def __init__(self, n: int, process_group, device, max_wait_iters: int = 1 << 22):
+        import ctypes
+        import torch.distributed as dist
+        from . import _lib
+        self.lib = _lib.load()
+        self._lib = _lib
+        self.ctypes = ctypes
+        self.pg = process_group
+        self.n = int(n)
+        self.world = dist.get_world_size(process_group)
+        self.rank = dist.get_rank(process_group)
+        self.max_wait = int(max_wait_iters)
+        if not 1 <= self.world <= _lib.NC_DP_MAX_RANKS:
+            raise ValueError(f"NVLink exchange supports 1..{_lib.NC_DP_MAX_RANKS} ranks, "
+                             f"got {self.world}")
+        dev = torch.device(device)
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        uuids = [None] * self.world
+        dist.all_gather_object(uuids, uuid, group=process_group)
+        if len(set(uuids)) != self.world:
+            raise ValueError("NVLink exchange needs one GPU per rank (two ranks share a device)")
+        self.shared = ctypes.c_void_p()
+        self.state = ctypes.c_void_p()
+        with torch.cuda.device(dev):
+            _lib.check(self.lib.nc_dp_alloc(self.lib.nc_dp_shared_bytes(self.n),
+                                            ctypes.byref(self.shared)), "nc_dp_alloc")
+            _lib.check(self.lib.nc_dp_alloc(self.lib.nc_dp_state_bytes(), ctypes.byref(self.state)),
+                       "nc_dp_alloc")
+            handle = ctypes.create_string_buffer(_lib.NC_IPC_HANDLE_BYTES)
+            _lib.check(self.lib.nc_ipc_get(self.shared, handle), "nc_ipc_get")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=process_group)
+            self.peers = (ctypes.c_void_p * self.world)()
+            self._opened = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.peers[r] = self.shared.value
+                    continue
+                p = ctypes.c_void_p()
+                _lib.check(self.lib.nc_ipc_open(ctypes.create_string_buffer(h, len(h)),
+                                                ctypes.byref(p)), "nc_ipc_open")
+                self.peers[r] = p.value
+                self._opened.append(p)
+        self.device = dev
+        self.closed = False
+
+    def allreduce_sgd(self, grads_ptr: int, params_ptr: int, lr: float, stream) -> None:
+        """``stream``: a ``ctypes.c_void_p`` holding the cudaStream_t to launch on."""
+        if self.closed:
+            raise RuntimeError("NVLinkExchange is closed")
+        c = self.ctypes
+        self._lib.check(self.lib.nc_dp_allreduce_sgd(self.peers, self.world, self.rank, self.state,
+                                                     c.c_void_p(grads_ptr), c.c_void_p(params_ptr),
+                                                     self.n, float(lr), self.max_wait, stream),
+                        "nc_dp_allreduce_sgd")
+
+    def status(self) -> int:
+        """0 = every exchange so far completed; 1 = a peer timed out (parameters of that step
+        were not updated, the ranks are out of step: treat as fatal).  Synchronises."""
+        c = self.ctypes
+        out = c.c_int32(-1)
+        self._lib.check(self.lib.nc_dp_status(self.state, c.byref(out),
+                                              c.c_void_p(torch.cuda.current_stream(self.device)
+                                                         .cuda_stream)), "nc_dp_status")
+        return int(out.value)
+
+    def close(self) -> None:
+        if self.closed:
+            return
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            self._lib.check(self.lib.nc_ipc_close(p), "nc_ipc_close")
+        self._opened = []
+        dist.barrier(group=self.pg)       # no peer reads this rank's buffer any more
+        self._lib.check(self.lib.nc_dp_free(self.shared), "nc_dp_free")
+        self._lib.check(self.lib.nc_dp_free(self.state), "nc_dp_free")
+        self.closed = True
+
+
 class VNNTrainStep:
     """One fused training step over static device buffers: forward, loss, backward,
-    optional data-parallel gradient all-reduce, SGD update.
+    optional data-parallel gradient exchange, SGD update.
 
     Parameters live in one packed device buffer ``[cell_params (3HW) | filters (MK)]`` and
-    gradients in a second one, so the data-parallel exchange is a single all-reduce of
-    3HW+MK floats (16,316 for the ALU chip).  ``step(x, y)`` copies the batch into the
-    static input buffers (host tensors: from pinned memory, asynchronously) and returns the
-    device loss.  ``capture()`` records the launch sequence into a CUDA graph (single
-    process only).  Every launch goes through ``libneurocell_b200.so``.
+    gradients in a second one, so the data-parallel exchange moves 3HW+MK floats (16,316
+    for the ALU chip).  ``exchange`` picks how, when ``process_group`` spans several ranks:
+    ``"nccl"`` all-reduces the packed gradient with the process group and then runs the SGD
+    kernel; ``"nvlink"`` runs one kernel that sums the ranks' gradients over NVLink peer
+    memory and applies SGD (:class:`NVLinkExchange`).  ``step(x, y)`` copies the batch into
+    the static input buffers (host tensors: from pinned memory, asynchronously) and returns
+    the device loss.  ``capture()`` records the launch sequence into a CUDA graph.  Every
+    kernel of the step except NCCL's comes from ``libneurocell_b200.so``.
     """
 
     def __init__(self, topology, params: VNNParams, batch_size: int, lr: float = 1e-2,
                  loss: str = "mse", activate=torch.tanh, final_activate=None, norm: bool = True,
                  hard_pin_io: bool = False, gated_filters: bool = False,
                  codd_mode: str = "continuous", state_temperature: float = 1.0,
-                 active_threshold: float = 0.6, in_shapes=None, process_group=None):
+                 active_threshold: float = 0.6, in_shapes=None, process_group=None,
+                 exchange: str = "nccl"):
         import ctypes
         from . import _lib
         from .params import check_codd_mode
         check_codd_mode(codd_mode)
         if loss not in ("mse", "ce"):
             raise ValueError(f"Unsupported loss '{loss}'; choose from ('mse', 'ce').")
+        if exchange not in ("nccl", "nvlink"):
+            raise ValueError(f"Unsupported exchange '{exchange}'; choose from ('nccl', 'nvlink').")
         dev = params.cell_params.device
         ops._require_cuda(params.cell_params, "params.cell_params")
         act, slope = ops.resolve_activation(activate)
@@ -129,12 +228,17 @@ class VNNTrainStep:
         self.loss = torch.zeros((), dtype=torch.float32, device=dev)
         self.codd = ops._codd(codd_mode, state_temperature, active_threshold)
         self.graph = None
+        self.exchange = None
+        if exchange == "nvlink" and self.world > 1:
+            self.exchange = NVLinkExchange(self.n_cell + self.n_filt, process_group, dev)
+        self._launches = None
 
-    # number of library kernel launches per step (for the bench's launch count)
     def launches_per_step(self) -> int:
-        t = self.plan.topo
-        bwd = 1 + 2 + (2 if (t.padding == 0 and t.depth > 1) else 0) + 1
-        return 2 + 1 + bwd + 1
+        """Kernels ``libneurocell_b200.so`` launches per step, counted by the library while
+        the step is captured (or, before ``capture()``, while one eager step runs)."""
+        if self._launches is None:
+            raise RuntimeError("run step() or capture() once before asking for the launch count")
+        return self._launches
 
     def set_temperature(self, tau: float) -> None:
         self.codd.temperature = float(tau)
@@ -142,6 +246,7 @@ class VNNTrainStep:
     def _launch(self) -> None:
         c, lib, P = self.ctypes, self.lib, ops._ptr
         st = ops._stream(self.device)
+        n0 = lib.nc_launch_count()
         t = c.byref(self.plan.topo)
         cell = self.flat.data_ptr()
         filt = cell + 4 * self.n_cell
@@ -162,10 +267,15 @@ class VNNTrainStep:
                                             P(self.x), self.B, c.byref(self.codd), P(self.g_out),
                                             c.c_void_p(gcell), c.c_void_p(gfilt), P(self.ws),
                                             self.ws_bytes, st), "nc_vnn_backward")
-        world = allreduce_mean_(self.grads, self.pg)
-        lr = self.lr / world                # mean of the per-rank mean-loss gradients
-        self._lib.check(lib.nc_sgd_update(c.c_void_p(cell), c.c_void_p(gcell),
-                                          self.n_cell + self.n_filt, lr, st), "nc_sgd_update")
+        if self.exchange is not None:
+            # sum over ranks + params -= lr / world * sum, in one kernel over NVLink
+            self.exchange.allreduce_sgd(gcell, cell, self.lr, st)
+        else:
+            world = allreduce_mean_(self.grads, self.pg)
+            lr = self.lr / world            # mean of the per-rank mean-loss gradients
+            self._lib.check(lib.nc_sgd_update(c.c_void_p(cell), c.c_void_p(gcell),
+                                              self.n_cell + self.n_filt, lr, st), "nc_sgd_update")
+        self._launches = int(lib.nc_launch_count() - n0)
 
     def load_batch(self, x: torch.Tensor, y: torch.Tensor) -> None:
         self.x.copy_(x.reshape(self.B, -1), non_blocking=True)
@@ -196,9 +306,16 @@ class VNNTrainStep:
         self.flat.copy_(saved)             # warm-up and capture must not move the parameters
         self.graph = g
 
+    def exchange_status(self) -> int:
+        """Status word of the NVLink exchange (0 ok, 1 a peer timed out); 0 without one."""
+        return 0 if self.exchange is None else self.exchange.status()
+
     def release(self) -> None:
-        """Drops the captured graph (required before destroy_process_group)."""
+        """Drops the captured graph and unmaps the NVLink exchange buffers (collective when
+        data parallel; required before destroy_process_group)."""
         self.graph = None
+        if self.exchange is not None:
+            self.exchange.close()
 
 
 class VNNTrainer:

@@ -27,7 +27,7 @@ def _problem(B):
     return cell, filt, x.reshape(B, -1), y
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, exchange="nccl", graph=False):
     import sys
     from datetime import timedelta
     import torch.distributed as dist
@@ -45,34 +45,75 @@ def _rank_main(rank, world, port, out_dir):
         topo = nc.ChipTopology2D.alu_chip()
         p = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
         st = nc.trainer.VNNTrainStep(topo, p, 32, lr=1e-2, in_shapes=((8, 1),) * 3,
-                                     process_group=dist.group.WORLD)
-        st.step(torch.tensor(x[shard], device=dev), torch.tensor(y[shard], device=dev))
+                                     process_group=dist.group.WORLD, exchange=exchange)
+        xs, ys = torch.tensor(x[shard], device=dev), torch.tensor(y[shard], device=dev)
+        if graph:
+            st.load_batch(xs, ys)
+            st.capture()
+        st.step(xs, ys)
         torch.cuda.synchronize()
         np.save(os.path.join(out_dir, f"grads{rank}.npy"), st.grads.cpu().numpy())
         np.save(os.path.join(out_dir, f"params{rank}.npy"), st.flat.cpu().numpy())
+        if graph:                       # three more steps through the graph
+            for _ in range(3):
+                st.step(xs, ys)
+            torch.cuda.synchronize()
+            np.save(os.path.join(out_dir, f"params4_{rank}.npy"), st.flat.cpu().numpy())
+        np.save(os.path.join(out_dir, f"status{rank}.npy"), np.array([st.exchange_status()]))
+        st.release()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_data_parallel_step_matches_full_batch(tmp_path):
-    import torch.multiprocessing as mp
-    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
-                       start_method="spawn")
+def _full_batch_reference(steps=1):
     import neurocell_b200 as nc
     cell, filt, x, y = _problem(64)
     dev = torch.device("cuda", 0)
     p = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
     st = nc.trainer.VNNTrainStep(nc.ChipTopology2D.alu_chip(), p, 64, lr=1e-2,
                                  in_shapes=((8, 1),) * 3)
-    st.step(torch.tensor(x, device=dev), torch.tensor(y, device=dev))
+    xs, ys = torch.tensor(x, device=dev), torch.tensor(y, device=dev)
+    st.step(xs, ys)
     torch.cuda.synchronize()
-    full = st.grads.cpu().numpy()
+    full_g, full_p = st.grads.cpu().numpy(), st.flat.cpu().numpy()
+    for _ in range(steps - 1):
+        st.step(xs, ys)
+    torch.cuda.synchronize()
+    return full_g, full_p, st.flat.cpu().numpy()
+
+
+def _run(tmp_path, exchange, graph=False):
+    import torch.multiprocessing as mp
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path), exchange, graph),
+                       nprocs=2, join=True, start_method="spawn")
+
+
+def _check_first_step(tmp_path, full_g, full_p):
     g0 = np.load(tmp_path / "grads0.npy") / 2.0
     g1 = np.load(tmp_path / "grads1.npy") / 2.0
     assert np.array_equal(g0, g1)                       # every rank holds the same sum
-    assert np.linalg.norm(g0 - full) / np.linalg.norm(full) <= 1e-5
+    assert np.linalg.norm(g0 - full_g) / np.linalg.norm(full_g) <= 1e-5
     p0, p1 = np.load(tmp_path / "params0.npy"), np.load(tmp_path / "params1.npy")
     assert np.array_equal(p0, p1)
-    assert np.linalg.norm(p0 - st.flat.cpu().numpy()) / np.linalg.norm(p0) <= 1e-6
+    assert np.linalg.norm(p0 - full_p) / np.linalg.norm(p0) <= 1e-6
+    assert np.load(tmp_path / "status0.npy")[0] == 0 and np.load(tmp_path / "status1.npy")[0] == 0
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_data_parallel_step_matches_full_batch(tmp_path):
+    _run(tmp_path, "nccl")
+    full_g, full_p, _ = _full_batch_reference()
+    _check_first_step(tmp_path, full_g, full_p)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_nvlink_exchange_matches_full_batch(tmp_path):
+    """The fused peer-memory sum + SGD kernel, eager step then three graph replays: the
+    ranks stay bitwise identical and track the single-GPU full-batch run."""
+    _run(tmp_path, "nvlink", graph=True)
+    full_g, full_p, full_p4 = _full_batch_reference(steps=4)
+    _check_first_step(tmp_path, full_g, full_p)
+    q0, q1 = np.load(tmp_path / "params4_0.npy"), np.load(tmp_path / "params4_1.npy")
+    assert np.array_equal(q0, q1)
+    assert np.linalg.norm(q0 - full_p4) / np.linalg.norm(full_p4) <= 1e-5
