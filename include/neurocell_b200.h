@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define NC_ABI_VERSION 1
+#define NC_ABI_VERSION 2
 
 typedef enum nc_status {
   NC_OK = 0,
@@ -54,6 +54,14 @@ typedef enum nc_activation {
   NC_ACT_LEAKY_RELU = 4,
   NC_ACT_GELU = 5, /* tanh approximation */
 } nc_activation;
+
+/*
+ * Green's convolution algorithm (the reference's backend choice, propagator.py:58-85):
+ * DIRECT = on-chip direct cross-correlation ("nchw_direct" / "pallas_fused"), FFT = 2-D
+ * FFT convolution on the next power-of-two grid ("pallas_sram"), AUTO = FFT when
+ * kh*kw > 512 and the padding is not CIRCULAR (the reference's auto rule), else DIRECT.
+ */
+typedef enum nc_conv_algo { NC_CONV_AUTO = 0, NC_CONV_DIRECT = 1, NC_CONV_FFT = 2 } nc_conv_algo;
 
 /* Codd modes (neurocell/params.py:23-28). */
 typedef enum nc_codd_mode {
@@ -83,6 +91,7 @@ typedef struct nc_topo {
   int32_t norm;            /* spatial standardisation on (1) / off (0)               */
   int32_t hard_pin_io;     /* params.py:55-79                                        */
   int32_t gated_filters;   /* propagator.py:262-264: filters -> sigmoid(filters)     */
+  int32_t conv_algo;       /* nc_conv_algo (FFT needs both FFT sides <= 1024)        */
 } nc_topo;
 
 /* Per-call Codd options (traced scalars in the reference, trainer.py:285-302). */

@@ -3,11 +3,15 @@
 #include <stdio.h>
 #include <string.h>
 #include <atomic>
+#include <cmath>
+#include <vector>
 
 #include <cuda_runtime.h>
 
 #include "nc_errors.h"
 #include "nc_fast.cuh"
+#include "nc_fft.cuh"
+#include "nc_fftconv.h"
 #include "nc_internal.h"
 #include "nc_kernels.cuh"
 
@@ -151,6 +155,8 @@ struct Prepared {
   const int32_t* out_index;
   const uint8_t* io;
   const uint8_t* owm;
+  const float2* tw_w;
+  const float2* tw_h;
 };
 
 static nc_status prepare(const nc_topo* topo, const void* plan, int32_t batch, uint32_t flags,
@@ -172,7 +178,44 @@ static nc_status prepare(const nc_topo* topo, const void* plan, int32_t batch, u
   pr->out_index = at<int32_t>(plan, PL.out_index);
   pr->io = at<uint8_t>(plan, PL.io_mask);
   pr->owm = at<uint8_t>(plan, PL.out_w_mask);
+  pr->tw_w = at<float2>(plan, PL.twid_w);
+  pr->tw_h = at<float2>(plan, PL.twid_h);
   return NC_OK;
+}
+
+// Arguments of the FFT-regime loop (nc_fftconv.cu) from a prepared call.
+static FftCall fft_call(const Prepared& pr, void* ws, const float* inputs, int batch, bool train) {
+  FftCall c;
+  memset(&c, 0, sizeof(c));
+  const WsLayout& L = pr.L;
+  c.g = pr.g;
+  c.batch = batch;
+  c.train = train;
+  c.sp = pr.sp;
+  c.in_index = pr.in_index;
+  c.out_index = pr.out_index;
+  c.inputs = inputs;
+  c.tw_w = pr.tw_w;
+  c.tw_h = pr.tw_h;
+  c.field = at<float>(ws, L.f_field);
+  c.xhat = at<float2>(ws, L.f_xhat);
+  c.tmp = at<float2>(ws, L.f_tmp);
+  c.gspec = at<float2>(ws, L.f_gspec);
+  c.mean = at<float>(ws, L.f_mean);
+  c.rstd = at<float>(ws, L.f_rstd);
+  c.zscr = at<float>(ws, L.zscr);
+  c.zhat = at<float>(ws, L.zhat);
+  c.rstd_save = at<float>(ws, L.rstd);
+  c.xsave = at<float>(ws, L.xsave);
+  c.q = at<float2>(ws, L.f_q);
+  c.dgacc = at<float2>(ws, L.f_dgacc);
+  c.gz = at<float>(ws, L.f_gz);
+  c.dx = at<float>(ws, L.f_dx);
+  c.gpart = at<float>(ws, L.f_gpart);
+  c.gsum = at<float>(ws, L.gsum);
+  c.gdsum = at<float>(ws, L.gdsum);
+  c.gborder = (pr.g.padding == NC_PAD_VALID && pr.g.d > 1) ? at<float>(ws, L.gborder) : nullptr;
+  return c;
 }
 
 static nc_status launch_prestep(const Prepared& pr, const float* cell, const float* filters,
@@ -215,6 +258,22 @@ nc_status nc_plan_build(const nc_topo* topo, const int32_t* in_index, const int3
     return set_error(NC_ERR_WORKSPACE, "plan buffer too small: %zu < %zu", plan_bytes, PL.total);
   if ((g.n_in > 0 && !in_index) || !out_index || !io_mask || !out_w_mask)
     return set_error(NC_ERR_INVALID, "null plan table");
+  // FFT stage twiddles exp(-2 pi i q j / S), stage by stage (layout: nc_fft.cuh)
+  std::vector<float2> tw[2];
+  if (PL.twid_w != SIZE_MAX) {
+    for (int side = 0; side < 2; ++side) {
+      const int N = side == 0 ? g.Nw : g.Nh;
+      for (int S = N; S > 1;) {
+        const int R = fft::stage_radix(S), h = S / R;
+        for (int q = 1; q < R; ++q)
+          for (int j = 0; j < h; ++j) {
+            const double a = -2.0 * M_PI * (double)q * (double)j / (double)S;
+            tw[side].push_back(make_float2((float)std::cos(a), (float)std::sin(a)));
+          }
+        S /= R;
+      }
+    }
+  }
   const int HW = g.H * g.W;
   for (int j = 0; j < g.n_in; ++j)
     if (in_index[j] >= HW || in_index[j] < -1)
@@ -239,6 +298,12 @@ nc_status nc_plan_build(const nc_topo* topo, const int32_t* in_index, const int3
                                 cudaMemcpyHostToDevice, st));
   NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.io_mask, io_mask, (size_t)HW, cudaMemcpyHostToDevice, st));
   NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.out_w_mask, out_w_mask, (size_t)HW, cudaMemcpyHostToDevice, st));
+  if (PL.twid_w != SIZE_MAX) {
+    NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.twid_w, tw[0].data(), sizeof(float2) * tw[0].size(),
+                                  cudaMemcpyHostToDevice, st));
+    NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.twid_h, tw[1].data(), sizeof(float2) * tw[1].size(),
+                                  cudaMemcpyHostToDevice, st));
+  }
   NC_CUDA_CHECK(cudaStreamSynchronize(st));   // host tables may be freed after return
   return NC_OK;
 }
@@ -264,6 +329,15 @@ nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* c
   NC_CHECK(launch_prestep(pr, cell_params, filters, codd, st));
 
   const bool train = (flags & NC_FLAG_TRAIN) != 0;
+  if (pr.g.algo == NC_CONV_FFT) {
+    FftCall c = fft_call(pr, d_ws, inputs, batch, train);
+    c.out = out;
+    if (g_prof.fs) NC_CUDA_CHECK(cudaEventRecord(g_prof.fs, st));
+    NC_CHECK(fft_forward(c, st));
+    if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
+    clear_error();
+    return NC_OK;
+  }
   FwdArgs a;
   memset(&a, 0, sizeof(a));
   a.g = pr.g;
@@ -318,6 +392,19 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
   cudaStream_t st = as_stream(stream);
   const Geo& g = pr.g;
   const WsLayout& L = pr.L;
+  if (g.algo == NC_CONV_FFT) {
+    FftCall c = fft_call(pr, d_ws, inputs, batch, true);
+    c.gout = g_out;
+    if (g_prof.bs) NC_CUDA_CHECK(cudaEventRecord(g_prof.bs, st));
+    NC_CHECK(fft_backward(c, st));
+    if (g_prof.be) NC_CUDA_CHECK(cudaEventRecord(g_prof.be, st));
+    const int HW = g.H * g.W;
+    prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, c.gsum,
+                                                         c.gborder, c.gdsum, g_cell_params, g_filters);
+    NC_CHECK(launch_check("prestep_bwd_kernel launch"));
+    clear_error();
+    return NC_OK;
+  }
 
   BwdArgs a;
   memset(&a, 0, sizeof(a));

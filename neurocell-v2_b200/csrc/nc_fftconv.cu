@@ -1,0 +1,730 @@
+// nc_fftconv.cu -- the d-step VNN loop with FFT Green's convolution (sm_100a).
+//
+// The reference's large-kernel regime ("pallas_sram": rfft2_pruned / irfft2_pruned and the
+// Plancherel VJP of neurocell/kernels_greens.py:25-66, 278-400 and
+// neurocell/kernels_pallas.py:1759-1826) rebuilt around complex power-of-two transforms:
+//
+//  * two samples share one complex transform (real parts = sample 2p, imaginary = 2p+1).
+//    The filter spectra are spectra of real signals, so a product with them keeps the two
+//    samples apart: IFFT(X^ . conj(G^_m)) = z_{2p,m} + i z_{2p+1,m} (forward) and
+//    IFFT(sum_m Q^_m . G^_m) = dX_{2p} + i dX_{2p+1} (field adjoint), and
+//    Re IFFT(X^ . conj(Q^_m)) = sum over the pair of corr(X_b, gz_{b,m}) (filter adjoint),
+//  * the forward transforms leave spectra digit-reversed and the inverse transforms take
+//    them back (nc_fft.cuh), so no pass reorders data,
+//  * the transforms are pruned to the rows that hold data (field rows < Fh, plane rows
+//    < roi_h) and to the rows and columns that are kept (ROI outputs, kh x kw filter lags),
+//  * the filter-gradient spectrum is accumulated over samples and steps in a fixed order
+//    and transformed back once per call (the reference's "dK reduced over B and d before one
+//    M-irfft2"); every other batch reduction is a fixed-order loop as well, so the backward
+//    is deterministic.
+// The per-step epilogues have the semantics of neurocell/epilogue.py:28-56 / :82-128 with
+// the centred two-pass variance of neurocell/kernels_pallas.py:202-205, as in nc_fused.cu.
+#include <cuda_runtime.h>
+
+#include "nc_common.cuh"
+#include "nc_errors.h"
+#include "nc_fft.cuh"
+#include "nc_fftconv.h"
+
+namespace nc {
+
+using fft::cadd;
+using fft::cmul;
+using fft::cmulc;
+using fft::line_stride;
+using fft::pidx;
+
+namespace {
+
+constexpr int kFftThreads = 256;
+constexpr int kEpiThreads = 256;
+
+// Real planes addressed as  base + b*sstride + m*plane + r*rs + e.
+struct Planes {
+  float* ptr;
+  size_t sstride;
+  int nsamp, ms, rows, cols, plane, rs;
+  int pack;     // 1: a line holds samples (2g, 2g+1) as (re, im); 0: one sample, im = 0
+  int units;    // lines / rows = (nsamp or pairs) * ms
+  float scale;
+};
+
+__device__ __forceinline__ int even_up(int x) { return (x + 1) & ~1; }
+
+// Forward row transforms of real planes -> dst (lines, N) complex.
+__global__ void __launch_bounds__(kFftThreads) rows_fwd_kernel(Planes a, float2* __restrict__ dst,
+                                                                int N, const float2* __restrict__ tw,
+                                                                int L) {
+  extern __shared__ float2 sm[];
+  const int TN = fft::twiddle_table_len(N);
+  float2* stw = sm;
+  float2* s = sm + even_up(TN);
+  const int LS = line_stride(N), lgN = fft::ilog2(N);
+  const int total = a.units * a.rows;
+  const int line0 = blockIdx.x * L;
+  const int nl = min(L, total - line0);
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
+  for (int idx = tid; idx < nl * N; idx += nt) {
+    const int l = idx >> lgN, e = idx & (N - 1);
+    const int line = line0 + l;
+    const int u = line / a.rows, r = line - u * a.rows;
+    const int gs = u / a.ms, m = u - gs * a.ms;
+    float re = 0.f, im = 0.f;
+    if (e < a.cols) {
+      const int b1 = a.pack ? 2 * gs : gs;
+      const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
+      re = a.ptr[(size_t)b1 * a.sstride + off] * a.scale;
+      if (a.pack && b1 + 1 < a.nsamp) im = a.ptr[(size_t)(b1 + 1) * a.sstride + off] * a.scale;
+    }
+    s[l * LS + pidx(e)] = make_float2(re, im);
+  }
+  fft::transform_lines<false>(s, nl, N, stw, tid, nt);
+  for (int idx = tid; idx < nl * N; idx += nt) {
+    const int l = idx >> lgN, e = idx & (N - 1);
+    dst[(size_t)(line0 + l) * N + e] = s[l * LS + pidx(e)];
+  }
+}
+
+// Inverse row transforms of src (lines, N) -> real planes (re -> sample 2g, im -> 2g+1).
+__global__ void __launch_bounds__(kFftThreads) rows_inv_kernel(const float2* __restrict__ src,
+                                                                Planes a, int N,
+                                                                const float2* __restrict__ tw,
+                                                                int L) {
+  extern __shared__ float2 sm[];
+  const int TN = fft::twiddle_table_len(N);
+  float2* stw = sm;
+  float2* s = sm + even_up(TN);
+  const int LS = line_stride(N), lgN = fft::ilog2(N);
+  const int total = a.units * a.rows;
+  const int line0 = blockIdx.x * L;
+  const int nl = min(L, total - line0);
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
+  for (int idx = tid; idx < nl * N; idx += nt) {
+    const int l = idx >> lgN, e = idx & (N - 1);
+    s[l * LS + pidx(e)] = src[(size_t)(line0 + l) * N + e];
+  }
+  fft::transform_lines<true>(s, nl, N, stw, tid, nt);
+  for (int idx = tid; idx < nl * a.cols; idx += nt) {
+    const int l = idx / a.cols, e = idx - l * a.cols;
+    const int line = line0 + l;
+    const int u = line / a.rows, r = line - u * a.rows;
+    const int gs = u / a.ms, m = u - gs * a.ms;
+    const int b1 = a.pack ? 2 * gs : gs;
+    const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
+    const float2 v = s[l * LS + pidx(e)];
+    a.ptr[(size_t)b1 * a.sstride + off] = v.x * a.scale;
+    if (a.pack && b1 + 1 < a.nsamp) a.ptr[(size_t)(b1 + 1) * a.sstride + off] = v.y * a.scale;
+  }
+}
+
+enum ColMode { COL_FWD = 0, COL_INV_MULCONJ = 1, COL_INV_SUM = 2, COL_INV_PLAIN = 3 };
+
+struct ColArgs {
+  const float2* src;    // FWD / PLAIN: (units, rows_in, Nw); MULCONJ: x^ (pairs, Nh, Nw);
+                        // SUM: q^ (pairs, M, Nh, Nw)
+  const float2* spec;   // (M, Nh, Nw) filter spectra (MULCONJ, SUM)
+  float2* dst;          // FWD: (units, Nh, Nw); inverse modes: (units, rows_out, Nw)
+  int Nh, Nw, rows_in, rows_out, M;
+  float scale;          // FWD only
+};
+
+// Column transforms of C adjacent columns per CTA (blockIdx.y = unit).
+template <int MODE>
+__global__ void __launch_bounds__(kFftThreads) cols_kernel(ColArgs a, const float2* __restrict__ tw,
+                                                            int C) {
+  extern __shared__ float2 sm[];
+  const int N = a.Nh;
+  const int TN = fft::twiddle_table_len(N);
+  float2* stw = sm;
+  float2* s = sm + even_up(TN);
+  const int LS = line_stride(N), lgC = fft::ilog2(C);
+  const int c0 = blockIdx.x * C;
+  const int u = blockIdx.y;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const size_t NN = (size_t)a.Nh * a.Nw;
+  for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
+  for (int idx = tid; idx < N * C; idx += nt) {
+    const int r = idx >> lgC, cc = idx & (C - 1);
+    const int c = c0 + cc;
+    float2 v = make_float2(0.f, 0.f);
+    if (MODE == COL_FWD || MODE == COL_INV_PLAIN) {
+      if (r < a.rows_in) {
+        v = a.src[((size_t)u * a.rows_in + r) * a.Nw + c];
+        if (MODE == COL_FWD) { v.x *= a.scale; v.y *= a.scale; }
+      }
+    } else if (MODE == COL_INV_MULCONJ) {
+      const int p = u / a.M, m = u - p * a.M;
+      const size_t off = (size_t)r * a.Nw + c;
+      v = cmulc(a.src[(size_t)p * NN + off], a.spec[(size_t)m * NN + off]);
+    } else {
+      const size_t off = (size_t)r * a.Nw + c;
+      const float2* q = a.src + (size_t)u * a.M * NN + off;
+      for (int m = 0; m < a.M; ++m) v = cadd(v, cmul(q[(size_t)m * NN], a.spec[(size_t)m * NN + off]));
+    }
+    s[cc * LS + pidx(r)] = v;
+  }
+  fft::transform_lines<MODE != COL_FWD>(s, C, N, stw, tid, nt);
+  const int rows_st = (MODE == COL_FWD) ? N : a.rows_out;
+  for (int idx = tid; idx < rows_st * C; idx += nt) {
+    const int r = idx >> lgC, cc = idx & (C - 1);
+    a.dst[((size_t)u * rows_st + r) * a.Nw + c0 + cc] = s[cc * LS + pidx(r)];
+  }
+}
+
+// acc[m][f] (+)= sum over pairs of x^[p][f] * conj(q^[p][m][f])  (fixed pair order).
+__global__ void dg_accum_kernel(const float2* __restrict__ xhat, const float2* __restrict__ q,
+                                float2* __restrict__ acc, int pairs, int M, size_t NN, int init) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)M * NN) return;
+  const int m = (int)(i / NN);
+  const size_t f = i - (size_t)m * NN;
+  float2 s = init ? make_float2(0.f, 0.f) : acc[i];
+  for (int p = 0; p < pairs; ++p) s = cadd(s, cmulc(xhat[(size_t)p * NN + f], q[((size_t)p * M + m) * NN + f]));
+  acc[i] = s;
+}
+
+__device__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    float r = lane < nw ? red[lane] : 0.f;
+    r = warp_sum(r);
+    if (lane == 0) red[32] = r;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// ---------------------------------------------------------------------------------------
+// fields
+// ---------------------------------------------------------------------------------------
+
+// Step-0 inputs scattered into a zeroed field (propagator.py:103-191).
+__global__ void field_inject_kernel(Geo g, float* __restrict__ field, const int32_t* __restrict__ in_index,
+                                    const float* __restrict__ inputs, int B) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)B * g.n_in) return;
+  const int b = (int)(i / g.n_in), j = (int)(i - (size_t)b * g.n_in);
+  const int idx = in_index[j];
+  if (idx < 0) return;
+  const int r = idx / g.W, c = idx - (idx / g.W) * g.W;
+  field[(size_t)b * g.Fh * g.Fw + (size_t)(r + g.gr) * g.Fw + c + g.gc] = inputs[i];
+}
+
+// Field ring for the next convolution: VALID -> border template, CIRCULAR -> wrapped
+// interior (SAME keeps its zero halo and never calls this).
+__global__ void field_ring_kernel(Geo g, float* __restrict__ field, const float* __restrict__ border, int B) {
+  const int FF = g.Fh * g.Fw;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)B * FF) return;
+  const int b = (int)(i / FF), k = (int)(i - (size_t)b * FF);
+  const int fr = k / g.Fw, fc = k - (k / g.Fw) * g.Fw;
+  const int r = fr - g.oh, c = fc - g.ow;
+  if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) return;
+  float* F = field + (size_t)b * FF;
+  if (g.padding == NC_PAD_VALID) {
+    F[k] = border[k];   // VALID: the field is the grid
+  } else {
+    int sr = r % g.roi_h; if (sr < 0) sr += g.roi_h;
+    int sc = c % g.roi_w; if (sc < 0) sc += g.roi_w;
+    F[k] = F[(sr + g.oh) * g.Fw + sc + g.ow];
+  }
+}
+
+// Interior of the field entering step t >= 1 from the saved residual.
+__global__ void field_interior_kernel(Geo g, float* __restrict__ field, const float* __restrict__ xs,
+                                      size_t xs_stride, int B) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)B * g.P) return;
+  const int b = (int)(i / g.P), p = (int)(i - (size_t)b * g.P);
+  const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+  field[(size_t)b * g.Fh * g.Fw + (size_t)(r + g.oh) * g.Fw + c + g.ow] = xs[(size_t)b * xs_stride + p];
+}
+
+// ---------------------------------------------------------------------------------------
+// forward epilogues (planes z at z + b*zs + m*P)
+// ---------------------------------------------------------------------------------------
+
+// Per-(b, m) mean and 1/sqrt(var + eps), centred two-pass (kernels_pallas.py:200-205).
+__global__ void __launch_bounds__(kEpiThreads) plane_stats_kernel(Geo g, const float* __restrict__ z,
+                                                                   size_t zs, float* mean, float* rstd,
+                                                                   float* rstd_save, int t) {
+  __shared__ float red[33];
+  const int bm = blockIdx.x, b = bm / g.M, m = bm - b * g.M;
+  const float* zp = z + (size_t)b * zs + (size_t)m * g.P;
+  float mu = 0.f, rs = 1.f;
+  if (g.norm) {
+    const float inv_n = 1.0f / (float)g.P;
+    float s = 0.f;
+    for (int p = threadIdx.x; p < g.P; p += blockDim.x) s += zp[p];
+    mu = block_sum(s, red) * inv_n;
+    float v = 0.f;
+    for (int p = threadIdx.x; p < g.P; p += blockDim.x) {
+      const float dz = zp[p] - mu;
+      v = fmaf(dz, dz, v);
+    }
+    const float var = block_sum(v, red) * inv_n;
+    rs = 1.0f / sqrtf(var + kNormEps);
+  }
+  if (threadIdx.x == 0) {
+    mean[bm] = mu;
+    rstd[bm] = rs;
+    if (rstd_save) rstd_save[((size_t)b * g.d + t) * g.M + m] = rs;
+  }
+}
+
+// Hidden-step epilogue (epilogue.py:28-56): standardise (in place when zhat != null), gate,
+// write the next field's interior and the training residual.
+__global__ void hidden_epi_kernel(Geo g, StepParams sp, float* z, size_t zs, int write_zhat,
+                                  const float* __restrict__ mean, const float* __restrict__ rstd,
+                                  float* __restrict__ field, float* __restrict__ xsave, int t, int B) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)B * g.P) return;
+  const int b = (int)(i / g.P), p = (int)(i - (size_t)b * g.P);
+  const float bb = sp.broi[p];
+  float lin = 0.f, act = 0.f;
+  float* zb = z + (size_t)b * zs + p;
+  for (int m = 0; m < g.M; ++m) {
+    const float zh = (zb[(size_t)m * g.P] - mean[b * g.M + m]) * rstd[b * g.M + m];
+    if (write_zhat) zb[(size_t)m * g.P] = zh;
+    lin += zh;
+    if (g.act != NC_ACT_NONE) act += act_fwd(g.act, zh + bb, g.slope);
+  }
+  if (g.act == NC_ACT_NONE) act = lin + (float)g.M * bb;
+  const float xn = sp.weff[p] * lin + sp.seff[p] * act;
+  const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+  field[(size_t)b * g.Fh * g.Fw + (size_t)(r + g.oh) * g.Fw + c + g.ow] = xn;
+  if (xsave) xsave[((size_t)b * (g.d - 1) + t) * g.P + p] = xn;
+}
+
+// Output-port epilogue (epilogue.py:82-128) from the raw planes and their statistics.
+__global__ void port_out_kernel(Geo g, StepParams sp, const int32_t* __restrict__ out_index,
+                                const float* __restrict__ z, size_t zs, const float* __restrict__ mean,
+                                const float* __restrict__ rstd, float* __restrict__ out, int B) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * g.n_out) return;
+  const int b = i / g.n_out, j = i - b * g.n_out;
+  const int idx = out_index[j];
+  const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
+  const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+  const float wo = sp.weff[p], so = sp.seff[p], bo = sp.broi[p];
+  const float* zb = z + (size_t)b * zs + p;
+  float lin = 0.f, act = 0.f;
+  for (int m = 0; m < g.M; ++m) {
+    const float zh = (zb[(size_t)m * g.P] - mean[b * g.M + m]) * rstd[b * g.M + m];
+    lin += zh;
+    if (g.fact != NC_ACT_NONE) act += act_fwd(g.fact, zh + bo, g.fslope);
+  }
+  out[i] = (g.fact == NC_ACT_NONE) ? (wo + so) * lin + ((float)g.M * so * bo)
+                                   : act_fwd(g.fact, wo * lin + so * act, g.fslope);
+}
+
+// Training residual of the output step: planes standardised in place.
+__global__ void normalize_kernel(Geo g, float* z, size_t zs, const float* __restrict__ mean,
+                                 const float* __restrict__ rstd, int B) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t MP = (size_t)g.M * g.P;
+  if (i >= (size_t)B * MP) return;
+  const int b = (int)(i / MP);
+  const size_t k = i - (size_t)b * MP;
+  const int m = (int)(k / g.P);
+  float* v = z + (size_t)b * zs + k;
+  *v = (*v - mean[b * g.M + m]) * rstd[b * g.M + m];
+}
+
+// ---------------------------------------------------------------------------------------
+// backward epilogues
+// ---------------------------------------------------------------------------------------
+
+// Output-step adjoint at the port cells (kernels_pallas.py:1378-1504): sparse plane
+// gradients (gz must be zero elsewhere) and the port cells' parameter gradients, summed
+// over the batch in sample order.
+__global__ void port_gz_kernel(Geo g, StepParams sp, const int32_t* __restrict__ out_index,
+                               const float* __restrict__ gout, const float* __restrict__ zh_t,
+                               size_t zs, float* __restrict__ gz, float* __restrict__ gsum, int B) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= g.n_out) return;
+  const int idx = out_index[j];
+  const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
+  const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+  const size_t P = (size_t)g.P;
+  const float wo = sp.weff[p], so = sp.seff[p], bo = sp.broi[p];
+  float gp0 = 0.f, gp1 = 0.f, gp2 = 0.f;
+  for (int b = 0; b < B; ++b) {
+    const float go = gout[(size_t)b * g.n_out + j];
+    const float* ZH = zh_t + (size_t)b * zs + p;
+    float* GZ = gz + (size_t)b * g.M * P + p;
+    float lin = 0.f;
+    for (int m = 0; m < g.M; ++m) lin += ZH[m * P];
+    if (g.fact == NC_ACT_NONE) {
+      gp0 += go * lin;
+      gp1 += go * (lin + (float)g.M * bo);
+      gp2 += go * (float)g.M * so;
+      const float gzh = (wo + so) * go;
+      for (int m = 0; m < g.M; ++m) GZ[m * P] = gzh;
+    } else {
+      float act = 0.f;
+      for (int m = 0; m < g.M; ++m) act += act_fwd(g.fact, ZH[m * P] + bo, g.fslope);
+      float dpre;
+      act_fwd_deriv(g.fact, wo * lin + so * act, g.fslope, &dpre);
+      const float gpre = go * dpre;
+      gp0 += gpre * lin;
+      gp1 += gpre * act;
+      float db = 0.f;
+      for (int m = 0; m < g.M; ++m) {
+        float dd;
+        act_fwd_deriv(g.fact, ZH[m * P] + bo, g.fslope, &dd);
+        GZ[m * P] = gpre * (wo + so * dd);
+        db += gpre * so * dd;
+      }
+      gp2 += db;
+    }
+  }
+  gsum[p] += gp0;
+  gsum[P + p] += gp1;
+  gsum[2 * P + p] += gp2;
+}
+
+// Standardisation adjoint per (b, m): gz <- rstd (gz - mean(gz) - zh mean(gz zh)).
+__global__ void __launch_bounds__(kEpiThreads) norm_bwd_kernel(Geo g, float* __restrict__ gz,
+                                                                const float* __restrict__ zh_t, size_t zs,
+                                                                const float* __restrict__ rstd_save, int t) {
+  __shared__ float red[33];
+  const int bm = blockIdx.x, b = bm / g.M, m = bm - b * g.M;
+  float* gp = gz + (size_t)bm * g.P;
+  const float* zp = zh_t + (size_t)b * zs + (size_t)m * g.P;
+  const float inv_n = 1.0f / (float)g.P;
+  float s1 = 0.f, s2 = 0.f;
+  for (int p = threadIdx.x; p < g.P; p += blockDim.x) {
+    const float v = gp[p];
+    s1 += v;
+    s2 = fmaf(v, zp[p], s2);
+  }
+  const float c1 = block_sum(s1, red) * inv_n;
+  const float c2 = block_sum(s2, red) * inv_n;
+  const float rs = rstd_save[((size_t)b * g.d + t) * g.M + m];
+  for (int p = threadIdx.x; p < g.P; p += blockDim.x) gp[p] = rs * (gp[p] - c1 - zp[p] * c2);
+}
+
+// Field adjoint at interior cell (r, c); CIRCULAR folds the wrapped halo copies back.
+__device__ __forceinline__ float field_grad(const Geo& g, const float* dxb, int r, int c) {
+  if (g.padding != NC_PAD_CIRCULAR) return dxb[(size_t)(r + g.oh) * g.Fw + c + g.ow];
+  float s = 0.f;
+  for (int fr = (r + g.oh) % g.roi_h; fr < g.Fh; fr += g.roi_h)
+    for (int fc = (c + g.ow) % g.roi_w; fc < g.Fw; fc += g.roi_w) s += dxb[(size_t)fr * g.Fw + fc];
+  return s;
+}
+
+// Hidden-step adjoint (kernels_pallas.py:221-291) of step t-1 for the samples of chunk
+// blockIdx.y; per-chunk pixel-gradient partials go to gpart.
+__global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__ dx,
+                                 const float* __restrict__ zh_t, size_t zs, float* __restrict__ gz,
+                                 float* __restrict__ gpart, int B, int bc) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= g.P) return;
+  const int k = blockIdx.y;
+  const int b0 = k * bc, b1 = min(B, b0 + bc);
+  const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+  const size_t P = (size_t)g.P, FF = (size_t)g.Fh * g.Fw;
+  const float bb = sp.broi[p], we = sp.weff[p], se = sp.seff[p];
+  float gp0 = 0.f, gp1 = 0.f, gp2 = 0.f;
+  for (int b = b0; b < b1; ++b) {
+    const float gy = field_grad(g, dx + (size_t)b * FF, r, c);
+    const float* ZH = zh_t + (size_t)b * zs + p;
+    float* GZ = gz + (size_t)b * g.M * P + p;
+    float lin = 0.f, act = 0.f, dsum = 0.f;
+    for (int m = 0; m < g.M; ++m) {
+      const float zh = ZH[m * P];
+      float dd;
+      const float av = act_fwd_deriv(g.act, zh + bb, g.slope, &dd);
+      lin += zh;
+      act += av;
+      dsum += dd;
+      GZ[m * P] = we * gy + se * gy * dd;
+    }
+    gp0 += gy * lin;
+    gp1 += gy * act;
+    gp2 += se * gy * dsum;
+  }
+  gpart[((size_t)k * 3 + 0) * P + p] = gp0;
+  gpart[((size_t)k * 3 + 1) * P + p] = gp1;
+  gpart[((size_t)k * 3 + 2) * P + p] = gp2;
+}
+
+// gsum += sum over chunks of gpart (chunk order).
+__global__ void gsum_chunks_kernel(const float* __restrict__ gpart, float* __restrict__ gsum, int P,
+                                   int nch) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 3 * P) return;
+  const int k3 = i / P, p = i - k3 * P;
+  float s = 0.f;
+  for (int k = 0; k < nch; ++k) s += gpart[((size_t)k * 3 + k3) * P + p];
+  gsum[i] += s;
+}
+
+// VALID border-template gradient: the ring of the field adjoint summed over the batch.
+__global__ void ring_grad_kernel(Geo g, const float* __restrict__ dx, float* __restrict__ gborder, int B) {
+  const int FF = g.Fh * g.Fw;
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= FF) return;
+  const int fr = k / g.Fw, fc = k - (k / g.Fw) * g.Fw;
+  const int r = fr - g.oh, c = fc - g.ow;
+  if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) return;
+  float s = 0.f;
+  for (int b = 0; b < B; ++b) s += dx[(size_t)b * FF + k];
+  gborder[k] += s;   // the VALID field is the grid
+}
+
+// ---------------------------------------------------------------------------------------
+// host helpers
+// ---------------------------------------------------------------------------------------
+
+nc_status launched(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, what);
+  note_launch();
+  return NC_OK;
+}
+
+int rows_per_cta(int N) {
+  int L = 40960 / (9 * N);
+  if (L < 1) L = 1;
+  if (L > 64) L = 64;
+  return L;
+}
+
+size_t rows_smem(int N, int L) {
+  const int TN = fft::twiddle_table_len(N);
+  return sizeof(float2) * ((size_t)((TN + 1) & ~1) + (size_t)L * line_stride(N));
+}
+
+int cols_per_cta(int Nh, int Nw) {
+  int C = Nh >= 1024 ? 8 : 16;
+  return C < Nw ? C : Nw;
+}
+
+size_t cols_smem(int Nh, int C) {
+  const int TN = fft::twiddle_table_len(Nh);
+  return sizeof(float2) * ((size_t)((TN + 1) & ~1) + (size_t)C * line_stride(Nh));
+}
+
+nc_status smem_attr(const void* fn, size_t bytes) {
+  if (bytes > 48 * 1024)
+    NC_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return NC_OK;
+}
+
+nc_status rows_fwd(const Planes& a, float2* dst, int N, const float2* tw, cudaStream_t st) {
+  const int L = rows_per_cta(N);
+  const size_t smem = rows_smem(N, L);
+  NC_CHECK(smem_attr((const void*)rows_fwd_kernel, smem));
+  const int lines = a.units * a.rows;
+  rows_fwd_kernel<<<(lines + L - 1) / L, kFftThreads, smem, st>>>(a, dst, N, tw, L);
+  return launched("rows_fwd_kernel launch");
+}
+
+nc_status rows_inv(const float2* src, const Planes& a, int N, const float2* tw, cudaStream_t st) {
+  const int L = rows_per_cta(N);
+  const size_t smem = rows_smem(N, L);
+  NC_CHECK(smem_attr((const void*)rows_inv_kernel, smem));
+  const int lines = a.units * a.rows;
+  rows_inv_kernel<<<(lines + L - 1) / L, kFftThreads, smem, st>>>(src, a, N, tw, L);
+  return launched("rows_inv_kernel launch");
+}
+
+template <int MODE>
+nc_status cols(const ColArgs& a, int units, const float2* tw, cudaStream_t st) {
+  const int C = cols_per_cta(a.Nh, a.Nw);
+  const size_t smem = cols_smem(a.Nh, C);
+  NC_CHECK(smem_attr((const void*)cols_kernel<MODE>, smem));
+  cols_kernel<MODE><<<dim3(a.Nw / C, units), kFftThreads, smem, st>>>(a, tw, C);
+  return launched("cols_kernel launch");
+}
+
+inline unsigned blocks_for(size_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
+
+// x^ (pairs) of the field currently in c.field.
+nc_status field_spectra(const FftCall& c, cudaStream_t st) {
+  const Geo& g = c.g;
+  const int pairs = (c.batch + 1) / 2;
+  Planes f{c.field, (size_t)g.Fh * g.Fw, c.batch, 1, g.Fh, g.Fw, 0, g.Fw, 1, pairs, 1.0f};
+  NC_CHECK(rows_fwd(f, c.tmp, g.Nw, c.tw_w, st));
+  ColArgs ca{c.tmp, nullptr, c.xhat, g.Nh, g.Nw, g.Fh, g.Nh, g.M, 1.0f};
+  return cols<COL_FWD>(ca, pairs, c.tw_h, st);
+}
+
+// Field of step 0: zeros + injected inputs (+ wrapped halo).
+nc_status build_field0(const FftCall& c, cudaStream_t st) {
+  const Geo& g = c.g;
+  const size_t FF = (size_t)g.Fh * g.Fw;
+  NC_CUDA_CHECK(cudaMemsetAsync(c.field, 0, sizeof(float) * FF * c.batch, st));
+  if (g.n_in > 0) {
+    field_inject_kernel<<<blocks_for((size_t)c.batch * g.n_in, 256), 256, 0, st>>>(g, c.field, c.in_index,
+                                                                                c.inputs, c.batch);
+    NC_CHECK(launched("field_inject_kernel launch"));
+  }
+  if (g.padding == NC_PAD_CIRCULAR) {
+    field_ring_kernel<<<blocks_for(FF * c.batch, 256), 256, 0, st>>>(g, c.field, c.sp.border, c.batch);
+    NC_CHECK(launched("field_ring_kernel launch"));
+  }
+  return NC_OK;
+}
+
+nc_status field_ring(const FftCall& c, cudaStream_t st) {
+  const Geo& g = c.g;
+  if (g.padding == NC_PAD_SAME) return NC_OK;
+  const size_t FF = (size_t)g.Fh * g.Fw;
+  field_ring_kernel<<<blocks_for(FF * c.batch, 256), 256, 0, st>>>(g, c.field, c.sp.border, c.batch);
+  return launched("field_ring_kernel launch");
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------------------
+nc_status fft_forward(const FftCall& c, cudaStream_t st) {
+  const Geo& g = c.g;
+  const int B = c.batch, pairs = (B + 1) / 2;
+  const size_t P = (size_t)g.P, M = (size_t)g.M;
+
+  // filter spectra G^_m / (Nh Nw), one per direction (the reference hoists them once per
+  // batch, kernels_greens.py:240-259)
+  {
+    Planes gf{c.sp.geff, (size_t)g.K, g.M, 1, g.kh, g.kw, 0, g.kw, 0, g.M, 1.0f};
+    NC_CHECK(rows_fwd(gf, c.tmp, g.Nw, c.tw_w, st));
+    ColArgs ca{c.tmp, nullptr, c.gspec, g.Nh, g.Nw, g.kh, g.Nh, g.M, 1.0f / ((float)g.Nh * (float)g.Nw)};
+    NC_CHECK(cols<COL_FWD>(ca, g.M, c.tw_h, st));
+  }
+
+  for (int t = 0; t < g.d; ++t) {
+    if (t == 0) {
+      NC_CHECK(build_field0(c, st));
+    } else {
+      NC_CHECK(field_ring(c, st));
+    }
+    NC_CHECK(field_spectra(c, st));
+    // z = IFFT(x^ . conj(G^_m)) on the ROI rows, then columns
+    {
+      ColArgs ca{c.xhat, c.gspec, c.tmp, g.Nh, g.Nw, 0, g.roi_h, g.M, 1.0f};
+      NC_CHECK(cols<COL_INV_MULCONJ>(ca, pairs * g.M, c.tw_h, st));
+    }
+    float* z = c.train ? c.zhat + (size_t)t * M * P : c.zscr;
+    const size_t zs = c.train ? (size_t)g.d * M * P : M * P;
+    {
+      Planes zp{z, zs, B, g.M, g.roi_h, g.roi_w, g.P, g.roi_w, 1, pairs * g.M, 1.0f};
+      NC_CHECK(rows_inv(c.tmp, zp, g.Nw, c.tw_w, st));
+    }
+    plane_stats_kernel<<<B * g.M, kEpiThreads, 0, st>>>(g, z, zs, c.mean, c.rstd,
+                                                         c.train ? c.rstd_save : nullptr, t);
+    NC_CHECK(launched("plane_stats_kernel launch"));
+    if (t < g.d - 1) {
+      hidden_epi_kernel<<<blocks_for((size_t)B * P, kEpiThreads), kEpiThreads, 0, st>>>(
+          g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, c.train ? c.xsave : nullptr, t, B);
+      NC_CHECK(launched("hidden_epi_kernel launch"));
+    } else {
+      port_out_kernel<<<blocks_for((size_t)B * g.n_out, 128), 128, 0, st>>>(g, c.sp, c.out_index, z, zs,
+                                                                             c.mean, c.rstd, c.out, B);
+      NC_CHECK(launched("port_out_kernel launch"));
+      if (c.train) {
+        normalize_kernel<<<blocks_for((size_t)B * M * P, kEpiThreads), kEpiThreads, 0, st>>>(
+            g, z, zs, c.mean, c.rstd, B);
+        NC_CHECK(launched("normalize_kernel launch"));
+      }
+    }
+  }
+  return NC_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------------------
+nc_status fft_backward(const FftCall& c, cudaStream_t st) {
+  const Geo& g = c.g;
+  const int B = c.batch, pairs = (B + 1) / 2;
+  const size_t P = (size_t)g.P, M = (size_t)g.M;
+  const size_t NN = (size_t)g.Nh * g.Nw;
+  const size_t zs = (size_t)g.d * M * P;
+  const int nch = B < kRedChunks ? B : kRedChunks;
+  const int bc = (B + nch - 1) / nch;
+
+  NC_CUDA_CHECK(cudaMemsetAsync(c.gsum, 0, sizeof(float) * 3 * P, st));
+  if (c.gborder) NC_CUDA_CHECK(cudaMemsetAsync(c.gborder, 0, sizeof(float) * g.H * g.W, st));
+  NC_CUDA_CHECK(cudaMemsetAsync(c.gz, 0, sizeof(float) * B * M * P, st));
+
+  // output step: sparse port adjoint, then the standardisation adjoint
+  {
+    const float* zh = c.zhat + (size_t)(g.d - 1) * M * P;
+    port_gz_kernel<<<blocks_for(g.n_out, 128), 128, 0, st>>>(g, c.sp, c.out_index, c.gout, zh, zs, c.gz,
+                                                              c.gsum, B);
+    NC_CHECK(launched("port_gz_kernel launch"));
+    if (g.norm) {
+      norm_bwd_kernel<<<B * g.M, kEpiThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, g.d - 1);
+      NC_CHECK(launched("norm_bwd_kernel launch"));
+    }
+  }
+
+  for (int t = g.d - 1; t >= 0; --t) {
+    // the field that entered step t, and its spectra
+    if (t == 0) {
+      NC_CHECK(build_field0(c, st));
+    } else {
+      field_interior_kernel<<<blocks_for((size_t)B * P, 256), 256, 0, st>>>(
+          g, c.field, c.xsave + (size_t)(t - 1) * P, (size_t)(g.d - 1) * P, B);
+      NC_CHECK(launched("field_interior_kernel launch"));
+      NC_CHECK(field_ring(c, st));
+    }
+    NC_CHECK(field_spectra(c, st));
+    // plane-gradient spectra q^ (pairs, M)
+    {
+      Planes gp{c.gz, M * P, B, g.M, g.roi_h, g.roi_w, g.P, g.roi_w, 1, pairs * g.M, 1.0f};
+      NC_CHECK(rows_fwd(gp, c.tmp, g.Nw, c.tw_w, st));
+      ColArgs ca{c.tmp, nullptr, c.q, g.Nh, g.Nw, g.roi_h, g.Nh, g.M, 1.0f};
+      NC_CHECK(cols<COL_FWD>(ca, pairs * g.M, c.tw_h, st));
+    }
+    dg_accum_kernel<<<blocks_for(M * NN, 256), 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, g.M, NN,
+                                                             t == g.d - 1 ? 1 : 0);
+    NC_CHECK(launched("dg_accum_kernel launch"));
+    if (t == 0) break;
+
+    // field adjoint dX = IFFT(sum_m q^_m . G^_m) on the field rows, then columns
+    {
+      ColArgs ca{c.q, c.gspec, c.tmp, g.Nh, g.Nw, 0, g.Fh, g.M, 1.0f};
+      NC_CHECK(cols<COL_INV_SUM>(ca, pairs, c.tw_h, st));
+      Planes dp{c.dx, (size_t)g.Fh * g.Fw, B, 1, g.Fh, g.Fw, 0, g.Fw, 1, pairs, 1.0f};
+      NC_CHECK(rows_inv(c.tmp, dp, g.Nw, c.tw_w, st));
+    }
+    if (c.gborder) {
+      ring_grad_kernel<<<blocks_for((size_t)g.Fh * g.Fw, 256), 256, 0, st>>>(g, c.dx, c.gborder, B);
+      NC_CHECK(launched("ring_grad_kernel launch"));
+    }
+    // hidden-step adjoint of step t-1
+    const float* zh = c.zhat + (size_t)(t - 1) * M * P;
+    hidden_gz_kernel<<<dim3(blocks_for(P, 256), nch), 256, 0, st>>>(g, c.sp, c.dx, zh, zs, c.gz, c.gpart,
+                                                                    B, bc);
+    NC_CHECK(launched("hidden_gz_kernel launch"));
+    gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
+    NC_CHECK(launched("gsum_chunks_kernel launch"));
+    if (g.norm) {
+      norm_bwd_kernel<<<B * g.M, kEpiThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, t - 1);
+      NC_CHECK(launched("norm_bwd_kernel launch"));
+    }
+  }
+
+  // filter gradient: Re IFFT(acc_m) / (Nh Nw) at lags [0, kh) x [0, kw)
+  {
+    ColArgs ca{c.dgacc, nullptr, c.tmp, g.Nh, g.Nw, g.Nh, g.kh, g.M, 1.0f};
+    NC_CHECK(cols<COL_INV_PLAIN>(ca, g.M, c.tw_h, st));
+    Planes dg{c.gdsum, (size_t)g.K, g.M, 1, g.kh, g.kw, 0, g.kw, 0, g.M,
+              1.0f / ((float)g.Nh * (float)g.Nw)};
+    NC_CHECK(rows_inv(c.tmp, dg, g.Nw, c.tw_w, st));
+  }
+  return NC_OK;
+}
+
+}  // namespace nc

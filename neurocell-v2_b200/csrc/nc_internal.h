@@ -28,13 +28,20 @@ struct Geo {
   float slope, fslope;
   int norm, hard_pin, gated;
   int F_elems;             // floats of one field buffer (incl. slack rows)
+  int algo;                // resolved nc_conv_algo: NC_CONV_DIRECT or NC_CONV_FFT
+  int Nh, Nw;              // FFT grid (next powers of two of Fh, Fw)
 };
+
+// Largest FFT side the on-chip line transforms handle.
+constexpr int kFftMaxN = 1024;
 
 nc_status make_geo(const nc_topo* t, Geo* g);
 
 // Offsets (bytes) of the plan buffer sections.
 struct PlanLayout {
-  size_t in_index, out_index, io_mask, out_w_mask, total;
+  size_t in_index, out_index, io_mask, out_w_mask;
+  size_t twid_w, twid_h;   // FFT stage twiddles for the Nw and Nh transforms (FFT only)
+  size_t total;
 };
 PlanLayout plan_layout(const nc_topo* t);
 
@@ -49,6 +56,17 @@ struct WsLayout {
   // backward partials and reductions
   size_t gpix, gdpart, gdelta, gsum, gdsum, gdeltasum, gborder;
   size_t redscr;          // partial rows of the two-stage batch reductions
+  // FFT convolution (complex sections hold float2)
+  size_t f_field;         // (B, Fh, Fw) field of the current step
+  size_t f_xhat;          // (B/2, Nh, Nw) spectra of sample-pair fields
+  size_t f_tmp;           // row-pass / column-pass intermediate lines
+  size_t f_gspec;         // (M, Nh, Nw) filter spectra / (Nh*Nw)
+  size_t f_mean, f_rstd;  // (B, M) plane statistics of the current step
+  size_t f_q;             // (B/2, M, Nh, Nw) plane-gradient spectra (train)
+  size_t f_dgacc;         // (M, Nh, Nw) filter-gradient spectrum accumulator (train)
+  size_t f_gz;            // (B, M, P) plane gradients (train)
+  size_t f_dx;            // (B, Fh, Fw) field gradient (train)
+  size_t f_gpart;         // (kRedChunks, 3, P) per-chunk pixel-gradient partials (train)
   size_t total;
 };
 

@@ -9,6 +9,12 @@ namespace nc {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+static int next_pow2(int x) {
+  int n = 2;
+  while (n < x) n <<= 1;
+  return n;
+}
+
 nc_status make_geo(const nc_topo* t, Geo* g) {
   if (!t) return set_error(NC_ERR_INVALID, "topology pointer is null");
   if (t->H <= 0 || t->W <= 0) return set_error(NC_ERR_INVALID, "grid must be positive, got %dx%d", t->H, t->W);
@@ -46,6 +52,19 @@ nc_status make_geo(const nc_topo* t, Geo* g) {
   g->F_elems = (g->Fh + 1) * g->Fs;   // one slack row
   const double total_px = (double)g->M * (double)g->P;
   if (total_px > 2.0e9) return set_error(NC_ERR_UNSUPPORTED, "plane too large (%g values)", total_px);
+  // Green's convolution algorithm (reference auto rule: propagator.py:68-85)
+  g->Nh = next_pow2(g->Fh);
+  g->Nw = next_pow2(g->Fw);
+  const bool fft_fits = g->Nh <= kFftMaxN && g->Nw <= kFftMaxN;
+  if (t->conv_algo < NC_CONV_AUTO || t->conv_algo > NC_CONV_FFT)
+    return set_error(NC_ERR_INVALID, "unsupported conv_algo id %d", t->conv_algo);
+  if (t->conv_algo == NC_CONV_FFT && !fft_fits)
+    return set_error(NC_ERR_UNSUPPORTED, "FFT grid %dx%d exceeds %d per side", g->Nh, g->Nw, kFftMaxN);
+  if (t->conv_algo == NC_CONV_AUTO)
+    g->algo = (fft_fits && t->padding != NC_PAD_CIRCULAR && t->kh * t->kw > 512) ? NC_CONV_FFT
+                                                                                 : NC_CONV_DIRECT;
+  else
+    g->algo = t->conv_algo;
   return NC_OK;
 }
 
@@ -56,6 +75,13 @@ PlanLayout plan_layout(const nc_topo* t) {
   L.out_index = o; o = align256(o + sizeof(int32_t) * (size_t)t->n_out);
   L.io_mask = o; o = align256(o + (size_t)t->H * t->W);
   L.out_w_mask = o; o = align256(o + (size_t)t->H * t->W);
+  Geo g;
+  if (make_geo(t, &g) == NC_OK && g.algo == NC_CONV_FFT) {
+    L.twid_w = o; o = align256(o + 8 * (size_t)g.Nw);
+    L.twid_h = o; o = align256(o + 8 * (size_t)g.Nh);
+  } else {
+    L.twid_w = L.twid_h = SIZE_MAX;
+  }
   L.total = o;
   return L;
 }
@@ -91,6 +117,42 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
   L.xsave = train ? take(fl * B * (dm1 ? dm1 : 1) * P) : SIZE_MAX;
   L.zhat = train ? take(fl * B * g.d * M * P) : SIZE_MAX;
   L.rstd = train ? take(fl * B * g.d * M) : SIZE_MAX;
+  L.f_field = L.f_xhat = L.f_tmp = L.f_gspec = L.f_mean = L.f_rstd = SIZE_MAX;
+  L.f_q = L.f_dgacc = L.f_gz = L.f_dx = L.f_gpart = SIZE_MAX;
+  if (g.algo == NC_CONV_FFT) {
+    // FFT convolution: per-step planes live in HBM, nothing per sample on chip
+    if (f_smem) *f_smem = false;
+    if (z_smem) *z_smem = false;
+    if (gz_smem) *gz_smem = false;
+    const size_t pairs = (B + 1) / 2, c64 = 2 * fl;
+    const size_t FF = (size_t)g.Fh * g.Fw, NN = (size_t)g.Nh * g.Nw;
+    size_t lines = pairs * M * (size_t)g.roi_h;
+    if (pairs * (size_t)g.Fh > lines) lines = pairs * (size_t)g.Fh;
+    if (M * (size_t)g.kh > lines) lines = M * (size_t)g.kh;
+    L.f_field = take(fl * B * FF);
+    L.f_xhat = take(c64 * pairs * NN);
+    L.f_tmp = take(c64 * lines * (size_t)g.Nw);
+    L.f_gspec = take(c64 * M * NN);
+    L.f_mean = take(fl * B * M);
+    L.f_rstd = take(fl * B * M);
+    L.fscr = SIZE_MAX;
+    L.zscr = train ? SIZE_MAX : take(fl * B * M * P);
+    L.gzscr = L.gpix = L.gdpart = L.gdelta = L.gdeltasum = L.redscr = SIZE_MAX;
+    if (train) {
+      L.f_q = take(c64 * pairs * M * NN);
+      L.f_dgacc = take(c64 * M * NN);
+      L.f_gz = take(fl * B * M * P);
+      L.f_dx = take(fl * B * FF);
+      L.f_gpart = take(fl * kRedChunks * 3 * P);
+      L.gsum = take(fl * 3 * P);
+      L.gdsum = take(fl * M * g.K);
+      L.gborder = take(fl * HW);
+    } else {
+      L.gsum = L.gdsum = L.gborder = SIZE_MAX;
+    }
+    L.total = o;
+    return L;
+  }
   L.fscr = fs ? SIZE_MAX : take(fl * B * g.F_elems);
   L.zscr = (!train && !zs) ? take(fl * B * M * P) : SIZE_MAX;
   if (train) {

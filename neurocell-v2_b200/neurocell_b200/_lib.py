@@ -12,12 +12,13 @@ import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libneurocell_b200.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 NC_OK, NC_ERR_INVALID, NC_ERR_WORKSPACE, NC_ERR_UNSUPPORTED, NC_ERR_CUDA = 0, 1, 2, 3, 4
 NC_PAD = {"VALID": 0, "SAME": 1, "CIRCULAR": 2}
 NC_ACT = {"identity": 0, "tanh": 1, "sigmoid": 2, "relu": 3, "leaky_relu": 4, "gelu": 5}
 NC_CODD = {"continuous": 0, "annealed": 1, "ste_binary": 2, "ste_ternary": 3}
+NC_CONV = {"auto": 0, "direct": 1, "fft": 2}
 NC_FLAG_TRAIN = 1
 
 # Every symbol the header declares (checked by the CPU test-suite).
@@ -43,7 +44,7 @@ class NcTopo(ctypes.Structure):
         ("act", ctypes.c_int32), ("final_act", ctypes.c_int32),
         ("act_slope", ctypes.c_float), ("final_act_slope", ctypes.c_float),
         ("norm", ctypes.c_int32), ("hard_pin_io", ctypes.c_int32),
-        ("gated_filters", ctypes.c_int32),
+        ("gated_filters", ctypes.c_int32), ("conv_algo", ctypes.c_int32),
     ]
 
 

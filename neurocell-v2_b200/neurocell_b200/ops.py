@@ -123,9 +123,12 @@ def _output_index(topology: ChipTopology2D) -> tuple[np.ndarray, tuple]:
 
 def get_plan(topology: ChipTopology2D, in_shapes: tuple, device: torch.device, act: str,
              act_slope: float, final_act: str, final_act_slope: float, norm: bool,
-             hard_pin_io: bool, gated_filters: bool) -> Plan:
+             hard_pin_io: bool, gated_filters: bool, conv: str = "auto") -> Plan:
+    """``conv``: Green's convolution algorithm, "auto" | "direct" | "fft" (nc_conv_algo)."""
+    if conv not in _lib.NC_CONV:
+        raise ValueError(f"Unsupported conv algorithm '{conv}'; choose from {tuple(_lib.NC_CONV)}.")
     key = (topology.key(), in_shapes, str(device), act, act_slope, final_act, final_act_slope,
-           bool(norm), bool(hard_pin_io), bool(gated_filters))
+           bool(norm), bool(hard_pin_io), bool(gated_filters), conv)
     plan = _PLANS.get(key)
     if plan is not None:
         return plan
@@ -145,9 +148,13 @@ def get_plan(topology: ChipTopology2D, in_shapes: tuple, device: torch.device, a
     t.act, t.final_act = _lib.NC_ACT[act], _lib.NC_ACT[final_act]
     t.act_slope, t.final_act_slope = float(act_slope), float(final_act_slope)
     t.norm, t.hard_pin_io, t.gated_filters = int(norm), int(hard_pin_io), int(gated_filters)
+    t.conv_algo = _lib.NC_CONV[conv]
     nbytes = lib.nc_plan_bytes(ctypes.byref(t))
     if nbytes == 0:
-        raise ValueError("neurocell_b200: invalid topology for the B200 path")
+        msg = lib.nc_last_error().decode(errors="replace")
+        if "exceeds" in msg:
+            raise NotImplementedError(f"neurocell_b200: {msg}")
+        raise ValueError(f"neurocell_b200: invalid topology for the B200 path ({msg})")
     buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
     io = np.ascontiguousarray(topology.io_state_mask, dtype=np.uint8)
     ow = np.ascontiguousarray(topology.out_weight_mask, dtype=np.uint8)

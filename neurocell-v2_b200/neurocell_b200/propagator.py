@@ -2,9 +2,12 @@
 
 Mirrors ``neurocell/propagator.py:209-734`` of shakes76/neurocell-v2: same signature,
 argument meaning and ValueError behaviour.  Every reference backend name is accepted and
-runs the single B200 path (``backend="b200"``), whose numerics follow the reference's
-semantic backend ``nchw_direct`` (propagator.py:413-432): the reference's other backends
-are performance variants of the same function.
+runs the B200 path, whose numerics follow the reference's semantic backend
+``nchw_direct`` (propagator.py:413-432).  The backend name picks the Green's convolution
+algorithm the way the reference's backends do: the FFT backends ("pallas_sram",
+"rfft_hoisted", "nchw_rfft_bwd") run the FFT convolution, "nchw_direct" and
+"pallas_fused" the direct one, and "auto" / "b200" apply the reference's auto rule
+(propagator.py:68-85: FFT for kh*kw > 512 outside CIRCULAR mode).
 """
 from __future__ import annotations
 
@@ -25,6 +28,13 @@ SUPPORTED_BACKENDS = (
     "pallas_sram",
     "b200",
 )
+
+
+CONV_OF_BACKEND = {
+    "auto": "auto", "b200": "auto",
+    "nchw_direct": "direct", "pallas_fused": "direct",
+    "rfft_hoisted": "fft", "nchw_rfft_bwd": "fft", "pallas_sram": "fft",
+}
 
 
 def select_optimal_backend(topology: ChipTopology2D) -> str:
@@ -110,7 +120,7 @@ def propagate_vnn_2d(
     if flat.device != device:
         flat = flat.to(device, non_blocking=True)
     plan = ops.get_plan(topology, shapes, device, act, slope, fact, fslope, norm, hard_pin_io,
-                        gated_filters)
+                        gated_filters, CONV_OF_BACKEND[backend])
     out = ops.propagate(params.cell_params, params.greens_filters, flat, plan, codd_mode,
                         state_temperature, active_threshold)
     return out.reshape((out.shape[0],) + plan.out_shape)

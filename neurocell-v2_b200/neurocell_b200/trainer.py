@@ -176,7 +176,7 @@ class VNNTrainStep:
                  hard_pin_io: bool = False, gated_filters: bool = False,
                  codd_mode: str = "continuous", state_temperature: float = 1.0,
                  active_threshold: float = 0.6, in_shapes=None, process_group=None,
-                 exchange: str = "nccl"):
+                 exchange: str = "nccl", conv: str = "auto"):
         import ctypes
         from . import _lib
         from .params import check_codd_mode
@@ -193,7 +193,7 @@ class VNNTrainStep:
             in_shapes = tuple(tuple(p.size) if not hasattr(p, "num_points") else (p.num_points,)
                               for p in topology.in_ports)
         self.plan = ops.get_plan(topology, tuple(in_shapes), dev, act, slope, fact, fslope, norm,
-                                 hard_pin_io, gated_filters)
+                                 hard_pin_io, gated_filters, conv)
         self.lib = _lib.load()
         self._lib = _lib
         self.ctypes = ctypes

@@ -37,7 +37,7 @@ def _nc_topo(g: O.Geometry):
                                     _to_nc_port(g.out_port), padding_mode=g.padding_mode)
 
 
-def run_gpu(geom, cfg, cell, filt, inputs, targets, loss="mse", train=True):
+def run_gpu(geom, cfg, cell, filt, inputs, targets, loss="mse", train=True, backend="b200"):
     topo = _nc_topo(geom)
     dev = torch.device("cuda:0")
     cp = torch.tensor(cell, dtype=torch.float32, device=dev, requires_grad=train)
@@ -50,7 +50,8 @@ def run_gpu(geom, cfg, cell, filt, inputs, targets, loss="mse", train=True):
         nc.VNNParams(cp, fl), xin, topo, activate=ACT[cfg.activate],
         final_activate=ACT[cfg.final_activate], norm=cfg.norm, gated_filters=cfg.gated_filters,
         hard_pin_io=cfg.hard_pin_io, codd_mode=cfg.codd_mode,
-        state_temperature=cfg.state_temperature, active_threshold=cfg.active_threshold)
+        state_temperature=cfg.state_temperature, active_threshold=cfg.active_threshold,
+        backend=backend)
     if not train:
         return out.detach().cpu().numpy(), None, None, None
     y = torch.tensor(np.asarray(targets), device=dev)
@@ -68,8 +69,8 @@ def run_oracle(geom, cfg, cell, filt, inputs, targets, loss="mse"):
     return out, lval, gc, gf
 
 
-def check_case(geom, cfg, cell, filt, inputs, targets, loss="mse", tol=TOL):
-    o_g, l_g, gc_g, gf_g = run_gpu(geom, cfg, cell, filt, inputs, targets, loss)
+def check_case(geom, cfg, cell, filt, inputs, targets, loss="mse", tol=TOL, backend="b200"):
+    o_g, l_g, gc_g, gf_g = run_gpu(geom, cfg, cell, filt, inputs, targets, loss, backend=backend)
     o_r, l_r, gc_r, gf_r = run_oracle(geom, cfg, cell, filt, inputs, targets, loss)
     errs = dict(out=_rel(o_g, o_r), loss=abs(l_g - l_r) / max(abs(l_r), 1e-30),
                 g_cell=_rel(gc_g, gc_r), g_filters=_rel(gf_g, gf_r))
@@ -230,3 +231,67 @@ def test_sgd_step_matches_oracle():
     assert _rel(p.cell_params.cpu().numpy(), new_cell) <= 1e-6
     assert _rel(p.greens_filters.cpu().numpy(), new_filt) <= 1e-6
     assert not np.array_equal(p.cell_params.cpu().numpy(), cell)
+
+
+# ---- FFT convolution regime ("pallas_sram" backend) -------------------------------------
+@pytest.mark.parametrize("mode", ["VALID", "SAME", "CIRCULAR"])
+@pytest.mark.parametrize("cfg", [
+    O.Config(),
+    O.Config(activate="gelu", final_activate="tanh"),
+    O.Config(activate="leaky_relu", final_activate="sigmoid", gated_filters=True),
+    O.Config(activate="relu", norm=False, hard_pin_io=True),
+    O.Config(activate=None, codd_mode="ste_binary", state_temperature=0.5),
+])
+def test_fft_modes_and_options_parity(mode, cfg):
+    geom = O.make_geometry((20, 22), (5, 3), 4, 3, (O.RectPort((6, 5), (4, 1)),),
+                           O.RectPort((6, 14), (4, 1)), padding_mode=mode)
+    cell, filt, ins, y = random_problem(geom, 5, 51)
+    check_case(geom, cfg, cell, filt, ins, y, backend="pallas_sram")
+
+
+@pytest.mark.parametrize("depth", [1, 2, 5])
+def test_fft_depth_and_border_inputs_parity(depth):
+    geom = O.make_geometry((24, 24), (7, 5), 6, depth,
+                           (O.RectPort((0, 4), (6, 6)), O.CoordPort(((12, 12), (13, 9)))),
+                           O.CoordPort(((10, 18), (11, 18), (14, 6))))
+    cell, filt, ins, y = random_problem(geom, 4, 61 + depth)
+    check_case(geom, O.Config(), cell, filt, ins, y, backend="pallas_sram")
+
+
+@pytest.mark.parametrize("B", [1, 6])
+def test_fft_alu_train_step_parity(B):
+    geom, cfg, cell, filt, x, y = alu_problem(B, 71)
+    check_case(geom, cfg, cell, filt, x, y, backend="pallas_sram")
+
+
+def test_fft_and_direct_agree_on_image_classifier_shape():
+    ports = (O.RectPort((0, 32), (32, 32)), O.RectPort((32, 32), (32, 32)), O.RectPort((64, 32), (32, 32)))
+    out = O.CoordPort(tuple((r, 80) for r in range(43, 53)))
+    geom = O.make_geometry(96, (15, 15), 16, 3, ports, out)
+    cell, filt, ins, y = random_problem(geom, 3, 31, loss="ce")
+    check_case(geom, O.Config(), cell, filt, ins, y, loss="ce", backend="pallas_sram")
+
+
+def test_fft_backward_is_deterministic():
+    geom = O.make_geometry(48, (31, 31), 16, 3, (O.CoordPort(tuple((r, 12) for r in range(16, 32))),),
+                           O.CoordPort(tuple((r, 36) for r in range(20, 28))), padding_mode="SAME")
+    cell, filt, ins, y = random_problem(geom, 4, 23)
+    a = run_gpu(geom, O.Config(), cell, filt, ins, y)
+    b = run_gpu(geom, O.Config(), cell, filt, ins, y)
+    assert np.array_equal(a[2], b[2]) and np.array_equal(a[3], b[3])
+
+
+def test_fft_backend_runs_the_fft_kernels():
+    """The FFT backend launches the transform kernels (more launches than the two of the
+    direct forward) and matches the direct backend on the same inputs."""
+    geom = O.make_geometry((20, 22), (5, 3), 4, 3, (O.RectPort((6, 5), (4, 1)),),
+                           O.RectPort((6, 14), (4, 1)))
+    cell, filt, ins, y = random_problem(geom, 4, 81)
+    lib = nc._lib.load()
+    n0 = lib.nc_launch_count()
+    o_d, *_ = run_gpu(geom, O.Config(), cell, filt, ins, y, train=False, backend="nchw_direct")
+    n1 = lib.nc_launch_count()
+    o_f, *_ = run_gpu(geom, O.Config(), cell, filt, ins, y, train=False, backend="pallas_sram")
+    n2 = lib.nc_launch_count()
+    assert n1 - n0 == 2 and n2 - n1 > 10
+    assert _rel(o_f, o_d) <= TOL
