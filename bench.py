@@ -345,6 +345,157 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------------------
+# the other BASELINE configs (secondary measurements; the default run is config 0)
+# ---------------------------------------------------------------------------------------
+HBM_PEAK_GBS = 6467.7       # MEASURED_PEAKS.json hbm_gbs (STREAM-style copy on this pool)
+
+
+def config_problem(cfg: int, batch: int, seed_rank: int):
+    """Topology and seeded synthetic data of BASELINE configs 1-4 (shapes, sizes and value
+    distributions as the configs state; seeds cfg*1000 + {0 params, 1 filters, 2 inputs,
+    3 targets})."""
+    import neurocell_b200 as nc
+    from oracle import vnn_oracle as O
+    r = [np.random.default_rng([cfg * 1000 + k, seed_rank]) for k in range(4)]
+    if cfg == 1:
+        topo = nc.ChipTopology2D.alu_chip()
+        cell = r[0].normal(0, 0.1, (3, 62, 62)).astype(np.float32)
+        u = r[0].uniform(1e-6, 1 - 1e-6, (62, 62))
+        cell[2] = np.log(u / (1 - u)).astype(np.float32)
+        filt = (r[1].normal(0, 1, (16, 1, 23, 13)) / np.sqrt(299)).astype(np.float32)
+        x, y, _ = O.alu_batch(r[2], batch, noise=0.0)
+        return topo, ((8, 1),) * 3, cell, filt, x.reshape(batch, -1), y, dict(
+            codd_mode="ste_ternary", loss="mse", train=False, K=23 * 13, M=16, P=2000, d=4)
+    if cfg == 2:
+        H, kh, M, d = 256, 31, 16, 8
+        inp = nc.CoordinatePortSpec(tuple((rr, 64) for rr in range(96, 160)), "in")
+        out = nc.CoordinatePortSpec(tuple((rr, 192) for rr in range(112, 144)), "out")
+        topo = nc.ChipTopology2D.create((H, H), (kh, kh), M, d, (inp,), out, padding_mode="SAME")
+        x = r[2].normal(size=(batch, 64)).astype(np.float32)
+        y = r[3].integers(0, 2, size=(batch, 32)).astype(np.float32)
+        shapes, P, loss = ((64,),), 256 * 256, "mse"
+    elif cfg == 3:
+        H, kh, M, d = 96, 15, 16, 6
+        ports = tuple(nc.PortSpec((o, 32), (32, 32), f"in{i}") for i, o in enumerate((0, 32, 64)))
+        out = nc.CoordinatePortSpec(tuple((rr, 80) for rr in range(43, 53)), "out")
+        topo = nc.ChipTopology2D.create((H, H), (kh, kh), M, d, ports, out)
+        x = r[2].normal(size=(batch, 3 * 32 * 32)).astype(np.float32)
+        y = r[3].integers(0, 10, size=batch).astype(np.int32)
+        shapes, P, loss = ((32, 32),) * 3, 82 * 82, "ce"
+    else:
+        H, kh, M, d = 1024, 63, 32, 8
+        inp = nc.CoordinatePortSpec(tuple((rr, 128) for rr in range(448, 576)), "in")
+        out = nc.CoordinatePortSpec(tuple((rr, 896) for rr in range(448, 576)), "out")
+        topo = nc.ChipTopology2D.create((H, H), (kh, kh), M, d, (inp,), out)
+        x = r[2].normal(size=(batch, 128)).astype(np.float32)
+        y = r[3].normal(size=(batch, 128)).astype(np.float32)
+        shapes, P, loss = ((128,),), 962 * 962, "mse"
+    cell = r[0].normal(0, 0.1, (3, H, H)).astype(np.float32)
+    filt = (r[1].normal(0, 1, (M, 1, kh, kh)) / kh).astype(np.float32)
+    return topo, shapes, cell, filt, x, y, dict(
+        codd_mode="annealed" if cfg == 4 else "continuous", loss=loss, train=True,
+        K=kh * kh, M=M, P=P, d=d)
+
+
+def run_config(args) -> None:
+    """One GPU, one BASELINE config other than 0: CUDA-graph replays of the step with the L2
+    flushed before each, CUDA events; prints one JSON line (not the driver's bench line)."""
+    import ctypes
+    import neurocell_b200 as nc
+    from neurocell_b200 import _lib, ops
+    cfg = args.config
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B = {1: 8192, 2: 64, 3: 256, 4: 16}[cfg]
+    topo, shapes, cell, filt, x, y, meta = config_problem(cfg, B, 0)
+    lib = _lib.load()
+    conv = args.conv
+    if meta["train"]:
+        runner = nc.trainer.VNNTrainStep(
+            topo, nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev)), B,
+            lr=LR, loss=meta["loss"], codd_mode=meta["codd_mode"], in_shapes=shapes, conv=conv,
+            state_temperature=1.0)
+        runner.load_batch(torch.tensor(x, device=dev), torch.tensor(y, device=dev))
+        step = runner.step
+        if not args.no_graph:
+            runner.capture()
+        n_launch = None
+    else:
+        plan = ops.get_plan(topo, shapes, dev, "tanh", 0.0, "identity", 1.0, True, False, False, conv)
+        cp, fl = torch.tensor(cell, device=dev), torch.tensor(filt, device=dev)
+        xd = torch.tensor(x, device=dev)
+        out = torch.empty((B, plan.n_out), device=dev)
+        wsb = lib.nc_workspace_bytes(ctypes.byref(plan.topo), B, 0)
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        codd = ops._codd(meta["codd_mode"], 1.0, 0.6)
+
+        def launch():
+            _lib.check(lib.nc_vnn_forward(ctypes.byref(plan.topo), ops._ptr(plan.buf), ops._ptr(cp),
+                                          ops._ptr(fl), ops._ptr(xd), B, ctypes.byref(codd), 0,
+                                          ops._ptr(out), ops._ptr(ws), wsb, ops._stream(dev)),
+                       "nc_vnn_forward")
+        n0 = lib.nc_launch_count()
+        launch()
+        n_launch = int(lib.nc_launch_count() - n0)
+        graph = None
+        if not args.no_graph:
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                launch()
+            torch.cuda.current_stream(dev).wait_stream(s)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                launch()
+
+        def step():
+            if graph is not None:
+                graph.replay()
+            else:
+                launch()
+    l2_flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    clocks = ClockSampler(0)
+    for i in range(K):
+        l2_flush.fill_(float(i))
+        ev[i][0].record()
+        step()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+    M, P, Kk, d = meta["M"], meta["P"], meta["K"], meta["d"]
+    passes = (3 * d - 1) if meta["train"] else d
+    flops = 2.0 * M * P * Kk * passes * B
+    zbytes = 4.0 * B * M * P * d * (5 if meta["train"] else 2)
+    if cfg in (2, 4):
+        roof = {"bound": "hbm", "achieved": zbytes / (ms * 1e-3) / 1e9, "peak": HBM_PEAK_GBS,
+                "unit": "GB/s", "model": "5*|Z|*d bytes, |Z| = 4*B*M*P (reporting rule)"}
+        roof["frac"] = roof["achieved"] / roof["peak"]
+    else:
+        peak = fp32_peak_tflops(dev)
+        roof = {"bound": "fp32", "achieved": flops / (ms * 1e-3) / 1e12, "peak": peak,
+                "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / peak,
+                "model": "effective direct-convolution FLOPs 2*M*P*K per pass"}
+    what = "train" if meta["train"] else "inference"
+    line = {
+        "metric": f"{what} samples/s (BASELINE config {cfg})", "value": B / (ms * 1e-3),
+        "unit": "samples/s", "n_gpus": 1, "steps": K, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "f32", "data": "synthetic (seeded numpy, config shapes)",
+        "config": {"workload": f"BASELINE config {cfg}", "batch": B, "conv": conv,
+                   "codd_mode": meta["codd_mode"], "cuda_graph": not args.no_graph,
+                   "l2": "flushed (256 MB write) before every timed step"},
+        "effective_tflops": flops / (ms * 1e-3) / 1e12, "roofline": roof, "clocks": clk,
+        "gpu_launches_per_step": runner.launches_per_step() if meta["train"] else n_launch,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -355,9 +506,17 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--exchange", choices=("nccl", "nvlink"), default="nccl",
                     help="data-parallel gradient exchange for --gpus > 1")
+    ap.add_argument("--config", type=int, choices=(0, 1, 2, 3, 4), default=0,
+                    help="BASELINE config; 1-4 print a secondary single-GPU line")
+    ap.add_argument("--conv", choices=("auto", "direct", "fft"), default="auto",
+                    help="Green's convolution algorithm for --config 1-4")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
+    if args.config != 0:
+        if args.impl == "b200":
+            run_config(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -60,11 +60,18 @@ nc_status make_geo(const nc_topo* t, Geo* g) {
     return set_error(NC_ERR_INVALID, "unsupported conv_algo id %d", t->conv_algo);
   if (t->conv_algo == NC_CONV_FFT && !fft_fits)
     return set_error(NC_ERR_UNSUPPORTED, "FFT grid %dx%d exceeds %d per side", g->Nh, g->Nw, kFftMaxN);
-  if (t->conv_algo == NC_CONV_AUTO)
-    g->algo = (fft_fits && t->padding != NC_PAD_CIRCULAR && t->kh * t->kw > 512) ? NC_CONV_FFT
-                                                                                 : NC_CONV_DIRECT;
-  else
+  if (t->conv_algo == NC_CONV_AUTO) {
+    // the reference's rule (large kernels) plus: mid-size kernels whose response planes do
+    // not fit on chip, where the direct kernels would stream every plane through HBM
+    const size_t on_chip = sizeof(float) * ((size_t)g->M * g->K + 4 * (size_t)g->M + 128 +
+                                            (size_t)g->F_elems + (size_t)g->M * g->P);
+    const bool planes_on_chip = on_chip <= kSmemBudget;   // the direct kernels' policy
+    const bool large_k = t->kh * t->kw > 512;
+    const bool mid_k = t->kh * t->kw >= 81 && !planes_on_chip;
+    g->algo = (fft_fits && (large_k || mid_k)) ? NC_CONV_FFT : NC_CONV_DIRECT;
+  } else {
     g->algo = t->conv_algo;
+  }
   return NC_OK;
 }
 

@@ -56,6 +56,46 @@ def test_host_only_entry_points_validate_geometry():
     assert lib.nc_workspace_bytes(ctypes.byref(t), 0, 0) == 0
 
 
+def _ws(t, algo, B=8):
+    t.conv_algo = algo
+    return _lib.load().nc_workspace_bytes(ctypes.byref(t), B, _lib.NC_FLAG_TRAIN)
+
+
+def test_conv_algorithm_selection():
+    """AUTO keeps the on-chip direct path for the ALU chip and picks the FFT regime for
+    large kernels (the reference's kh*kw > 512 rule) and for mid-size kernels whose planes
+    do not fit on chip; FFT grids above 1024 per side are refused."""
+    lib = _lib.load()
+    t = _alu_topo()
+    assert _ws(t, 0) == _ws(t, 1) != _ws(t, 2)
+    t.H = t.W = 256
+    t.kh = t.kw = 31
+    t.padding = 1                     # BASELINE config 2 shape
+    assert _ws(t, 0) == _ws(t, 2) != _ws(t, 1)
+    t.H = t.W = 96
+    t.kh = t.kw = 15
+    t.padding = 0                     # BASELINE config 3 shape: planes off chip
+    assert _ws(t, 0) == _ws(t, 2) != _ws(t, 1)
+    t.H = t.W = 24
+    t.kh = t.kw = 9                   # small planes stay on chip
+    assert _ws(t, 0) == _ws(t, 1) != _ws(t, 2)
+    t.H = t.W = 1500
+    t.kh = t.kw = 63                  # FFT side 2048
+    t.conv_algo = 2
+    assert lib.nc_plan_bytes(ctypes.byref(t)) == 0
+    assert b"exceeds" in lib.nc_last_error()
+    t.conv_algo = 0                   # AUTO falls back to the direct path
+    assert lib.nc_plan_bytes(ctypes.byref(t)) > 0
+    t.conv_algo = 7
+    assert lib.nc_plan_bytes(ctypes.byref(t)) == 0
+
+
+def test_backend_names_select_the_convolution():
+    from neurocell_b200.propagator import CONV_OF_BACKEND, SUPPORTED_BACKENDS
+    assert set(CONV_OF_BACKEND) == set(SUPPORTED_BACKENDS)
+    assert CONV_OF_BACKEND["pallas_sram"] == "fft" and CONV_OF_BACKEND["nchw_direct"] == "direct"
+
+
 def test_null_and_invalid_arguments_fail_without_touching_the_gpu():
     lib = _lib.load()
     t = _alu_topo()
