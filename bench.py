@@ -332,7 +332,9 @@ def run_b200(args) -> None:
             "roofline": {"bound": "fp32", "kernel": dom, "achieved": ach, "peak": peak,
                          "unit": "TFLOP/s", "frac": ach / peak if peak else None,
                          "peak_source": "live FFMA probe (nc_fp32_peak_probe); MEASURED_PEAKS.json has no FP32 figure",
-                         "traffic": None},
+                         "traffic": ncu_traffic("fast::bwd_kernel<23, 13>" if dom == "vnn_fused_bwd_kernel"
+                                                else "fast::fwd_kernel_mt<23, 13, 8>"),
+                         "traffic_source": "profiles/ncu_traffic.json (one ncu capture, dram read+write per launch)"},
             "clocks": clk,
         }
         if world == 1 and not args.no_cpu:
@@ -348,7 +350,22 @@ def run_b200(args) -> None:
 # ---------------------------------------------------------------------------------------
 # the other BASELINE configs (secondary measurements; the default run is config 0)
 # ---------------------------------------------------------------------------------------
-HBM_PEAK_GBS = 6467.7       # MEASURED_PEAKS.json hbm_gbs (STREAM-style copy on this pool)
+def hbm_peak() -> tuple[float, str]:
+    """Measured HBM copy bandwidth of this pool (MEASURED_PEAKS.json), else the fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback (profiling recipe)"
+
+
+def ncu_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f).get(kernel, {}).get("bytes")
+    except (OSError, ValueError):
+        return None
 
 
 def config_problem(cfg: int, batch: int, seed_rank: int):
@@ -474,8 +491,10 @@ def run_config(args) -> None:
     flops = 2.0 * M * P * Kk * passes * B
     zbytes = 4.0 * B * M * P * d * (5 if meta["train"] else 2)
     if cfg in (2, 4):
-        roof = {"bound": "hbm", "achieved": zbytes / (ms * 1e-3) / 1e9, "peak": HBM_PEAK_GBS,
-                "unit": "GB/s", "model": "5*|Z|*d bytes, |Z| = 4*B*M*P (reporting rule)"}
+        peak, src = hbm_peak()
+        roof = {"bound": "hbm", "achieved": zbytes / (ms * 1e-3) / 1e9, "peak": peak,
+                "unit": "GB/s", "peak_source": src,
+                "model": "5*|Z|*d bytes, |Z| = 4*B*M*P (reporting rule)"}
         roof["frac"] = roof["achieved"] / roof["peak"]
     else:
         peak = fp32_peak_tflops(dev)
