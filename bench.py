@@ -217,7 +217,7 @@ def run_b200(args) -> None:
     topo = nc.ChipTopology2D.alu_chip()
     params = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
     runner = nc.trainer.VNNTrainStep(topo, params, BATCH, lr=LR, in_shapes=((8, 1),) * 3,
-                                     process_group=pg, exchange=args.exchange)
+                                     process_group=pg, exchange=args.exchange, conv=args.conv)
     x_dev = torch.tensor(xs.reshape(nb, BATCH, -1), device=dev)
     y_dev = torch.tensor(ys, device=dev)
     if not args.no_graph:
@@ -324,7 +324,8 @@ def run_b200(args) -> None:
                        "optimizer": "sgd(1e-2)", "per_gpu_batch": BATCH, "global_batch": BATCH * world,
                        "parallelism": f"dp{world}", "l2": "flushed (256 MB write) before every timed step",
                        "cuda_graph": runner.graph is not None,
-                       "grad_exchange": (args.exchange if world > 1 else "none")},
+                       "grad_exchange": (args.exchange if world > 1 else "none"),
+                       "conv": args.conv},
             "e2e": {"value": BATCH * world / (e2e_ms * 1e-3), "unit": "samples/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms},
             "gpu_launches": runner.launches_per_step() * K,
@@ -528,7 +529,7 @@ def main():
     ap.add_argument("--config", type=int, choices=(0, 1, 2, 3, 4), default=0,
                     help="BASELINE config; 1-4 print a secondary single-GPU line")
     ap.add_argument("--conv", choices=("auto", "direct", "fft"), default="auto",
-                    help="Green's convolution algorithm for --config 1-4")
+                    help="Green's convolution algorithm (nc_conv_algo)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3

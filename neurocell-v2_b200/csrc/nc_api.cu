@@ -12,6 +12,7 @@
 #include "nc_fast.cuh"
 #include "nc_fft.cuh"
 #include "nc_fftconv.h"
+#include "nc_fftf.h"
 #include "nc_internal.h"
 #include "nc_kernels.cuh"
 
@@ -218,6 +219,28 @@ static FftCall fft_call(const Prepared& pr, void* ws, const float* inputs, int b
   return c;
 }
 
+// Arguments of the fused small-grid FFT kernels (nc_fftf.cu).
+static FftfArgs fftf_args(const Prepared& pr, void* ws, const float* inputs, int batch, bool train) {
+  FftfArgs a;
+  memset(&a, 0, sizeof(a));
+  const WsLayout& L = pr.L;
+  a.g = pr.g;
+  a.sp = pr.sp;
+  a.in_index = pr.in_index;
+  a.out_index = pr.out_index;
+  a.inputs = inputs;
+  a.H = at<float2>(ws, L.f_h);
+  a.zhat = at<float>(ws, L.zhat);
+  a.rstd = at<float>(ws, L.rstd);
+  a.xsave = at<float>(ws, L.xsave);
+  a.train = train ? 1 : 0;
+  a.batch = batch;
+  a.gpix = at<float>(ws, L.gpix);
+  a.gdpart = at<float>(ws, L.gdpart);
+  a.gring = at<float>(ws, L.f_gring);
+  return a;
+}
+
 static nc_status launch_prestep(const Prepared& pr, const float* cell, const float* filters,
                                 const nc_codd* codd, cudaStream_t st) {
   const int HW = pr.g.H * pr.g.W;
@@ -332,9 +355,19 @@ nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* c
   if (pr.g.algo == NC_CONV_FFT) {
     FftCall c = fft_call(pr, d_ws, inputs, batch, train);
     c.out = out;
-    if (g_prof.fs) NC_CUDA_CHECK(cudaEventRecord(g_prof.fs, st));
-    NC_CHECK(fft_forward(c, st));
-    if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
+    if (fftf_fits(pr.g)) {
+      // small grid: direction-pair filter spectra, then one fused kernel per sample
+      FftfArgs fa = fftf_args(pr, d_ws, inputs, batch, train);
+      fa.out = out;
+      NC_CHECK(fftf_pair_spectra(pr.g, pr.sp.geff, at<float2>(d_ws, pr.L.f_h), st));
+      if (g_prof.fs) NC_CUDA_CHECK(cudaEventRecord(g_prof.fs, st));
+      NC_CHECK(fftf_forward(fa, st));
+      if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
+    } else {
+      if (g_prof.fs) NC_CUDA_CHECK(cudaEventRecord(g_prof.fs, st));
+      NC_CHECK(fft_forward(c, st));
+      if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
+    }
     clear_error();
     return NC_OK;
   }
@@ -392,6 +425,30 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
   cudaStream_t st = as_stream(stream);
   const Geo& g = pr.g;
   const WsLayout& L = pr.L;
+  if (g.algo == NC_CONV_FFT && fftf_fits(g)) {
+    FftfArgs fa = fftf_args(pr, d_ws, inputs, batch, true);
+    fa.gout = g_out;
+    if (g_prof.bs) NC_CUDA_CHECK(cudaEventRecord(g_prof.bs, st));
+    NC_CHECK(fftf_backward(fa, st));
+    if (g_prof.be) NC_CUDA_CHECK(cudaEventRecord(g_prof.be, st));
+    float* gsum = at<float>(d_ws, L.gsum);
+    float* gdsum = at<float>(d_ws, L.gdsum);
+    float* gborder = fa.gring ? at<float>(d_ws, L.gborder) : nullptr;
+    const int P3 = 3 * g.P, MK = g.M * g.K, FF = g.Fh * g.Fw, HW = g.H * g.W;
+    batch_sum_kernel<<<(P3 + 255) / 256, 256, 0, st>>>(fa.gpix, (size_t)P3, P3, batch, gsum);
+    NC_CHECK(launch_check("batch_sum_kernel(pixels) launch"));
+    batch_sum_kernel<<<(MK + 255) / 256, 256, 0, st>>>(fa.gdpart, (size_t)MK, MK, batch, gdsum);
+    NC_CHECK(launch_check("batch_sum_kernel(filters) launch"));
+    if (gborder) {
+      batch_sum_kernel<<<(FF + 255) / 256, 256, 0, st>>>(fa.gring, (size_t)FF, FF, batch, gborder);
+      NC_CHECK(launch_check("batch_sum_kernel(ring) launch"));
+    }
+    prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, gsum,
+                                                         gborder, gdsum, g_cell_params, g_filters);
+    NC_CHECK(launch_check("prestep_bwd_kernel launch"));
+    clear_error();
+    return NC_OK;
+  }
   if (g.algo == NC_CONV_FFT) {
     FftCall c = fft_call(pr, d_ws, inputs, batch, true);
     c.gout = g_out;

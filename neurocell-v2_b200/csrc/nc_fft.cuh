@@ -150,4 +150,162 @@ __device__ void transform_lines(float2* s, int L, int N, const float2* tw, int t
 }
 
 }  // namespace fft
+
+// ---------------------------------------------------------------------------------------
+// 64 x 64 planes in natural order, radix-8 in registers (the fused small-grid kernels).
+//
+// A 64-point transform runs on 8 lanes: lane j loads x[j + 8n] (n < 8), does an 8-point
+// DFT, multiplies output q by w64^(j q), the 8 lanes transpose their values with three
+// xor-shuffle rounds, and lane q does a second 8-point DFT whose output n' is
+// X[q + 8 n'] -- stored back at that position, so spectra stay in natural order.  A CTA
+// of 512 threads runs 64 such groups: one pass transforms every row (or every column) of a
+// plane.  Plane layout: element (r, c) at r * 66 + c; with this stride the 8-lane groups
+// of a half-warp (rows r and r+4, or columns c and c+1) hit 16 distinct bank pairs.
+// ---------------------------------------------------------------------------------------
+namespace fft64 {
+
+constexpr int kN = 64;
+constexpr int kLS = 66;
+constexpr int kPlane = kN * kLS;
+
+__device__ __forceinline__ int at(int r, int c) { return r * kLS + c; }
+
+// y[q] = sum_n a[n] w8^(n q) (INVERSE: conjugate roots); radix-2 network, natural order.
+template <bool INVERSE>
+__device__ __forceinline__ void dft8(float2 a[8]) {
+  constexpr float h = 0.70710678118654752f;
+  // w8 = (h, -h) forward, (h, +h) inverse; w8^2 = -i (forward) / +i (inverse)
+  auto mw1 = [](float2 v) {   // v * w8
+    return INVERSE ? make_float2(h * (v.x - v.y), h * (v.x + v.y))
+                   : make_float2(h * (v.x + v.y), h * (v.y - v.x));
+  };
+  auto mw2 = [](float2 v) {   // v * w8^2
+    return INVERSE ? make_float2(-v.y, v.x) : make_float2(v.y, -v.x);
+  };
+  auto mw3 = [](float2 v) {   // v * w8^3
+    return INVERSE ? make_float2(-h * (v.x + v.y), h * (v.x - v.y))
+                   : make_float2(h * (v.y - v.x), -h * (v.x + v.y));
+  };
+  const float2 b0 = fft::cadd(a[0], a[4]), b1 = fft::cadd(a[1], a[5]);
+  const float2 b2 = fft::cadd(a[2], a[6]), b3 = fft::cadd(a[3], a[7]);
+  const float2 b4 = fft::csub(a[0], a[4]), b5 = mw1(fft::csub(a[1], a[5]));
+  const float2 b6 = mw2(fft::csub(a[2], a[6])), b7 = mw3(fft::csub(a[3], a[7]));
+  const float2 c0 = fft::cadd(b0, b2), c1 = fft::cadd(b1, b3);
+  const float2 c2 = fft::csub(b0, b2), c3 = mw2(fft::csub(b1, b3));
+  const float2 c4 = fft::cadd(b4, b6), c5 = fft::cadd(b5, b7);
+  const float2 c6 = fft::csub(b4, b6), c7 = mw2(fft::csub(b5, b7));
+  a[0] = fft::cadd(c0, c1);
+  a[4] = fft::csub(c0, c1);
+  a[2] = fft::cadd(c2, c3);
+  a[6] = fft::csub(c2, c3);
+  a[1] = fft::cadd(c4, c5);
+  a[5] = fft::csub(c4, c5);
+  a[3] = fft::cadd(c6, c7);
+  a[7] = fft::csub(c6, c7);
+}
+
+// 8 x 8 transpose across the 8 lanes of a group: afterwards lane l holds, in v[e], what
+// lane e held in v[l].
+__device__ __forceinline__ void transpose8(float2 v[8], int lane8) {
+#pragma unroll
+  for (int s = 4; s >= 1; s >>= 1) {
+    const bool up = (lane8 & s) != 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (e & s) continue;
+      const float2 send = up ? v[e] : v[e | s];
+      float2 recv;
+      recv.x = __shfl_xor_sync(0xffffffffu, send.x, s);
+      recv.y = __shfl_xor_sync(0xffffffffu, send.y, s);
+      if (up) v[e] = recv; else v[e | s] = recv;
+    }
+  }
+}
+
+// Lane roles of a 512-thread CTA: group g = one line, j = lane within the group.
+struct Lane {
+  int j;      // 0..7
+  int row;    // line index of a row pass
+  int col;    // line index of a column pass
+};
+
+__device__ __forceinline__ Lane lane_of(int tid) {
+  const int w = tid >> 5, lane = tid & 31;
+  Lane L;
+  L.j = lane & 7;
+  L.row = 8 * (w >> 1) + 2 * (w & 1) + (lane >> 4) + 4 * ((lane >> 3) & 1);
+  L.col = 4 * w + (lane >> 3);
+  return L;
+}
+
+// The middle of a 64-point transform: first DFT8 done on v (v[n] = x[j + 8n]), then
+// twiddle, transpose, second DFT8: afterwards v[n'] = X[j + 8 n'].
+template <bool INVERSE>
+__device__ __forceinline__ void fft64_lanes(float2 v[8], int j, const float2* tw64) {
+  dft8<INVERSE>(v);
+#pragma unroll
+  for (int q = 1; q < 8; ++q) {
+    const float2 w = tw64[(j * q) & 63];
+    v[q] = INVERSE ? fft::cmulc(v[q], w) : fft::cmul(v[q], w);
+  }
+  transpose8(v, j);
+  dft8<INVERSE>(v);
+}
+
+// Transforms rows [0, nrows) (COLS = false) or all 64 columns (COLS = true) of a plane in
+// place.  All 512 threads must call it (the shuffles need whole warps); lines beyond
+// nrows are computed on zeros and not stored.  No barrier inside: callers separate
+// passes that read each other's data with __syncthreads().
+template <bool COLS, bool INVERSE>
+__device__ __forceinline__ void pass64(float2* s, int nrows, const float2* tw64, const Lane& L) {
+  const int line = COLS ? L.col : L.row;
+  const bool active = COLS || line < nrows;
+  if (!COLS && !__any_sync(0xffffffffu, active)) return;   // whole warp beyond nrows
+  float2 v[8];
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+    v[n] = active ? s[COLS ? at(L.j + 8 * n, line) : at(line, L.j + 8 * n)] : make_float2(0.f, 0.f);
+  fft64_lanes<INVERSE>(v, L.j, tw64);
+  if (active) {
+#pragma unroll
+    for (int n = 0; n < 8; ++n) s[COLS ? at(L.j + 8 * n, line) : at(line, L.j + 8 * n)] = v[n];
+  }
+}
+
+// pass64 over two planes at once (independent transforms interleave).
+template <bool COLS, bool INVERSE>
+__device__ __forceinline__ void pass64x2(float2* s1, float2* s2, int nrows, const float2* tw64,
+                                         const Lane& L) {
+  const int line = COLS ? L.col : L.row;
+  const bool active = COLS || line < nrows;
+  if (!COLS && !__any_sync(0xffffffffu, active)) return;
+  float2 v[8], u[8];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    const int o = COLS ? at(L.j + 8 * n, line) : at(line, L.j + 8 * n);
+    v[n] = active ? s1[o] : make_float2(0.f, 0.f);
+    u[n] = active ? s2[o] : make_float2(0.f, 0.f);
+  }
+  fft64_lanes<INVERSE>(v, L.j, tw64);
+  fft64_lanes<INVERSE>(u, L.j, tw64);
+  if (active) {
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int o = COLS ? at(L.j + 8 * n, line) : at(line, L.j + 8 * n);
+      s1[o] = v[n];
+      s2[o] = u[n];
+    }
+  }
+}
+
+// tw64[e] = exp(-2 pi i e / 64) (sincospif: CUDA's own single-precision routine).
+__device__ __forceinline__ void init_tw64(float2* tw64, int tid) {
+  if (tid < kN) {
+    float sn, cs;
+    sincospif(-2.0f * (float)tid / (float)kN, &sn, &cs);
+    tw64[tid] = make_float2(cs, sn);
+  }
+}
+
+}  // namespace fft64
 }  // namespace nc

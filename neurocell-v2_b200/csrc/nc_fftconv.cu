@@ -588,19 +588,22 @@ nc_status field_ring(const FftCall& c, cudaStream_t st) {
 // ---------------------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------------------
+
+// Filter spectra G^_m / (Nh Nw), one per direction (the reference hoists them once per
+// batch, kernels_greens.py:240-259).
+nc_status fft_filter_spectra(const FftCall& c, cudaStream_t st) {
+  const Geo& g = c.g;
+  Planes gf{c.sp.geff, (size_t)g.K, g.M, 1, g.kh, g.kw, 0, g.kw, 0, g.M, 1.0f};
+  NC_CHECK(rows_fwd(gf, c.tmp, g.Nw, c.tw_w, st));
+  ColArgs ca{c.tmp, nullptr, c.gspec, g.Nh, g.Nw, g.kh, g.Nh, g.M, 1.0f / ((float)g.Nh * (float)g.Nw)};
+  return cols<COL_FWD>(ca, g.M, c.tw_h, st);
+}
+
 nc_status fft_forward(const FftCall& c, cudaStream_t st) {
   const Geo& g = c.g;
   const int B = c.batch, pairs = (B + 1) / 2;
   const size_t P = (size_t)g.P, M = (size_t)g.M;
-
-  // filter spectra G^_m / (Nh Nw), one per direction (the reference hoists them once per
-  // batch, kernels_greens.py:240-259)
-  {
-    Planes gf{c.sp.geff, (size_t)g.K, g.M, 1, g.kh, g.kw, 0, g.kw, 0, g.M, 1.0f};
-    NC_CHECK(rows_fwd(gf, c.tmp, g.Nw, c.tw_w, st));
-    ColArgs ca{c.tmp, nullptr, c.gspec, g.Nh, g.Nw, g.kh, g.Nh, g.M, 1.0f / ((float)g.Nh * (float)g.Nw)};
-    NC_CHECK(cols<COL_FWD>(ca, g.M, c.tw_h, st));
-  }
+  NC_CHECK(fft_filter_spectra(c, st));
 
   for (int t = 0; t < g.d; ++t) {
     if (t == 0) {

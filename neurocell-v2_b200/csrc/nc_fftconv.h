@@ -42,6 +42,8 @@ struct FftCall {
   float* out;                 // forward: (B, n_out)
 };
 
+// Filter spectra G^_m / (Nh*Nw) into c.gspec (uses c.tmp).
+nc_status fft_filter_spectra(const FftCall& c, cudaStream_t st);
 // Forward d-step loop with FFT convolution (filter spectra included).  Launch count is
 // reported through note_launch().
 nc_status fft_forward(const FftCall& c, cudaStream_t st);

@@ -1,0 +1,569 @@
+// nc_fftf.cu -- per-sample fused FFT propagation for small grids (FFT side 64), sm_100a.
+//
+// One CTA owns one sample for all d steps, as in the direct kernels, but convolves in the
+// frequency domain: the field spectrum X^ (64 x 64 complex) and a working spectrum stay in
+// shared memory, and two directions share one complex inverse transform.  With the
+// per-launch tables H_j = conj(G^_{2j}) + i conj(G^_{2j+1}) (spectra / 64^2, natural order;
+// H_j(w) = F_j(-w) with F_j = FFT(g_{2j} + i g_{2j+1})):
+//   forward      IFFT(X^ . H_j)               = z_{2j} + i z_{2j+1}        (X^ is Hermitian)
+//   field adjoint Re IFFT(sum_j Q^_j . conj(H_j)) = sum_m gz_m (*) G_m, with
+//                Q^_j = FFT(gz_{2j} + i gz_{2j+1}) (the imaginary part holds cross terms only)
+//   filter adjoint IFFT(X^ . conj(Q^_j)) / 64^2 = corr(X, gz_{2j}) - i corr(X, gz_{2j+1}).
+// So a step costs one field transform plus M/2 inverse transforms forward, and M/2 forward
+// plus M/2 pruned inverse transforms plus one inverse backward, instead of 2*M*P*K FMAs per
+// pass.  The 64-point transforms are radix-8 in registers with shuffle transposes
+// (nc_fft.cuh, fft64).  The epilogues (neurocell/epilogue.py:28-56, :82-128; centred two-pass variance of
+// neurocell/kernels_pallas.py:202-205) run plane pair by plane pair, accumulating the
+// per-pixel sums over directions, so no more than two planes are ever on chip.
+#include <cuda_runtime.h>
+
+#include "nc_common.cuh"
+#include "nc_errors.h"
+#include "nc_fft.cuh"
+#include "nc_fftf.h"
+
+namespace nc {
+
+using fft::cadd;
+using fft::cmul;
+using fft::cmulc;
+
+namespace {
+
+constexpr int kN = kFftfN;                    // FFT side
+constexpr int kPlane = fft64::kPlane;         // float2 per on-chip plane
+constexpr int kThreads = 512;
+constexpr float kInvNN = 1.0f / (float)(kN * kN);
+static_assert(kN == fft64::kN, "fused kernels are built on the 64-point transforms");
+
+__device__ __forceinline__ int at2(int r, int c) { return fft64::at(r, c); }
+
+// Forward 2-D transform of rows [0, nrows) then all columns; barriers on both sides.
+__device__ __forceinline__ void fwd2d(float2* s, int nrows, const float2* tw, const fft64::Lane& L) {
+  __syncthreads();
+  fft64::pass64<false, false>(s, nrows, tw, L);
+  __syncthreads();
+  fft64::pass64<true, false>(s, kN, tw, L);
+  __syncthreads();
+}
+
+// Inverse 2-D transform: all columns, then rows [0, nrows) (the rows that are kept).
+__device__ __forceinline__ void inv2d(float2* s, int nrows, const float2* tw, const fft64::Lane& L) {
+  __syncthreads();
+  fft64::pass64<true, true>(s, kN, tw, L);
+  __syncthreads();
+  fft64::pass64<false, true>(s, nrows, tw, L);
+  __syncthreads();
+}
+
+// ROI pixels p = tid + 512 k of this thread: their plane offsets (r, c) -> at2(r, c), or -1.
+constexpr int kPixPerThread = kN * kN / kThreads;   // a ROI has at most 64 x 64 pixels
+__device__ __forceinline__ void pixel_offsets(const Geo& g, int tid, int poff[kPixPerThread]) {
+#pragma unroll
+  for (int k = 0; k < kPixPerThread; ++k) {
+    const int p = tid + k * kThreads;
+    const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+    poff[k] = p < g.P ? at2(r, c) : -1;
+  }
+}
+
+// Sum of up to four per-thread values over the CTA (result broadcast to every thread).
+__device__ __forceinline__ void block_sum4(float v[4], float* red) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v[k] = warp_sum(v[k]);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) red[k * 32 + w] = v[k];
+  __syncthreads();
+  if (w == 0) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float r = lane < nw ? red[k * 32 + lane] : 0.f;
+      r = warp_sum(r);
+      if (lane == 0) red[128 + k] = r;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v[k] = red[128 + k];
+}
+
+// Field of step t into X (real part; zero imaginary, zero beyond Fh x Fw).
+//   src_interior(p): the ROI value; ring: VALID border template, SAME zero, CIRCULAR wrap.
+// Step 0 (src == nullptr): zeros, injected inputs, wrapped halo.
+__device__ void load_field(const FftfArgs& a, float2* X, const float* roi_src, const float* inp,
+                           int tid, int nt) {
+  const Geo& g = a.g;
+  if (!roi_src) {
+    for (int i = tid; i < kPlane; i += nt) X[i] = make_float2(0.f, 0.f);
+    __syncthreads();
+    for (int j = tid; j < g.n_in; j += nt) {
+      const int idx = a.in_index[j];
+      if (idx < 0) continue;
+      const int r = idx / g.W, c = idx - (idx / g.W) * g.W;
+      X[at2(r + g.gr, c + g.gc)].x = inp[j];
+    }
+    __syncthreads();
+    if (g.padding == NC_PAD_CIRCULAR) {
+      for (int i = tid; i < g.Fh * g.Fw; i += nt) {
+        const int fr = i / g.Fw, fc = i - (i / g.Fw) * g.Fw;
+        const int r = fr - g.oh, c = fc - g.ow;
+        if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) continue;
+        int sr = r % g.roi_h; if (sr < 0) sr += g.roi_h;
+        int sc = c % g.roi_w; if (sc < 0) sc += g.roi_w;
+        X[at2(fr, fc)].x = X[at2(sr + g.oh, sc + g.ow)].x;
+      }
+      __syncthreads();
+    }
+    return;
+  }
+  for (int i = tid; i < kN * kN; i += nt) {
+    const int fr = i / kN, fc = i - (i / kN) * kN;
+    float v = 0.f;
+    if (fr < g.Fh && fc < g.Fw) {
+      int r = fr - g.oh, c = fc - g.ow;
+      const bool inside = r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w;
+      if (inside) {
+        v = roi_src[r * g.roi_w + c];
+      } else if (g.padding == NC_PAD_VALID) {
+        v = a.sp.border[fr * g.W + fc];
+      } else if (g.padding == NC_PAD_CIRCULAR) {
+        r %= g.roi_h; if (r < 0) r += g.roi_h;
+        c %= g.roi_w; if (c < 0) c += g.roi_w;
+        v = roi_src[r * g.roi_w + c];
+      }
+    }
+    X[at2(fr, fc)] = make_float2(v, 0.f);
+  }
+}
+
+
+// ---------------------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
+  extern __shared__ float4 smem4[];
+  float2* stw = reinterpret_cast<float2*>(smem4);
+  float2* X = stw + kN;
+  float2* Wp = X + kPlane;
+  float2* Wq = Wp + kPlane;
+  float* lin = reinterpret_cast<float*>(Wq + kPlane);
+  float* acc = lin + a.g.P;
+  float* red = acc + a.g.P;      // 160 floats
+  const Geo& g = a.g;
+  const int tid = threadIdx.x, nt = blockDim.x, b = blockIdx.x;
+  const size_t P = (size_t)g.P, M = (size_t)g.M;
+  const int pairs = g.M / 2;
+  fft64::init_tw64(stw, tid);
+  const fft64::Lane Ln = fft64::lane_of(tid);
+  int poff[kPixPerThread];
+  pixel_offsets(g, tid, poff);
+
+  for (int t = 0; t < g.d; ++t) {
+    const bool last = (t == g.d - 1);
+    load_field(a, X, t == 0 ? nullptr : lin, a.inputs + (size_t)b * g.n_in, tid, nt);
+    fwd2d(X, g.Fh, stw, Ln);
+    const int act_id = last ? g.fact : g.act;
+    const float slope = last ? g.fslope : g.slope;
+    for (int p = tid; p < g.P; p += nt) { lin[p] = 0.f; acc[p] = 0.f; }
+
+    // two direction pairs (four planes) per round: independent transforms interleave
+    for (int j = 0; j < pairs; j += 2) {
+      const bool two = j + 1 < pairs;
+      const float2* Ha = a.H + (size_t)j * kN * kN;
+      const float2* Hb = two ? Ha + kN * kN : Ha;
+      // inverse column passes of X^ . H_j and X^ . H_{j+1} (products taken at load time)
+      {
+        float2 va[8], vb[8];
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const int r = Ln.j + 8 * n;
+          const float2 x = X[at2(r, Ln.col)];
+          va[n] = cmul(x, __ldg(&Ha[r * kN + Ln.col]));
+          vb[n] = cmul(x, __ldg(&Hb[r * kN + Ln.col]));
+        }
+        fft64::fft64_lanes<true>(va, Ln.j, stw);
+        fft64::fft64_lanes<true>(vb, Ln.j, stw);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          Wp[at2(Ln.j + 8 * n, Ln.col)] = va[n];
+          Wq[at2(Ln.j + 8 * n, Ln.col)] = vb[n];
+        }
+      }
+      __syncthreads();
+      // inverse row passes of the ROI rows (warps beyond them skip)
+      fft64::pass64x2<false, true>(Wp, Wq, g.roi_h, stw, Ln);
+      __syncthreads();
+      // statistics of planes 2j, 2j+1 (Wp re, im) and 2j+2, 2j+3 (Wq), centred two-pass;
+      // thread tid owns pixels p = tid + 512 k
+      float mu[4] = {0.f, 0.f, 0.f, 0.f}, rs[4] = {1.f, 1.f, 1.f, 1.f};
+      if (g.norm) {
+        const float inv_n = 1.0f / (float)g.P;
+#pragma unroll
+        for (int k = 0; k < kPixPerThread; ++k) {
+          if (poff[k] < 0) continue;
+          const float2 w = Wp[poff[k]], u = Wq[poff[k]];
+          mu[0] += w.x; mu[1] += w.y; mu[2] += u.x; mu[3] += u.y;
+        }
+        block_sum4(mu, red);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mu[k] *= inv_n;
+        float q[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < kPixPerThread; ++k) {
+          if (poff[k] < 0) continue;
+          const float2 w = Wp[poff[k]], u = Wq[poff[k]];
+          const float d0 = w.x - mu[0], d1 = w.y - mu[1], d2 = u.x - mu[2], d3 = u.y - mu[3];
+          q[0] = fmaf(d0, d0, q[0]); q[1] = fmaf(d1, d1, q[1]);
+          q[2] = fmaf(d2, d2, q[2]); q[3] = fmaf(d3, d3, q[3]);
+        }
+        block_sum4(q, red);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) rs[k] = 1.0f / sqrtf(q[k] * inv_n + kNormEps);
+      }
+      const int np = two ? 4 : 2;
+      if (a.train && tid < np) a.rstd[((size_t)b * g.d + t) * M + 2 * j + tid] = rs[tid];
+      float* zh = a.train ? a.zhat + (((size_t)b * g.d + t) * M + 2 * j) * P : nullptr;
+#pragma unroll
+      for (int k = 0; k < kPixPerThread; ++k) {
+        if (poff[k] < 0) continue;
+        const int p = tid + k * kThreads;
+        const float2 w = Wp[poff[k]], u = Wq[poff[k]];
+        const float h0 = (w.x - mu[0]) * rs[0], h1 = (w.y - mu[1]) * rs[1];
+        const float h2 = (u.x - mu[2]) * rs[2], h3 = (u.y - mu[3]) * rs[3];
+        const float bb = a.sp.broi[p];
+        if (zh) { zh[p] = h0; zh[P + p] = h1; }
+        float l = h0 + h1;
+        float ac = (act_id != NC_ACT_NONE) ? act_fwd(act_id, h0 + bb, slope) + act_fwd(act_id, h1 + bb, slope) : 0.f;
+        if (two) {
+          if (zh) { zh[2 * P + p] = h2; zh[3 * P + p] = h3; }
+          l += h2 + h3;
+          if (act_id != NC_ACT_NONE) ac += act_fwd(act_id, h2 + bb, slope) + act_fwd(act_id, h3 + bb, slope);
+        }
+        lin[p] += l;
+        acc[p] += ac;
+      }
+      __syncthreads();
+    }
+    __syncthreads();
+
+    if (!last) {
+      float* xs = a.train ? a.xsave + ((size_t)b * (g.d - 1) + t) * P : nullptr;
+      for (int p = tid; p < g.P; p += nt) {
+        const float bb = a.sp.broi[p];
+        const float act = (g.act == NC_ACT_NONE) ? lin[p] + (float)g.M * bb : acc[p];
+        const float xn = a.sp.weff[p] * lin[p] + a.sp.seff[p] * act;
+        lin[p] = xn;                      // the next step's ROI field
+        if (xs) xs[p] = xn;
+      }
+      __syncthreads();
+    } else {
+      for (int jo = tid; jo < g.n_out; jo += nt) {
+        const int idx = a.out_index[jo];
+        const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
+        const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+        const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];
+        a.out[(size_t)b * g.n_out + jo] = (g.fact == NC_ACT_NONE)
+                                              ? (wo + so) * lin[p] + ((float)g.M * so * bo)
+                                              : act_fwd(g.fact, wo * lin[p] + so * acc[p], g.fslope);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
+  extern __shared__ float4 smem4[];
+  const Geo& g = a.g;
+  const int tid = threadIdx.x, nt = blockDim.x, b = blockIdx.x;
+  const size_t P = (size_t)g.P, M = (size_t)g.M;
+  const int pairs = g.M / 2;
+  const int FF = g.Fh * g.Fw;
+  float2* stw = reinterpret_cast<float2*>(smem4);
+  float2* X = stw + kN;
+  float2* Wp = X + kPlane;
+  float2* D = Wp + kPlane;
+  float* gy = reinterpret_cast<float*>(D + kPlane);
+  float* gp0 = gy + g.P;
+  float* gp1 = gp0 + g.P;
+  float* gp2 = gp1 + g.P;
+  float* dg = gp2 + g.P;                       // M*K
+  float* gport = dg + M * g.K;                 // n_out * M
+  float* red = gport + (size_t)g.n_out * M;    // 160
+  float* ring = red + 160;                     // Fh*Fw when a.gring
+  int16_t* pmap = reinterpret_cast<int16_t*>(ring + (a.gring ? FF : 0));   // P
+  fft64::init_tw64(stw, tid);
+  const fft64::Lane Ln = fft64::lane_of(tid);
+  for (int p = tid; p < g.P; p += nt) { gp0[p] = 0.f; gp1[p] = 0.f; gp2[p] = 0.f; pmap[p] = -1; }
+  for (int i = tid; i < (int)(M * g.K); i += nt) dg[i] = 0.f;
+  if (a.gring)
+    for (int i = tid; i < FF; i += nt) ring[i] = 0.f;
+  __syncthreads();
+
+  // output step (t = d-1): the port cells' plane gradients and parameter gradients
+  // (kernels_pallas.py:1378-1504)
+  {
+    const float* ZH = a.zhat + ((size_t)b * g.d + (g.d - 1)) * M * P;
+    for (int jo = tid; jo < g.n_out; jo += nt) {
+      const int idx = a.out_index[jo];
+      const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
+      const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+      pmap[p] = (int16_t)jo;
+      const float go = a.gout[(size_t)b * g.n_out + jo];
+      const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];
+      float lin = 0.f;
+      for (int m = 0; m < g.M; ++m) lin += ZH[m * P + p];
+      if (g.fact == NC_ACT_NONE) {
+        gp0[p] += go * lin;
+        gp1[p] += go * (lin + (float)g.M * bo);
+        gp2[p] += go * (float)g.M * so;
+        for (int m = 0; m < g.M; ++m) gport[jo * g.M + m] = (wo + so) * go;
+      } else {
+        float act = 0.f;
+        for (int m = 0; m < g.M; ++m) act += act_fwd(g.fact, ZH[m * P + p] + bo, g.fslope);
+        float dpre;
+        act_fwd_deriv(g.fact, wo * lin + so * act, g.fslope, &dpre);
+        const float gpre = go * dpre;
+        gp0[p] += gpre * lin;
+        gp1[p] += gpre * act;
+        float db = 0.f;
+        for (int m = 0; m < g.M; ++m) {
+          float dd;
+          act_fwd_deriv(g.fact, ZH[m * P + p] + bo, g.fslope, &dd);
+          gport[jo * g.M + m] = gpre * (wo + so * dd);
+          db += gpre * so * dd;
+        }
+        gp2[p] += db;
+      }
+    }
+  }
+  __syncthreads();
+
+  for (int t = g.d - 1; t >= 0; --t) {
+    const bool last = (t == g.d - 1);
+    const float* xs = t > 0 ? a.xsave + ((size_t)b * (g.d - 1) + (t - 1)) * P : nullptr;
+    load_field(a, X, xs, a.inputs + (size_t)b * g.n_in, tid, nt);
+    fwd2d(X, g.Fh, stw, Ln);
+    if (t > 0)
+      for (int i = tid; i < kPlane; i += nt) D[i] = make_float2(0.f, 0.f);
+    const float* ZH = a.zhat + ((size_t)b * g.d + t) * M * P;
+
+    for (int j = 0; j < pairs; ++j) {
+      const int m1 = 2 * j, m2 = 2 * j + 1;
+      const float* z1 = ZH + (size_t)m1 * P;
+      const float* z2 = ZH + (size_t)m2 * P;
+      const float rs1 = a.rstd[((size_t)b * g.d + t) * M + m1];
+      const float rs2 = a.rstd[((size_t)b * g.d + t) * M + m2];
+      // plane gradients before the standardisation adjoint at plane positions
+      // i = tid + 512 k (row i / 64, column i % 64; zero outside the ROI), and their moments
+      float h1[kPixPerThread], h2[kPixPerThread];
+      float2 v[kPixPerThread];
+      float mo[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < kPixPerThread; ++k) {
+        const int i = tid + k * kThreads, r = i >> 6, c = i & (kN - 1);
+        h1[k] = 0.f;
+        h2[k] = 0.f;
+        v[k] = make_float2(0.f, 0.f);
+        if (r >= g.roi_h || c >= g.roi_w) continue;
+        const int p = r * g.roi_w + c;
+        h1[k] = z1[p];
+        h2[k] = z2[p];
+        if (last) {
+          const int jo = pmap[p];
+          if (jo >= 0) v[k] = make_float2(gport[jo * g.M + m1], gport[jo * g.M + m2]);
+        } else {
+          const float y = gy[p], bb = a.sp.broi[p], we = a.sp.weff[p], se = a.sp.seff[p];
+          float d1, d2;
+          const float a1 = act_fwd_deriv(g.act, h1[k] + bb, g.slope, &d1);
+          const float a2 = act_fwd_deriv(g.act, h2[k] + bb, g.slope, &d2);
+          v[k] = make_float2(we * y + se * y * d1, we * y + se * y * d2);
+          // pixel-parameter gradients, summed over directions pair by pair
+          gp0[p] += y * (h1[k] + h2[k]);
+          gp1[p] += y * (a1 + a2);
+          gp2[p] += se * y * (d1 + d2);
+        }
+        mo[0] += v[k].x;
+        mo[1] = fmaf(v[k].x, h1[k], mo[1]);
+        mo[2] += v[k].y;
+        mo[3] = fmaf(v[k].y, h2[k], mo[3]);
+      }
+      if (g.norm) {
+        block_sum4(mo, red);
+        const float inv_n = 1.0f / (float)g.P;
+        const float c11 = mo[0] * inv_n, c21 = mo[1] * inv_n, c12 = mo[2] * inv_n, c22 = mo[3] * inv_n;
+#pragma unroll
+        for (int k = 0; k < kPixPerThread; ++k) {
+          const int i = tid + k * kThreads, r = i >> 6, c = i & (kN - 1);
+          if (r >= g.roi_h || c >= g.roi_w) continue;
+          v[k].x = rs1 * (v[k].x - c11 - h1[k] * c21);
+          v[k].y = rs2 * (v[k].y - c12 - h2[k] * c22);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kPixPerThread; ++k) {
+        const int i = tid + k * kThreads;
+        Wp[at2(i >> 6, i & (kN - 1))] = v[k];
+      }
+      __syncthreads();
+      // Q^_j = FFT(gz_{2j} + i gz_{2j+1}): rows of the ROI, then the columns
+      fft64::pass64<false, false>(Wp, g.roi_h, stw, Ln);
+      __syncthreads();
+      const float2* H = a.H + (size_t)j * kN * kN;
+      {
+        float2 q[8];
+#pragma unroll
+        for (int n = 0; n < 8; ++n) q[n] = Wp[at2(Ln.j + 8 * n, Ln.col)];
+        fft64::fft64_lanes<false>(q, Ln.j, stw);
+        // D += Q^ . conj(H_j) (field adjoint); X^ . conj(Q^) (filter adjoint)
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          const int r = Ln.j + 8 * n, o = at2(r, Ln.col);
+          if (t > 0) D[o] = cadd(D[o], cmulc(q[n], __ldg(&H[r * kN + Ln.col])));
+          q[n] = cmulc(X[o], q[n]);
+        }
+        // inverse column pass of the product, on the registers just formed
+        fft64::fft64_lanes<true>(q, Ln.j, stw);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) Wp[at2(Ln.j + 8 * n, Ln.col)] = q[n];
+      }
+      __syncthreads();
+      // corr(X, gz_{2j}) - i corr(X, gz_{2j+1}) at lags [0, kh) x [0, kw): inverse row pass
+      // of the first kh rows (warps beyond them skip), kept in registers
+      {
+        const bool lagok = Ln.row < g.kh;
+        if (__any_sync(0xffffffffu, lagok)) {
+          float2 w[8];
+#pragma unroll
+          for (int n = 0; n < 8; ++n) w[n] = lagok ? Wp[at2(Ln.row, Ln.j + 8 * n)] : make_float2(0.f, 0.f);
+          fft64::fft64_lanes<true>(w, Ln.j, stw);
+          if (lagok) {
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+              const int vv = Ln.j + 8 * n;
+              if (vv >= g.kw) continue;
+              const int k = Ln.row * g.kw + vv;
+              dg[(size_t)m1 * g.K + k] += w[n].x * kInvNN;
+              dg[(size_t)m2 * g.K + k] -= w[n].y * kInvNN;
+            }
+          }
+        }
+      }
+      __syncthreads();
+    }
+    if (t == 0) break;
+
+    // field adjoint of step t: Re IFFT(D) on the field rows
+    inv2d(D, g.Fh, stw, Ln);
+    for (int p = tid; p < g.P; p += nt) {
+      const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+      float s;
+      if (g.padding != NC_PAD_CIRCULAR) {
+        s = D[at2(r + g.oh, c + g.ow)].x;
+      } else {
+        s = 0.f;
+        for (int fr = (r + g.oh) % g.roi_h; fr < g.Fh; fr += g.roi_h)
+          for (int fc = (c + g.ow) % g.roi_w; fc < g.Fw; fc += g.roi_w) s += D[at2(fr, fc)].x;
+      }
+      gy[p] = s;
+    }
+    if (a.gring) {
+      for (int i = tid; i < FF; i += nt) {
+        const int fr = i / g.Fw, fc = i - (i / g.Fw) * g.Fw;
+        const int r = fr - g.oh, c = fc - g.ow;
+        if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) continue;
+        ring[i] += D[at2(fr, fc)].x;
+      }
+    }
+    __syncthreads();
+  }
+
+  // per-sample partials; the batch sums run in fixed order afterwards
+  float* gpx = a.gpix + (size_t)b * 3 * P;
+  for (int p = tid; p < g.P; p += nt) { gpx[p] = gp0[p]; gpx[P + p] = gp1[p]; gpx[2 * P + p] = gp2[p]; }
+  float* gd = a.gdpart + (size_t)b * M * g.K;
+  for (int i = tid; i < (int)(M * g.K); i += nt) gd[i] = dg[i];
+  if (a.gring) {
+    float* gr = a.gring + (size_t)b * FF;
+    for (int i = tid; i < FF; i += nt) gr[i] = ring[i];
+  }
+}
+
+// H_j(w) = conj(G^_{2j}(w)) + i conj(G^_{2j+1}(w)) = F_j(-w) / 64^2 with
+// F_j = FFT(g_{2j} + i g_{2j+1}) (both filters real); one CTA per direction pair.
+__global__ void __launch_bounds__(kThreads, 1) fftf_pair_spectra_kernel(Geo g, const float* __restrict__ geff,
+                                                                        float2* __restrict__ H) {
+  __shared__ float2 plane[kPlane];
+  __shared__ float2 stw[kN];
+  const int tid = threadIdx.x, nt = blockDim.x, j = blockIdx.x;
+  fft64::init_tw64(stw, tid);
+  const fft64::Lane Ln = fft64::lane_of(tid);
+  const float* g1 = geff + (size_t)(2 * j) * g.K;
+  const float* g2 = g1 + g.K;
+  for (int i = tid; i < kN * kN; i += nt) {
+    const int r = i / kN, c = i - (i / kN) * kN;
+    plane[at2(r, c)] = (r < g.kh && c < g.kw) ? make_float2(g1[r * g.kw + c], g2[r * g.kw + c])
+                                              : make_float2(0.f, 0.f);
+  }
+  fwd2d(plane, g.kh, stw, Ln);
+  float2* Hj = H + (size_t)j * kN * kN;
+  for (int i = tid; i < kN * kN; i += nt) {
+    const int r = i / kN, c = i - (i / kN) * kN;
+    const float2 v = plane[at2((kN - r) & (kN - 1), (kN - c) & (kN - 1))];
+    Hj[i] = make_float2(v.x * kInvNN, v.y * kInvNN);
+  }
+}
+
+nc_status launched(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, what);
+  note_launch();
+  return NC_OK;
+}
+
+}  // namespace
+
+size_t fftf_fwd_smem(const Geo& g) {
+  return sizeof(float2) * (kN + 3 * (size_t)kPlane) + sizeof(float) * (2 * (size_t)g.P + 160);
+}
+
+
+size_t fftf_bwd_smem(const Geo& g, bool ring) {
+  size_t f = 4 * (size_t)g.P + (size_t)g.M * g.K + (size_t)g.n_out * g.M + 160 +
+             (ring ? (size_t)g.Fh * g.Fw : 0);
+  return sizeof(float2) * (kN + 3 * (size_t)kPlane) + sizeof(float) * f + sizeof(int16_t) * (size_t)g.P +
+         16;
+}
+
+bool fftf_fits(const Geo& g) {
+  if (g.Nh != kN || g.Nw != kN || g.M % 2 != 0 || g.P > 32767) return false;
+  const bool ring = g.padding == NC_PAD_VALID && g.d > 1;
+  return fftf_fwd_smem(g) <= kFftfSmemMax && fftf_bwd_smem(g, ring) <= kFftfSmemMax;
+}
+
+nc_status fftf_pair_spectra(const Geo& g, const float* geff, float2* H, cudaStream_t st) {
+  fftf_pair_spectra_kernel<<<g.M / 2, kThreads, 0, st>>>(g, geff, H);
+  return launched("fftf_pair_spectra_kernel launch");
+}
+
+nc_status fftf_forward(const FftfArgs& a, cudaStream_t st) {
+  const size_t smem = fftf_fwd_smem(a.g);
+  NC_CUDA_CHECK(cudaFuncSetAttribute((const void*)fftf_fwd_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  fftf_fwd_kernel<<<a.batch, kThreads, smem, st>>>(a);
+  return launched("fftf_fwd_kernel launch");
+}
+
+nc_status fftf_backward(const FftfArgs& a, cudaStream_t st) {
+  const size_t smem = fftf_bwd_smem(a.g, a.gring != nullptr);
+  NC_CUDA_CHECK(cudaFuncSetAttribute((const void*)fftf_bwd_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  fftf_bwd_kernel<<<a.batch, kThreads, smem, st>>>(a);
+  return launched("fftf_bwd_kernel launch");
+}
+
+}  // namespace nc

@@ -1,0 +1,41 @@
+// nc_fftf.h -- per-sample fused FFT propagation for 64 x 64 FFT grids (nc_fftf.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "nc_kernels.cuh"
+
+namespace nc {
+
+constexpr int kFftfN = 64;                     // the FFT side these kernels are built for
+constexpr size_t kFftfSmemMax = 227 * 1024;    // opt-in dynamic shared memory per CTA
+
+struct FftfArgs {
+  Geo g;
+  StepParams sp;
+  const int32_t* in_index;
+  const int32_t* out_index;
+  const float* inputs;        // (B, n_in)
+  const float2* H;            // (M/2, 64, 64) pair spectra conj(G^_2j) + i conj(G^_2j+1), / 64^2
+  float* out;                 // forward: (B, n_out)
+  float* zhat;                // train: (B, d, M, P)
+  float* rstd;                // train: (B, d, M)
+  float* xsave;               // train: (B, d-1, P)
+  int train;
+  int batch;
+  const float* gout;          // backward: (B, n_out)
+  float* gpix;                // backward: (B, 3, P) per-sample pixel-parameter gradients
+  float* gdpart;              // backward: (B, M*K) per-sample filter gradients
+  float* gring;               // backward: (B, Fh*Fw) per-sample ring gradients (VALID, d>1) or null
+};
+
+// True when the fused kernels serve this geometry (FFT side 64, even M, fits on chip).
+bool fftf_fits(const Geo& g);
+size_t fftf_fwd_smem(const Geo& g);
+size_t fftf_bwd_smem(const Geo& g, bool ring);
+// H_j (natural order) from the effective filters (M, kh, kw).
+nc_status fftf_pair_spectra(const Geo& g, const float* geff, float2* H, cudaStream_t st);
+nc_status fftf_forward(const FftfArgs& a, cudaStream_t st);
+nc_status fftf_backward(const FftfArgs& a, cudaStream_t st);
+
+}  // namespace nc

@@ -67,6 +67,8 @@ struct WsLayout {
   size_t f_gz;            // (B, M, P) plane gradients (train)
   size_t f_dx;            // (B, Fh, Fw) field gradient (train)
   size_t f_gpart;         // (kRedChunks, 3, P) per-chunk pixel-gradient partials (train)
+  size_t f_h;             // fused small-grid kernels: (M/2, 64, 64) pair spectra
+  size_t f_gring;         // fused small-grid kernels: (B, Fh*Fw) ring gradients (train)
   size_t total;
 };
 

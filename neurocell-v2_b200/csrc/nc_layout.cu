@@ -4,6 +4,7 @@
 
 #include "nc_internal.h"
 #include "nc_errors.h"
+#include "nc_fftf.h"
 
 namespace nc {
 
@@ -68,7 +69,10 @@ nc_status make_geo(const nc_topo* t, Geo* g) {
     const bool planes_on_chip = on_chip <= kSmemBudget;   // the direct kernels' policy
     const bool large_k = t->kh * t->kw > 512;
     const bool mid_k = t->kh * t->kw >= 81 && !planes_on_chip;
-    g->algo = (fft_fits && (large_k || mid_k)) ? NC_CONV_FFT : NC_CONV_DIRECT;
+    // 64 x 64 FFT grids run the fused per-sample FFT kernels, which beat the direct
+    // kernels from about 11 x 11 taps on (ALU chip: 0.49 vs 0.82 ms per train step)
+    const bool small_fused = fftf_fits(*g) && t->kh * t->kw >= 121;
+    g->algo = (fft_fits && (large_k || mid_k || small_fused)) ? NC_CONV_FFT : NC_CONV_DIRECT;
   } else {
     g->algo = t->conv_algo;
   }
@@ -125,7 +129,28 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
   L.zhat = train ? take(fl * B * g.d * M * P) : SIZE_MAX;
   L.rstd = train ? take(fl * B * g.d * M) : SIZE_MAX;
   L.f_field = L.f_xhat = L.f_tmp = L.f_gspec = L.f_mean = L.f_rstd = SIZE_MAX;
-  L.f_q = L.f_dgacc = L.f_gz = L.f_dx = L.f_gpart = SIZE_MAX;
+  L.f_q = L.f_dgacc = L.f_gz = L.f_dx = L.f_gpart = L.f_h = L.f_gring = SIZE_MAX;
+  if (g.algo == NC_CONV_FFT && fftf_fits(g)) {
+    // fused per-sample FFT kernels: spectra tables + per-sample partials only
+    if (f_smem) *f_smem = true;
+    if (z_smem) *z_smem = true;
+    if (gz_smem) *gz_smem = true;
+    const size_t c64 = 2 * fl, NN = (size_t)g.Nh * g.Nw;
+    L.f_h = take(c64 * (M / 2) * NN);
+    L.fscr = L.zscr = L.gzscr = L.gdelta = L.gdeltasum = L.redscr = SIZE_MAX;
+    if (train) {
+      L.gpix = take(fl * B * 3 * P);
+      L.gdpart = take(fl * B * M * g.K);
+      L.f_gring = (g.padding == NC_PAD_VALID && g.d > 1) ? take(fl * B * (size_t)g.Fh * g.Fw) : SIZE_MAX;
+      L.gsum = take(fl * 3 * P);
+      L.gdsum = take(fl * M * g.K);
+      L.gborder = take(fl * HW);
+    } else {
+      L.gpix = L.gdpart = L.gsum = L.gdsum = L.gborder = SIZE_MAX;
+    }
+    L.total = o;
+    return L;
+  }
   if (g.algo == NC_CONV_FFT) {
     // FFT convolution: per-step planes live in HBM, nothing per sample on chip
     if (f_smem) *f_smem = false;

@@ -107,22 +107,30 @@ def random_problem(geom, B, seed, pscale=0.3, fscale=None, loss="mse"):
 
 
 # ---- BASELINE config 0 shape: ALU train step ------------------------------------------
+# "b200" (auto) runs the fused FFT kernels on the ALU chip; "nchw_direct" the specialised
+# direct kernels.
+ALU_BACKENDS = ("b200", "nchw_direct")
+
+
+@pytest.mark.parametrize("backend", ALU_BACKENDS)
 @pytest.mark.parametrize("codd,tau", [("continuous", 1.0), ("annealed", 0.4),
                                       ("ste_binary", 0.3), ("ste_ternary", 0.3)])
-def test_alu_train_step_parity(codd, tau):
+def test_alu_train_step_parity(codd, tau, backend):
     geom, cfg, cell, filt, x, y = alu_problem(16, 100, codd, tau)
-    check_case(geom, cfg, cell, filt, x, y)
+    check_case(geom, cfg, cell, filt, x, y, backend=backend)
 
 
-def test_alu_train_step_parity_full_batch():
+@pytest.mark.parametrize("backend", ALU_BACKENDS)
+def test_alu_train_step_parity_full_batch(backend):
     geom, cfg, cell, filt, x, y = alu_problem(128, 7)
-    check_case(geom, cfg, cell, filt, x, y)
+    check_case(geom, cfg, cell, filt, x, y, backend=backend)
 
 
 # ---- BASELINE config 1 shape: ALU inference, ste_ternary, sigma(S) uniform --------------
-def test_alu_inference_ste_ternary_and_exact_roles():
+@pytest.mark.parametrize("backend", ALU_BACKENDS)
+def test_alu_inference_ste_ternary_and_exact_roles(backend):
     geom, cfg, cell, filt, x, y = alu_problem(256, 11, "ste_ternary", 1.0, s_uniform=True)
-    o_g, *_ = run_gpu(geom, cfg, cell, filt, x, y, train=False)
+    o_g, *_ = run_gpu(geom, cfg, cell, filt, x, y, train=False, backend=backend)
     o_r, _ = O.forward(cell, filt, x, geom, cfg)
     assert _rel(o_g, o_r) <= TOL
     topo = _nc_topo(geom)
@@ -197,10 +205,11 @@ def test_depth_and_border_inputs_parity(depth):
     check_case(geom, O.Config(), cell, filt, ins, y)
 
 
-def test_backward_is_deterministic():
+@pytest.mark.parametrize("backend", ALU_BACKENDS)
+def test_backward_is_deterministic(backend):
     geom, cfg, cell, filt, x, y = alu_problem(32, 5)
-    a = run_gpu(geom, cfg, cell, filt, x, y)
-    b = run_gpu(geom, cfg, cell, filt, x, y)
+    a = run_gpu(geom, cfg, cell, filt, x, y, backend=backend)
+    b = run_gpu(geom, cfg, cell, filt, x, y, backend=backend)
     for u, v in zip(a, b):
         assert np.array_equal(np.asarray(u), np.asarray(v))
 
@@ -295,3 +304,46 @@ def test_fft_backend_runs_the_fft_kernels():
     n2 = lib.nc_launch_count()
     assert n1 - n0 == 2 and n2 - n1 > 10
     assert _rel(o_f, o_d) <= TOL
+
+
+# ---- fused small-grid FFT kernels (FFT side 64, even M) ---------------------------------
+@pytest.mark.parametrize("mode", ["VALID", "SAME", "CIRCULAR"])
+@pytest.mark.parametrize("cfg", [
+    O.Config(),
+    O.Config(activate="gelu", final_activate="tanh"),
+    O.Config(activate="leaky_relu", final_activate="sigmoid", gated_filters=True),
+    O.Config(activate="relu", norm=False, hard_pin_io=True),
+    O.Config(activate=None, codd_mode="ste_binary", state_temperature=0.5),
+])
+def test_fft_fused_small_grid_parity(mode, cfg):
+    geom = O.make_geometry((40, 44), (9, 7), 6, 3, (O.RectPort((10, 8), (4, 1)),),
+                           O.RectPort((12, 30), (4, 1)), padding_mode=mode)
+    cell, filt, ins, y = random_problem(geom, 3, 91)
+    check_case(geom, cfg, cell, filt, ins, y, backend="pallas_sram")
+
+
+@pytest.mark.parametrize("depth", [1, 2, 5])
+def test_fft_fused_depth_and_border_inputs_parity(depth):
+    geom = O.make_geometry((48, 50), (9, 7), 4, depth,
+                           (O.RectPort((0, 4), (6, 6)), O.CoordPort(((20, 20), (21, 17)))),
+                           O.CoordPort(((18, 30), (19, 30), (24, 12))))
+    cell, filt, ins, y = random_problem(geom, 4, 95 + depth)
+    check_case(geom, O.Config(), cell, filt, ins, y, backend="pallas_sram")
+
+
+def test_fft_fused_kernel_is_used_for_the_alu_grid():
+    """FFT side 64 with even M runs the fused per-sample kernel: pre-step, direction-pair
+    filter spectra and one propagation kernel; odd M falls back to the per-step kernels and
+    still matches."""
+    geom, cfg, cell, filt, x, y = alu_problem(4, 97)
+    lib = nc._lib.load()
+    n0 = lib.nc_launch_count()
+    o_f, *_ = run_gpu(geom, cfg, cell, filt, x, y, train=False, backend="pallas_sram")
+    n1 = lib.nc_launch_count()
+    o_d, *_ = run_gpu(geom, cfg, cell, filt, x, y, train=False, backend="nchw_direct")
+    assert n1 - n0 == 3
+    assert _rel(o_f, o_d) <= TOL
+    geom5 = O.make_geometry((40, 44), (9, 7), 5, 3, (O.RectPort((10, 8), (4, 1)),),
+                            O.RectPort((12, 30), (4, 1)))
+    cell, filt, ins, y = random_problem(geom5, 3, 98)
+    check_case(geom5, O.Config(), cell, filt, ins, y, backend="pallas_sram")

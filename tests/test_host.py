@@ -62,12 +62,16 @@ def _ws(t, algo, B=8):
 
 
 def test_conv_algorithm_selection():
-    """AUTO keeps the on-chip direct path for the ALU chip and picks the FFT regime for
-    large kernels (the reference's kh*kw > 512 rule) and for mid-size kernels whose planes
-    do not fit on chip; FFT grids above 1024 per side are refused."""
+    """AUTO picks the FFT regime for large kernels (the reference's kh*kw > 512 rule), for
+    mid-size kernels whose planes do not fit on chip and for 64 x 64 FFT grids with at least
+    11 x 11 taps (the fused kernels); small kernels stay direct; FFT grids above 1024 per
+    side are refused."""
     lib = _lib.load()
     t = _alu_topo()
-    assert _ws(t, 0) == _ws(t, 1) != _ws(t, 2)
+    assert _ws(t, 0) == _ws(t, 2) != _ws(t, 1)    # ALU chip: fused 64 x 64 FFT kernels
+    t.kh, t.kw = 5, 3
+    assert _ws(t, 0) == _ws(t, 1) != _ws(t, 2)    # small kernels: direct
+    t.kh, t.kw = 23, 13
     t.H = t.W = 256
     t.kh = t.kw = 31
     t.padding = 1                     # BASELINE config 2 shape
