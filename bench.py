@@ -309,8 +309,11 @@ def run_b200(args) -> None:
     peak = fp32_peak_tflops(dev)
     flops_fwd = BATCH * 2.0 * 16 * 2000 * 299 * 4            # d forward passes
     flops_bwd = BATCH * 2.0 * 16 * 2000 * 299 * 7            # d dG + (d-1) dX passes
-    dom = "vnn_fused_bwd_kernel" if bwd_ms >= fwd_ms else "vnn_fused_fwd_kernel"
-    ach = (flops_bwd / (bwd_ms * 1e-3) if dom == "vnn_fused_bwd_kernel" else flops_fwd / (fwd_ms * 1e-3)) / 1e12
+    path = lib.nc_conv_path(ctypes.byref(runner.plan.topo))
+    names = {1: ("fast::fwd_kernel_mt<23, 13, 8>", "fast::bwd_kernel<23, 13>"),
+             3: ("fftf_fwd_kernel", "fftf_bwd_kernel")}.get(path, ("forward kernels", "backward kernels"))
+    dom = names[1] if bwd_ms >= fwd_ms else names[0]
+    ach = (flops_bwd / (bwd_ms * 1e-3) if dom == names[1] else flops_fwd / (fwd_ms * 1e-3)) / 1e12
 
     if rank == 0:
         line = {
@@ -329,12 +332,15 @@ def run_b200(args) -> None:
             "e2e": {"value": BATCH * world / (e2e_ms * 1e-3), "unit": "samples/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms},
             "gpu_launches": runner.launches_per_step() * K,
-            "kernels_ms": {"vnn_fused_fwd_kernel": fwd_ms, "vnn_fused_bwd_kernel": bwd_ms},
+            "conv_path": {1: "direct per-sample kernels", 2: "FFT per-step kernels",
+                          3: "fused per-sample FFT kernels"}.get(path, "?"),
+            "kernels_ms": {names[0]: fwd_ms, names[1]: bwd_ms},
             "roofline": {"bound": "fp32", "kernel": dom, "achieved": ach, "peak": peak,
                          "unit": "TFLOP/s", "frac": ach / peak if peak else None,
+                         "work": "effective direct-convolution FLOPs (2*M*P*K per pass) per the "
+                                 "reporting rule; the FFT kernels execute far fewer",
                          "peak_source": "live FFMA probe (nc_fp32_peak_probe); MEASURED_PEAKS.json has no FP32 figure",
-                         "traffic": ncu_traffic("fast::bwd_kernel<23, 13>" if dom == "vnn_fused_bwd_kernel"
-                                                else "fast::fwd_kernel_mt<23, 13, 8>"),
+                         "traffic": ncu_traffic(dom),
                          "traffic_source": "profiles/ncu_traffic.json (one ncu capture, dram read+write per launch)"},
             "clocks": clk,
         }

@@ -59,7 +59,9 @@ typedef enum nc_activation {
  * Green's convolution algorithm (the reference's backend choice, propagator.py:58-85):
  * DIRECT = on-chip direct cross-correlation ("nchw_direct" / "pallas_fused"), FFT = 2-D
  * FFT convolution on the next power-of-two grid ("pallas_sram"), AUTO = FFT when
- * kh*kw > 512 and the padding is not CIRCULAR (the reference's auto rule), else DIRECT.
+ * kh*kw > 512 (the reference's auto rule), when kh*kw >= 81 and the response planes do
+ * not fit on chip, or when the FFT grid is 64 x 64 and kh*kw >= 121 (fused per-sample FFT
+ * kernels); else DIRECT.
  */
 typedef enum nc_conv_algo { NC_CONV_AUTO = 0, NC_CONV_DIRECT = 1, NC_CONV_FFT = 2 } nc_conv_algo;
 
@@ -253,6 +255,11 @@ int32_t nc_abi_version(void);
 /* Number of kernels this library has launched in the process so far (all host threads;
  * launches recorded into a CUDA graph count once, at capture). */
 uint64_t nc_launch_count(void);
+
+/* Which kernels nc_vnn_forward / nc_vnn_backward run for `topo` (no reference counterpart):
+ * 1 = direct per-sample kernels, 2 = FFT per-step kernels, 3 = fused per-sample FFT kernels
+ * (64 x 64 FFT grids); 0 if the topology is invalid. */
+int32_t nc_conv_path(const nc_topo* topo);
 
 #ifdef __cplusplus
 }

@@ -260,6 +260,13 @@ int32_t nc_abi_version(void) { return NC_ABI_VERSION; }
 
 uint64_t nc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int32_t nc_conv_path(const nc_topo* topo) {
+  Geo g;
+  if (make_geo(topo, &g) != NC_OK) return 0;
+  if (g.algo != NC_CONV_FFT) return 1;
+  return fftf_fits(g) ? 3 : 2;
+}
+
 const char* nc_last_error(void) { return g_err; }
 
 size_t nc_plan_bytes(const nc_topo* topo) {

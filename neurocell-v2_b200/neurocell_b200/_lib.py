@@ -28,7 +28,7 @@ EXPORTED = (
     "nc_sgd_update", "nc_last_error", "nc_abi_version", "nc_set_profile_events",
     "nc_fp32_peak_probe", "nc_vnn_forward_static", "nc_dp_shared_bytes", "nc_dp_state_bytes",
     "nc_dp_alloc", "nc_dp_free", "nc_ipc_get", "nc_ipc_open", "nc_ipc_close",
-    "nc_dp_allreduce_sgd", "nc_dp_status", "nc_launch_count",
+    "nc_dp_allreduce_sgd", "nc_dp_status", "nc_launch_count", "nc_conv_path",
 )
 NC_DP_MAX_RANKS = 8
 NC_IPC_HANDLE_BYTES = 64
@@ -84,6 +84,7 @@ _SIGS = {
     "nc_last_error": (ctypes.c_char_p, []),
     "nc_abi_version": (_i32, []),
     "nc_launch_count": (ctypes.c_uint64, []),
+    "nc_conv_path": (_i32, [_TP]),
 }
 
 _lib = None
