@@ -4,7 +4,9 @@
 
 * ``--impl b200`` (default): every rank trains the ALU chip (K=23x13, M=16, d=4,
   continuous Codd, MSE, SGD lr=1e-2) on its own 128-sample batches; gradients are
-  all-reduced with NCCL (data parallel, weak scaling: global batch = 128*N).  Prints ONE
+  summed over the ranks by one NVLink peer-memory kernel fused with the SGD update
+  (``--exchange nccl``: NCCL all-reduce + SGD kernel) -- data parallel, weak scaling:
+  global batch = 128*N.  Prints ONE
   JSON line on rank 0: device-resident throughput (``value``), the end-to-end figure through
   the public ``VNNTrainStep`` API with pinned host batches (``e2e``), the fused-kernel
   roofline against a live-measured FP32 FFMA peak, the clocks seen during the timed region
@@ -530,8 +532,9 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--exchange", choices=("nccl", "nvlink"), default="nccl",
-                    help="data-parallel gradient exchange for --gpus > 1")
+    ap.add_argument("--exchange", choices=("nccl", "nvlink"), default="nvlink",
+                    help="data-parallel gradient exchange for --gpus > 1: the fused NVLink "
+                         "peer-memory sum + SGD kernel (default) or NCCL all-reduce + SGD")
     ap.add_argument("--config", type=int, choices=(0, 1, 2, 3, 4), default=0,
                     help="BASELINE config; 1-4 print a secondary single-GPU line")
     ap.add_argument("--conv", choices=("auto", "direct", "fft"), default="auto",

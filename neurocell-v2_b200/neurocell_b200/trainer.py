@@ -76,7 +76,7 @@ class NVLinkExchange:
     frees the buffers (collective: every rank calls it).
     """
 
-    def __init__(self, n: int, process_group, device, max_wait_iters: int = 1 << 22):
+    def __init__(self, n: int, process_group, device, max_wait_iters: int = 1 << 24):
         import ctypes
         import torch.distributed as dist
         from . import _lib
@@ -291,8 +291,12 @@ class VNNTrainStep:
         return self.loss
 
     def capture(self) -> None:
-        """Records one step into a CUDA graph (the NCCL all-reduce included when data
+        """Records one step into a CUDA graph (the gradient exchange included when data
         parallel; call ``release()`` before destroying the process group)."""
+        if self.exchange is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.pg)      # ranks enter the first exchange together
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         saved = self.flat.clone()
