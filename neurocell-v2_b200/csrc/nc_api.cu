@@ -29,6 +29,8 @@ __global__ void batch_sum_kernel(const float* in, size_t stride, int n, int batc
 __global__ void batch_step_sum4_kernel(const float* in, int batch, int d, int t0, size_t slot, int n,
                                        int bc, float* part);
 __global__ void rows_sum_kernel(const float* part, int rows, int n, float* out);
+__global__ void seg_batch_sum1_kernel(SegSum j, int batch, int bc, float* part);
+__global__ void seg_batch_sum2_kernel(SegSum j, int rows, const float* part);
 
 // out[i] = sum_b sum_{t0<=t<d} in[(b*d+t)*slot + i] in two deterministic stages over
 // kRedChunks sample chunks (n, slot multiples of 4; `scratch` holds kRedChunks*n floats).
@@ -442,13 +444,22 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
     float* gdsum = at<float>(d_ws, L.gdsum);
     float* gborder = fa.gring ? at<float>(d_ws, L.gborder) : nullptr;
     const int P3 = 3 * g.P, MK = g.M * g.K, FF = g.Fh * g.Fw, HW = g.H * g.W;
-    batch_sum_kernel<<<(P3 + 255) / 256, 256, 0, st>>>(fa.gpix, (size_t)P3, P3, batch, gsum);
-    NC_CHECK(launch_check("batch_sum_kernel(pixels) launch"));
-    batch_sum_kernel<<<(MK + 255) / 256, 256, 0, st>>>(fa.gdpart, (size_t)MK, MK, batch, gdsum);
-    NC_CHECK(launch_check("batch_sum_kernel(filters) launch"));
-    if (gborder) {
-      batch_sum_kernel<<<(FF + 255) / 256, 256, 0, st>>>(fa.gring, (size_t)FF, FF, batch, gborder);
-      NC_CHECK(launch_check("batch_sum_kernel(ring) launch"));
+    {
+      // fixed-order batch sums of the per-sample partials, in two stages
+      SegSum j;
+      memset(&j, 0, sizeof(j));
+      j.in[0] = fa.gpix; j.out[0] = gsum; j.n[0] = P3;
+      j.in[1] = fa.gdpart; j.out[1] = gdsum; j.n[1] = MK;
+      j.nseg = 2;
+      if (gborder) { j.in[2] = fa.gring; j.out[2] = gborder; j.n[2] = FF; j.nseg = 3; }
+      j.total = j.n[0] + j.n[1] + j.n[2];
+      const int chunks = batch < kRedChunks ? batch : kRedChunks;
+      const int bc = (batch + chunks - 1) / chunks;
+      float* part = at<float>(d_ws, L.redscr);
+      seg_batch_sum1_kernel<<<dim3((j.total + 255) / 256, chunks), 256, 0, st>>>(j, batch, bc, part);
+      NC_CHECK(launch_check("seg_batch_sum1_kernel launch"));
+      seg_batch_sum2_kernel<<<(j.total + 255) / 256, 256, 0, st>>>(j, chunks, part);
+      NC_CHECK(launch_check("seg_batch_sum2_kernel launch"));
     }
     prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, gsum,
                                                          gborder, gdsum, g_cell_params, g_filters);

@@ -53,4 +53,12 @@ struct BwdArgs {
   int batch;
 };
 
+// Up to three (batch, n_s) per-sample partial arrays summed over the batch.
+struct SegSum {
+  const float* in[3];
+  float* out[3];
+  int n[3];
+  int nseg, total;
+};
+
 }  // namespace nc

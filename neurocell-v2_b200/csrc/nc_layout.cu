@@ -141,7 +141,9 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
     if (train) {
       L.gpix = take(fl * B * 3 * P);
       L.gdpart = take(fl * B * M * g.K);
-      L.f_gring = (g.padding == NC_PAD_VALID && g.d > 1) ? take(fl * B * (size_t)g.Fh * g.Fw) : SIZE_MAX;
+      const bool ringp = g.padding == NC_PAD_VALID && g.d > 1;
+      L.f_gring = ringp ? take(fl * B * (size_t)g.Fh * g.Fw) : SIZE_MAX;
+      L.redscr = take(fl * kRedChunks * (3 * P + M * g.K + (ringp ? (size_t)g.Fh * g.Fw : 0)));
       L.gsum = take(fl * 3 * P);
       L.gdsum = take(fl * M * g.K);
       L.gborder = take(fl * HW);
