@@ -228,6 +228,7 @@ class VNNTrainStep:
         self.loss = torch.zeros((), dtype=torch.float32, device=dev)
         self.codd = ops._codd(codd_mode, state_temperature, active_threshold)
         self.graph = None
+        self.epoch_graph = None
         self.exchange = None
         if exchange == "nvlink" and self.world > 1:
             self.exchange = NVLinkExchange(self.n_cell + self.n_filt, process_group, dev)
@@ -243,8 +244,9 @@ class VNNTrainStep:
     def set_temperature(self, tau: float) -> None:
         self.codd.temperature = float(tau)
 
-    def _launch(self) -> None:
+    def _launch(self, loss_out: torch.Tensor | None = None) -> None:
         c, lib, P = self.ctypes, self.lib, ops._ptr
+        loss_t = self.loss if loss_out is None else loss_out
         st = ops._stream(self.device)
         n0 = lib.nc_launch_count()
         t = c.byref(self.plan.topo)
@@ -258,10 +260,10 @@ class VNNTrainStep:
                                            self.ws_bytes, st), "nc_vnn_forward")
         if self.loss_kind == "mse":
             self._lib.check(lib.nc_mse_loss(P(self.out), P(self.y), self.B, self.plan.n_out,
-                                            P(self.loss), P(self.g_out), st), "nc_mse_loss")
+                                            P(loss_t), P(self.g_out), st), "nc_mse_loss")
         else:
             self._lib.check(lib.nc_softmax_ce_loss(P(self.out), P(self.y), self.B, self.plan.n_out,
-                                                   P(self.loss), P(self.g_out), st),
+                                                   P(loss_t), P(self.g_out), st),
                             "nc_softmax_ce_loss")
         self._lib.check(lib.nc_vnn_backward(t, P(self.plan.buf), c.c_void_p(cell), c.c_void_p(filt),
                                             P(self.x), self.B, c.byref(self.codd), P(self.g_out),
@@ -314,10 +316,54 @@ class VNNTrainStep:
         """Status word of the NVLink exchange (0 ok, 1 a peer timed out); 0 without one."""
         return 0 if self.exchange is None else self.exchange.status()
 
+    def capture_epoch(self, x_epoch: torch.Tensor, y_epoch: torch.Tensor) -> None:
+        """Records a whole epoch as one CUDA graph (the reference's ``lax.scan`` epoch,
+        trainer.py:108-119): for every batch i of the device-resident ``x_epoch``
+        (n_batches, B, ...) / ``y_epoch`` the graph copies the batch into the step's static
+        buffers, trains one step and writes that step's loss to ``epoch_losses[i]``.
+        ``train_epoch()`` then replays the epoch with a single launch from the host."""
+        if x_epoch.device != self.device or y_epoch.device != self.device:
+            raise ValueError("capture_epoch needs device-resident batches")
+        nb = int(x_epoch.shape[0])
+        xs = x_epoch.reshape(nb, self.B, -1)
+        ys = y_epoch.reshape((nb,) + tuple(self.y.shape))
+        self.epoch_losses = torch.zeros(nb, dtype=torch.float32, device=self.device)
+        if self.exchange is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.pg)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        saved = self.flat.clone()
+        with torch.cuda.stream(s):
+            for i in range(min(nb, 2)):      # warm-up (kernel attributes, lazy loading)
+                self.x.copy_(xs[i])
+                self.y.copy_(ys[i])
+                self._launch(self.epoch_losses[i])
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(nb):
+                self.x.copy_(xs[i])
+                self.y.copy_(ys[i])
+                self._launch(self.epoch_losses[i])
+        self.flat.copy_(saved)
+        self.epoch_graph = g
+        self._epoch_src = (xs, ys)           # the graph reads these buffers
+
+    def train_epoch(self) -> torch.Tensor:
+        """Replays the captured epoch; returns the per-step losses (device tensor).  The
+        reference's epoch loss is ``epoch_losses.sum() / batch_size``."""
+        if getattr(self, "epoch_graph", None) is None:
+            raise RuntimeError("call capture_epoch() first")
+        self.epoch_graph.replay()
+        return self.epoch_losses
+
     def release(self) -> None:
         """Drops the captured graph and unmaps the NVLink exchange buffers (collective when
         data parallel; required before destroy_process_group)."""
         self.graph = None
+        self.epoch_graph = None
         if self.exchange is not None:
             self.exchange.close()
 
@@ -346,6 +392,16 @@ class VNNTrainer:
             ops.sgd_(params.cell_params, grads.cell_params, self.lr)
             ops.sgd_(params.greens_filters, grads.greens_filters, self.lr)
         return params, loss
+
+    def train_epoch(self, params: VNNParams, x_epoch, y_epoch, **apply_kw):
+        """Steps over the batches of ``x_epoch`` / ``y_epoch`` in order (trainer.py:108-119);
+        returns ``(params, epoch_loss)`` with epoch_loss = sum of the batch losses /
+        batch_size, as the reference reports it."""
+        total = None
+        for bx, by in zip(x_epoch, y_epoch):
+            params, loss = self.train_step(params, bx, by, **apply_kw)
+            total = loss if total is None else total + loss
+        return params, total / float(self.batch_size)
 
     @torch.no_grad()
     def evaluate_packed(self, params: VNNParams, x_batches, y_packed_batches, **apply_kw):
