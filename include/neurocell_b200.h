@@ -150,6 +150,29 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
                           float* g_filters, void* d_ws, size_t ws_bytes, void* stream);
 
 /*
+ * propagate_vnn_2d(..., return_universe=True) (neurocell/propagator.py:657-734 and the
+ * CIRCULAR branch 330-341): the last step runs the ROI epilogue with the final activation
+ * over the whole ROI; universe (batch, H, W) holds those cells, on the VALID ring
+ * f(B) * s_prob (B * s_prob without a final activation), with f applied to every cell;
+ * out (batch, n_out) are the port cells of the universe (equal to nc_vnn_forward's).
+ * Same plan and workspace as nc_vnn_forward.
+ */
+nc_status nc_vnn_forward_universe(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                                  const float* filters, const float* inputs, int32_t batch,
+                                  const nc_codd* codd, uint32_t flags, float* out, float* universe,
+                                  void* d_ws, size_t ws_bytes, void* stream);
+
+/*
+ * Vector-Jacobian product of nc_vnn_forward_universe from the gradients of both results:
+ * g_out (batch, n_out, may be null) and g_universe (batch, H, W).
+ */
+nc_status nc_vnn_backward_universe(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                                   const float* filters, const float* inputs, int32_t batch,
+                                   const nc_codd* codd, const float* g_out, const float* g_universe,
+                                   float* g_cell_params, float* g_filters, void* d_ws,
+                                   size_t ws_bytes, void* stream);
+
+/*
  * nc_vnn_forward_static -- no counterpart in the reference.  Inference forward (flags 0)
  * that takes no workspace: its scratch is a static device array of
  * NC_STATIC_SCRATCH_BYTES inside this library, held on every GPU that loads the library

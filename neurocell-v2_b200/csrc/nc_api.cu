@@ -53,7 +53,18 @@ static nc_status batch_step_sum(const float* in, int batch, int d, int t0, size_
 __global__ void border_grad_kernel(Geo g, const float* G, const float* gdelta, float* gborder);
 __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* cell, const float* filters,
                                    const uint8_t* owm, const float* gsum, const float* gborder,
-                                   const float* gdsum, float* gcell, float* gfilt);
+                                   const float* gdsum, const float* gring_final, float* gcell,
+                                   float* gfilt);
+__global__ void universe_fwd_kernel(Geo g, StepParams sp, const float* cell, const float* uroi,
+                                    float* universe, int B);
+__global__ void gather_out_kernel(Geo g, const int32_t* out_index, const float* universe, float* out,
+                                  int B);
+__global__ void universe_bwd_roi_kernel(Geo g, StepParams sp, const float* cell, const float* uroi,
+                                        const float* guni, float* guroi, int B);
+__global__ void universe_bwd_ring_kernel(Geo g, StepParams sp, const float* cell, const float* guni,
+                                         float* gring, int B);
+__global__ void universe_bwd_ports_kernel(Geo g, const int32_t* out_index, const float* uroi,
+                                          const float* gout, float* guroi, int B);
 __global__ void mse_kernel(const float* o, const float* y, int n, float* loss, float* g);
 __global__ void softmax_ce_kernel(const float* x, const int32_t* lab, int batch, int n,
                                   float* loss, float* g);
@@ -243,6 +254,17 @@ static FftfArgs fftf_args(const Prepared& pr, void* ws, const float* inputs, int
   return a;
 }
 
+// Universe (B, H, W) from the last step's ROI cells, and the port outputs gathered from it.
+static nc_status assemble_universe(const Prepared& pr, const float* cell, const float* uroi,
+                                   float* universe, float* out, int batch, cudaStream_t st) {
+  const size_t n = (size_t)batch * pr.g.H * pr.g.W;
+  universe_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(pr.g, pr.sp, cell, uroi, universe, batch);
+  NC_CHECK(launch_check("universe_fwd_kernel launch"));
+  gather_out_kernel<<<(batch * pr.g.n_out + 127) / 128, 128, 0, st>>>(pr.g, pr.out_index, universe, out,
+                                                                      batch);
+  return launch_check("gather_out_kernel launch");
+}
+
 static nc_status launch_prestep(const Prepared& pr, const float* cell, const float* filters,
                                 const nc_codd* codd, cudaStream_t st) {
   const int HW = pr.g.H * pr.g.W;
@@ -346,28 +368,34 @@ size_t nc_workspace_bytes(const nc_topo* topo, int32_t batch, uint32_t flags) {
   return ws_layout(g, batch, flags, nullptr, nullptr, nullptr).total;
 }
 
-nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* cell_params,
-                         const float* filters, const float* inputs, int32_t batch,
-                         const nc_codd* codd, uint32_t flags, float* out, void* d_ws,
-                         size_t ws_bytes, void* stream) {
+// The forward of both entry points; `universe` (non-null) selects universe mode, in which
+// the last step writes its ROI cells to the workspace and the universe is assembled.
+static nc_status vnn_forward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                             const float* filters, const float* inputs, int32_t batch,
+                             const nc_codd* codd, uint32_t flags, float* out, float* universe,
+                             void* d_ws, size_t ws_bytes, void* stream) {
   Prepared pr;
   NC_CHECK(prepare(topo, d_plan, batch, flags, d_ws, ws_bytes, &pr));
   NC_CHECK(check_codd(codd));
   NC_CHECK(check_ptr(cell_params, "cell_params"));
   NC_CHECK(check_ptr(filters, "filters"));
   NC_CHECK(check_ptr(out, "out"));
+  if (universe) NC_CHECK(check_ptr(universe, "universe"));
   if (pr.g.n_in > 0) NC_CHECK(check_ptr(inputs, "inputs"));
   cudaStream_t st = as_stream(stream);
   NC_CHECK(launch_prestep(pr, cell_params, filters, codd, st));
+  float* uroi = universe ? at<float>(d_ws, pr.L.uroi) : nullptr;
 
   const bool train = (flags & NC_FLAG_TRAIN) != 0;
   if (pr.g.algo == NC_CONV_FFT) {
     FftCall c = fft_call(pr, d_ws, inputs, batch, train);
     c.out = out;
+    c.uroi = uroi;
     if (fftf_fits(pr.g)) {
       // small grid: direction-pair filter spectra, then one fused kernel per sample
       FftfArgs fa = fftf_args(pr, d_ws, inputs, batch, train);
       fa.out = out;
+      fa.uroi = uroi;
       NC_CHECK(fftf_pair_spectra(pr.g, pr.sp.geff, at<float2>(d_ws, pr.L.f_h), st));
       if (g_prof.fs) NC_CUDA_CHECK(cudaEventRecord(g_prof.fs, st));
       NC_CHECK(fftf_forward(fa, st));
@@ -377,6 +405,7 @@ nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* c
       NC_CHECK(fft_forward(c, st));
       if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
     }
+    if (universe) NC_CHECK(assemble_universe(pr, cell_params, uroi, universe, out, batch, st));
     clear_error();
     return NC_OK;
   }
@@ -393,6 +422,7 @@ nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* c
   a.rstd = at<float>(d_ws, pr.L.rstd);
   a.fscr = at<float>(d_ws, pr.L.fscr);
   a.zscr = at<float>(d_ws, pr.L.zscr);
+  a.uroi = uroi;
   a.train = train ? 1 : 0;
   a.g_smem = pr.gs ? 1 : 0;
   a.f_smem = (pr.gs && pr.fs) ? 1 : 0;
@@ -402,7 +432,8 @@ nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* c
     return set_error(NC_ERR_UNSUPPORTED, "field does not fit on chip and no scratch was laid out");
   if (!a.z_smem && !train && !a.zscr)
     return set_error(NC_ERR_UNSUPPORTED, "planes do not fit on chip and no scratch was laid out");
-  const FastKernels fk = fast_kernels(pr.g);
+  // universe mode runs the generic kernels (the specialised ones end in the port epilogue)
+  const FastKernels fk = universe ? FastKernels{} : fast_kernels(pr.g);
   const void* fn = fk.fwd ? fk.fwd : (const void*)vnn_fused_fwd_kernel;
   const size_t smem = fk.fwd ? fk.fwd_smem : fused_smem_bytes(pr.g, a.g_smem, a.f_smem, a.z_smem);
   NC_CHECK(set_smem_attr(fn, smem));
@@ -414,29 +445,74 @@ nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* c
   }
   NC_CHECK(launch_check("fused forward kernel launch"));
   if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
+  if (universe) NC_CHECK(assemble_universe(pr, cell_params, uroi, universe, out, batch, st));
   clear_error();
   return NC_OK;
 }
 
-nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* cell_params,
-                          const float* filters, const float* inputs, int32_t batch,
-                          const nc_codd* codd, const float* g_out, float* g_cell_params,
-                          float* g_filters, void* d_ws, size_t ws_bytes, void* stream) {
+nc_status nc_vnn_forward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                         const float* filters, const float* inputs, int32_t batch,
+                         const nc_codd* codd, uint32_t flags, float* out, void* d_ws,
+                         size_t ws_bytes, void* stream) {
+  return vnn_forward(topo, d_plan, cell_params, filters, inputs, batch, codd, flags, out, nullptr, d_ws,
+                     ws_bytes, stream);
+}
+
+nc_status nc_vnn_forward_universe(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                                  const float* filters, const float* inputs, int32_t batch,
+                                  const nc_codd* codd, uint32_t flags, float* out, float* universe,
+                                  void* d_ws, size_t ws_bytes, void* stream) {
+  if (!universe) return set_error(NC_ERR_INVALID, "universe is null");
+  return vnn_forward(topo, d_plan, cell_params, filters, inputs, batch, codd, flags, out, universe,
+                     d_ws, ws_bytes, stream);
+}
+
+// The backward of both entry points; g_universe (non-null) selects universe mode.
+static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                              const float* filters, const float* inputs, int32_t batch,
+                              const nc_codd* codd, const float* g_out, const float* g_universe,
+                              float* g_cell_params, float* g_filters, void* d_ws, size_t ws_bytes,
+                              void* stream) {
   Prepared pr;
   NC_CHECK(prepare(topo, d_plan, batch, NC_FLAG_TRAIN, d_ws, ws_bytes, &pr));
   NC_CHECK(check_codd(codd));
   NC_CHECK(check_ptr(cell_params, "cell_params"));
   NC_CHECK(check_ptr(filters, "filters"));
-  NC_CHECK(check_ptr(g_out, "g_out"));
+  NC_CHECK(check_ptr(g_universe ? g_universe : g_out, g_universe ? "g_universe" : "g_out"));
+  if (g_universe && g_out) NC_CHECK(check_ptr(g_out, "g_out"));
   NC_CHECK(check_ptr(g_cell_params, "g_cell_params"));
   NC_CHECK(check_ptr(g_filters, "g_filters"));
   if (pr.g.n_in > 0) NC_CHECK(check_ptr(inputs, "inputs"));
   cudaStream_t st = as_stream(stream);
   const Geo& g = pr.g;
   const WsLayout& L = pr.L;
+  float* guroi = nullptr;
+  float* gringf = nullptr;
+  if (g_universe) {
+    // universe adjoint: the last step's ROI-cell gradient and the VALID ring gradient
+    const float* uroi = at<float>(d_ws, L.uroi);
+    guroi = at<float>(d_ws, L.guroi);
+    const size_t n = (size_t)batch * g.P;
+    universe_bwd_roi_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, pr.sp, cell_params, uroi,
+                                                                         g_universe, guroi, batch);
+    NC_CHECK(launch_check("universe_bwd_roi_kernel launch"));
+    if (g_out) {
+      universe_bwd_ports_kernel<<<(batch * g.n_out + 127) / 128, 128, 0, st>>>(g, pr.out_index, uroi, g_out,
+                                                                               guroi, batch);
+      NC_CHECK(launch_check("universe_bwd_ports_kernel launch"));
+    }
+    if (g.padding == NC_PAD_VALID) {
+      gringf = at<float>(d_ws, L.gringf);
+      universe_bwd_ring_kernel<<<(g.H * g.W + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, g_universe,
+                                                                        gringf, batch);
+      NC_CHECK(launch_check("universe_bwd_ring_kernel launch"));
+    }
+  }
+  if (g_universe) g_out = nullptr;   // folded into guroi above
   if (g.algo == NC_CONV_FFT && fftf_fits(g)) {
     FftfArgs fa = fftf_args(pr, d_ws, inputs, batch, true);
     fa.gout = g_out;
+    fa.guroi = guroi;
     if (g_prof.bs) NC_CUDA_CHECK(cudaEventRecord(g_prof.bs, st));
     NC_CHECK(fftf_backward(fa, st));
     if (g_prof.be) NC_CUDA_CHECK(cudaEventRecord(g_prof.be, st));
@@ -462,7 +538,7 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
       NC_CHECK(launch_check("seg_batch_sum2_kernel launch"));
     }
     prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, gsum,
-                                                         gborder, gdsum, g_cell_params, g_filters);
+                                                         gborder, gdsum, gringf, g_cell_params, g_filters);
     NC_CHECK(launch_check("prestep_bwd_kernel launch"));
     clear_error();
     return NC_OK;
@@ -470,12 +546,13 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
   if (g.algo == NC_CONV_FFT) {
     FftCall c = fft_call(pr, d_ws, inputs, batch, true);
     c.gout = g_out;
+    c.guroi = guroi;
     if (g_prof.bs) NC_CUDA_CHECK(cudaEventRecord(g_prof.bs, st));
     NC_CHECK(fft_backward(c, st));
     if (g_prof.be) NC_CUDA_CHECK(cudaEventRecord(g_prof.be, st));
     const int HW = g.H * g.W;
     prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, c.gsum,
-                                                         c.gborder, c.gdsum, g_cell_params, g_filters);
+                                                         c.gborder, c.gdsum, gringf, g_cell_params, g_filters);
     NC_CHECK(launch_check("prestep_bwd_kernel launch"));
     clear_error();
     return NC_OK;
@@ -497,6 +574,7 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
   a.gpix = at<float>(d_ws, L.gpix);
   a.gdpart = at<float>(d_ws, L.gdpart);
   a.gdelta = at<float>(d_ws, L.gdelta);
+  a.guroi = guroi;
   a.g_smem = pr.gs ? 1 : 0;
   a.f_smem = (pr.gs && pr.fs) ? 1 : 0;
   a.gz_smem = (a.f_smem && pr.gzs) ? 1 : 0;
@@ -505,7 +583,7 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
     return set_error(NC_ERR_UNSUPPORTED, "field does not fit on chip and no scratch was laid out");
   if (!a.gz_smem && !a.gzscr)
     return set_error(NC_ERR_UNSUPPORTED, "plane gradients do not fit on chip and no scratch was laid out");
-  const FastKernels fk = fast_kernels(g);
+  const FastKernels fk = g_universe ? FastKernels{} : fast_kernels(g);
   const void* fn = fk.bwd ? fk.bwd : (const void*)vnn_fused_bwd_kernel;
   const size_t smem = fk.bwd ? fk.bwd_smem : fused_smem_bytes(g, a.g_smem, a.f_smem, a.gz_smem);
   NC_CHECK(set_smem_attr(fn, smem));
@@ -551,10 +629,28 @@ nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* 
     NC_CHECK(launch_check("border_grad_kernel launch"));
   }
   prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, gsum,
-                                                       gborder, gdsum, g_cell_params, g_filters);
+                                                       gborder, gdsum, gringf, g_cell_params, g_filters);
   NC_CHECK(launch_check("prestep_bwd_kernel launch"));
   clear_error();
   return NC_OK;
+}
+
+nc_status nc_vnn_backward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                          const float* filters, const float* inputs, int32_t batch,
+                          const nc_codd* codd, const float* g_out, float* g_cell_params,
+                          float* g_filters, void* d_ws, size_t ws_bytes, void* stream) {
+  return vnn_backward(topo, d_plan, cell_params, filters, inputs, batch, codd, g_out, nullptr,
+                      g_cell_params, g_filters, d_ws, ws_bytes, stream);
+}
+
+nc_status nc_vnn_backward_universe(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                                   const float* filters, const float* inputs, int32_t batch,
+                                   const nc_codd* codd, const float* g_out, const float* g_universe,
+                                   float* g_cell_params, float* g_filters, void* d_ws,
+                                   size_t ws_bytes, void* stream) {
+  if (!g_universe) return set_error(NC_ERR_INVALID, "g_universe is null");
+  return vnn_backward(topo, d_plan, cell_params, filters, inputs, batch, codd, g_out, g_universe,
+                      g_cell_params, g_filters, d_ws, ws_bytes, stream);
 }
 
 nc_status nc_codd_states(const nc_topo* topo, const void* d_plan, const float* states_raw,

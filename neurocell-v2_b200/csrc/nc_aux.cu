@@ -161,8 +161,8 @@ __global__ void border_grad_kernel(Geo g, const float* __restrict__ G,
 __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* __restrict__ cell,
                                    const float* __restrict__ filters, const uint8_t* __restrict__ owm,
                                    const float* __restrict__ gsum, const float* __restrict__ gborder,
-                                   const float* __restrict__ gdsum, float* __restrict__ gcell,
-                                   float* __restrict__ gfilt) {
+                                   const float* __restrict__ gdsum, const float* __restrict__ gring_final,
+                                   float* __restrict__ gcell, float* __restrict__ gfilt) {
   const int HW = g.H * g.W;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < HW) {
@@ -184,6 +184,13 @@ __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* __restrict
       const float av = act_fwd_deriv(g.act, Bv, g.slope, &da);
       g_b += gb * da * s;
       g_s += gb * av;
+    }
+    if (gring_final) {              // universe ring f(B) * s_prob (propagator.py:700-705)
+      const float gr = gring_final[i];
+      float da;
+      const float av = act_fwd_deriv(g.fact, Bv, g.fslope, &da);
+      g_b += gr * da * s;
+      g_s += gr * av;
     }
     gcell[i] = owm[i] ? 0.f : g_wp;
     gcell[HW + i] = g_b;
@@ -275,6 +282,95 @@ __global__ void fp32_peak_kernel(int iters, float* sink) {
 #pragma unroll
   for (int j = 0; j < 16; ++j) s += a[j];
   if (s == 12345.678f) sink[0] = s;   // practically never true; keeps the chains live
+}
+
+}  // namespace nc
+
+// ---------------------------------------------------------------------------------------
+// universe assembly (propagate_vnn_2d(..., return_universe=True), propagator.py:684-734)
+// ---------------------------------------------------------------------------------------
+namespace nc {
+
+// Value of grid cell k before the final activation: the last step's ROI cell, or on the
+// VALID ring f(B) * s_prob (B * s_prob without a final activation).
+__device__ __forceinline__ bool universe_pre(const Geo& g, const StepParams& sp, const float* cell,
+                                             const float* uroi_b, int k, float* pre) {
+  const int r = k / g.W - g.pad_h, c = k - (k / g.W) * g.W - g.pad_w;
+  if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) {
+    *pre = uroi_b[r * g.roi_w + c];
+    return true;
+  }
+  const float Bv = cell[g.H * g.W + k];
+  *pre = act_fwd(g.fact, Bv, g.fslope) * sp.sprob[k];
+  return false;
+}
+
+__global__ void universe_fwd_kernel(Geo g, StepParams sp, const float* __restrict__ cell,
+                                    const float* __restrict__ uroi, float* __restrict__ universe, int B) {
+  const int HW = g.H * g.W;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)B * HW) return;
+  const int b = (int)(i / HW), k = (int)(i - (size_t)b * HW);
+  float pre;
+  universe_pre(g, sp, cell, uroi + (size_t)b * g.P, k, &pre);
+  universe[i] = act_fwd(g.fact, pre, g.fslope);
+}
+
+__global__ void gather_out_kernel(Geo g, const int32_t* __restrict__ out_index,
+                                  const float* __restrict__ universe, float* __restrict__ out, int B) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * g.n_out) return;
+  const int b = i / g.n_out, j = i - b * g.n_out;
+  out[i] = universe[(size_t)b * g.H * g.W + out_index[j]];
+}
+
+// g_universe -> gradient of the last step's ROI cells (B, P)
+__global__ void universe_bwd_roi_kernel(Geo g, StepParams sp, const float* __restrict__ cell,
+                                        const float* __restrict__ uroi, const float* __restrict__ guni,
+                                        float* __restrict__ guroi, int B) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)B * g.P) return;
+  const int b = (int)(i / g.P), p = (int)(i - (size_t)b * g.P);
+  const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+  const int k = (r + g.pad_h) * g.W + c + g.pad_w;
+  float d;
+  act_fwd_deriv(g.fact, uroi[i], g.fslope, &d);
+  guroi[i] = guni[(size_t)b * g.H * g.W + k] * d;
+}
+
+// The outputs' gradient added at their cells: guroi[b][p_j] += g_out[b][j] f'(pre)
+// (output cells are distinct, so every thread owns its cell).
+__global__ void universe_bwd_ports_kernel(Geo g, const int32_t* __restrict__ out_index,
+                                          const float* __restrict__ uroi, const float* __restrict__ gout,
+                                          float* __restrict__ guroi, int B) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * g.n_out) return;
+  const int b = i / g.n_out, j = i - b * g.n_out;
+  const int idx = out_index[j];
+  const int p = (idx / g.W - g.pad_h) * g.roi_w + (idx - (idx / g.W) * g.W - g.pad_w);
+  const size_t o = (size_t)b * g.P + p;
+  float d;
+  act_fwd_deriv(g.fact, uroi[o], g.fslope, &d);
+  guroi[o] += gout[i] * d;
+}
+
+// g_universe on the VALID ring, summed over the batch in sample order -> (H*W)
+__global__ void universe_bwd_ring_kernel(Geo g, StepParams sp, const float* __restrict__ cell,
+                                         const float* __restrict__ guni, float* __restrict__ gring, int B) {
+  const int HW = g.H * g.W;
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= HW) return;
+  const int r = k / g.W - g.pad_h, c = k - (k / g.W) * g.W - g.pad_w;
+  if (g.padding != NC_PAD_VALID || (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w)) {
+    gring[k] = 0.f;
+    return;
+  }
+  const float pre = act_fwd(g.fact, cell[HW + k], g.fslope) * sp.sprob[k];
+  float s = 0.f;
+  for (int b = 0; b < B; ++b) s += guni[(size_t)b * HW + k];
+  float d;
+  act_fwd_deriv(g.fact, pre, g.fslope, &d);
+  gring[k] = s * d;
 }
 
 }  // namespace nc

@@ -278,11 +278,13 @@ __global__ void __launch_bounds__(kEpiThreads) plane_stats_kernel(Geo g, const f
   }
 }
 
-// Hidden-step epilogue (epilogue.py:28-56): standardise (in place when zhat != null), gate,
-// write the next field's interior and the training residual.
+// ROI epilogue (epilogue.py:28-56): standardise (in place when write_zhat), gate, write the
+// next field's interior and the training residual -- or, in universe mode (uroi != null),
+// the last step's ROI cells.
 __global__ void hidden_epi_kernel(Geo g, StepParams sp, float* z, size_t zs, int write_zhat,
                                   const float* __restrict__ mean, const float* __restrict__ rstd,
-                                  float* __restrict__ field, float* __restrict__ xsave, int t, int B) {
+                                  float* __restrict__ field, float* __restrict__ xsave, int t, int B,
+                                  int act_id, float slope, float* __restrict__ uroi) {
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)B * g.P) return;
   const int b = (int)(i / g.P), p = (int)(i - (size_t)b * g.P);
@@ -293,10 +295,14 @@ __global__ void hidden_epi_kernel(Geo g, StepParams sp, float* z, size_t zs, int
     const float zh = (zb[(size_t)m * g.P] - mean[b * g.M + m]) * rstd[b * g.M + m];
     if (write_zhat) zb[(size_t)m * g.P] = zh;
     lin += zh;
-    if (g.act != NC_ACT_NONE) act += act_fwd(g.act, zh + bb, g.slope);
+    if (act_id != NC_ACT_NONE) act += act_fwd(act_id, zh + bb, slope);
   }
-  if (g.act == NC_ACT_NONE) act = lin + (float)g.M * bb;
+  if (act_id == NC_ACT_NONE) act = lin + (float)g.M * bb;
   const float xn = sp.weff[p] * lin + sp.seff[p] * act;
+  if (uroi) {
+    uroi[i] = xn;
+    return;
+  }
   const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
   field[(size_t)b * g.Fh * g.Fw + (size_t)(r + g.oh) * g.Fw + c + g.ow] = xn;
   if (xsave) xsave[((size_t)b * (g.d - 1) + t) * g.P + p] = xn;
@@ -420,11 +426,13 @@ __device__ __forceinline__ float field_grad(const Geo& g, const float* dxb, int 
   return s;
 }
 
-// Hidden-step adjoint (kernels_pallas.py:221-291) of step t-1 for the samples of chunk
-// blockIdx.y; per-chunk pixel-gradient partials go to gpart.
+// ROI-epilogue adjoint (kernels_pallas.py:221-291) for the samples of chunk blockIdx.y:
+// the cell gradient comes from the field adjoint dx (hidden step t-1) or, in universe mode,
+// from gy_roi (B, P) with the final activation; per-chunk pixel-gradient partials go to gpart.
 __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__ dx,
                                  const float* __restrict__ zh_t, size_t zs, float* __restrict__ gz,
-                                 float* __restrict__ gpart, int B, int bc) {
+                                 float* __restrict__ gpart, int B, int bc, int act_id, float slope,
+                                 const float* __restrict__ gy_roi) {
   const int p = blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= g.P) return;
   const int k = blockIdx.y;
@@ -434,14 +442,14 @@ __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__
   const float bb = sp.broi[p], we = sp.weff[p], se = sp.seff[p];
   float gp0 = 0.f, gp1 = 0.f, gp2 = 0.f;
   for (int b = b0; b < b1; ++b) {
-    const float gy = field_grad(g, dx + (size_t)b * FF, r, c);
+    const float gy = gy_roi ? gy_roi[(size_t)b * P + p] : field_grad(g, dx + (size_t)b * FF, r, c);
     const float* ZH = zh_t + (size_t)b * zs + p;
     float* GZ = gz + (size_t)b * g.M * P + p;
     float lin = 0.f, act = 0.f, dsum = 0.f;
     for (int m = 0; m < g.M; ++m) {
       const float zh = ZH[m * P];
       float dd;
-      const float av = act_fwd_deriv(g.act, zh + bb, g.slope, &dd);
+      const float av = act_fwd_deriv(act_id, zh + bb, slope, &dd);
       lin += zh;
       act += av;
       dsum += dd;
@@ -628,7 +636,14 @@ nc_status fft_forward(const FftCall& c, cudaStream_t st) {
     NC_CHECK(launched("plane_stats_kernel launch"));
     if (t < g.d - 1) {
       hidden_epi_kernel<<<blocks_for((size_t)B * P, kEpiThreads), kEpiThreads, 0, st>>>(
-          g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, c.train ? c.xsave : nullptr, t, B);
+          g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, c.train ? c.xsave : nullptr, t, B,
+          g.act, g.slope, nullptr);
+      NC_CHECK(launched("hidden_epi_kernel launch"));
+    } else if (c.uroi) {
+      // universe mode: the ROI epilogue with the final activation (propagator.py:657-682)
+      hidden_epi_kernel<<<blocks_for((size_t)B * P, kEpiThreads), kEpiThreads, 0, st>>>(
+          g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, nullptr, t, B, g.fact, g.fslope,
+          c.uroi);
       NC_CHECK(launched("hidden_epi_kernel launch"));
     } else {
       port_out_kernel<<<blocks_for((size_t)B * g.n_out, 128), 128, 0, st>>>(g, c.sp, c.out_index, z, zs,
@@ -660,12 +675,21 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
   if (c.gborder) NC_CUDA_CHECK(cudaMemsetAsync(c.gborder, 0, sizeof(float) * g.H * g.W, st));
   NC_CUDA_CHECK(cudaMemsetAsync(c.gz, 0, sizeof(float) * B * M * P, st));
 
-  // output step: sparse port adjoint, then the standardisation adjoint
+  // output step: sparse port adjoint (or the universe ROI adjoint), then the
+  // standardisation adjoint
   {
     const float* zh = c.zhat + (size_t)(g.d - 1) * M * P;
-    port_gz_kernel<<<blocks_for(g.n_out, 128), 128, 0, st>>>(g, c.sp, c.out_index, c.gout, zh, zs, c.gz,
-                                                              c.gsum, B);
-    NC_CHECK(launched("port_gz_kernel launch"));
+    if (c.guroi) {
+      hidden_gz_kernel<<<dim3(blocks_for(P, 256), nch), 256, 0, st>>>(g, c.sp, c.dx, zh, zs, c.gz, c.gpart,
+                                                                      B, bc, g.fact, g.fslope, c.guroi);
+      NC_CHECK(launched("hidden_gz_kernel launch"));
+      gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
+      NC_CHECK(launched("gsum_chunks_kernel launch"));
+    } else {
+      port_gz_kernel<<<blocks_for(g.n_out, 128), 128, 0, st>>>(g, c.sp, c.out_index, c.gout, zh, zs, c.gz,
+                                                                c.gsum, B);
+      NC_CHECK(launched("port_gz_kernel launch"));
+    }
     if (g.norm) {
       norm_bwd_kernel<<<B * g.M, kEpiThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, g.d - 1);
       NC_CHECK(launched("norm_bwd_kernel launch"));
@@ -709,7 +733,7 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
     // hidden-step adjoint of step t-1
     const float* zh = c.zhat + (size_t)(t - 1) * M * P;
     hidden_gz_kernel<<<dim3(blocks_for(P, 256), nch), 256, 0, st>>>(g, c.sp, c.dx, zh, zs, c.gz, c.gpart,
-                                                                    B, bc);
+                                                                    B, bc, g.act, g.slope, nullptr);
     NC_CHECK(launched("hidden_gz_kernel launch"));
     gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
     NC_CHECK(launched("gsum_chunks_kernel launch"));

@@ -40,6 +40,8 @@ struct FftCall {
   // call arguments
   const float* gout;          // backward: (B, n_out)
   float* out;                 // forward: (B, n_out)
+  float* uroi;                // universe mode forward: (B, P) last-step ROI cells, else null
+  const float* guroi;         // universe mode backward: (B, P) their gradient, else null
 };
 
 // Filter spectra G^_m / (Nh*Nw) into c.gspec (uses c.tmp).

@@ -249,7 +249,14 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
     }
     __syncthreads();
 
-    if (!last) {
+    if (last && a.uroi) {
+      // universe mode: the last step's ROI cells (ROI epilogue with the final activation)
+      for (int p = tid; p < g.P; p += nt) {
+        const float bb = a.sp.broi[p];
+        const float act = (g.fact == NC_ACT_NONE) ? lin[p] + (float)g.M * bb : acc[p];
+        a.uroi[(size_t)b * P + p] = a.sp.weff[p] * lin[p] + a.sp.seff[p] * act;
+      }
+    } else if (!last) {
       float* xs = a.train ? a.xsave + ((size_t)b * (g.d - 1) + t) * P : nullptr;
       for (int p = tid; p < g.P; p += nt) {
         const float bb = a.sp.broi[p];
@@ -305,8 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   __syncthreads();
 
   // output step (t = d-1): the port cells' plane gradients and parameter gradients
-  // (kernels_pallas.py:1378-1504)
-  {
+  // (kernels_pallas.py:1378-1504); universe mode: the last step's cell gradient instead
+  if (a.guroi) {
+    for (int p = tid; p < g.P; p += nt) gy[p] = a.guroi[(size_t)b * P + p];
+  } else {
     const float* ZH = a.zhat + ((size_t)b * g.d + (g.d - 1)) * M * P;
     for (int jo = tid; jo < g.n_out; jo += nt) {
       const int idx = a.out_index[jo];
@@ -351,6 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
     if (t > 0)
       for (int i = tid; i < kPlane; i += nt) D[i] = make_float2(0.f, 0.f);
     const float* ZH = a.zhat + ((size_t)b * g.d + t) * M * P;
+    const int act_id = last ? g.fact : g.act;     // universe mode runs the last step's ROI
+    const float slope = last ? g.fslope : g.slope;  // epilogue with the final activation
 
     for (int j = 0; j < pairs; ++j) {
       const int m1 = 2 * j, m2 = 2 * j + 1;
@@ -373,14 +384,14 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
         const int p = r * g.roi_w + c;
         h1[k] = z1[p];
         h2[k] = z2[p];
-        if (last) {
+        if (last && !a.guroi) {
           const int jo = pmap[p];
           if (jo >= 0) v[k] = make_float2(gport[jo * g.M + m1], gport[jo * g.M + m2]);
         } else {
           const float y = gy[p], bb = a.sp.broi[p], we = a.sp.weff[p], se = a.sp.seff[p];
           float d1, d2;
-          const float a1 = act_fwd_deriv(g.act, h1[k] + bb, g.slope, &d1);
-          const float a2 = act_fwd_deriv(g.act, h2[k] + bb, g.slope, &d2);
+          const float a1 = act_fwd_deriv(act_id, h1[k] + bb, slope, &d1);
+          const float a2 = act_fwd_deriv(act_id, h2[k] + bb, slope, &d2);
           v[k] = make_float2(we * y + se * y * d1, we * y + se * y * d2);
           // pixel-parameter gradients, summed over directions pair by pair
           gp0[p] += y * (h1[k] + h2[k]);

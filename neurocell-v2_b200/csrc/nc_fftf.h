@@ -27,6 +27,8 @@ struct FftfArgs {
   float* gpix;                // backward: (B, 3, P) per-sample pixel-parameter gradients
   float* gdpart;              // backward: (B, M*K) per-sample filter gradients
   float* gring;               // backward: (B, Fh*Fw) per-sample ring gradients (VALID, d>1) or null
+  float* uroi;                // universe mode forward: (B, P) last-step ROI cells, else null
+  const float* guroi;         // universe mode backward: (B, P) their gradient, else null
 };
 
 // True when the fused kernels serve this geometry (FFT side 64, even M, fits on chip).

@@ -155,9 +155,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) vnn_fused_fwd_kernel(FwdArgs
     if (a.train)
       for (int m = tid; m < g.M; m += nt) a.rstd[((size_t)b * g.d + t) * M + m] = s_rstd[m];
 
-    if (t < g.d - 1) {
-      // hidden-step epilogue (epilogue.py:28-56) -> new ROI field inside F
-      float* xs = a.train ? a.xsave + ((size_t)b * (g.d - 1) + t) * P : nullptr;
+    const bool last = (t == g.d - 1);
+    if (!last || a.uroi) {
+      // ROI epilogue (epilogue.py:28-56) -> new ROI field inside F; in universe mode the
+      // last step runs it with the final activation into uroi (propagator.py:657-682)
+      const int act_id = last ? g.fact : g.act;
+      const float slope = last ? g.fslope : g.slope;
+      float* xs = (a.train && !last) ? a.xsave + ((size_t)b * (g.d - 1) + t) * P : nullptr;
       for (int p = tid; p < g.P; p += nt) {
         const float bb = a.sp.broi[p];
         float lin = 0.f, act = 0.f;
@@ -165,15 +169,20 @@ __global__ void __launch_bounds__(kFusedThreads, 1) vnn_fused_fwd_kernel(FwdArgs
           const float zh = (Z[m * P + p] - s_mean[m]) * s_rstd[m];
           if (ZH) ZH[m * P + p] = zh;
           lin += zh;
-          if (g.act != NC_ACT_NONE) act += act_fwd(g.act, zh + bb, g.slope);
+          if (act_id != NC_ACT_NONE) act += act_fwd(act_id, zh + bb, slope);
         }
-        if (g.act == NC_ACT_NONE) act = lin + (float)g.M * bb;
+        if (act_id == NC_ACT_NONE) act = lin + (float)g.M * bb;
         const float xn = a.sp.weff[p] * lin + a.sp.seff[p] * act;
+        if (last) {
+          a.uroi[(size_t)b * P + p] = xn;
+          continue;
+        }
         const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
         F[(r + g.oh) * g.Fs + c + g.ow] = xn;
         if (xs) xs[p] = xn;
       }
       __syncthreads();
+      if (last) continue;
       if (t == 0 && g.padding == NC_PAD_VALID) {
         field_border_ring(g, F, a.sp.border, tid, nt);
         __syncthreads();
@@ -331,12 +340,33 @@ __global__ void __launch_bounds__(kFusedThreads, 1) vnn_fused_bwd_kernel(BwdArgs
   __syncthreads();
   if (g.padding == NC_PAD_VALID && g.d > 1) field_border_ring(g, F, a.sp.border, tid, nt);
 
-  // ---- output step (t = d-1): sparse port adjoint (kernels_pallas.py:1107-1179) --------
+  // ---- output step (t = d-1): sparse port adjoint (kernels_pallas.py:1107-1179), or in
+  // universe mode the ROI-epilogue adjoint with the final activation ------------------------
   {
     const int t = g.d - 1;
     const float* ZH = a.zhat + ((size_t)b * g.d + t) * M * P;
     for (int m = tid; m < g.M; m += nt) s_rstd[m] = a.rstd[((size_t)b * g.d + t) * M + m];
-    for (int j = tid; j < g.n_out; j += nt) {
+    if (a.guroi) {
+      for (int p = tid; p < g.P; p += nt) {
+        const float gy = a.guroi[(size_t)b * P + p];
+        const float bb = a.sp.broi[p], we = a.sp.weff[p], se = a.sp.seff[p];
+        float lin = 0.f, act = 0.f, dsum = 0.f;
+        for (int m = 0; m < g.M; ++m) {
+          const float zh = ZH[m * P + p];
+          float dd;
+          const float av = act_fwd_deriv(g.fact, zh + bb, g.fslope, &dd);
+          lin += zh;
+          act += av;
+          dsum += dd;
+          GZ[m * P + p] = we * gy + se * gy * dd;
+        }
+        if (g.fact == NC_ACT_NONE) act = lin + (float)g.M * bb;
+        gp0[p] += gy * lin;
+        gp1[p] += gy * act;
+        gp2[p] += se * gy * dsum;
+      }
+    }
+    for (int j = tid; j < g.n_out && !a.guroi; j += nt) {
       const int idx = a.out_index[j];
       const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
       const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);

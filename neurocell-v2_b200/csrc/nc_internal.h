@@ -49,6 +49,8 @@ PlanLayout plan_layout(const nc_topo* t);
 struct WsLayout {
   // step parameters (pre-step fusion output)
   size_t weff, seff, broi, border, sprob, dsprob, wpinned, geff;
+  // universe mode: last-step ROI cells (B, P), their gradient (B, P), ring gradient (H*W)
+  size_t uroi, guroi, gringf;
   // forward residuals (train)
   size_t xsave, zhat, rstd;
   // scratch when on-chip buffers do not fit

@@ -30,6 +30,8 @@ struct FwdArgs {
   float* rstd;                // train: (B, d, M)
   float* fscr;                // (B, F_elems) field scratch when F is not on-chip
   float* zscr;                // (B, M, P) plane scratch when z is not on-chip (inference)
+  float* uroi;                // universe mode: (B, P) last-step ROI cells (ROI epilogue with
+                              // the final activation) instead of the port outputs; else null
   int train, g_smem, f_smem, z_smem;
   int batch;
 };
@@ -49,6 +51,7 @@ struct BwdArgs {
   float* gpix;                // (B, 3, P) per-sample partials + (B, P) dX plane after them
   float* gdpart;              // (B, M*K) per-sample filter-gradient partials
   float* gdelta;              // (B, M, P) per-sample sum over t>=1 of gz (VALID, d>1)
+  const float* guroi;         // universe mode: (B, P) gradient of the last-step ROI cells
   int g_smem, f_smem, gz_smem;
   int batch;
 };

@@ -124,6 +124,9 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
   L.dsprob = take(fl * HW);
   L.wpinned = take(fl * HW);
   L.geff = take(fl * M * g.K);
+  L.uroi = take(fl * B * P);
+  L.guroi = train ? take(fl * B * P) : SIZE_MAX;
+  L.gringf = train ? take(fl * HW) : SIZE_MAX;
   const size_t dm1 = (size_t)(g.d > 1 ? g.d - 1 : 0);
   L.xsave = train ? take(fl * B * (dm1 ? dm1 : 1) * P) : SIZE_MAX;
   L.zhat = train ? take(fl * B * g.d * M * P) : SIZE_MAX;

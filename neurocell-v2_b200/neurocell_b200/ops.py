@@ -216,6 +216,64 @@ class _VNNPropagate(torch.autograd.Function):
         return g_cell, g_filt, None, None, None, None
 
 
+class _VNNPropagateUniverse(torch.autograd.Function):
+    """``propagate_vnn_2d(..., return_universe=True)``: (outputs, universe) through
+    nc_vnn_forward_universe / nc_vnn_backward_universe."""
+
+    @staticmethod
+    def forward(ctx, cell_params, filters, flat_inputs, plan: Plan, codd: _lib.NcCodd, train: bool):
+        lib = _lib.load()
+        dev = cell_params.device
+        B = flat_inputs.shape[0]
+        H, W = plan.topology.grid_shape
+        flags = _lib.NC_FLAG_TRAIN if train else 0
+        ws_bytes = lib.nc_workspace_bytes(ctypes.byref(plan.topo), B, flags)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        out = torch.empty((B, plan.n_out), dtype=torch.float32, device=dev)
+        uni = torch.empty((B, H, W), dtype=torch.float32, device=dev)
+        _lib.check(lib.nc_vnn_forward_universe(ctypes.byref(plan.topo), _ptr(plan.buf), _ptr(cell_params),
+                                               _ptr(filters), _ptr(flat_inputs), B, ctypes.byref(codd),
+                                               flags, _ptr(out), _ptr(uni), _ptr(ws), ws_bytes,
+                                               _stream(dev)), "nc_vnn_forward_universe")
+        if train:
+            ctx.save_for_backward(cell_params, filters, flat_inputs)
+            ctx.ws, ctx.ws_bytes, ctx.plan, ctx.codd = ws, ws_bytes, plan, codd
+        return out, uni
+
+    @staticmethod
+    def backward(ctx, g_out, g_uni):
+        lib = _lib.load()
+        cell_params, filters, flat_inputs = ctx.saved_tensors
+        plan = ctx.plan
+        dev = cell_params.device
+        B = flat_inputs.shape[0]
+        H, W = plan.topology.grid_shape
+        g_uni = (torch.zeros((B, H, W), dtype=torch.float32, device=dev) if g_uni is None
+                 else g_uni.contiguous().float())
+        g_out = None if g_out is None else g_out.contiguous().float()
+        g_cell = torch.empty_like(cell_params)
+        g_filt = torch.empty_like(filters)
+        _lib.check(lib.nc_vnn_backward_universe(ctypes.byref(plan.topo), _ptr(plan.buf), _ptr(cell_params),
+                                                _ptr(filters), _ptr(flat_inputs), B, ctypes.byref(ctx.codd),
+                                                _ptr(g_out), _ptr(g_uni), _ptr(g_cell), _ptr(g_filt),
+                                                _ptr(ctx.ws), ctx.ws_bytes, _stream(dev)),
+                   "nc_vnn_backward_universe")
+        ctx.ws = None
+        return g_cell, g_filt, None, None, None, None
+
+
+def propagate_universe(cell_params: torch.Tensor, filters: torch.Tensor, flat_inputs: torch.Tensor,
+                       plan: Plan, codd_mode: str, tau, thr):
+    """(B, n_in) -> ((B, n_out), (B, H, W)); differentiable in the parameters."""
+    for t, n in ((cell_params, "cell_params"), (filters, "greens_filters"), (flat_inputs, "inputs")):
+        _require_cuda(t, n)
+    cp = cell_params.contiguous().float()
+    fl = filters.contiguous().float()
+    xi = flat_inputs.contiguous().float()
+    train = torch.is_grad_enabled() and (cp.requires_grad or fl.requires_grad)
+    return _VNNPropagateUniverse.apply(cp, fl, xi, plan, _codd(codd_mode, tau, thr), train)
+
+
 def propagate(cell_params: torch.Tensor, filters: torch.Tensor, flat_inputs: torch.Tensor,
               plan: Plan, codd_mode: str, tau, thr) -> torch.Tensor:
     """(B, n_in) -> (B, n_out) through the CUDA library; differentiable in the parameters."""

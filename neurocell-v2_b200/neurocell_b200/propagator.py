@@ -109,8 +109,6 @@ def propagate_vnn_2d(
     fact, fslope = ops.resolve_activation(final_activate)
     if sharpen_filter is not None:
         raise NotImplementedError("sharpen_filter (filters.py) is not part of the B200 hot path")
-    if return_universe:
-        raise NotImplementedError("return_universe=True (full-grid assembly) is not built on the B200 path")
     if spatial_mask is not None and not getattr(spatial_mask, "is_full_roi", False):
         raise NotImplementedError("adaptive sub-ROI masks are not built on the B200 path")
     ops._require_cuda(params.cell_params, "params.cell_params")
@@ -121,6 +119,11 @@ def propagate_vnn_2d(
         flat = flat.to(device, non_blocking=True)
     plan = ops.get_plan(topology, shapes, device, act, slope, fact, fslope, norm, hard_pin_io,
                         gated_filters, CONV_OF_BACKEND[backend])
+    if return_universe:
+        # (outputs, full-grid universe) as the reference returns them (propagator.py:730-733)
+        out, uni = ops.propagate_universe(params.cell_params, params.greens_filters, flat, plan,
+                                          codd_mode, state_temperature, active_threshold)
+        return out.reshape((out.shape[0],) + plan.out_shape), uni
     out = ops.propagate(params.cell_params, params.greens_filters, flat, plan, codd_mode,
                         state_temperature, active_threshold)
     return out.reshape((out.shape[0],) + plan.out_shape)

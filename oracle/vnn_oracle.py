@@ -594,10 +594,12 @@ class Config:
     active_threshold: float = 0.6
 
 
-def forward(cell_params, filters, inputs, geom: Geometry, cfg: Config = Config(), dtype=np.float64):
-    """Returns ``(outputs (B, oh, ow), tape)``.  ``filters`` is OIHW (M, 1, kh, kw)."""
-    if not geom.out_in_roi:
-        raise NotImplementedError("output ports outside the ROI are not part of this oracle")
+def forward(cell_params, filters, inputs, geom: Geometry, cfg: Config = Config(), dtype=np.float64,
+            universe=False):
+    """Returns ``(outputs (B, oh, ow), tape)``.  ``filters`` is OIHW (M, 1, kh, kw).
+    ``universe=True`` stops before the output-port epilogue (``forward_universe``)."""
+    if not geom.out_in_roi and not universe:
+        raise NotImplementedError("output ports outside the ROI need forward_universe")
     cp = np.asarray(cell_params, dtype=dtype)
     G0 = np.asarray(filters, dtype=dtype)[:, 0]
     G = _sigmoid(G0) if cfg.gated_filters else G0
@@ -646,14 +648,65 @@ def forward(cell_params, filters, inputs, geom: Geometry, cfg: Config = Config()
         x, et = hidden_epilogue(z, sp, cfg.activate, cfg.act_slope, cfg.norm)
         tape["epis"].append(et)
     z = conv_step(d - 1, x)
+    tape["z_final"] = z
+    if universe:
+        return None, tape
     out, pt = port_epilogue(z, sp, geom, cfg.final_activate, cfg.final_act_slope, cfg.norm)
     tape["port"] = pt
     tape["B"] = out.shape[0]
     return out, tape
 
 
-def backward(gout, tape, geom: Geometry, cfg: Config = Config()):
-    """Returns ``(g_cell_params (3,H,W), g_filters (M,1,kh,kw))``."""
+def forward_universe(cell_params, filters, inputs, geom: Geometry, cfg: Config = Config(),
+                     dtype=np.float64):
+    """``propagate_vnn_2d(..., return_universe=True)`` (propagator.py:657-734 and the
+    CIRCULAR branch 330-341): the last step runs the ROI epilogue with ``final_activate``
+    over the whole ROI; the universe is the (B, H, W) grid with the VALID ring
+    ``f(B) * s_prob`` (``B * s_prob`` without a final activation) and ``f`` applied to every
+    cell afterwards; the outputs are the port cells of the universe.  Returns
+    ``(outputs (B, oh, ow), universe (B, H, W), tape)``."""
+    _, tape = forward(cell_params, filters, inputs, geom, cfg, dtype, universe=True)
+    sp = tape["sp"]
+    fa, fs = cfg.final_activate, cfg.final_act_slope
+    roi_final, et = hidden_epilogue(tape["z_final"], sp, fa, fs, cfg.norm)
+    B = roi_final.shape[0]
+    H, W = geom.grid_shape
+    if geom.padding_mode == "VALID":
+        Bf = tape["cp"][1]
+        ring = (Bf if fa is None else act_fwd(Bf, fa, fs)) * sp["s_prob"]
+        pre = np.broadcast_to(ring[None], (B, H, W)).copy()
+        pre[(slice(None),) + _roi(geom)] = roi_final
+    else:
+        pre = roi_final
+    uni = pre if fa is None else act_fwd(pre, fa, fs)
+    rr, cc = _out_index(geom)
+    r0, c0 = geom.pad_h, geom.pad_w
+    outputs = uni[:, rr + r0, cc + c0]
+    oh, ow = geom.out_port.size
+    tape["uni"] = dict(et=et, pre=pre)
+    return outputs.reshape(B, oh, ow), uni, tape
+
+
+def backward_universe(g_universe, tape, geom: Geometry, cfg: Config = Config()):
+    """VJP of ``forward_universe`` from the gradient of the universe (add the outputs'
+    gradient at the port cells first).  Returns ``(g_cell_params, g_filters)``."""
+    g = np.asarray(g_universe, dtype=tape["G"].dtype)
+    fa, fs = cfg.final_activate, cfg.final_act_slope
+    pre = tape["uni"]["pre"]
+    gpre = g if fa is None else g * act_deriv(pre, fa, fs)
+    roi = _roi(geom)
+    gy = gpre[(slice(None),) + roi]
+    ring_g = None
+    if geom.padding_mode == "VALID":
+        ring_g = gpre.sum(axis=0)
+        ring_g[roi] = 0.0
+    return backward(None, tape, geom, cfg, final_gy=gy, ring_final_g=ring_g)
+
+
+def backward(gout, tape, geom: Geometry, cfg: Config = Config(), final_gy=None, ring_final_g=None):
+    """Returns ``(g_cell_params (3,H,W), g_filters (M,1,kh,kw))``.  ``final_gy`` (universe
+    mode): gradient of the last step's ROI cells, which then run the ROI epilogue with the
+    final activation; ``ring_final_g``: gradient of the VALID ring of the universe."""
     sp, G = tape["sp"], tape["G"]
     kh, kw = geom.kernel_size
     H, W = geom.grid_shape
@@ -665,8 +718,12 @@ def backward(gout, tape, geom: Geometry, cfg: Config = Config()):
             grads[k] = np.zeros_like(sp[k])
     dG = np.zeros_like(G)
     g_delta = None
-    gz = port_epilogue_bwd(np.asarray(gout, dtype=G.dtype), tape["port"], sp, geom,
-                           cfg.final_activate, cfg.final_act_slope, cfg.norm, grads)
+    if final_gy is None:
+        gz = port_epilogue_bwd(np.asarray(gout, dtype=G.dtype), tape["port"], sp, geom,
+                               cfg.final_activate, cfg.final_act_slope, cfg.norm, grads)
+    else:
+        gz = hidden_epilogue_bwd(np.asarray(final_gy, dtype=G.dtype), tape["uni"]["et"], sp,
+                                 cfg.final_activate, cfg.final_act_slope, cfg.norm, grads)
     for t in range(d - 1, -1, -1):
         kind, xin = tape["convs"][t]
         if valid and t > 0:
@@ -713,6 +770,12 @@ def backward(gout, tape, geom: Geometry, cfg: Config = Config()):
     Bf = cp[1]
     g_B += g_border * act_deriv(Bf, cfg.activate, cfg.act_slope) * sp["s_prob"]
     g_s += g_border * act_fwd(Bf, cfg.activate, cfg.act_slope)
+    if ring_final_g is not None:           # universe ring f(B) * s_prob (B * s_prob for None)
+        fa, fs = cfg.final_activate, cfg.final_act_slope
+        fb = Bf if fa is None else act_fwd(Bf, fa, fs)
+        dfb = np.ones_like(Bf) if fa is None else act_deriv(Bf, fa, fs)
+        g_B += ring_final_g * dfb * sp["s_prob"]
+        g_s += ring_final_g * fb
     g_W = np.where(geom.out_weight_mask, 0.0, g_wp)
     g_S = g_s * sp["ds_prob"]
     g_cell = np.stack([g_W, g_B, g_S]).astype(G.dtype)

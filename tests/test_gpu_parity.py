@@ -347,3 +347,50 @@ def test_fft_fused_kernel_is_used_for_the_alu_grid():
                             O.RectPort((12, 30), (4, 1)))
     cell, filt, ins, y = random_problem(geom5, 3, 98)
     check_case(geom5, O.Config(), cell, filt, ins, y, backend="pallas_sram")
+
+
+# ---- return_universe=True (propagator.py:657-734) ----------------------------------------
+def _universe_case(geom, cfg, backend, seed):
+    cell, filt, ins, _ = random_problem(geom, 3, seed)
+    rng = np.random.default_rng(seed + 1)
+    H, W = geom.grid_shape
+    oh, ow = geom.out_port.size
+    wo = rng.normal(size=(3, oh, ow))
+    wu = rng.normal(size=(3, H, W))
+    topo = _nc_topo(geom)
+    dev = torch.device("cuda:0")
+    cp = torch.tensor(cell, device=dev, requires_grad=True)
+    fl = torch.tensor(filt, device=dev, requires_grad=True)
+    xin = [torch.tensor(np.asarray(a), dtype=torch.float32, device=dev) for a in ins]
+    out, uni = nc.propagate_vnn_2d(
+        nc.VNNParams(cp, fl), xin, topo, activate=ACT[cfg.activate],
+        final_activate=ACT[cfg.final_activate], norm=cfg.norm, return_universe=True, backend=backend)
+    L = (out * torch.tensor(wo, device=dev, dtype=torch.float32)).sum() + \
+        (uni * torch.tensor(wu, device=dev, dtype=torch.float32)).sum()
+    L.backward()
+    o_r, u_r, tape = O.forward_universe(cell, filt, ins, geom, cfg)
+    gu = wu.copy()
+    rr, cc = O._out_index(geom)
+    gu[:, rr + geom.pad_h, cc + geom.pad_w] += wo.reshape(3, -1)
+    gc_r, gf_r = O.backward_universe(gu, tape, geom, cfg)
+    errs = dict(out=_rel(out.detach().cpu().numpy(), o_r), uni=_rel(uni.detach().cpu().numpy(), u_r),
+                g_cell=_rel(cp.grad.cpu().numpy(), gc_r), g_filters=_rel(fl.grad.cpu().numpy(), gf_r))
+    bad = {k: v for k, v in errs.items() if not v <= TOL}
+    assert not bad, f"universe parity failure {bad} (all: {errs})"
+
+
+@pytest.mark.parametrize("backend", ["nchw_direct", "pallas_sram"])
+@pytest.mark.parametrize("mode", ["VALID", "SAME", "CIRCULAR"])
+@pytest.mark.parametrize("final", [None, "tanh"])
+def test_return_universe_parity(backend, mode, final):
+    geom = O.make_geometry((20, 22), (5, 3), 4, 3, (O.RectPort((6, 5), (4, 1)),),
+                           O.RectPort((6, 14), (4, 1)), padding_mode=mode)
+    _universe_case(geom, O.Config(final_activate=final), backend, 111)
+
+
+@pytest.mark.parametrize("mode", ["VALID", "SAME"])
+@pytest.mark.parametrize("final", [None, "sigmoid"])
+def test_return_universe_fused_fft_parity(mode, final):
+    geom = O.make_geometry((40, 44), (9, 7), 6, 3, (O.RectPort((10, 8), (4, 1)),),
+                           O.RectPort((12, 30), (4, 1)), padding_mode=mode)
+    _universe_case(geom, O.Config(final_activate=final), "pallas_sram", 121)
