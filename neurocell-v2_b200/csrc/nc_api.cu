@@ -65,6 +65,9 @@ __global__ void universe_bwd_ring_kernel(Geo g, StepParams sp, const float* cell
                                          float* gring, int B);
 __global__ void universe_bwd_ports_kernel(Geo g, const int32_t* out_index, const float* uroi,
                                           const float* gout, float* guroi, int B);
+__global__ void universe_bwd_border_ports_kernel(Geo g, StepParams sp, const float* cell,
+                                                 const int32_t* out_index, const float* gout,
+                                                 float* gring, int B);
 __global__ void mse_kernel(const float* o, const float* y, int n, float* loss, float* g);
 __global__ void softmax_ce_kernel(const float* x, const int32_t* lab, int batch, int n,
                                   float* loss, float* g);
@@ -335,11 +338,6 @@ nc_status nc_plan_build(const nc_topo* topo, const int32_t* in_index, const int3
   for (int j = 0; j < g.n_out; ++j) {
     const int idx = out_index[j];
     if (idx < 0 || idx >= HW) return set_error(NC_ERR_INVALID, "output index %d out of grid", j);
-    const int r = idx / g.W - g.pad_h, c = idx % g.W - g.pad_w;
-    if (r < 0 || r >= g.roi_h || c < 0 || c >= g.roi_w)
-      return set_error(NC_ERR_UNSUPPORTED,
-                       "output cell (%d, %d) lies outside the active ROI; border outputs are not built",
-                       idx / g.W, idx % g.W);
     for (int k = 0; k < j; ++k)
       if (out_index[k] == idx) return set_error(NC_ERR_UNSUPPORTED, "duplicate output cell %d", idx);
   }
@@ -506,6 +504,11 @@ static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const flo
       universe_bwd_ring_kernel<<<(g.H * g.W + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, g_universe,
                                                                         gringf, batch);
       NC_CHECK(launch_check("universe_bwd_ring_kernel launch"));
+      if (g_out) {
+        universe_bwd_border_ports_kernel<<<(g.n_out + 127) / 128, 128, 0, st>>>(
+            g, pr.sp, cell_params, pr.out_index, g_out, gringf, batch);
+        NC_CHECK(launch_check("universe_bwd_border_ports_kernel launch"));
+      }
     }
   }
   if (g_universe) g_out = nullptr;   // folded into guroi above

@@ -347,11 +347,31 @@ __global__ void universe_bwd_ports_kernel(Geo g, const int32_t* __restrict__ out
   if (i >= B * g.n_out) return;
   const int b = i / g.n_out, j = i - b * g.n_out;
   const int idx = out_index[j];
-  const int p = (idx / g.W - g.pad_h) * g.roi_w + (idx - (idx / g.W) * g.W - g.pad_w);
-  const size_t o = (size_t)b * g.P + p;
+  const int r = idx / g.W - g.pad_h, c = idx - (idx / g.W) * g.W - g.pad_w;
+  if (r < 0 || r >= g.roi_h || c < 0 || c >= g.roi_w) return;   // border ports: ring kernel
+  const size_t o = (size_t)b * g.P + r * g.roi_w + c;
   float d;
   act_fwd_deriv(g.fact, uroi[o], g.fslope, &d);
   guroi[o] += gout[i] * d;
+}
+
+// Outputs on the VALID ring: their gradient summed over the batch joins the ring
+// gradient (runs after universe_bwd_ring_kernel; output cells are distinct).
+__global__ void universe_bwd_border_ports_kernel(Geo g, StepParams sp, const float* __restrict__ cell,
+                                                 const int32_t* __restrict__ out_index,
+                                                 const float* __restrict__ gout,
+                                                 float* __restrict__ gring, int B) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= g.n_out) return;
+  const int k = out_index[j];
+  const int r = k / g.W - g.pad_h, c = k - (k / g.W) * g.W - g.pad_w;
+  if (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) return;
+  float s = 0.f;
+  for (int b = 0; b < B; ++b) s += gout[(size_t)b * g.n_out + j];
+  const float pre = act_fwd(g.fact, cell[g.H * g.W + k], g.fslope) * sp.sprob[k];
+  float d;
+  act_fwd_deriv(g.fact, pre, g.fslope, &d);
+  gring[k] += s * d;
 }
 
 // g_universe on the VALID ring, summed over the batch in sample order -> (H*W)

@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(NT, 1) bwd_kernel(BwdArgs a, FastBwdLayout L) 
 #pragma unroll 1
       for (int j = tid; j < g.n_out; j += NT) {
         const int p = out_pixel(g, a.out_index[j]);
+        if (p < 0) continue;                 // border outputs run in universe mode only
         float z[M], gzh[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) z[m] = ZH[(size_t)m * P + p];

@@ -84,9 +84,10 @@ inline __device__ void border_ring(const Geo& g, float* F, int fs, const float* 
   }
 }
 
+// ROI pixel of an output cell, -1 outside the ROI (border outputs: universe mode only).
 __device__ __forceinline__ int out_pixel(const Geo& g, int idx) {
-  const int r = idx / g.W, c = idx - (idx / g.W) * g.W;
-  return (r - g.pad_h) * g.roi_w + (c - g.pad_w);
+  const int r = idx / g.W - g.pad_h, c = idx - (idx / g.W) * g.W - g.pad_w;
+  return (r >= 0 && r < g.roi_h && c >= 0 && c < g.roi_w) ? r * g.roi_w + c : -1;
 }
 
 // ---------------------------------------------------------------------------------------

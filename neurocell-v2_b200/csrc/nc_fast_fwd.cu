@@ -53,7 +53,11 @@ __global__ void __launch_bounds__(FwdCfg<KH, KW, MT>::NTF, 1) fwd_kernel_mt(FwdA
   }
   for (int p = tid; p < P; p += NTF) pmap[p] = -1;
   inject(g, F, FS, FROWS, a.in_index, a.inputs + (size_t)b * g.n_in);
-  for (int j = tid; j < g.n_out; j += NTF) pmap[out_pixel(g, a.out_index[j])] = j;
+  for (int j = tid; j < g.n_out; j += NTF) {
+    const int p = out_pixel(g, a.out_index[j]);
+    if (p >= 0) pmap[p] = j;
+    else a.out[(size_t)b * g.n_out + j] = __int_as_float(0x7fc00000);   // border output: NaN
+  }
   if (g.padding == NC_PAD_CIRCULAR) wrap_ring(g, F, FS);
   __syncthreads();
 

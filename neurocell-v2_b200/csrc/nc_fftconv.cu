@@ -318,6 +318,10 @@ __global__ void port_out_kernel(Geo g, StepParams sp, const int32_t* __restrict_
   const int idx = out_index[j];
   const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
   const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+  if (gr_ < g.pad_h || gr_ >= g.pad_h + g.roi_h || gc_ < g.pad_w || gc_ >= g.pad_w + g.roi_w) {
+    out[i] = __int_as_float(0x7fc00000);   // border outputs run in universe mode only
+    return;
+  }
   const float wo = sp.weff[p], so = sp.seff[p], bo = sp.broi[p];
   const float* zb = z + (size_t)b * zs + p;
   float lin = 0.f, act = 0.f;
@@ -358,6 +362,7 @@ __global__ void port_gz_kernel(Geo g, StepParams sp, const int32_t* __restrict__
   const int idx = out_index[j];
   const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
   const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+  if (gr_ < g.pad_h || gr_ >= g.pad_h + g.roi_h || gc_ < g.pad_w || gc_ >= g.pad_w + g.roi_w) return;
   const size_t P = (size_t)g.P;
   const float wo = sp.weff[p], so = sp.seff[p], bo = sp.broi[p];
   float gp0 = 0.f, gp1 = 0.f, gp2 = 0.f;

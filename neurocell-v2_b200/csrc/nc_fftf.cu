@@ -271,6 +271,10 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
         const int idx = a.out_index[jo];
         const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
         const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+        if (gr_ < g.pad_h || gr_ >= g.pad_h + g.roi_h || gc_ < g.pad_w || gc_ >= g.pad_w + g.roi_w) {
+          a.out[(size_t)b * g.n_out + jo] = __int_as_float(0x7fc00000);   // universe mode only
+          continue;
+        }
         const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];
         a.out[(size_t)b * g.n_out + jo] = (g.fact == NC_ACT_NONE)
                                               ? (wo + so) * lin[p] + ((float)g.M * so * bo)
@@ -321,6 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
       const int idx = a.out_index[jo];
       const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
       const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+      if (gr_ < g.pad_h || gr_ >= g.pad_h + g.roi_h || gc_ < g.pad_w || gc_ >= g.pad_w + g.roi_w) continue;
       pmap[p] = (int16_t)jo;
       const float go = a.gout[(size_t)b * g.n_out + jo];
       const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];

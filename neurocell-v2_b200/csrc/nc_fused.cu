@@ -208,6 +208,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) vnn_fused_fwd_kernel(FwdArgs
         const int idx = a.out_index[j];
         const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
         const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+        if (gr_ < g.pad_h || gr_ >= g.pad_h + g.roi_h || gc_ < g.pad_w || gc_ >= g.pad_w + g.roi_w) {
+          a.out[(size_t)b * g.n_out + j] = __int_as_float(0x7fc00000);   // border output: NaN
+          continue;                                                      // (universe mode only)
+        }
         const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];
         float lin = 0.f, act = 0.f;
         for (int m = 0; m < g.M; ++m) {
@@ -370,6 +374,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) vnn_fused_bwd_kernel(BwdArgs
       const int idx = a.out_index[j];
       const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
       const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+      if (gr_ < g.pad_h || gr_ >= g.pad_h + g.roi_h || gc_ < g.pad_w || gc_ >= g.pad_w + g.roi_w) continue;
       const float go = a.gout[(size_t)b * g.n_out + j];
       const float wo = a.sp.weff[p], so = a.sp.seff[p], bo = a.sp.broi[p];
       float lin = 0.f;

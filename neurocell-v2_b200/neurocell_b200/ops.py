@@ -132,10 +132,6 @@ def get_plan(topology: ChipTopology2D, in_shapes: tuple, device: torch.device, a
     plan = _PLANS.get(key)
     if plan is not None:
         return plan
-    if not topology.out_in_roi:
-        raise NotImplementedError(
-            "output ports outside the active ROI (full-grid / border outputs, "
-            "propagator.py:684-734) are not built on the B200 path")
     lib = _lib.load()
     in_idx = _input_index(topology, in_shapes)
     out_idx, out_shape = _output_index(topology)

@@ -119,11 +119,13 @@ def propagate_vnn_2d(
         flat = flat.to(device, non_blocking=True)
     plan = ops.get_plan(topology, shapes, device, act, slope, fact, fslope, norm, hard_pin_io,
                         gated_filters, CONV_OF_BACKEND[backend])
-    if return_universe:
-        # (outputs, full-grid universe) as the reference returns them (propagator.py:730-733)
+    if return_universe or not topology.out_in_roi:
+        # (outputs, full-grid universe) as the reference returns them (propagator.py:730-733);
+        # output ports outside the ROI always take this full-grid path (propagator.py:684)
         out, uni = ops.propagate_universe(params.cell_params, params.greens_filters, flat, plan,
                                           codd_mode, state_temperature, active_threshold)
-        return out.reshape((out.shape[0],) + plan.out_shape), uni
+        out = out.reshape((out.shape[0],) + plan.out_shape)
+        return (out, uni) if return_universe else out
     out = ops.propagate(params.cell_params, params.greens_filters, flat, plan, codd_mode,
                         state_temperature, active_threshold)
     return out.reshape((out.shape[0],) + plan.out_shape)

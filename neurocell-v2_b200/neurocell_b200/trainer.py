@@ -187,6 +187,9 @@ class VNNTrainStep:
             raise ValueError(f"Unsupported exchange '{exchange}'; choose from ('nccl', 'nvlink').")
         dev = params.cell_params.device
         ops._require_cuda(params.cell_params, "params.cell_params")
+        if not topology.out_in_roi:
+            raise NotImplementedError("VNNTrainStep needs output ports inside the ROI; use "
+                                      "propagate_vnn_2d (full-grid path) with VNNTrainer")
         act, slope = ops.resolve_activation(activate)
         fact, fslope = ops.resolve_activation(final_activate)
         if in_shapes is None:

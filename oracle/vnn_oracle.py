@@ -463,6 +463,16 @@ def _out_index(geom):
     return rr.ravel(), cc.ravel()
 
 
+def _out_grid_index(geom):
+    """Output-port cells as (rows, cols) arrays in grid coordinates (any position)."""
+    op = geom.out_port
+    if isinstance(op, CoordPort):
+        return np.array([r for r, _ in op.coords]), np.array([c for _, c in op.coords])
+    (r0, c0), (oh, ow) = op.offset, op.size
+    rr, cc = np.meshgrid(np.arange(r0, r0 + oh), np.arange(c0, c0 + ow), indexing="ij")
+    return rr.ravel(), cc.ravel()
+
+
 def precompute(cell_params, geom, activate="tanh", act_slope=0.01, hard_pin_io=False,
                codd_mode="continuous", state_temperature=1.0, active_threshold=0.6):
     Wf, Bf, Sf = cell_params[0], cell_params[1], cell_params[2]
@@ -679,9 +689,8 @@ def forward_universe(cell_params, filters, inputs, geom: Geometry, cfg: Config =
     else:
         pre = roi_final
     uni = pre if fa is None else act_fwd(pre, fa, fs)
-    rr, cc = _out_index(geom)
-    r0, c0 = geom.pad_h, geom.pad_w
-    outputs = uni[:, rr + r0, cc + c0]
+    rr, cc = _out_grid_index(geom)
+    outputs = uni[:, rr, cc]
     oh, ow = geom.out_port.size
     tape["uni"] = dict(et=et, pre=pre)
     return outputs.reshape(B, oh, ow), uni, tape

@@ -370,8 +370,8 @@ def _universe_case(geom, cfg, backend, seed):
     L.backward()
     o_r, u_r, tape = O.forward_universe(cell, filt, ins, geom, cfg)
     gu = wu.copy()
-    rr, cc = O._out_index(geom)
-    gu[:, rr + geom.pad_h, cc + geom.pad_w] += wo.reshape(3, -1)
+    rr, cc = O._out_grid_index(geom)
+    gu[:, rr, cc] += wo.reshape(3, -1)
     gc_r, gf_r = O.backward_universe(gu, tape, geom, cfg)
     errs = dict(out=_rel(out.detach().cpu().numpy(), o_r), uni=_rel(uni.detach().cpu().numpy(), u_r),
                 g_cell=_rel(cp.grad.cpu().numpy(), gc_r), g_filters=_rel(fl.grad.cpu().numpy(), gf_r))
@@ -394,3 +394,35 @@ def test_return_universe_fused_fft_parity(mode, final):
     geom = O.make_geometry((40, 44), (9, 7), 6, 3, (O.RectPort((10, 8), (4, 1)),),
                            O.RectPort((12, 30), (4, 1)), padding_mode=mode)
     _universe_case(geom, O.Config(final_activate=final), "pallas_sram", 121)
+
+
+@pytest.mark.parametrize("backend", ["nchw_direct", "pallas_sram"])
+def test_full_grid_outputs_parity(backend):
+    """Output port covering the whole grid, ring cells included (the reference's full-grid
+    output path, propagator.py:684-734; Game-of-Life style chips)."""
+    geom = O.make_geometry((16, 16), (3, 3), 2, 2, (O.RectPort((0, 0), (16, 16)),),
+                           O.RectPort((0, 0), (16, 16)))
+    assert not geom.out_in_roi
+    cell, filt, ins, _ = random_problem(geom, 3, 131)
+    rng = np.random.default_rng(132)
+    wo = rng.normal(size=(3, 16, 16))
+    topo = _nc_topo(geom)
+    dev = torch.device("cuda:0")
+    cp = torch.tensor(cell, device=dev, requires_grad=True)
+    fl = torch.tensor(filt, device=dev, requires_grad=True)
+    xin = [torch.tensor(np.asarray(a), dtype=torch.float32, device=dev) for a in ins]
+    for final in (None, "sigmoid"):
+        cp.grad = None
+        fl.grad = None
+        cfg = O.Config(final_activate=final)
+        out = nc.propagate_vnn_2d(nc.VNNParams(cp, fl), xin, topo, final_activate=ACT[final],
+                                  backend=backend)
+        (out * torch.tensor(wo, device=dev, dtype=torch.float32)).sum().backward()
+        o_r, u_r, tape = O.forward_universe(cell, filt, ins, geom, cfg)
+        gu = np.zeros_like(u_r)
+        rr, cc = O._out_grid_index(geom)
+        gu[:, rr, cc] += wo.reshape(3, -1)
+        gc_r, gf_r = O.backward_universe(gu, tape, geom, cfg)
+        assert _rel(out.detach().cpu().numpy(), o_r) <= TOL
+        assert _rel(cp.grad.cpu().numpy(), gc_r) <= TOL
+        assert _rel(fl.grad.cpu().numpy(), gf_r) <= TOL
