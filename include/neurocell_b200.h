@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define NC_ABI_VERSION 2
+#define NC_ABI_VERSION 3
 
 typedef enum nc_status {
   NC_OK = 0,
@@ -118,10 +118,14 @@ size_t nc_plan_bytes(const nc_topo* topo);
  *                     full-grid output path) -- nc_vnn_forward writes NaN for them
  *   io_mask[H*W]      io_state_mask      (neurocell/topology.py:241-253), 0/1 bytes
  *   out_w_mask[H*W]   out_weight_mask    (neurocell/topology.py:245-253), 0/1 bytes
+ *   border_mask[H*W]  1 where the VALID border template border_2d applies, 0 where it is
+ *                     forced to zero; null = all ones.  Zeros mark the cells of an adaptive
+ *                     sub-ROI window that lie inside the full ROI (the reference zeroes the
+ *                     whole ROI of border_2d before cropping, propagator.py:354-366).
  */
 nc_status nc_plan_build(const nc_topo* topo, const int32_t* in_index, const int32_t* out_index,
-                        const uint8_t* io_mask, const uint8_t* out_w_mask, void* d_plan,
-                        size_t plan_bytes, void* stream);
+                        const uint8_t* io_mask, const uint8_t* out_w_mask,
+                        const uint8_t* border_mask, void* d_plan, size_t plan_bytes, void* stream);
 
 /* ---- forward / backward ---------------------------------------------------------------- */
 

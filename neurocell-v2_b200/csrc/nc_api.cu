@@ -22,7 +22,8 @@ namespace nc {
 __global__ void vnn_fused_fwd_kernel(FwdArgs a);
 __global__ void vnn_fused_bwd_kernel(BwdArgs a);
 __global__ void prestep_kernel(Geo g, StepParams sp, const float* cell, const float* filters,
-                               const uint8_t* io, const uint8_t* owm, nc_codd codd);
+                               const uint8_t* io, const uint8_t* owm, const uint8_t* bmask,
+                               nc_codd codd);
 __global__ void codd_kernel(int HW, const float* s_raw, const uint8_t* io, int hard_pin,
                             nc_codd codd, float* out);
 __global__ void batch_sum_kernel(const float* in, size_t stride, int n, int batch, float* out);
@@ -52,7 +53,8 @@ static nc_status batch_step_sum(const float* in, int batch, int d, int t0, size_
 }
 __global__ void border_grad_kernel(Geo g, const float* G, const float* gdelta, float* gborder);
 __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* cell, const float* filters,
-                                   const uint8_t* owm, const float* gsum, const float* gborder,
+                                   const uint8_t* owm, const uint8_t* bmask, const float* gsum,
+                                   const float* gborder,
                                    const float* gdsum, const float* gring_final, float* gcell,
                                    float* gfilt);
 __global__ void universe_fwd_kernel(Geo g, StepParams sp, const float* cell, const float* uroi,
@@ -172,6 +174,7 @@ struct Prepared {
   const int32_t* out_index;
   const uint8_t* io;
   const uint8_t* owm;
+  const uint8_t* bmask;
   const float2* tw_w;
   const float2* tw_h;
 };
@@ -195,6 +198,7 @@ static nc_status prepare(const nc_topo* topo, const void* plan, int32_t batch, u
   pr->out_index = at<int32_t>(plan, PL.out_index);
   pr->io = at<uint8_t>(plan, PL.io_mask);
   pr->owm = at<uint8_t>(plan, PL.out_w_mask);
+  pr->bmask = at<uint8_t>(plan, PL.border_mask);
   pr->tw_w = at<float2>(plan, PL.twid_w);
   pr->tw_h = at<float2>(plan, PL.twid_h);
   return NC_OK;
@@ -273,7 +277,8 @@ static nc_status launch_prestep(const Prepared& pr, const float* cell, const flo
   const int HW = pr.g.H * pr.g.W;
   const int nthreads = 256;
   const int nblocks = (HW + nthreads - 1) / nthreads;
-  prestep_kernel<<<nblocks, nthreads, 0, st>>>(pr.g, pr.sp, cell, filters, pr.io, pr.owm, *codd);
+  prestep_kernel<<<nblocks, nthreads, 0, st>>>(pr.g, pr.sp, cell, filters, pr.io, pr.owm, pr.bmask,
+                                               *codd);
   return launch_check("prestep_kernel launch");
 }
 
@@ -303,8 +308,8 @@ size_t nc_plan_bytes(const nc_topo* topo) {
 }
 
 nc_status nc_plan_build(const nc_topo* topo, const int32_t* in_index, const int32_t* out_index,
-                        const uint8_t* io_mask, const uint8_t* out_w_mask, void* d_plan,
-                        size_t plan_bytes, void* stream) {
+                        const uint8_t* io_mask, const uint8_t* out_w_mask,
+                        const uint8_t* border_mask, void* d_plan, size_t plan_bytes, void* stream) {
   Geo g;
   NC_CHECK(make_geo(topo, &g));
   const PlanLayout PL = plan_layout(topo);
@@ -350,6 +355,10 @@ nc_status nc_plan_build(const nc_topo* topo, const int32_t* in_index, const int3
                                 cudaMemcpyHostToDevice, st));
   NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.io_mask, io_mask, (size_t)HW, cudaMemcpyHostToDevice, st));
   NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.out_w_mask, out_w_mask, (size_t)HW, cudaMemcpyHostToDevice, st));
+  if (border_mask)
+    NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.border_mask, border_mask, (size_t)HW, cudaMemcpyHostToDevice, st));
+  else
+    NC_CUDA_CHECK(cudaMemsetAsync(base + PL.border_mask, 1, (size_t)HW, st));
   if (PL.twid_w != SIZE_MAX) {
     NC_CUDA_CHECK(cudaMemcpyAsync(base + PL.twid_w, tw[0].data(), sizeof(float2) * tw[0].size(),
                                   cudaMemcpyHostToDevice, st));
@@ -540,7 +549,7 @@ static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const flo
       seg_batch_sum2_kernel<<<(j.total + 255) / 256, 256, 0, st>>>(j, chunks, part);
       NC_CHECK(launch_check("seg_batch_sum2_kernel launch"));
     }
-    prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, gsum,
+    prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, pr.bmask, gsum,
                                                          gborder, gdsum, gringf, g_cell_params, g_filters);
     NC_CHECK(launch_check("prestep_bwd_kernel launch"));
     clear_error();
@@ -554,7 +563,7 @@ static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const flo
     NC_CHECK(fft_backward(c, st));
     if (g_prof.be) NC_CUDA_CHECK(cudaEventRecord(g_prof.be, st));
     const int HW = g.H * g.W;
-    prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, c.gsum,
+    prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, pr.bmask, c.gsum,
                                                          c.gborder, c.gdsum, gringf, g_cell_params, g_filters);
     NC_CHECK(launch_check("prestep_bwd_kernel launch"));
     clear_error();
@@ -631,7 +640,7 @@ static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const flo
     border_grad_kernel<<<(HW + 7) / 8, 256, 0, st>>>(g, pr.sp.geff, gdeltasum, gborder);
     NC_CHECK(launch_check("border_grad_kernel launch"));
   }
-  prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, gsum,
+  prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, pr.bmask, gsum,
                                                        gborder, gdsum, gringf, g_cell_params, g_filters);
   NC_CHECK(launch_check("prestep_bwd_kernel launch"));
   clear_error();

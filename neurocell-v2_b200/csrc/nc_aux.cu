@@ -10,7 +10,8 @@ namespace nc {
 // grid cell; the filter gate (propagator.py:262-264) rides along on a grid-stride loop.
 __global__ void prestep_kernel(Geo g, StepParams sp, const float* __restrict__ cell,
                                const float* __restrict__ filters, const uint8_t* __restrict__ io,
-                               const uint8_t* __restrict__ owm, nc_codd codd) {
+                               const uint8_t* __restrict__ owm, const uint8_t* __restrict__ bmask,
+                               nc_codd codd) {
   const int HW = g.H * g.W;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < HW) {
@@ -22,7 +23,7 @@ __global__ void prestep_kernel(Geo g, StepParams sp, const float* __restrict__ c
     sp.sprob[i] = s;
     sp.dsprob[i] = ds;
     sp.wpinned[i] = wp;
-    sp.border[i] = act_fwd(g.act, Bv, g.slope) * s;
+    sp.border[i] = bmask[i] ? act_fwd(g.act, Bv, g.slope) * s : 0.0f;
     const int r = i / g.W, c = i - (i / g.W) * g.W;
     const int rr = r - g.pad_h, cc = c - g.pad_w;
     if (rr >= 0 && rr < g.roi_h && cc >= 0 && cc < g.roi_w) {
@@ -160,6 +161,7 @@ __global__ void border_grad_kernel(Geo g, const float* __restrict__ G,
 // and gate the filter gradient.  gsum = [g w_eff | g s_eff | g b_roi] summed over batch.
 __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* __restrict__ cell,
                                    const float* __restrict__ filters, const uint8_t* __restrict__ owm,
+                                   const uint8_t* __restrict__ bmask,
                                    const float* __restrict__ gsum, const float* __restrict__ gborder,
                                    const float* __restrict__ gdsum, const float* __restrict__ gring_final,
                                    float* __restrict__ gcell, float* __restrict__ gfilt) {
@@ -178,7 +180,7 @@ __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* __restrict
       g_s = -gwe * inv_m * wp + gse * inv_m;
       g_b = gbr;
     }
-    if (gborder) {
+    if (gborder && bmask[i]) {
       const float gb = gborder[i];
       float da;
       const float av = act_fwd_deriv(g.act, Bv, g.slope, &da);

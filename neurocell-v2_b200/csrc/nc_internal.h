@@ -39,7 +39,7 @@ nc_status make_geo(const nc_topo* t, Geo* g);
 
 // Offsets (bytes) of the plan buffer sections.
 struct PlanLayout {
-  size_t in_index, out_index, io_mask, out_w_mask;
+  size_t in_index, out_index, io_mask, out_w_mask, border_mask;
   size_t twid_w, twid_h;   // FFT stage twiddles for the Nw and Nh transforms (FFT only)
   size_t total;
 };

@@ -86,6 +86,7 @@ PlanLayout plan_layout(const nc_topo* t) {
   L.out_index = o; o = align256(o + sizeof(int32_t) * (size_t)t->n_out);
   L.io_mask = o; o = align256(o + (size_t)t->H * t->W);
   L.out_w_mask = o; o = align256(o + (size_t)t->H * t->W);
+  L.border_mask = o; o = align256(o + (size_t)t->H * t->W);
   Geo g;
   if (make_geo(t, &g) == NC_OK && g.algo == NC_CONV_FFT) {
     L.twid_w = o; o = align256(o + 8 * (size_t)g.Nw);

@@ -12,6 +12,7 @@ from .params import (
 )
 from .propagator import SUPPORTED_BACKENDS, select_optimal_backend, propagate_vnn_2d
 from .model import VonNeumannNetwork
+from .adaptive_mask import AdaptiveMaskSpec, compute_adaptive_spatial_mask, estimate_effective_filter_radii
 from .trainer import VNNTrainer, compute_annealed_temperature, default_mse_loss
 from . import ops
 from ._lib import load as load_library, LIB_PATH
@@ -22,5 +23,6 @@ __all__ = [
     "compute_codd_state_probs", "init_vnn_params", "export_legacy_haiku_params",
     "import_legacy_haiku_params", "SUPPORTED_BACKENDS", "select_optimal_backend",
     "propagate_vnn_2d", "VonNeumannNetwork", "VNNTrainer", "compute_annealed_temperature",
-    "default_mse_loss", "ops", "load_library", "LIB_PATH",
+    "default_mse_loss", "ops", "load_library", "LIB_PATH", "AdaptiveMaskSpec",
+    "compute_adaptive_spatial_mask", "estimate_effective_filter_radii",
 ]

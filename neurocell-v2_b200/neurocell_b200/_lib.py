@@ -12,7 +12,7 @@ import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libneurocell_b200.so")
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 NC_OK, NC_ERR_INVALID, NC_ERR_WORKSPACE, NC_ERR_UNSUPPORTED, NC_ERR_CUDA = 0, 1, 2, 3, 4
 NC_PAD = {"VALID": 0, "SAME": 1, "CIRCULAR": 2}
@@ -61,7 +61,7 @@ _CP = ctypes.POINTER(NcCodd)
 
 _SIGS = {
     "nc_plan_bytes": (_sz, [_TP]),
-    "nc_plan_build": (_i32, [_TP, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "nc_plan_build": (_i32, [_TP, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "nc_workspace_bytes": (_sz, [_TP, _i32, _u32]),
     "nc_vnn_forward": (_i32, [_TP, _vp, _vp, _vp, _vp, _i32, _CP, _u32, _vp, _vp, _sz, _vp]),
     "nc_vnn_backward": (_i32, [_TP, _vp, _vp, _vp, _vp, _i32, _CP, _vp, _vp, _vp, _vp, _sz, _vp]),

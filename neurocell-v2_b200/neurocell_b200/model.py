@@ -41,6 +41,14 @@ class VonNeumannNetwork:
                                clear_outside_io=clear_outside_io, legacy_compat=legacy_compat,
                                device=device)
 
+    def compute_spatial_mask(self, params: VNNParams, margin=4, bucket_multiple: int = 8,
+                             prev_mask=None, **kwargs):
+        """The pre-epoch adaptive sub-ROI (model.py:84-103 -> adaptive_mask.py:318-481)."""
+        from .adaptive_mask import compute_adaptive_spatial_mask
+        return compute_adaptive_spatial_mask(params=params, topology=self.topology, margin=margin,
+                                             bucket_multiple=bucket_multiple, prev_mask=prev_mask,
+                                             **kwargs)
+
     def apply(self, params: VNNParams, inputs, return_universe: bool = False, spatial_mask=None,
               codd_mode: str | None = None, state_temperature=None, active_threshold=None):
         return propagate_vnn_2d(

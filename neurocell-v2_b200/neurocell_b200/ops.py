@@ -65,6 +65,7 @@ class Plan:
     n_in: int
     n_out: int
     out_shape: tuple
+    window: tuple | None = None    # adaptive sub-ROI: grid slice (r0, r1, c0, c1) of the plan
 
 
 _PLANS: dict = {}
@@ -121,22 +122,64 @@ def _output_index(topology: ChipTopology2D) -> tuple[np.ndarray, tuple]:
     return (rr * W + cc).ravel().astype(np.int32), (oh, ow)
 
 
+def _window_tables(topology: ChipTopology2D, roi_bbox, in_idx, out_idx):
+    """Adaptive sub-ROI (propagator.py:228-241, 343-371) as its own VALID / SAME problem: the
+    grid window that holds the sub-ROI and its kernel halo.  Returns the window slice, its
+    shape, the remapped port tables (inputs outside the window dropped), the cropped masks
+    and the border mask (the full ROI is dead in the reference's border template)."""
+    H, W = topology.grid_shape
+    ph, pw = topology.pad_h, topology.pad_w
+    r0, r1, c0, c1 = roi_bbox
+    gr0, gr1, gc0, gc1 = r0, r1 + 2 * ph, c0, c1 + 2 * pw       # grid rows / cols of the window
+    wh, ww = gr1 - gr0, gc1 - gc0
+
+    def remap(idx, required):
+        r, c = idx // W - gr0, idx % W - gc0
+        inside = (idx >= 0) & (r >= 0) & (r < wh) & (c >= 0) & (c < ww)
+        if required and not inside.all():
+            raise NotImplementedError("output ports outside the adaptive sub-ROI")
+        return np.where(inside, r * ww + c, -1).astype(np.int32)
+
+    io = np.asarray(topology.io_state_mask, np.uint8)[gr0:gr1, gc0:gc1]
+    ow = np.asarray(topology.out_weight_mask, np.uint8)[gr0:gr1, gc0:gc1]
+    bmask = np.ones((H, W), np.uint8)
+    if topology.padding_mode == "VALID":
+        bmask[ph:H - ph, pw:W - pw] = 0
+    out_w = remap(out_idx, True)
+    orr, occ = out_w // ww - ph, out_w % ww - pw
+    if ((orr < 0) | (orr >= r1 - r0) | (occ < 0) | (occ >= c1 - c0)).any():
+        raise NotImplementedError("output ports outside the adaptive sub-ROI")
+    return ((gr0, gr1, gc0, gc1), (wh, ww), remap(in_idx, False), out_w, np.ascontiguousarray(io),
+            np.ascontiguousarray(ow), np.ascontiguousarray(bmask[gr0:gr1, gc0:gc1]))
+
+
 def get_plan(topology: ChipTopology2D, in_shapes: tuple, device: torch.device, act: str,
              act_slope: float, final_act: str, final_act_slope: float, norm: bool,
-             hard_pin_io: bool, gated_filters: bool, conv: str = "auto") -> Plan:
-    """``conv``: Green's convolution algorithm, "auto" | "direct" | "fft" (nc_conv_algo)."""
+             hard_pin_io: bool, gated_filters: bool, conv: str = "auto", roi_bbox=None) -> Plan:
+    """``conv``: Green's convolution algorithm, "auto" | "direct" | "fft" (nc_conv_algo).
+    ``roi_bbox``: adaptive sub-ROI (r0, r1, c0, c1) in ROI coordinates, or None."""
     if conv not in _lib.NC_CONV:
         raise ValueError(f"Unsupported conv algorithm '{conv}'; choose from {tuple(_lib.NC_CONV)}.")
     key = (topology.key(), in_shapes, str(device), act, act_slope, final_act, final_act_slope,
-           bool(norm), bool(hard_pin_io), bool(gated_filters), conv)
+           bool(norm), bool(hard_pin_io), bool(gated_filters), conv,
+           None if roi_bbox is None else tuple(int(v) for v in roi_bbox))
     plan = _PLANS.get(key)
     if plan is not None:
         return plan
     lib = _lib.load()
     in_idx = _input_index(topology, in_shapes)
     out_idx, out_shape = _output_index(topology)
+    io = np.ascontiguousarray(topology.io_state_mask, dtype=np.uint8)
+    ow = np.ascontiguousarray(topology.out_weight_mask, dtype=np.uint8)
+    bmask, window = None, None
+    grid = topology.grid_shape
+    if roi_bbox is not None:
+        if topology.padding_mode == "CIRCULAR":
+            raise NotImplementedError("adaptive sub-ROIs are not defined for CIRCULAR chips")
+        window, grid, in_idx, out_idx, io, ow, bmask = _window_tables(topology, roi_bbox, in_idx,
+                                                                      out_idx)
     t = _lib.NcTopo()
-    t.H, t.W = topology.grid_shape
+    t.H, t.W = grid
     t.kh, t.kw = topology.kernel_size
     t.M, t.depth = topology.directions, topology.depth
     t.padding = _lib.NC_PAD[topology.padding_mode]
@@ -152,14 +195,13 @@ def get_plan(topology: ChipTopology2D, in_shapes: tuple, device: torch.device, a
             raise NotImplementedError(f"neurocell_b200: {msg}")
         raise ValueError(f"neurocell_b200: invalid topology for the B200 path ({msg})")
     buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
-    io = np.ascontiguousarray(topology.io_state_mask, dtype=np.uint8)
-    ow = np.ascontiguousarray(topology.out_weight_mask, dtype=np.uint8)
     in_c = np.ascontiguousarray(in_idx) if in_idx.size else np.zeros(1, np.int32)
     with torch.cuda.device(device):
         _lib.check(lib.nc_plan_build(ctypes.byref(t), in_c.ctypes.data, out_idx.ctypes.data,
-                                     io.ctypes.data, ow.ctypes.data, _ptr(buf), nbytes,
-                                     _stream(device)), "nc_plan_build")
-    plan = Plan(topology, t, buf, int(in_idx.size), int(out_idx.size), tuple(out_shape))
+                                     io.ctypes.data, ow.ctypes.data,
+                                     None if bmask is None else bmask.ctypes.data, _ptr(buf),
+                                     nbytes, _stream(device)), "nc_plan_build")
+    plan = Plan(topology, t, buf, int(in_idx.size), int(out_idx.size), tuple(out_shape), window)
     _PLANS[key] = plan
     return plan
 
@@ -297,7 +339,8 @@ def codd_states(s_raw: torch.Tensor, io_state_mask, hard_pin_io, codd_mode, tau,
     zero = np.zeros(1, dtype=np.int32)
     noio = np.zeros((H, W), dtype=np.uint8)
     _lib.check(lib.nc_plan_build(ctypes.byref(t), zero.ctypes.data, zero.ctypes.data, io.ctypes.data,
-                                 noio.ctypes.data, _ptr(buf), nbytes, _stream(dev)), "nc_plan_build")
+                                 noio.ctypes.data, None, _ptr(buf), nbytes, _stream(dev)),
+               "nc_plan_build")
     out = torch.empty((H, W), dtype=torch.float32, device=dev)
     src = s_raw.contiguous().float()
     c = _codd(codd_mode, tau, thr)

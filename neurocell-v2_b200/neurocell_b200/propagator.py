@@ -109,8 +109,13 @@ def propagate_vnn_2d(
     fact, fslope = ops.resolve_activation(final_activate)
     if sharpen_filter is not None:
         raise NotImplementedError("sharpen_filter (filters.py) is not part of the B200 hot path")
-    if spatial_mask is not None and not getattr(spatial_mask, "is_full_roi", False):
-        raise NotImplementedError("adaptive sub-ROI masks are not built on the B200 path")
+    roi_bbox = None
+    if (spatial_mask is not None and not spatial_mask.is_full_roi
+            and topology.padding_mode != "CIRCULAR"):
+        # adaptive sub-ROI (propagator.py:235-241): the kernels run on the sub-ROI's window
+        roi_bbox = tuple(int(v) for v in spatial_mask.roi_bbox)
+        if return_universe or not topology.out_in_roi:
+            raise NotImplementedError("the full-grid universe of an adaptive sub-ROI is not built")
     ops._require_cuda(params.cell_params, "params.cell_params")
     ops._require_cuda(params.greens_filters, "params.greens_filters")
     flat, shapes = flatten_inputs(inputs, topology)
@@ -118,7 +123,12 @@ def propagate_vnn_2d(
     if flat.device != device:
         flat = flat.to(device, non_blocking=True)
     plan = ops.get_plan(topology, shapes, device, act, slope, fact, fslope, norm, hard_pin_io,
-                        gated_filters, CONV_OF_BACKEND[backend])
+                        gated_filters, CONV_OF_BACKEND[backend], roi_bbox)
+    if plan.window is not None:
+        r0, r1, c0, c1 = plan.window
+        out = ops.propagate(params.cell_params[:, r0:r1, c0:c1], params.greens_filters, flat, plan,
+                            codd_mode, state_temperature, active_threshold)
+        return out.reshape((out.shape[0],) + plan.out_shape)
     if return_universe or not topology.out_in_roi:
         # (outputs, full-grid universe) as the reference returns them (propagator.py:730-733);
         # output ports outside the ROI always take this full-grid path (propagator.py:684)

@@ -69,8 +69,21 @@ class TorchVNN:
             s = torch.where(self.io, torch.ones_like(s), s)
         return s
 
-    def forward(self, cell, filt, cells_t0_full):
-        """``cells_t0_full``: (B, H, W) injected field (inputs already placed)."""
+    def _inputs_fit(self, lo_r, hi_r, lo_c, hi_c):
+        for p in self.g.in_ports:
+            cells = (p.coords if isinstance(p, O.CoordPort) else
+                     [(p.offset[0] + i, p.offset[1] + j) for i in range(p.size[0]) for j in range(p.size[1])])
+            if not all(lo_r <= r < hi_r and lo_c <= c < hi_c for r, c in cells):
+                return False
+        return True
+
+    def forward(self, cell, filt, cells_t0_full, roi_bbox=None):
+        """``cells_t0_full``: (B, H, W) injected field (inputs already placed).
+        ``roi_bbox``: adaptive sub-ROI (r0, r1, c0, c1) in ROI coordinates (propagator.py:
+        228-241, 343-371, 394-397, 657-660): step parameters sliced to it, t=0 inputs injected
+        into it when they fit (else the full-grid VALID conv cropped to it), SAME convolution
+        of the sub-ROI cells, the border hoist over the window of the border template whose
+        whole ROI is zeroed, the output port epilogue on the cropped planes."""
         g, c = self.g, self.cfg
         H, W = g.grid_shape
         kh, kw = g.kernel_size
@@ -84,15 +97,20 @@ class TorchVNN:
         w_eff = w_pinned[roi] * (1.0 - s[roi]) / M
         s_eff = s[roi] / M
         b_roi = Bf[roi]
+        roi_h, roi_w = g.roi_shape
+        br0, br1, bc0, bc1 = roi_bbox if roi_bbox is not None else (0, roi_h, 0, roi_w)
+        sub = (slice(br0, br1), slice(bc0, bc1))
+        w_eff, s_eff, b_roi = w_eff[sub], s_eff[sub], b_roi[sub]
         circ = g.padding_mode == "CIRCULAR"
         valid = g.padding_mode == "VALID"
         if valid:
             border = _act(Bf, c.activate, c.act_slope) * s
             mask = torch.ones_like(border)
             mask[roi] = 0.0
-            delta = F.conv2d((border * mask)[None, None], G)
-        fits = g.in_in_roi and not circ
-        x = cells_t0_full[:, roi[0], roi[1]] if fits else cells_t0_full
+            bo = (border * mask)[br0:br1 + kh - 1, bc0:bc1 + kw - 1]
+            delta = F.conv2d(bo[None, None], G)
+        fits = g.in_in_roi and not circ and self._inputs_fit(ph + br0, ph + br1, pw + bc0, pw + bc1)
+        x = (cells_t0_full[:, ph + br0:ph + br1, pw + bc0:pw + bc1] if fits else cells_t0_full)
         cp = ((kh - 1) // 2, (kw - 1) // 2)
 
         def conv(t, x):
@@ -100,7 +118,7 @@ class TorchVNN:
                 xp = F.pad(x[:, None], (cp[1], cp[1], cp[0], cp[0]), mode="circular")
                 return F.conv2d(xp, G)
             if t == 0 and not fits:
-                z = F.conv2d(x[:, None], G)
+                z = F.conv2d(x[:, None], G)[:, :, br0:br1, bc0:bc1]
             else:
                 z = F.conv2d(x[:, None], G, padding=cp)
             if valid and t > 0:
@@ -123,9 +141,10 @@ class TorchVNN:
                 act = _act(zh + b_roi, c.activate, c.act_slope).sum(1)
             x = w_eff * lin + s_eff * act
         zh = std(conv(g.depth - 1, x))
-        zo = zh[:, :, self.rr, self.cc]
+        rr, cc = self.rr - br0, self.cc - bc0
+        zo = zh[:, :, rr, cc]
         lin = zo.sum(1)
-        w_o, s_o, b_o = w_eff[self.rr, self.cc], s_eff[self.rr, self.cc], b_roi[self.rr, self.cc]
+        w_o, s_o, b_o = w_eff[rr, cc], s_eff[rr, cc], b_roi[rr, cc]
         if c.final_activate is None:
             out = (w_o + s_o) * lin + M * s_o * b_o
         else:
@@ -135,13 +154,14 @@ class TorchVNN:
         return out.reshape(-1, oh, ow)
 
 
-def value_and_grad(geom, cfg, cell_params, filters, inputs, targets, loss="mse", dtype=torch.float64):
+def value_and_grad(geom, cfg, cell_params, filters, inputs, targets, loss="mse", dtype=torch.float64,
+                   roi_bbox=None):
     """Returns ``(loss, out, g_cell, g_filters)`` as numpy arrays (autograd)."""
     tv = TorchVNN(geom, cfg, dtype)
     cell = torch.tensor(np.asarray(cell_params), dtype=dtype, requires_grad=True)
     filt = torch.tensor(np.asarray(filters)[:, :1], dtype=dtype, requires_grad=True)
     x0 = torch.from_numpy(O.inject_full(inputs, geom, np.float64)).to(dtype)
-    out = tv.forward(cell, filt, x0)
+    out = tv.forward(cell, filt, x0, roi_bbox)
     o = out.reshape(out.shape[0], -1)
     if loss == "mse":
         y = torch.as_tensor(np.asarray(targets), dtype=dtype).reshape(o.shape)

@@ -426,3 +426,62 @@ def test_full_grid_outputs_parity(backend):
         assert _rel(out.detach().cpu().numpy(), o_r) <= TOL
         assert _rel(cp.grad.cpu().numpy(), gc_r) <= TOL
         assert _rel(fl.grad.cpu().numpy(), gf_r) <= TOL
+
+
+# ---- adaptive sub-ROI masks (adaptive_mask.py; propagator.py:228-241, 343-371) ----------
+def _mask(geom, bbox):
+    from neurocell_b200.adaptive_mask import AdaptiveMaskSpec
+    r0, r1, c0, c1 = bbox
+    return AdaptiveMaskSpec(bbox, (r0 + geom.pad_h, r1 + geom.pad_h, c0 + geom.pad_w, c1 + geom.pad_w),
+                            (r1 - r0, c1 - c0), None, None, None, (1, 1), 0.5, 0, False, None, (0, 0))
+
+
+def _sub_roi_case(geom, cfg, cell, filt, inputs, targets, bbox, backend):
+    from oracle import torch_port as T
+    topo = _nc_topo(geom)
+    dev = torch.device("cuda:0")
+    cp = torch.tensor(cell, dtype=torch.float32, device=dev, requires_grad=True)
+    fl = torch.tensor(filt, dtype=torch.float32, device=dev, requires_grad=True)
+    if isinstance(inputs, (list, tuple)):
+        xin = [torch.tensor(np.asarray(a), dtype=torch.float32, device=dev) for a in inputs]
+    else:
+        xin = torch.tensor(inputs, dtype=torch.float32, device=dev)
+    out = nc.propagate_vnn_2d(nc.VNNParams(cp, fl), xin, topo, activate=ACT[cfg.activate],
+                              final_activate=ACT[cfg.final_activate], codd_mode=cfg.codd_mode,
+                              state_temperature=cfg.state_temperature,
+                              active_threshold=cfg.active_threshold,
+                              spatial_mask=_mask(geom, bbox), backend=backend)
+    L = nc.ops.mse_loss(out, torch.tensor(np.asarray(targets), device=dev).float())
+    L.backward()
+    l_r, o_r, gc_r, gf_r = T.value_and_grad(geom, cfg, cell, filt, inputs, targets, roi_bbox=bbox)
+    errs = dict(out=_rel(out.detach().cpu().numpy(), o_r), loss=abs(float(L.detach()) - l_r) / l_r,
+                g_cell=_rel(cp.grad.cpu().numpy(), gc_r), g_filters=_rel(fl.grad.cpu().numpy(), gf_r))
+    bad = {k: v for k, v in errs.items() if not v <= TOL}
+    assert not bad, f"sub-ROI parity failure {bad} (all: {errs})"
+
+
+@pytest.mark.parametrize("backend", ALU_BACKENDS)
+def test_adaptive_sub_roi_trained_alu_parity(backend):
+    params = nc.VonNeumannNetwork.load_checkpoint(os.path.join(GOLDEN, "alu_trained_cells.npz"))
+    topo = nc.ChipTopology2D.alu_chip()
+    spec = nc.compute_adaptive_spatial_mask(params, topo)
+    assert not spec.is_full_roi and spec.active_shape[1] < 50
+    geom = O.alu_geometry()
+    rng = np.random.default_rng(141)
+    x, y, _ = O.alu_batch(rng, 8, noise=0.0)
+    _sub_roi_case(geom, O.Config(codd_mode="ste_ternary", state_temperature=0.2),
+                  params.cell_params.cpu().numpy(), params.greens_filters.cpu().numpy(), x, y,
+                  spec.roi_bbox, backend)
+
+
+@pytest.mark.parametrize("backend", ["nchw_direct", "pallas_sram"])
+@pytest.mark.parametrize("mode", ["VALID", "SAME"])
+def test_adaptive_sub_roi_border_inputs_parity(backend, mode):
+    """Inputs on the dead ring (VALID) take the full-grid t=0 convolution cropped to the
+    sub-ROI; SAME crops the grid itself."""
+    ports = ((O.RectPort((0, 4), (6, 6)), O.CoordPort(((12, 12), (13, 9)))) if mode == "VALID"
+             else (O.CoordPort(((12, 12), (13, 9), (16, 14))),))
+    geom = O.make_geometry((28, 30), (7, 5), 4, 3, ports, O.CoordPort(((14, 16), (15, 16), (18, 12))),
+                           padding_mode=mode)
+    cell, filt, ins, y = random_problem(geom, 3, 151)
+    _sub_roi_case(geom, O.Config(), cell, filt, ins, y, (6, 20, 6, 22), backend)
