@@ -179,6 +179,35 @@ nc_status nc_vnn_backward_universe(const nc_topo* topo, const void* d_plan, cons
                                    size_t ws_bytes, void* stream);
 
 /*
+ * Full-grid universe of an adaptive sub-ROI call (neurocell/propagator.py:700-718 with
+ * roi_bbox, then 726-733).  The sub-ROI runs as its own plan over a grid window of the chip
+ * (nc_vnn_forward_universe on the window's cell parameters gives universe_window, shape
+ * (batch, win_h, win_w)); this call places it in the full grid.  topo / d_plan describe the
+ * FULL chip (VALID or SAME).  The window's top-left grid cell is (win_row, win_col).
+ * Writes universe (batch, H, W): the window copied in, every other cell f(f(B) * s_prob)
+ * on VALID chips (B * s_prob without a final activation) and f(0) on SAME chips.  When out
+ * is not null it also writes out (batch, n_out), gathered from universe at the full plan's
+ * output cells.
+ */
+nc_status nc_universe_embed_forward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                                    const nc_codd* codd, int32_t win_row, int32_t win_col,
+                                    int32_t win_h, int32_t win_w, const float* universe_window,
+                                    int32_t batch, float* universe, float* out, void* stream);
+
+/*
+ * Vector-Jacobian product of nc_universe_embed_forward.  Inputs: g_out (batch, n_out) and
+ * g_universe (batch, H, W); either may be null.  Writes g_universe_window
+ * (batch, win_h, win_w) and g_cell_params (3, H, W).  g_cell_params is the gradient of the
+ * cells outside the window.  Inside the window it is zero, because the window's parameters
+ * get their gradient from the sub-ROI call's own backward.
+ */
+nc_status nc_universe_embed_backward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                                     const nc_codd* codd, int32_t win_row, int32_t win_col,
+                                     int32_t win_h, int32_t win_w, const float* g_out,
+                                     const float* g_universe, int32_t batch, float* g_universe_window,
+                                     float* g_cell_params, void* stream);
+
+/*
  * nc_vnn_forward_static -- no counterpart in the reference.  Inference forward (flags 0)
  * that takes no workspace: its scratch is a static device array of
  * NC_STATIC_SCRATCH_BYTES inside this library, held on every GPU that loads the library

@@ -70,6 +70,14 @@ __global__ void universe_bwd_ports_kernel(Geo g, const int32_t* out_index, const
 __global__ void universe_bwd_border_ports_kernel(Geo g, StepParams sp, const float* cell,
                                                  const int32_t* out_index, const float* gout,
                                                  float* gring, int B);
+__global__ void universe_embed_fwd_kernel(Geo g, UniWindow wn, const float* cell, const uint8_t* io,
+                                          nc_codd codd, const float* uwin, float* universe, int B);
+__global__ void universe_embed_bwd_kernel(Geo g, UniWindow wn, const float* cell, const uint8_t* io,
+                                          nc_codd codd, const float* guni, float* guwin, float* gcell,
+                                          int B);
+__global__ void universe_embed_bwd_ports_kernel(Geo g, UniWindow wn, const int32_t* out_index,
+                                                const float* cell, const uint8_t* io, nc_codd codd,
+                                                const float* gout, float* guwin, float* gcell, int B);
 __global__ void mse_kernel(const float* o, const float* y, int n, float* loss, float* g);
 __global__ void softmax_ce_kernel(const float* x, const int32_t* lab, int batch, int n,
                                   float* loss, float* g);
@@ -663,6 +671,75 @@ nc_status nc_vnn_backward_universe(const nc_topo* topo, const void* d_plan, cons
   if (!g_universe) return set_error(NC_ERR_INVALID, "g_universe is null");
   return vnn_backward(topo, d_plan, cell_params, filters, inputs, batch, codd, g_out, g_universe,
                       g_cell_params, g_filters, d_ws, ws_bytes, stream);
+}
+
+// Arguments shared by both universe-embedding entry points.
+static nc_status check_embed(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                             const nc_codd* codd, int32_t win_row, int32_t win_col, int32_t win_h,
+                             int32_t win_w, int32_t batch, Geo* g, UniWindow* wn) {
+  NC_CHECK(make_geo(topo, g));
+  NC_CHECK(check_codd(codd));
+  if (!d_plan) return set_error(NC_ERR_INVALID, "plan buffer is null");
+  NC_CHECK(check_ptr(cell_params, "cell_params"));
+  if (batch <= 0) return set_error(NC_ERR_INVALID, "batch must be >= 1, got %d", batch);
+  if (g->padding == NC_PAD_CIRCULAR)
+    return set_error(NC_ERR_UNSUPPORTED, "adaptive sub-ROIs are not defined for CIRCULAR chips");
+  if (win_h <= 0 || win_w <= 0 || win_row < 0 || win_col < 0 || win_row + win_h > g->H ||
+      win_col + win_w > g->W)
+    return set_error(NC_ERR_INVALID, "window (%d, %d) + (%d, %d) outside the %dx%d grid", win_row,
+                     win_col, win_h, win_w, g->H, g->W);
+  *wn = UniWindow{win_row, win_col, win_h, win_w};
+  return NC_OK;
+}
+
+nc_status nc_universe_embed_forward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                                    const nc_codd* codd, int32_t win_row, int32_t win_col,
+                                    int32_t win_h, int32_t win_w, const float* universe_window,
+                                    int32_t batch, float* universe, float* out, void* stream) {
+  Geo g;
+  UniWindow wn;
+  NC_CHECK(check_embed(topo, d_plan, cell_params, codd, win_row, win_col, win_h, win_w, batch, &g, &wn));
+  NC_CHECK(check_ptr(universe_window, "universe_window"));
+  NC_CHECK(check_ptr(universe, "universe"));
+  const PlanLayout PL = plan_layout(topo);
+  cudaStream_t st = as_stream(stream);
+  const size_t n = (size_t)batch * g.H * g.W;
+  universe_embed_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+      g, wn, cell_params, at<uint8_t>(d_plan, PL.io_mask), *codd, universe_window, universe, batch);
+  NC_CHECK(launch_check("universe_embed_fwd_kernel launch"));
+  if (out) {
+    gather_out_kernel<<<(batch * g.n_out + 127) / 128, 128, 0, st>>>(
+        g, at<int32_t>(d_plan, PL.out_index), universe, out, batch);
+    NC_CHECK(launch_check("gather_out_kernel launch"));
+  }
+  clear_error();
+  return NC_OK;
+}
+
+nc_status nc_universe_embed_backward(const nc_topo* topo, const void* d_plan, const float* cell_params,
+                                     const nc_codd* codd, int32_t win_row, int32_t win_col,
+                                     int32_t win_h, int32_t win_w, const float* g_out,
+                                     const float* g_universe, int32_t batch, float* g_universe_window,
+                                     float* g_cell_params, void* stream) {
+  Geo g;
+  UniWindow wn;
+  NC_CHECK(check_embed(topo, d_plan, cell_params, codd, win_row, win_col, win_h, win_w, batch, &g, &wn));
+  NC_CHECK(check_ptr(g_universe_window, "g_universe_window"));
+  NC_CHECK(check_ptr(g_cell_params, "g_cell_params"));
+  const PlanLayout PL = plan_layout(topo);
+  const uint8_t* io = at<uint8_t>(d_plan, PL.io_mask);
+  cudaStream_t st = as_stream(stream);
+  universe_embed_bwd_kernel<<<(g.H * g.W + 255) / 256, 256, 0, st>>>(
+      g, wn, cell_params, io, *codd, g_universe, g_universe_window, g_cell_params, batch);
+  NC_CHECK(launch_check("universe_embed_bwd_kernel launch"));
+  if (g_out) {
+    universe_embed_bwd_ports_kernel<<<(g.n_out + 127) / 128, 128, 0, st>>>(
+        g, wn, at<int32_t>(d_plan, PL.out_index), cell_params, io, *codd, g_out, g_universe_window,
+        g_cell_params, batch);
+    NC_CHECK(launch_check("universe_embed_bwd_ports_kernel launch"));
+  }
+  clear_error();
+  return NC_OK;
 }
 
 nc_status nc_codd_states(const nc_topo* topo, const void* d_plan, const float* states_raw,

@@ -395,4 +395,103 @@ __global__ void universe_bwd_ring_kernel(Geo g, StepParams sp, const float* __re
   gring[k] = s * d;
 }
 
+
+// ---------------------------------------------------------------------------------------
+// full-grid universe of an adaptive sub-ROI (propagator.py:700-718, 730-733): the window
+// holds the sub-ROI call's own universe; every other cell is the final border template
+// f(f(B) * s_prob) on VALID chips and f(0) on SAME chips.  g is the FULL chip's geometry.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ bool in_window(const UniWindow& w, int r, int c) {
+  return r >= w.r0 && r < w.r0 + w.h && c >= w.c0 && c < w.c0 + w.w;
+}
+
+// Value of a cell outside the window before the final activation, with its partials
+// d pre / d B and d pre / d S_raw.
+__device__ __forceinline__ float fill_pre(const Geo& g, const float* cell, const uint8_t* io,
+                                          const nc_codd& codd, int k, float* dB, float* dS) {
+  *dB = 0.f;
+  *dS = 0.f;
+  if (g.padding != NC_PAD_VALID) return 0.f;
+  const int HW = g.H * g.W;
+  float ds, da;
+  const float s = codd_prob(cell[2 * HW + k], io[k] != 0, g.hard_pin, codd.mode, codd.temperature,
+                            codd.active_threshold, &ds);
+  const float fb = act_fwd_deriv(g.fact, cell[HW + k], g.fslope, &da);
+  *dB = da * s;
+  *dS = fb * ds;
+  return fb * s;
+}
+
+__global__ void universe_embed_fwd_kernel(Geo g, UniWindow wn, const float* __restrict__ cell,
+                                          const uint8_t* __restrict__ io, nc_codd codd,
+                                          const float* __restrict__ uwin, float* __restrict__ universe,
+                                          int B) {
+  const int HW = g.H * g.W;
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)B * HW) return;
+  const int b = (int)(i / HW), k = (int)(i - (size_t)b * HW);
+  const int r = k / g.W, c = k - (k / g.W) * g.W;
+  if (in_window(wn, r, c)) {
+    universe[i] = uwin[((size_t)b * wn.h + (r - wn.r0)) * wn.w + (c - wn.c0)];
+    return;
+  }
+  float dB, dS;
+  universe[i] = act_fwd(g.fact, fill_pre(g, cell, io, codd, k, &dB, &dS), g.fslope);
+}
+
+// One thread per grid cell: the window's slice of g_universe (batch order), and outside the
+// window the batch-summed fill gradient into (W, B, S_raw) = (0, gB, gS).
+__global__ void universe_embed_bwd_kernel(Geo g, UniWindow wn, const float* __restrict__ cell,
+                                          const uint8_t* __restrict__ io, nc_codd codd,
+                                          const float* __restrict__ guni, float* __restrict__ guwin,
+                                          float* __restrict__ gcell, int B) {
+  const int HW = g.H * g.W;
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= HW) return;
+  const int r = k / g.W, c = k - (k / g.W) * g.W;
+  gcell[k] = 0.f;
+  if (in_window(wn, r, c)) {
+    const size_t o = (size_t)(r - wn.r0) * wn.w + (c - wn.c0), wsz = (size_t)wn.h * wn.w;
+    for (int b = 0; b < B; ++b) guwin[b * wsz + o] = guni ? guni[(size_t)b * HW + k] : 0.f;
+    gcell[HW + k] = 0.f;
+    gcell[2 * HW + k] = 0.f;
+    return;
+  }
+  float gsum = 0.f;
+  if (guni)
+    for (int b = 0; b < B; ++b) gsum += guni[(size_t)b * HW + k];
+  float dB, dS, d;
+  const float pre = fill_pre(g, cell, io, codd, k, &dB, &dS);
+  act_fwd_deriv(g.fact, pre, g.fslope, &d);
+  gcell[HW + k] = gsum * d * dB;
+  gcell[2 * HW + k] = gsum * d * dS;
+}
+
+// The outputs' gradient at their cells (runs after universe_embed_bwd_kernel; output cells
+// are distinct, so every thread owns its cell).
+__global__ void universe_embed_bwd_ports_kernel(Geo g, UniWindow wn, const int32_t* __restrict__ out_index,
+                                                const float* __restrict__ cell,
+                                                const uint8_t* __restrict__ io, nc_codd codd,
+                                                const float* __restrict__ gout,
+                                                float* __restrict__ guwin, float* __restrict__ gcell,
+                                                int B) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= g.n_out) return;
+  const int HW = g.H * g.W;
+  const int k = out_index[j];
+  const int r = k / g.W, c = k - (k / g.W) * g.W;
+  if (in_window(wn, r, c)) {
+    const size_t o = (size_t)(r - wn.r0) * wn.w + (c - wn.c0), wsz = (size_t)wn.h * wn.w;
+    for (int b = 0; b < B; ++b) guwin[b * wsz + o] += gout[(size_t)b * g.n_out + j];
+    return;
+  }
+  float gsum = 0.f;
+  for (int b = 0; b < B; ++b) gsum += gout[(size_t)b * g.n_out + j];
+  float dB, dS, d;
+  const float pre = fill_pre(g, cell, io, codd, k, &dB, &dS);
+  act_fwd_deriv(g.fact, pre, g.fslope, &d);
+  gcell[HW + k] += gsum * d * dB;
+  gcell[2 * HW + k] += gsum * d * dS;
+}
+
 }  // namespace nc

@@ -64,4 +64,9 @@ struct SegSum {
   int nseg, total;
 };
 
+// Grid window of an adaptive sub-ROI call inside the full chip: top-left grid cell and size.
+struct UniWindow {
+  int r0, c0, h, w;
+};
+
 }  // namespace nc

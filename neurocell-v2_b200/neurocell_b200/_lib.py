@@ -29,7 +29,8 @@ EXPORTED = (
     "nc_fp32_peak_probe", "nc_vnn_forward_static", "nc_dp_shared_bytes", "nc_dp_state_bytes",
     "nc_dp_alloc", "nc_dp_free", "nc_ipc_get", "nc_ipc_open", "nc_ipc_close",
     "nc_dp_allreduce_sgd", "nc_dp_status", "nc_launch_count", "nc_conv_path",
-    "nc_vnn_forward_universe", "nc_vnn_backward_universe",
+    "nc_vnn_forward_universe", "nc_vnn_backward_universe", "nc_universe_embed_forward",
+    "nc_universe_embed_backward",
 )
 NC_DP_MAX_RANKS = 8
 NC_IPC_HANDLE_BYTES = 64
@@ -69,6 +70,10 @@ _SIGS = {
                                         _vp]),
     "nc_vnn_backward_universe": (_i32, [_TP, _vp, _vp, _vp, _vp, _i32, _CP, _vp, _vp, _vp, _vp, _vp,
                                          _sz, _vp]),
+    "nc_universe_embed_forward": (_i32, [_TP, _vp, _vp, _CP, _i32, _i32, _i32, _i32, _vp, _i32, _vp,
+                                          _vp, _vp]),
+    "nc_universe_embed_backward": (_i32, [_TP, _vp, _vp, _CP, _i32, _i32, _i32, _i32, _vp, _vp, _i32,
+                                           _vp, _vp, _vp]),
     "nc_codd_states": (_i32, [_TP, _vp, _vp, _CP, _vp, _vp]),
     "nc_mse_loss": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp]),
     "nc_softmax_ce_loss": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp]),

@@ -122,11 +122,15 @@ def _output_index(topology: ChipTopology2D) -> tuple[np.ndarray, tuple]:
     return (rr * W + cc).ravel().astype(np.int32), (oh, ow)
 
 
-def _window_tables(topology: ChipTopology2D, roi_bbox, in_idx, out_idx):
+def _window_tables(topology: ChipTopology2D, roi_bbox, in_idx, out_idx, universe=False):
     """Adaptive sub-ROI (propagator.py:228-241, 343-371) as its own VALID / SAME problem: the
     grid window that holds the sub-ROI and its kernel halo.  Returns the window slice, its
     shape, the remapped port tables (inputs outside the window dropped), the cropped masks
-    and the border mask (the full ROI is dead in the reference's border template)."""
+    and the border mask (the full ROI is dead in the reference's border template).
+
+    ``universe``: the window plan of the full-grid path, whose outputs are gathered from the
+    assembled full grid (nc_universe_embed_forward); its own output table is one placeholder
+    cell, the sub-ROI's first cell, so output ports may lie anywhere on the chip."""
     H, W = topology.grid_shape
     ph, pw = topology.pad_h, topology.pad_w
     r0, r1, c0, c1 = roi_bbox
@@ -145,6 +149,10 @@ def _window_tables(topology: ChipTopology2D, roi_bbox, in_idx, out_idx):
     bmask = np.ones((H, W), np.uint8)
     if topology.padding_mode == "VALID":
         bmask[ph:H - ph, pw:W - pw] = 0
+    if universe:
+        out_w = np.array([ph * ww + pw], np.int32)
+        return ((gr0, gr1, gc0, gc1), (wh, ww), remap(in_idx, False), out_w, np.ascontiguousarray(io),
+                np.ascontiguousarray(ow), np.ascontiguousarray(bmask[gr0:gr1, gc0:gc1]))
     out_w = remap(out_idx, True)
     orr, occ = out_w // ww - ph, out_w % ww - pw
     if ((orr < 0) | (orr >= r1 - r0) | (occ < 0) | (occ >= c1 - c0)).any():
@@ -155,14 +163,17 @@ def _window_tables(topology: ChipTopology2D, roi_bbox, in_idx, out_idx):
 
 def get_plan(topology: ChipTopology2D, in_shapes: tuple, device: torch.device, act: str,
              act_slope: float, final_act: str, final_act_slope: float, norm: bool,
-             hard_pin_io: bool, gated_filters: bool, conv: str = "auto", roi_bbox=None) -> Plan:
+             hard_pin_io: bool, gated_filters: bool, conv: str = "auto", roi_bbox=None,
+             universe: bool = False) -> Plan:
     """``conv``: Green's convolution algorithm, "auto" | "direct" | "fft" (nc_conv_algo).
-    ``roi_bbox``: adaptive sub-ROI (r0, r1, c0, c1) in ROI coordinates, or None."""
+    ``roi_bbox``: adaptive sub-ROI (r0, r1, c0, c1) in ROI coordinates, or None.
+    ``universe``: with ``roi_bbox``, the window plan of the full-grid universe path."""
     if conv not in _lib.NC_CONV:
         raise ValueError(f"Unsupported conv algorithm '{conv}'; choose from {tuple(_lib.NC_CONV)}.")
     key = (topology.key(), in_shapes, str(device), act, act_slope, final_act, final_act_slope,
            bool(norm), bool(hard_pin_io), bool(gated_filters), conv,
-           None if roi_bbox is None else tuple(int(v) for v in roi_bbox))
+           None if roi_bbox is None else tuple(int(v) for v in roi_bbox),
+           bool(universe) and roi_bbox is not None)
     plan = _PLANS.get(key)
     if plan is not None:
         return plan
@@ -177,7 +188,7 @@ def get_plan(topology: ChipTopology2D, in_shapes: tuple, device: torch.device, a
         if topology.padding_mode == "CIRCULAR":
             raise NotImplementedError("adaptive sub-ROIs are not defined for CIRCULAR chips")
         window, grid, in_idx, out_idx, io, ow, bmask = _window_tables(topology, roi_bbox, in_idx,
-                                                                      out_idx)
+                                                                      out_idx, universe)
     t = _lib.NcTopo()
     t.H, t.W = grid
     t.kh, t.kw = topology.kernel_size
@@ -263,7 +274,7 @@ class _VNNPropagateUniverse(torch.autograd.Function):
         lib = _lib.load()
         dev = cell_params.device
         B = flat_inputs.shape[0]
-        H, W = plan.topology.grid_shape
+        H, W = plan.topo.H, plan.topo.W          # a window plan's universe is its window
         flags = _lib.NC_FLAG_TRAIN if train else 0
         ws_bytes = lib.nc_workspace_bytes(ctypes.byref(plan.topo), B, flags)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
@@ -285,7 +296,7 @@ class _VNNPropagateUniverse(torch.autograd.Function):
         plan = ctx.plan
         dev = cell_params.device
         B = flat_inputs.shape[0]
-        H, W = plan.topology.grid_shape
+        H, W = plan.topo.H, plan.topo.W
         g_uni = (torch.zeros((B, H, W), dtype=torch.float32, device=dev) if g_uni is None
                  else g_uni.contiguous().float())
         g_out = None if g_out is None else g_out.contiguous().float()
@@ -310,6 +321,56 @@ def propagate_universe(cell_params: torch.Tensor, filters: torch.Tensor, flat_in
     xi = flat_inputs.contiguous().float()
     train = torch.is_grad_enabled() and (cp.requires_grad or fl.requires_grad)
     return _VNNPropagateUniverse.apply(cp, fl, xi, plan, _codd(codd_mode, tau, thr), train)
+
+
+class _UniverseEmbed(torch.autograd.Function):
+    """Full-grid universe of an adaptive sub-ROI call (propagator.py:700-718, 726-733)
+    through nc_universe_embed_forward / nc_universe_embed_backward."""
+
+    @staticmethod
+    def forward(ctx, cell_params, uni_window, full_plan: Plan, window, codd: _lib.NcCodd):
+        lib = _lib.load()
+        dev = cell_params.device
+        B = uni_window.shape[0]
+        H, W = full_plan.topology.grid_shape
+        r0, r1, c0, c1 = window
+        out = torch.empty((B, full_plan.n_out), dtype=torch.float32, device=dev)
+        uni = torch.empty((B, H, W), dtype=torch.float32, device=dev)
+        _lib.check(lib.nc_universe_embed_forward(ctypes.byref(full_plan.topo), _ptr(full_plan.buf),
+                                                 _ptr(cell_params), ctypes.byref(codd), r0, c0,
+                                                 r1 - r0, c1 - c0, _ptr(uni_window), B, _ptr(uni),
+                                                 _ptr(out), _stream(dev)), "nc_universe_embed_forward")
+        ctx.save_for_backward(cell_params)
+        ctx.plan, ctx.window, ctx.codd, ctx.B = full_plan, window, codd, B
+        return out, uni
+
+    @staticmethod
+    def backward(ctx, g_out, g_uni):
+        lib = _lib.load()
+        (cell_params,) = ctx.saved_tensors
+        plan, (r0, r1, c0, c1), B = ctx.plan, ctx.window, ctx.B
+        dev = cell_params.device
+        g_out = None if g_out is None else g_out.contiguous().float()
+        g_uni = None if g_uni is None else g_uni.contiguous().float()
+        g_win = torch.empty((B, r1 - r0, c1 - c0), dtype=torch.float32, device=dev)
+        g_cell = torch.empty_like(cell_params)
+        _lib.check(lib.nc_universe_embed_backward(ctypes.byref(plan.topo), _ptr(plan.buf),
+                                                  _ptr(cell_params), ctypes.byref(ctx.codd), r0, c0,
+                                                  r1 - r0, c1 - c0, _ptr(g_out), _ptr(g_uni), B,
+                                                  _ptr(g_win), _ptr(g_cell), _stream(dev)),
+                   "nc_universe_embed_backward")
+        return g_cell, g_win, None, None, None
+
+
+def embed_universe(cell_params: torch.Tensor, uni_window: torch.Tensor, full_plan: Plan, window,
+                   codd_mode: str, tau, thr):
+    """(B, win_h, win_w) window universe -> ((B, n_out), (B, H, W)) on the full chip;
+    differentiable in ``cell_params`` (cells outside the window) and ``uni_window``."""
+    _require_cuda(cell_params, "cell_params")
+    _require_cuda(uni_window, "uni_window")
+    return _UniverseEmbed.apply(cell_params.contiguous().float(), uni_window.contiguous().float(),
+                                full_plan, tuple(int(v) for v in window),
+                                _codd(codd_mode, tau, thr))
 
 
 def propagate(cell_params: torch.Tensor, filters: torch.Tensor, flat_inputs: torch.Tensor,

@@ -114,8 +114,7 @@ def propagate_vnn_2d(
             and topology.padding_mode != "CIRCULAR"):
         # adaptive sub-ROI (propagator.py:235-241): the kernels run on the sub-ROI's window
         roi_bbox = tuple(int(v) for v in spatial_mask.roi_bbox)
-        if return_universe or not topology.out_in_roi:
-            raise NotImplementedError("the full-grid universe of an adaptive sub-ROI is not built")
+    full_grid = return_universe or not topology.out_in_roi
     ops._require_cuda(params.cell_params, "params.cell_params")
     ops._require_cuda(params.greens_filters, "params.greens_filters")
     flat, shapes = flatten_inputs(inputs, topology)
@@ -123,13 +122,25 @@ def propagate_vnn_2d(
     if flat.device != device:
         flat = flat.to(device, non_blocking=True)
     plan = ops.get_plan(topology, shapes, device, act, slope, fact, fslope, norm, hard_pin_io,
-                        gated_filters, CONV_OF_BACKEND[backend], roi_bbox)
+                        gated_filters, CONV_OF_BACKEND[backend], roi_bbox, universe=full_grid)
     if plan.window is not None:
         r0, r1, c0, c1 = plan.window
-        out = ops.propagate(params.cell_params[:, r0:r1, c0:c1], params.greens_filters, flat, plan,
-                            codd_mode, state_temperature, active_threshold)
+        cell_w = params.cell_params[:, r0:r1, c0:c1]
+        if full_grid:
+            # the sub-ROI's window universe placed in the full grid, outputs read from it
+            # (propagator.py:700-718, 726-733)
+            _, uni_w = ops.propagate_universe(cell_w, params.greens_filters, flat, plan, codd_mode,
+                                              state_temperature, active_threshold)
+            full = ops.get_plan(topology, shapes, device, act, slope, fact, fslope, norm,
+                                hard_pin_io, gated_filters, CONV_OF_BACKEND[backend])
+            out, uni = ops.embed_universe(params.cell_params, uni_w, full, plan.window, codd_mode,
+                                          state_temperature, active_threshold)
+            out = out.reshape((out.shape[0],) + full.out_shape)
+            return (out, uni) if return_universe else out
+        out = ops.propagate(cell_w, params.greens_filters, flat, plan, codd_mode, state_temperature,
+                            active_threshold)
         return out.reshape((out.shape[0],) + plan.out_shape)
-    if return_universe or not topology.out_in_roi:
+    if full_grid:
         # (outputs, full-grid universe) as the reference returns them (propagator.py:730-733);
         # output ports outside the ROI always take this full-grid path (propagator.py:684)
         out, uni = ops.propagate_universe(params.cell_params, params.greens_filters, flat, plan,

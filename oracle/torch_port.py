@@ -77,13 +77,17 @@ class TorchVNN:
                 return False
         return True
 
-    def forward(self, cell, filt, cells_t0_full, roi_bbox=None):
+    def forward(self, cell, filt, cells_t0_full, roi_bbox=None, universe=False):
         """``cells_t0_full``: (B, H, W) injected field (inputs already placed).
         ``roi_bbox``: adaptive sub-ROI (r0, r1, c0, c1) in ROI coordinates (propagator.py:
         228-241, 343-371, 394-397, 657-660): step parameters sliced to it, t=0 inputs injected
         into it when they fit (else the full-grid VALID conv cropped to it), SAME convolution
         of the sub-ROI cells, the border hoist over the window of the border template whose
-        whole ROI is zeroed, the output port epilogue on the cropped planes."""
+        whole ROI is zeroed, the output port epilogue on the cropped planes.
+        ``universe``: returns ``(outputs, (B, H, W) universe)`` by the full-grid path
+        (propagator.py:684-733): the last step's ROI epilogue with the final activation, the
+        cells outside the (sub-)ROI f(B) * s_prob (VALID) or 0 (SAME), f over the grid, the
+        outputs read from it.  Not for CIRCULAR chips."""
         g, c = self.g, self.cfg
         H, W = g.grid_shape
         kh, kw = g.kernel_size
@@ -141,6 +145,20 @@ class TorchVNN:
                 act = _act(zh + b_roi, c.activate, c.act_slope).sum(1)
             x = w_eff * lin + s_eff * act
         zh = std(conv(g.depth - 1, x))
+        if universe:
+            if circ:
+                raise NotImplementedError("the torch port's universe path is for VALID / SAME chips")
+            fa, fsl = c.final_activate, c.final_act_slope
+            lin = zh.sum(1)
+            act = lin + M * b_roi if fa in (None, "identity") else _act(zh + b_roi, fa, fsl).sum(1)
+            roi_final = w_eff * lin + s_eff * act
+            fill = _act(Bf, fa, fsl) * s if valid else torch.zeros_like(Bf)
+            final = fill[None].expand(zh.shape[0], H, W).clone()
+            final[:, ph + br0:ph + br1, pw + bc0:pw + bc1] = roi_final
+            final = _act(final, fa, fsl)
+            gr, gc = O._out_grid_index(g)
+            oh, ow = g.out_port.size
+            return final[:, torch.as_tensor(gr), torch.as_tensor(gc)].reshape(-1, oh, ow), final
         rr, cc = self.rr - br0, self.cc - bc0
         zo = zh[:, :, rr, cc]
         lin = zo.sum(1)
@@ -171,3 +189,18 @@ def value_and_grad(geom, cfg, cell_params, filters, inputs, targets, loss="mse",
         L = F.cross_entropy(o, lab)
     L.backward()
     return float(L.detach()), out.detach().numpy(), cell.grad.numpy(), filt.grad.numpy()
+
+
+def universe_value_and_grad(geom, cfg, cell_params, filters, inputs, w_out, w_uni, roi_bbox=None,
+                            dtype=torch.float64):
+    """Full-grid path (``return_universe=True``) under the scalar loss
+    sum(out * w_out) + sum(universe * w_uni); returns ``(out, universe, g_cell, g_filters)``."""
+    tv = TorchVNN(geom, cfg, dtype)
+    cell = torch.tensor(np.asarray(cell_params), dtype=dtype, requires_grad=True)
+    filt = torch.tensor(np.asarray(filters)[:, :1], dtype=dtype, requires_grad=True)
+    x0 = torch.from_numpy(O.inject_full(inputs, geom, np.float64)).to(dtype)
+    out, uni = tv.forward(cell, filt, x0, roi_bbox, universe=True)
+    L = (out * torch.as_tensor(np.asarray(w_out), dtype=dtype).reshape(out.shape)).sum() + \
+        (uni * torch.as_tensor(np.asarray(w_uni), dtype=dtype)).sum()
+    L.backward()
+    return out.detach().numpy(), uni.detach().numpy(), cell.grad.numpy(), filt.grad.numpy()

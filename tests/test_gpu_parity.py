@@ -34,7 +34,8 @@ def _to_nc_port(p):
 def _nc_topo(g: O.Geometry):
     return nc.ChipTopology2D.create(g.grid_shape, g.kernel_size, g.directions, g.depth,
                                     tuple(_to_nc_port(p) for p in g.in_ports),
-                                    _to_nc_port(g.out_port), padding_mode=g.padding_mode)
+                                    _to_nc_port(g.out_port), padding_mode=g.padding_mode,
+                                    allow_border_output=not g.out_in_roi)
 
 
 def run_gpu(geom, cfg, cell, filt, inputs, targets, loss="mse", train=True, backend="b200"):
@@ -485,3 +486,62 @@ def test_adaptive_sub_roi_border_inputs_parity(backend, mode):
                            padding_mode=mode)
     cell, filt, ins, y = random_problem(geom, 3, 151)
     _sub_roi_case(geom, O.Config(), cell, filt, ins, y, (6, 20, 6, 22), backend)
+
+
+def _sub_roi_universe_case(geom, cfg, cell, filt, inputs, bbox, backend, seed):
+    """return_universe=True with an adaptive sub-ROI (propagator.py:700-718, 726-733)."""
+    from oracle import torch_port as T
+    rng = np.random.default_rng(seed)
+    B = (inputs[0] if isinstance(inputs, (list, tuple)) else inputs).shape[0]
+    H, W = geom.grid_shape
+    wo = rng.normal(size=(B,) + tuple(geom.out_port.size))
+    wu = rng.normal(size=(B, H, W))
+    topo = _nc_topo(geom)
+    dev = torch.device("cuda:0")
+    cp = torch.tensor(cell, dtype=torch.float32, device=dev, requires_grad=True)
+    fl = torch.tensor(filt, dtype=torch.float32, device=dev, requires_grad=True)
+    if isinstance(inputs, (list, tuple)):
+        xin = [torch.tensor(np.asarray(a), dtype=torch.float32, device=dev) for a in inputs]
+    else:
+        xin = torch.tensor(inputs, dtype=torch.float32, device=dev)
+    out, uni = nc.propagate_vnn_2d(nc.VNNParams(cp, fl), xin, topo, activate=ACT[cfg.activate],
+                                   final_activate=ACT[cfg.final_activate], codd_mode=cfg.codd_mode,
+                                   state_temperature=cfg.state_temperature,
+                                   active_threshold=cfg.active_threshold, return_universe=True,
+                                   spatial_mask=_mask(geom, bbox), backend=backend)
+    assert uni.shape == (B, H, W)
+    L = (out * torch.tensor(wo, device=dev, dtype=torch.float32)).sum() + \
+        (uni * torch.tensor(wu, device=dev, dtype=torch.float32)).sum()
+    L.backward()
+    o_r, u_r, gc_r, gf_r = T.universe_value_and_grad(geom, cfg, cell, filt, inputs, wo, wu, roi_bbox=bbox)
+    errs = dict(out=_rel(out.detach().cpu().numpy(), o_r), uni=_rel(uni.detach().cpu().numpy(), u_r),
+                g_cell=_rel(cp.grad.cpu().numpy(), gc_r), g_filters=_rel(fl.grad.cpu().numpy(), gf_r))
+    bad = {k: v for k, v in errs.items() if not v <= TOL}
+    assert not bad, f"sub-ROI universe parity failure {bad} (all: {errs})"
+
+
+@pytest.mark.parametrize("backend", ALU_BACKENDS)
+def test_adaptive_sub_roi_universe_trained_alu_parity(backend):
+    params = nc.VonNeumannNetwork.load_checkpoint(os.path.join(GOLDEN, "alu_trained_cells.npz"))
+    spec = nc.compute_adaptive_spatial_mask(params, nc.ChipTopology2D.alu_chip())
+    geom = O.alu_geometry()
+    x, _, _ = O.alu_batch(np.random.default_rng(161), 6, noise=0.0)
+    _sub_roi_universe_case(geom, O.Config(codd_mode="ste_ternary", state_temperature=0.2),
+                           params.cell_params.cpu().numpy(), params.greens_filters.cpu().numpy(), x,
+                           spec.roi_bbox, backend, 162)
+
+
+@pytest.mark.parametrize("backend", ["nchw_direct", "pallas_sram"])
+@pytest.mark.parametrize("mode", ["VALID", "SAME"])
+@pytest.mark.parametrize("final", [None, "sigmoid"])
+def test_adaptive_sub_roi_universe_outputs_outside_window(backend, mode, final):
+    """Output cells inside the sub-ROI, in the ROI outside the window and on the VALID ring:
+    the outputs are read from the assembled full grid."""
+    ports = ((O.RectPort((0, 4), (6, 6)), O.CoordPort(((12, 12), (13, 9)))) if mode == "VALID"
+             else (O.CoordPort(((12, 12), (13, 9), (16, 14))),))
+    outs = ((14, 16), (4, 10), (2, 3), (27, 28)) if mode == "VALID" else ((14, 16), (4, 10), (1, 1))
+    geom = O.make_geometry((28, 30), (7, 5), 4, 3, ports, O.CoordPort(outs), padding_mode=mode,
+                           allow_border_output=True)
+    cell, filt, ins, _ = random_problem(geom, 3, 171)
+    _sub_roi_universe_case(geom, O.Config(final_activate=final), cell, filt, ins, (6, 20, 6, 22),
+                           backend, 172)
