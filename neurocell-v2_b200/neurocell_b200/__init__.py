@@ -13,7 +13,8 @@ from .params import (
 from .propagator import SUPPORTED_BACKENDS, select_optimal_backend, propagate_vnn_2d
 from .model import VonNeumannNetwork
 from .adaptive_mask import AdaptiveMaskSpec, compute_adaptive_spatial_mask, estimate_effective_filter_radii
-from .trainer import VNNTrainer, compute_annealed_temperature, default_mse_loss
+from .trainer import (VNNTrainer, VNNTrainStep, compute_annealed_temperature, default_mse_loss,
+                      default_exact_match_metric, packbits_u8_on_device)
 from . import ops
 from ._lib import load as load_library, LIB_PATH
 
@@ -24,5 +25,6 @@ __all__ = [
     "import_legacy_haiku_params", "SUPPORTED_BACKENDS", "select_optimal_backend",
     "propagate_vnn_2d", "VonNeumannNetwork", "VNNTrainer", "compute_annealed_temperature",
     "default_mse_loss", "ops", "load_library", "LIB_PATH", "AdaptiveMaskSpec",
-    "compute_adaptive_spatial_mask", "estimate_effective_filter_radii",
+    "compute_adaptive_spatial_mask", "estimate_effective_filter_radii", "VNNTrainStep",
+    "default_exact_match_metric", "packbits_u8_on_device",
 ]

@@ -272,8 +272,9 @@ class ChipTopology2D:
     @classmethod
     def gol_chip(cls, grid_shape=(64, 64), kernel_size=(3, 3), directions: int = 64,
                  depth: int = 2, padding_mode: str = "VALID", n=None):
-        """Full-grid cellular automaton (topology.py:359-388).  Its full-grid output lies
-        outside the VALID ROI, which the B200 path does not build (see propagate_vnn_2d)."""
+        """Full-grid cellular automaton (topology.py:359-388).  Its output port covers the
+        whole grid, so propagate_vnn_2d reads it from the assembled universe (the reference's
+        full-grid output path, propagator.py:684-734)."""
         if n is not None:
             grid_shape = (int(n), int(n))
         elif isinstance(grid_shape, int):

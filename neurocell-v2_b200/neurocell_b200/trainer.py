@@ -2,9 +2,13 @@
 
 Mirrors the parts of ``neurocell/trainer.py`` that drive the hot path:
 ``compute_annealed_temperature`` (trainer.py:23-46), ``default_mse_loss`` (57-61),
-``packbits_u8_on_device`` (49-54) and a ``VNNTrainer`` whose ``train_step`` is
-value_and_grad + SGD (trainer.py:101-106 with optax.sgd).  Optimizers other than SGD,
-``lax.scan`` epochs and adaptive caches are not part of the B200 hot path.
+``default_exact_match_metric`` (64-69), ``packbits_u8_on_device`` (49-54) and a
+``VNNTrainer`` whose steps are value_and_grad + SGD (trainer.py:101-106 with optax.sgd),
+with the reference's epoch, evaluation, adaptive sub-ROI, annealed-temperature and
+multi-epoch entry points (trainer.py:108-156, 164-268, 270-356, 358-398).  The
+``lax.scan`` programs become either an eager loop over the library's operators
+(``VNNTrainer``) or one CUDA graph per step or per epoch (``VNNTrainStep``).  Optimizers
+other than SGD are not part of the B200 hot path.
 """
 from __future__ import annotations
 
@@ -34,6 +38,13 @@ def compute_annealed_temperature(epoch: int, total_epochs: int, init_temp: float
 def default_mse_loss(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
     """Mean squared error (trainer.py:57-61), evaluated by the CUDA library."""
     return ops.mse_loss(logits, targets)
+
+
+def default_exact_match_metric(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+    """Rounded exact-match accuracy (trainer.py:64-69)."""
+    if logits.ndim == 3 and logits.shape[-1] == 1 and targets.ndim == 2:
+        logits = logits[..., 0]
+    return (torch.round(logits) == torch.round(targets.to(logits.dtype))).float().mean()
 
 
 def softmax_cross_entropy_loss(logits: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
@@ -176,7 +187,7 @@ class VNNTrainStep:
                  hard_pin_io: bool = False, gated_filters: bool = False,
                  codd_mode: str = "continuous", state_temperature: float = 1.0,
                  active_threshold: float = 0.6, in_shapes=None, process_group=None,
-                 exchange: str = "nccl", conv: str = "auto"):
+                 exchange: str = "nccl", conv: str = "auto", spatial_mask=None):
         import ctypes
         from . import _lib
         from .params import check_codd_mode
@@ -195,8 +206,13 @@ class VNNTrainStep:
         if in_shapes is None:
             in_shapes = tuple(tuple(p.size) if not hasattr(p, "num_points") else (p.num_points,)
                               for p in topology.in_ports)
+        roi_bbox = None
+        if (spatial_mask is not None and not spatial_mask.is_full_roi
+                and topology.padding_mode != "CIRCULAR"):
+            roi_bbox = tuple(int(v) for v in spatial_mask.roi_bbox)
         self.plan = ops.get_plan(topology, tuple(in_shapes), dev, act, slope, fact, fslope, norm,
-                                 hard_pin_io, gated_filters, conv)
+                                 hard_pin_io, gated_filters, conv, roi_bbox)
+        self.window = self.plan.window
         self.lib = _lib.load()
         self._lib = _lib
         self.ctypes = ctypes
@@ -209,15 +225,22 @@ class VNNTrainStep:
         if process_group is not None:
             import torch.distributed as dist
             self.world = dist.get_world_size(process_group)
-        H, W = topology.grid_shape
-        self.n_cell = 3 * H * W
+        cell = params.cell_params.detach()
+        self._full_cell = None
+        if self.window is not None:
+            # adaptive sub-ROI (trainer.py:164-268): the step trains the window's cells; the
+            # cells outside it get no gradient and keep their values in the full copy
+            r0, r1, c0, c1 = self.window
+            self._full_cell = cell.to(torch.float32).clone()
+            cell = self._full_cell[:, r0:r1, c0:c1]
+        self.n_cell = int(cell.numel())
         self.n_filt = int(params.greens_filters.numel())
         self.flat = torch.empty(self.n_cell + self.n_filt, dtype=torch.float32, device=dev)
-        self.flat[: self.n_cell].copy_(params.cell_params.reshape(-1))
+        self.flat[: self.n_cell].copy_(cell.reshape(-1))
         self.flat[self.n_cell:].copy_(params.greens_filters.reshape(-1))
         self.grads = torch.zeros_like(self.flat)
-        self.params = VNNParams(self.flat[: self.n_cell].view(params.cell_params.shape),
-                                self.flat[self.n_cell:].view(params.greens_filters.shape))
+        self._cell_view = self.flat[: self.n_cell].view(tuple(cell.shape))
+        self._filt_view = self.flat[self.n_cell:].view(params.greens_filters.shape)
         self.ws_bytes = self.lib.nc_workspace_bytes(ctypes.byref(self.plan.topo), self.B,
                                                     _lib.NC_FLAG_TRAIN)
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
@@ -236,6 +259,16 @@ class VNNTrainStep:
         if exchange == "nvlink" and self.world > 1:
             self.exchange = NVLinkExchange(self.n_cell + self.n_filt, process_group, dev)
         self._launches = None
+
+    @property
+    def params(self) -> VNNParams:
+        """The trained parameters, full (3, H, W) cells and filters.  With a sub-ROI the
+        window's cells are written into the full copy first (stream-ordered)."""
+        if self.window is None:
+            return VNNParams(self._cell_view, self._filt_view)
+        r0, r1, c0, c1 = self.window
+        self._full_cell[:, r0:r1, c0:c1].copy_(self._cell_view)
+        return VNNParams(self._full_cell, self._filt_view)
 
     def launches_per_step(self) -> int:
         """Kernels ``libneurocell_b200.so`` launches per step, counted by the library while
@@ -372,13 +405,19 @@ class VNNTrainStep:
 
 
 class VNNTrainer:
-    """value_and_grad + SGD over ``apply_fn`` (trainer.py:71-106, optimizer = SGD(lr))."""
+    """value_and_grad + SGD over ``apply_fn`` (trainer.py:71-106, optimizer = SGD(lr)).
 
-    def __init__(self, apply_fn, lr: float = 1e-2, batch_size: int = 128, loss_fn=None):
+    ``apply_fn(params, batch_x, **kw)`` is ``VonNeumannNetwork.apply`` or a closure over
+    ``propagate_vnn_2d``; the adaptive and annealed entry points pass ``spatial_mask``,
+    ``codd_mode`` and ``state_temperature`` through it as the reference does."""
+
+    def __init__(self, apply_fn, lr: float = 1e-2, batch_size: int = 128, loss_fn=None,
+                 eval_metric_fn=None):
         self.apply_fn = apply_fn
         self.lr = float(lr)
         self.batch_size = batch_size
         self.loss_fn = loss_fn or default_mse_loss
+        self.eval_metric_fn = eval_metric_fn or default_exact_match_metric
 
     def value_and_grad(self, params: VNNParams, batch_x, batch_y, **apply_kw):
         cp = params.cell_params.detach().requires_grad_(True)
@@ -419,3 +458,64 @@ class VNNTrainer:
             acc += float((p.reshape(by.shape) == by).float().mean())
             preds.append(p)
         return acc / max(1, len(preds)), preds
+
+    @torch.no_grad()
+    def evaluate_metric(self, params: VNNParams, x_batches, y_batches, **apply_kw):
+        """Mean of ``eval_metric_fn`` over the batches (trainer.py:140-153)."""
+        total, n = 0.0, 0
+        for bx, by in zip(x_batches, y_batches):
+            total += float(self.eval_metric_fn(self.apply_fn(params, bx, **apply_kw), by))
+            n += 1
+        return total / max(1, n)
+
+    # adaptive sub-ROI entry points (trainer.py:164-268); the library's plan cache keys the
+    # sub-ROI windows by roi_bbox, as the reference caches one executable per bucket
+    @staticmethod
+    def _mask_kw(mask_spec) -> dict:
+        return {} if mask_spec is None or mask_spec.is_full_roi else {"spatial_mask": mask_spec}
+
+    def train_step_adaptive(self, params: VNNParams, batch_x, batch_y, mask_spec):
+        return self.train_step(params, batch_x, batch_y, **self._mask_kw(mask_spec))
+
+    def train_epoch_adaptive(self, params: VNNParams, x_epoch, y_epoch, mask_spec):
+        return self.train_epoch(params, x_epoch, y_epoch, **self._mask_kw(mask_spec))
+
+    def evaluate_packed_adaptive(self, params: VNNParams, x_batches, y_packed_batches, mask_spec):
+        return self.evaluate_packed(params, x_batches, y_packed_batches, **self._mask_kw(mask_spec))
+
+    def evaluate_metric_adaptive(self, params: VNNParams, x_batches, y_batches, mask_spec):
+        return self.evaluate_metric(params, x_batches, y_batches, **self._mask_kw(mask_spec))
+
+    # dynamic temperature and Codd mode (trainer.py:270-356): tau is a plain argument of
+    # the library call, nothing is recompiled when it changes
+    def train_step_annealed(self, params: VNNParams, batch_x, batch_y,
+                            state_temperature: float = 1.0, codd_mode: str = "annealed",
+                            mask_spec=None):
+        return self.train_step(params, batch_x, batch_y, codd_mode=codd_mode,
+                               state_temperature=float(state_temperature), **self._mask_kw(mask_spec))
+
+    def train_epoch_annealed(self, params: VNNParams, x_epoch, y_epoch,
+                             state_temperature: float = 1.0, codd_mode: str = "annealed",
+                             mask_spec=None):
+        return self.train_epoch(params, x_epoch, y_epoch, codd_mode=codd_mode,
+                                state_temperature=float(state_temperature), **self._mask_kw(mask_spec))
+
+    def train_epochs(self, params: VNNParams, x_train: torch.Tensor, y_train: torch.Tensor, rng,
+                     num_epochs: int):
+        """``num_epochs`` epochs with an on-device shuffle at every epoch boundary
+        (trainer.py:358-398): a device permutation of the samples, truncated to whole
+        batches.  ``rng``: int seed or ``torch.Generator`` on the data's device.  Returns
+        ``(params, epoch_losses)`` with one device scalar per epoch."""
+        dev = x_train.device
+        gen = rng if isinstance(rng, torch.Generator) else torch.Generator(dev).manual_seed(int(rng))
+        n = int(x_train.shape[0])
+        steps = n // self.batch_size
+        usable = steps * self.batch_size
+        losses = []
+        for _ in range(int(num_epochs)):
+            perm = torch.randperm(n, generator=gen, device=dev)[:usable]
+            xe = x_train[perm].reshape((steps, self.batch_size) + tuple(x_train.shape[1:]))
+            ye = y_train[perm].reshape((steps, self.batch_size) + tuple(y_train.shape[1:]))
+            params, ep = self.train_epoch(params, xe, ye)
+            losses.append(ep)
+        return params, torch.stack(losses) if losses else torch.zeros(0, device=dev)

@@ -69,3 +69,94 @@ def test_vnn_trainer_epoch_and_packed_evaluation():
     packed = [torch.tensor(np.packbits(np.asarray(y, np.uint8), axis=1), device=dev) for y in ys]
     acc, preds = tr.evaluate_packed(p, xd, packed)
     assert 0.0 <= acc <= 1.0 and len(preds) == 2
+
+
+def test_train_step_sub_roi_graph_equals_eager_adaptive_steps():
+    """VNNTrainStep on an adaptive sub-ROI (the window's cells in the packed buffer, one
+    CUDA graph per epoch) trains exactly as VNNTrainer.train_step_adaptive does through the
+    autograd operator (trainer.py:250-258)."""
+    cell, filt, xs, ys = _alu(3, 32, 13)
+    dev = torch.device("cuda:0")
+    topo = nc.ChipTopology2D.alu_chip()
+    p0 = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
+    spec = nc.compute_adaptive_spatial_mask(nc.init_vnn_params(701, topo, device=dev), topo)
+    assert not spec.is_full_roi
+    xd, yd = torch.tensor(xs, device=dev), torch.tensor(ys, device=dev)
+
+    model = nc.VonNeumannNetwork(topo)
+    tr = nc.VNNTrainer(model.apply, lr=1e-2, batch_size=32)
+    p = nc.VNNParams(p0.cell_params.clone(), p0.greens_filters.clone())
+    ref_losses = []
+    for i in range(3):
+        p, loss = tr.train_step_adaptive(p, xd[i].reshape(32, 3, 8, 1), yd[i], spec)
+        ref_losses.append(float(loss))
+
+    st = nc.VNNTrainStep(topo, p0, 32, lr=1e-2, in_shapes=((8, 1),) * 3, spatial_mask=spec)
+    assert st.window is not None and st.n_cell < 3 * 62 * 62
+    st.capture_epoch(xd, yd)
+    got = st.train_epoch().cpu().numpy()
+    q = st.params
+    torch.cuda.synchronize()
+    assert q.cell_params.shape == (3, 62, 62)
+    assert np.allclose(got, np.asarray(ref_losses, np.float32), rtol=1e-6, atol=0)
+    rel = (torch.linalg.norm(q.cell_params - p.cell_params) / torch.linalg.norm(p.cell_params)).item()
+    relf = (torch.linalg.norm(q.greens_filters - p.greens_filters) /
+            torch.linalg.norm(p.greens_filters)).item()
+    assert rel <= 1e-6 and relf <= 1e-6
+    # cells outside the window keep their initial values
+    r0, r1, c0, c1 = st.window
+    outside = torch.ones((62, 62), dtype=torch.bool, device=dev)
+    outside[r0:r1, c0:c1] = False
+    assert torch.equal(q.cell_params[:, outside], p0.cell_params[:, outside])
+
+
+def test_adaptive_epochs_one_bucket_and_convergence():
+    """unit_milestone7_adaptive_mask.py:186-220: the mask is recomputed before every epoch,
+    one sub-ROI bucket (one window plan) serves all three epochs, the loss falls, and the
+    packed evaluation runs on the same mask."""
+    from neurocell_b200 import ops
+    dev = torch.device("cuda:0")
+    topo = nc.ChipTopology2D.alu_chip()
+    model = nc.VonNeumannNetwork(topo, backend="auto")
+    params = nc.init_vnn_params(708, topo, device=dev)
+    tr = nc.VNNTrainer(model.apply, lr=0.05, batch_size=32)
+    g = torch.Generator(dev).manual_seed(709)
+    x_ep = torch.randint(0, 2, (4, 32, 3, 8, 1), generator=g, device=dev).float()
+    y_ep = torch.randint(0, 2, (4, 32, 8), generator=g, device=dev).float()
+    losses, bboxes, plans = [], set(), []
+    for _ in range(3):
+        spec = model.compute_spatial_mask(params, margin=4, bucket_multiple=8)
+        bboxes.add(spec.roi_bbox)
+        params, ep_loss = tr.train_epoch_adaptive(params, x_ep, y_ep, spec)
+        losses.append(float(ep_loss))
+        plans.append({k for k in ops._PLANS if k[-2] is not None})
+    # epochs 2 and 3 reuse the window plan built for the bucket in epoch 1
+    assert len(bboxes) == 1 and plans[0] == plans[1] == plans[2]
+    assert any(k[-2] == next(iter(bboxes)) for k in plans[0])
+    assert losses[-1] < losses[0]
+    y_packed = nc.packbits_u8_on_device(y_ep.to(torch.uint8))
+    acc, preds = tr.evaluate_packed_adaptive(params, x_ep, y_packed, spec)
+    assert len(preds) == 4 and preds[0].shape == (32, 1) and 0.0 <= acc <= 1.0
+    m = tr.evaluate_metric_adaptive(params, x_ep, y_ep, spec)
+    assert 0.0 <= m <= 1.0
+
+
+def test_annealed_steps_and_multi_epoch_shuffle():
+    """train_step_annealed / train_epochs (trainer.py:322-398): the temperature is a plain
+    argument, the multi-epoch loop shuffles on the device."""
+    dev = torch.device("cuda:0")
+    topo = nc.ChipTopology2D.alu_chip()
+    model = nc.VonNeumannNetwork(topo)
+    params = nc.init_vnn_params(711, topo, device=dev)
+    tr = nc.VNNTrainer(model.apply, lr=0.05, batch_size=16)
+    g = torch.Generator(dev).manual_seed(712)
+    x = torch.randint(0, 2, (16, 3, 8, 1), generator=g, device=dev).float()
+    y = torch.randint(0, 2, (16, 8), generator=g, device=dev).float()
+    taus = [nc.compute_annealed_temperature(e, 3) for e in range(3)]
+    for tau in taus:
+        params, loss = tr.train_step_annealed(params, x, y, state_temperature=tau, codd_mode="ste_ternary")
+        assert torch.isfinite(loss)
+    xt = torch.randint(0, 2, (40, 3, 8, 1), generator=g, device=dev).float()
+    yt = torch.randint(0, 2, (40, 8), generator=g, device=dev).float()
+    params, ep = tr.train_epochs(params, xt, yt, 5, 3)
+    assert ep.shape == (3,) and bool(torch.isfinite(ep).all())
