@@ -218,8 +218,16 @@ def run_b200(args) -> None:
     cell, filt, xs, ys = make_problem(rank, nb, BATCH)
     topo = nc.ChipTopology2D.alu_chip()
     params = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
+    spec, n_pix = None, 2000
+    if args.adaptive:
+        # the reference's adaptive-mask measurement (README stage 06/07): the pre-epoch mask
+        # of a freshly initialised ALU chip, margin 4, buckets of 8 -> a 32x32 sub-ROI
+        spec = nc.compute_adaptive_spatial_mask(nc.init_vnn_params(701, topo, device=dev), topo,
+                                                margin=4, bucket_multiple=8)
+        n_pix = spec.active_shape[0] * spec.active_shape[1]
     runner = nc.trainer.VNNTrainStep(topo, params, BATCH, lr=LR, in_shapes=((8, 1),) * 3,
-                                     process_group=pg, exchange=args.exchange, conv=args.conv)
+                                     process_group=pg, exchange=args.exchange, conv=args.conv,
+                                     spatial_mask=spec)
     x_dev = torch.tensor(xs.reshape(nb, BATCH, -1), device=dev)
     y_dev = torch.tensor(ys, device=dev)
     if not args.no_graph:
@@ -309,8 +317,8 @@ def run_b200(args) -> None:
     h2d = x_host[0].numel() * 4 + y_host[0].numel() * 4
 
     peak = fp32_peak_tflops(dev)
-    flops_fwd = BATCH * 2.0 * 16 * 2000 * 299 * 4            # d forward passes
-    flops_bwd = BATCH * 2.0 * 16 * 2000 * 299 * 7            # d dG + (d-1) dX passes
+    flops_fwd = BATCH * 2.0 * 16 * n_pix * 299 * 4           # d forward passes
+    flops_bwd = BATCH * 2.0 * 16 * n_pix * 299 * 7           # d dG + (d-1) dX passes
     path = lib.nc_conv_path(ctypes.byref(runner.plan.topo))
     names = {1: ("fast::fwd_kernel_mt<23, 13, 8>", "fast::bwd_kernel<23, 13>"),
              3: ("fftf_fwd_kernel", "fftf_bwd_kernel")}.get(path, ("forward kernels", "backward kernels"))
@@ -319,7 +327,9 @@ def run_b200(args) -> None:
 
     if rank == 0:
         line = {
-            "metric": "train samples/s (62x62 ALU VNN, B=128 per GPU)", "value": value,
+            "metric": ("train samples/s (62x62 ALU VNN, B=128 per GPU)" if spec is None else
+                       "train samples/s (62x62 ALU VNN on its adaptive %dx%d sub-ROI, B=128 per GPU)"
+                       % spec.active_shape), "value": value,
             "unit": "samples/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32",
@@ -330,7 +340,8 @@ def run_b200(args) -> None:
                        "parallelism": f"dp{world}", "l2": "flushed (256 MB write) before every timed step",
                        "cuda_graph": runner.graph is not None,
                        "grad_exchange": (args.exchange if world > 1 else "none"),
-                       "conv": args.conv},
+                       "conv": args.conv,
+                       "sub_roi": None if spec is None else list(spec.roi_bbox)},
             "e2e": {"value": BATCH * world / (e2e_ms * 1e-3), "unit": "samples/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms},
             "gpu_launches": runner.launches_per_step() * K,
@@ -346,7 +357,7 @@ def run_b200(args) -> None:
                          "traffic_source": "profiles/ncu_traffic.json (one ncu capture, dram read+write per launch)"},
             "clocks": clk,
         }
-        if world == 1 and not args.no_cpu:
+        if world == 1 and not args.no_cpu and spec is None:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     runner.release()                # graphs holding NCCL calls and the IPC maps go first
@@ -537,6 +548,9 @@ def main():
                          "peer-memory sum + SGD kernel (default) or NCCL all-reduce + SGD")
     ap.add_argument("--config", type=int, choices=(0, 1, 2, 3, 4), default=0,
                     help="BASELINE config; 1-4 print a secondary single-GPU line")
+    ap.add_argument("--adaptive", action="store_true",
+                    help="config 0 on the adaptive sub-ROI of a freshly initialised chip "
+                         "(secondary measurement)")
     ap.add_argument("--conv", choices=("auto", "direct", "fft"), default="auto",
                     help="Green's convolution algorithm (nc_conv_algo)")
     args = ap.parse_args()
