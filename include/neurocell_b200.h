@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define NC_ABI_VERSION 3
+#define NC_ABI_VERSION 4
 
 typedef enum nc_status {
   NC_OK = 0,
@@ -249,10 +249,11 @@ nc_status nc_sgd_update(float* params, const float* grads, int64_t n, float lr, 
 /*
  * No counterpart in the reference (it has no multi-GPU code; the north star asks for the
  * ~16k-parameter gradient to be all-reduced across 1/2/4/8 GPUs).  nc_dp_allreduce_sgd
- * fuses the cross-GPU gradient sum with the SGD update in one kernel: every rank copies
- * its packed gradient into its slot of a double-buffered shared buffer, raises per-slice
- * flags, waits (bounded) for the same slices of all peers, sums them in rank order with
- * peer loads over NVLink (bitwise identical on every rank) and updates its parameters.
+ * fuses the cross-GPU gradient sum with the SGD update in one kernel: every rank stores
+ * its packed gradient into its slot of every peer's double-buffered receive buffer over
+ * NVLink, raises per-slice flags there, waits (bounded) for the same slices of all peers
+ * in its own buffer, sums them in rank order from local memory (bitwise identical on
+ * every rank) and updates its parameters.
  * Set-up: nc_dp_alloc on every rank, exchange nc_ipc_get handles (e.g. all_gather), open
  * the peers' buffers with nc_ipc_open, zero-initialised state from nc_dp_alloc.
  * Step counters live on the device, so the call can be captured in a CUDA graph.
@@ -260,8 +261,9 @@ nc_status nc_sgd_update(float* params, const float* grads, int64_t n, float lr, 
 #define NC_DP_MAX_RANKS 8
 #define NC_IPC_HANDLE_BYTES 64
 
-/* Device bytes of the shared exchange buffer for n parameters. */
-size_t nc_dp_shared_bytes(int64_t n);
+/* Device bytes of the shared receive buffer for n parameters and world ranks (0 when
+   world is outside 1..NC_DP_MAX_RANKS). */
+size_t nc_dp_shared_bytes(int64_t n, int32_t world);
 /* Device bytes of the private per-rank state (step counters, status word). */
 size_t nc_dp_state_bytes(void);
 /* Set-up time allocations (cudaMalloc + zero fill); not for the hot path. */

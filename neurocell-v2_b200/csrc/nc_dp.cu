@@ -1,15 +1,20 @@
 // nc_dp.cu -- fused cross-GPU gradient sum + SGD over NVLink peer memory (sm_100a).
 //
-// Each rank owns a shared buffer  [2 parity slots of n floats][flags: 2 x kDpBlocks u32]
-// mapped into every peer with CUDA IPC.  Block k of the kernel owns slice k of the
-// gradient: it copies the slice into the slot of this step's parity, publishes it with a
-// system-scope release on flag[parity][k] = step, waits (bounded) until every peer's flag
-// for the same slice reaches `step`, then sums the slice over ranks 0..world-1 in that
-// order with peer loads and applies SGD.  Every rank therefore ends with bitwise identical
-// parameters.  Double buffering makes the next step safe: a rank can overwrite slot
-// `parity` only at step+2, after every peer has published step+1, i.e. after every peer
-// finished reading step's slot.  Step counters are per block and live on the device, so
-// the launch can be captured in a CUDA graph.  No multicast and no TMA: plain loads only.
+// Push protocol with step-tagged lines.  Each rank owns a receive buffer of 16-byte lines
+//   [2 parity][world source ranks][n_lines]   line = {g[2l], step, g[2l+1], step}
+// mapped into every peer with CUDA IPC.  Every step each rank stores its gradient, two
+// values per line, into slot (parity, own rank) of every PEER's buffer with one 16-byte
+// store per line (posted NVLink writes; each 8-byte half {value, step} is written as one
+// unit).  A receiver knows a value has arrived when the step tag next to it equals the
+// current step, so no fences and no separate flags are needed: block k polls the lines of
+// its slice in its OWN buffer (bounded), then sums the slice over ranks 0..world-1 in that
+// order (its own contribution straight from `grads`) and applies SGD.  Every rank adds the
+// same values in the same order and ends with bitwise identical parameters.  Double
+// buffering makes the next step safe: a rank writes slot `parity` again only at step+2,
+// after every peer has published step+1, i.e. after every peer finished reading step's
+// slot (its step kernel ended before its step+1 kernel began).  Step counters are per block
+// and live on the device, so the launch can be captured in a CUDA graph.  No multicast,
+// no TMA, no atomics on peer memory: plain stores and volatile loads.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -25,109 +30,99 @@ constexpr int kDpBlocks = 32;
 constexpr int kDpThreads = 128;
 
 struct Peers {
-  float* p[NC_DP_MAX_RANKS];
+  uint4* p[NC_DP_MAX_RANKS];
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+__host__ __device__ inline long long n_lines(long long n) { return (n + 1) / 2; }
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void st_line(uint4* p, uint4 v) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_line(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ float2 load_pair(const float* g, long long n, long long l) {
+  const long long i = 2 * l;
+  return make_float2(g[i], i + 1 < n ? g[i + 1] : 0.f);
 }
 
-// Sum of one element (or one float4) over the ranks, in rank order: all loads are issued
-// before the first add so the NVLink round trips overlap.
-template <typename T>
-__device__ __forceinline__ T rank_sum(const Peers& peers, int world, size_t off);
-
-template <>
-__device__ __forceinline__ float rank_sum<float>(const Peers& peers, int world, size_t off) {
-  float v[NC_DP_MAX_RANKS];
-#pragma unroll
-  for (int r = 0; r < NC_DP_MAX_RANKS; ++r) v[r] = (r < world) ? __ldcv(peers.p[r] + off) : 0.f;
-  float s = v[0];
-#pragma unroll
-  for (int r = 1; r < NC_DP_MAX_RANKS; ++r)
-    if (r < world) s += v[r];
-  return s;
-}
-
-template <>
-__device__ __forceinline__ float4 rank_sum<float4>(const Peers& peers, int world, size_t off) {
-  float4 v[NC_DP_MAX_RANKS];
-#pragma unroll
-  for (int r = 0; r < NC_DP_MAX_RANKS; ++r)
-    v[r] = (r < world) ? __ldcv(reinterpret_cast<const float4*>(peers.p[r] + off))
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 s = v[0];
-#pragma unroll
-  for (int r = 1; r < NC_DP_MAX_RANKS; ++r)
-    if (r < world) { s.x += v[r].x; s.y += v[r].y; s.z += v[r].z; s.w += v[r].w; }
-  return s;
-}
-
-// Block k owns elements [k*slice, min(n, (k+1)*slice)); `vec` = n % 4 == 0 and the caller's
-// buffers are 16-byte aligned, so the slice (a multiple of 4) moves as float4.
+// Block k owns lines [k*slice, min(L, (k+1)*slice)) of the L = ceil(n/2) lines.
 __global__ void __launch_bounds__(kDpThreads) dp_allreduce_sgd_kernel(
-    Peers peers, int world, int rank, long long n, int vec, size_t flag_off, unsigned* counters,
-    int* status, float* grads, float* params, float lr_eff, int max_wait) {
+    Peers peers, int world, int rank, long long n, unsigned* counters, int* status, float* grads,
+    float* params, float lr_eff, int max_wait) {
   const int k = blockIdx.x;
-  const long long slice = (((n + gridDim.x - 1) / gridDim.x) + 3) & ~3LL;
-  const long long i0 = (long long)k * slice < n ? (long long)k * slice : n;
-  const long long i1 = (i0 + slice < n) ? i0 + slice : n;
+  const long long L = n_lines(n);
+  const long long slice = (L + gridDim.x - 1) / gridDim.x;
+  const long long l0 = (long long)k * slice < L ? (long long)k * slice : L;
+  const long long l1 = (l0 + slice < L) ? l0 + slice : L;
   __shared__ unsigned s_step;
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) s_step = counters[k] + 1u;
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) {
+    s_step = counters[k] + 1u;
+    s_bad = 0;
+  }
   __syncthreads();
   const unsigned step = s_step;
   const int par = (int)(step & 1u);
-  const size_t base = (size_t)par * (size_t)n;
-  float* mine = peers.p[rank] + base;
-  if (vec) {
-    for (long long i = i0 + 4 * threadIdx.x; i < i1; i += 4 * blockDim.x)
-      *reinterpret_cast<float4*>(mine + i) = *reinterpret_cast<const float4*>(grads + i);
-  } else {
-    for (long long i = i0 + threadIdx.x; i < i1; i += blockDim.x) mine[i] = grads[i];
+  auto slot = [&](int owner, int src) {   // slot (par, src) of rank owner's buffer
+    return peers.p[owner] + ((size_t)par * world + src) * (size_t)L;
+  };
+  // 1. push this rank's lines to every peer
+  for (long long l = l0 + threadIdx.x; l < l1; l += blockDim.x) {
+    const float2 v = load_pair(grads, n, l);
+    const uint4 line = make_uint4(__float_as_uint(v.x), step, __float_as_uint(v.y), step);
+    for (int r = 0; r < world; ++r)
+      if (r != rank) st_line(slot(r, rank) + l, line);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    unsigned* myflag = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(peers.p[rank]) + flag_off) +
-                       par * kDpBlocks + k;
-    st_release_sys(myflag, step);
-    int ok = 1, it = 0;                   // one poll budget for all peers together
-    for (int r = 0; r < world && ok; ++r) {
-      const unsigned* f = reinterpret_cast<const unsigned*>(reinterpret_cast<const char*>(peers.p[r]) +
-                                                            flag_off) + par * kDpBlocks + k;
-      while (ld_acquire_sys(f) != step) {
-        if (++it > max_wait) { ok = 0; break; }
-        __nanosleep(128);
+  // 2. wait until every peer's lines of this slice carry this step's tag (bounded)
+  int it = 0, bad = 0;
+  for (long long l = l0 + threadIdx.x; l < l1 && !bad; l += blockDim.x) {
+    for (int r = 0; r < world && !bad; ++r) {
+      if (r == rank) continue;
+      const uint4* q = slot(rank, r) + l;
+      for (;;) {
+        const uint4 v = ld_line(q);
+        if (v.y == step && v.w == step) break;
+        if (++it > max_wait) { bad = 1; break; }
+        if (it > 64) __nanosleep(32);
       }
     }
-    if (!ok) atomicExch(status, 1);
-    s_ok = ok;
   }
+  if (bad) s_bad = 1;
   __syncthreads();
-  if (!s_ok) return;                      // a peer did not arrive: no update, status set
-  __threadfence_system();
-  if (vec) {
-    for (long long i = i0 + 4 * threadIdx.x; i < i1; i += 4 * blockDim.x) {
-      const float4 s = rank_sum<float4>(peers, world, base + (size_t)i);
-      *reinterpret_cast<float4*>(grads + i) = s;
-      float4 p = *reinterpret_cast<const float4*>(params + i);
-      p.x -= lr_eff * s.x; p.y -= lr_eff * s.y; p.z -= lr_eff * s.z; p.w -= lr_eff * s.w;
-      *reinterpret_cast<float4*>(params + i) = p;
+  if (s_bad) {                            // a peer did not arrive: no update, status set
+    if (threadIdx.x == 0) atomicExch(status, 1);
+    return;
+  }
+  // 3. sum in rank order, SGD
+  for (long long l = l0 + threadIdx.x; l < l1; l += blockDim.x) {
+    float2 s = make_float2(0.f, 0.f);
+    for (int r = 0; r < world; ++r) {
+      float2 v;
+      if (r == rank) {
+        v = load_pair(grads, n, l);
+      } else {
+        const uint4 q = ld_line(slot(rank, r) + l);
+        v = make_float2(__uint_as_float(q.x), __uint_as_float(q.z));
+      }
+      if (r == 0) s = v; else { s.x += v.x; s.y += v.y; }
     }
-  } else {
-    for (long long i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-      const float s = rank_sum<float>(peers, world, base + (size_t)i);
-      grads[i] = s;
-      params[i] -= lr_eff * s;
+    const long long i = 2 * l;
+    grads[i] = s.x;
+    params[i] -= lr_eff * s.x;
+    if (i + 1 < n) {
+      grads[i + 1] = s.y;
+      params[i + 1] -= lr_eff * s.y;
     }
   }
   __syncthreads();
@@ -141,9 +136,9 @@ using namespace nc;
 
 extern "C" {
 
-size_t nc_dp_shared_bytes(int64_t n) {
-  if (n <= 0) return 0;
-  return align256(sizeof(float) * 2 * (size_t)n) + align256(sizeof(unsigned) * 2 * kDpBlocks);
+size_t nc_dp_shared_bytes(int64_t n, int32_t world) {
+  if (n <= 0 || world < 1 || world > NC_DP_MAX_RANKS) return 0;
+  return align256(sizeof(uint4) * 2 * (size_t)world * (size_t)n_lines(n));
 }
 
 size_t nc_dp_state_bytes(void) { return align256(sizeof(unsigned) * kDpBlocks + sizeof(int)); }
@@ -194,16 +189,15 @@ nc_status nc_dp_allreduce_sgd(void* const* peers, int32_t world, int32_t rank, v
   Peers pp{};
   for (int r = 0; r < world; ++r) {
     if (!peers[r]) return set_error(NC_ERR_INVALID, "peer buffer %d is null", r);
-    pp.p[r] = static_cast<float*>(peers[r]);
+    if (reinterpret_cast<uintptr_t>(peers[r]) % 16 != 0)
+      return set_error(NC_ERR_INVALID, "peer buffer %d is not 16-byte aligned", r);
+    pp.p[r] = static_cast<uint4*>(peers[r]);
   }
   unsigned* counters = static_cast<unsigned*>(d_state);
   int* status = reinterpret_cast<int*>(counters + kDpBlocks);
-  const size_t flag_off = align256(sizeof(float) * 2 * (size_t)n);
-  const int vec = (n % 4 == 0) && (reinterpret_cast<uintptr_t>(grads) % 16 == 0) &&
-                  (reinterpret_cast<uintptr_t>(params) % 16 == 0);
   dp_allreduce_sgd_kernel<<<kDpBlocks, kDpThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      pp, world, rank, (long long)n, vec, flag_off, counters, status, grads, params,
-      lr / (float)world, max_wait_iters);
+      pp, world, rank, (long long)n, counters, status, grads, params, lr / (float)world,
+      max_wait_iters);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "dp_allreduce_sgd_kernel launch");
   note_launch();

@@ -12,7 +12,7 @@ import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libneurocell_b200.so")
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 NC_OK, NC_ERR_INVALID, NC_ERR_WORKSPACE, NC_ERR_UNSUPPORTED, NC_ERR_CUDA = 0, 1, 2, 3, 4
 NC_PAD = {"VALID": 0, "SAME": 1, "CIRCULAR": 2}
@@ -81,7 +81,7 @@ _SIGS = {
     "nc_vnn_forward_static": (_i32, [_TP, _vp, _vp, _vp, _vp, _i32, _CP, _vp, _vp]),
     "nc_set_profile_events": (None, [_vp, _vp, _vp, _vp]),
     "nc_fp32_peak_probe": (_i32, [_i32, ctypes.POINTER(ctypes.c_double), _vp, _vp]),
-    "nc_dp_shared_bytes": (_sz, [_i64]),
+    "nc_dp_shared_bytes": (_sz, [_i64, _i32]),
     "nc_dp_state_bytes": (_sz, []),
     "nc_dp_alloc": (_i32, [_sz, ctypes.POINTER(_vp)]),
     "nc_dp_free": (_i32, [_vp]),

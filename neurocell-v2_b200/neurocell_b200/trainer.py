@@ -78,11 +78,12 @@ class NVLinkExchange:
     """Gradient sum over the ranks of a process group fused with the SGD update, one kernel
     over NVLink peer memory (``nc_dp_allreduce_sgd``).
 
-    Each rank allocates a double-buffered exchange buffer, the ranks swap CUDA IPC handles
-    with one ``all_gather_object`` and map each other's buffers.  Every step each rank's
-    kernel publishes its gradient, waits (bounded by ``max_wait_iters`` polls) for the same
-    slices of all peers, sums them in rank order (bitwise the same on every rank) and applies
-    ``params -= lr / world * sum``.  One process per GPU; ranks on one GPU are rejected,
+    Each rank allocates a double-buffered receive buffer (one slot per rank), the ranks swap
+    CUDA IPC handles with one ``all_gather_object`` and map each other's buffers.  Every step
+    each rank's kernel stores its gradient into every peer's buffer and raises flags there,
+    waits (bounded by ``max_wait_iters`` polls of its own flags) for the same slices of all
+    peers, sums them in rank order from local memory (bitwise the same on every rank) and
+    applies ``params -= lr / world * sum``.  One process per GPU; ranks on one GPU are rejected,
     because kernels that wait on one another cannot share a device.  ``close()`` unmaps and
     frees the buffers (collective: every rank calls it).
     """
@@ -111,7 +112,7 @@ class NVLinkExchange:
         self.shared = ctypes.c_void_p()
         self.state = ctypes.c_void_p()
         with torch.cuda.device(dev):
-            _lib.check(self.lib.nc_dp_alloc(self.lib.nc_dp_shared_bytes(self.n),
+            _lib.check(self.lib.nc_dp_alloc(self.lib.nc_dp_shared_bytes(self.n, self.world),
                                             ctypes.byref(self.shared)), "nc_dp_alloc")
             _lib.check(self.lib.nc_dp_alloc(self.lib.nc_dp_state_bytes(), ctypes.byref(self.state)),
                        "nc_dp_alloc")
