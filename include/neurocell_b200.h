@@ -309,6 +309,14 @@ nc_status nc_fp32_peak_probe(int32_t iters, double* flops, float* sink, void* st
 /* Message of the last failing call on this host thread ("" if none). */
 const char* nc_last_error(void);
 
+/*
+ * Sticky error word of the current device: 0 ok; 1 when a kernel's bounded wait for its
+ * own asynchronous copies into shared memory gave up (the results of that call are
+ * invalid); -1 when it could not be read.  clear != 0 resets it.  Synchronous (a device
+ * read); not for the hot path.
+ */
+int32_t nc_device_error(int32_t clear);
+
 /* NC_ABI_VERSION of the loaded library. */
 int32_t nc_abi_version(void);
 

@@ -309,6 +309,8 @@ int32_t nc_conv_path(const nc_topo* topo) {
 
 const char* nc_last_error(void) { return g_err; }
 
+int32_t nc_device_error(int32_t clear) { return fftf_device_error(clear != 0); }
+
 size_t nc_plan_bytes(const nc_topo* topo) {
   Geo g;
   if (make_geo(topo, &g) != NC_OK) return 0;

@@ -35,8 +35,82 @@ constexpr int kPlane = fft64::kPlane;         // float2 per on-chip plane
 constexpr int kThreads = 512;
 constexpr float kInvNN = 1.0f / (float)(kN * kN);
 static_assert(kN == fft64::kN, "fused kernels are built on the 64-point transforms");
+static_assert(kPlane == kFftfPlane, "stored spectra use the on-chip plane layout");
+constexpr unsigned kPlaneBytes = kPlane * sizeof(float2);        // 33,792
+constexpr unsigned kPlaneChunk = kPlaneBytes / 4;                // 8,448: bulk copy size
 
 __device__ __forceinline__ int at2(int r, int c) { return fft64::at(r, c); }
+
+// ---- bulk copies global -> shared (cp.async.bulk, completion on an mbarrier) ------------
+// Used to stage the next direction pair's spectra and saved planes while the current pair
+// computes.  Every wait is bounded; a wait that gives up sets g_fftf_error, waits once more
+// (bounded) for the copy in flight and lets the kernel run on (its results are invalid).
+__device__ int g_fftf_error;
+constexpr int kWaitLimit = 1 << 20;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// Orders this thread's earlier generic-proxy accesses of shared memory before its bulk copies.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// `bytes` and both addresses are multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the completion of phase `parity` of `bar` (bounded, see above).
+__device__ __forceinline__ void mbar_wait(uint64_t* bar, unsigned parity) {
+  for (int it = 0; it < kWaitLimit; ++it)
+    if (mbar_try_wait(bar, parity)) return;
+  atomicExch(&g_fftf_error, 1);
+  for (int it = 0; it < kWaitLimit; ++it)
+    if (mbar_try_wait(bar, parity)) return;
+}
+
+#if NC_PHASE_TIMING
+// Debug builds only: clock64 cycles of CTA 0's thread 0 between phase marks, summed over
+// launches ([0] forward, [1] backward; see the FFTF_MARK slots in each kernel).
+__device__ long long g_fftf_phase[2][16];
+#define FFTF_T0() long long fftf_t_last = clock64()
+#define FFTF_MARK(kern, slot)                                          \
+  do {                                                                 \
+    if (blockIdx.x == 0 && threadIdx.x == 0) {                         \
+      const long long now = clock64();                                 \
+      g_fftf_phase[kern][slot] += now - fftf_t_last;                   \
+      fftf_t_last = now;                                               \
+    }                                                                  \
+  } while (0)
+#else
+#define FFTF_T0() \
+  do {            \
+  } while (0)
+#define FFTF_MARK(kern, slot) \
+  do {                        \
+  } while (0)
+#endif
 
 // Forward 2-D transform of rows [0, nrows) then all columns; barriers on both sides.
 __device__ __forceinline__ void fwd2d(float2* s, int nrows, const float2* tw, const fft64::Lane& L) {
@@ -67,27 +141,30 @@ __device__ __forceinline__ void pixel_offsets(const Geo& g, int tid, int poff[kP
   }
 }
 
-// Sum of up to four per-thread values over the CTA (result broadcast to every thread).
-__device__ __forceinline__ void block_sum4(float v[4], float* red) {
+// Sum of four per-thread values over the CTA, broadcast to every thread, with ONE barrier:
+// warp partials go to half `par` of `red` (2 x 4 x 16 floats) and every thread adds the 16
+// partials in warp order (the same order everywhere, so all threads get identical sums).
+// Alternating halves makes a barrier before the writes unnecessary: a thread writes half
+// `par` again only after the barrier of the next call, which every thread reaches after
+// its reads of this call.  Callers flip `par` after each call, uniformly.
+__device__ __forceinline__ void block_sum4(float v[4], float* red, int& par) {
+  static_assert(kThreads / 32 == 16, "16 warp partials");
 #pragma unroll
   for (int k = 0; k < 4; ++k) v[k] = warp_sum(v[k]);
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  __syncthreads();
+  float* h = red + par * 64;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) red[k * 32 + w] = v[k];
+    for (int k = 0; k < 4; ++k) h[k * 16 + w] = v[k];
   __syncthreads();
-  if (w == 0) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float r = lane < nw ? red[k * 32 + lane] : 0.f;
-      r = warp_sum(r);
-      if (lane == 0) red[128 + k] = r;
-    }
+  for (int k = 0; k < 4; ++k) {
+    const float4* q = reinterpret_cast<const float4*>(h + k * 16);
+    const float4 a0 = q[0], a1 = q[1], a2 = q[2], a3 = q[3];
+    v[k] = ((((a0.x + a0.y) + (a0.z + a0.w)) + ((a1.x + a1.y) + (a1.z + a1.w))) +
+            (((a2.x + a2.y) + (a2.z + a2.w)) + ((a3.x + a3.y) + (a3.z + a3.w))));
   }
-  __syncthreads();
-#pragma unroll
-  for (int k = 0; k < 4; ++k) v[k] = red[128 + k];
+  par ^= 1;
 }
 
 // Field of step t into X (real part; zero imaginary, zero beyond Fh x Fw).
@@ -145,13 +222,16 @@ __device__ void load_field(const FftfArgs& a, float2* X, const float* roi_src, c
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
   extern __shared__ float4 smem4[];
-  float2* stw = reinterpret_cast<float2*>(smem4);
+  uint64_t* hbar = reinterpret_cast<uint64_t*>(smem4);   // staging barrier (16 B slot)
+  float2* stw = reinterpret_cast<float2*>(smem4 + 1);
   float2* X = stw + kN;
   float2* Wp = X + kPlane;
   float2* Wq = Wp + kPlane;
-  float* lin = reinterpret_cast<float*>(Wq + kPlane);
+  float2* Hs = Wq + kPlane;                               // staged spectra of one round
+  const bool stage = a.stage != 0;
+  float* red = reinterpret_cast<float*>(Hs + (stage ? 2 * kPlane : 0));   // 160, 16-B aligned
+  float* lin = red + 160;
   float* acc = lin + a.g.P;
-  float* red = acc + a.g.P;      // 160 floats
   const Geo& g = a.g;
   const int tid = threadIdx.x, nt = blockDim.x, b = blockIdx.x;
   const size_t P = (size_t)g.P, M = (size_t)g.M;
@@ -160,11 +240,37 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
   const fft64::Lane Ln = fft64::lane_of(tid);
   int poff[kPixPerThread];
   pixel_offsets(g, tid, poff);
+  // Spectra of round j0 (pairs j0, j0+1) -> Hs: the stored planes already have the on-chip
+  // layout (row stride 66: the column pass reads them without bank conflicts), so they
+  // move as four bulk copies each.  Warp 0, after a barrier that ends the previous readers
+  // of Hs.
+  unsigned huse = 0;
+  auto issue_h = [&](int j0) {
+    if (tid < 32) {
+      const int np = (j0 + 1 < pairs) ? 2 : 1;
+      if (tid == 0) mbar_expect_tx(hbar, np * kPlaneBytes);
+      __syncwarp();
+      fence_proxy_async();
+      if (tid < 4 * np)
+        bulk_g2s(reinterpret_cast<char*>(Hs) + tid * kPlaneChunk,
+                 reinterpret_cast<const char*>(a.H + (size_t)j0 * kPlane) + tid * kPlaneChunk,
+                 kPlaneChunk, hbar);
+    }
+  };
+  if (stage) {
+    if (tid == 0) mbar_init(hbar, 1);
+    __syncthreads();
+    issue_h(0);
+  }
+  int rpar = 0;                  // block_sum4 half
+  FFTF_T0();
 
   for (int t = 0; t < g.d; ++t) {
     const bool last = (t == g.d - 1);
     load_field(a, X, t == 0 ? nullptr : lin, a.inputs + (size_t)b * g.n_in, tid, nt);
+    FFTF_MARK(0, 0);
     fwd2d(X, g.Fh, stw, Ln);
+    FFTF_MARK(0, 1);
     const int act_id = last ? g.fact : g.act;
     const float slope = last ? g.fslope : g.slope;
     for (int p = tid; p < g.P; p += nt) { lin[p] = 0.f; acc[p] = 0.f; }
@@ -172,8 +278,12 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
     // two direction pairs (four planes) per round: independent transforms interleave
     for (int j = 0; j < pairs; j += 2) {
       const bool two = j + 1 < pairs;
-      const float2* Ha = a.H + (size_t)j * kN * kN;
-      const float2* Hb = two ? Ha + kN * kN : Ha;
+      const float2* Ha = a.H + (size_t)j * kPlane;
+      const float2* Hb = two ? Ha + kPlane : Ha;
+      if (stage) {
+        mbar_wait(hbar, huse & 1u);
+        ++huse;
+      }
       // inverse column passes of X^ . H_j and X^ . H_{j+1} (products taken at load time)
       {
         float2 va[8], vb[8];
@@ -181,8 +291,10 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
         for (int n = 0; n < 8; ++n) {
           const int r = Ln.j + 8 * n;
           const float2 x = X[at2(r, Ln.col)];
-          va[n] = cmul(x, __ldg(&Ha[r * kN + Ln.col]));
-          vb[n] = cmul(x, __ldg(&Hb[r * kN + Ln.col]));
+          const float2 ha = stage ? Hs[at2(r, Ln.col)] : __ldg(&Ha[at2(r, Ln.col)]);
+          const float2 hb = stage ? Hs[(two ? kPlane : 0) + at2(r, Ln.col)] : __ldg(&Hb[at2(r, Ln.col)]);
+          va[n] = cmul(x, ha);
+          vb[n] = cmul(x, hb);
         }
         fft64::fft64_lanes<true>(va, Ln.j, stw);
         fft64::fft64_lanes<true>(vb, Ln.j, stw);
@@ -193,9 +305,15 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
         }
       }
       __syncthreads();
+      if (stage) {                       // the next round's spectra land during this round
+        const int nj = (j + 2 < pairs) ? j + 2 : (t + 1 < g.d ? 0 : -1);
+        if (nj >= 0) issue_h(nj);
+      }
+      FFTF_MARK(0, 2);
       // inverse row passes of the ROI rows (warps beyond them skip)
       fft64::pass64x2<false, true>(Wp, Wq, g.roi_h, stw, Ln);
       __syncthreads();
+      FFTF_MARK(0, 3);
       // statistics of planes 2j, 2j+1 (Wp re, im) and 2j+2, 2j+3 (Wq), centred two-pass;
       // thread tid owns pixels p = tid + 512 k
       float mu[4] = {0.f, 0.f, 0.f, 0.f}, rs[4] = {1.f, 1.f, 1.f, 1.f};
@@ -207,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
           const float2 w = Wp[poff[k]], u = Wq[poff[k]];
           mu[0] += w.x; mu[1] += w.y; mu[2] += u.x; mu[3] += u.y;
         }
-        block_sum4(mu, red);
+        block_sum4(mu, red, rpar);
 #pragma unroll
         for (int k = 0; k < 4; ++k) mu[k] *= inv_n;
         float q[4] = {0.f, 0.f, 0.f, 0.f};
@@ -219,10 +337,11 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
           q[0] = fmaf(d0, d0, q[0]); q[1] = fmaf(d1, d1, q[1]);
           q[2] = fmaf(d2, d2, q[2]); q[3] = fmaf(d3, d3, q[3]);
         }
-        block_sum4(q, red);
+        block_sum4(q, red, rpar);
 #pragma unroll
         for (int k = 0; k < 4; ++k) rs[k] = 1.0f / sqrtf(q[k] * inv_n + kNormEps);
       }
+      FFTF_MARK(0, 4);
       const int np = two ? 4 : 2;
       if (a.train && tid < np) a.rstd[((size_t)b * g.d + t) * M + 2 * j + tid] = rs[tid];
       float* zh = a.train ? a.zhat + (((size_t)b * g.d + t) * M + 2 * j) * P : nullptr;
@@ -246,6 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
         acc[p] += ac;
       }
       __syncthreads();
+      FFTF_MARK(0, 5);
     }
     __syncthreads();
 
@@ -281,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
                                               : act_fwd(g.fact, wo * lin[p] + so * acc[p], g.fslope);
       }
     }
+    FFTF_MARK(0, 6);
   }
 }
 
@@ -294,18 +415,22 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   const size_t P = (size_t)g.P, M = (size_t)g.M;
   const int pairs = g.M / 2;
   const int FF = g.Fh * g.Fw;
-  float2* stw = reinterpret_cast<float2*>(smem4);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem4);   // staging barriers: [0] planes, [1] spectra
+  float2* stw = reinterpret_cast<float2*>(smem4 + 1);
   float2* X = stw + kN;
   float2* Wp = X + kPlane;
   float2* D = Wp + kPlane;
-  float* gy = reinterpret_cast<float*>(D + kPlane);
+  const bool stage = a.stage != 0;
+  float2* Hs = D + kPlane;                                // staged spectrum H_j
+  float* red = reinterpret_cast<float*>(Hs + (stage ? kPlane : 0));  // 160, 16-B aligned
+  float* zs = red + 160;                                  // staged planes 2j, 2j+1
+  float* gy = zs + (stage ? 2 * g.P : 0);
   float* gp0 = gy + g.P;
   float* gp1 = gp0 + g.P;
   float* gp2 = gp1 + g.P;
   float* dg = gp2 + g.P;                       // M*K
   float* gport = dg + M * g.K;                 // n_out * M
-  float* red = gport + (size_t)g.n_out * M;    // 160
-  float* ring = red + 160;                     // Fh*Fw when a.gring
+  float* ring = gport + (size_t)g.n_out * M;   // Fh*Fw when a.gring
   int16_t* pmap = reinterpret_cast<int16_t*>(ring + (a.gring ? FF : 0));   // P
   fft64::init_tw64(stw, tid);
   const fft64::Lane Ln = fft64::lane_of(tid);
@@ -313,7 +438,45 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   for (int i = tid; i < (int)(M * g.K); i += nt) dg[i] = 0.f;
   if (a.gring)
     for (int i = tid; i < FF; i += nt) ring[i] = 0.f;
+  if (stage && tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+  }
   __syncthreads();
+  // Saved planes 2j, 2j+1 of step t_ (8P contiguous bytes, P % 4 == 0) -> zs, and the
+  // spectrum H_j -> Hs (stored in the on-chip layout, four bulk copies).  Warp 0, after a barrier that ends the
+  // previous readers of the buffer.  Spectra are staged only for steps t > 0 (the field
+  // adjoint); step 0 needs none.
+  unsigned zuse = 0, huse = 0;
+  auto issue_z = [&](int t_, int j_) {
+    if (tid < 32) {
+      const unsigned bytes = (unsigned)(2 * P * sizeof(float));
+      if (tid == 0) mbar_expect_tx(&bars[0], bytes);
+      __syncwarp();
+      fence_proxy_async();
+      const char* src = reinterpret_cast<const char*>(a.zhat + (((size_t)b * g.d + t_) * M + 2 * j_) * P);
+      constexpr unsigned kChunk = 4096;
+      for (unsigned o = tid * kChunk; o < bytes; o += 32 * kChunk)
+        bulk_g2s(reinterpret_cast<char*>(zs) + o, src + o, min(kChunk, bytes - o), &bars[0]);
+    }
+  };
+  auto issue_h = [&](int j_) {
+    if (tid < 32) {
+      if (tid == 0) mbar_expect_tx(&bars[1], kPlaneBytes);
+      __syncwarp();
+      fence_proxy_async();
+      if (tid < 4)
+        bulk_g2s(reinterpret_cast<char*>(Hs) + tid * kPlaneChunk,
+                 reinterpret_cast<const char*>(a.H + (size_t)j_ * kPlane) + tid * kPlaneChunk,
+                 kPlaneChunk, &bars[1]);
+    }
+  };
+  if (stage) {
+    issue_z(g.d - 1, 0);
+    if (g.d > 1) issue_h(0);
+  }
+  int rpar = 0;                  // block_sum4 half
+  FFTF_T0();
 
   // output step (t = d-1): the port cells' plane gradients and parameter gradients
   // (kernels_pallas.py:1378-1504); universe mode: the last step's cell gradient instead
@@ -356,6 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
     }
   }
   __syncthreads();
+  FFTF_MARK(1, 0);
 
   for (int t = g.d - 1; t >= 0; --t) {
     const bool last = (t == g.d - 1);
@@ -364,6 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
     fwd2d(X, g.Fh, stw, Ln);
     if (t > 0)
       for (int i = tid; i < kPlane; i += nt) D[i] = make_float2(0.f, 0.f);
+    FFTF_MARK(1, 1);
     const float* ZH = a.zhat + ((size_t)b * g.d + t) * M * P;
     const int act_id = last ? g.fact : g.act;     // universe mode runs the last step's ROI
     const float slope = last ? g.fslope : g.slope;  // epilogue with the final activation
@@ -372,6 +537,12 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
       const int m1 = 2 * j, m2 = 2 * j + 1;
       const float* z1 = ZH + (size_t)m1 * P;
       const float* z2 = ZH + (size_t)m2 * P;
+      if (stage) {
+        mbar_wait(&bars[0], zuse & 1u);
+        ++zuse;
+        z1 = zs;
+        z2 = zs + P;
+      }
       const float rs1 = a.rstd[((size_t)b * g.d + t) * M + m1];
       const float rs2 = a.rstd[((size_t)b * g.d + t) * M + m2];
       // plane gradients before the standardisation adjoint at plane positions
@@ -408,8 +579,9 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
         mo[2] += v[k].y;
         mo[3] = fmaf(v[k].y, h2[k], mo[3]);
       }
+      FFTF_MARK(1, 2);
       if (g.norm) {
-        block_sum4(mo, red);
+        block_sum4(mo, red, rpar);
         const float inv_n = 1.0f / (float)g.P;
         const float c11 = mo[0] * inv_n, c21 = mo[1] * inv_n, c12 = mo[2] * inv_n, c22 = mo[3] * inv_n;
 #pragma unroll
@@ -426,10 +598,20 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
         Wp[at2(i >> 6, i & (kN - 1))] = v[k];
       }
       __syncthreads();
+      if (stage) {                       // the next pair's planes land during this pair
+        if (j + 1 < pairs) issue_z(t, j + 1);
+        else if (t > 0) issue_z(t - 1, 0);
+      }
+      FFTF_MARK(1, 3);
       // Q^_j = FFT(gz_{2j} + i gz_{2j+1}): rows of the ROI, then the columns
       fft64::pass64<false, false>(Wp, g.roi_h, stw, Ln);
       __syncthreads();
-      const float2* H = a.H + (size_t)j * kN * kN;
+      FFTF_MARK(1, 4);
+      const float2* H = a.H + (size_t)j * kPlane;
+      if (stage && t > 0) {
+        mbar_wait(&bars[1], huse & 1u);
+        ++huse;
+      }
       {
         float2 q[8];
 #pragma unroll
@@ -439,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           const int r = Ln.j + 8 * n, o = at2(r, Ln.col);
-          if (t > 0) D[o] = cadd(D[o], cmulc(q[n], __ldg(&H[r * kN + Ln.col])));
+          if (t > 0) D[o] = cadd(D[o], cmulc(q[n], stage ? Hs[o] : __ldg(&H[o])));
           q[n] = cmulc(X[o], q[n]);
         }
         // inverse column pass of the product, on the registers just formed
@@ -448,6 +630,11 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
         for (int n = 0; n < 8; ++n) Wp[at2(Ln.j + 8 * n, Ln.col)] = q[n];
       }
       __syncthreads();
+      if (stage) {                       // the next spectrum lands during this pair
+        if (t > 0 && j + 1 < pairs) issue_h(j + 1);
+        else if (j + 1 == pairs && t > 1) issue_h(0);
+      }
+      FFTF_MARK(1, 5);
       // corr(X, gz_{2j}) - i corr(X, gz_{2j+1}) at lags [0, kh) x [0, kw): inverse row pass
       // of the first kh rows (warps beyond them skip), kept in registers
       {
@@ -470,6 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
         }
       }
       __syncthreads();
+      FFTF_MARK(1, 6);
     }
     if (t == 0) break;
 
@@ -496,6 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
       }
     }
     __syncthreads();
+    FFTF_MARK(1, 7);
   }
 
   // per-sample partials; the batch sums run in fixed order afterwards
@@ -507,6 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
     float* gr = a.gring + (size_t)b * FF;
     for (int i = tid; i < FF; i += nt) gr[i] = ring[i];
   }
+  FFTF_MARK(1, 8);
 }
 
 // H_j(w) = conj(G^_{2j}(w)) + i conj(G^_{2j+1}(w)) = F_j(-w) / 64^2 with
@@ -526,11 +716,15 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_pair_spectra_kernel(Geo g, c
                                               : make_float2(0.f, 0.f);
   }
   fwd2d(plane, g.kh, stw, Ln);
-  float2* Hj = H + (size_t)j * kN * kN;
-  for (int i = tid; i < kN * kN; i += nt) {
-    const int r = i / kN, c = i - (i / kN) * kN;
-    const float2 v = plane[at2((kN - r) & (kN - 1), (kN - c) & (kN - 1))];
-    Hj[i] = make_float2(v.x * kInvNN, v.y * kInvNN);
+  float2* Hj = H + (size_t)j * kPlane;             // stored in the on-chip plane layout
+  for (int i = tid; i < kPlane; i += nt) {
+    const int r = i / fft64::kLS, c = i - (i / fft64::kLS) * fft64::kLS;
+    float2 v = make_float2(0.f, 0.f);
+    if (c < kN) {
+      v = plane[at2((kN - r) & (kN - 1), (kN - c) & (kN - 1))];
+      v = make_float2(v.x * kInvNN, v.y * kInvNN);
+    }
+    Hj[i] = v;
   }
 }
 
@@ -543,22 +737,23 @@ nc_status launched(const char* what) {
 
 }  // namespace
 
-size_t fftf_fwd_smem(const Geo& g) {
-  return sizeof(float2) * (kN + 3 * (size_t)kPlane) + sizeof(float) * (2 * (size_t)g.P + 160);
+size_t fftf_fwd_smem(const Geo& g, bool stage) {
+  return 16 + sizeof(float2) * (kN + (3 + (stage ? 2 : 0)) * (size_t)kPlane) +
+         sizeof(float) * (2 * (size_t)g.P + 160);
 }
 
 
-size_t fftf_bwd_smem(const Geo& g, bool ring) {
+size_t fftf_bwd_smem(const Geo& g, bool ring, bool stage) {
   size_t f = 4 * (size_t)g.P + (size_t)g.M * g.K + (size_t)g.n_out * g.M + 160 +
-             (ring ? (size_t)g.Fh * g.Fw : 0);
-  return sizeof(float2) * (kN + 3 * (size_t)kPlane) + sizeof(float) * f + sizeof(int16_t) * (size_t)g.P +
-         16;
+             (ring ? (size_t)g.Fh * g.Fw : 0) + (stage ? 2 * (size_t)g.P : 0);
+  return 16 + sizeof(float2) * (kN + (3 + (stage ? 1 : 0)) * (size_t)kPlane) + sizeof(float) * f +
+         sizeof(int16_t) * (size_t)g.P + 16;
 }
 
 bool fftf_fits(const Geo& g) {
   if (g.Nh != kN || g.Nw != kN || g.M % 2 != 0 || g.P > 32767) return false;
   const bool ring = g.padding == NC_PAD_VALID && g.d > 1;
-  return fftf_fwd_smem(g) <= kFftfSmemMax && fftf_bwd_smem(g, ring) <= kFftfSmemMax;
+  return fftf_fwd_smem(g, false) <= kFftfSmemMax && fftf_bwd_smem(g, ring, false) <= kFftfSmemMax;
 }
 
 nc_status fftf_pair_spectra(const Geo& g, const float* geff, float2* H, cudaStream_t st) {
@@ -566,20 +761,45 @@ nc_status fftf_pair_spectra(const Geo& g, const float* geff, float2* H, cudaStre
   return launched("fftf_pair_spectra_kernel launch");
 }
 
-nc_status fftf_forward(const FftfArgs& a, cudaStream_t st) {
-  const size_t smem = fftf_fwd_smem(a.g);
+nc_status fftf_forward(const FftfArgs& args, cudaStream_t st) {
+  FftfArgs a = args;
+  a.stage = fftf_fwd_smem(a.g, true) <= kFftfSmemMax ? 1 : 0;
+  const size_t smem = fftf_fwd_smem(a.g, a.stage != 0);
   NC_CUDA_CHECK(cudaFuncSetAttribute((const void*)fftf_fwd_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   fftf_fwd_kernel<<<a.batch, kThreads, smem, st>>>(a);
   return launched("fftf_fwd_kernel launch");
 }
 
-nc_status fftf_backward(const FftfArgs& a, cudaStream_t st) {
-  const size_t smem = fftf_bwd_smem(a.g, a.gring != nullptr);
+nc_status fftf_backward(const FftfArgs& args, cudaStream_t st) {
+  FftfArgs a = args;
+  const bool ring = a.gring != nullptr;
+  a.stage = (a.g.P % 4 == 0 && fftf_bwd_smem(a.g, ring, true) <= kFftfSmemMax) ? 1 : 0;
+  const size_t smem = fftf_bwd_smem(a.g, ring, a.stage != 0);
   NC_CUDA_CHECK(cudaFuncSetAttribute((const void*)fftf_bwd_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   fftf_bwd_kernel<<<a.batch, kThreads, smem, st>>>(a);
   return launched("fftf_bwd_kernel launch");
 }
 
+int fftf_device_error(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_fftf_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_fftf_error, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+
 }  // namespace nc
+
+#if NC_PHASE_TIMING
+// Debug builds only: copies (and clears) the fused-FFT phase clocks, 2 x 16 long longs.
+extern "C" int nc_debug_fftf_phases(long long* out) {
+  if (cudaMemcpyFromSymbol(out, nc::g_fftf_phase, sizeof(long long) * 32) != cudaSuccess) return 1;
+  static const long long zero[32] = {};
+  if (cudaMemcpyToSymbol(nc::g_fftf_phase, zero, sizeof(zero)) != cudaSuccess) return 1;
+  return 0;
+}
+#endif

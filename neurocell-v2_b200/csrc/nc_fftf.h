@@ -8,6 +8,7 @@
 namespace nc {
 
 constexpr int kFftfN = 64;                     // the FFT side these kernels are built for
+constexpr int kFftfPlane = 64 * 66;            // float2 per stored plane (row stride 66)
 constexpr size_t kFftfSmemMax = 227 * 1024;    // opt-in dynamic shared memory per CTA
 
 struct FftfArgs {
@@ -16,7 +17,8 @@ struct FftfArgs {
   const int32_t* in_index;
   const int32_t* out_index;
   const float* inputs;        // (B, n_in)
-  const float2* H;            // (M/2, 64, 64) pair spectra conj(G^_2j) + i conj(G^_2j+1), / 64^2
+  const float2* H;            // (M/2, 64, 66) pair spectra conj(G^_2j) + i conj(G^_2j+1), / 64^2,
+                              // rows padded to the on-chip plane layout (columns 64, 65 zero)
   float* out;                 // forward: (B, n_out)
   float* zhat;                // train: (B, d, M, P)
   float* rstd;                // train: (B, d, M)
@@ -29,12 +31,17 @@ struct FftfArgs {
   float* gring;               // backward: (B, Fh*Fw) per-sample ring gradients (VALID, d>1) or null
   float* uroi;                // universe mode forward: (B, P) last-step ROI cells, else null
   const float* guroi;         // universe mode backward: (B, P) their gradient, else null
+  int stage;                  // set by fftf_forward / fftf_backward: bulk-copy staging on
 };
 
 // True when the fused kernels serve this geometry (FFT side 64, even M, fits on chip).
 bool fftf_fits(const Geo& g);
-size_t fftf_fwd_smem(const Geo& g);
-size_t fftf_bwd_smem(const Geo& g, bool ring);
+// Dynamic shared memory of the kernels; `stage` adds the bulk-copy staging buffers.
+size_t fftf_fwd_smem(const Geo& g, bool stage);
+size_t fftf_bwd_smem(const Geo& g, bool ring, bool stage);
+// Sticky error word of the current device: 1 when a bounded wait of the fused kernels for
+// their own bulk copies gave up (that call's results are invalid).  Synchronous.
+int fftf_device_error(bool clear);
 // H_j (natural order) from the effective filters (M, kh, kw).
 nc_status fftf_pair_spectra(const Geo& g, const float* geff, float2* H, cudaStream_t st);
 nc_status fftf_forward(const FftfArgs& a, cudaStream_t st);

@@ -140,7 +140,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
     if (z_smem) *z_smem = true;
     if (gz_smem) *gz_smem = true;
     const size_t c64 = 2 * fl, NN = (size_t)g.Nh * g.Nw;
-    L.f_h = take(c64 * (M / 2) * NN);
+    L.f_h = take(c64 * (M / 2) * (size_t)kFftfPlane);   // planes in the on-chip layout
     L.fscr = L.zscr = L.gzscr = L.gdelta = L.gdeltasum = L.redscr = SIZE_MAX;
     if (train) {
       L.gpix = take(fl * B * 3 * P);

@@ -30,7 +30,7 @@ EXPORTED = (
     "nc_dp_alloc", "nc_dp_free", "nc_ipc_get", "nc_ipc_open", "nc_ipc_close",
     "nc_dp_allreduce_sgd", "nc_dp_status", "nc_launch_count", "nc_conv_path",
     "nc_vnn_forward_universe", "nc_vnn_backward_universe", "nc_universe_embed_forward",
-    "nc_universe_embed_backward",
+    "nc_universe_embed_backward", "nc_device_error",
 )
 NC_DP_MAX_RANKS = 8
 NC_IPC_HANDLE_BYTES = 64
@@ -95,6 +95,7 @@ _SIGS = {
     "nc_abi_version": (_i32, []),
     "nc_launch_count": (ctypes.c_uint64, []),
     "nc_conv_path": (_i32, [_TP]),
+    "nc_device_error": (_i32, [_i32]),
 }
 
 _lib = None

@@ -385,6 +385,12 @@ def propagate(cell_params: torch.Tensor, filters: torch.Tensor, flat_inputs: tor
     return _VNNPropagate.apply(cp, fl, xi, plan, _codd(codd_mode, tau, thr), train)
 
 
+def device_error(clear: bool = True) -> int:
+    """Sticky device error word of the current device (nc_device_error): 0 ok, 1 when a
+    kernel's bounded wait for its own asynchronous copies gave up.  Synchronous."""
+    return int(_lib.load().nc_device_error(1 if clear else 0))
+
+
 def codd_states(s_raw: torch.Tensor, io_state_mask, hard_pin_io, codd_mode, tau, thr) -> torch.Tensor:
     """Codd gating of a raw state field through ``nc_codd_states``."""
     _require_cuda(s_raw, "s_raw")

@@ -545,3 +545,10 @@ def test_adaptive_sub_roi_universe_outputs_outside_window(backend, mode, final):
     cell, filt, ins, _ = random_problem(geom, 3, 171)
     _sub_roi_universe_case(geom, O.Config(final_activate=final), cell, filt, ins, (6, 20, 6, 22),
                            backend, 172)
+
+
+def test_zz_no_bounded_wait_gave_up():
+    """Runs after the parity tests of this module: no kernel's bounded wait for its own
+    bulk copies into shared memory timed out (nc_device_error)."""
+    torch.cuda.synchronize()
+    assert nc.ops.device_error() == 0
