@@ -284,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
         mbar_wait(hbar, huse & 1u);
         ++huse;
       }
+      FFTF_MARK(0, 7);
       // inverse column passes of X^ . H_j and X^ . H_{j+1} (products taken at load time)
       {
         float2 va[8], vb[8];
@@ -543,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
         z1 = zs;
         z2 = zs + P;
       }
+      FFTF_MARK(1, 9);
       const float rs1 = a.rstd[((size_t)b * g.d + t) * M + m1];
       const float rs2 = a.rstd[((size_t)b * g.d + t) * M + m2];
       // plane gradients before the standardisation adjoint at plane positions
@@ -612,6 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
         mbar_wait(&bars[1], huse & 1u);
         ++huse;
       }
+      FFTF_MARK(1, 10);
       {
         float2 q[8];
 #pragma unroll
