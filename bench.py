@@ -436,23 +436,43 @@ def config_problem(cfg: int, batch: int, seed_rank: int):
 
 
 def run_config(args) -> None:
-    """One GPU, one BASELINE config other than 0: CUDA-graph replays of the step with the L2
-    flushed before each, CUDA events; prints one JSON line (not the driver's bench line)."""
+    """A BASELINE config other than 0 (secondary line, not the driver's bench line): CUDA-graph
+    replays of the step with the L2 flushed before each, CUDA events, max over ranks.  Under
+    torchrun the ranks train data-parallel with the gradient exchange in the graph: configs 2
+    and 3 keep their batch per GPU (weak scaling), config 4 shards its batch of 16 over the
+    GPUs (strong scaling, as BASELINE states); config 1 (inference) runs one replica per GPU."""
     import ctypes
+    import torch.distributed as dist
     import neurocell_b200 as nc
     from neurocell_b200 import _lib, ops
     cfg = args.config
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    B = {1: 8192, 2: 64, 3: 256, 4: 16}[cfg]
-    topo, shapes, cell, filt, x, y, meta = config_problem(cfg, B, 0)
+    pg = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+        pg = dist.group.WORLD
+    B_total = {1: 8192, 2: 64, 3: 256, 4: 16}[cfg]
+    strong = cfg == 4
+    if strong and B_total % world != 0:
+        raise SystemExit(f"config 4 shards its batch of {B_total}; --gpus must divide it")
+    B = B_total // world if strong else B_total
+    topo, shapes, cell, filt, x, y, meta = config_problem(cfg, B, rank)
+    if meta["train"]:
+        cell, filt = config_problem(cfg, 1, 0)[2:4]       # every rank starts from the same params
     lib = _lib.load()
     conv = args.conv
     if meta["train"]:
         runner = nc.trainer.VNNTrainStep(
             topo, nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev)), B,
             lr=LR, loss=meta["loss"], codd_mode=meta["codd_mode"], in_shapes=shapes, conv=conv,
-            state_temperature=1.0)
+            state_temperature=1.0, process_group=pg, exchange=args.exchange)
         runner.load_batch(torch.tensor(x, device=dev), torch.tensor(y, device=dev))
         step = runner.step
         if not args.no_graph:
@@ -495,9 +515,12 @@ def run_config(args) -> None:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+        torch.cuda.synchronize()
     K = args.steps
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    clocks = ClockSampler(0)
+    clocks = ClockSampler(local)
     for i in range(K):
         l2_flush.fill_(float(i))
         ev[i][0].record()
@@ -506,6 +529,10 @@ def run_config(args) -> None:
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+    if pg is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     M, P, Kk, d = meta["M"], meta["P"], meta["K"], meta["d"]
     passes = (3 * d - 1) if meta["train"] else d
     flops = 2.0 * M * P * Kk * passes * B
@@ -523,16 +550,27 @@ def run_config(args) -> None:
                 "model": "effective direct-convolution FLOPs 2*M*P*K per pass"}
     what = "train" if meta["train"] else "inference"
     line = {
-        "metric": f"{what} samples/s (BASELINE config {cfg})", "value": B / (ms * 1e-3),
-        "unit": "samples/s", "n_gpus": 1, "steps": K, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "dtype": "f32", "data": "synthetic (seeded numpy, config shapes)",
-        "config": {"workload": f"BASELINE config {cfg}", "batch": B, "conv": conv,
-                   "codd_mode": meta["codd_mode"], "cuda_graph": not args.no_graph,
+        "metric": f"{what} samples/s (BASELINE config {cfg})", "value": B * world / (ms * 1e-3),
+        "unit": "samples/s", "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong" if strong else "weak",
+        "dtype": "f32", "data": "synthetic (seeded numpy, config shapes)",
+        "config": {"workload": f"BASELINE config {cfg}", "batch_per_gpu": B,
+                   "global_batch": B * world, "conv": conv, "codd_mode": meta["codd_mode"],
+                   "cuda_graph": not args.no_graph,
+                   "parallelism": (f"dp{world}" if meta["train"] else f"{world} replicas"),
+                   "grad_exchange": (args.exchange if world > 1 and meta["train"] else "none"),
                    "l2": "flushed (256 MB write) before every timed step"},
         "effective_tflops": flops / (ms * 1e-3) / 1e12, "roofline": roof, "clocks": clk,
         "gpu_launches_per_step": runner.launches_per_step() if meta["train"] else n_launch,
     }
-    print(json.dumps(line), flush=True)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if meta["train"]:
+        runner.release()           # graphs holding exchange calls and the IPC maps go first
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():
@@ -547,7 +585,7 @@ def main():
                     help="data-parallel gradient exchange for --gpus > 1: the fused NVLink "
                          "peer-memory sum + SGD kernel (default) or NCCL all-reduce + SGD")
     ap.add_argument("--config", type=int, choices=(0, 1, 2, 3, 4), default=0,
-                    help="BASELINE config; 1-4 print a secondary single-GPU line")
+                    help="BASELINE config; 1-4 print a secondary line (data parallel under torchrun)")
     ap.add_argument("--adaptive", action="store_true",
                     help="config 0 on the adaptive sub-ROI of a freshly initialised chip "
                          "(secondary measurement)")
