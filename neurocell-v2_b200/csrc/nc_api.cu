@@ -330,11 +330,25 @@ nc_status nc_plan_build(const nc_topo* topo, const int32_t* in_index, const int3
     return set_error(NC_ERR_WORKSPACE, "plan buffer too small: %zu < %zu", plan_bytes, PL.total);
   if ((g.n_in > 0 && !in_index) || !out_index || !io_mask || !out_w_mask)
     return set_error(NC_ERR_INVALID, "null plan table");
-  // FFT stage twiddles exp(-2 pi i q j / S), stage by stage (layout: nc_fft.cuh)
+  // FFT line twiddles (layouts: nc_fft.cuh): two-stage plans (64 <= N <= 1024) take
+  // exp(-2 pi i n2 k1 / N) at [k1 * 64 + n2] then exp(-2 pi i e / 64); radix-4 plans take
+  // exp(-2 pi i q j / S) stage by stage
   std::vector<float2> tw[2];
   if (PL.twid_w != SIZE_MAX) {
     for (int side = 0; side < 2; ++side) {
       const int N = side == 0 ? g.Nw : g.Nh;
+      if (fft::two_stage(N)) {
+        for (int k1 = 0; k1 < N / 64; ++k1)
+          for (int n2 = 0; n2 < 64; ++n2) {
+            const double a = -2.0 * M_PI * (double)n2 * (double)k1 / (double)N;
+            tw[side].push_back(make_float2((float)std::cos(a), (float)std::sin(a)));
+          }
+        for (int e = 0; e < 64; ++e) {
+          const double a = -2.0 * M_PI * (double)e / 64.0;
+          tw[side].push_back(make_float2((float)std::cos(a), (float)std::sin(a)));
+        }
+        continue;
+      }
       for (int S = N; S > 1;) {
         const int R = fft::stage_radix(S), h = S / R;
         for (int q = 1; q < R; ++q)

@@ -308,4 +308,172 @@ __device__ __forceinline__ void init_tw64(float2* tw64, int tid) {
 }
 
 }  // namespace fft64
+
+// ---------------------------------------------------------------------------------------
+// Two-stage line transforms for N = 64 * R, R in {1, 2, 4, 8, 16} (64 <= N <= 1024): the
+// lines of the per-step FFT regime (nc_fftconv.cu) in two passes through shared memory
+// instead of log4(N) radix-4 passes.
+//
+// With n = n2 + 64 n1 and f = k1 + R k2 (n2, k2 < 64; n1, k1 < R):
+//   X[k1 + R k2] = sum_n2 w64^(n2 k2) * ( wN^(n2 k1) * sum_n1 x[n2 + 64 n1] wR^(n1 k1) ).
+// Stage A: one thread per (line, n2) does the radix-R DFT over n1 in registers, multiplies
+// by wN^(n2 k1) and stores y[k1][n2] at position 64 k1 + n2.  Stage B: the 64-point DFT of
+// each block k1 over n2 on 8 lanes (fft64::fft64_lanes), stored at 64 k1 + k2.  Position
+// 64 k1 + k2 of a line therefore holds frequency k1 + R k2: a fixed permutation shared by
+// every spectrum of the plan (products are pointwise), which the inverse -- the exact
+// adjoint, stage B then stage A with conjugate roots -- takes back to natural order.
+//
+// Twiddles (plan table, built on the host in double precision): [k1 * 64 + n2] =
+// exp(-2 pi i n2 k1 / N) for k1 < R, n2 < 64, then exp(-2 pi i e / 64) for e < 64.
+// ---------------------------------------------------------------------------------------
+namespace fft {
+
+__host__ __device__ inline bool two_stage(int N) { return N >= 64 && N <= 1024; }
+
+// Plan twiddle entries for an N-point line transform.
+__host__ __device__ inline int plan_twiddle_len(int N) {
+  return two_stage(N) ? N + 64 : twiddle_table_len(N);
+}
+
+// y[k] = sum_n a[n] wR^(n k), wR = exp(-+2 pi i / R); natural order in and out.
+template <int R, bool INV>
+__device__ __forceinline__ void dft_r(float2* a) {
+  if constexpr (R == 2) {
+    const float2 t = a[1];
+    a[1] = csub(a[0], t);
+    a[0] = cadd(a[0], t);
+  } else if constexpr (R == 4) {
+    // w4 = -i (forward) / +i (inverse)
+    const float2 t0 = cadd(a[0], a[2]), t1 = csub(a[0], a[2]);
+    const float2 t2 = cadd(a[1], a[3]), t3 = csub(a[1], a[3]);
+    const float2 jt3 = INV ? make_float2(-t3.y, t3.x) : make_float2(t3.y, -t3.x);   // t3 * w4
+    a[0] = cadd(t0, t2);
+    a[2] = csub(t0, t2);
+    a[1] = cadd(t1, jt3);
+    a[3] = csub(t1, jt3);
+  } else if constexpr (R == 8) {
+    fft64::dft8<INV>(a);
+  } else if constexpr (R == 16) {
+    // n = n1 + 4 n2, k = k1 + 4 k2:  X[k1 + 4 k2] = sum_n1 w4^(n1 k2) w16^(n1 k1)
+    //                                 * sum_n2 x[n1 + 4 n2] w4^(n2 k1)
+    float2 b[16];
+#pragma unroll
+    for (int n1 = 0; n1 < 4; ++n1) {
+      float2 q[4] = {a[n1], a[n1 + 4], a[n1 + 8], a[n1 + 12]};
+      dft_r<4, INV>(q);
+#pragma unroll
+      for (int k1 = 0; k1 < 4; ++k1) {
+        float2 v = q[k1];
+        const int e = n1 * k1;                        // w16^e, e < 10
+        if (e != 0) {
+          // cos(2 pi e / 16), sin(2 pi e / 16)
+          constexpr float c1 = 0.92387953251128674f, s1 = 0.38268343236508978f;
+          constexpr float h = 0.70710678118654752f;
+          constexpr float kc[10] = {1.f, c1, h, s1, 0.f, -s1, -h, -c1, -1.f, -c1};
+          constexpr float ks[10] = {0.f, s1, h, c1, 1.f, c1, h, s1, 0.f, -s1};
+          v = cmul(v, make_float2(kc[e], INV ? ks[e] : -ks[e]));
+        }
+        b[n1 * 4 + k1] = v;
+      }
+    }
+#pragma unroll
+    for (int k1 = 0; k1 < 4; ++k1) {
+      float2 q[4] = {b[k1], b[4 + k1], b[8 + k1], b[12 + k1]};
+      dft_r<4, INV>(q);
+#pragma unroll
+      for (int k2 = 0; k2 < 4; ++k2) a[k1 + 4 * k2] = q[k2];
+    }
+  }
+}
+
+// Stage A over all lines (see above); R == 1 is the identity.
+template <int R, bool INV>
+__device__ __forceinline__ void stage_a(float2* s, int L, int LS, const float2* twA, int tid, int nt) {
+  for (int task = tid; task < L * 64; task += nt) {
+    const int l = task >> 6, n2 = task & 63;
+    float2* sl = s + l * LS;
+    float2 v[R];
+    if (!INV) {
+#pragma unroll
+      for (int n1 = 0; n1 < R; ++n1) v[n1] = sl[pidx(n2 + 64 * n1)];
+      dft_r<R, false>(v);
+#pragma unroll
+      for (int k1 = 1; k1 < R; ++k1) v[k1] = cmul(v[k1], twA[k1 * 64 + n2]);
+#pragma unroll
+      for (int k1 = 0; k1 < R; ++k1) sl[pidx(64 * k1 + n2)] = v[k1];
+    } else {
+#pragma unroll
+      for (int k1 = 0; k1 < R; ++k1) v[k1] = sl[pidx(64 * k1 + n2)];
+#pragma unroll
+      for (int k1 = 1; k1 < R; ++k1) v[k1] = cmulc(v[k1], twA[k1 * 64 + n2]);
+      dft_r<R, true>(v);
+#pragma unroll
+      for (int n1 = 0; n1 < R; ++n1) sl[pidx(n2 + 64 * n1)] = v[n1];
+    }
+  }
+}
+
+// Stage B: 64-point transforms of the L * R blocks, 8 lanes per block, four per warp.
+// The loop bound is warp-uniform (the shuffles need whole warps).
+template <bool INV>
+__device__ __forceinline__ void stage_b(float2* s, int L, int R, int LS, const float2* tw64, int tid,
+                                        int nt) {
+  const int lane = tid & 31, j = lane & 7;
+  const int nblk = L * R, quads = (nblk + 3) >> 2;
+  for (int q = tid >> 5; q < quads; q += nt >> 5) {
+    const int blk = 4 * q + (lane >> 3);
+    const bool active = blk < nblk;
+    const int l = active ? blk / R : 0, k1 = active ? blk - (blk / R) * R : 0;
+    float2* sb = s + l * LS;
+    float2 v[8];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) v[n] = active ? sb[pidx(64 * k1 + j + 8 * n)] : make_float2(0.f, 0.f);
+    fft64::fft64_lanes<INV>(v, j, tw64);
+    if (active) {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) sb[pidx(64 * k1 + j + 8 * n)] = v[n];
+    }
+  }
+}
+
+template <bool INV>
+__device__ void transform_lines_2s(float2* s, int L, int N, const float2* tw, int tid, int nt) {
+  const int R = N >> 6, LS = line_stride(N);
+  const float2* tw64 = tw + N;
+  __syncthreads();
+  if (!INV) {
+    switch (R) {
+      case 2: stage_a<2, false>(s, L, LS, tw, tid, nt); break;
+      case 4: stage_a<4, false>(s, L, LS, tw, tid, nt); break;
+      case 8: stage_a<8, false>(s, L, LS, tw, tid, nt); break;
+      case 16: stage_a<16, false>(s, L, LS, tw, tid, nt); break;
+      default: break;
+    }
+    if (R > 1) __syncthreads();
+    stage_b<false>(s, L, R, LS, tw64, tid, nt);
+  } else {
+    stage_b<true>(s, L, R, LS, tw64, tid, nt);
+    if (R > 1) __syncthreads();
+    switch (R) {
+      case 2: stage_a<2, true>(s, L, LS, tw, tid, nt); break;
+      case 4: stage_a<4, true>(s, L, LS, tw, tid, nt); break;
+      case 8: stage_a<8, true>(s, L, LS, tw, tid, nt); break;
+      case 16: stage_a<16, true>(s, L, LS, tw, tid, nt); break;
+      default: break;
+    }
+  }
+  __syncthreads();
+}
+
+// The line transform of the plan for N: two-stage for 64 <= N <= 1024, radix-4 otherwise.
+// Starts after and ends with a __syncthreads().
+template <bool INV>
+__device__ void transform_lines_plan(float2* s, int L, int N, const float2* tw, int tid, int nt) {
+  if (two_stage(N))
+    transform_lines_2s<INV>(s, L, N, tw, tid, nt);
+  else
+    transform_lines<INV>(s, L, N, tw, tid, nt);
+}
+
+}  // namespace fft
 }  // namespace nc

@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(kFftThreads) rows_fwd_kernel(Planes a, float2*
                                                                 int N, const float2* __restrict__ tw,
                                                                 int L) {
   extern __shared__ float2 sm[];
-  const int TN = fft::twiddle_table_len(N);
+  const int TN = fft::plan_twiddle_len(N);
   float2* stw = sm;
   float2* s = sm + even_up(TN);
   const int LS = line_stride(N), lgN = fft::ilog2(N);
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(kFftThreads) rows_fwd_kernel(Planes a, float2*
     }
     s[l * LS + pidx(e)] = make_float2(re, im);
   }
-  fft::transform_lines<false>(s, nl, N, stw, tid, nt);
+  fft::transform_lines_plan<false>(s, nl, N, stw, tid, nt);
   for (int idx = tid; idx < nl * N; idx += nt) {
     const int l = idx >> lgN, e = idx & (N - 1);
     dst[(size_t)(line0 + l) * N + e] = s[l * LS + pidx(e)];
@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(kFftThreads) rows_inv_kernel(const float2* __r
                                                                 const float2* __restrict__ tw,
                                                                 int L) {
   extern __shared__ float2 sm[];
-  const int TN = fft::twiddle_table_len(N);
+  const int TN = fft::plan_twiddle_len(N);
   float2* stw = sm;
   float2* s = sm + even_up(TN);
   const int LS = line_stride(N), lgN = fft::ilog2(N);
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kFftThreads) rows_inv_kernel(const float2* __r
     const int l = idx >> lgN, e = idx & (N - 1);
     s[l * LS + pidx(e)] = src[(size_t)(line0 + l) * N + e];
   }
-  fft::transform_lines<true>(s, nl, N, stw, tid, nt);
+  fft::transform_lines_plan<true>(s, nl, N, stw, tid, nt);
   for (int idx = tid; idx < nl * a.cols; idx += nt) {
     const int l = idx / a.cols, e = idx - l * a.cols;
     const int line = line0 + l;
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kFftThreads) cols_kernel(ColArgs a, const floa
                                                             int C) {
   extern __shared__ float2 sm[];
   const int N = a.Nh;
-  const int TN = fft::twiddle_table_len(N);
+  const int TN = fft::plan_twiddle_len(N);
   float2* stw = sm;
   float2* s = sm + even_up(TN);
   const int LS = line_stride(N), lgC = fft::ilog2(C);
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(kFftThreads) cols_kernel(ColArgs a, const floa
     }
     s[cc * LS + pidx(r)] = v;
   }
-  fft::transform_lines<MODE != COL_FWD>(s, C, N, stw, tid, nt);
+  fft::transform_lines_plan<MODE != COL_FWD>(s, C, N, stw, tid, nt);
   const int rows_st = (MODE == COL_FWD) ? N : a.rows_out;
   for (int idx = tid; idx < rows_st * C; idx += nt) {
     const int r = idx >> lgC, cc = idx & (C - 1);
@@ -512,7 +512,7 @@ int rows_per_cta(int N) {
 }
 
 size_t rows_smem(int N, int L) {
-  const int TN = fft::twiddle_table_len(N);
+  const int TN = fft::plan_twiddle_len(N);
   return sizeof(float2) * ((size_t)((TN + 1) & ~1) + (size_t)L * line_stride(N));
 }
 
@@ -522,7 +522,7 @@ int cols_per_cta(int Nh, int Nw) {
 }
 
 size_t cols_smem(int Nh, int C) {
-  const int TN = fft::twiddle_table_len(Nh);
+  const int TN = fft::plan_twiddle_len(Nh);
   return sizeof(float2) * ((size_t)((TN + 1) & ~1) + (size_t)C * line_stride(Nh));
 }
 

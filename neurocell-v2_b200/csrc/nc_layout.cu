@@ -4,6 +4,7 @@
 
 #include "nc_internal.h"
 #include "nc_errors.h"
+#include "nc_fft.cuh"
 #include "nc_fftf.h"
 
 namespace nc {
@@ -89,8 +90,8 @@ PlanLayout plan_layout(const nc_topo* t) {
   L.border_mask = o; o = align256(o + (size_t)t->H * t->W);
   Geo g;
   if (make_geo(t, &g) == NC_OK && g.algo == NC_CONV_FFT) {
-    L.twid_w = o; o = align256(o + 8 * (size_t)g.Nw);
-    L.twid_h = o; o = align256(o + 8 * (size_t)g.Nh);
+    L.twid_w = o; o = align256(o + 8 * (size_t)fft::plan_twiddle_len(g.Nw));
+    L.twid_h = o; o = align256(o + 8 * (size_t)fft::plan_twiddle_len(g.Nh));
   } else {
     L.twid_w = L.twid_h = SIZE_MAX;
   }

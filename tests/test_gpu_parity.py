@@ -552,3 +552,20 @@ def test_zz_no_bounded_wait_gave_up():
     bulk copies into shared memory timed out (nc_device_error)."""
     torch.cuda.synchronize()
     assert nc.ops.device_error() == 0
+
+
+# ---- two-stage line transforms of the FFT regime (N = 64 R: 128 .. 1024) ----------------
+@pytest.mark.parametrize("grid,kernel,mode", [
+    ((160, 160), (31, 31), "VALID"),     # N = 256 x 256 (R = 4)
+    ((300, 100), (9, 9), "VALID"),       # N = 512 x 128 (R = 8 rows, R = 2 columns)
+    ((280, 20), (17, 5), "SAME"),        # N = 512 x 32: two-stage rows, radix-4 columns
+    ((600, 60), (25, 5), "VALID"),       # N = 1024 x 64 (R = 16, R = 1)
+])
+def test_fft_two_stage_line_transforms_parity(grid, kernel, mode):
+    H, W = grid
+    r0 = H // 2 - 2
+    geom = O.make_geometry(grid, kernel, 4, 2, (O.CoordPort(tuple((r, W // 3) for r in range(r0, r0 + 4))),),
+                           O.CoordPort(tuple((r, 2 * W // 3) for r in range(r0, r0 + 3))), padding_mode=mode)
+    cell, filt, ins, y = random_problem(geom, 2, 181)
+    check_case(geom, O.Config(codd_mode="ste_ternary", state_temperature=0.5), cell, filt, ins, y,
+               backend="pallas_sram")
