@@ -38,6 +38,7 @@ namespace {
 
 constexpr int kFftThreads = 256;
 constexpr int kEpiThreads = 256;
+constexpr int kStatThreads = 512;      // per-plane statistics kernels
 
 // Real planes addressed as  base + b*sstride + m*plane + r*rs + e.
 struct Planes {
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(kFftThreads) rows_fwd_kernel(Planes a, float2*
   fft::transform_lines_plan<false>(s, nl, N, stw, tid, nt);
   for (int idx = tid; idx < nl * N; idx += nt) {
     const int l = idx >> lgN, e = idx & (N - 1);
-    dst[(size_t)(line0 + l) * N + e] = s[l * LS + pidx(e)];
+    __stcs(&dst[(size_t)(line0 + l) * N + e], s[l * LS + pidx(e)]);   // read once
   }
 }
 
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(kFftThreads) rows_inv_kernel(const float2* __r
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
   for (int idx = tid; idx < nl * N; idx += nt) {
     const int l = idx >> lgN, e = idx & (N - 1);
-    s[l * LS + pidx(e)] = src[(size_t)(line0 + l) * N + e];
+    s[l * LS + pidx(e)] = __ldcs(&src[(size_t)(line0 + l) * N + e]);   // last use
   }
   fft::transform_lines_plan<true>(s, nl, N, stw, tid, nt);
   for (int idx = tid; idx < nl * a.cols; idx += nt) {
@@ -151,7 +152,7 @@ __global__ void __launch_bounds__(kFftThreads) cols_kernel(ColArgs a, const floa
     float2 v = make_float2(0.f, 0.f);
     if (MODE == COL_FWD || MODE == COL_INV_PLAIN) {
       if (r < a.rows_in) {
-        v = a.src[((size_t)u * a.rows_in + r) * a.Nw + c];
+        v = __ldcs(&a.src[((size_t)u * a.rows_in + r) * a.Nw + c]);   // last use
         if (MODE == COL_FWD) { v.x *= a.scale; v.y *= a.scale; }
       }
     } else if (MODE == COL_INV_MULCONJ) {
@@ -169,7 +170,9 @@ __global__ void __launch_bounds__(kFftThreads) cols_kernel(ColArgs a, const floa
   const int rows_st = (MODE == COL_FWD) ? N : a.rows_out;
   for (int idx = tid; idx < rows_st * C; idx += nt) {
     const int r = idx >> lgC, cc = idx & (C - 1);
-    a.dst[((size_t)u * rows_st + r) * a.Nw + c0 + cc] = s[cc * LS + pidx(r)];
+    float2* o = &a.dst[((size_t)u * rows_st + r) * a.Nw + c0 + cc];
+    if (MODE == COL_FWD) *o = s[cc * LS + pidx(r)];     // spectra: reused
+    else __stcs(o, s[cc * LS + pidx(r)]);              // read once by the row pass
   }
 }
 
@@ -181,7 +184,8 @@ __global__ void dg_accum_kernel(const float2* __restrict__ xhat, const float2* _
   const int m = (int)(i / NN);
   const size_t f = i - (size_t)m * NN;
   float2 s = init ? make_float2(0.f, 0.f) : acc[i];
-  for (int p = 0; p < pairs; ++p) s = cadd(s, cmulc(xhat[(size_t)p * NN + f], q[((size_t)p * M + m) * NN + f]));
+#pragma unroll 8
+  for (int p = 0; p < pairs; ++p) s = cadd(s, cmulc(__ldg(&xhat[(size_t)p * NN + f]), q[((size_t)p * M + m) * NN + f]));
   acc[i] = s;
 }
 
@@ -250,31 +254,65 @@ __global__ void field_interior_kernel(Geo g, float* __restrict__ field, const fl
 // forward epilogues (planes z at z + b*zs + m*P)
 // ---------------------------------------------------------------------------------------
 
-// Per-(b, m) mean and 1/sqrt(var + eps), centred two-pass (kernels_pallas.py:200-205).
-__global__ void __launch_bounds__(kEpiThreads) plane_stats_kernel(Geo g, const float* __restrict__ z,
-                                                                   size_t zs, float* mean, float* rstd,
-                                                                   float* rstd_save, int t) {
-  __shared__ float red[33];
-  const int bm = blockIdx.x, b = bm / g.M, m = bm - b * g.M;
-  const float* zp = z + (size_t)b * zs + (size_t)m * g.P;
-  float mu = 0.f, rs = 1.f;
-  if (g.norm) {
-    const float inv_n = 1.0f / (float)g.P;
-    float s = 0.f;
-    for (int p = threadIdx.x; p < g.P; p += blockDim.x) s += zp[p];
-    mu = block_sum(s, red) * inv_n;
-    float v = 0.f;
-    for (int p = threadIdx.x; p < g.P; p += blockDim.x) {
-      const float dz = zp[p] - mu;
-      v = fmaf(dz, dz, v);
+// Plane sums for the per-(b, m) statistics: float4 loads with four independent partial
+// sums when `vec` (P % 4 == 0 and 16-byte aligned planes), then a fixed-order combination,
+// so every call adds in the same order.
+__device__ __forceinline__ float plane_sum(const float* __restrict__ a, int P, int vec) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (vec) {
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    for (int i = threadIdx.x; i < P / 4; i += blockDim.x) {
+      const float4 v = a4[i];
+      s0 += v.x; s1 += v.y; s2 += v.z; s3 += v.w;
     }
-    const float var = block_sum(v, red) * inv_n;
-    rs = 1.0f / sqrtf(var + kNormEps);
+  } else {
+    for (int p = threadIdx.x; p < P; p += blockDim.x) s0 += a[p];
   }
-  if (threadIdx.x == 0) {
-    mean[bm] = mu;
-    rstd[bm] = rs;
-    if (rstd_save) rstd_save[((size_t)b * g.d + t) * g.M + m] = rs;
+  return (s0 + s1) + (s2 + s3);
+}
+
+// sum (a - mu)^2 over the plane (centred second pass).
+__device__ __forceinline__ float plane_sq(const float* __restrict__ a, int P, float mu, int vec) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (vec) {
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    for (int i = threadIdx.x; i < P / 4; i += blockDim.x) {
+      const float4 v = a4[i];
+      const float d0 = v.x - mu, d1 = v.y - mu, d2 = v.z - mu, d3 = v.w - mu;
+      s0 = fmaf(d0, d0, s0); s1 = fmaf(d1, d1, s1); s2 = fmaf(d2, d2, s2); s3 = fmaf(d3, d3, s3);
+    }
+  } else {
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+      const float d = a[p] - mu;
+      s0 = fmaf(d, d, s0);
+    }
+  }
+  return (s0 + s1) + (s2 + s3);
+}
+
+// Per-(b, m) mean and 1/sqrt(var + eps), centred two-pass (kernels_pallas.py:200-205).  The
+// grid covers a bounded number of planes at a time (2 CTAs per SM, each looping over
+// planes), so a plane's second pass reads it back from L2 rather than HBM.
+__global__ void __launch_bounds__(kStatThreads) plane_stats_kernel(Geo g, const float* __restrict__ z,
+                                                                   size_t zs, float* mean, float* rstd,
+                                                                   float* rstd_save, int t, int nplanes,
+                                                                   int vec) {
+  __shared__ float red[33];
+  for (int bm = blockIdx.x; bm < nplanes; bm += gridDim.x) {
+    const int b = bm / g.M, m = bm - b * g.M;
+    const float* zp = z + (size_t)b * zs + (size_t)m * g.P;
+    float mu = 0.f, rs = 1.f;
+    if (g.norm) {
+      const float inv_n = 1.0f / (float)g.P;
+      mu = block_sum(plane_sum(zp, g.P, vec), red) * inv_n;
+      const float var = block_sum(plane_sq(zp, g.P, mu, vec), red) * inv_n;
+      rs = 1.0f / sqrtf(var + kNormEps);
+    }
+    if (threadIdx.x == 0) {
+      mean[bm] = mu;
+      rstd[bm] = rs;
+      if (rstd_save) rstd_save[((size_t)b * g.d + t) * g.M + m] = rs;
+    }
   }
 }
 
@@ -402,24 +440,53 @@ __global__ void port_gz_kernel(Geo g, StepParams sp, const int32_t* __restrict__
 }
 
 // Standardisation adjoint per (b, m): gz <- rstd (gz - mean(gz) - zh mean(gz zh)).
-__global__ void __launch_bounds__(kEpiThreads) norm_bwd_kernel(Geo g, float* __restrict__ gz,
-                                                                const float* __restrict__ zh_t, size_t zs,
-                                                                const float* __restrict__ rstd_save, int t) {
+__global__ void __launch_bounds__(kStatThreads) norm_bwd_kernel(Geo g, float* __restrict__ gz,
+                                                                 const float* __restrict__ zh_t, size_t zs,
+                                                                 const float* __restrict__ rstd_save, int t,
+                                                                 int nplanes, int vec) {
   __shared__ float red[33];
-  const int bm = blockIdx.x, b = bm / g.M, m = bm - b * g.M;
-  float* gp = gz + (size_t)bm * g.P;
-  const float* zp = zh_t + (size_t)b * zs + (size_t)m * g.P;
   const float inv_n = 1.0f / (float)g.P;
-  float s1 = 0.f, s2 = 0.f;
-  for (int p = threadIdx.x; p < g.P; p += blockDim.x) {
-    const float v = gp[p];
-    s1 += v;
-    s2 = fmaf(v, zp[p], s2);
+  for (int bm = blockIdx.x; bm < nplanes; bm += gridDim.x) {
+    const int b = bm / g.M, m = bm - b * g.M;
+    float* gp = gz + (size_t)bm * g.P;
+    const float* zp = zh_t + (size_t)b * zs + (size_t)m * g.P;
+    float s1 = 0.f, s2 = 0.f, u1 = 0.f, u2 = 0.f;
+    if (vec) {
+      const float4* g4 = reinterpret_cast<const float4*>(gp);
+      const float4* z4 = reinterpret_cast<const float4*>(zp);
+      for (int i = threadIdx.x; i < g.P / 4; i += blockDim.x) {
+        const float4 v = g4[i], w = z4[i];
+        s1 += v.x + v.y;
+        u1 += v.z + v.w;
+        s2 = fmaf(v.x, w.x, fmaf(v.y, w.y, s2));
+        u2 = fmaf(v.z, w.z, fmaf(v.w, w.w, u2));
+      }
+    } else {
+      for (int p = threadIdx.x; p < g.P; p += blockDim.x) {
+        const float v = gp[p];
+        s1 += v;
+        s2 = fmaf(v, zp[p], s2);
+      }
+    }
+    const float c1 = block_sum(s1 + u1, red) * inv_n;
+    const float c2 = block_sum(s2 + u2, red) * inv_n;
+    const float rs = rstd_save[((size_t)b * g.d + t) * g.M + m];
+    if (vec) {
+      float4* g4 = reinterpret_cast<float4*>(gp);
+      const float4* z4 = reinterpret_cast<const float4*>(zp);
+      for (int i = threadIdx.x; i < g.P / 4; i += blockDim.x) {
+        float4 v = g4[i];
+        const float4 w = z4[i];
+        v.x = rs * (v.x - c1 - w.x * c2);
+        v.y = rs * (v.y - c1 - w.y * c2);
+        v.z = rs * (v.z - c1 - w.z * c2);
+        v.w = rs * (v.w - c1 - w.w * c2);
+        g4[i] = v;
+      }
+    } else {
+      for (int p = threadIdx.x; p < g.P; p += blockDim.x) gp[p] = rs * (gp[p] - c1 - zp[p] * c2);
+    }
   }
-  const float c1 = block_sum(s1, red) * inv_n;
-  const float c2 = block_sum(s2, red) * inv_n;
-  const float rs = rstd_save[((size_t)b * g.d + t) * g.M + m];
-  for (int p = threadIdx.x; p < g.P; p += blockDim.x) gp[p] = rs * (gp[p] - c1 - zp[p] * c2);
 }
 
 // Field adjoint at interior cell (r, c); CIRCULAR folds the wrapped halo copies back.
@@ -561,6 +628,22 @@ nc_status cols(const ColArgs& a, int units, const float2* tw, cudaStream_t st) {
 
 inline unsigned blocks_for(size_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
 
+// Grid of the per-plane statistics kernels: two CTAs per SM looping over the planes.
+unsigned stat_grid(int nplanes) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      sms = 148;
+  }
+  const int n = 2 * sms;
+  return (unsigned)(nplanes < n ? nplanes : n);
+}
+
+// float4 plane access: P and the sample stride multiples of 4 (the buffers are 256-byte aligned).
+int plane_vec(const Geo& g, size_t zs) { return (g.P % 4 == 0 && zs % 4 == 0) ? 1 : 0; }
+
 // x^ (pairs) of the field currently in c.field.
 nc_status field_spectra(const FftCall& c, cudaStream_t st) {
   const Geo& g = c.g;
@@ -636,8 +719,9 @@ nc_status fft_forward(const FftCall& c, cudaStream_t st) {
       Planes zp{z, zs, B, g.M, g.roi_h, g.roi_w, g.P, g.roi_w, 1, pairs * g.M, 1.0f};
       NC_CHECK(rows_inv(c.tmp, zp, g.Nw, c.tw_w, st));
     }
-    plane_stats_kernel<<<B * g.M, kEpiThreads, 0, st>>>(g, z, zs, c.mean, c.rstd,
-                                                         c.train ? c.rstd_save : nullptr, t);
+    plane_stats_kernel<<<stat_grid(B * g.M), kStatThreads, 0, st>>>(g, z, zs, c.mean, c.rstd,
+                                                                     c.train ? c.rstd_save : nullptr, t,
+                                                                     B * g.M, plane_vec(g, zs));
     NC_CHECK(launched("plane_stats_kernel launch"));
     if (t < g.d - 1) {
       hidden_epi_kernel<<<blocks_for((size_t)B * P, kEpiThreads), kEpiThreads, 0, st>>>(
@@ -696,7 +780,8 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
       NC_CHECK(launched("port_gz_kernel launch"));
     }
     if (g.norm) {
-      norm_bwd_kernel<<<B * g.M, kEpiThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, g.d - 1);
+      norm_bwd_kernel<<<stat_grid(B * g.M), kStatThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, g.d - 1,
+                                                                   B * g.M, plane_vec(g, zs));
       NC_CHECK(launched("norm_bwd_kernel launch"));
     }
   }
@@ -743,7 +828,8 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
     gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
     NC_CHECK(launched("gsum_chunks_kernel launch"));
     if (g.norm) {
-      norm_bwd_kernel<<<B * g.M, kEpiThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, t - 1);
+      norm_bwd_kernel<<<stat_grid(B * g.M), kStatThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, t - 1,
+                                                                   B * g.M, plane_vec(g, zs));
       NC_CHECK(launched("norm_bwd_kernel launch"));
     }
   }
