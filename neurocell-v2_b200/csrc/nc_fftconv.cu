@@ -319,31 +319,73 @@ __global__ void __launch_bounds__(kStatThreads) plane_stats_kernel(Geo g, const 
 // ROI epilogue (epilogue.py:28-56): standardise (in place when write_zhat), gate, write the
 // next field's interior and the training residual -- or, in universe mode (uroi != null),
 // the last step's ROI cells.
+// V consecutive floats (V = 4: one 16-byte access; callers guarantee the alignment).
+template <int V>
+__device__ __forceinline__ void ldv(const float* __restrict__ p, float* v) {
+  if constexpr (V == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = p[i];
+  }
+}
+template <int V>
+__device__ __forceinline__ void stv(float* __restrict__ p, const float* v) {
+  if constexpr (V == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) p[i] = v[i];
+  }
+}
+
+// One thread per V consecutive pixels of one sample (V = 4 when P % 4 == 0).
+template <int V>
 __global__ void hidden_epi_kernel(Geo g, StepParams sp, float* z, size_t zs, int write_zhat,
                                   const float* __restrict__ mean, const float* __restrict__ rstd,
                                   float* __restrict__ field, float* __restrict__ xsave, int t, int B,
                                   int act_id, float slope, float* __restrict__ uroi) {
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (size_t)B * g.P) return;
-  const int b = (int)(i / g.P), p = (int)(i - (size_t)b * g.P);
-  const float bb = sp.broi[p];
-  float lin = 0.f, act = 0.f;
-  float* zb = z + (size_t)b * zs + p;
+  const size_t gidx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gidx * V >= (size_t)B * g.P) return;
+  const size_t e0 = gidx * V;
+  const int b = (int)(e0 / g.P), p0 = (int)(e0 - (size_t)b * g.P);
+  float bb[V], lin[V], act[V];
+  ldv<V>(sp.broi + p0, bb);
+#pragma unroll
+  for (int v = 0; v < V; ++v) { lin[v] = 0.f; act[v] = 0.f; }
+  float* zb = z + (size_t)b * zs + p0;
   for (int m = 0; m < g.M; ++m) {
-    const float zh = (zb[(size_t)m * g.P] - mean[b * g.M + m]) * rstd[b * g.M + m];
-    if (write_zhat) zb[(size_t)m * g.P] = zh;
-    lin += zh;
-    if (act_id != NC_ACT_NONE) act += act_fwd(act_id, zh + bb, slope);
+    const float mu = mean[b * g.M + m], rs = rstd[b * g.M + m];
+    float zv[V];
+    ldv<V>(zb + (size_t)m * g.P, zv);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const float zh = (zv[v] - mu) * rs;
+      zv[v] = zh;
+      lin[v] += zh;
+      if (act_id != NC_ACT_NONE) act[v] += act_fwd(act_id, zh + bb[v], slope);
+    }
+    if (write_zhat) stv<V>(zb + (size_t)m * g.P, zv);
   }
-  if (act_id == NC_ACT_NONE) act = lin + (float)g.M * bb;
-  const float xn = sp.weff[p] * lin + sp.seff[p] * act;
+  float we[V], se[V], xn[V];
+  ldv<V>(sp.weff + p0, we);
+  ldv<V>(sp.seff + p0, se);
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const float a = (act_id == NC_ACT_NONE) ? lin[v] + (float)g.M * bb[v] : act[v];
+    xn[v] = we[v] * lin[v] + se[v] * a;
+  }
   if (uroi) {
-    uroi[i] = xn;
+    stv<V>(uroi + e0, xn);
     return;
   }
-  const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
-  field[(size_t)b * g.Fh * g.Fw + (size_t)(r + g.oh) * g.Fw + c + g.ow] = xn;
-  if (xsave) xsave[((size_t)b * (g.d - 1) + t) * g.P + p] = xn;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int p = p0 + v, r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+    field[(size_t)b * g.Fh * g.Fw + (size_t)(r + g.oh) * g.Fw + c + g.ow] = xn[v];
+  }
+  if (xsave) stv<V>(xsave + ((size_t)b * (g.d - 1) + t) * g.P + p0, xn);
 }
 
 // Output-port epilogue (epilogue.py:82-128) from the raw planes and their statistics.
@@ -501,39 +543,57 @@ __device__ __forceinline__ float field_grad(const Geo& g, const float* dxb, int 
 // ROI-epilogue adjoint (kernels_pallas.py:221-291) for the samples of chunk blockIdx.y:
 // the cell gradient comes from the field adjoint dx (hidden step t-1) or, in universe mode,
 // from gy_roi (B, P) with the final activation; per-chunk pixel-gradient partials go to gpart.
+template <int V>
 __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__ dx,
                                  const float* __restrict__ zh_t, size_t zs, float* __restrict__ gz,
                                  float* __restrict__ gpart, int B, int bc, int act_id, float slope,
                                  const float* __restrict__ gy_roi) {
-  const int p = blockIdx.x * blockDim.x + threadIdx.x;
-  if (p >= g.P) return;
+  const int gi = blockIdx.x * blockDim.x + threadIdx.x;
+  if (gi * V >= g.P) return;
+  const int p0 = gi * V;
   const int k = blockIdx.y;
   const int b0 = k * bc, b1 = min(B, b0 + bc);
-  const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
   const size_t P = (size_t)g.P, FF = (size_t)g.Fh * g.Fw;
-  const float bb = sp.broi[p], we = sp.weff[p], se = sp.seff[p];
-  float gp0 = 0.f, gp1 = 0.f, gp2 = 0.f;
+  float bb[V], we[V], se[V], gp0[V], gp1[V], gp2[V];
+  ldv<V>(sp.broi + p0, bb);
+  ldv<V>(sp.weff + p0, we);
+  ldv<V>(sp.seff + p0, se);
+#pragma unroll
+  for (int v = 0; v < V; ++v) { gp0[v] = 0.f; gp1[v] = 0.f; gp2[v] = 0.f; }
   for (int b = b0; b < b1; ++b) {
-    const float gy = gy_roi ? gy_roi[(size_t)b * P + p] : field_grad(g, dx + (size_t)b * FF, r, c);
-    const float* ZH = zh_t + (size_t)b * zs + p;
-    float* GZ = gz + (size_t)b * g.M * P + p;
-    float lin = 0.f, act = 0.f, dsum = 0.f;
-    for (int m = 0; m < g.M; ++m) {
-      const float zh = ZH[m * P];
-      float dd;
-      const float av = act_fwd_deriv(act_id, zh + bb, slope, &dd);
-      lin += zh;
-      act += av;
-      dsum += dd;
-      GZ[m * P] = we * gy + se * gy * dd;
+    float gy[V], lin[V], act[V], dsum[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int p = p0 + v, r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
+      gy[v] = gy_roi ? gy_roi[(size_t)b * P + p] : field_grad(g, dx + (size_t)b * FF, r, c);
+      lin[v] = 0.f; act[v] = 0.f; dsum[v] = 0.f;
     }
-    gp0 += gy * lin;
-    gp1 += gy * act;
-    gp2 += se * gy * dsum;
+    const float* ZH = zh_t + (size_t)b * zs + p0;
+    float* GZ = gz + (size_t)b * g.M * P + p0;
+    for (int m = 0; m < g.M; ++m) {
+      float zv[V], gv[V];
+      ldv<V>(ZH + (size_t)m * P, zv);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        float dd;
+        const float av = act_fwd_deriv(act_id, zv[v] + bb[v], slope, &dd);
+        lin[v] += zv[v];
+        act[v] += av;
+        dsum[v] += dd;
+        gv[v] = we[v] * gy[v] + se[v] * gy[v] * dd;
+      }
+      stv<V>(GZ + (size_t)m * P, gv);
+    }
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      gp0[v] += gy[v] * lin[v];
+      gp1[v] += gy[v] * act[v];
+      gp2[v] += se[v] * gy[v] * dsum[v];
+    }
   }
-  gpart[((size_t)k * 3 + 0) * P + p] = gp0;
-  gpart[((size_t)k * 3 + 1) * P + p] = gp1;
-  gpart[((size_t)k * 3 + 2) * P + p] = gp2;
+  stv<V>(gpart + ((size_t)k * 3 + 0) * P + p0, gp0);
+  stv<V>(gpart + ((size_t)k * 3 + 1) * P + p0, gp1);
+  stv<V>(gpart + ((size_t)k * 3 + 2) * P + p0, gp2);
 }
 
 // gsum += sum over chunks of gpart (chunk order).
@@ -644,6 +704,33 @@ unsigned stat_grid(int nplanes) {
 // float4 plane access: P and the sample stride multiples of 4 (the buffers are 256-byte aligned).
 int plane_vec(const Geo& g, size_t zs) { return (g.P % 4 == 0 && zs % 4 == 0) ? 1 : 0; }
 
+// ROI epilogue over all samples (train: xsave; universe mode: uroi); 4 pixels per thread
+// when the planes allow 16-byte accesses.
+nc_status hidden_epi(const Geo& g, const FftCall& c, float* z, size_t zs, int t, int act_id, float slope,
+                     float* uroi, cudaStream_t st) {
+  const size_t n = (size_t)c.batch * g.P;
+  float* xs = (c.train && !uroi) ? c.xsave : nullptr;
+  if (plane_vec(g, zs))
+    hidden_epi_kernel<4><<<blocks_for(n / 4, kEpiThreads), kEpiThreads, 0, st>>>(
+        g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, xs, t, c.batch, act_id, slope, uroi);
+  else
+    hidden_epi_kernel<1><<<blocks_for(n, kEpiThreads), kEpiThreads, 0, st>>>(
+        g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, xs, t, c.batch, act_id, slope, uroi);
+  return launched("hidden_epi_kernel launch");
+}
+
+// ROI-epilogue adjoint (see hidden_gz_kernel); 4 pixels per thread when possible.
+nc_status hidden_gz(const Geo& g, const FftCall& c, const float* zh, size_t zs, int nch, int bc, int act_id,
+                    float slope, const float* gy_roi, cudaStream_t st) {
+  if (plane_vec(g, zs))
+    hidden_gz_kernel<4><<<dim3(blocks_for((size_t)g.P / 4, 256), nch), 256, 0, st>>>(
+        g, c.sp, c.dx, zh, zs, c.gz, c.gpart, c.batch, bc, act_id, slope, gy_roi);
+  else
+    hidden_gz_kernel<1><<<dim3(blocks_for((size_t)g.P, 256), nch), 256, 0, st>>>(
+        g, c.sp, c.dx, zh, zs, c.gz, c.gpart, c.batch, bc, act_id, slope, gy_roi);
+  return launched("hidden_gz_kernel launch");
+}
+
 // x^ (pairs) of the field currently in c.field.
 nc_status field_spectra(const FftCall& c, cudaStream_t st) {
   const Geo& g = c.g;
@@ -724,16 +811,10 @@ nc_status fft_forward(const FftCall& c, cudaStream_t st) {
                                                                      B * g.M, plane_vec(g, zs));
     NC_CHECK(launched("plane_stats_kernel launch"));
     if (t < g.d - 1) {
-      hidden_epi_kernel<<<blocks_for((size_t)B * P, kEpiThreads), kEpiThreads, 0, st>>>(
-          g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, c.train ? c.xsave : nullptr, t, B,
-          g.act, g.slope, nullptr);
-      NC_CHECK(launched("hidden_epi_kernel launch"));
+      NC_CHECK(hidden_epi(g, c, z, zs, t, g.act, g.slope, nullptr, st));
     } else if (c.uroi) {
       // universe mode: the ROI epilogue with the final activation (propagator.py:657-682)
-      hidden_epi_kernel<<<blocks_for((size_t)B * P, kEpiThreads), kEpiThreads, 0, st>>>(
-          g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, nullptr, t, B, g.fact, g.fslope,
-          c.uroi);
-      NC_CHECK(launched("hidden_epi_kernel launch"));
+      NC_CHECK(hidden_epi(g, c, z, zs, t, g.fact, g.fslope, c.uroi, st));
     } else {
       port_out_kernel<<<blocks_for((size_t)B * g.n_out, 128), 128, 0, st>>>(g, c.sp, c.out_index, z, zs,
                                                                              c.mean, c.rstd, c.out, B);
@@ -769,9 +850,7 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
   {
     const float* zh = c.zhat + (size_t)(g.d - 1) * M * P;
     if (c.guroi) {
-      hidden_gz_kernel<<<dim3(blocks_for(P, 256), nch), 256, 0, st>>>(g, c.sp, c.dx, zh, zs, c.gz, c.gpart,
-                                                                      B, bc, g.fact, g.fslope, c.guroi);
-      NC_CHECK(launched("hidden_gz_kernel launch"));
+      NC_CHECK(hidden_gz(g, c, zh, zs, nch, bc, g.fact, g.fslope, c.guroi, st));
       gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
       NC_CHECK(launched("gsum_chunks_kernel launch"));
     } else {
@@ -822,9 +901,7 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
     }
     // hidden-step adjoint of step t-1
     const float* zh = c.zhat + (size_t)(t - 1) * M * P;
-    hidden_gz_kernel<<<dim3(blocks_for(P, 256), nch), 256, 0, st>>>(g, c.sp, c.dx, zh, zs, c.gz, c.gpart,
-                                                                    B, bc, g.act, g.slope, nullptr);
-    NC_CHECK(launched("hidden_gz_kernel launch"));
+    NC_CHECK(hidden_gz(g, c, zh, zs, nch, bc, g.act, g.slope, nullptr, st));
     gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
     NC_CHECK(launched("gsum_chunks_kernel launch"));
     if (g.norm) {
