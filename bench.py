@@ -357,6 +357,14 @@ def run_b200(args) -> None:
                          "traffic_source": "profiles/ncu_traffic.json (one ncu capture, dram read+write per launch)"},
             "clocks": clk,
         }
+        tr = ncu_traffic(dom)
+        if tr:
+            # the same kernel against HBM: captured DRAM bytes per launch / its event time
+            hp, hsrc = hbm_peak()
+            dom_ms = bwd_ms if dom == names[1] else fwd_ms
+            hgbs = tr / (dom_ms * 1e-3) / 1e9
+            line["roofline"]["hbm"] = {"achieved": hgbs, "peak": hp, "unit": "GB/s", "frac": hgbs / hp,
+                                       "peak_source": hsrc}
         if world == 1 and not args.no_cpu and spec is None:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
