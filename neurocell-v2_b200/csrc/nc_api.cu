@@ -56,7 +56,7 @@ __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* cell, cons
                                    const uint8_t* owm, const uint8_t* bmask, const float* gsum,
                                    const float* gborder,
                                    const float* gdsum, const float* gring_final, float* gcell,
-                                   float* gfilt);
+                                   float* gfilt, int rows, size_t stride);
 __global__ void universe_fwd_kernel(Geo g, StepParams sp, const float* cell, const float* uroi,
                                     float* universe, int B);
 __global__ void gather_out_kernel(Geo g, const int32_t* out_index, const float* universe, float* out,
@@ -414,7 +414,12 @@ static nc_status vnn_forward(const nc_topo* topo, const void* d_plan, const floa
   if (universe) NC_CHECK(check_ptr(universe, "universe"));
   if (pr.g.n_in > 0) NC_CHECK(check_ptr(inputs, "inputs"));
   cudaStream_t st = as_stream(stream);
-  NC_CHECK(launch_prestep(pr, cell_params, filters, codd, st));
+  const bool fused_fft = pr.g.algo == NC_CONV_FFT && fftf_fits(pr.g);
+  if (fused_fft)   // pre-step and filter-pair spectra in one launch
+    NC_CHECK(fftf_prestep_spectra(pr.g, pr.sp, cell_params, filters, pr.io, pr.owm, pr.bmask, *codd,
+                                  at<float2>(d_ws, pr.L.f_h), st));
+  else
+    NC_CHECK(launch_prestep(pr, cell_params, filters, codd, st));
   float* uroi = universe ? at<float>(d_ws, pr.L.uroi) : nullptr;
 
   const bool train = (flags & NC_FLAG_TRAIN) != 0;
@@ -427,7 +432,6 @@ static nc_status vnn_forward(const nc_topo* topo, const void* d_plan, const floa
       FftfArgs fa = fftf_args(pr, d_ws, inputs, batch, train);
       fa.out = out;
       fa.uroi = uroi;
-      NC_CHECK(fftf_pair_spectra(pr.g, pr.sp.geff, at<float2>(d_ws, pr.L.f_h), st));
       if (g_prof.fs) NC_CUDA_CHECK(cudaEventRecord(g_prof.fs, st));
       NC_CHECK(fftf_forward(fa, st));
       if (g_prof.fe) NC_CUDA_CHECK(cudaEventRecord(g_prof.fe, st));
@@ -570,12 +574,14 @@ static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const flo
       float* part = at<float>(d_ws, L.redscr);
       seg_batch_sum1_kernel<<<dim3((j.total + 255) / 256, chunks), 256, 0, st>>>(j, batch, bc, part);
       NC_CHECK(launch_check("seg_batch_sum1_kernel launch"));
-      seg_batch_sum2_kernel<<<(j.total + 255) / 256, 256, 0, st>>>(j, chunks, part);
-      NC_CHECK(launch_check("seg_batch_sum2_kernel launch"));
+      // the second stage (chunk order) runs inside the pre-step adjoint
+      prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(
+          g, pr.sp, cell_params, filters, pr.owm, pr.bmask, part, gborder ? part + P3 + MK : nullptr,
+          part + P3, gringf, g_cell_params, g_filters, chunks, (size_t)j.total);
+      NC_CHECK(launch_check("prestep_bwd_kernel launch"));
     }
-    prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, pr.bmask, gsum,
-                                                         gborder, gdsum, gringf, g_cell_params, g_filters);
-    NC_CHECK(launch_check("prestep_bwd_kernel launch"));
+    (void)gsum;
+    (void)gdsum;
     clear_error();
     return NC_OK;
   }
@@ -588,7 +594,7 @@ static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const flo
     if (g_prof.be) NC_CUDA_CHECK(cudaEventRecord(g_prof.be, st));
     const int HW = g.H * g.W;
     prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, pr.bmask, c.gsum,
-                                                         c.gborder, c.gdsum, gringf, g_cell_params, g_filters);
+                                                         c.gborder, c.gdsum, gringf, g_cell_params, g_filters, 0, 0);
     NC_CHECK(launch_check("prestep_bwd_kernel launch"));
     clear_error();
     return NC_OK;
@@ -665,7 +671,7 @@ static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const flo
     NC_CHECK(launch_check("border_grad_kernel launch"));
   }
   prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(g, pr.sp, cell_params, filters, pr.owm, pr.bmask, gsum,
-                                                       gborder, gdsum, gringf, g_cell_params, g_filters);
+                                                       gborder, gdsum, gringf, g_cell_params, g_filters, 0, 0);
   NC_CHECK(launch_check("prestep_bwd_kernel launch"));
   clear_error();
   return NC_OK;

@@ -3,6 +3,7 @@
 
 #include "nc_common.cuh"
 #include "nc_kernels.cuh"
+#include "nc_prestep.cuh"
 
 namespace nc {
 
@@ -14,31 +15,9 @@ __global__ void prestep_kernel(Geo g, StepParams sp, const float* __restrict__ c
                                nc_codd codd) {
   const int HW = g.H * g.W;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < HW) {
-    const float Wv = cell[i], Bv = cell[HW + i], Sv = cell[2 * HW + i];
-    float ds;
-    const float s = codd_prob(Sv, io[i] != 0, g.hard_pin, codd.mode, codd.temperature,
-                              codd.active_threshold, &ds);
-    const float wp = owm[i] ? 1.0f : Wv;
-    sp.sprob[i] = s;
-    sp.dsprob[i] = ds;
-    sp.wpinned[i] = wp;
-    sp.border[i] = bmask[i] ? act_fwd(g.act, Bv, g.slope) * s : 0.0f;
-    const int r = i / g.W, c = i - (i / g.W) * g.W;
-    const int rr = r - g.pad_h, cc = c - g.pad_w;
-    if (rr >= 0 && rr < g.roi_h && cc >= 0 && cc < g.roi_w) {
-      const int p = rr * g.roi_w + cc;
-      const float inv_m = 1.0f / (float)g.M;
-      sp.weff[p] = inv_m * wp * (1.0f - s);
-      sp.seff[p] = inv_m * s;
-      sp.broi[p] = Bv;
-    }
-  }
+  if (i < HW) prestep_cell(g, sp, cell, io, owm, bmask, codd, i);
   const int nf = g.M * g.K;
-  for (int j = i; j < nf; j += gridDim.x * blockDim.x) {
-    const float f = filters[j];
-    sp.geff[j] = g.gated ? sigmoidf_(f) : f;
-  }
+  for (int j = i; j < nf; j += gridDim.x * blockDim.x) sp.geff[j] = geff_tap(g, filters, j);
 }
 
 __global__ void codd_kernel(int HW, const float* __restrict__ s_raw, const uint8_t* __restrict__ io,
@@ -157,14 +136,26 @@ __global__ void border_grad_kernel(Geo g, const float* __restrict__ G,
   if (lane == 0) gborder[i] = acc;
 }
 
+// Value idx of a batch-summed array: the array itself, or (rows > 0) the sum over `rows`
+// chunk partials of stride `stride`, added in chunk order.
+__device__ __forceinline__ float chunk_sum(const float* __restrict__ a, int idx, int rows, size_t stride) {
+  if (rows <= 0) return a[idx];
+  float acc = 0.f;
+  for (int r = 0; r < rows; ++r) acc += a[(size_t)r * stride + idx];
+  return acc;
+}
+
 // Pre-step adjoint: chain the ROI partials and the border gradient back to (W, B, S_raw)
 // and gate the filter gradient.  gsum = [g w_eff | g s_eff | g b_roi] summed over batch.
+// rows > 0: gsum, gborder and gdsum point into chunk partials of row stride `stride` and
+// are summed here (the second stage of the fixed-order batch sums).
 __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* __restrict__ cell,
                                    const float* __restrict__ filters, const uint8_t* __restrict__ owm,
                                    const uint8_t* __restrict__ bmask,
                                    const float* __restrict__ gsum, const float* __restrict__ gborder,
                                    const float* __restrict__ gdsum, const float* __restrict__ gring_final,
-                                   float* __restrict__ gcell, float* __restrict__ gfilt) {
+                                   float* __restrict__ gcell, float* __restrict__ gfilt, int rows,
+                                   size_t stride) {
   const int HW = g.H * g.W;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < HW) {
@@ -175,13 +166,15 @@ __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* __restrict
     const int rr = r - g.pad_h, cc = c - g.pad_w;
     if (rr >= 0 && rr < g.roi_h && cc >= 0 && cc < g.roi_w) {
       const int p = rr * g.roi_w + cc;
-      const float gwe = gsum[p], gse = gsum[g.P + p], gbr = gsum[2 * g.P + p];
+      const float gwe = chunk_sum(gsum, p, rows, stride);
+      const float gse = chunk_sum(gsum, g.P + p, rows, stride);
+      const float gbr = chunk_sum(gsum, 2 * g.P + p, rows, stride);
       g_wp = gwe * inv_m * (1.0f - s);
       g_s = -gwe * inv_m * wp + gse * inv_m;
       g_b = gbr;
     }
     if (gborder && bmask[i]) {
-      const float gb = gborder[i];
+      const float gb = chunk_sum(gborder, i, rows, stride);
       float da;
       const float av = act_fwd_deriv(g.act, Bv, g.slope, &da);
       g_b += gb * da * s;
@@ -200,7 +193,7 @@ __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* __restrict
   }
   const int nf = g.M * g.K;
   for (int j = i; j < nf; j += gridDim.x * blockDim.x) {
-    float gv = gdsum[j];
+    float gv = chunk_sum(gdsum, j, rows, stride);
     if (g.gated) {
       const float sg = sigmoidf_(filters[j]);
       gv *= sg * (1.0f - sg);

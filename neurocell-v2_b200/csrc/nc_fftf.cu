@@ -21,6 +21,7 @@
 #include "nc_errors.h"
 #include "nc_fft.cuh"
 #include "nc_fftf.h"
+#include "nc_prestep.cuh"
 
 namespace nc {
 
@@ -703,20 +704,19 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
 }
 
 // H_j(w) = conj(G^_{2j}(w)) + i conj(G^_{2j+1}(w)) = F_j(-w) / 64^2 with
-// F_j = FFT(g_{2j} + i g_{2j+1}) (both filters real); one CTA per direction pair.
-__global__ void __launch_bounds__(kThreads, 1) fftf_pair_spectra_kernel(Geo g, const float* __restrict__ geff,
-                                                                        float2* __restrict__ H) {
-  __shared__ float2 plane[kPlane];
-  __shared__ float2 stw[kN];
-  const int tid = threadIdx.x, nt = blockDim.x, j = blockIdx.x;
+// F_j = FFT(g_{2j} + i g_{2j+1}) (both filters real); one CTA per direction pair.  The taps
+// are gated here (geff_tap), so the spectra do not wait for the pre-step kernel.
+__device__ __forceinline__ void pair_spectra_cta(const Geo& g, const float* __restrict__ filters,
+                                                 float2* __restrict__ H, int j, float2* plane, float2* stw) {
+  const int tid = threadIdx.x, nt = blockDim.x;
   fft64::init_tw64(stw, tid);
   const fft64::Lane Ln = fft64::lane_of(tid);
-  const float* g1 = geff + (size_t)(2 * j) * g.K;
-  const float* g2 = g1 + g.K;
+  const int k1 = 2 * j * g.K, k2 = k1 + g.K;
   for (int i = tid; i < kN * kN; i += nt) {
     const int r = i / kN, c = i - (i / kN) * kN;
-    plane[at2(r, c)] = (r < g.kh && c < g.kw) ? make_float2(g1[r * g.kw + c], g2[r * g.kw + c])
-                                              : make_float2(0.f, 0.f);
+    plane[at2(r, c)] = (r < g.kh && c < g.kw)
+                           ? make_float2(geff_tap(g, filters, k1 + r * g.kw + c), geff_tap(g, filters, k2 + r * g.kw + c))
+                           : make_float2(0.f, 0.f);
   }
   fwd2d(plane, g.kh, stw, Ln);
   float2* Hj = H + (size_t)j * kPlane;             // stored in the on-chip plane layout
@@ -729,6 +729,25 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_pair_spectra_kernel(Geo g, c
     }
     Hj[i] = v;
   }
+}
+
+// The pre-step fusion and the pair spectra in one launch: CTAs [0, M/2) build H_j, the
+// others run the per-cell pre-step (nc_prestep.cuh) and write the gated filters.
+__global__ void __launch_bounds__(kThreads, 1) fftf_prestep_spectra_kernel(
+    Geo g, StepParams sp, const float* __restrict__ cell, const float* __restrict__ filters,
+    const uint8_t* __restrict__ io, const uint8_t* __restrict__ owm, const uint8_t* __restrict__ bmask,
+    nc_codd codd, float2* __restrict__ H) {
+  __shared__ float2 plane[kPlane];
+  __shared__ float2 stw[kN];
+  const int pairs = g.M / 2;
+  if ((int)blockIdx.x < pairs) {
+    pair_spectra_cta(g, filters, H, blockIdx.x, plane, stw);
+    return;
+  }
+  const int i = ((int)blockIdx.x - pairs) * blockDim.x + threadIdx.x;
+  if (i < g.H * g.W) prestep_cell(g, sp, cell, io, owm, bmask, codd, i);
+  const int stride = ((int)gridDim.x - pairs) * blockDim.x;
+  for (int j = i; j < g.M * g.K; j += stride) sp.geff[j] = geff_tap(g, filters, j);
 }
 
 nc_status launched(const char* what) {
@@ -759,9 +778,13 @@ bool fftf_fits(const Geo& g) {
   return fftf_fwd_smem(g, false) <= kFftfSmemMax && fftf_bwd_smem(g, ring, false) <= kFftfSmemMax;
 }
 
-nc_status fftf_pair_spectra(const Geo& g, const float* geff, float2* H, cudaStream_t st) {
-  fftf_pair_spectra_kernel<<<g.M / 2, kThreads, 0, st>>>(g, geff, H);
-  return launched("fftf_pair_spectra_kernel launch");
+nc_status fftf_prestep_spectra(const Geo& g, const StepParams& sp, const float* cell, const float* filters,
+                               const uint8_t* io, const uint8_t* owm, const uint8_t* bmask,
+                               const nc_codd& codd, float2* H, cudaStream_t st) {
+  const int HW = g.H * g.W;
+  const int grid = g.M / 2 + (HW + kThreads - 1) / kThreads;
+  fftf_prestep_spectra_kernel<<<grid, kThreads, 0, st>>>(g, sp, cell, filters, io, owm, bmask, codd, H);
+  return launched("fftf_prestep_spectra_kernel launch");
 }
 
 nc_status fftf_forward(const FftfArgs& args, cudaStream_t st) {

@@ -42,8 +42,11 @@ size_t fftf_bwd_smem(const Geo& g, bool ring, bool stage);
 // Sticky error word of the current device: 1 when a bounded wait of the fused kernels for
 // their own bulk copies gave up (that call's results are invalid).  Synchronous.
 int fftf_device_error(bool clear);
-// H_j (natural order) from the effective filters (M, kh, kw).
-nc_status fftf_pair_spectra(const Geo& g, const float* geff, float2* H, cudaStream_t st);
+// One launch: the pre-step fusion (step parameters, gated filters) and H_j (the filter-pair
+// spectra, gated from `filters` directly).
+nc_status fftf_prestep_spectra(const Geo& g, const StepParams& sp, const float* cell, const float* filters,
+                               const uint8_t* io, const uint8_t* owm, const uint8_t* bmask,
+                               const nc_codd& codd, float2* H, cudaStream_t st);
 nc_status fftf_forward(const FftfArgs& a, cudaStream_t st);
 nc_status fftf_backward(const FftfArgs& a, cudaStream_t st);
 
