@@ -529,7 +529,10 @@ def run_config(args) -> None:
     K = args.steps
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     clocks = ClockSampler(local)
+    anneal = meta["train"] and meta["codd_mode"] == "annealed"
     for i in range(K):
+        if anneal:       # tau 1.0 -> 0.1 over the steps (exponential)
+            runner.set_temperature(nc.compute_annealed_temperature(i, K, 1.0, 0.1))
         l2_flush.fill_(float(i))
         ev[i][0].record()
         step()
@@ -564,6 +567,8 @@ def run_config(args) -> None:
         "dtype": "f32", "data": "synthetic (seeded numpy, config shapes)",
         "config": {"workload": f"BASELINE config {cfg}", "batch_per_gpu": B,
                    "global_batch": B * world, "conv": conv, "codd_mode": meta["codd_mode"],
+                   "state_temperature": ("1.0 -> 0.1 over the timed steps (exponential)"
+                                         if meta["codd_mode"] == "annealed" else 1.0),
                    "cuda_graph": not args.no_graph,
                    "parallelism": (f"dp{world}" if meta["train"] else f"{world} replicas"),
                    "grad_exchange": (args.exchange if world > 1 and meta["train"] else "none"),

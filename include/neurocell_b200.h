@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define NC_ABI_VERSION 4
+#define NC_ABI_VERSION 5
 
 typedef enum nc_status {
   NC_OK = 0,
@@ -101,6 +101,10 @@ typedef struct nc_codd {
   int32_t mode;            /* nc_codd_mode */
   float temperature;       /* tau, clamped to >= 1e-4 as params.py:63 */
   float active_threshold;  /* ste_ternary role-2 threshold (default 0.6) */
+  /* Optional device scalar: when not null the kernels read tau from it when they run, so a
+     captured CUDA graph replays with the current value (the reference passes tau as a
+     traced scalar for the same reason).  Null: `temperature` is used. */
+  const float* temperature_dev;
 } nc_codd;
 
 /* ---- plan: device copy of the static port tables and masks -------------------------- */

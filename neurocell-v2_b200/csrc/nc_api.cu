@@ -126,6 +126,8 @@ static nc_status check_codd(const nc_codd* c) {
     return set_error(NC_ERR_INVALID,
                      "Unsupported codd_mode id %d; choose from (continuous, annealed, ste_binary, ste_ternary)",
                      c->mode);
+  if (reinterpret_cast<uintptr_t>(c->temperature_dev) % 4 != 0)
+    return set_error(NC_ERR_INVALID, "codd temperature_dev is not 4-byte aligned");
   return NC_OK;
 }
 

@@ -25,7 +25,7 @@ __global__ void codd_kernel(int HW, const float* __restrict__ s_raw, const uint8
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= HW) return;
   float ds;
-  out[i] = codd_prob(s_raw[i], io[i] != 0, hard_pin, codd.mode, codd.temperature,
+  out[i] = codd_prob(s_raw[i], io[i] != 0, hard_pin, codd.mode, codd_tau(codd),
                      codd.active_threshold, &ds);
 }
 
@@ -407,7 +407,7 @@ __device__ __forceinline__ float fill_pre(const Geo& g, const float* cell, const
   if (g.padding != NC_PAD_VALID) return 0.f;
   const int HW = g.H * g.W;
   float ds, da;
-  const float s = codd_prob(cell[2 * HW + k], io[k] != 0, g.hard_pin, codd.mode, codd.temperature,
+  const float s = codd_prob(cell[2 * HW + k], io[k] != 0, g.hard_pin, codd.mode, codd_tau(codd),
                             codd.active_threshold, &ds);
   const float fb = act_fwd_deriv(g.fact, cell[HW + k], g.fslope, &da);
   *dB = da * s;

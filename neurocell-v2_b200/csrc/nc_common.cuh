@@ -68,6 +68,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+// Codd temperature of a call: the device scalar when given (read at run time), else the
+// value passed by the host.
+__device__ __forceinline__ float codd_tau(const nc_codd& c) {
+  return c.temperature_dev ? *c.temperature_dev : c.temperature;
+}
+
 // Codd gating of one cell (neurocell/params.py:31-80).  Returns s_prob and writes the
 // derivative of the surrogate used in backward (sigmoid' / tau for the STE modes).
 __device__ __forceinline__ float codd_prob(float s_raw, bool io, int hard_pin, int mode,

@@ -16,7 +16,7 @@ __device__ __forceinline__ void prestep_cell(const Geo& g, const StepParams& sp,
   const int HW = g.H * g.W;
   const float Wv = cell[i], Bv = cell[HW + i], Sv = cell[2 * HW + i];
   float ds;
-  const float s = codd_prob(Sv, io[i] != 0, g.hard_pin, codd.mode, codd.temperature,
+  const float s = codd_prob(Sv, io[i] != 0, g.hard_pin, codd.mode, codd_tau(codd),
                             codd.active_threshold, &ds);
   const float wp = owm[i] ? 1.0f : Wv;
   sp.sprob[i] = s;

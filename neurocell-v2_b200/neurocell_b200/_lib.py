@@ -12,7 +12,7 @@ import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libneurocell_b200.so")
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 NC_OK, NC_ERR_INVALID, NC_ERR_WORKSPACE, NC_ERR_UNSUPPORTED, NC_ERR_CUDA = 0, 1, 2, 3, 4
 NC_PAD = {"VALID": 0, "SAME": 1, "CIRCULAR": 2}
@@ -52,7 +52,7 @@ class NcTopo(ctypes.Structure):
 
 class NcCodd(ctypes.Structure):
     _fields_ = [("mode", ctypes.c_int32), ("temperature", ctypes.c_float),
-                ("active_threshold", ctypes.c_float)]
+                ("active_threshold", ctypes.c_float), ("temperature_dev", ctypes.c_void_p)]
 
 
 _vp, _sz, _i32, _u32, _i64, _f32 = (ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32,

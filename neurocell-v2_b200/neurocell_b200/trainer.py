@@ -254,6 +254,9 @@ class VNNTrainStep:
         self.g_out = torch.empty_like(self.out)
         self.loss = torch.zeros((), dtype=torch.float32, device=dev)
         self.codd = ops._codd(codd_mode, state_temperature, active_threshold)
+        # tau lives on the device so captured graphs replay with the current temperature
+        self.tau_dev = torch.full((1,), float(state_temperature), dtype=torch.float32, device=dev)
+        self.codd.temperature_dev = self.tau_dev.data_ptr()
         self.graph = None
         self.epoch_graph = None
         self.exchange = None
@@ -279,7 +282,10 @@ class VNNTrainStep:
         return self._launches
 
     def set_temperature(self, tau: float) -> None:
+        """Codd temperature of the following steps (annealed and STE modes).  Stream-ordered
+        device write, so it also reaches steps and epochs already captured as CUDA graphs."""
         self.codd.temperature = float(tau)
+        self.tau_dev.fill_(float(tau))
 
     def _launch(self, loss_out: torch.Tensor | None = None) -> None:
         c, lib, P = self.ctypes, self.lib, ops._ptr

@@ -160,3 +160,36 @@ def test_annealed_steps_and_multi_epoch_shuffle():
     yt = torch.randint(0, 2, (40, 8), generator=g, device=dev).float()
     params, ep = tr.train_epochs(params, xt, yt, 5, 3)
     assert ep.shape == (3,) and bool(torch.isfinite(ep).all())
+
+
+def test_graph_step_follows_the_annealed_temperature():
+    """set_temperature reaches a captured step (tau is a device scalar the kernels read when
+    they run): three graph replays at tau = 1.0, 0.4, 0.1 equal three eager steps at the same
+    temperatures, and differ from replays at a fixed tau."""
+    cell, filt, xs, ys = _alu(3, 32, 21)
+    dev = torch.device("cuda:0")
+    topo = nc.ChipTopology2D.alu_chip()
+    xd, yd = torch.tensor(xs, device=dev), torch.tensor(ys, device=dev)
+
+    def runner():
+        p = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
+        return nc.trainer.VNNTrainStep(topo, p, 32, lr=5e-2, in_shapes=((8, 1),) * 3,
+                                       codd_mode="annealed", state_temperature=1.0)
+
+    taus = (1.0, 0.4, 0.1)
+    eager, graph, fixed = runner(), runner(), runner()
+    graph.load_batch(xd[0], yd[0])
+    graph.capture()
+    fixed.load_batch(xd[0], yd[0])
+    fixed.capture()
+    le, lg = [], []
+    for i, tau in enumerate(taus):
+        eager.set_temperature(tau)
+        le.append(float(eager.step(xd[i], yd[i])))
+        graph.set_temperature(tau)
+        lg.append(float(graph.step(xd[i], yd[i])))
+        fixed.step(xd[i], yd[i])
+    torch.cuda.synchronize()
+    assert le == lg
+    assert torch.equal(graph.flat, eager.flat)
+    assert not torch.equal(fixed.flat, eager.flat)
