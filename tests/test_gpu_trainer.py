@@ -193,3 +193,38 @@ def test_graph_step_follows_the_annealed_temperature():
     assert le == lg
     assert torch.equal(graph.flat, eager.flat)
     assert not torch.equal(fixed.flat, eager.flat)
+
+
+def test_exchange_timeout_sets_status_and_skips_the_update():
+    """Failure detection without a GPU fault: rank 0 of a two-rank exchange whose peer never
+    arrives (the peer's receive buffer is a plain buffer on this GPU that nothing writes
+    into rank 0's slots).  The bounded wait runs out, the status word reads 1 and the
+    parameters are left as they were."""
+    import ctypes
+    from neurocell_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    n, world = 1000, 2
+    bufs = [ctypes.c_void_p() for _ in range(3)]
+    sizes = [lib.nc_dp_shared_bytes(n, world), lib.nc_dp_shared_bytes(n, world), lib.nc_dp_state_bytes()]
+    with torch.cuda.device(dev):
+        for b, sz in zip(bufs, sizes):
+            _lib.check(lib.nc_dp_alloc(sz, ctypes.byref(b)), "nc_dp_alloc")
+        try:
+            peers = (ctypes.c_void_p * world)(bufs[0], bufs[1])
+            g = torch.randn(n, device=dev)
+            p = torch.randn(n, device=dev)
+            p0 = p.clone()
+            st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+            _lib.check(lib.nc_dp_allreduce_sgd(peers, world, 0, bufs[2], ctypes.c_void_p(g.data_ptr()),
+                                               ctypes.c_void_p(p.data_ptr()), n, 0.1, 2000, st),
+                       "nc_dp_allreduce_sgd")
+            status = ctypes.c_int32(-1)
+            _lib.check(lib.nc_dp_status(bufs[2], ctypes.byref(status), st), "nc_dp_status")
+            torch.cuda.synchronize()
+            assert status.value == 1
+            assert torch.equal(p, p0)
+        finally:
+            torch.cuda.synchronize()
+            for b in bufs:
+                lib.nc_dp_free(b)
