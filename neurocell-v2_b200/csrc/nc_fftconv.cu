@@ -66,6 +66,7 @@ __global__ void __launch_bounds__(kFftThreads) rows_fwd_kernel(Planes a, float2*
   const int nl = min(L, total - line0);
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
+#pragma unroll 4
   for (int idx = tid; idx < nl * N; idx += nt) {
     const int l = idx >> lgN, e = idx & (N - 1);
     const int line = line0 + l;
@@ -81,6 +82,7 @@ __global__ void __launch_bounds__(kFftThreads) rows_fwd_kernel(Planes a, float2*
     s[l * LS + pidx(e)] = make_float2(re, im);
   }
   fft::transform_lines_plan<false>(s, nl, N, stw, tid, nt);
+#pragma unroll 4
   for (int idx = tid; idx < nl * N; idx += nt) {
     const int l = idx >> lgN, e = idx & (N - 1);
     __stcs(&dst[(size_t)(line0 + l) * N + e], s[l * LS + pidx(e)]);   // read once
@@ -102,11 +104,13 @@ __global__ void __launch_bounds__(kFftThreads) rows_inv_kernel(const float2* __r
   const int nl = min(L, total - line0);
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
+#pragma unroll 4
   for (int idx = tid; idx < nl * N; idx += nt) {
     const int l = idx >> lgN, e = idx & (N - 1);
     s[l * LS + pidx(e)] = __ldcs(&src[(size_t)(line0 + l) * N + e]);   // last use
   }
   fft::transform_lines_plan<true>(s, nl, N, stw, tid, nt);
+#pragma unroll 4
   for (int idx = tid; idx < nl * a.cols; idx += nt) {
     const int l = idx / a.cols, e = idx - l * a.cols;
     const int line = line0 + l;
@@ -146,6 +150,7 @@ __global__ void __launch_bounds__(kFftThreads) cols_kernel(ColArgs a, const floa
   const int tid = threadIdx.x, nt = blockDim.x;
   const size_t NN = (size_t)a.Nh * a.Nw;
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
+#pragma unroll 4
   for (int idx = tid; idx < N * C; idx += nt) {
     const int r = idx >> lgC, cc = idx & (C - 1);
     const int c = c0 + cc;
@@ -168,6 +173,7 @@ __global__ void __launch_bounds__(kFftThreads) cols_kernel(ColArgs a, const floa
   }
   fft::transform_lines_plan<MODE != COL_FWD>(s, C, N, stw, tid, nt);
   const int rows_st = (MODE == COL_FWD) ? N : a.rows_out;
+#pragma unroll 4
   for (int idx = tid; idx < rows_st * C; idx += nt) {
     const int r = idx >> lgC, cc = idx & (C - 1);
     float2* o = &a.dst[((size_t)u * rows_st + r) * a.Nw + c0 + cc];
@@ -643,8 +649,10 @@ size_t rows_smem(int N, int L) {
   return sizeof(float2) * ((size_t)((TN + 1) & ~1) + (size_t)L * line_stride(N));
 }
 
+// Columns per CTA: 8 from 512-point columns on (37 KB of lines at N = 512, six CTAs per
+// SM; measured faster than 16 at N = 512 and than 4 at N = 1024), 16 below.
 int cols_per_cta(int Nh, int Nw) {
-  int C = Nh >= 1024 ? 8 : 16;
+  int C = Nh >= 512 ? 8 : 16;
   return C < Nw ? C : Nw;
 }
 
