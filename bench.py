@@ -38,6 +38,10 @@ BATCH = 128
 SEED = 0            # config index 0 -> seeds 0 (params), 1 (filters), 2 (inputs)
 LR = 1e-2
 WORKLOAD = "BASELINE config 0: 62x62 ALU VNN train step (fwd+bwd+SGD)"
+METRIC = "train samples/s (62x62 ALU VNN, B=128 per GPU)"   # both arms report this metric
+# the workload fields both arms report
+WORKLOAD_FIELDS = {"workload": WORKLOAD, "grid": [62, 62], "roi": [40, 50], "kernel": [23, 13], "M": 16,
+                   "depth": 4, "codd_mode": "continuous", "loss": "mse", "optimizer": "sgd(1e-2)"}
 
 
 def alu_flops_per_sample(train: bool = True) -> float:
@@ -180,12 +184,12 @@ def run_reference(args) -> None:
     ms = 1e3 * statistics.mean(times)
     val = BATCH / (ms * 1e-3)
     line = {
-        "impl": "reference", "metric": "train samples/s (62x62 ALU VNN, B=128)", "value": val,
+        "impl": "reference", "metric": METRIC, "value": val,
         "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded numpy ALU batches)",
-        "config": {"workload": WORKLOAD, "per_gpu_batch": BATCH, "global_batch": BATCH,
-                   "parallelism": "cpu"},
+        "config": dict(WORKLOAD_FIELDS, per_gpu_batch=BATCH, global_batch=BATCH,
+                       parallelism=f"cpu, {threads} threads"),
         "cpu_baseline": {"value": val, "unit": "samples/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} full B={BATCH} train steps of oracle/torch_port.py "
                                    "(the reference's JAX CPU path is not installable here)"},
@@ -327,16 +331,14 @@ def run_b200(args) -> None:
 
     if rank == 0:
         line = {
-            "metric": ("train samples/s (62x62 ALU VNN, B=128 per GPU)" if spec is None else
+            "metric": (METRIC if spec is None else
                        "train samples/s (62x62 ALU VNN on its adaptive %dx%d sub-ROI, B=128 per GPU)"
                        % spec.active_shape), "value": value,
             "unit": "samples/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded numpy ALU batches, random-init params as BASELINE config 0)",
-            "config": {"workload": WORKLOAD, "grid": [62, 62], "roi": [40, 50], "kernel": [23, 13],
-                       "M": 16, "depth": 4, "codd_mode": "continuous", "loss": "mse",
-                       "optimizer": "sgd(1e-2)", "per_gpu_batch": BATCH, "global_batch": BATCH * world,
+            "config": {**WORKLOAD_FIELDS, "per_gpu_batch": BATCH, "global_batch": BATCH * world,
                        "parallelism": f"dp{world}", "l2": "flushed (256 MB write) before every timed step",
                        "cuda_graph": runner.graph is not None,
                        "grad_exchange": (args.exchange if world > 1 else "none"),
