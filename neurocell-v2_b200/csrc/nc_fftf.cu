@@ -221,6 +221,12 @@ __device__ void load_field(const FftfArgs& a, float2* X, const float* roi_src, c
 // ---------------------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------------------
+// ACT / FACT: the hidden and final activations as compile-time constants (the common
+// tanh / identity chip), or kActRuntime to read them from the geometry.  Fixing them lets
+// the compiler specialise the per-pixel epilogue loops.
+constexpr int kActRuntime = -1;
+
+template <int ACT, int FACT>
 __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
   extern __shared__ float4 smem4[];
   uint64_t* hbar = reinterpret_cast<uint64_t*>(smem4);   // staging barrier (16 B slot)
@@ -272,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
     FFTF_MARK(0, 0);
     fwd2d(X, g.Fh, stw, Ln);
     FFTF_MARK(0, 1);
-    const int act_id = last ? g.fact : g.act;
+    const int act_id = last ? (FACT != kActRuntime ? FACT : g.fact) : (ACT != kActRuntime ? ACT : g.act);
     const float slope = last ? g.fslope : g.slope;
     for (int p = tid; p < g.P; p += nt) { lin[p] = 0.f; acc[p] = 0.f; }
 
@@ -410,6 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
 // ---------------------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------------------
+template <int ACT, int FACT>
 __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   extern __shared__ float4 smem4[];
   const Geo& g = a.g;
@@ -532,8 +539,9 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
       for (int i = tid; i < kPlane; i += nt) D[i] = make_float2(0.f, 0.f);
     FFTF_MARK(1, 1);
     const float* ZH = a.zhat + ((size_t)b * g.d + t) * M * P;
-    const int act_id = last ? g.fact : g.act;     // universe mode runs the last step's ROI
-    const float slope = last ? g.fslope : g.slope;  // epilogue with the final activation
+    // universe mode runs the last step's ROI epilogue with the final activation
+    const int act_id = last ? (FACT != kActRuntime ? FACT : g.fact) : (ACT != kActRuntime ? ACT : g.act);
+    const float slope = last ? g.fslope : g.slope;
 
     for (int j = 0; j < pairs; ++j) {
       const int m1 = 2 * j, m2 = 2 * j + 1;
@@ -787,13 +795,18 @@ nc_status fftf_prestep_spectra(const Geo& g, const StepParams& sp, const float* 
   return launched("fftf_prestep_spectra_kernel launch");
 }
 
+// The tanh hidden / identity final activation pair runs the specialised kernels.
+static bool fixed_acts(const Geo& g) { return g.act == NC_ACT_TANH && g.fact == NC_ACT_NONE; }
+
 nc_status fftf_forward(const FftfArgs& args, cudaStream_t st) {
   FftfArgs a = args;
   a.stage = fftf_fwd_smem(a.g, true) <= kFftfSmemMax ? 1 : 0;
   const size_t smem = fftf_fwd_smem(a.g, a.stage != 0);
-  NC_CUDA_CHECK(cudaFuncSetAttribute((const void*)fftf_fwd_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  fftf_fwd_kernel<<<a.batch, kThreads, smem, st>>>(a);
+  const void* fn = fixed_acts(a.g) ? (const void*)fftf_fwd_kernel<NC_ACT_TANH, NC_ACT_NONE>
+                                   : (const void*)fftf_fwd_kernel<kActRuntime, kActRuntime>;
+  NC_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  void* kargs[] = {&a};
+  NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(a.batch), dim3(kThreads), kargs, smem, st));
   return launched("fftf_fwd_kernel launch");
 }
 
@@ -802,9 +815,11 @@ nc_status fftf_backward(const FftfArgs& args, cudaStream_t st) {
   const bool ring = a.gring != nullptr;
   a.stage = (a.g.P % 4 == 0 && fftf_bwd_smem(a.g, ring, true) <= kFftfSmemMax) ? 1 : 0;
   const size_t smem = fftf_bwd_smem(a.g, ring, a.stage != 0);
-  NC_CUDA_CHECK(cudaFuncSetAttribute((const void*)fftf_bwd_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  fftf_bwd_kernel<<<a.batch, kThreads, smem, st>>>(a);
+  const void* fn = fixed_acts(a.g) ? (const void*)fftf_bwd_kernel<NC_ACT_TANH, NC_ACT_NONE>
+                                   : (const void*)fftf_bwd_kernel<kActRuntime, kActRuntime>;
+  NC_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  void* kargs[] = {&a};
+  NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(a.batch), dim3(kThreads), kargs, smem, st));
   return launched("fftf_bwd_kernel launch");
 }
 
