@@ -268,6 +268,7 @@ static FftfArgs fftf_args(const Prepared& pr, void* ws, const float* inputs, int
   a.gpix = at<float>(ws, L.gpix);
   a.gdpart = at<float>(ws, L.gdpart);
   a.gring = at<float>(ws, L.f_gring);
+  a.xspec = at<float2>(ws, L.f_xspec);
   return a;
 }
 

@@ -277,6 +277,10 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
     load_field(a, X, t == 0 ? nullptr : lin, a.inputs + (size_t)b * g.n_in, tid, nt);
     FFTF_MARK(0, 0);
     fwd2d(X, g.Fh, stw, Ln);
+    if (a.train && a.xspec) {          // the backward reuses this step's field spectrum
+      float2* xo = a.xspec + ((size_t)b * g.d + t) * kPlane;
+      for (int i = tid; i < kPlane; i += nt) xo[i] = X[i];
+    }
     FFTF_MARK(0, 1);
     const int act_id = last ? (FACT != kActRuntime ? FACT : g.fact) : (ACT != kActRuntime ? ACT : g.act);
     const float slope = last ? g.fslope : g.slope;
@@ -424,8 +428,9 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   const size_t P = (size_t)g.P, M = (size_t)g.M;
   const int pairs = g.M / 2;
   const int FF = g.Fh * g.Fw;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem4);   // staging barriers: [0] planes, [1] spectra
-  float2* stw = reinterpret_cast<float2*>(smem4 + 1);
+  // staging barriers: [0] saved planes, [1] filter-pair spectrum, [2] field spectrum
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem4);
+  float2* stw = reinterpret_cast<float2*>(smem4 + 2);
   float2* X = stw + kN;
   float2* Wp = X + kPlane;
   float2* D = Wp + kPlane;
@@ -450,6 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   if (stage && tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
+    mbar_init(&bars[2], 1);
   }
   __syncthreads();
   // Saved planes 2j, 2j+1 of step t_ (8P contiguous bytes, P % 4 == 0) -> zs, and the
@@ -480,9 +486,25 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
                  kPlaneChunk, &bars[1]);
     }
   };
+  // the forward's field spectrum of step t_ -> X (four bulk copies); X is free from the
+  // last column pass of the step before (the field adjoint uses D)
+  const bool xstage = stage && a.xspec != nullptr;
+  unsigned xuse = 0;
+  auto issue_x = [&](int t_) {
+    if (tid < 32) {
+      if (tid == 0) mbar_expect_tx(&bars[2], kPlaneBytes);
+      __syncwarp();
+      fence_proxy_async();
+      if (tid < 4)
+        bulk_g2s(reinterpret_cast<char*>(X) + tid * kPlaneChunk,
+                 reinterpret_cast<const char*>(a.xspec + ((size_t)b * g.d + t_) * kPlane) + tid * kPlaneChunk,
+                 kPlaneChunk, &bars[2]);
+    }
+  };
   if (stage) {
     issue_z(g.d - 1, 0);
     if (g.d > 1) issue_h(0);
+    if (xstage) issue_x(g.d - 1);
   }
   int rpar = 0;                  // block_sum4 half
   FFTF_T0();
@@ -532,9 +554,14 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
 
   for (int t = g.d - 1; t >= 0; --t) {
     const bool last = (t == g.d - 1);
-    const float* xs = t > 0 ? a.xsave + ((size_t)b * (g.d - 1) + (t - 1)) * P : nullptr;
-    load_field(a, X, xs, a.inputs + (size_t)b * g.n_in, tid, nt);
-    fwd2d(X, g.Fh, stw, Ln);
+    if (xstage) {
+      mbar_wait(&bars[2], xuse & 1u);
+      ++xuse;
+    } else {
+      const float* xs = t > 0 ? a.xsave + ((size_t)b * (g.d - 1) + (t - 1)) * P : nullptr;
+      load_field(a, X, xs, a.inputs + (size_t)b * g.n_in, tid, nt);
+      fwd2d(X, g.Fh, stw, Ln);
+    }
     if (t > 0)
       for (int i = tid; i < kPlane; i += nt) D[i] = make_float2(0.f, 0.f);
     FFTF_MARK(1, 1);
@@ -645,6 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
       if (stage) {                       // the next spectrum lands during this pair
         if (t > 0 && j + 1 < pairs) issue_h(j + 1);
         else if (j + 1 == pairs && t > 1) issue_h(0);
+        if (xstage && j + 1 == pairs && t > 0) issue_x(t - 1);
       }
       FFTF_MARK(1, 5);
       // corr(X, gz_{2j}) - i corr(X, gz_{2j+1}) at lags [0, kh) x [0, kw): inverse row pass
@@ -776,7 +804,7 @@ size_t fftf_fwd_smem(const Geo& g, bool stage) {
 size_t fftf_bwd_smem(const Geo& g, bool ring, bool stage) {
   size_t f = 4 * (size_t)g.P + (size_t)g.M * g.K + (size_t)g.n_out * g.M + 160 +
              (ring ? (size_t)g.Fh * g.Fw : 0) + (stage ? 2 * (size_t)g.P : 0);
-  return 16 + sizeof(float2) * (kN + (3 + (stage ? 1 : 0)) * (size_t)kPlane) + sizeof(float) * f +
+  return 32 + sizeof(float2) * (kN + (3 + (stage ? 1 : 0)) * (size_t)kPlane) + sizeof(float) * f +
          sizeof(int16_t) * (size_t)g.P + 16;
 }
 

@@ -31,6 +31,7 @@ struct FftfArgs {
   float* gring;               // backward: (B, Fh*Fw) per-sample ring gradients (VALID, d>1) or null
   float* uroi;                // universe mode forward: (B, P) last-step ROI cells, else null
   const float* guroi;         // universe mode backward: (B, P) their gradient, else null
+  float2* xspec;              // train: (B, d, 64 x 66) field spectra the forward computed
   int stage;                  // set by fftf_forward / fftf_backward: bulk-copy staging on
 };
 

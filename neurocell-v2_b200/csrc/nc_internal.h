@@ -71,6 +71,7 @@ struct WsLayout {
   size_t f_gpart;         // (kRedChunks, 3, P) per-chunk pixel-gradient partials (train)
   size_t f_h;             // fused small-grid kernels: (M/2, 64, 64) pair spectra
   size_t f_gring;         // fused small-grid kernels: (B, Fh*Fw) ring gradients (train)
+  size_t f_xspec;         // fused small-grid kernels: (B, d, 64 x 66) field spectra (train)
   size_t total;
 };
 

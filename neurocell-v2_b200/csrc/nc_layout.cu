@@ -134,7 +134,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
   L.zhat = train ? take(fl * B * g.d * M * P) : SIZE_MAX;
   L.rstd = train ? take(fl * B * g.d * M) : SIZE_MAX;
   L.f_field = L.f_xhat = L.f_tmp = L.f_gspec = L.f_mean = L.f_rstd = SIZE_MAX;
-  L.f_q = L.f_dgacc = L.f_gz = L.f_dx = L.f_gpart = L.f_h = L.f_gring = SIZE_MAX;
+  L.f_q = L.f_dgacc = L.f_gz = L.f_dx = L.f_gpart = L.f_h = L.f_gring = L.f_xspec = SIZE_MAX;
   if (g.algo == NC_CONV_FFT && fftf_fits(g)) {
     // fused per-sample FFT kernels: spectra tables + per-sample partials only
     if (f_smem) *f_smem = true;
@@ -146,6 +146,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
     if (train) {
       L.gpix = take(fl * B * 3 * P);
       L.gdpart = take(fl * B * M * g.K);
+      L.f_xspec = take(c64 * B * (size_t)g.d * kFftfPlane);   // the forward's field spectra
       const bool ringp = g.padding == NC_PAD_VALID && g.d > 1;
       L.f_gring = ringp ? take(fl * B * (size_t)g.Fh * g.Fw) : SIZE_MAX;
       L.redscr = take(fl * kRedChunks * (3 * P + M * g.K + (ringp ? (size_t)g.Fh * g.Fw : 0)));
