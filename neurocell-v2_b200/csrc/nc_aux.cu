@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 
 #include "nc_common.cuh"
+#include "nc_internal.h"
 #include "nc_kernels.cuh"
 #include "nc_prestep.cuh"
 
@@ -138,10 +139,16 @@ __global__ void border_grad_kernel(Geo g, const float* __restrict__ G,
 
 // Value idx of a batch-summed array: the array itself, or (rows > 0) the sum over `rows`
 // chunk partials of stride `stride`, added in chunk order.
+// All loads are issued before the first add (rows <= kRedChunks), the adds run in chunk order.
 __device__ __forceinline__ float chunk_sum(const float* __restrict__ a, int idx, int rows, size_t stride) {
   if (rows <= 0) return a[idx];
+  float v[kRedChunks];
+#pragma unroll
+  for (int r = 0; r < kRedChunks; ++r) v[r] = r < rows ? a[(size_t)r * stride + idx] : 0.f;
   float acc = 0.f;
-  for (int r = 0; r < rows; ++r) acc += a[(size_t)r * stride + idx];
+#pragma unroll
+  for (int r = 0; r < kRedChunks; ++r)
+    if (r < rows) acc += v[r];
   return acc;
 }
 
