@@ -31,7 +31,6 @@ __global__ void batch_step_sum4_kernel(const float* in, int batch, int d, int t0
                                        int bc, float* part);
 __global__ void rows_sum_kernel(const float* part, int rows, int n, float* out);
 __global__ void seg_batch_sum1_kernel(SegSum j, int batch, int bc, float* part);
-__global__ void seg_batch_sum2_kernel(SegSum j, int rows, const float* part);
 
 // out[i] = sum_b sum_{t0<=t<d} in[(b*d+t)*slot + i] in two deterministic stages over
 // kRedChunks sample chunks (n, slot multiples of 4; `scratch` holds kRedChunks*n floats).
@@ -559,32 +558,27 @@ static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const flo
     if (g_prof.bs) NC_CUDA_CHECK(cudaEventRecord(g_prof.bs, st));
     NC_CHECK(fftf_backward(fa, st));
     if (g_prof.be) NC_CUDA_CHECK(cudaEventRecord(g_prof.be, st));
-    float* gsum = at<float>(d_ws, L.gsum);
-    float* gdsum = at<float>(d_ws, L.gdsum);
-    float* gborder = fa.gring ? at<float>(d_ws, L.gborder) : nullptr;
     const int P3 = 3 * g.P, MK = g.M * g.K, FF = g.Fh * g.Fw, HW = g.H * g.W;
     {
-      // fixed-order batch sums of the per-sample partials, in two stages
+      // fixed-order batch sums of the per-sample partials, in two stages: chunk partials
+      // here, the chunk sums inside the pre-step adjoint
       SegSum j;
       memset(&j, 0, sizeof(j));
-      j.in[0] = fa.gpix; j.out[0] = gsum; j.n[0] = P3;
-      j.in[1] = fa.gdpart; j.out[1] = gdsum; j.n[1] = MK;
+      j.in[0] = fa.gpix; j.n[0] = P3;
+      j.in[1] = fa.gdpart; j.n[1] = MK;
       j.nseg = 2;
-      if (gborder) { j.in[2] = fa.gring; j.out[2] = gborder; j.n[2] = FF; j.nseg = 3; }
+      if (fa.gring) { j.in[2] = fa.gring; j.n[2] = FF; j.nseg = 3; }
       j.total = j.n[0] + j.n[1] + j.n[2];
       const int chunks = batch < kRedChunks ? batch : kRedChunks;
       const int bc = (batch + chunks - 1) / chunks;
       float* part = at<float>(d_ws, L.redscr);
       seg_batch_sum1_kernel<<<dim3((j.total + 255) / 256, chunks), 256, 0, st>>>(j, batch, bc, part);
       NC_CHECK(launch_check("seg_batch_sum1_kernel launch"));
-      // the second stage (chunk order) runs inside the pre-step adjoint
       prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(
-          g, pr.sp, cell_params, filters, pr.owm, pr.bmask, part, gborder ? part + P3 + MK : nullptr,
+          g, pr.sp, cell_params, filters, pr.owm, pr.bmask, part, fa.gring ? part + P3 + MK : nullptr,
           part + P3, gringf, g_cell_params, g_filters, chunks, (size_t)j.total);
       NC_CHECK(launch_check("prestep_bwd_kernel launch"));
     }
-    (void)gsum;
-    (void)gdsum;
     clear_error();
     return NC_OK;
   }

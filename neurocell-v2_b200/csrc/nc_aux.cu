@@ -63,7 +63,8 @@ __global__ void batch_step_sum4_kernel(const float* __restrict__ in, int batch, 
 
 // Batch sums of up to three per-sample partial arrays (sample stride = their length) in two
 // deterministic stages: block row y sums samples [y*bc, (y+1)*bc) of every element of the
-// concatenated arrays into part[y][*]; stage 2 adds the rows in order into the outputs.
+// concatenated arrays into part[y][*]; the second stage (chunk_sum in prestep_bwd_kernel)
+// adds the rows in order.
 __device__ __forceinline__ int seg_of(const SegSum& j, int i, int* off) {
   int s = 0, o = 0;
   while (s + 1 < j.nseg && i >= o + j.n[s]) { o += j.n[s]; ++s; }
@@ -82,16 +83,6 @@ __global__ void seg_batch_sum1_kernel(SegSum j, int batch, int bc, float* __rest
 #pragma unroll 4
   for (int b = b0; b < b1; ++b) acc += j.in[s][(size_t)b * n + e];
   part[(size_t)blockIdx.y * j.total + i] = acc;
-}
-
-__global__ void seg_batch_sum2_kernel(SegSum j, int rows, const float* __restrict__ part) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= j.total) return;
-  int off;
-  const int s = seg_of(j, i, &off);
-  float acc = 0.f;
-  for (int r = 0; r < rows; ++r) acc += part[(size_t)r * j.total + i];
-  j.out[s][i - off] = acc;
 }
 
 __global__ void rows_sum_kernel(const float* __restrict__ part, int rows, int n, float* __restrict__ out) {

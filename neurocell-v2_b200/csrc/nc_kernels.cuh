@@ -56,10 +56,10 @@ struct BwdArgs {
   int batch;
 };
 
-// Up to three (batch, n_s) per-sample partial arrays summed over the batch.
+// Up to three (batch, n_s) per-sample partial arrays, summed over sample chunks into one
+// (chunks, total) partial array (seg_batch_sum1_kernel).
 struct SegSum {
   const float* in[3];
-  float* out[3];
   int n[3];
   int nseg, total;
 };

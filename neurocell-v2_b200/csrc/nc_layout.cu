@@ -150,9 +150,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
       const bool ringp = g.padding == NC_PAD_VALID && g.d > 1;
       L.f_gring = ringp ? take(fl * B * (size_t)g.Fh * g.Fw) : SIZE_MAX;
       L.redscr = take(fl * kRedChunks * (3 * P + M * g.K + (ringp ? (size_t)g.Fh * g.Fw : 0)));
-      L.gsum = take(fl * 3 * P);
-      L.gdsum = take(fl * M * g.K);
-      L.gborder = take(fl * HW);
+      L.gsum = L.gdsum = L.gborder = SIZE_MAX;   // summed inside the pre-step adjoint
     } else {
       L.gpix = L.gdpart = L.gsum = L.gdsum = L.gborder = SIZE_MAX;
     }
