@@ -228,3 +228,30 @@ def test_exchange_timeout_sets_status_and_skips_the_update():
             torch.cuda.synchronize()
             for b in bufs:
                 lib.nc_dp_free(b)
+
+
+def test_five_step_sgd_trajectory_matches_oracle():
+    """Five graph-captured SGD steps of the fused step on the ALU chip follow the float64
+    oracle's trajectory (the reference's multi-step trajectory parity,
+    tests/unit_vnn_alu_parity.py:141-194 and tests/unit_kernels_pallas.py:130-198, with SGD
+    instead of AdamW): parameters within rel-L2 1e-5 after five steps, every loss within
+    1e-5 relative."""
+    cell, filt, xs, ys = _alu(5, 32, 33)
+    dev = torch.device("cuda:0")
+    topo = nc.ChipTopology2D.alu_chip()
+    p = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
+    st = nc.trainer.VNNTrainStep(topo, p, 32, lr=1e-2, in_shapes=((8, 1),) * 3)   # the bench's SGD
+    xd, yd = torch.tensor(xs, device=dev), torch.tensor(ys, device=dev)
+    st.load_batch(xd[0], yd[0])
+    st.capture()
+    geom = O.alu_geometry()
+    c, f = cell.astype(np.float64), filt.astype(np.float64)
+    for i in range(5):
+        loss = float(st.step(xd[i], yd[i]))
+        lval, c, f, _, _ = O.train_step(c, f, xs[i].reshape(32, 3, 8, 1), ys[i], geom, O.Config(), lr=1e-2)
+        assert abs(loss - lval) / lval <= 1e-5, (i, loss, lval)
+    q = st.params
+    torch.cuda.synchronize()
+    rc = np.linalg.norm(q.cell_params.cpu().numpy() - c) / np.linalg.norm(c)
+    rf = np.linalg.norm(q.greens_filters.cpu().numpy() - f) / np.linalg.norm(f)
+    assert rc <= 1e-5 and rf <= 1e-5, (rc, rf)
