@@ -48,6 +48,7 @@ struct Planes {
   int pack;     // 1: a line holds samples (2g, 2g+1) as (re, im); 0: one sample, im = 0
   int units;    // lines / rows = (nsamp or pairs) * ms
   float scale;
+  float2* rowstats;   // rows_inv: per stored row (mean, M2) of its `cols` values, or null
 };
 
 __device__ __forceinline__ int even_up(int x) { return (x + 1) & ~1; }
@@ -121,6 +122,39 @@ __global__ void __launch_bounds__(kFftThreads) rows_inv_kernel(const float2* __r
     const float2 v = s[l * LS + pidx(e)];
     a.ptr[(size_t)b1 * a.sstride + off] = v.x * a.scale;
     if (a.pack && b1 + 1 < a.nsamp) a.ptr[(size_t)(b1 + 1) * a.sstride + off] = v.y * a.scale;
+  }
+  if (a.rowstats) {
+    // centred statistics of each stored row, two passes over the row in shared memory (one
+    // warp per row): the first stage of the plane statistics (plane_stats_rows_kernel)
+    const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
+    const float inv_c = 1.0f / (float)a.cols;
+    for (int l = warp; l < nl; l += nw) {
+      const float2* sl = s + l * LS;
+      float sx = 0.f, sy = 0.f;
+      for (int e = lane; e < a.cols; e += 32) {
+        const float2 v = sl[pidx(e)];
+        sx += v.x * a.scale;
+        sy += v.y * a.scale;
+      }
+      const float mx = warp_sum(sx) * inv_c, my = warp_sum(sy) * inv_c;
+      float qx = 0.f, qy = 0.f;
+      for (int e = lane; e < a.cols; e += 32) {
+        const float2 v = sl[pidx(e)];
+        const float dx = v.x * a.scale - mx, dy = v.y * a.scale - my;
+        qx = fmaf(dx, dx, qx);
+        qy = fmaf(dy, dy, qy);
+      }
+      qx = warp_sum(qx);
+      qy = warp_sum(qy);
+      if (lane == 0) {
+        const int line = line0 + l;
+        const int u = line / a.rows, r = line - u * a.rows;
+        const int gs = u / a.ms, m = u - gs * a.ms;
+        const int b1 = a.pack ? 2 * gs : gs;
+        a.rowstats[((size_t)b1 * a.ms + m) * a.rows + r] = make_float2(mx, qx);
+        if (a.pack && b1 + 1 < a.nsamp) a.rowstats[((size_t)(b1 + 1) * a.ms + m) * a.rows + r] = make_float2(my, qy);
+      }
+    }
   }
 }
 
@@ -260,65 +294,33 @@ __global__ void field_interior_kernel(Geo g, float* __restrict__ field, const fl
 // forward epilogues (planes z at z + b*zs + m*P)
 // ---------------------------------------------------------------------------------------
 
-// Plane sums for the per-(b, m) statistics: float4 loads with four independent partial
-// sums when `vec` (P % 4 == 0 and 16-byte aligned planes), then a fixed-order combination,
-// so every call adds in the same order.
-__device__ __forceinline__ float plane_sum(const float* __restrict__ a, int P, int vec) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  if (vec) {
-    const float4* a4 = reinterpret_cast<const float4*>(a);
-    for (int i = threadIdx.x; i < P / 4; i += blockDim.x) {
-      const float4 v = a4[i];
-      s0 += v.x; s1 += v.y; s2 += v.z; s3 += v.w;
-    }
-  } else {
-    for (int p = threadIdx.x; p < P; p += blockDim.x) s0 += a[p];
-  }
-  return (s0 + s1) + (s2 + s3);
-}
-
-// sum (a - mu)^2 over the plane (centred second pass).
-__device__ __forceinline__ float plane_sq(const float* __restrict__ a, int P, float mu, int vec) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  if (vec) {
-    const float4* a4 = reinterpret_cast<const float4*>(a);
-    for (int i = threadIdx.x; i < P / 4; i += blockDim.x) {
-      const float4 v = a4[i];
-      const float d0 = v.x - mu, d1 = v.y - mu, d2 = v.z - mu, d3 = v.w - mu;
-      s0 = fmaf(d0, d0, s0); s1 = fmaf(d1, d1, s1); s2 = fmaf(d2, d2, s2); s3 = fmaf(d3, d3, s3);
-    }
-  } else {
-    for (int p = threadIdx.x; p < P; p += blockDim.x) {
-      const float d = a[p] - mu;
-      s0 = fmaf(d, d, s0);
-    }
-  }
-  return (s0 + s1) + (s2 + s3);
-}
-
-// Per-(b, m) mean and 1/sqrt(var + eps), centred two-pass (kernels_pallas.py:200-205).  The
-// grid covers a bounded number of planes at a time (2 CTAs per SM, each looping over
-// planes), so a plane's second pass reads it back from L2 rather than HBM.
-__global__ void __launch_bounds__(kStatThreads) plane_stats_kernel(Geo g, const float* __restrict__ z,
-                                                                   size_t zs, float* mean, float* rstd,
-                                                                   float* rstd_save, int t, int nplanes,
-                                                                   int vec) {
+// Per-(b, m) mean and 1/sqrt(var + eps) from the rows' centred statistics (equal-sized
+// rows: the plane mean is the mean of the row means, M2 = sum_r M2_r + n (mean_r - mean)^2),
+// the two-stage variance the reference uses for tiled planes (kernels_pallas.py:740-837).
+__global__ void __launch_bounds__(kEpiThreads) plane_stats_rows_kernel(Geo g, const float2* __restrict__ rowstats,
+                                                                       float* mean, float* rstd,
+                                                                       float* rstd_save, int t) {
   __shared__ float red[33];
-  for (int bm = blockIdx.x; bm < nplanes; bm += gridDim.x) {
-    const int b = bm / g.M, m = bm - b * g.M;
-    const float* zp = z + (size_t)b * zs + (size_t)m * g.P;
-    float mu = 0.f, rs = 1.f;
-    if (g.norm) {
-      const float inv_n = 1.0f / (float)g.P;
-      mu = block_sum(plane_sum(zp, g.P, vec), red) * inv_n;
-      const float var = block_sum(plane_sq(zp, g.P, mu, vec), red) * inv_n;
-      rs = 1.0f / sqrtf(var + kNormEps);
+  const int bm = blockIdx.x, b = bm / g.M, m = bm - b * g.M;
+  const int rows = g.roi_h;
+  const float2* rs_ = rowstats + (size_t)bm * rows;
+  float mu = 0.f, rs = 1.f;
+  if (g.norm) {
+    float s = 0.f;
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) s += rs_[r].x;
+    mu = block_sum(s, red) / (float)rows;
+    float q = 0.f;
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+      const float d = rs_[r].x - mu;
+      q += rs_[r].y + (float)g.roi_w * d * d;
     }
-    if (threadIdx.x == 0) {
-      mean[bm] = mu;
-      rstd[bm] = rs;
-      if (rstd_save) rstd_save[((size_t)b * g.d + t) * g.M + m] = rs;
-    }
+    const float var = block_sum(q, red) / (float)g.P;
+    rs = 1.0f / sqrtf(var + kNormEps);
+  }
+  if (threadIdx.x == 0) {
+    mean[bm] = mu;
+    rstd[bm] = rs;
+    if (rstd_save) rstd_save[((size_t)b * g.d + t) * g.M + m] = rs;
   }
 }
 
@@ -811,13 +813,13 @@ nc_status fft_forward(const FftCall& c, cudaStream_t st) {
     float* z = c.train ? c.zhat + (size_t)t * M * P : c.zscr;
     const size_t zs = c.train ? (size_t)g.d * M * P : M * P;
     {
-      Planes zp{z, zs, B, g.M, g.roi_h, g.roi_w, g.P, g.roi_w, 1, pairs * g.M, 1.0f};
+      Planes zp{z, zs, B, g.M, g.roi_h, g.roi_w, g.P, g.roi_w, 1, pairs * g.M, 1.0f, c.rowstats};
       NC_CHECK(rows_inv(c.tmp, zp, g.Nw, c.tw_w, st));
     }
-    plane_stats_kernel<<<stat_grid(B * g.M), kStatThreads, 0, st>>>(g, z, zs, c.mean, c.rstd,
-                                                                     c.train ? c.rstd_save : nullptr, t,
-                                                                     B * g.M, plane_vec(g, zs));
-    NC_CHECK(launched("plane_stats_kernel launch"));
+    // plane statistics from the row statistics the row pass wrote
+    plane_stats_rows_kernel<<<B * g.M, kEpiThreads, 0, st>>>(g, c.rowstats, c.mean, c.rstd,
+                                                             c.train ? c.rstd_save : nullptr, t);
+    NC_CHECK(launched("plane_stats_rows_kernel launch"));
     if (t < g.d - 1) {
       NC_CHECK(hidden_epi(g, c, z, zs, t, g.act, g.slope, nullptr, st));
     } else if (c.uroi) {

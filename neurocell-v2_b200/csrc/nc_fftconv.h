@@ -25,6 +25,7 @@ struct FftCall {
   float2* gspec;              // (M, Nh, Nw)
   float* mean;                // (B, M)
   float* rstd;                // (B, M)
+  float2* rowstats;           // (B, M, roi_h) per-row (mean, M2) of the forward planes
   float* zscr;                // (B, M, P) inference planes
   float* zhat;                // train: (B, d, M, P)
   float* rstd_save;           // train: (B, d, M)

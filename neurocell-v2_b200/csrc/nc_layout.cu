@@ -133,7 +133,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
   L.xsave = train ? take(fl * B * (dm1 ? dm1 : 1) * P) : SIZE_MAX;
   L.zhat = train ? take(fl * B * g.d * M * P) : SIZE_MAX;
   L.rstd = train ? take(fl * B * g.d * M) : SIZE_MAX;
-  L.f_field = L.f_xhat = L.f_tmp = L.f_gspec = L.f_mean = L.f_rstd = SIZE_MAX;
+  L.f_field = L.f_xhat = L.f_tmp = L.f_gspec = L.f_mean = L.f_rstd = L.f_rowstats = SIZE_MAX;
   L.f_q = L.f_dgacc = L.f_gz = L.f_dx = L.f_gpart = L.f_h = L.f_gring = L.f_xspec = SIZE_MAX;
   if (g.algo == NC_CONV_FFT && fftf_fits(g)) {
     // fused per-sample FFT kernels: spectra tables + per-sample partials only
@@ -173,6 +173,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
     L.f_gspec = take(c64 * M * NN);
     L.f_mean = take(fl * B * M);
     L.f_rstd = take(fl * B * M);
+    L.f_rowstats = take(c64 * B * M * (size_t)g.roi_h);
     L.fscr = SIZE_MAX;
     L.zscr = train ? SIZE_MAX : take(fl * B * M * P);
     L.gzscr = L.gpix = L.gdpart = L.gdelta = L.gdeltasum = L.redscr = SIZE_MAX;
