@@ -490,10 +490,13 @@ __global__ void port_gz_kernel(Geo g, StepParams sp, const int32_t* __restrict__
 }
 
 // Standardisation adjoint per (b, m): gz <- rstd (gz - mean(gz) - zh mean(gz zh)).
+// gzpart (not null): the sums come from hidden_gz_kernel's per-CTA partials (ncta of them,
+// added in CTA order) and the planes are read once.
 __global__ void __launch_bounds__(kStatThreads) norm_bwd_kernel(Geo g, float* __restrict__ gz,
                                                                  const float* __restrict__ zh_t, size_t zs,
                                                                  const float* __restrict__ rstd_save, int t,
-                                                                 int nplanes, int vec) {
+                                                                 int nplanes, int vec,
+                                                                 const float* __restrict__ gzpart, int ncta) {
   __shared__ float red[33];
   const float inv_n = 1.0f / (float)g.P;
   for (int bm = blockIdx.x; bm < nplanes; bm += gridDim.x) {
@@ -501,7 +504,12 @@ __global__ void __launch_bounds__(kStatThreads) norm_bwd_kernel(Geo g, float* __
     float* gp = gz + (size_t)bm * g.P;
     const float* zp = zh_t + (size_t)b * zs + (size_t)m * g.P;
     float s1 = 0.f, s2 = 0.f, u1 = 0.f, u2 = 0.f;
-    if (vec) {
+    if (gzpart) {
+      for (int k = threadIdx.x; k < ncta; k += blockDim.x) {
+        s1 += gzpart[((size_t)k * nplanes + bm) * 2 + 0];
+        s2 += gzpart[((size_t)k * nplanes + bm) * 2 + 1];
+      }
+    } else if (vec) {
       const float4* g4 = reinterpret_cast<const float4*>(gp);
       const float4* z4 = reinterpret_cast<const float4*>(zp);
       for (int i = threadIdx.x; i < g.P / 4; i += blockDim.x) {
@@ -551,14 +559,20 @@ __device__ __forceinline__ float field_grad(const Geo& g, const float* dxb, int 
 // ROI-epilogue adjoint (kernels_pallas.py:221-291) for the samples of chunk blockIdx.y:
 // the cell gradient comes from the field adjoint dx (hidden step t-1) or, in universe mode,
 // from gy_roi (B, P) with the final activation; per-chunk pixel-gradient partials go to gpart.
+// gzpart (not null): the CTA's sums of gz and gz * zhat over its pixels per (b, m) of its
+// chunk, at gzpart[((blockIdx.x * B + b) * M + m) * 2 + {0, 1}] (warp shuffles, then the
+// warps in order), so the standardisation adjoint needs one pass.  `red` in dynamic shared
+// memory holds bc * M * 2 values per warp.
 template <int V>
 __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__ dx,
                                  const float* __restrict__ zh_t, size_t zs, float* __restrict__ gz,
                                  float* __restrict__ gpart, int B, int bc, int act_id, float slope,
-                                 const float* __restrict__ gy_roi) {
+                                 const float* __restrict__ gy_roi, float* __restrict__ gzpart) {
+  extern __shared__ float red[];
   const int gi = blockIdx.x * blockDim.x + threadIdx.x;
-  if (gi * V >= g.P) return;
-  const int p0 = gi * V;
+  const bool on = gi * V < g.P;       // threads past the plane join the warp sums with zeros
+  const int p0 = on ? gi * V : 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int k = blockIdx.y;
   const int b0 = k * bc, b1 = min(B, b0 + bc);
   const size_t P = (size_t)g.P, FF = (size_t)g.Fh * g.Fw;
@@ -573,14 +587,20 @@ __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       const int p = p0 + v, r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
-      gy[v] = gy_roi ? gy_roi[(size_t)b * P + p] : field_grad(g, dx + (size_t)b * FF, r, c);
+      gy[v] = !on ? 0.f : gy_roi ? gy_roi[(size_t)b * P + p] : field_grad(g, dx + (size_t)b * FF, r, c);
       lin[v] = 0.f; act[v] = 0.f; dsum[v] = 0.f;
     }
     const float* ZH = zh_t + (size_t)b * zs + p0;
     float* GZ = gz + (size_t)b * g.M * P + p0;
     for (int m = 0; m < g.M; ++m) {
       float zv[V], gv[V];
-      ldv<V>(ZH + (size_t)m * P, zv);
+      if (on) {
+        ldv<V>(ZH + (size_t)m * P, zv);
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v) zv[v] = 0.f;
+      }
+      float s1 = 0.f, s2 = 0.f;
 #pragma unroll
       for (int v = 0; v < V; ++v) {
         float dd;
@@ -588,9 +608,20 @@ __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__
         lin[v] += zv[v];
         act[v] += av;
         dsum[v] += dd;
-        gv[v] = we[v] * gy[v] + se[v] * gy[v] * dd;
+        gv[v] = on ? we[v] * gy[v] + se[v] * gy[v] * dd : 0.f;
+        s1 += gv[v];
+        s2 = fmaf(gv[v], zv[v], s2);
       }
-      stv<V>(GZ + (size_t)m * P, gv);
+      if (on) stv<V>(GZ + (size_t)m * P, gv);
+      if (gzpart) {
+        s1 = warp_sum(s1);
+        s2 = warp_sum(s2);
+        if (lane == 0) {
+          float* rw = red + ((size_t)((b - b0) * g.M + m) * nw + warp) * 2;
+          rw[0] = s1;
+          rw[1] = s2;
+        }
+      }
     }
 #pragma unroll
     for (int v = 0; v < V; ++v) {
@@ -599,9 +630,21 @@ __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__
       gp2[v] += se[v] * gy[v] * dsum[v];
     }
   }
-  stv<V>(gpart + ((size_t)k * 3 + 0) * P + p0, gp0);
-  stv<V>(gpart + ((size_t)k * 3 + 1) * P + p0, gp1);
-  stv<V>(gpart + ((size_t)k * 3 + 2) * P + p0, gp2);
+  if (on) {
+    stv<V>(gpart + ((size_t)k * 3 + 0) * P + p0, gp0);
+    stv<V>(gpart + ((size_t)k * 3 + 1) * P + p0, gp1);
+    stv<V>(gpart + ((size_t)k * 3 + 2) * P + p0, gp2);
+  }
+  if (gzpart) {
+    __syncthreads();
+    const int nv = (b1 - b0) * g.M * 2;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+      const int bm = i >> 1, e = i & 1;      // bm = (b - b0) * M + m
+      float s = 0.f;
+      for (int w = 0; w < nw; ++w) s += red[((size_t)bm * nw + w) * 2 + e];
+      gzpart[(((size_t)blockIdx.x * B + b0) * g.M + bm) * 2 + e] = s;
+    }
+  }
 }
 
 // gsum += sum over chunks of gpart (chunk order).
@@ -730,14 +773,26 @@ nc_status hidden_epi(const Geo& g, const FftCall& c, float* z, size_t zs, int t,
 }
 
 // ROI-epilogue adjoint (see hidden_gz_kernel); 4 pixels per thread when possible.
+// *ncta: the number of per-CTA sum partials written to c.gzpart for the standardisation
+// adjoint, or 0 when they did not fit the kernel's shared memory (norm_bwd then takes two
+// passes).
 nc_status hidden_gz(const Geo& g, const FftCall& c, const float* zh, size_t zs, int nch, int bc, int act_id,
-                    float slope, const float* gy_roi, cudaStream_t st) {
-  if (plane_vec(g, zs))
-    hidden_gz_kernel<4><<<dim3(blocks_for((size_t)g.P / 4, 256), nch), 256, 0, st>>>(
-        g, c.sp, c.dx, zh, zs, c.gz, c.gpart, c.batch, bc, act_id, slope, gy_roi);
-  else
-    hidden_gz_kernel<1><<<dim3(blocks_for((size_t)g.P, 256), nch), 256, 0, st>>>(
-        g, c.sp, c.dx, zh, zs, c.gz, c.gpart, c.batch, bc, act_id, slope, gy_roi);
+                    float slope, const float* gy_roi, int* ncta, cudaStream_t st) {
+  const size_t red = sizeof(float) * (size_t)bc * g.M * (256 / 32) * 2;
+  const bool part = c.gzpart != nullptr && red <= 48 * 1024;
+  float* gzp = part ? c.gzpart : nullptr;
+  const size_t smem = part ? red : 0;
+  unsigned grid;
+  if (plane_vec(g, zs)) {
+    grid = blocks_for((size_t)g.P / 4, 256);
+    hidden_gz_kernel<4><<<dim3(grid, nch), 256, smem, st>>>(g, c.sp, c.dx, zh, zs, c.gz, c.gpart, c.batch,
+                                                            bc, act_id, slope, gy_roi, gzp);
+  } else {
+    grid = blocks_for((size_t)g.P, 256);
+    hidden_gz_kernel<1><<<dim3(grid, nch), 256, smem, st>>>(g, c.sp, c.dx, zh, zs, c.gz, c.gpart, c.batch,
+                                                            bc, act_id, slope, gy_roi, gzp);
+  }
+  *ncta = part ? (int)grid : 0;
   return launched("hidden_gz_kernel launch");
 }
 
@@ -859,8 +914,9 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
   // standardisation adjoint
   {
     const float* zh = c.zhat + (size_t)(g.d - 1) * M * P;
+    int ncta_out = 0;   // the port adjoint writes no partial sums
     if (c.guroi) {
-      NC_CHECK(hidden_gz(g, c, zh, zs, nch, bc, g.fact, g.fslope, c.guroi, st));
+      NC_CHECK(hidden_gz(g, c, zh, zs, nch, bc, g.fact, g.fslope, c.guroi, &ncta_out, st));
       gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
       NC_CHECK(launched("gsum_chunks_kernel launch"));
     } else {
@@ -870,7 +926,8 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
     }
     if (g.norm) {
       norm_bwd_kernel<<<stat_grid(B * g.M), kStatThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, g.d - 1,
-                                                                   B * g.M, plane_vec(g, zs));
+                                                                   B * g.M, plane_vec(g, zs),
+                                                                   ncta_out ? c.gzpart : nullptr, ncta_out);
       NC_CHECK(launched("norm_bwd_kernel launch"));
     }
   }
@@ -911,12 +968,14 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
     }
     // hidden-step adjoint of step t-1
     const float* zh = c.zhat + (size_t)(t - 1) * M * P;
-    NC_CHECK(hidden_gz(g, c, zh, zs, nch, bc, g.act, g.slope, nullptr, st));
+    int ncta = 0;
+    NC_CHECK(hidden_gz(g, c, zh, zs, nch, bc, g.act, g.slope, nullptr, &ncta, st));
     gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
     NC_CHECK(launched("gsum_chunks_kernel launch"));
     if (g.norm) {
       norm_bwd_kernel<<<stat_grid(B * g.M), kStatThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, t - 1,
-                                                                   B * g.M, plane_vec(g, zs));
+                                                                   B * g.M, plane_vec(g, zs),
+                                                                   ncta ? c.gzpart : nullptr, ncta);
       NC_CHECK(launched("norm_bwd_kernel launch"));
     }
   }
