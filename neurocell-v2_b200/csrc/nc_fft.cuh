@@ -475,5 +475,106 @@ __device__ void transform_lines_plan(float2* s, int L, int N, const float2* tw, 
     transform_lines<INV>(s, L, N, tw, tid, nt);
 }
 
+// ---------------------------------------------------------------------------------------
+// Two-stage transforms with the radix-R stage on global memory: the same arithmetic as
+// transform_lines_2s (same stage order, twiddles and output permutation), but stage A
+// takes its operands from global memory through ld(l, e) (forward) or hands its results
+// to st(l, e, v) (inverse) instead of going through shared memory, so each element costs
+// four shared-memory accesses instead of six.  Stage B and the copy on its side stay in
+// shared memory, where their 8-lane blocks are free of bank conflicts and the global side
+// stays fully coalesced.  For R = 1 (N = 64) callers use transform_lines_2s.
+//
+// LFAST = true (column tiles, L a power of two): consecutive lanes take consecutive lines,
+// so the global accesses of a warp coalesce across the tile's columns; the line stride is
+// then line_stride_cols(N), which keeps this mapping, stage B and the column-tile copy
+// loops free of bank conflicts.  LFAST = false (rows): consecutive lanes take consecutive
+// elements of a line, stride line_stride.
+// ---------------------------------------------------------------------------------------
+__host__ __device__ inline int line_stride_cols(int N) {
+  const int b = N + (N >> 3);
+  return b + ((4 - b) & 15);   // b rounded up to 4 (mod 16) float2 words
+}
+
+template <bool LFAST>
+__device__ __forceinline__ void task_of(int task, int L, int lgL, int& l, int& n2) {
+  if (LFAST) { l = task & (L - 1); n2 = task >> lgL; }
+  else { l = task >> 6; n2 = task & 63; }
+}
+
+// Forward, R > 1: stage A from ld(l, e) (natural order, e < N) into the lines, then stage B
+// in place; afterwards position 64 k1 + k2 of line l holds frequency k1 + R k2.  Starts
+// after a barrier that published the twiddles, ends with a barrier.
+template <int R, bool LFAST, class Ld>
+__device__ __forceinline__ void fwd_a_global(float2* s, int L, int lgL, int LS, const float2* tw, int tid,
+                                             int nt, Ld ld) {
+  for (int task = tid; task < L * 64; task += nt) {
+    int l, n2;
+    task_of<LFAST>(task, L, lgL, l, n2);
+    float2 v[R];
+#pragma unroll
+    for (int n1 = 0; n1 < R; ++n1) v[n1] = ld(l, n2 + 64 * n1);
+    dft_r<R, false>(v);
+#pragma unroll
+    for (int k1 = 1; k1 < R; ++k1) v[k1] = cmul(v[k1], tw[k1 * 64 + n2]);
+    float2* sl = s + l * LS;
+#pragma unroll
+    for (int k1 = 0; k1 < R; ++k1) sl[pidx(64 * k1 + n2)] = v[k1];
+  }
+  __syncthreads();
+  stage_b<false>(s, L, R, LS, tw + 64 * R, tid, nt);
+  __syncthreads();
+}
+
+// Inverse, R > 1: stage B in place on the lines (spectrum order), then stage A hands
+// element e (natural order, every e < N) of line l to st(l, e, v).  Starts after a barrier
+// that published the lines and the twiddles; returns without a barrier.
+template <int R, bool LFAST, class St>
+__device__ __forceinline__ void inv_a_global(float2* s, int L, int lgL, int LS, const float2* tw, int tid,
+                                             int nt, St st) {
+  stage_b<true>(s, L, R, LS, tw + 64 * R, tid, nt);
+  __syncthreads();
+  for (int task = tid; task < L * 64; task += nt) {
+    int l, n2;
+    task_of<LFAST>(task, L, lgL, l, n2);
+    const float2* sl = s + l * LS;
+    float2 v[R];
+#pragma unroll
+    for (int k1 = 0; k1 < R; ++k1) v[k1] = sl[pidx(64 * k1 + n2)];
+#pragma unroll
+    for (int k1 = 1; k1 < R; ++k1) v[k1] = cmulc(v[k1], tw[k1 * 64 + n2]);
+    dft_r<R, true>(v);
+#pragma unroll
+    for (int n1 = 0; n1 < R; ++n1) st(l, n2 + 64 * n1, v[n1]);
+  }
+}
+
+// Whether the global-stage variants apply: two-stage plans with a radix-R stage.
+__host__ __device__ inline bool a_global(int N) { return two_stage(N) && N > 64; }
+
+// Runtime R = N / 64 dispatch (N in {128, 256, 512, 1024}).
+template <bool LFAST, class Ld>
+__device__ __forceinline__ void fwd_a_global_plan(float2* s, int L, int lgL, int LS, int N, const float2* tw,
+                                                  int tid, int nt, Ld ld) {
+  switch (N >> 6) {
+    case 2: fwd_a_global<2, LFAST>(s, L, lgL, LS, tw, tid, nt, ld); break;
+    case 4: fwd_a_global<4, LFAST>(s, L, lgL, LS, tw, tid, nt, ld); break;
+    case 8: fwd_a_global<8, LFAST>(s, L, lgL, LS, tw, tid, nt, ld); break;
+    case 16: fwd_a_global<16, LFAST>(s, L, lgL, LS, tw, tid, nt, ld); break;
+    default: break;
+  }
+}
+
+template <bool LFAST, class St>
+__device__ __forceinline__ void inv_a_global_plan(float2* s, int L, int lgL, int LS, int N, const float2* tw,
+                                                  int tid, int nt, St st) {
+  switch (N >> 6) {
+    case 2: inv_a_global<2, LFAST>(s, L, lgL, LS, tw, tid, nt, st); break;
+    case 4: inv_a_global<4, LFAST>(s, L, lgL, LS, tw, tid, nt, st); break;
+    case 8: inv_a_global<8, LFAST>(s, L, lgL, LS, tw, tid, nt, st); break;
+    case 16: inv_a_global<16, LFAST>(s, L, lgL, LS, tw, tid, nt, st); break;
+    default: break;
+  }
+}
+
 }  // namespace fft
 }  // namespace nc

@@ -53,8 +53,19 @@ struct Planes {
 
 __device__ __forceinline__ int even_up(int x) { return (x + 1) & ~1; }
 
-// Forward row transforms of real planes -> dst (lines, N) complex.
-__global__ void __launch_bounds__(kFftThreads) rows_fwd_kernel(Planes a, float2* __restrict__ dst,
+// Variants of the transform kernels: RA = N / 64 (2, 4, 8) specialises the radix-R stage that
+// runs on global memory; RA = -1 chooses at run time between that stage (any R) and the
+// shared-memory plan (used for N = 1024: measured faster than the radix-16
+// specialisation); RA = 0 is the shared-memory plan alone (N <= 64 or N > 1024).  fft_ctas: CTAs per SM each variant is compiled for (registers per thread
+// <= 64K / (256 * that)): five (48 registers, no spills) for the specialisations, four for
+// the run-time variant and the column pass that sums over the directions (`heavy`); the
+// shared-memory plans leave the choice to the compiler.
+constexpr int fft_ctas(int RA, bool heavy = false) { return RA == 0 ? 1 : (RA < 0 || heavy) ? 4 : 5; }
+
+// Forward row transforms of real planes -> dst (lines, N) complex.  For N > 64 (RA = N/64)
+// the radix-R stage reads the planes directly (fft::fwd_a_global).
+template <int RA>
+__global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_fwd_kernel(Planes a, float2* __restrict__ dst,
                                                                 int N, const float2* __restrict__ tw,
                                                                 int L) {
   extern __shared__ float2 sm[];
@@ -67,22 +78,39 @@ __global__ void __launch_bounds__(kFftThreads) rows_fwd_kernel(Planes a, float2*
   const int nl = min(L, total - line0);
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
-#pragma unroll 4
-  for (int idx = tid; idx < nl * N; idx += nt) {
-    const int l = idx >> lgN, e = idx & (N - 1);
-    const int line = line0 + l;
-    const int u = line / a.rows, r = line - u * a.rows;
-    const int gs = u / a.ms, m = u - gs * a.ms;
-    float re = 0.f, im = 0.f;
-    if (e < a.cols) {
+  if (RA > 0 || (RA < 0 && fft::a_global(N))) {
+    __syncthreads();
+    auto ld = [&](int l, int e) -> float2 {
+      if (e >= a.cols) return make_float2(0.f, 0.f);
+      const int line = line0 + l;
+      const int u = line / a.rows, r = line - u * a.rows;
+      const int gs = u / a.ms, m = u - gs * a.ms;
       const int b1 = a.pack ? 2 * gs : gs;
       const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
-      re = a.ptr[(size_t)b1 * a.sstride + off] * a.scale;
-      if (a.pack && b1 + 1 < a.nsamp) im = a.ptr[(size_t)(b1 + 1) * a.sstride + off] * a.scale;
+      const float re = a.ptr[(size_t)b1 * a.sstride + off] * a.scale;
+      const float im = (a.pack && b1 + 1 < a.nsamp) ? a.ptr[(size_t)(b1 + 1) * a.sstride + off] * a.scale : 0.f;
+      return make_float2(re, im);
+    };
+    if constexpr (RA > 0) fft::fwd_a_global<RA, false>(s, nl, 0, LS, stw, tid, nt, ld);
+    else fft::fwd_a_global_plan<false>(s, nl, 0, LS, N, stw, tid, nt, ld);
+  } else {
+#pragma unroll 4
+    for (int idx = tid; idx < nl * N; idx += nt) {
+      const int l = idx >> lgN, e = idx & (N - 1);
+      const int line = line0 + l;
+      const int u = line / a.rows, r = line - u * a.rows;
+      const int gs = u / a.ms, m = u - gs * a.ms;
+      float re = 0.f, im = 0.f;
+      if (e < a.cols) {
+        const int b1 = a.pack ? 2 * gs : gs;
+        const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
+        re = a.ptr[(size_t)b1 * a.sstride + off] * a.scale;
+        if (a.pack && b1 + 1 < a.nsamp) im = a.ptr[(size_t)(b1 + 1) * a.sstride + off] * a.scale;
+      }
+      s[l * LS + pidx(e)] = make_float2(re, im);
     }
-    s[l * LS + pidx(e)] = make_float2(re, im);
+    fft::transform_lines_plan<false>(s, nl, N, stw, tid, nt);
   }
-  fft::transform_lines_plan<false>(s, nl, N, stw, tid, nt);
 #pragma unroll 4
   for (int idx = tid; idx < nl * N; idx += nt) {
     const int l = idx >> lgN, e = idx & (N - 1);
@@ -91,7 +119,9 @@ __global__ void __launch_bounds__(kFftThreads) rows_fwd_kernel(Planes a, float2*
 }
 
 // Inverse row transforms of src (lines, N) -> real planes (re -> sample 2g, im -> 2g+1).
-__global__ void __launch_bounds__(kFftThreads) rows_inv_kernel(const float2* __restrict__ src,
+// For N > 64 (RA = N/64) the radix-R stage writes the planes directly (fft::inv_a_global).
+template <int RA>
+__global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_inv_kernel(const float2* __restrict__ src,
                                                                 Planes a, int N,
                                                                 const float2* __restrict__ tw,
                                                                 int L) {
@@ -110,18 +140,37 @@ __global__ void __launch_bounds__(kFftThreads) rows_inv_kernel(const float2* __r
     const int l = idx >> lgN, e = idx & (N - 1);
     s[l * LS + pidx(e)] = __ldcs(&src[(size_t)(line0 + l) * N + e]);   // last use
   }
-  fft::transform_lines_plan<true>(s, nl, N, stw, tid, nt);
+  if (RA > 0 || (RA < 0 && fft::a_global(N))) {
+    __syncthreads();
+    const bool keep = a.rowstats != nullptr;   // the row statistics read the lines back
+    auto st = [&](int l, int e, float2 v) {
+      if (keep) s[l * LS + pidx(e)] = v;       // in place: the positions this thread read
+      if (e >= a.cols) return;
+      const int line = line0 + l;
+      const int u = line / a.rows, r = line - u * a.rows;
+      const int gs = u / a.ms, m = u - gs * a.ms;
+      const int b1 = a.pack ? 2 * gs : gs;
+      const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
+      a.ptr[(size_t)b1 * a.sstride + off] = v.x * a.scale;
+      if (a.pack && b1 + 1 < a.nsamp) a.ptr[(size_t)(b1 + 1) * a.sstride + off] = v.y * a.scale;
+    };
+    if constexpr (RA > 0) fft::inv_a_global<RA, false>(s, nl, 0, LS, stw, tid, nt, st);
+    else fft::inv_a_global_plan<false>(s, nl, 0, LS, N, stw, tid, nt, st);
+    if (keep) __syncthreads();
+  } else {
+    fft::transform_lines_plan<true>(s, nl, N, stw, tid, nt);
 #pragma unroll 4
-  for (int idx = tid; idx < nl * a.cols; idx += nt) {
-    const int l = idx / a.cols, e = idx - l * a.cols;
-    const int line = line0 + l;
-    const int u = line / a.rows, r = line - u * a.rows;
-    const int gs = u / a.ms, m = u - gs * a.ms;
-    const int b1 = a.pack ? 2 * gs : gs;
-    const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
-    const float2 v = s[l * LS + pidx(e)];
-    a.ptr[(size_t)b1 * a.sstride + off] = v.x * a.scale;
-    if (a.pack && b1 + 1 < a.nsamp) a.ptr[(size_t)(b1 + 1) * a.sstride + off] = v.y * a.scale;
+    for (int idx = tid; idx < nl * a.cols; idx += nt) {
+      const int l = idx / a.cols, e = idx - l * a.cols;
+      const int line = line0 + l;
+      const int u = line / a.rows, r = line - u * a.rows;
+      const int gs = u / a.ms, m = u - gs * a.ms;
+      const int b1 = a.pack ? 2 * gs : gs;
+      const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
+      const float2 v = s[l * LS + pidx(e)];
+      a.ptr[(size_t)b1 * a.sstride + off] = v.x * a.scale;
+      if (a.pack && b1 + 1 < a.nsamp) a.ptr[(size_t)(b1 + 1) * a.sstride + off] = v.y * a.scale;
+    }
   }
   if (a.rowstats) {
     // centred statistics of each stored row, two passes over the row in shared memory (one
@@ -169,43 +218,72 @@ struct ColArgs {
   float scale;          // FWD only
 };
 
-// Column transforms of C adjacent columns per CTA (blockIdx.y = unit).
-template <int MODE>
-__global__ void __launch_bounds__(kFftThreads) cols_kernel(ColArgs a, const float2* __restrict__ tw,
+// Line stride of the column tiles (see fft::line_stride_cols).
+__host__ __device__ inline int col_line_stride(int N) {
+  return fft::a_global(N) ? fft::line_stride_cols(N) : line_stride(N);
+}
+
+// Column transforms of C adjacent columns per CTA (blockIdx.y = unit).  For N > 64
+// (RA = N/64) the radix-R stage reads (forward) or writes (inverse) global memory directly.
+template <int MODE, int RA>
+__global__ void __launch_bounds__(kFftThreads, fft_ctas(RA, MODE == 2)) cols_kernel(ColArgs a, const float2* __restrict__ tw,
                                                             int C) {
   extern __shared__ float2 sm[];
   const int N = a.Nh;
   const int TN = fft::plan_twiddle_len(N);
   float2* stw = sm;
   float2* s = sm + even_up(TN);
-  const int LS = line_stride(N), lgC = fft::ilog2(C);
+  const int LS = col_line_stride(N), lgC = fft::ilog2(C);
   const int c0 = blockIdx.x * C;
   const int u = blockIdx.y;
   const int tid = threadIdx.x, nt = blockDim.x;
   const size_t NN = (size_t)a.Nh * a.Nw;
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
+  if (MODE == COL_FWD && (RA > 0 || (RA < 0 && fft::a_global(N)))) {
+    __syncthreads();
+    auto ld = [&](int l, int r) -> float2 {
+      if (r >= a.rows_in) return make_float2(0.f, 0.f);
+      float2 v = __ldcs(&a.src[((size_t)u * a.rows_in + r) * a.Nw + c0 + l]);   // last use
+      v.x *= a.scale;
+      v.y *= a.scale;
+      return v;
+    };
+    if constexpr (RA > 0) fft::fwd_a_global<RA, true>(s, C, lgC, LS, stw, tid, nt, ld);
+    else fft::fwd_a_global_plan<true>(s, C, lgC, LS, N, stw, tid, nt, ld);
+  } else {
 #pragma unroll 4
-  for (int idx = tid; idx < N * C; idx += nt) {
-    const int r = idx >> lgC, cc = idx & (C - 1);
-    const int c = c0 + cc;
-    float2 v = make_float2(0.f, 0.f);
-    if (MODE == COL_FWD || MODE == COL_INV_PLAIN) {
-      if (r < a.rows_in) {
-        v = __ldcs(&a.src[((size_t)u * a.rows_in + r) * a.Nw + c]);   // last use
-        if (MODE == COL_FWD) { v.x *= a.scale; v.y *= a.scale; }
+    for (int idx = tid; idx < N * C; idx += nt) {
+      const int r = idx >> lgC, cc = idx & (C - 1);
+      const int c = c0 + cc;
+      float2 v = make_float2(0.f, 0.f);
+      if (MODE == COL_FWD || MODE == COL_INV_PLAIN) {
+        if (r < a.rows_in) {
+          v = __ldcs(&a.src[((size_t)u * a.rows_in + r) * a.Nw + c]);   // last use
+          if (MODE == COL_FWD) { v.x *= a.scale; v.y *= a.scale; }
+        }
+      } else if (MODE == COL_INV_MULCONJ) {
+        const int p = u / a.M, m = u - p * a.M;
+        const size_t off = (size_t)r * a.Nw + c;
+        v = cmulc(a.src[(size_t)p * NN + off], a.spec[(size_t)m * NN + off]);
+      } else {
+        const size_t off = (size_t)r * a.Nw + c;
+        const float2* q = a.src + (size_t)u * a.M * NN + off;
+        for (int m = 0; m < a.M; ++m) v = cadd(v, cmul(q[(size_t)m * NN], a.spec[(size_t)m * NN + off]));
       }
-    } else if (MODE == COL_INV_MULCONJ) {
-      const int p = u / a.M, m = u - p * a.M;
-      const size_t off = (size_t)r * a.Nw + c;
-      v = cmulc(a.src[(size_t)p * NN + off], a.spec[(size_t)m * NN + off]);
-    } else {
-      const size_t off = (size_t)r * a.Nw + c;
-      const float2* q = a.src + (size_t)u * a.M * NN + off;
-      for (int m = 0; m < a.M; ++m) v = cadd(v, cmul(q[(size_t)m * NN], a.spec[(size_t)m * NN + off]));
+      s[cc * LS + pidx(r)] = v;
     }
-    s[cc * LS + pidx(r)] = v;
+    if (MODE != COL_FWD && (RA > 0 || (RA < 0 && fft::a_global(N)))) {
+      __syncthreads();
+      auto st = [&](int l, int r, float2 v) {
+        if (r < a.rows_out) __stcs(&a.dst[((size_t)u * a.rows_out + r) * a.Nw + c0 + l], v);   // read once
+      };
+      if constexpr (RA > 0) fft::inv_a_global<RA, true>(s, C, lgC, LS, stw, tid, nt, st);
+      else fft::inv_a_global_plan<true>(s, C, lgC, LS, N, stw, tid, nt, st);
+      return;
+    } else {
+      fft::transform_lines_plan<MODE != COL_FWD>(s, C, N, stw, tid, nt);
+    }
   }
-  fft::transform_lines_plan<MODE != COL_FWD>(s, C, N, stw, tid, nt);
   const int rows_st = (MODE == COL_FWD) ? N : a.rows_out;
 #pragma unroll 4
   for (int idx = tid; idx < rows_st * C; idx += nt) {
@@ -703,7 +781,7 @@ int cols_per_cta(int Nh, int Nw) {
 
 size_t cols_smem(int Nh, int C) {
   const int TN = fft::plan_twiddle_len(Nh);
-  return sizeof(float2) * ((size_t)((TN + 1) & ~1) + (size_t)C * line_stride(Nh));
+  return sizeof(float2) * ((size_t)((TN + 1) & ~1) + (size_t)C * col_line_stride(Nh));
 }
 
 nc_status smem_attr(const void* fn, size_t bytes) {
@@ -712,31 +790,70 @@ nc_status smem_attr(const void* fn, size_t bytes) {
   return NC_OK;
 }
 
-nc_status rows_fwd(const Planes& a, float2* dst, int N, const float2* tw, cudaStream_t st) {
+// RA of the transform kernels for N-point lines (see fft_ctas).
+int kernel_ra(int N) {
+  if (!fft::a_global(N)) return 0;
+  return N >= 1024 ? -1 : N >> 6;
+}
+
+template <int RA>
+nc_status rows_fwd_ra(const Planes& a, float2* dst, int N, const float2* tw, cudaStream_t st) {
   const int L = rows_per_cta(N);
   const size_t smem = rows_smem(N, L);
-  NC_CHECK(smem_attr((const void*)rows_fwd_kernel, smem));
+  NC_CHECK(smem_attr((const void*)rows_fwd_kernel<RA>, smem));
   const int lines = a.units * a.rows;
-  rows_fwd_kernel<<<(lines + L - 1) / L, kFftThreads, smem, st>>>(a, dst, N, tw, L);
+  rows_fwd_kernel<RA><<<(lines + L - 1) / L, kFftThreads, smem, st>>>(a, dst, N, tw, L);
   return launched("rows_fwd_kernel launch");
 }
 
-nc_status rows_inv(const float2* src, const Planes& a, int N, const float2* tw, cudaStream_t st) {
+template <int RA>
+nc_status rows_inv_ra(const float2* src, const Planes& a, int N, const float2* tw, cudaStream_t st) {
   const int L = rows_per_cta(N);
   const size_t smem = rows_smem(N, L);
-  NC_CHECK(smem_attr((const void*)rows_inv_kernel, smem));
+  NC_CHECK(smem_attr((const void*)rows_inv_kernel<RA>, smem));
   const int lines = a.units * a.rows;
-  rows_inv_kernel<<<(lines + L - 1) / L, kFftThreads, smem, st>>>(src, a, N, tw, L);
+  rows_inv_kernel<RA><<<(lines + L - 1) / L, kFftThreads, smem, st>>>(src, a, N, tw, L);
   return launched("rows_inv_kernel launch");
+}
+
+nc_status rows_fwd(const Planes& a, float2* dst, int N, const float2* tw, cudaStream_t st) {
+  switch (kernel_ra(N)) {
+    case 2: return rows_fwd_ra<2>(a, dst, N, tw, st);
+    case 4: return rows_fwd_ra<4>(a, dst, N, tw, st);
+    case 8: return rows_fwd_ra<8>(a, dst, N, tw, st);
+    case -1: return rows_fwd_ra<-1>(a, dst, N, tw, st);
+    default: return rows_fwd_ra<0>(a, dst, N, tw, st);
+  }
+}
+
+nc_status rows_inv(const float2* src, const Planes& a, int N, const float2* tw, cudaStream_t st) {
+  switch (kernel_ra(N)) {
+    case 2: return rows_inv_ra<2>(src, a, N, tw, st);
+    case 4: return rows_inv_ra<4>(src, a, N, tw, st);
+    case 8: return rows_inv_ra<8>(src, a, N, tw, st);
+    case -1: return rows_inv_ra<-1>(src, a, N, tw, st);
+    default: return rows_inv_ra<0>(src, a, N, tw, st);
+  }
+}
+
+template <int MODE, int RA>
+nc_status cols_ra(const ColArgs& a, int units, const float2* tw, cudaStream_t st) {
+  const int C = cols_per_cta(a.Nh, a.Nw);
+  const size_t smem = cols_smem(a.Nh, C);
+  NC_CHECK(smem_attr((const void*)cols_kernel<MODE, RA>, smem));
+  cols_kernel<MODE, RA><<<dim3(a.Nw / C, units), kFftThreads, smem, st>>>(a, tw, C);
+  return launched("cols_kernel launch");
 }
 
 template <int MODE>
 nc_status cols(const ColArgs& a, int units, const float2* tw, cudaStream_t st) {
-  const int C = cols_per_cta(a.Nh, a.Nw);
-  const size_t smem = cols_smem(a.Nh, C);
-  NC_CHECK(smem_attr((const void*)cols_kernel<MODE>, smem));
-  cols_kernel<MODE><<<dim3(a.Nw / C, units), kFftThreads, smem, st>>>(a, tw, C);
-  return launched("cols_kernel launch");
+  switch (kernel_ra(a.Nh)) {
+    case 2: return cols_ra<MODE, 2>(a, units, tw, st);
+    case 4: return cols_ra<MODE, 4>(a, units, tw, st);
+    case 8: return cols_ra<MODE, 8>(a, units, tw, st);
+    case -1: return cols_ra<MODE, -1>(a, units, tw, st);
+    default: return cols_ra<MODE, 0>(a, units, tw, st);
+  }
 }
 
 inline unsigned blocks_for(size_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
