@@ -294,17 +294,45 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA, MODE == 2)) cols_ker
   }
 }
 
-// acc[m][f] (+)= sum over pairs of x^[p][f] * conj(q^[p][m][f])  (fixed pair order).
+// acc[m][f] (+)= sum over pairs of x^[p][f] * conj(q^[p][m][f])  (fixed pair order).  A
+// thread takes two adjacent frequencies (16-byte accesses) of kDgM directions
+// (blockIdx.y), so x^ is read once per kDgM directions and the kDgM q^ loads of a pair are
+// independent.  NN is even (power-of-two grids) and the spectra are 16-byte aligned.
+// dg_accum picks kDgM per grid size so that small grids still fill the GPU.
+template <int kDgM>
 __global__ void dg_accum_kernel(const float2* __restrict__ xhat, const float2* __restrict__ q,
                                 float2* __restrict__ acc, int pairs, int M, size_t NN, int init) {
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (size_t)M * NN) return;
-  const int m = (int)(i / NN);
-  const size_t f = i - (size_t)m * NN;
-  float2 s = init ? make_float2(0.f, 0.f) : acc[i];
-#pragma unroll 8
-  for (int p = 0; p < pairs; ++p) s = cadd(s, cmulc(__ldg(&xhat[(size_t)p * NN + f]), q[((size_t)p * M + m) * NN + f]));
-  acc[i] = s;
+  const size_t h = (size_t)blockIdx.x * blockDim.x + threadIdx.x;   // frequencies 2h, 2h+1
+  const size_t NN2 = NN / 2;
+  if (h >= NN2) return;
+  const int m0 = blockIdx.y * kDgM;
+  const int mc = min(kDgM, M - m0);
+  const float4* x4 = reinterpret_cast<const float4*>(xhat);
+  const float4* q4 = reinterpret_cast<const float4*>(q);
+  float4* a4 = reinterpret_cast<float4*>(acc);
+  float4 s[kDgM];
+#pragma unroll
+  for (int j = 0; j < kDgM; ++j)
+    s[j] = (j < mc && !init) ? a4[(size_t)(m0 + j) * NN2 + h] : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int p = 0; p < pairs; ++p) {
+    const float4 x = __ldg(&x4[(size_t)p * NN2 + h]);
+    const float4* qp = q4 + ((size_t)p * M + m0) * NN2 + h;
+#pragma unroll
+    for (int j = 0; j < kDgM; ++j) {
+      if (j < mc) {
+        const float4 v = qp[(size_t)j * NN2];
+        const float2 lo = cmulc(make_float2(x.x, x.y), make_float2(v.x, v.y));
+        const float2 hi = cmulc(make_float2(x.z, x.w), make_float2(v.z, v.w));
+        s[j].x += lo.x;
+        s[j].y += lo.y;
+        s[j].z += hi.x;
+        s[j].w += hi.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kDgM; ++j)
+    if (j < mc) a4[(size_t)(m0 + j) * NN2 + h] = s[j];
 }
 
 __device__ float block_sum(float v, float* red) {
@@ -637,10 +665,27 @@ __device__ __forceinline__ float field_grad(const Geo& g, const float* dxb, int 
 // ROI-epilogue adjoint (kernels_pallas.py:221-291) for the samples of chunk blockIdx.y:
 // the cell gradient comes from the field adjoint dx (hidden step t-1) or, in universe mode,
 // from gy_roi (B, P) with the final activation; per-chunk pixel-gradient partials go to gpart.
+// Warp sums of four values in six shuffles: the first two butterfly levels split the values
+// over the half- and quarter-warps, the last three finish one value per 8-lane group.
+// Afterwards lanes 0, 8, 16 and 24 hold the sums of a, b, c and d.
+__device__ __forceinline__ float warp_sum4(float a, float b, float c, float d, int lane) {
+  const bool h16 = (lane & 16) != 0, h8 = (lane & 8) != 0;
+  float x0 = h16 ? c : a, x1 = h16 ? d : b;
+  const float y0 = h16 ? a : c, y1 = h16 ? b : d;
+  x0 += __shfl_xor_sync(0xffffffffu, y0, 16);
+  x1 += __shfl_xor_sync(0xffffffffu, y1, 16);
+  float z = h8 ? x1 : x0;
+  z += __shfl_xor_sync(0xffffffffu, h8 ? x0 : x1, 8);
+  z += __shfl_xor_sync(0xffffffffu, z, 4);
+  z += __shfl_xor_sync(0xffffffffu, z, 2);
+  z += __shfl_xor_sync(0xffffffffu, z, 1);
+  return z;
+}
+
 // gzpart (not null): the CTA's sums of gz and gz * zhat over its pixels per (b, m) of its
-// chunk, at gzpart[((blockIdx.x * B + b) * M + m) * 2 + {0, 1}] (warp shuffles, then the
-// warps in order), so the standardisation adjoint needs one pass.  `red` in dynamic shared
-// memory holds bc * M * 2 values per warp.
+// chunk, at gzpart[((blockIdx.x * B + b) * M + m) * 2 + {0, 1}] (warp_sum4 over directions
+// m, m+1, then the warps in order), so the standardisation adjoint needs one pass.  `red`
+// in dynamic shared memory holds bc * M * 2 values per warp.
 template <int V>
 __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__ dx,
                                  const float* __restrict__ zh_t, size_t zs, float* __restrict__ gz,
@@ -670,35 +715,36 @@ __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__
     }
     const float* ZH = zh_t + (size_t)b * zs + p0;
     float* GZ = gz + (size_t)b * g.M * P + p0;
-    for (int m = 0; m < g.M; ++m) {
-      float zv[V], gv[V];
-      if (on) {
-        ldv<V>(ZH + (size_t)m * P, zv);
-      } else {
+    for (int m = 0; m < g.M; m += 2) {          // directions m, m+1 (m+1 < M or empty)
+      float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int v = 0; v < V; ++v) zv[v] = 0.f;
-      }
-      float s1 = 0.f, s2 = 0.f;
+      for (int k = 0; k < 2; ++k) {
+        if (m + k >= g.M) break;
+        float zv[V], gv[V];
+        if (on) {
+          ldv<V>(ZH + (size_t)(m + k) * P, zv);
+        } else {
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        float dd;
-        const float av = act_fwd_deriv(act_id, zv[v] + bb[v], slope, &dd);
-        lin[v] += zv[v];
-        act[v] += av;
-        dsum[v] += dd;
-        gv[v] = on ? we[v] * gy[v] + se[v] * gy[v] * dd : 0.f;
-        s1 += gv[v];
-        s2 = fmaf(gv[v], zv[v], s2);
-      }
-      if (on) stv<V>(GZ + (size_t)m * P, gv);
-      if (gzpart) {
-        s1 = warp_sum(s1);
-        s2 = warp_sum(s2);
-        if (lane == 0) {
-          float* rw = red + ((size_t)((b - b0) * g.M + m) * nw + warp) * 2;
-          rw[0] = s1;
-          rw[1] = s2;
+          for (int v = 0; v < V; ++v) zv[v] = 0.f;
         }
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          float dd;
+          const float av = act_fwd_deriv(act_id, zv[v] + bb[v], slope, &dd);
+          lin[v] += zv[v];
+          act[v] += av;
+          dsum[v] += dd;
+          gv[v] = on ? we[v] * gy[v] + se[v] * gy[v] * dd : 0.f;
+          s[2 * k] += gv[v];
+          s[2 * k + 1] = fmaf(gv[v], zv[v], s[2 * k + 1]);
+        }
+        if (on) stv<V>(GZ + (size_t)(m + k) * P, gv);
+      }
+      if (gzpart) {
+        const float r = warp_sum4(s[0], s[1], s[2], s[3], lane);
+        const int e = lane >> 3;                  // 0: s1(m), 1: s2(m), 2: s1(m+1), 3: s2(m+1)
+        if ((lane & 7) == 0 && m + (e >> 1) < g.M)
+          red[((size_t)((b - b0) * g.M + m + (e >> 1)) * nw + warp) * 2 + (e & 1)] = r;
       }
     }
 #pragma unroll
@@ -858,16 +904,23 @@ nc_status cols(const ColArgs& a, int units, const float2* tw, cudaStream_t st) {
 
 inline unsigned blocks_for(size_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
 
-// Grid of the per-plane statistics kernels: two CTAs per SM looping over the planes.
-unsigned stat_grid(int nplanes) {
+// SMs of the current device (148 on B200 if the query fails).
+int sm_count() {
   static int sms = 0;
   if (sms == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+      sms = n;
+    else
       sms = 148;
   }
-  const int n = 2 * sms;
+  return sms;
+}
+
+// Grid of the per-plane statistics kernels: two CTAs per SM looping over the planes.
+unsigned stat_grid(int nplanes) {
+  const int n = 2 * sm_count();
   return (unsigned)(nplanes < n ? nplanes : n);
 }
 
@@ -911,6 +964,24 @@ nc_status hidden_gz(const Geo& g, const FftCall& c, const float* zh, size_t zs, 
   }
   *ncta = part ? (int)grid : 0;
   return launched("hidden_gz_kernel launch");
+}
+
+// Filter-gradient spectrum accumulation (dg_accum_kernel): the largest direction block
+// (8, 4, 2, 1) that still launches two CTAs per SM.
+nc_status dg_accum(const FftCall& c, int pairs, size_t NN, int init, cudaStream_t st) {
+  const int M = c.g.M;
+  const unsigned bx = blocks_for(NN / 2, 256);
+  const unsigned want = 2 * (unsigned)sm_count();
+  int mb = 8;
+  while (mb > 1 && bx * (unsigned)((M + mb - 1) / mb) < want) mb >>= 1;
+  const dim3 grid(bx, (M + mb - 1) / mb);
+  switch (mb) {
+    case 8: dg_accum_kernel<8><<<grid, 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, M, NN, init); break;
+    case 4: dg_accum_kernel<4><<<grid, 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, M, NN, init); break;
+    case 2: dg_accum_kernel<2><<<grid, 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, M, NN, init); break;
+    default: dg_accum_kernel<1><<<grid, 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, M, NN, init); break;
+  }
+  return launched("dg_accum_kernel launch");
 }
 
 // x^ (pairs) of the field currently in c.field.
@@ -1067,9 +1138,7 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
       ColArgs ca{c.tmp, nullptr, c.q, g.Nh, g.Nw, g.roi_h, g.Nh, g.M, 1.0f};
       NC_CHECK(cols<COL_FWD>(ca, pairs * g.M, c.tw_h, st));
     }
-    dg_accum_kernel<<<blocks_for(M * NN, 256), 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, g.M, NN,
-                                                             t == g.d - 1 ? 1 : 0);
-    NC_CHECK(launched("dg_accum_kernel launch"));
+    NC_CHECK(dg_accum(c, pairs, NN, t == g.d - 1 ? 1 : 0, st));
     if (t == 0) break;
 
     // field adjoint dX = IFFT(sum_m q^_m . G^_m) on the field rows, then columns
