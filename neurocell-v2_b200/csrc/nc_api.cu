@@ -235,6 +235,7 @@ static FftCall fft_call(const Prepared& pr, void* ws, const float* inputs, int b
   c.rstd = at<float>(ws, L.f_rstd);
   c.rowstats = at<float2>(ws, L.f_rowstats);
   c.gzpart = at<float>(ws, L.f_gzpart);
+  c.ncoef = at<float4>(ws, L.f_ncoef);
   c.zscr = at<float>(ws, L.zscr);
   c.zhat = at<float>(ws, L.zhat);
   c.rstd_save = at<float>(ws, L.rstd);

@@ -49,7 +49,21 @@ struct Planes {
   int units;    // lines / rows = (nsamp or pairs) * ms
   float scale;
   float2* rowstats;   // rows_inv: per stored row (mean, M2) of its `cols` values, or null
+  // rows_fwd: with coef set, the pass reads the standardisation adjoint of the planes,
+  // coef.x * (v - coef.y - zh * coef.z) per (sample, m) plane, from the planes v and the
+  // standardised planes zh (same layout, sample stride zstride)
+  const float* zh;
+  size_t zstride;
+  const float4* coef;
 };
+
+// Element `off` of plane (b, m) as the row pass reads it (see Planes::coef).
+__device__ __forceinline__ float plane_in(const Planes& a, int b, int m, size_t off) {
+  const float v = a.ptr[(size_t)b * a.sstride + off];
+  if (!a.coef) return v * a.scale;
+  const float4 k = a.coef[(size_t)b * a.ms + m];
+  return k.x * (v - k.y - a.zh[(size_t)b * a.zstride + off] * k.z) * a.scale;
+}
 
 __device__ __forceinline__ int even_up(int x) { return (x + 1) & ~1; }
 
@@ -87,8 +101,8 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_fwd_kernel(Pla
       const int gs = u / a.ms, m = u - gs * a.ms;
       const int b1 = a.pack ? 2 * gs : gs;
       const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
-      const float re = a.ptr[(size_t)b1 * a.sstride + off] * a.scale;
-      const float im = (a.pack && b1 + 1 < a.nsamp) ? a.ptr[(size_t)(b1 + 1) * a.sstride + off] * a.scale : 0.f;
+      const float re = plane_in(a, b1, m, off);
+      const float im = (a.pack && b1 + 1 < a.nsamp) ? plane_in(a, b1 + 1, m, off) : 0.f;
       return make_float2(re, im);
     };
     if constexpr (RA > 0) fft::fwd_a_global<RA, false>(s, nl, 0, LS, stw, tid, nt, ld);
@@ -104,8 +118,8 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_fwd_kernel(Pla
       if (e < a.cols) {
         const int b1 = a.pack ? 2 * gs : gs;
         const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
-        re = a.ptr[(size_t)b1 * a.sstride + off] * a.scale;
-        if (a.pack && b1 + 1 < a.nsamp) im = a.ptr[(size_t)(b1 + 1) * a.sstride + off] * a.scale;
+        re = plane_in(a, b1, m, off);
+        if (a.pack && b1 + 1 < a.nsamp) im = plane_in(a, b1 + 1, m, off);
       }
       s[l * LS + pidx(e)] = make_float2(re, im);
     }
@@ -653,6 +667,29 @@ __global__ void __launch_bounds__(kStatThreads) norm_bwd_kernel(Geo g, float* __
   }
 }
 
+// Coefficients of the standardisation adjoint gz <- rstd (gz - mean(gz) - zhat mean(gz zhat))
+// from hidden_gz_kernel's per-CTA sums (ncta of them, one warp per plane, lanes over the
+// CTAs in a fixed order); the next row pass applies them while it reads the planes.
+__global__ void norm_coef_kernel(Geo g, const float* __restrict__ gzpart, int ncta,
+                                 const float* __restrict__ rstd_save, int t, int nplanes,
+                                 float4* __restrict__ coef) {
+  const int bm = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (bm >= nplanes) return;                 // whole warps leave together
+  float s1 = 0.f, s2 = 0.f;
+  for (int k = lane; k < ncta; k += 32) {
+    s1 += gzpart[((size_t)k * nplanes + bm) * 2 + 0];
+    s2 += gzpart[((size_t)k * nplanes + bm) * 2 + 1];
+  }
+  s1 = warp_sum(s1);
+  s2 = warp_sum(s2);
+  if (lane == 0) {
+    const float inv_n = 1.0f / (float)g.P;
+    const int b = bm / g.M, m = bm - b * g.M;
+    coef[bm] = make_float4(rstd_save[((size_t)b * g.d + t) * g.M + m], s1 * inv_n, s2 * inv_n, 0.f);
+  }
+}
+
 // Field adjoint at interior cell (r, c); CIRCULAR folds the wrapped halo copies back.
 __device__ __forceinline__ float field_grad(const Geo& g, const float* dxb, int r, int c) {
   if (g.padding != NC_PAD_CIRCULAR) return dxb[(size_t)(r + g.oh) * g.Fw + c + g.ow];
@@ -1085,6 +1122,26 @@ nc_status fft_forward(const FftCall& c, cudaStream_t st) {
 // ---------------------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------------------
+// Standardisation adjoint of step t's plane gradients in c.gz: deferred to the next row pass
+// (*pending = true, coefficients in c.ncoef) when hidden_gz_kernel wrote the per-CTA sums
+// (ncta > 0), else applied in place by norm_bwd_kernel (two passes over the planes).
+nc_status norm_adjoint(const FftCall& c, const float* zh, size_t zs, int t, int ncta, bool* pending,
+                       cudaStream_t st) {
+  const Geo& g = c.g;
+  const int nplanes = c.batch * g.M;
+  if (ncta > 0 && c.ncoef) {
+    norm_coef_kernel<<<blocks_for((size_t)nplanes * 32, 256), 256, 0, st>>>(g, c.gzpart, ncta, c.rstd_save, t,
+                                                                           nplanes, c.ncoef);
+    *pending = true;
+    return launched("norm_coef_kernel launch");
+  }
+  norm_bwd_kernel<<<stat_grid(nplanes), kStatThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, t, nplanes,
+                                                               plane_vec(g, zs), ncta ? c.gzpart : nullptr,
+                                                               ncta);
+  *pending = false;
+  return launched("norm_bwd_kernel launch");
+}
+
 nc_status fft_backward(const FftCall& c, cudaStream_t st) {
   const Geo& g = c.g;
   const int B = c.batch, pairs = (B + 1) / 2;
@@ -1097,6 +1154,12 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
   NC_CUDA_CHECK(cudaMemsetAsync(c.gsum, 0, sizeof(float) * 3 * P, st));
   if (c.gborder) NC_CUDA_CHECK(cudaMemsetAsync(c.gborder, 0, sizeof(float) * g.H * g.W, st));
   NC_CUDA_CHECK(cudaMemsetAsync(c.gz, 0, sizeof(float) * B * M * P, st));
+
+  // The standardisation adjoint of the planes in c.gz is either applied in place
+  // (norm_bwd_kernel) or left `pending`: its coefficients are in c.ncoef and the row pass
+  // that reads c.gz next applies it (the corrected planes have no other reader).
+  bool pending = false;
+  int pending_t = 0;
 
   // output step: sparse port adjoint (or the universe ROI adjoint), then the
   // standardisation adjoint
@@ -1112,12 +1175,8 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
                                                                 c.gsum, B);
       NC_CHECK(launched("port_gz_kernel launch"));
     }
-    if (g.norm) {
-      norm_bwd_kernel<<<stat_grid(B * g.M), kStatThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, g.d - 1,
-                                                                   B * g.M, plane_vec(g, zs),
-                                                                   ncta_out ? c.gzpart : nullptr, ncta_out);
-      NC_CHECK(launched("norm_bwd_kernel launch"));
-    }
+    if (g.norm) NC_CHECK(norm_adjoint(c, zh, zs, g.d - 1, ncta_out, &pending, st));
+    pending_t = g.d - 1;
   }
 
   for (int t = g.d - 1; t >= 0; --t) {
@@ -1134,6 +1193,11 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
     // plane-gradient spectra q^ (pairs, M)
     {
       Planes gp{c.gz, M * P, B, g.M, g.roi_h, g.roi_w, g.P, g.roi_w, 1, pairs * g.M, 1.0f};
+      if (pending) {
+        gp.zh = c.zhat + (size_t)pending_t * M * P;
+        gp.zstride = zs;
+        gp.coef = c.ncoef;
+      }
       NC_CHECK(rows_fwd(gp, c.tmp, g.Nw, c.tw_w, st));
       ColArgs ca{c.tmp, nullptr, c.q, g.Nh, g.Nw, g.roi_h, g.Nh, g.M, 1.0f};
       NC_CHECK(cols<COL_FWD>(ca, pairs * g.M, c.tw_h, st));
@@ -1158,12 +1222,9 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
     NC_CHECK(hidden_gz(g, c, zh, zs, nch, bc, g.act, g.slope, nullptr, &ncta, st));
     gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
     NC_CHECK(launched("gsum_chunks_kernel launch"));
-    if (g.norm) {
-      norm_bwd_kernel<<<stat_grid(B * g.M), kStatThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, t - 1,
-                                                                   B * g.M, plane_vec(g, zs),
-                                                                   ncta ? c.gzpart : nullptr, ncta);
-      NC_CHECK(launched("norm_bwd_kernel launch"));
-    }
+    pending = false;
+    pending_t = t - 1;
+    if (g.norm) NC_CHECK(norm_adjoint(c, zh, zs, t - 1, ncta, &pending, st));
   }
 
   // filter gradient: Re IFFT(acc_m) / (Nh Nw) at lags [0, kh) x [0, kw)

@@ -27,6 +27,7 @@ struct FftCall {
   float* rstd;                // (B, M)
   float2* rowstats;           // (B, M, roi_h) per-row (mean, M2) of the forward planes
   float* gzpart;              // train: (ceil(P/256), B, M, 2) per-CTA sums of gz, gz*zhat
+  float4* ncoef;              // train: (B, M) standardisation-adjoint coefficients
   float* zscr;                // (B, M, P) inference planes
   float* zhat;                // train: (B, d, M, P)
   float* rstd_save;           // train: (B, d, M)

@@ -66,6 +66,8 @@ struct WsLayout {
   size_t f_mean, f_rstd;  // (B, M) plane statistics of the current step
   size_t f_rowstats;      // (B, M, roi_h) per-row (mean, M2) of the current step's planes
   size_t f_gzpart;        // train: (ceil(P/256), B, M, 2) per-CTA sums of gz and gz*zhat
+  size_t f_ncoef;         // train: (B, M) float4 (rstd, mean gz, mean gz*zhat, 0) of the
+                          // standardisation adjoint applied by the next row pass
   size_t f_q;             // (B/2, M, Nh, Nw) plane-gradient spectra (train)
   size_t f_dgacc;         // (M, Nh, Nw) filter-gradient spectrum accumulator (train)
   size_t f_gz;            // (B, M, P) plane gradients (train)

@@ -569,3 +569,18 @@ def test_fft_two_stage_line_transforms_parity(grid, kernel, mode):
     cell, filt, ins, y = random_problem(geom, 2, 181)
     check_case(geom, O.Config(codd_mode="ste_ternary", state_temperature=0.5), cell, filt, ins, y,
                backend="pallas_sram")
+
+
+# ---- direction blocks of the filter-gradient accumulation, odd direction counts ---------
+@pytest.mark.parametrize("grid,kernel,M", [
+    ((300, 150), (9, 9), 16),    # FFT 512 x 256: the accumulation holds 8 directions per thread
+    ((160, 160), (31, 31), 5),   # FFT 256 x 256, M odd: blocks of 2 with a partial last block,
+                                 # and the paired-direction reductions end on a single direction
+])
+def test_fft_direction_blocks_parity(grid, kernel, M):
+    H, W = grid
+    r0 = H // 2 - 2
+    geom = O.make_geometry(grid, kernel, M, 2, (O.CoordPort(tuple((r, W // 3) for r in range(r0, r0 + 4))),),
+                           O.CoordPort(tuple((r, 2 * W // 3) for r in range(r0, r0 + 3))))
+    cell, filt, ins, y = random_problem(geom, 3, 191 + M)
+    check_case(geom, O.Config(), cell, filt, ins, y, backend="pallas_sram")
