@@ -468,7 +468,7 @@ def run_config(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
         pg = dist.group.WORLD
-    B_total = {1: 8192, 2: 64, 3: 256, 4: 16}[cfg]
+    B_total = args.batch or {1: 8192, 2: 64, 3: 256, 4: 16}[cfg]
     strong = cfg == 4
     if strong and B_total % world != 0:
         raise SystemExit(f"config 4 shards its batch of {B_total}; --gpus must divide it")
@@ -567,7 +567,9 @@ def run_config(args) -> None:
         "unit": "samples/s", "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong" if strong else "weak",
         "dtype": "f32", "data": "synthetic (seeded numpy, config shapes)",
-        "config": {"workload": f"BASELINE config {cfg}", "batch_per_gpu": B,
+        "config": {"workload": f"BASELINE config {cfg}" + (f" shapes at batch {B_total} (not the config's batch)"
+                                                            if args.batch else ""),
+                   "batch_per_gpu": B,
                    "global_batch": B * world, "conv": conv, "codd_mode": meta["codd_mode"],
                    "state_temperature": ("1.0 -> 0.1 over the timed steps (exponential)"
                                          if meta["codd_mode"] == "annealed" else 1.0),
@@ -606,6 +608,9 @@ def main():
                          "(secondary measurement)")
     ap.add_argument("--conv", choices=("auto", "direct", "fft"), default="auto",
                     help="Green's convolution algorithm (nc_conv_algo)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="--config 1-4: batch in place of the config's own (reduced cases for "
+                         "profiling; the line then names a batch the BASELINE config does not)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
