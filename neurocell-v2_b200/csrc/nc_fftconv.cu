@@ -400,16 +400,6 @@ __global__ void field_ring_kernel(Geo g, float* __restrict__ field, const float*
   }
 }
 
-// Interior of the field entering step t >= 1 from the saved residual.
-__global__ void field_interior_kernel(Geo g, float* __restrict__ field, const float* __restrict__ xs,
-                                      size_t xs_stride, int B) {
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (size_t)B * g.P) return;
-  const int b = (int)(i / g.P), p = (int)(i - (size_t)b * g.P);
-  const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
-  field[(size_t)b * g.Fh * g.Fw + (size_t)(r + g.oh) * g.Fw + c + g.ow] = xs[(size_t)b * xs_stride + p];
-}
-
 // ---------------------------------------------------------------------------------------
 // forward epilogues (planes z at z + b*zs + m*P)
 // ---------------------------------------------------------------------------------------
@@ -1003,9 +993,9 @@ nc_status hidden_gz(const Geo& g, const FftCall& c, const float* zh, size_t zs, 
   return launched("hidden_gz_kernel launch");
 }
 
-// Filter-gradient spectrum accumulation (dg_accum_kernel): the largest direction block
-// (8, 4, 2, 1) that still launches two CTAs per SM.
-nc_status dg_accum(const FftCall& c, int pairs, size_t NN, int init, cudaStream_t st) {
+// Filter-gradient spectrum accumulation (dg_accum_kernel) against the field spectra xh: the
+// largest direction block (8, 4, 2, 1) that still launches two CTAs per SM.
+nc_status dg_accum(const FftCall& c, const float2* xh, int pairs, size_t NN, int init, cudaStream_t st) {
   const int M = c.g.M;
   const unsigned bx = blocks_for(NN / 2, 256);
   const unsigned want = 2 * (unsigned)sm_count();
@@ -1013,21 +1003,21 @@ nc_status dg_accum(const FftCall& c, int pairs, size_t NN, int init, cudaStream_
   while (mb > 1 && bx * (unsigned)((M + mb - 1) / mb) < want) mb >>= 1;
   const dim3 grid(bx, (M + mb - 1) / mb);
   switch (mb) {
-    case 8: dg_accum_kernel<8><<<grid, 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, M, NN, init); break;
-    case 4: dg_accum_kernel<4><<<grid, 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, M, NN, init); break;
-    case 2: dg_accum_kernel<2><<<grid, 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, M, NN, init); break;
-    default: dg_accum_kernel<1><<<grid, 256, 0, st>>>(c.xhat, c.q, c.dgacc, pairs, M, NN, init); break;
+    case 8: dg_accum_kernel<8><<<grid, 256, 0, st>>>(xh, c.q, c.dgacc, pairs, M, NN, init); break;
+    case 4: dg_accum_kernel<4><<<grid, 256, 0, st>>>(xh, c.q, c.dgacc, pairs, M, NN, init); break;
+    case 2: dg_accum_kernel<2><<<grid, 256, 0, st>>>(xh, c.q, c.dgacc, pairs, M, NN, init); break;
+    default: dg_accum_kernel<1><<<grid, 256, 0, st>>>(xh, c.q, c.dgacc, pairs, M, NN, init); break;
   }
   return launched("dg_accum_kernel launch");
 }
 
-// x^ (pairs) of the field currently in c.field.
-nc_status field_spectra(const FftCall& c, cudaStream_t st) {
+// x^ (pairs) of the field currently in c.field, into xh.
+nc_status field_spectra(const FftCall& c, float2* xh, cudaStream_t st) {
   const Geo& g = c.g;
   const int pairs = (c.batch + 1) / 2;
   Planes f{c.field, (size_t)g.Fh * g.Fw, c.batch, 1, g.Fh, g.Fw, 0, g.Fw, 1, pairs, 1.0f};
   NC_CHECK(rows_fwd(f, c.tmp, g.Nw, c.tw_w, st));
-  ColArgs ca{c.tmp, nullptr, c.xhat, g.Nh, g.Nw, g.Fh, g.Nh, g.M, 1.0f};
+  ColArgs ca{c.tmp, nullptr, xh, g.Nh, g.Nw, g.Fh, g.Nh, g.M, 1.0f};
   return cols<COL_FWD>(ca, pairs, c.tw_h, st);
 }
 
@@ -1084,10 +1074,12 @@ nc_status fft_forward(const FftCall& c, cudaStream_t st) {
     } else {
       NC_CHECK(field_ring(c, st));
     }
-    NC_CHECK(field_spectra(c, st));
+    // the field spectra; training keeps one slot per step for the backward
+    float2* xh = c.xhat + (c.train ? (size_t)t * pairs * ((size_t)g.Nh * g.Nw) : 0);
+    NC_CHECK(field_spectra(c, xh, st));
     // z = IFFT(x^ . conj(G^_m)) on the ROI rows, then columns
     {
-      ColArgs ca{c.xhat, c.gspec, c.tmp, g.Nh, g.Nw, 0, g.roi_h, g.M, 1.0f};
+      ColArgs ca{xh, c.gspec, c.tmp, g.Nh, g.Nw, 0, g.roi_h, g.M, 1.0f};
       NC_CHECK(cols<COL_INV_MULCONJ>(ca, pairs * g.M, c.tw_h, st));
     }
     float* z = c.train ? c.zhat + (size_t)t * M * P : c.zscr;
@@ -1180,16 +1172,8 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
   }
 
   for (int t = g.d - 1; t >= 0; --t) {
-    // the field that entered step t, and its spectra
-    if (t == 0) {
-      NC_CHECK(build_field0(c, st));
-    } else {
-      field_interior_kernel<<<blocks_for((size_t)B * P, 256), 256, 0, st>>>(
-          g, c.field, c.xsave + (size_t)(t - 1) * P, (size_t)(g.d - 1) * P, B);
-      NC_CHECK(launched("field_interior_kernel launch"));
-      NC_CHECK(field_ring(c, st));
-    }
-    NC_CHECK(field_spectra(c, st));
+    // spectra of the field that entered step t, kept by the training forward
+    const float2* xh = c.xhat + (size_t)t * pairs * NN;
     // plane-gradient spectra q^ (pairs, M)
     {
       Planes gp{c.gz, M * P, B, g.M, g.roi_h, g.roi_w, g.P, g.roi_w, 1, pairs * g.M, 1.0f};
@@ -1202,7 +1186,7 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
       ColArgs ca{c.tmp, nullptr, c.q, g.Nh, g.Nw, g.roi_h, g.Nh, g.M, 1.0f};
       NC_CHECK(cols<COL_FWD>(ca, pairs * g.M, c.tw_h, st));
     }
-    NC_CHECK(dg_accum(c, pairs, NN, t == g.d - 1 ? 1 : 0, st));
+    NC_CHECK(dg_accum(c, xh, pairs, NN, t == g.d - 1 ? 1 : 0, st));
     if (t == 0) break;
 
     // field adjoint dX = IFFT(sum_m q^_m . G^_m) on the field rows, then columns

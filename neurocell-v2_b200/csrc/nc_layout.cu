@@ -168,7 +168,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
     if (pairs * (size_t)g.Fh > lines) lines = pairs * (size_t)g.Fh;
     if (M * (size_t)g.kh > lines) lines = M * (size_t)g.kh;
     L.f_field = take(fl * B * FF);
-    L.f_xhat = take(c64 * pairs * NN);
+    L.f_xhat = take(c64 * pairs * NN * (train ? g.d : 1));   // train: one slot per step
     L.f_tmp = take(c64 * lines * (size_t)g.Nw);
     L.f_gspec = take(c64 * M * NN);
     L.f_mean = take(fl * B * M);
