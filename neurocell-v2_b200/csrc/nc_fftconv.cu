@@ -264,6 +264,47 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA, MODE == 2)) cols_ker
     };
     if constexpr (RA > 0) fft::fwd_a_global<RA, true>(s, C, lgC, LS, stw, tid, nt, ld);
     else fft::fwd_a_global_plan<true>(s, C, lgC, LS, N, stw, tid, nt, ld);
+  } else if ((MODE == COL_INV_MULCONJ || MODE == COL_INV_SUM) && C >= 2) {
+    // two adjacent columns per thread: one 16-byte load per operand (Nw even, spectra
+    // 16-byte aligned)
+    const int lgH = lgC - 1;
+#pragma unroll 4
+    for (int idx = tid; idx < N * (C >> 1); idx += nt) {
+      const int r = idx >> lgH, cc = (idx & ((C >> 1) - 1)) * 2;
+      const size_t off = (size_t)r * a.Nw + c0 + cc;
+      float4 v;
+      if (MODE == COL_INV_MULCONJ) {
+        const int p = u / a.M, m = u - p * a.M;
+        const float4 x = *reinterpret_cast<const float4*>(a.src + (size_t)p * NN + off);
+        const float4 h = *reinterpret_cast<const float4*>(a.spec + (size_t)m * NN + off);
+        const float2 lo = cmulc(make_float2(x.x, x.y), make_float2(h.x, h.y));
+        const float2 hi = cmulc(make_float2(x.z, x.w), make_float2(h.z, h.w));
+        v = make_float4(lo.x, lo.y, hi.x, hi.y);
+      } else {
+        float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+        const float2* q = a.src + (size_t)u * a.M * NN + off;
+        for (int m = 0; m < a.M; ++m) {
+          const float4 x = *reinterpret_cast<const float4*>(q + (size_t)m * NN);
+          const float4 h = *reinterpret_cast<const float4*>(a.spec + (size_t)m * NN + off);
+          lo = cadd(lo, cmul(make_float2(x.x, x.y), make_float2(h.x, h.y)));
+          hi = cadd(hi, cmul(make_float2(x.z, x.w), make_float2(h.z, h.w)));
+        }
+        v = make_float4(lo.x, lo.y, hi.x, hi.y);
+      }
+      s[cc * LS + pidx(r)] = make_float2(v.x, v.y);
+      s[(cc + 1) * LS + pidx(r)] = make_float2(v.z, v.w);
+    }
+    if (RA > 0 || (RA < 0 && fft::a_global(N))) {
+      __syncthreads();
+      auto st = [&](int l, int r, float2 v) {
+        if (r < a.rows_out) __stcs(&a.dst[((size_t)u * a.rows_out + r) * a.Nw + c0 + l], v);   // read once
+      };
+      if constexpr (RA > 0) fft::inv_a_global<RA, true>(s, C, lgC, LS, stw, tid, nt, st);
+      else fft::inv_a_global_plan<true>(s, C, lgC, LS, N, stw, tid, nt, st);
+      return;
+    } else {
+      fft::transform_lines_plan<true>(s, C, N, stw, tid, nt);
+    }
   } else {
 #pragma unroll 4
     for (int idx = tid; idx < N * C; idx += nt) {
