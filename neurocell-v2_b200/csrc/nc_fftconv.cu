@@ -9,8 +9,9 @@
 //    samples apart: IFFT(X^ . conj(G^_m)) = z_{2p,m} + i z_{2p+1,m} (forward) and
 //    IFFT(sum_m Q^_m . G^_m) = dX_{2p} + i dX_{2p+1} (field adjoint), and
 //    Re IFFT(X^ . conj(Q^_m)) = sum over the pair of corr(X_b, gz_{b,m}) (filter adjoint),
-//  * the forward transforms leave spectra digit-reversed and the inverse transforms take
-//    them back (nc_fft.cuh), so no pass reorders data,
+//  * the forward transforms leave spectra in a fixed permuted order (digit-reversed for the
+//    radix-4 plans, frequency k1 + R k2 at position 64 k1 + k2 for the two-stage plans) and
+//    the inverse transforms take them back (nc_fft.cuh), so no pass reorders data,
 //  * the transforms are pruned to the rows that hold data (field rows < Fh, plane rows
 //    < roi_h) and to the rows and columns that are kept (ROI outputs, kh x kw filter lags),
 //  * the filter-gradient spectrum is accumulated over samples and steps in a fixed order
@@ -18,7 +19,9 @@
 //    M-irfft2"); every other batch reduction is a fixed-order loop as well, so the backward
 //    is deterministic.
 // The per-step epilogues have the semantics of neurocell/epilogue.py:28-56 / :82-128 with
-// the centred two-pass variance of neurocell/kernels_pallas.py:202-205, as in nc_fused.cu.
+// the centred variance of neurocell/kernels_pallas.py:202-205: per-row centred statistics
+// merged per plane with the two-stage formula of the reference's tiled path
+// (kernels_pallas.py:740-837).
 #include <cuda_runtime.h>
 
 #include "nc_common.cuh"
