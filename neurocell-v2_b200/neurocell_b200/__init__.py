@@ -15,7 +15,8 @@ from .model import VonNeumannNetwork
 from .adaptive_mask import AdaptiveMaskSpec, compute_adaptive_spatial_mask, estimate_effective_filter_radii
 from .trainer import (VNNTrainer, VNNTrainStep, compute_annealed_temperature, default_mse_loss,
                       default_exact_match_metric, packbits_u8_on_device)
-from . import ops
+from . import filters, ops
+from .filters import apply_spatial_filter_2d
 from ._lib import load as load_library, LIB_PATH
 
 __all__ = [
@@ -26,5 +27,5 @@ __all__ = [
     "propagate_vnn_2d", "VonNeumannNetwork", "VNNTrainer", "compute_annealed_temperature",
     "default_mse_loss", "ops", "load_library", "LIB_PATH", "AdaptiveMaskSpec",
     "compute_adaptive_spatial_mask", "estimate_effective_filter_radii", "VNNTrainStep",
-    "default_exact_match_metric", "packbits_u8_on_device",
+    "default_exact_match_metric", "packbits_u8_on_device", "filters", "apply_spatial_filter_2d",
 ]

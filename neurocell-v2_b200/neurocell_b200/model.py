@@ -8,6 +8,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from . import filters
 from .params import VNNParams, compute_codd_state_probs, init_vnn_params
 from .propagator import propagate_vnn_2d
 from .topology import ChipTopology2D
@@ -19,8 +20,6 @@ class VonNeumannNetwork:
                  hard_pin_io: bool = False, backend: str = "b200", dtype=torch.float32,
                  codd_mode: str = "continuous", state_temperature: float = 1.0,
                  active_threshold: float = 0.6):
-        if sharpen:
-            raise NotImplementedError("sharpen=True is not part of the B200 hot path")
         self.topology = topology
         self.activate = activate
         self.final_activate = final_activate
@@ -33,7 +32,8 @@ class VonNeumannNetwork:
         self.codd_mode = codd_mode
         self.state_temperature = state_temperature
         self.active_threshold = active_threshold
-        self.sharpen_filter = None
+        # model.py:65-66: the normalised 3x3 sharpen stencil, applied to W in propagate_vnn_2d
+        self.sharpen_filter = filters.sharpen(norm=True) if sharpen else None
 
     def init(self, rng, clear_outside_io: bool = False, legacy_compat: bool = True,
              device="cuda") -> VNNParams:

@@ -16,6 +16,7 @@ from typing import Sequence
 import torch
 
 from . import ops
+from .filters import apply_spatial_filter_2d
 from .params import VNNParams, check_codd_mode
 from .topology import ChipTopology2D, CoordinatePortSpec
 
@@ -108,7 +109,11 @@ def propagate_vnn_2d(
     act, slope = ops.resolve_activation(activate)
     fact, fslope = ops.resolve_activation(final_activate)
     if sharpen_filter is not None:
-        raise NotImplementedError("sharpen_filter (filters.py) is not part of the B200 hot path")
+        # params.py:246-247: W is filtered (SAME, zeros outside) before the output-port pin,
+        # on the full grid, ahead of any sub-ROI crop; autograd takes the gradient back to W
+        cp = params.cell_params
+        w_sharp = apply_spatial_filter_2d(cp[0], torch.as_tensor(sharpen_filter), padding="SAME")
+        params = VNNParams(torch.cat([w_sharp[None], cp[1:]], dim=0), params.greens_filters)
     roi_bbox = None
     if (spatial_mask is not None and not spatial_mask.is_full_roi
             and topology.padding_mode != "CIRCULAR"):

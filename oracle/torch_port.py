@@ -94,6 +94,9 @@ class TorchVNN:
         M = g.directions
         ph, pw = g.pad_h, g.pad_w
         Wf, Bf, Sf = cell[0], cell[1], cell[2]
+        if c.sharpen:                   # params.py:246-247 (kernels_greens.py:220-237)
+            k = torch.from_numpy(O.sharpen_stencil(True)).to(Wf.dtype)
+            Wf = torch.nn.functional.conv2d(Wf[None, None], k[None, None], padding=1)[0, 0]
         G = torch.sigmoid(filt) if c.gated_filters else filt
         w_pinned = torch.where(self.ow, torch.ones_like(Wf), Wf)
         s = self.codd(Sf)

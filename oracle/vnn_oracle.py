@@ -602,6 +602,36 @@ class Config:
     codd_mode: str = "continuous"
     state_temperature: float = 1.0
     active_threshold: float = 0.6
+    sharpen: bool = False          # model.py:65-66: the normalised 3x3 sharpen stencil on W
+
+
+# ----------------------------------------------------------------------------------------
+# Spatial stencils (filters.py:12-83) and their application to a weight plane
+# (kernels_greens.py:220-237, applied to W before the output-port pin, params.py:246-249)
+# ----------------------------------------------------------------------------------------
+def sharpen_stencil(norm: bool = True, dtype=np.float64):
+    """filters.py:56-68: [[0,-1,0],[-1,5,-1],[0,-1,0]], divided by 5 when ``norm``."""
+    k = np.array([[0, -1, 0], [-1, 5, -1], [0, -1, 0]], dtype=dtype)
+    return k / 5.0 if norm else k
+
+
+def spatial_filter_same(x, k):
+    """SAME cross-correlation of a 2-D plane with an odd stencil, zeros outside
+    (``conv_general_dilated`` with padding "SAME", kernels_greens.py:220-237)."""
+    kh, kw = k.shape
+    ph, pw = kh // 2, kw // 2
+    xp = np.pad(x, ((ph, ph), (pw, pw)))
+    out = np.zeros_like(x)
+    for a in range(kh):
+        for b in range(kw):
+            if k[a, b] != 0:
+                out += k[a, b] * xp[a:a + x.shape[0], b:b + x.shape[1]]
+    return out
+
+
+def spatial_filter_same_adjoint(gy, k):
+    """Adjoint of :func:`spatial_filter_same`: the SAME correlation with the flipped stencil."""
+    return spatial_filter_same(gy, k[::-1, ::-1])
 
 
 def forward(cell_params, filters, inputs, geom: Geometry, cfg: Config = Config(), dtype=np.float64,
@@ -615,7 +645,11 @@ def forward(cell_params, filters, inputs, geom: Geometry, cfg: Config = Config()
     G = _sigmoid(G0) if cfg.gated_filters else G0
     kh, kw = geom.kernel_size
     H, W = geom.grid_shape
-    sp = precompute(cp, geom, cfg.activate, cfg.act_slope, cfg.hard_pin_io, cfg.codd_mode,
+    cp_used = cp
+    if cfg.sharpen:                     # params.py:246-247: W sharpened before the pin
+        cp_used = cp.copy()
+        cp_used[0] = spatial_filter_same(cp[0], sharpen_stencil(True, dtype))
+    sp = precompute(cp_used, geom, cfg.activate, cfg.act_slope, cfg.hard_pin_io, cfg.codd_mode,
                     cfg.state_temperature, cfg.active_threshold)
     d = geom.depth
     tape = dict(sp=sp, G=G, G0=G0, convs=[], epis=[], cp=cp)
@@ -786,6 +820,8 @@ def backward(gout, tape, geom: Geometry, cfg: Config = Config(), final_gy=None, 
         g_B += ring_final_g * dfb * sp["s_prob"]
         g_s += ring_final_g * fb
     g_W = np.where(geom.out_weight_mask, 0.0, g_wp)
+    if cfg.sharpen:
+        g_W = spatial_filter_same_adjoint(g_W, sharpen_stencil(True, g_W.dtype))
     g_S = g_s * sp["ds_prob"]
     g_cell = np.stack([g_W, g_B, g_S]).astype(G.dtype)
     if cfg.gated_filters:

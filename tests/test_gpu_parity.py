@@ -52,7 +52,7 @@ def run_gpu(geom, cfg, cell, filt, inputs, targets, loss="mse", train=True, back
         final_activate=ACT[cfg.final_activate], norm=cfg.norm, gated_filters=cfg.gated_filters,
         hard_pin_io=cfg.hard_pin_io, codd_mode=cfg.codd_mode,
         state_temperature=cfg.state_temperature, active_threshold=cfg.active_threshold,
-        backend=backend)
+        sharpen_filter=nc.filters.sharpen(norm=True) if cfg.sharpen else None, backend=backend)
     if not train:
         return out.detach().cpu().numpy(), None, None, None
     y = torch.tensor(np.asarray(targets), device=dev)
@@ -584,3 +584,23 @@ def test_fft_direction_blocks_parity(grid, kernel, M):
                            O.CoordPort(tuple((r, 2 * W // 3) for r in range(r0, r0 + 3))))
     cell, filt, ins, y = random_problem(geom, 3, 191 + M)
     check_case(geom, O.Config(), cell, filt, ins, y, backend="pallas_sram")
+
+
+# ---- the sharpen weight filter (model.py:65-66, params.py:246-247) ----------------------
+@pytest.mark.parametrize("backend", ["b200", "nchw_direct", "pallas_sram"])
+def test_sharpen_filter_parity(backend):
+    """W sharpened by the normalised 3x3 stencil before the pin, on every kernel family
+    (the ALU chip: fused 64x64 FFT kernels for "b200", direct kernels, per-step FFT kernels)."""
+    geom, cfg, cell, filt, x, y = alu_problem(4, 211)
+    check_case(geom, O.Config(sharpen=True), cell, filt, x, y, backend=backend)
+
+
+def test_sharpen_option_of_the_model_facade():
+    geom, cfg, cell, filt, x, y = alu_problem(2, 212)
+    topo = _nc_topo(geom)
+    dev = torch.device("cuda:0")
+    p = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
+    xin = torch.tensor(x, dtype=torch.float32, device=dev)
+    out = nc.VonNeumannNetwork(topo, sharpen=True).apply(p, xin)
+    ref, _ = O.forward(cell, filt, x, geom, O.Config(sharpen=True))
+    assert _rel(out.cpu().numpy(), ref) <= TOL

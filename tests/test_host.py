@@ -194,3 +194,28 @@ def test_annealed_temperature_schedule():
     assert nc.compute_annealed_temperature(5, 11, 1.0, 0.1, "linear") == pytest.approx(0.55)
     with pytest.raises(ValueError):
         nc.compute_annealed_temperature(1, 3, schedule="step")
+
+
+def test_filter_stencils_and_spatial_filter():
+    """The reference's stencils (filters.py:12-83) and apply_spatial_filter_2d
+    (kernels_greens.py:220-237) on CPU tensors, against the oracle's SAME correlation."""
+    f = nc.filters
+    assert f.sharpen(norm=False).tolist() == [[0, -1, 0], [-1, 5, -1], [0, -1, 0]]
+    assert torch.allclose(f.sharpen(), f.sharpen(norm=False) / 5)
+    assert f.smooth(norm=True).tolist() == [[1, 1, 1], [1, 8, 1], [1, 1, 1]]
+    assert f.backward(norm=True).tolist() == [[1, 0, 0], [1, 3, 0], [1, 0, 0]]
+    assert f.forward().tolist() == [[0, 0, 1], [0, 0, 1], [0, 0, 1]]
+    assert f.von_neumann().tolist() == [[1, 0, 1], [1, 1, 1], [1, 0, 1]]
+    k3 = f.sharpen_3d(norm=False)
+    assert k3.shape == (3, 3, 3) and float(k3.sum()) == -1.0 and float(k3[1, 1, 1]) == 5.0
+    rng = np.random.default_rng(5)
+    x = torch.from_numpy(rng.normal(size=(10, 8)))
+    k = torch.from_numpy(rng.normal(size=(3, 3)))
+    same = nc.apply_spatial_filter_2d(x, k)
+    assert same.shape == (10, 8)
+    assert np.allclose(same.numpy(), O.spatial_filter_same(x.numpy(), k.numpy()), atol=1e-13)
+    assert nc.apply_spatial_filter_2d(x, k, padding="VALID").shape == (8, 6)
+    with pytest.raises(ValueError):
+        nc.apply_spatial_filter_2d(x, torch.ones(2, 2))
+    with pytest.raises(ValueError):
+        nc.apply_spatial_filter_2d(x, k, padding="FULL")
