@@ -219,3 +219,18 @@ def test_filter_stencils_and_spatial_filter():
         nc.apply_spatial_filter_2d(x, torch.ones(2, 2))
     with pytest.raises(ValueError):
         nc.apply_spatial_filter_2d(x, k, padding="FULL")
+
+
+def test_product_path_refuses_cpu_tensors():
+    """No CPU fallback: the public entry points refuse host tensors instead of computing."""
+    topo = nc.ChipTopology2D.alu_chip()
+    cell = torch.zeros(3, 62, 62)
+    filt = torch.zeros(16, 1, 23, 13)
+    p = nc.VNNParams(cell, filt)
+    x = torch.zeros(2, 3, 8, 1)
+    with pytest.raises(ValueError, match="no CPU path"):
+        nc.propagate_vnn_2d(p, x, topo)
+    with pytest.raises(ValueError, match="no CPU path"):
+        nc.VonNeumannNetwork(topo).apply(p, x)
+    with pytest.raises(ValueError, match="no CPU path"):
+        nc.VNNTrainStep(topo, p, 2)
