@@ -355,7 +355,8 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA, MODE == 2)) cols_ker
 // acc[m][f] (+)= sum over pairs of x^[p][f] * conj(q^[p][m][f])  (fixed pair order).  A
 // thread takes two adjacent frequencies (16-byte accesses) of kDgM directions
 // (blockIdx.y), so x^ is read once per kDgM directions and the kDgM q^ loads of a pair are
-// independent.  NN is even (power-of-two grids) and the spectra are 16-byte aligned.
+// independent.  NN is even (the planner's FFT sides are powers of two, at least 2) and the
+// spectra are 16-byte aligned.
 // dg_accum picks kDgM per grid size so that small grids still fill the GPU.
 template <int kDgM>
 __global__ void dg_accum_kernel(const float2* __restrict__ xhat, const float2* __restrict__ q,
