@@ -44,6 +44,33 @@ WORKLOAD_FIELDS = {"workload": WORKLOAD, "grid": [62, 62], "roi": [40, 50], "ker
                    "depth": 4, "codd_mode": "continuous", "loss": "mse", "optimizer": "sgd(1e-2)"}
 
 
+L2_NOTE = "GPU arm: L2 flushed (256 MB write) before every timed step; CPU arm: not applicable"
+
+
+def workload_config(world: int) -> dict:
+    """The `config` object of the bench line: the same keys and values in both arms."""
+    return {**WORKLOAD_FIELDS, "per_gpu_batch": BATCH, "global_batch": BATCH * world,
+            "parallelism": f"dp{world}", "l2": L2_NOTE}
+
+
+def fftf_executed_flops(M: int, roi_h: int, Fh: int, kh: int, d: int) -> tuple[float, float]:
+    """FLOPs the fused 64 x 64 FFT kernels execute per sample (forward, backward), counted per
+    transform and pointwise product: 5 N log2 N = 1920 per 64-point complex transform (the
+    usual FFT count), 6 per complex product, 8 per complex multiply-accumulate.  Per step the
+    forward transforms the field (Fh rows + 64 columns) and, per direction pair, forms
+    X^.H_j and runs 64 inverse columns and roi_h inverse rows.  The backward, per pair, runs
+    roi_h + 64 forward lines of the plane gradients, D += Q^.conj(H_j) (steps t > 0),
+    X^.conj(Q^), 64 inverse columns and kh inverse lag rows, and per step t > 0 the
+    inverse field adjoint (64 columns + Fh rows); it reloads the forward's field spectra."""
+    c64, nn = 5.0 * 64 * 6, 64.0 * 64.0
+    pairs = M // 2
+    fwd_step = (Fh + 64) * c64 + pairs * (6 * nn + (64 + roi_h) * c64)
+    bwd_pair = (roi_h + 64 + 64 + kh) * c64 + 6 * nn
+    bwd = sum(pairs * (bwd_pair + (8 * nn if t > 0 else 0)) + ((64 + Fh) * c64 if t > 0 else 0)
+              for t in range(d))
+    return d * fwd_step, bwd
+
+
 def alu_flops_per_sample(train: bool = True) -> float:
     """Effective direct-convolution FLOPs per sample: 2*M*P*K per pass; a train step makes
     d forward passes, d filter-gradient passes and d-1 field-adjoint passes."""
@@ -69,50 +96,77 @@ def make_problem(rank: int, n_batches: int, batch: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clocks and clock-event (throttle) reasons of one GPU, polled through NVML every
+    2 ms in a background thread (the timed regions of config 0 last only a few ms, too short
+    for nvidia-smi's 200 ms loop).  ``mark_start()`` / ``mark_stop()`` bracket the timed
+    region; ``stop()`` summarises the samples taken inside it.  Falls back to nvidia-smi
+    when NVML is unavailable."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, gpu_index: int):
-        self.rows = []
-        self.proc = None
+    def __init__(self, device):
+        self.rows = []                 # (t, sm_mhz, max_mhz, reason bits)
+        self.t0 = self.t1 = None
+        self.source = "nvml (2 ms polling)"
+        self._stop = threading.Event()
+        self.nvml = None
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(gpu_index)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.nvml, self.h = pynvml, h
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.t = threading.Thread(target=self._poll, daemon=True)
             self.t.start()
-        except OSError:
-            self.proc = None
+        except Exception as e:   # noqa: BLE001 -- no NVML: nothing to sample
+            self.source = f"unavailable ({type(e).__name__})"
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+    def _poll(self):
+        nv, h = self.nvml, self.h
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                              getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                bits = int(get_reasons(h)) if get_reasons else 0
+                self.rows.append((time.perf_counter(), sm, bits))
+            except Exception:   # noqa: BLE001
+                pass
+            time.sleep(0.002)
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_stop(self):
+        self.t1 = time.perf_counter()
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-            except (ValueError, IndexError):
-                continue
-            for n, v in zip(names, r[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "source": self.source}
+        self._stop.set()
+        self.t.join(timeout=2)
+        inside = [r for r in self.rows if self.t0 is not None and self.t1 is not None
+                  and self.t0 <= r[0] <= self.t1]
+        sm = [r[1] for r in inside]
+        reasons = set()
+        for name, const in self.REASONS:
+            bit = getattr(self.nvml, const, 0)
+            if any(r[2] & bit for r in inside):
+                reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "window_ms": (self.t1 - self.t0) * 1e3 if self.t0 and self.t1 else None,
+                "source": self.source}
+
+
+def spread(ms: list) -> dict:
+    """Median and 10th / 90th percentiles of per-step times (ms)."""
+    q = np.percentile(np.asarray(ms, dtype=np.float64), [10, 50, 90])
+    return {"p10": float(q[0]), "median": float(q[1]), "p90": float(q[2]), "n": len(ms)}
 
 
 def fp32_peak_tflops(device) -> float:
@@ -181,18 +235,20 @@ def run_reference(args) -> None:
         t0 = time.perf_counter()
         T.value_and_grad(g, O.Config(), cell, filt, ports, ys[0], dtype=torch.float32)
         times.append(time.perf_counter() - t0)
-    ms = 1e3 * statistics.mean(times)
+    sp = spread([1e3 * t for t in times])
+    ms = sp["median"]
     val = BATCH / (ms * 1e-3)
     line = {
         "impl": "reference", "metric": METRIC, "value": val,
         "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded numpy ALU batches)",
-        "config": dict(WORKLOAD_FIELDS, per_gpu_batch=BATCH, global_batch=BATCH,
-                       parallelism=f"cpu, {threads} threads"),
+        "ms_per_step": ms, "ms_spread": sp, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy ALU batches)",
+        "config": workload_config(args.gpus),
         "cpu_baseline": {"value": val, "unit": "samples/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} full B={BATCH} train steps of oracle/torch_port.py "
-                                   "(the reference's JAX CPU path is not installable here)"},
+                         "sample": f"{args.steps} full B={BATCH} train steps of oracle/torch_port.py, "
+                                   f"median, on {threads} host threads (one {BATCH}-sample batch of "
+                                   f"the {BATCH * args.gpus}-sample global step; the reference's JAX "
+                                   "CPU path is not installable here)"},
         "e2e": {"value": val, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -256,9 +312,11 @@ def run_b200(args) -> None:
         for e in row:
             e.record()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(dev)
+    time.sleep(0.02)
     barrier()
     torch.cuda.synchronize()
+    clocks.mark_start()
     for i in range(K):
         runner.load_batch(x_dev[i % nb], y_dev[i % nb])
         l2_flush.fill_(float(i))
@@ -269,10 +327,12 @@ def run_b200(args) -> None:
         ev[i][1].record()
     lib.nc_set_profile_events(None, None, None, None)
     torch.cuda.synchronize()
+    clocks.mark_stop()
     barrier()
     clk = clocks.stop()
     step_ms = [a.elapsed_time(b) for a, b in ev]
-    ms = statistics.mean(step_ms)
+    sp = spread(step_ms)
+    ms = sp["median"]
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if pg is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -289,8 +349,8 @@ def run_b200(args) -> None:
         lib.nc_set_profile_events(None, None, None, None)
         torch.cuda.synchronize()
         kev = kev[:min(K, 10)]
-    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in kev)
-    bwd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in kev)
+    fwd_ms = statistics.median(e[0].elapsed_time(e[1]) for e in kev)
+    bwd_ms = statistics.median(e[2].elapsed_time(e[3]) for e in kev)
 
     # ---- end to end through the public API: pinned host batches, H2D + step + D2H loss
     x_host = torch.tensor(xs.reshape(nb, BATCH, -1)).pin_memory()
@@ -307,7 +367,8 @@ def run_b200(args) -> None:
         eev[i][1].record()
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = statistics.mean(a.elapsed_time(b) for a, b in eev)
+    e2e_sp = spread([a.elapsed_time(b) for a, b in eev])
+    e2e_ms = e2e_sp["median"]
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if pg is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -335,17 +396,17 @@ def run_b200(args) -> None:
                        "train samples/s (62x62 ALU VNN on its adaptive %dx%d sub-ROI, B=128 per GPU)"
                        % spec.active_shape), "value": value,
             "unit": "samples/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
-            "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": ms_max, "ms_spread": sp, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded numpy ALU batches, random-init params as BASELINE config 0)",
-            "config": {**WORKLOAD_FIELDS, "per_gpu_batch": BATCH, "global_batch": BATCH * world,
-                       "parallelism": f"dp{world}", "l2": "flushed (256 MB write) before every timed step",
-                       "cuda_graph": runner.graph is not None,
-                       "grad_exchange": (args.exchange if world > 1 else "none"),
-                       "conv": args.conv,
-                       "sub_roi": None if spec is None else list(spec.roi_bbox)},
+            "config": workload_config(world),
+            "run": {"cuda_graph": runner.graph is not None,
+                    "grad_exchange": (args.exchange if world > 1 else "none"),
+                    "conv": args.conv, "sub_roi": None if spec is None else list(spec.roi_bbox),
+                    "timing": "median of per-step CUDA-event times on the launching stream, max over ranks"},
             "e2e": {"value": BATCH * world / (e2e_ms * 1e-3), "unit": "samples/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms,
+                    "ms_spread": e2e_sp},
             "gpu_launches": runner.launches_per_step() * K,
             "conv_path": {1: "direct per-sample kernels", 2: "FFT per-step kernels",
                           3: "fused per-sample FFT kernels"}.get(path, "?"),
@@ -356,9 +417,20 @@ def run_b200(args) -> None:
                                  "reporting rule; the FFT kernels execute far fewer",
                          "peak_source": "live FFMA probe (nc_fp32_peak_probe); MEASURED_PEAKS.json has no FP32 figure",
                          "traffic": ncu_traffic(dom),
-                         "traffic_source": "profiles/ncu_traffic.json (one ncu capture, dram read+write per launch)"},
+                         "traffic_source": "profiles/ncu_traffic.json (one ncu capture, dram read+write per launch)",
+                         "fma_pipe_active_ncu": ncu_entry(dom, "fma_pipe_active"),
+                         "issue_active_ncu": ncu_entry(dom, "issue_active")},
             "clocks": clk,
         }
+        if path == 3:
+            # what the FFT kernels really execute, beside the effective direct-convolution figure
+            ef, eb = fftf_executed_flops(16, 40, 62, 23, 4)
+            dom_ms = bwd_ms if dom == names[1] else fwd_ms
+            ex = BATCH * (eb if dom == names[1] else ef) / (dom_ms * 1e-3) / 1e12
+            line["roofline"].update(
+                executed_tflops=ex, executed_frac=ex / peak if peak else None,
+                executed_work="5 N log2 N per 64-point complex transform, 6 per complex product, "
+                              "8 per complex multiply-accumulate (bench.py fftf_executed_flops)")
         tr = ncu_traffic(dom)
         if tr:
             # the same kernel against HBM: captured DRAM bytes per launch / its event time
@@ -389,13 +461,18 @@ def hbm_peak() -> tuple[float, str]:
         return 6650.0, "fallback (profiling recipe)"
 
 
-def ncu_traffic(kernel: str):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary, or None."""
+def ncu_entry(kernel: str, key: str):
+    """A figure of `kernel` from the committed ncu summary (profiles/ncu_traffic.json), or None."""
     try:
         with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
-            return json.load(f).get(kernel, {}).get("bytes")
+            return json.load(f).get(kernel, {}).get(key)
     except (OSError, ValueError):
         return None
+
+
+def ncu_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, or None."""
+    return ncu_entry(kernel, "bytes")
 
 
 def config_problem(cfg: int, batch: int, seed_rank: int):
@@ -530,7 +607,9 @@ def run_config(args) -> None:
         torch.cuda.synchronize()
     K = args.steps
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(dev)
+    time.sleep(0.02)
+    clocks.mark_start()
     anneal = meta["train"] and meta["codd_mode"] == "annealed"
     for i in range(K):
         if anneal:       # tau 1.0 -> 0.1 over the steps (exponential)
@@ -540,6 +619,7 @@ def run_config(args) -> None:
         step()
         ev[i][1].record()
     torch.cuda.synchronize()
+    clocks.mark_stop()
     clk = clocks.stop()
     ms = statistics.median(a.elapsed_time(b) for a, b in ev)
     if pg is not None:

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define NC_ABI_VERSION 5
+#define NC_ABI_VERSION 6
 
 typedef enum nc_status {
   NC_OK = 0,
@@ -255,9 +255,10 @@ nc_status nc_sgd_update(float* params, const float* grads, int64_t n, float lr, 
  * ~16k-parameter gradient to be all-reduced across 1/2/4/8 GPUs).  nc_dp_allreduce_sgd
  * fuses the cross-GPU gradient sum with the SGD update in one kernel: every rank stores
  * its packed gradient into its slot of every peer's double-buffered receive buffer over
- * NVLink, raises per-slice flags there, waits (bounded) for the same slices of all peers
- * in its own buffer, sums them in rank order from local memory (bitwise identical on
- * every rank) and updates its parameters.
+ * NVLink, each value in one 64-bit element together with the current step number (so a
+ * value and its tag always arrive together), waits (bounded) until the elements of all
+ * peers in its own buffer carry this step's tag, sums them in rank order from local memory
+ * (bitwise identical on every rank) and updates its parameters.
  * Set-up: nc_dp_alloc on every rank, exchange nc_ipc_get handles (e.g. all_gather), open
  * the peers' buffers with nc_ipc_open, zero-initialised state from nc_dp_alloc.
  * Step counters live on the device, so the call can be captured in a CUDA graph.
@@ -281,15 +282,26 @@ nc_status nc_ipc_close(void* d_peer_ptr);
 /*
  * grads[n] (this rank's gradient of its mean loss) -> grads[n] = sum over ranks,
  * params[n] -= lr / world * grads[n].  peers[world] are the shared buffers of all ranks
- * (this rank's own at index rank).  A peer that does not arrive within max_wait_iters
- * polls makes the kernel skip the update and set the status word; read it with
- * nc_dp_status (0 = ok, 1 = a peer timed out).
+ * (this rank's own at index rank).
+ * Failure: a peer that does not arrive within max_wait_iters polls sets the status word
+ * (read it with nc_dp_status: 0 = ok, 1 = a peer timed out).  The slices whose peers did
+ * not arrive are left untouched; slices whose peers did arrive in that call were updated,
+ * so the ranks' parameters no longer agree.  The status is terminal: every later call on
+ * this state returns without storing to peers or updating, which makes every peer time out
+ * at its next step too.  To go on, restore the parameters from a consistent copy, call
+ * nc_dp_reset on every rank and pass a host barrier before the next exchange.
  */
 nc_status nc_dp_allreduce_sgd(void* const* peers, int32_t world, int32_t rank, void* d_state,
                               float* grads, float* params, int64_t n, float lr,
                               int32_t max_wait_iters, void* stream);
 /* Copies the device status word of d_state to *status (synchronises the stream). */
 nc_status nc_dp_status(const void* d_state, int32_t* status, void* stream);
+/*
+ * Clears this rank's state (step counters, status word) and its own receive buffer
+ * (d_shared, shared_bytes from nc_dp_shared_bytes), stream-ordered.  Every rank resets, then
+ * the ranks pass a host barrier, with no exchange kernel in flight on any rank.
+ */
+nc_status nc_dp_reset(void* d_state, void* d_shared, size_t shared_bytes, void* stream);
 
 /* ---- measurement ----------------------------------------------------------------------- */
 
@@ -314,12 +326,14 @@ nc_status nc_fp32_peak_probe(int32_t iters, double* flops, float* sink, void* st
 const char* nc_last_error(void);
 
 /*
- * Sticky error word of the current device: 0 ok; 1 when a kernel's bounded wait for its
- * own asynchronous copies into shared memory gave up (the results of that call are
- * invalid); -1 when it could not be read.  clear != 0 resets it.  Synchronous (a device
- * read); not for the hot path.
+ * Status word of a workspace (the first 4 bytes of every layout): 0 ok; 1 when a kernel of
+ * the latest nc_vnn_forward / nc_vnn_forward_universe on d_ws, or of a backward after it,
+ * gave up a bounded wait for its own asynchronous copies into shared memory (every result
+ * of that call is then invalid).  Each forward clears it when it starts; calls on other
+ * workspaces never touch it.  Copies the word to *status and synchronises the stream;
+ * not for the hot path.
  */
-int32_t nc_device_error(int32_t clear);
+nc_status nc_workspace_status(const void* d_ws, int32_t* status, void* stream);
 
 /* NC_ABI_VERSION of the loaded library. */
 int32_t nc_abi_version(void);

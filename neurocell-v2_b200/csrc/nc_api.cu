@@ -146,6 +146,7 @@ static StepParams step_params(void* ws, const WsLayout& L) {
   sp.dsprob = at<float>(ws, L.dsprob);
   sp.wpinned = at<float>(ws, L.wpinned);
   sp.geff = at<float>(ws, L.geff);
+  sp.status = at<int>(ws, L.status);
   return sp;
 }
 
@@ -314,7 +315,18 @@ int32_t nc_conv_path(const nc_topo* topo) {
 
 const char* nc_last_error(void) { return g_err; }
 
-int32_t nc_device_error(int32_t clear) { return fftf_device_error(clear != 0); }
+nc_status nc_workspace_status(const void* d_ws, int32_t* status, void* stream) {
+  if (!d_ws || !status) return set_error(NC_ERR_INVALID, "bad nc_workspace_status arguments");
+  if (reinterpret_cast<uintptr_t>(d_ws) % 256 != 0)
+    return set_error(NC_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  int v = -1;
+  NC_CUDA_CHECK(cudaMemcpyAsync(&v, d_ws, sizeof(int), cudaMemcpyDeviceToHost, st));
+  NC_CUDA_CHECK(cudaStreamSynchronize(st));
+  *status = v;
+  clear_error();
+  return NC_OK;
+}
 
 size_t nc_plan_bytes(const nc_topo* topo) {
   Geo g;

@@ -16,6 +16,7 @@ __global__ void prestep_kernel(Geo g, StepParams sp, const float* __restrict__ c
                                nc_codd codd) {
   const int HW = g.H * g.W;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i == 0 && sp.status) *sp.status = 0;   // a new forward call starts
   if (i < HW) prestep_cell(g, sp, cell, io, owm, bmask, codd, i);
   const int nf = g.M * g.K;
   for (int j = i; j < nf; j += gridDim.x * blockDim.x) sp.geff[j] = geff_tap(g, filters, j);

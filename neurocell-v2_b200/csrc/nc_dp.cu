@@ -1,20 +1,32 @@
 // nc_dp.cu -- fused cross-GPU gradient sum + SGD over NVLink peer memory (sm_100a).
 //
-// Push protocol with step-tagged lines.  Each rank owns a receive buffer of 16-byte lines
-//   [2 parity][world source ranks][n_lines]   line = {g[2l], step, g[2l+1], step}
-// mapped into every peer with CUDA IPC.  Every step each rank stores its gradient, two
-// values per line, into slot (parity, own rank) of every PEER's buffer with one 16-byte
-// store per line (posted NVLink writes; each 8-byte half {value, step} is written as one
-// unit).  A receiver knows a value has arrived when the step tag next to it equals the
-// current step, so no fences and no separate flags are needed: block k polls the lines of
-// its slice in its OWN buffer (bounded), then sums the slice over ranks 0..world-1 in that
-// order (its own contribution straight from `grads`) and applies SGD.  Every rank adds the
-// same values in the same order and ends with bitwise identical parameters.  Double
-// buffering makes the next step safe: a rank writes slot `parity` again only at step+2,
-// after every peer has published step+1, i.e. after every peer finished reading step's
-// slot (its step kernel ended before its step+1 kernel began).  Step counters are per block
-// and live on the device, so the launch can be captured in a CUDA graph.  No multicast,
-// no TMA, no atomics on peer memory: plain stores and volatile loads.
+// Push protocol with step-tagged elements.  Each rank owns a receive buffer of 8-byte
+// elements
+//   [2 parity][world source ranks][n_elems]   element = (uint64(step) << 32) | float_bits(g)
+// mapped into every peer with CUDA IPC.  Every step each rank stores its gradient into slot
+// (parity, own rank) of every PEER's buffer, two elements per 16-byte vector store (posted
+// NVLink writes).  Each element is one naturally aligned 64-bit access, which the PTX
+// memory model makes single-copy atomic even inside a vector access, so a reader sees a
+// value together with the tag written with it -- never the current tag beside an older
+// value.  A receiver knows a value has arrived when its tag equals the current step, so no
+// fences and no separate flags are needed: block k polls the elements of its slice in its
+// OWN buffer (bounded), then sums the slice over ranks 0..world-1 in that order (its own
+// contribution straight from `grads`) and applies SGD.  Every rank adds the same values in
+// the same order and ends with bitwise identical parameters.  Double buffering makes the
+// next step safe: a rank writes slot `parity` again only at step+2, after every peer has
+// published step+1, i.e. after every peer finished reading step's slot (its step kernel
+// ended before its step+1 kernel began).  Step counters are per block and live on the
+// device, so the launch can be captured in a CUDA graph.  No multicast, no TMA, no atomics
+// on peer memory: plain volatile stores and loads.
+//
+// Failure: a block whose peers do not arrive within max_wait polls sets the status word
+// and returns without touching its slice.  The status is terminal: every later call on
+// that state returns at once (no stores to peers, no update), so the peers of this rank
+// time out at their next step as well and the failure reaches every rank within one step.
+// Parameters of slices whose blocks did complete the failing step WERE updated, so after a
+// failure the ranks' parameters are no longer known to agree: restore them from a
+// consistent copy, then call nc_dp_reset on every rank (and a host barrier) before the
+// next exchange.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -30,24 +42,24 @@ constexpr int kDpBlocks = 32;
 constexpr int kDpThreads = 128;
 
 struct Peers {
-  uint4* p[NC_DP_MAX_RANKS];
+  ulonglong2* p[NC_DP_MAX_RANKS];
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+// 16-byte lines of two elements each
 __host__ __device__ inline long long n_lines(long long n) { return (n + 1) / 2; }
 
-__device__ __forceinline__ void st_line(uint4* p, uint4 v) {
-  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
+__device__ __forceinline__ unsigned long long tagged(float v, unsigned step) {
+  return ((unsigned long long)step << 32) | (unsigned long long)__float_as_uint(v);
 }
 
-__device__ __forceinline__ uint4 ld_line(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p)
-               : "memory");
+__device__ __forceinline__ void st_line(ulonglong2* p, ulonglong2 v) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(v.x), "l"(v.y) : "memory");
+}
+
+__device__ __forceinline__ ulonglong2 ld_line(const ulonglong2* p) {
+  ulonglong2 v;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
   return v;
 }
 
@@ -69,9 +81,10 @@ __global__ void __launch_bounds__(kDpThreads) dp_allreduce_sgd_kernel(
   __shared__ int s_bad;
   if (threadIdx.x == 0) {
     s_step = counters[k] + 1u;
-    s_bad = 0;
+    s_bad = *reinterpret_cast<volatile int*>(status);   // terminal after a failure
   }
   __syncthreads();
+  if (s_bad) return;
   const unsigned step = s_step;
   const int par = (int)(step & 1u);
   auto slot = [&](int owner, int src) {   // slot (par, src) of rank owner's buffer
@@ -80,7 +93,7 @@ __global__ void __launch_bounds__(kDpThreads) dp_allreduce_sgd_kernel(
   // 1. push this rank's lines to every peer
   for (long long l = l0 + threadIdx.x; l < l1; l += blockDim.x) {
     const float2 v = load_pair(grads, n, l);
-    const uint4 line = make_uint4(__float_as_uint(v.x), step, __float_as_uint(v.y), step);
+    const ulonglong2 line = make_ulonglong2(tagged(v.x, step), tagged(v.y, step));
     for (int r = 0; r < world; ++r)
       if (r != rank) st_line(slot(r, rank) + l, line);
   }
@@ -89,10 +102,10 @@ __global__ void __launch_bounds__(kDpThreads) dp_allreduce_sgd_kernel(
   for (long long l = l0 + threadIdx.x; l < l1 && !bad; l += blockDim.x) {
     for (int r = 0; r < world && !bad; ++r) {
       if (r == rank) continue;
-      const uint4* q = slot(rank, r) + l;
+      const ulonglong2* q = slot(rank, r) + l;
       for (;;) {
-        const uint4 v = ld_line(q);
-        if (v.y == step && v.w == step) break;
+        const ulonglong2 v = ld_line(q);
+        if ((unsigned)(v.x >> 32) == step && (unsigned)(v.y >> 32) == step) break;
         if (++it > max_wait) { bad = 1; break; }
         if (it > 64) __nanosleep(32);
       }
@@ -104,7 +117,7 @@ __global__ void __launch_bounds__(kDpThreads) dp_allreduce_sgd_kernel(
     if (threadIdx.x == 0) atomicExch(status, 1);
     return;
   }
-  // 3. sum in rank order, SGD
+  // 3. sum in rank order, SGD (the tags were checked above; the values came with them)
   for (long long l = l0 + threadIdx.x; l < l1; l += blockDim.x) {
     float2 s = make_float2(0.f, 0.f);
     for (int r = 0; r < world; ++r) {
@@ -112,8 +125,8 @@ __global__ void __launch_bounds__(kDpThreads) dp_allreduce_sgd_kernel(
       if (r == rank) {
         v = load_pair(grads, n, l);
       } else {
-        const uint4 q = ld_line(slot(rank, r) + l);
-        v = make_float2(__uint_as_float(q.x), __uint_as_float(q.z));
+        const ulonglong2 q = ld_line(slot(rank, r) + l);
+        v = make_float2(__uint_as_float((unsigned)q.x), __uint_as_float((unsigned)q.y));
       }
       if (r == 0) s = v; else { s.x += v.x; s.y += v.y; }
     }
@@ -138,7 +151,7 @@ extern "C" {
 
 size_t nc_dp_shared_bytes(int64_t n, int32_t world) {
   if (n <= 0 || world < 1 || world > NC_DP_MAX_RANKS) return 0;
-  return align256(sizeof(uint4) * 2 * (size_t)world * (size_t)n_lines(n));
+  return align256(sizeof(ulonglong2) * 2 * (size_t)world * (size_t)n_lines(n));
 }
 
 size_t nc_dp_state_bytes(void) { return align256(sizeof(unsigned) * kDpBlocks + sizeof(int)); }
@@ -191,7 +204,7 @@ nc_status nc_dp_allreduce_sgd(void* const* peers, int32_t world, int32_t rank, v
     if (!peers[r]) return set_error(NC_ERR_INVALID, "peer buffer %d is null", r);
     if (reinterpret_cast<uintptr_t>(peers[r]) % 16 != 0)
       return set_error(NC_ERR_INVALID, "peer buffer %d is not 16-byte aligned", r);
-    pp.p[r] = static_cast<uint4*>(peers[r]);
+    pp.p[r] = static_cast<ulonglong2*>(peers[r]);
   }
   unsigned* counters = static_cast<unsigned*>(d_state);
   int* status = reinterpret_cast<int*>(counters + kDpBlocks);
@@ -211,6 +224,16 @@ nc_status nc_dp_status(const void* d_state, int32_t* status, void* stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   NC_CUDA_CHECK(cudaMemcpyAsync(status, s, sizeof(int), cudaMemcpyDeviceToHost, st));
   NC_CUDA_CHECK(cudaStreamSynchronize(st));
+  return NC_OK;
+}
+
+nc_status nc_dp_reset(void* d_state, void* d_shared, size_t shared_bytes, void* stream) {
+  if (!d_state || !d_shared || shared_bytes == 0 || shared_bytes % 16 != 0)
+    return set_error(NC_ERR_INVALID, "bad nc_dp_reset arguments");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  NC_CUDA_CHECK(cudaMemsetAsync(d_state, 0, nc_dp_state_bytes(), st));
+  NC_CUDA_CHECK(cudaMemsetAsync(d_shared, 0, shared_bytes, st));
+  clear_error();
   return NC_OK;
 }
 

@@ -44,9 +44,11 @@ __device__ __forceinline__ int at2(int r, int c) { return fft64::at(r, c); }
 
 // ---- bulk copies global -> shared (cp.async.bulk, completion on an mbarrier) ------------
 // Used to stage the next direction pair's spectra and saved planes while the current pair
-// computes.  Every wait is bounded; a wait that gives up sets g_fftf_error, waits once more
-// (bounded) for the copy in flight and lets the kernel run on (its results are invalid).
-__device__ int g_fftf_error;
+// computes.  Every wait is bounded.  A wait that gives up sets the call's status word in the
+// workspace (StepParams::status, read by nc_workspace_status) and the CTA's abort flag in
+// shared memory, then waits once more (bounded) for the copy in flight.  The kernels read
+// the abort flag after the next barrier, wait (bounded) for every copy they still have in
+// flight, and return together; every output of that launch is then invalid.
 constexpr int kWaitLimit = 1 << 20;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -83,12 +85,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   return ok != 0;
 }
 // Waits for the completion of phase `parity` of `bar` (bounded, see above).
-__device__ __forceinline__ void mbar_wait(uint64_t* bar, unsigned parity) {
+__device__ __forceinline__ void mbar_wait(uint64_t* bar, unsigned parity, int* status, volatile int* abort_flag) {
   for (int it = 0; it < kWaitLimit; ++it)
     if (mbar_try_wait(bar, parity)) return;
-  atomicExch(&g_fftf_error, 1);
+  if (status) atomicExch(status, 1);
+  *abort_flag = 1;
   for (int it = 0; it < kWaitLimit; ++it)
     if (mbar_try_wait(bar, parity)) return;
+}
+// Before an early return: bounded waits for the copies issued on `bar` and not yet waited.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, unsigned used, unsigned issued) {
+  for (; used < issued; ++used)
+    for (int it = 0; it < kWaitLimit; ++it)
+      if (mbar_try_wait(bar, used & 1u)) break;
 }
 
 #if NC_PHASE_TIMING
@@ -230,6 +239,7 @@ template <int ACT, int FACT>
 __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
   extern __shared__ float4 smem4[];
   uint64_t* hbar = reinterpret_cast<uint64_t*>(smem4);   // staging barrier (16 B slot)
+  volatile int* abort_flag = reinterpret_cast<int*>(smem4) + 2;   // in the same slot
   float2* stw = reinterpret_cast<float2*>(smem4 + 1);
   float2* X = stw + kN;
   float2* Wp = X + kPlane;
@@ -251,8 +261,9 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
   // layout (row stride 66: the column pass reads them without bank conflicts), so they
   // move as four bulk copies each.  Warp 0, after a barrier that ends the previous readers
   // of Hs.
-  unsigned huse = 0;
+  unsigned huse = 0, hiss = 0;
   auto issue_h = [&](int j0) {
+    ++hiss;
     if (tid < 32) {
       const int np = (j0 + 1 < pairs) ? 2 : 1;
       if (tid == 0) mbar_expect_tx(hbar, np * kPlaneBytes);
@@ -264,6 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
                  kPlaneChunk, hbar);
     }
   };
+  if (tid == 0) *abort_flag = 0;
   if (stage) {
     if (tid == 0) mbar_init(hbar, 1);
     __syncthreads();
@@ -292,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
       const float2* Ha = a.H + (size_t)j * kPlane;
       const float2* Hb = two ? Ha + kPlane : Ha;
       if (stage) {
-        mbar_wait(hbar, huse & 1u);
+        mbar_wait(hbar, huse & 1u, a.sp.status, abort_flag);
         ++huse;
       }
       FFTF_MARK(0, 7);
@@ -317,6 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
         }
       }
       __syncthreads();
+      if (stage && *abort_flag) {        // uniform: set before the barrier above
+        mbar_drain(hbar, huse, hiss);
+        return;
+      }
       if (stage) {                       // the next round's spectra land during this round
         const int nj = (j + 2 < pairs) ? j + 2 : (t + 1 < g.d ? 0 : -1);
         if (nj >= 0) issue_h(nj);
@@ -430,6 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   const int FF = g.Fh * g.Fw;
   // staging barriers: [0] saved planes, [1] filter-pair spectrum, [2] field spectrum
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem4);
+  volatile int* abort_flag = reinterpret_cast<int*>(smem4) + 6;   // after the three barriers
   float2* stw = reinterpret_cast<float2*>(smem4 + 2);
   float2* X = stw + kN;
   float2* Wp = X + kPlane;
@@ -452,6 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   for (int i = tid; i < (int)(M * g.K); i += nt) dg[i] = 0.f;
   if (a.gring)
     for (int i = tid; i < FF; i += nt) ring[i] = 0.f;
+  if (tid == 0) *abort_flag = 0;
   if (stage && tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
@@ -462,8 +480,9 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   // spectrum H_j -> Hs (stored in the on-chip layout, four bulk copies).  Warp 0, after a barrier that ends the
   // previous readers of the buffer.  Spectra are staged only for steps t > 0 (the field
   // adjoint); step 0 needs none.
-  unsigned zuse = 0, huse = 0;
+  unsigned zuse = 0, huse = 0, ziss = 0, hiss = 0;
   auto issue_z = [&](int t_, int j_) {
+    ++ziss;
     if (tid < 32) {
       const unsigned bytes = (unsigned)(2 * P * sizeof(float));
       if (tid == 0) mbar_expect_tx(&bars[0], bytes);
@@ -476,6 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
     }
   };
   auto issue_h = [&](int j_) {
+    ++hiss;
     if (tid < 32) {
       if (tid == 0) mbar_expect_tx(&bars[1], kPlaneBytes);
       __syncwarp();
@@ -489,8 +509,9 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   // the forward's field spectrum of step t_ -> X (four bulk copies); X is free from the
   // last column pass of the step before (the field adjoint uses D)
   const bool xstage = stage && a.xspec != nullptr;
-  unsigned xuse = 0;
+  unsigned xuse = 0, xiss = 0;
   auto issue_x = [&](int t_) {
+    ++xiss;
     if (tid < 32) {
       if (tid == 0) mbar_expect_tx(&bars[2], kPlaneBytes);
       __syncwarp();
@@ -500,6 +521,11 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
                  reinterpret_cast<const char*>(a.xspec + ((size_t)b * g.d + t_) * kPlane) + tid * kPlaneChunk,
                  kPlaneChunk, &bars[2]);
     }
+  };
+  auto drain = [&]() {
+    mbar_drain(&bars[0], zuse, ziss);
+    mbar_drain(&bars[1], huse, hiss);
+    mbar_drain(&bars[2], xuse, xiss);
   };
   if (stage) {
     issue_z(g.d - 1, 0);
@@ -555,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   for (int t = g.d - 1; t >= 0; --t) {
     const bool last = (t == g.d - 1);
     if (xstage) {
-      mbar_wait(&bars[2], xuse & 1u);
+      mbar_wait(&bars[2], xuse & 1u, a.sp.status, abort_flag);
       ++xuse;
     } else {
       const float* xs = t > 0 ? a.xsave + ((size_t)b * (g.d - 1) + (t - 1)) * P : nullptr;
@@ -575,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
       const float* z1 = ZH + (size_t)m1 * P;
       const float* z2 = ZH + (size_t)m2 * P;
       if (stage) {
-        mbar_wait(&bars[0], zuse & 1u);
+        mbar_wait(&bars[0], zuse & 1u, a.sp.status, abort_flag);
         ++zuse;
         z1 = zs;
         z2 = zs + P;
@@ -636,6 +662,10 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
         Wp[at2(i >> 6, i & (kN - 1))] = v[k];
       }
       __syncthreads();
+      if (stage && *abort_flag) {        // uniform: set before the barrier above
+        drain();
+        return;
+      }
       if (stage) {                       // the next pair's planes land during this pair
         if (j + 1 < pairs) issue_z(t, j + 1);
         else if (t > 0) issue_z(t - 1, 0);
@@ -647,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
       FFTF_MARK(1, 4);
       const float2* H = a.H + (size_t)j * kPlane;
       if (stage && t > 0) {
-        mbar_wait(&bars[1], huse & 1u);
+        mbar_wait(&bars[1], huse & 1u, a.sp.status, abort_flag);
         ++huse;
       }
       FFTF_MARK(1, 10);
@@ -669,6 +699,10 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
         for (int n = 0; n < 8; ++n) Wp[at2(Ln.j + 8 * n, Ln.col)] = q[n];
       }
       __syncthreads();
+      if (stage && *abort_flag) {
+        drain();
+        return;
+      }
       if (stage) {                       // the next spectrum lands during this pair
         if (t > 0 && j + 1 < pairs) issue_h(j + 1);
         else if (j + 1 == pairs && t > 1) issue_h(0);
@@ -776,6 +810,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_prestep_spectra_kernel(
   __shared__ float2 plane[kPlane];
   __shared__ float2 stw[kN];
   const int pairs = g.M / 2;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && sp.status) *sp.status = 0;   // a new forward call starts
   if ((int)blockIdx.x < pairs) {
     pair_spectra_cta(g, filters, H, blockIdx.x, plane, stw);
     return;
@@ -849,16 +884,6 @@ nc_status fftf_backward(const FftfArgs& args, cudaStream_t st) {
   void* kargs[] = {&a};
   NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(a.batch), dim3(kThreads), kargs, smem, st));
   return launched("fftf_bwd_kernel launch");
-}
-
-int fftf_device_error(bool clear) {
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_fftf_error, sizeof(int)) != cudaSuccess) return -1;
-  if (clear && v) {
-    const int zero = 0;
-    if (cudaMemcpyToSymbol(g_fftf_error, &zero, sizeof(int)) != cudaSuccess) return -1;
-  }
-  return v;
 }
 
 }  // namespace nc

@@ -40,9 +40,6 @@ bool fftf_fits(const Geo& g);
 // Dynamic shared memory of the kernels; `stage` adds the bulk-copy staging buffers.
 size_t fftf_fwd_smem(const Geo& g, bool stage);
 size_t fftf_bwd_smem(const Geo& g, bool ring, bool stage);
-// Sticky error word of the current device: 1 when a bounded wait of the fused kernels for
-// their own bulk copies gave up (that call's results are invalid).  Synchronous.
-int fftf_device_error(bool clear);
 // One launch: the pre-step fusion (step parameters, gated filters) and H_j (the filter-pair
 // spectra, gated from `filters` directly).
 nc_status fftf_prestep_spectra(const Geo& g, const StepParams& sp, const float* cell, const float* filters,

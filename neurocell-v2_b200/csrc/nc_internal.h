@@ -47,6 +47,8 @@ PlanLayout plan_layout(const nc_topo* t);
 
 // Offsets (bytes) of the workspace sections; 0-sized sections have offset SIZE_MAX.
 struct WsLayout {
+  // status word of the call (always at offset 0; nc_workspace_status)
+  size_t status;
   // step parameters (pre-step fusion output)
   size_t weff, seff, broi, border, sprob, dsprob, wpinned, geff;
   // universe mode: last-step ROI cells (B, P), their gradient (B, P), ring gradient (H*W)

@@ -16,6 +16,8 @@ struct StepParams {           // pre-step fusion output (neurocell/params.py:104
   float* dsprob;              // (H*W) d s_prob / d S_raw (surrogate)
   float* wpinned;             // (H*W) W with the output port pinned to 1
   float* geff;                // (M*K) filters (sigmoid-gated when requested)
+  int* status;                // workspace status word: cleared by the forward's pre-step
+                              // kernel, set to 1 when a kernel's bounded wait gives up
 };
 
 struct FwdArgs {

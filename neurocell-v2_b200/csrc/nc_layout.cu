@@ -118,6 +118,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
   WsLayout L;
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t r = o; o = align256(o + (bytes ? bytes : 1)); return r; };
+  L.status = take(sizeof(int));   // offset 0 in every layout
   L.weff = take(fl * P);
   L.seff = take(fl * P);
   L.broi = take(fl * P);

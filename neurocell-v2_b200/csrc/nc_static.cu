@@ -11,6 +11,7 @@
 // exits.
 #include <mutex>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "nc_errors.h"
@@ -26,20 +27,48 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mutex;
+// Per device: the context the address was resolved in, and the address.  A context that
+// was destroyed and created again (cudaDeviceReset) loads the module again, possibly at
+// another address, so a new context resolves again.
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 void* g_scratch_addr[kMaxDevices] = {};
 
-// Once per device, with that device current: resolve the array's device address.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// The current context through the runtime's driver entry point (no link against libcuda).
+nc_status current_context(CUcontext* ctx) {
+  static CtxGetCurrentFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetDriverEntryPointByVersion(cuCtxGetCurrent)");
+    if (q != cudaDriverEntryPointSuccess || !p)
+      return set_error(NC_ERR_CUDA, "cuCtxGetCurrent is not available from the driver");
+    fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  *ctx = nullptr;
+  if (fn(ctx) != CUDA_SUCCESS) return set_error(NC_ERR_CUDA, "cuCtxGetCurrent failed");
+  return NC_OK;   // null when the runtime has not made a context current yet
+}
+
+// Once per device and context, with that device current: resolve the array's device address.
 nc_status static_scratch_address(void** out) {
   int dev = -1;
   NC_CUDA_CHECK(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return set_error(NC_ERR_UNSUPPORTED, "device ordinal %d too large", dev);
+  CUcontext ctx = nullptr;
+  NC_CHECK(current_context(&ctx));
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!g_scratch_addr[dev]) {
+  if (!ctx || !g_scratch_addr[dev] || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
+    // also makes the device's primary context current when no call has done so yet
     cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(static scratch)");
     if (!p) return set_error(NC_ERR_CUDA, "cudaGetSymbolAddress returned a null address");
+    NC_CHECK(current_context(&ctx));
     g_scratch_addr[dev] = p;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_addr[dev];
   return NC_OK;

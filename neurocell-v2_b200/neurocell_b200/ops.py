@@ -242,6 +242,7 @@ class _VNNPropagate(torch.autograd.Function):
                                       _ptr(filters), _ptr(flat_inputs), B, ctypes.byref(codd),
                                       flags, _ptr(out), _ptr(ws), ws_bytes, _stream(dev)),
                    "nc_vnn_forward")
+        _after_call(ws, "nc_vnn_forward")
         if train:
             ctx.save_for_backward(cell_params, filters, flat_inputs)
             ctx.ws, ctx.ws_bytes, ctx.plan, ctx.codd = ws, ws_bytes, plan, codd
@@ -261,6 +262,7 @@ class _VNNPropagate(torch.autograd.Function):
                                        ctypes.byref(ctx.codd), _ptr(g_out), _ptr(g_cell),
                                        _ptr(g_filt), _ptr(ctx.ws), ctx.ws_bytes, _stream(dev)),
                    "nc_vnn_backward")
+        _after_call(ctx.ws, "nc_vnn_backward")
         ctx.ws = None
         return g_cell, g_filt, None, None, None, None
 
@@ -284,6 +286,7 @@ class _VNNPropagateUniverse(torch.autograd.Function):
                                                _ptr(filters), _ptr(flat_inputs), B, ctypes.byref(codd),
                                                flags, _ptr(out), _ptr(uni), _ptr(ws), ws_bytes,
                                                _stream(dev)), "nc_vnn_forward_universe")
+        _after_call(ws, "nc_vnn_forward_universe")
         if train:
             ctx.save_for_backward(cell_params, filters, flat_inputs)
             ctx.ws, ctx.ws_bytes, ctx.plan, ctx.codd = ws, ws_bytes, plan, codd
@@ -307,6 +310,7 @@ class _VNNPropagateUniverse(torch.autograd.Function):
                                                 _ptr(g_out), _ptr(g_uni), _ptr(g_cell), _ptr(g_filt),
                                                 _ptr(ctx.ws), ctx.ws_bytes, _stream(dev)),
                    "nc_vnn_backward_universe")
+        _after_call(ctx.ws, "nc_vnn_backward_universe")
         ctx.ws = None
         return g_cell, g_filt, None, None, None, None
 
@@ -385,10 +389,31 @@ def propagate(cell_params: torch.Tensor, filters: torch.Tensor, flat_inputs: tor
     return _VNNPropagate.apply(cp, fl, xi, plan, _codd(codd_mode, tau, thr), train)
 
 
-def device_error(clear: bool = True) -> int:
-    """Sticky device error word of the current device (nc_device_error): 0 ok, 1 when a
-    kernel's bounded wait for its own asynchronous copies gave up.  Synchronous."""
-    return int(_lib.load().nc_device_error(1 if clear else 0))
+def workspace_status(ws: torch.Tensor) -> int:
+    """Status word of a workspace (nc_workspace_status): 0 ok, 1 when a kernel of the latest
+    forward on ``ws`` (or a backward after it) gave up a bounded wait for its own
+    asynchronous copies, so that call's results are invalid.  Synchronises the stream."""
+    out = ctypes.c_int32(-1)
+    _lib.check(_lib.load().nc_workspace_status(_ptr(ws), ctypes.byref(out), _stream(ws.device)),
+               "nc_workspace_status")
+    return int(out.value)
+
+
+# When True, every forward and backward of the autograd operators reads its workspace's
+# status word afterwards and raises if a bounded wait gave up (synchronises; for tests and
+# health checks).  STATUS_CHECKS counts the reads.
+CHECK_WAIT_STATUS = False
+STATUS_CHECKS = 0
+
+
+def _after_call(ws: torch.Tensor, what: str) -> None:
+    global STATUS_CHECKS
+    if not CHECK_WAIT_STATUS:
+        return
+    STATUS_CHECKS += 1
+    if workspace_status(ws) != 0:
+        raise RuntimeError(f"neurocell_b200: {what}: a kernel's bounded wait for its own copies "
+                           "gave up; the results of this call are invalid")
 
 
 def codd_states(s_raw: torch.Tensor, io_state_mask, hard_pin_io, codd_mode, tau, thr) -> torch.Tensor:

@@ -80,12 +80,14 @@ class NVLinkExchange:
 
     Each rank allocates a double-buffered receive buffer (one slot per rank), the ranks swap
     CUDA IPC handles with one ``all_gather_object`` and map each other's buffers.  Every step
-    each rank's kernel stores its gradient into every peer's buffer and raises flags there,
-    waits (bounded by ``max_wait_iters`` polls of its own flags) for the same slices of all
-    peers, sums them in rank order from local memory (bitwise the same on every rank) and
-    applies ``params -= lr / world * sum``.  One process per GPU; ranks on one GPU are rejected,
-    because kernels that wait on one another cannot share a device.  ``close()`` unmaps and
-    frees the buffers (collective: every rank calls it).
+    each rank's kernel stores its gradient into every peer's buffer, each value in one 64-bit
+    element together with the step number, waits (bounded by ``max_wait_iters`` polls of its
+    own buffer) until the same slices of all peers carry this step's tag, sums them in rank
+    order from local memory (bitwise the same on every rank) and applies
+    ``params -= lr / world * sum``.  One process per GPU; ranks on one GPU are rejected,
+    because kernels that wait on one another cannot share a device.  A timeout is terminal
+    (``status()`` reads 1 and later exchanges do nothing) until every rank calls ``reset()``.
+    ``close()`` unmaps and frees the buffers (collective: every rank calls it).
     """
 
     def __init__(self, n: int, process_group, device, max_wait_iters: int = 1 << 24):
@@ -145,14 +147,31 @@ class NVLinkExchange:
                         "nc_dp_allreduce_sgd")
 
     def status(self) -> int:
-        """0 = every exchange so far completed; 1 = a peer timed out (parameters of that step
-        were not updated, the ranks are out of step: treat as fatal).  Synchronises."""
+        """0 = every exchange so far completed; 1 = a peer timed out.  Slices whose peers had
+        arrived in that step were updated and the others were not, so the ranks' parameters
+        no longer agree; later exchanges do nothing until ``reset()``.  Synchronises."""
         c = self.ctypes
         out = c.c_int32(-1)
         self._lib.check(self.lib.nc_dp_status(self.state, c.byref(out),
                                               c.c_void_p(torch.cuda.current_stream(self.device)
                                                          .cuda_stream)), "nc_dp_status")
         return int(out.value)
+
+    def reset(self) -> None:
+        """Clears the step counters, the status word and this rank's receive buffer, then
+        passes a barrier of the process group (collective: every rank calls it, with no
+        exchange in flight).  Restore consistent parameters before the next step."""
+        if self.closed:
+            raise RuntimeError("NVLinkExchange is closed")
+        import torch.distributed as dist
+        c = self.ctypes
+        torch.cuda.synchronize(self.device)
+        self._lib.check(self.lib.nc_dp_reset(self.state, self.shared,
+                                             self.lib.nc_dp_shared_bytes(self.n, self.world),
+                                             c.c_void_p(torch.cuda.current_stream(self.device)
+                                                        .cuda_stream)), "nc_dp_reset")
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.pg)
 
     def close(self) -> None:
         if self.closed:

@@ -31,7 +31,7 @@ def test_reference_arm_line():
     assert d["impl"] == "reference" and d["metric"] == bench.METRIC and d["unit"] == "samples/s"
     assert d["steps"] == 1 and d["warmup"] == 3 and d["n_gpus"] == 1 and d["higher_is_better"] is True
     assert d["value"] > 0 and d["ms_per_step"] > 0
-    assert d["config"]["workload"] == bench.WORKLOAD_FIELDS["workload"]
+    assert d["config"] == bench.workload_config(1)     # the B200 arm's config, key for key
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
     e2e = d["e2e"]

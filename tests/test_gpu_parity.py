@@ -14,6 +14,15 @@ from oracle import vnn_oracle as O
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-5
+
+
+@pytest.fixture(autouse=True)
+def _check_wait_status():
+    """Every library call of these tests reads its workspace's status word afterwards and
+    fails if a kernel's bounded wait for its own bulk copies gave up."""
+    nc.ops.CHECK_WAIT_STATUS = True
+    yield
+    nc.ops.CHECK_WAIT_STATUS = False
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 ACT = {None: None, "tanh": torch.tanh, "sigmoid": torch.sigmoid, "relu": torch.relu,
        "leaky_relu": "leaky_relu", "gelu": "gelu", "identity": "identity"}
@@ -547,11 +556,33 @@ def test_adaptive_sub_roi_universe_outputs_outside_window(backend, mode, final):
                            backend, 172)
 
 
-def test_zz_no_bounded_wait_gave_up():
-    """Runs after the parity tests of this module: no kernel's bounded wait for its own
-    bulk copies into shared memory timed out (nc_device_error)."""
-    torch.cuda.synchronize()
-    assert nc.ops.device_error() == 0
+def test_zz_workspace_status_was_read():
+    """Runs after the parity tests of this module.  Their library calls had their workspace
+    status words read (a bounded wait that gave up would have failed them), and a forward
+    clears a status word that holds a stale value when it starts (nc_workspace_status)."""
+    import ctypes
+    from neurocell_b200 import _lib
+    assert nc.ops.STATUS_CHECKS > 0
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    geom, cfg, cell, filt, x, y = alu_problem(4, 5)
+    plan = nc.ops.get_plan(_nc_topo(geom), ((8, 1),) * 3, dev, "tanh", 0.0, "identity", 1.0,
+                           True, False, False)
+    B = 4
+    ws_bytes = lib.nc_workspace_bytes(ctypes.byref(plan.topo), B, 0)
+    ws = torch.full((ws_bytes,), 0xFF, dtype=torch.uint8, device=dev)   # stale word: -1
+    assert nc.ops.workspace_status(ws) == -1
+    out = torch.empty((B, plan.n_out), device=dev)
+    xs = torch.tensor(x.reshape(B, -1), device=dev)
+    c = torch.tensor(cell, device=dev)
+    f = torch.tensor(filt, device=dev)
+    st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(lib.nc_vnn_forward(ctypes.byref(plan.topo), ctypes.c_void_p(plan.buf.data_ptr()),
+                                  ctypes.c_void_p(c.data_ptr()), ctypes.c_void_p(f.data_ptr()),
+                                  ctypes.c_void_p(xs.data_ptr()), B, ctypes.byref(nc.ops._codd("continuous", 1.0, 0.6)),
+                                  0, ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                  ws_bytes, st), "nc_vnn_forward")
+    assert nc.ops.workspace_status(ws) == 0
 
 
 # ---- two-stage line transforms of the FFT regime (N = 64 R: 128 .. 1024) ----------------

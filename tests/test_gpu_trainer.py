@@ -195,39 +195,109 @@ def test_graph_step_follows_the_annealed_temperature():
     assert not torch.equal(fixed.flat, eager.flat)
 
 
-def test_exchange_timeout_sets_status_and_skips_the_update():
-    """Failure detection without a GPU fault: rank 0 of a two-rank exchange whose peer never
-    arrives (the peer's receive buffer is a plain buffer on this GPU that nothing writes
-    into rank 0's slots).  The bounded wait runs out, the status word reads 1 and the
-    parameters are left as they were."""
+def _dp_call(lib, peers, world, rank, state, g, p, n, lr, max_wait, dev):
+    import ctypes
+    from neurocell_b200 import _lib
+    st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(lib.nc_dp_allreduce_sgd(peers, world, rank, ctypes.c_void_p(state.data_ptr()),
+                                       ctypes.c_void_p(g.data_ptr()), ctypes.c_void_p(p.data_ptr()),
+                                       n, lr, max_wait, st), "nc_dp_allreduce_sgd")
+    status = ctypes.c_int32(-1)
+    _lib.check(lib.nc_dp_status(ctypes.c_void_p(state.data_ptr()), ctypes.byref(status), st),
+               "nc_dp_status")
+    return status.value
+
+
+def _tagged(values: np.ndarray, step: int) -> torch.Tensor:
+    """Elements of the receive buffer: (step << 32) | float bits, as int64."""
+    bits = values.astype(np.float32).view(np.uint32).astype(np.uint64)
+    return torch.tensor(((np.uint64(step) << np.uint64(32)) | bits).view(np.int64))
+
+
+def test_exchange_timeout_is_terminal_until_reset():
+    """Failure detection without a GPU fault.  Rank 0 of a two-rank exchange whose peer is
+    a plain buffer on this GPU: rank 0's own receive buffer is pre-filled from the host with
+    the peer's step-1 values for the first half of the slices only.  Blocks whose slices
+    arrived sum and update them; the others time out, leave their slices untouched and set
+    the status word.  The status is terminal: a second call changes nothing.  After
+    nc_dp_reset and a complete pre-fill the exchange completes again."""
     import ctypes
     from neurocell_b200 import _lib
     lib = _lib.load()
     dev = torch.device("cuda:0")
-    n, world = 1000, 2
-    bufs = [ctypes.c_void_p() for _ in range(3)]
-    sizes = [lib.nc_dp_shared_bytes(n, world), lib.nc_dp_shared_bytes(n, world), lib.nc_dp_state_bytes()]
-    with torch.cuda.device(dev):
-        for b, sz in zip(bufs, sizes):
-            _lib.check(lib.nc_dp_alloc(sz, ctypes.byref(b)), "nc_dp_alloc")
-        try:
-            peers = (ctypes.c_void_p * world)(bufs[0], bufs[1])
-            g = torch.randn(n, device=dev)
-            p = torch.randn(n, device=dev)
-            p0 = p.clone()
-            st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-            _lib.check(lib.nc_dp_allreduce_sgd(peers, world, 0, bufs[2], ctypes.c_void_p(g.data_ptr()),
-                                               ctypes.c_void_p(p.data_ptr()), n, 0.1, 2000, st),
-                       "nc_dp_allreduce_sgd")
-            status = ctypes.c_int32(-1)
-            _lib.check(lib.nc_dp_status(bufs[2], ctypes.byref(status), st), "nc_dp_status")
-            torch.cuda.synchronize()
-            assert status.value == 1
-            assert torch.equal(p, p0)
-        finally:
-            torch.cuda.synchronize()
-            for b in bufs:
-                lib.nc_dp_free(b)
+    n, world, lr = 1000, 2, 0.1
+    L = (n + 1) // 2                       # 16-byte lines of two elements
+    blocks = 32
+    slice_lines = -(-L // blocks)
+    good_lines = 16 * slice_lines          # blocks 0..15 see their peer's values
+    shared_bytes = lib.nc_dp_shared_bytes(n, world)
+    assert shared_bytes >= 2 * world * L * 16
+    own = torch.zeros(shared_bytes // 8, dtype=torch.int64, device=dev)
+    peer = torch.zeros(shared_bytes // 8, dtype=torch.int64, device=dev)
+    state = torch.zeros(lib.nc_dp_state_bytes() // 4, dtype=torch.int32, device=dev)
+    peers = (ctypes.c_void_p * world)(own.data_ptr(), peer.data_ptr())
+    rng = np.random.default_rng(3)
+    v = rng.normal(size=2 * L).astype(np.float32)          # the peer's gradient, 2 per line
+    slot = (1 * world + 1) * L * 2                         # (parity 1, source 1) in elements
+    own[slot:slot + 2 * good_lines] = _tagged(v[:2 * good_lines], 1).to(dev)
+    g = torch.tensor(rng.normal(size=n).astype(np.float32), device=dev)
+    p = torch.tensor(rng.normal(size=n).astype(np.float32), device=dev)
+    g0, p0 = g.clone(), p.clone()
+    assert _dp_call(lib, peers, world, 0, state, g, p, n, lr, 2000, dev) == 1
+    k = 2 * good_lines
+    vt = torch.tensor(v[:n], device=dev)
+    s = g0[:k] + vt[:k]
+    assert torch.equal(g[:k], s)
+    assert torch.equal(p[:k], p0[:k] - (lr / world) * s)
+    assert torch.equal(g[k:], g0[k:]) and torch.equal(p[k:], p0[k:])
+    # rank 0 pushed its own values with tag 1 into the peer's slot (parity 1, source 0)
+    pushed = peer[(1 * world + 0) * L * 2:(1 * world + 0) * L * 2 + n].cpu().numpy().view(np.uint64)
+    assert np.all((pushed >> np.uint64(32)) == 1)
+    # terminal: nothing moves, nothing is pushed
+    g1, p1 = g.clone(), p.clone()
+    peer.zero_()
+    own[slot:slot + 2 * L] = _tagged(v, 2).to(dev)
+    assert _dp_call(lib, peers, world, 0, state, g, p, n, lr, 2000, dev) == 1
+    assert torch.equal(g, g1) and torch.equal(p, p1) and int(peer.abs().sum()) == 0
+    # reset, complete pre-fill of step 1: the exchange completes
+    st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(lib.nc_dp_reset(ctypes.c_void_p(state.data_ptr()), ctypes.c_void_p(own.data_ptr()),
+                               shared_bytes, st), "nc_dp_reset")
+    assert int(own.abs().sum()) == 0 and int(state.abs().sum()) == 0
+    own[slot:slot + 2 * L] = _tagged(v, 1).to(dev)
+    g2, p2 = g.clone(), p.clone()
+    assert _dp_call(lib, peers, world, 0, state, g, p, n, lr, 2000, dev) == 0
+    s = g2 + vt
+    assert torch.equal(g, s) and torch.equal(p, p2 - (lr / world) * s)
+    torch.cuda.synchronize()
+
+
+def test_exchange_ignores_stale_step_tags():
+    """A value whose tag is from an older step (the other parity's leftovers, or the same
+    slot two steps back) is never summed: the block waits for the current tag."""
+    import ctypes
+    from neurocell_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    n, world, lr = 64, 2, 0.5
+    L = (n + 1) // 2
+    shared_bytes = lib.nc_dp_shared_bytes(n, world)
+    own = torch.zeros(shared_bytes // 8, dtype=torch.int64, device=dev)
+    peer = torch.zeros(shared_bytes // 8, dtype=torch.int64, device=dev)
+    state = torch.zeros(lib.nc_dp_state_bytes() // 4, dtype=torch.int32, device=dev)
+    peers = (ctypes.c_void_p * world)(own.data_ptr(), peer.data_ptr())
+    v = np.arange(2 * L, dtype=np.float32)
+    slot1 = (1 * world + 1) * L * 2
+    slot0 = (0 * world + 1) * L * 2
+    own[slot1:slot1 + 2 * L] = _tagged(v, 1).to(dev)            # step 1 (parity 1)
+    g = torch.ones(n, device=dev)
+    p = torch.zeros(n, device=dev)
+    assert _dp_call(lib, peers, world, 0, state, g, p, n, lr, 4000, dev) == 0
+    # step 2 (parity 0) finds only a stale step-0 tag there: it must time out, not sum
+    own[slot0:slot0 + 2 * L] = _tagged(v + 100, 0).to(dev)
+    g3, p3 = g.clone(), p.clone()
+    assert _dp_call(lib, peers, world, 0, state, g, p, n, lr, 4000, dev) == 1
+    assert torch.equal(g, g3) and torch.equal(p, p3)
 
 
 def test_five_step_sgd_trajectory_matches_oracle():
