@@ -183,9 +183,35 @@ def alu_geometry(n=8, kernel_size=(23, 13), directions=16, depth=4, gap=5, ctrl_
 _GELU_C = math.sqrt(2.0 / math.pi)
 
 
+_PAR_MIN = 1 << 22          # elementwise work above this size is split over threads
+
+
+def _chunked(fn, x):
+    """fn applied elementwise to ``x`` in chunks on a thread pool (numpy ufuncs release the
+    GIL); the values are exactly fn(x)."""
+    x = np.asarray(x)
+    if x.size < _PAR_MIN:
+        return fn(x)
+    import concurrent.futures as cf
+    import os
+    flat = np.ascontiguousarray(x).reshape(-1)
+    out = np.empty_like(flat)
+    n = os.cpu_count() or 1
+    step = -(-flat.size // (4 * n))
+
+    def work(a):
+        out[a:a + step] = fn(flat[a:a + step])
+
+    with cf.ThreadPoolExecutor(max_workers=n) as ex:
+        list(ex.map(work, range(0, flat.size, step)))
+    return out.reshape(x.shape)
+
+
 def act_fwd(x, name, slope=0.01):
     if name in (None, "identity"):
         return x
+    if np.size(x) >= _PAR_MIN:
+        return _chunked(lambda v: act_fwd(v, name, slope), x)
     if name == "tanh":
         return np.tanh(x)
     if name == "sigmoid":
@@ -202,6 +228,8 @@ def act_fwd(x, name, slope=0.01):
 def act_deriv(x, name, slope=0.01):
     if name in (None, "identity"):
         return np.ones_like(x)
+    if np.size(x) >= _PAR_MIN:
+        return _chunked(lambda v: act_deriv(v, name, slope), x)
     if name == "tanh":
         y = np.tanh(x)
         return 1.0 - y * y
@@ -335,6 +363,24 @@ def _fft_size(n):
     return s
 
 
+try:                      # threaded transforms when scipy is present (same float64 results)
+    import os as _os
+    import scipy.fft as _sfft
+    _WORKERS = _os.cpu_count() or 1
+
+    def _rfft2(x, s):
+        return _sfft.rfft2(x, s=s, workers=_WORKERS)
+
+    def _irfft2(x, s):
+        return _sfft.irfft2(x, s=s, workers=_WORKERS)
+except ImportError:       # pragma: no cover
+    def _rfft2(x, s):
+        return np.fft.rfft2(x, s=s)
+
+    def _irfft2(x, s):
+        return np.fft.irfft2(x, s=s)
+
+
 def conv_valid(x, G, chunk=16, method=None):
     """VALID cross-correlation: ``x`` (B, h+kh-1, w+kw-1), ``G`` (M, kh, kw) -> (B, M, h, w)."""
     if (method or CONV_METHOD) == "fft":
@@ -355,11 +401,11 @@ def _conv_valid_fft(x, G):
     M, kh, kw = G.shape
     h, w = Hp - kh + 1, Wp - kw + 1
     N1, N2 = _fft_size(Hp), _fft_size(Wp)
-    X = np.fft.rfft2(x, s=(N1, N2))
-    Gh = np.conj(np.fft.rfft2(G, s=(N1, N2)))
+    X = _rfft2(x, (N1, N2))
+    Gh = np.conj(_rfft2(G, (N1, N2)))
     out = np.empty((B, M, h, w), dtype=np.result_type(x, G))
     for m in range(M):
-        out[:, m] = np.fft.irfft2(X * Gh[m][None], s=(N1, N2))[:, :h, :w]
+        out[:, m] = _irfft2(X * Gh[m][None], (N1, N2))[:, :h, :w]
     return out
 
 
@@ -367,16 +413,16 @@ def _conv_valid_bwd_fft(x, G, gz, need_dx):
     B, Hp, Wp = x.shape
     M, kh, kw = G.shape
     N1, N2 = _fft_size(Hp), _fft_size(Wp)
-    X = np.fft.rfft2(x, s=(N1, N2))
-    GZ = np.fft.rfft2(gz, s=(N1, N2))                 # (B, M, N1, N2//2+1)
+    X = _rfft2(x, (N1, N2))
+    GZ = _rfft2(gz, (N1, N2))                        # (B, M, N1, N2//2+1)
     # dG[u] = sum_i gz[i] x[i+u]  ->  irfft(sum_b X * conj(GZ))
     acc = np.einsum("bij,bmij->mij", X, np.conj(GZ))
-    dG = np.fft.irfft2(acc, s=(N1, N2))[:, :kh, :kw].astype(np.result_type(x, G))
+    dG = _irfft2(acc, (N1, N2))[:, :kh, :kw].astype(np.result_type(x, G))
     dx = None
     if need_dx:
         # dx[j] = sum_u G[u] gz[j-u]  ->  irfft(sum_m GZ * Ghat)
-        Gh = np.fft.rfft2(G, s=(N1, N2))
-        dx = np.fft.irfft2(np.einsum("bmij,mij->bij", GZ, Gh), s=(N1, N2))[:, :Hp, :Wp]
+        Gh = _rfft2(G, (N1, N2))
+        dx = _irfft2(np.einsum("bmij,mij->bij", GZ, Gh), (N1, N2))[:, :Hp, :Wp]
         dx = dx.astype(x.dtype)
     return dx, dG
 
@@ -499,9 +545,32 @@ def precompute(cell_params, geom, activate="tanh", act_slope=0.01, hard_pin_io=F
 # ----------------------------------------------------------------------------------------
 # Epilogues (epilogue.py:20-128)
 # ----------------------------------------------------------------------------------------
+def _by_planes(fn, *arrays):
+    """fn over chunks of the (B, M) planes of same-shaped (B, M, h, w) arrays on a thread
+    pool; returns the tuple of fn's outputs reassembled (each (B, M, ...))."""
+    import concurrent.futures as cf
+    import os
+    B, M = arrays[0].shape[:2]
+    flat = [np.ascontiguousarray(a).reshape((B * M,) + a.shape[2:]) for a in arrays]
+    n = os.cpu_count() or 1
+    step = max(1, -(-(B * M) // (2 * n)))
+    parts = [None] * len(range(0, B * M, step))
+
+    def work(i):
+        a = i * step
+        parts[i] = fn(*(f[a:a + step] for f in flat))
+
+    with cf.ThreadPoolExecutor(max_workers=n) as ex:
+        list(ex.map(work, range(len(parts))))
+    return tuple(np.concatenate([p[k] for p in parts]).reshape((B, M) + parts[0][k].shape[1:])
+                 for k in range(len(parts[0])))
+
+
 def _standardize(z, norm=True):
     if not norm:
         return z, None
+    if z.ndim == 4 and z.size >= _PAR_MIN:
+        return _by_planes(lambda v: _standardize(v, True), z)
     mean = z.mean(axis=(-2, -1), keepdims=True)
     var = ((z - mean) ** 2).mean(axis=(-2, -1), keepdims=True)
     rstd = 1.0 / np.sqrt(var + NORM_EPS)
@@ -511,6 +580,10 @@ def _standardize(z, norm=True):
 def _standardize_bwd(gzh, zh, rstd, norm=True):
     if not norm:
         return gzh
+    if zh.ndim == 4 and zh.size >= _PAR_MIN:
+        g = np.broadcast_to(gzh, zh.shape)
+        r = np.broadcast_to(rstd, zh.shape[:2] + (1, 1))
+        return _by_planes(lambda a, b, c: (_standardize_bwd(a, b, c, True),), g, zh, r)[0]
     c1 = gzh.mean(axis=(-2, -1), keepdims=True)
     c2 = (gzh * zh).mean(axis=(-2, -1), keepdims=True)
     return rstd * (gzh - c1 - zh * c2)
@@ -873,6 +946,31 @@ def train_step(cell_params, filters, inputs, targets, geom, cfg: Config = Config
 # ----------------------------------------------------------------------------------------
 # ALU data (datasets.py:77-130), seeded numpy stand-in
 # ----------------------------------------------------------------------------------------
+# ----------------------------------------------------------------------------------------
+# Packed 8-bit evaluation (trainer.py:49-54, 122-138)
+# ----------------------------------------------------------------------------------------
+BIT_WEIGHTS_U8 = np.array([128, 64, 32, 16, 8, 4, 2, 1], dtype=np.uint8)
+
+
+def packed_predictions(logits) -> np.ndarray:
+    """``packbits_u8_on_device(jnp.round(logits).astype(jnp.uint8))`` of the reference: each
+    rounded logit is cast to uint8 (XLA's float-to-integer conversion saturates: below 0
+    gives 0, above 255 gives 255), multiplied by its bit weight and summed in uint8, which
+    wraps modulo 256 -- so a rounded logit of 2 at bit weight 128 contributes 0, not a set
+    bit.  ``logits`` (B, 8) or (B, 8, 1) -> (B, 1) uint8."""
+    x = np.asarray(logits, dtype=np.float64)
+    if x.ndim == 3 and x.shape[-1] == 1:
+        x = x[..., 0]
+    u8 = np.clip(np.round(x), 0, 255).astype(np.uint8)
+    return ((u8.astype(np.int64) * BIT_WEIGHTS_U8.astype(np.int64)).sum(-1) % 256).astype(np.uint8)[:, None]
+
+
+def packed_accuracy(logits, packed_targets) -> float:
+    """Fraction of samples whose packed prediction equals the packed target byte."""
+    p = packed_predictions(logits)[:, 0]
+    return float((p == np.asarray(packed_targets).reshape(-1)).mean())
+
+
 def alu_truth_table(numbers, operands, controls):
     """The vectorised uint8 ALU table of datasets.py:97-116."""
     one = np.uint8(1)

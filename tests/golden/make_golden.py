@@ -39,8 +39,7 @@ def main(ref_root: str) -> None:
     out, _ = O.forward(cell, filt, x, geom, cfg)
     np.savez_compressed(os.path.join(HERE, "alu_trained_eval.npz"), inputs=x, targets=y,
                         packed=packed, out_f64=out)
-    pred = np.packbits(np.clip(np.round(out[:, :, 0]), 0, 255).astype(np.uint8), axis=1)[:, 0]
-    print("oracle packed accuracy on the fixture batch:", float((pred == packed).mean()))
+    print("oracle packed accuracy on the fixture batch:", O.packed_accuracy(out, packed))
 
 
 if __name__ == "__main__":
