@@ -177,6 +177,100 @@ __device__ __forceinline__ void block_sum4(float v[4], float* red, int& par) {
   par ^= 1;
 }
 
+// Chan's pairwise merge of (count, mean, centred sum of squares): the two-stage variance of
+// the reference's tiled epilogue (neurocell/kernels_pallas.py:740-837).
+__device__ __forceinline__ void chan_merge(float& n, float& mean, float& m2, float nb, float mb, float m2b) {
+  if (nb == 0.f) return;
+  if (n == 0.f) {
+    n = nb; mean = mb; m2 = m2b;
+    return;
+  }
+  const float nn = n + nb, delta = mb - mean, f = nb / nn;
+  mean = fmaf(delta, f, mean);
+  m2 += m2b + delta * delta * n * f;
+  n = nn;
+}
+
+// Inverse row pass of the ROI rows of two planes (re and im parts: four real planes) that
+// also leaves each row's centred statistics (mean, M2 over its `roi_w` columns) in
+// rowst[row * 4 + k], k = (Wp re, Wp im, Wq re, Wq im).  The 8 lanes of a row sum their
+// values with three xor shuffles, then sum the squared deviations from the row mean the
+// same way; the row values never leave registers for it.
+__device__ __forceinline__ void rows_inv_x2_stats(float2* s1, float2* s2, int nrows, int roi_w,
+                                                  const float2* tw64, const fft64::Lane& L, float2* rowst) {
+  const int line = L.row;
+  const bool active = line < nrows;
+  if (!__any_sync(0xffffffffu, active)) return;
+  float2 v[8], u[8];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    const int o = at2(line, L.j + 8 * n);
+    v[n] = active ? s1[o] : make_float2(0.f, 0.f);
+    u[n] = active ? s2[o] : make_float2(0.f, 0.f);
+  }
+  fft64::fft64_lanes<true>(v, L.j, tw64);
+  fft64::fft64_lanes<true>(u, L.j, tw64);
+  float sm[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    if (L.j + 8 * n < roi_w) {
+      sm[0] += v[n].x; sm[1] += v[n].y; sm[2] += u[n].x; sm[3] += u[n].y;
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) sm[k] += __shfl_xor_sync(0xffffffffu, sm[k], o);
+  const float inv_w = 1.0f / (float)roi_w;
+  float mu[4], q[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) mu[k] = sm[k] * inv_w;
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    if (L.j + 8 * n < roi_w) {
+      const float d0 = v[n].x - mu[0], d1 = v[n].y - mu[1], d2 = u[n].x - mu[2], d3 = u[n].y - mu[3];
+      q[0] = fmaf(d0, d0, q[0]); q[1] = fmaf(d1, d1, q[1]);
+      q[2] = fmaf(d2, d2, q[2]); q[3] = fmaf(d3, d3, q[3]);
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) q[k] += __shfl_xor_sync(0xffffffffu, q[k], o);
+  if (active) {
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int o = at2(line, L.j + 8 * n);
+      s1[o] = v[n];
+      s2[o] = u[n];
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)       // lane k of the row writes plane k (no indexed registers)
+      if (L.j == k) rowst[line * 4 + k] = make_float2(mu[k], q[k]);
+  }
+}
+
+// Plane statistics of the four real planes from the row statistics (after a barrier):
+// warp k < 4 merges the rows of plane k (lane l takes rows l, l + 32, ...), then the lanes
+// merge in a fixed butterfly; lane 0 writes (mean, 1 / sqrt(var + eps)) to st[k].
+__device__ __forceinline__ void merge_row_stats(const float2* rowst, int roi_h, int roi_w, float2* st) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (w >= 4) return;
+  float n = 0.f, mean = 0.f, m2 = 0.f;
+  for (int r = lane; r < roi_h; r += 32) {
+    const float2 rs = rowst[r * 4 + w];
+    chan_merge(n, mean, m2, (float)roi_w, rs.x, rs.y);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float nb = __shfl_xor_sync(0xffffffffu, n, o);
+    const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
+    const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
+    chan_merge(n, mean, m2, nb, mb, m2b);
+  }
+  if (lane == 0) st[w] = make_float2(mean, 1.0f / sqrtf(m2 / n + kNormEps));
+}
+
 // Field of step t into X (real part; zero imaginary, zero beyond Fh x Fw).
 //   src_interior(p): the ROI value; ring: VALID border template, SAME zero, CIRCULAR wrap.
 // Step 0 (src == nullptr): zeros, injected inputs, wrapped halo.
@@ -246,8 +340,9 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
   float2* Wq = Wp + kPlane;
   float2* Hs = Wq + kPlane;                               // staged spectra of one round
   const bool stage = a.stage != 0;
-  float* red = reinterpret_cast<float*>(Hs + (stage ? 2 * kPlane : 0));   // 160, 16-B aligned
-  float* lin = red + 160;
+  float2* rowst = Hs + (stage ? 2 * kPlane : 0);          // (64 rows, 4 planes) row statistics
+  float2* pst = rowst + 4 * kN;                           // 4 plane statistics (8 slots)
+  float* lin = reinterpret_cast<float*>(pst + 8);
   float* acc = lin + a.g.P;
   const Geo& g = a.g;
   const int tid = threadIdx.x, nt = blockDim.x, b = blockIdx.x;
@@ -281,7 +376,6 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
     __syncthreads();
     issue_h(0);
   }
-  int rpar = 0;                  // block_sum4 half
   FFTF_T0();
 
   for (int t = 0; t < g.d; ++t) {
@@ -338,40 +432,29 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
         if (nj >= 0) issue_h(nj);
       }
       FFTF_MARK(0, 2);
-      // inverse row passes of the ROI rows (warps beyond them skip)
-      fft64::pass64x2<false, true>(Wp, Wq, g.roi_h, stw, Ln);
+      // inverse row passes of the ROI rows (warps beyond them skip); with the spatial norm
+      // the pass also leaves every row's centred statistics, merged per plane below
+      if (g.norm) rows_inv_x2_stats(Wp, Wq, g.roi_h, g.roi_w, stw, Ln, rowst);
+      else fft64::pass64x2<false, true>(Wp, Wq, g.roi_h, stw, Ln);
       __syncthreads();
       FFTF_MARK(0, 3);
-      // statistics of planes 2j, 2j+1 (Wp re, im) and 2j+2, 2j+3 (Wq), centred two-pass;
-      // thread tid owns pixels p = tid + 512 k
+      // plane statistics of 2j, 2j+1 (Wp re, im) and 2j+2, 2j+3 (Wq): centred per row, merged
+      // over the rows with Chan's formula; thread tid owns pixels p = tid + 512 k
       float mu[4] = {0.f, 0.f, 0.f, 0.f}, rs[4] = {1.f, 1.f, 1.f, 1.f};
       if (g.norm) {
-        const float inv_n = 1.0f / (float)g.P;
+        merge_row_stats(rowst, g.roi_h, g.roi_w, pst);
+        __syncthreads();
 #pragma unroll
-        for (int k = 0; k < kPixPerThread; ++k) {
-          if (poff[k] < 0) continue;
-          const float2 w = Wp[poff[k]], u = Wq[poff[k]];
-          mu[0] += w.x; mu[1] += w.y; mu[2] += u.x; mu[3] += u.y;
+        for (int k = 0; k < 4; ++k) {
+          const float2 q = pst[k];
+          mu[k] = q.x;
+          rs[k] = q.y;
         }
-        block_sum4(mu, red, rpar);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) mu[k] *= inv_n;
-        float q[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k = 0; k < kPixPerThread; ++k) {
-          if (poff[k] < 0) continue;
-          const float2 w = Wp[poff[k]], u = Wq[poff[k]];
-          const float d0 = w.x - mu[0], d1 = w.y - mu[1], d2 = u.x - mu[2], d3 = u.y - mu[3];
-          q[0] = fmaf(d0, d0, q[0]); q[1] = fmaf(d1, d1, q[1]);
-          q[2] = fmaf(d2, d2, q[2]); q[3] = fmaf(d3, d3, q[3]);
-        }
-        block_sum4(q, red, rpar);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) rs[k] = 1.0f / sqrtf(q[k] * inv_n + kNormEps);
       }
       FFTF_MARK(0, 4);
       const int np = two ? 4 : 2;
-      if (a.train && tid < np) a.rstd[((size_t)b * g.d + t) * M + 2 * j + tid] = rs[tid];
+      if (a.train && tid < np)           // pst holds them when norm is on (no indexed registers)
+        a.rstd[((size_t)b * g.d + t) * M + 2 * j + tid] = g.norm ? pst[tid].y : 1.0f;
       float* zh = a.train ? a.zhat + (((size_t)b * g.d + t) * M + 2 * j) * P : nullptr;
 #pragma unroll
       for (int k = 0; k < kPixPerThread; ++k) {
@@ -396,7 +479,6 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
       FFTF_MARK(0, 5);
     }
     __syncthreads();
-
     if (last && a.uroi) {
       // universe mode: the last step's ROI cells (ROI epilogue with the final activation)
       for (int p = tid; p < g.P; p += nt) {
@@ -831,8 +913,8 @@ nc_status launched(const char* what) {
 }  // namespace
 
 size_t fftf_fwd_smem(const Geo& g, bool stage) {
-  return 16 + sizeof(float2) * (kN + (3 + (stage ? 2 : 0)) * (size_t)kPlane) +
-         sizeof(float) * (2 * (size_t)g.P + 160);
+  return 16 + sizeof(float2) * (kN + (3 + (stage ? 2 : 0)) * (size_t)kPlane + 4 * kN + 8) +
+         sizeof(float) * 2 * (size_t)g.P;
 }
 
 

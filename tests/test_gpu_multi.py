@@ -27,7 +27,7 @@ def _problem(B):
     return cell, filt, x.reshape(B, -1), y
 
 
-def _rank_main(rank, world, port, out_dir, exchange="nccl", graph=False):
+def _rank_main(rank, world, port, out_dir, exchange="nccl", graph=False, long_steps=0):
     import sys
     from datetime import timedelta
     import torch.distributed as dist
@@ -59,6 +59,14 @@ def _rank_main(rank, world, port, out_dir, exchange="nccl", graph=False):
                 st.step(xs, ys)
             torch.cuda.synchronize()
             np.save(os.path.join(out_dir, f"params4_{rank}.npy"), st.flat.cpu().numpy())
+        if long_steps:                  # many graph replays over four batches per rank
+            cellb, filtb, xb, yb = _problem(256)
+            xr = torch.tensor(xb.reshape(4, 2, 32, -1)[:, rank], device=dev)
+            yr = torch.tensor(yb.reshape(4, 2, 32, -1)[:, rank], device=dev)
+            for i in range(long_steps):
+                st.step(xr[i % 4], yr[i % 4])
+            torch.cuda.synchronize()
+            np.save(os.path.join(out_dir, f"params_long_{rank}.npy"), st.flat.cpu().numpy())
         np.save(os.path.join(out_dir, f"status{rank}.npy"), np.array([st.exchange_status()]))
         st.release()
         dist.barrier()
@@ -83,9 +91,9 @@ def _full_batch_reference(steps=1):
     return full_g, full_p, st.flat.cpu().numpy()
 
 
-def _run(tmp_path, exchange, graph=False):
+def _run(tmp_path, exchange, graph=False, long_steps=0):
     import torch.multiprocessing as mp
-    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path), exchange, graph),
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path), exchange, graph, long_steps),
                        nprocs=2, join=True, start_method="spawn")
 
 
@@ -117,3 +125,24 @@ def test_two_gpu_nvlink_exchange_matches_full_batch(tmp_path):
     q0, q1 = np.load(tmp_path / "params4_0.npy"), np.load(tmp_path / "params4_1.npy")
     assert np.array_equal(q0, q1)
     assert np.linalg.norm(q0 - full_p4) / np.linalg.norm(full_p4) <= 1e-5
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_nvlink_exchange_long_graph_replay(tmp_path):
+    """1,000 graph-captured steps with the NVLink exchange: both ranks end with bitwise
+    identical parameters, every exchange completed, and the trajectory matches the same
+    1,000 steps with NCCL's all-reduce to 1e-6."""
+    a, b = tmp_path / "nvlink", tmp_path / "nccl"
+    a.mkdir()
+    b.mkdir()
+    _run(a, "nvlink", graph=True, long_steps=1000)
+    _run(b, "nccl", graph=True, long_steps=1000)
+    p0, p1 = np.load(a / "params_long_0.npy"), np.load(a / "params_long_1.npy")
+    assert np.array_equal(p0, p1)
+    assert np.load(a / "status0.npy")[0] == 0 and np.load(a / "status1.npy")[0] == 0
+    q0, q1 = np.load(b / "params_long_0.npy"), np.load(b / "params_long_1.npy")
+    assert np.array_equal(q0, q1)
+    assert np.linalg.norm(p0 - q0) / np.linalg.norm(q0) <= 1e-6
+    start = _problem(64)
+    init = np.concatenate([start[0].reshape(-1), start[1].reshape(-1)])
+    assert np.linalg.norm(p0 - init) / np.linalg.norm(init) > 1e-3     # training moved them
