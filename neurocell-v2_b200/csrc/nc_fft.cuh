@@ -310,9 +310,10 @@ __device__ __forceinline__ void init_tw64(float2* tw64, int tid) {
 }  // namespace fft64
 
 // ---------------------------------------------------------------------------------------
-// Two-stage line transforms for N = 64 * R, R in {1, 2, 4, 8, 16} (64 <= N <= 1024): the
-// lines of the per-step FFT regime (nc_fftconv.cu) in two passes through shared memory
-// instead of log4(N) radix-4 passes.
+// Two-stage line transforms for N = 64 * R, R in {1, 2, 3, 4, 5, 6, 8, 16} (64 <= N <=
+// 1024): the lines of the per-step FFT regime (nc_fftconv.cu) in two passes through shared
+// memory instead of log4(N) radix-4 passes.  The radices 3, 5 and 6 let the planner pick a
+// line length close to the field (286 -> 320 instead of 512).
 //
 // With n = n2 + 64 n1 and f = k1 + R k2 (n2, k2 < 64; n1, k1 < R):
 //   X[k1 + R k2] = sum_n2 w64^(n2 k2) * ( wN^(n2 k1) * sum_n1 x[n2 + 64 n1] wR^(n1 k1) ).
@@ -328,7 +329,15 @@ __device__ __forceinline__ void init_tw64(float2* tw64, int tid) {
 // ---------------------------------------------------------------------------------------
 namespace fft {
 
-__host__ __device__ inline bool two_stage(int N) { return N >= 64 && N <= 1024; }
+// Radices of the first stage (a DFT below for each).  Radices 10 and 12 would need more
+// registers than the run-time-radix kernels of N = 1024 can give without spilling, so
+// lines of 513 ... 1023 points keep N = 1024.
+__host__ __device__ inline bool stage_a_radix(int R) {
+  return R == 1 || R == 2 || R == 3 || R == 4 || R == 5 || R == 6 || R == 8 || R == 16;
+}
+__host__ __device__ inline bool two_stage(int N) {
+  return N >= 64 && N <= 1024 && N % 64 == 0 && stage_a_radix(N / 64);
+}
 
 // Plan twiddle entries for an N-point line transform.
 __host__ __device__ inline int plan_twiddle_len(int N) {
@@ -337,8 +346,86 @@ __host__ __device__ inline int plan_twiddle_len(int N) {
 
 // y[k] = sum_n a[n] wR^(n k), wR = exp(-+2 pi i / R); natural order in and out.
 template <int R, bool INV>
+__device__ __forceinline__ void dft_r(float2* a);
+
+// cos and sin of 2 pi e / R for the composite radix 6 (exact values; e < R).
+template <int R>
+__device__ __forceinline__ float2 root_cs(int e) {
+  static_assert(R == 6, "composite radix 6");
+  constexpr float h3 = 0.86602540378443865f;                 // sqrt(3) / 2
+  constexpr float c[6] = {1.f, 0.5f, -0.5f, -1.f, -0.5f, 0.5f};
+  constexpr float s[6] = {0.f, h3, h3, 0.f, -h3, -h3};
+  return make_float2(c[e], s[e]);
+}
+
+// R = P * Q from a DFT-Q and a DFT-P (Cooley-Tukey): with n = n1 + P n2, k = k1 + Q k2,
+//   X[k1 + Q k2] = sum_n1 wP^(n1 k2) * ( wR^(n1 k1) * sum_n2 x[n1 + P n2] wQ^(n2 k1) ).
+template <int P, int Q, bool INV>
+__device__ __forceinline__ void dft_pq(float2* a) {
+  constexpr int R = P * Q;
+  float2 b[R];
+#pragma unroll
+  for (int n1 = 0; n1 < P; ++n1) {
+    float2 q[Q];
+#pragma unroll
+    for (int n2 = 0; n2 < Q; ++n2) q[n2] = a[n1 + P * n2];
+    dft_r<Q, INV>(q);
+#pragma unroll
+    for (int k1 = 0; k1 < Q; ++k1) {
+      float2 v = q[k1];
+      const int e = n1 * k1;
+      if (e != 0) {
+        const float2 cs = root_cs<R>(e);
+        v = cmul(v, make_float2(cs.x, INV ? cs.y : -cs.y));   // wR^e (conjugate inverse)
+      }
+      b[n1 * Q + k1] = v;
+    }
+  }
+#pragma unroll
+  for (int k1 = 0; k1 < Q; ++k1) {
+    float2 q[P];
+#pragma unroll
+    for (int n1 = 0; n1 < P; ++n1) q[n1] = b[n1 * Q + k1];
+    dft_r<P, INV>(q);
+#pragma unroll
+    for (int k2 = 0; k2 < P; ++k2) a[k1 + Q * k2] = q[k2];
+  }
+}
+
+template <int R, bool INV>
 __device__ __forceinline__ void dft_r(float2* a) {
-  if constexpr (R == 2) {
+  if constexpr (R == 3) {
+    // y1 = x0 + c t1 -/+ i s t2, y2 = x0 + c t1 +/- i s t2 with t1 = x1 + x2, t2 = x1 - x2,
+    // c = cos(2 pi / 3) = -1/2, s = sin(2 pi / 3) (upper signs forward)
+    constexpr float s3 = 0.86602540378443865f;
+    const float2 t1 = cadd(a[1], a[2]), t2 = csub(a[1], a[2]);
+    const float2 m = make_float2(fmaf(-0.5f, t1.x, a[0].x), fmaf(-0.5f, t1.y, a[0].y));
+    const float2 is = make_float2(-s3 * t2.y, s3 * t2.x);   // i s t2
+    a[0] = cadd(a[0], t1);
+    a[1] = INV ? cadd(m, is) : csub(m, is);
+    a[2] = INV ? csub(m, is) : cadd(m, is);
+  } else if constexpr (R == 5) {
+    // t1 = x1 + x4, t2 = x2 + x3, t3 = x1 - x4, t4 = x2 - x3; with c1, c2 = cos(2 pi / 5),
+    // cos(4 pi / 5) and s1, s2 = sin(2 pi / 5), sin(4 pi / 5):
+    //   y1, y4 = x0 + c1 t1 + c2 t2 -/+ i (s1 t3 + s2 t4)
+    //   y2, y3 = x0 + c2 t1 + c1 t2 -/+ i (s2 t3 - s1 t4)      (upper signs forward)
+    constexpr float c1 = 0.30901699437494742f, c2 = -0.80901699437494742f;
+    constexpr float s1 = 0.95105651629515357f, s2 = 0.58778525229247314f;
+    const float2 t1 = cadd(a[1], a[4]), t2 = cadd(a[2], a[3]);
+    const float2 t3 = csub(a[1], a[4]), t4 = csub(a[2], a[3]);
+    const float2 r1 = make_float2(fmaf(c2, t2.x, fmaf(c1, t1.x, a[0].x)), fmaf(c2, t2.y, fmaf(c1, t1.y, a[0].y)));
+    const float2 r2 = make_float2(fmaf(c1, t2.x, fmaf(c2, t1.x, a[0].x)), fmaf(c1, t2.y, fmaf(c2, t1.y, a[0].y)));
+    const float2 u1 = make_float2(fmaf(s2, t4.x, s1 * t3.x), fmaf(s2, t4.y, s1 * t3.y));
+    const float2 u2 = make_float2(fmaf(-s1, t4.x, s2 * t3.x), fmaf(-s1, t4.y, s2 * t3.y));
+    const float2 iu1 = make_float2(-u1.y, u1.x), iu2 = make_float2(-u2.y, u2.x);   // i u
+    a[0] = cadd(a[0], cadd(t1, t2));
+    a[1] = INV ? cadd(r1, iu1) : csub(r1, iu1);
+    a[4] = INV ? csub(r1, iu1) : cadd(r1, iu1);
+    a[2] = INV ? cadd(r2, iu2) : csub(r2, iu2);
+    a[3] = INV ? csub(r2, iu2) : cadd(r2, iu2);
+  } else if constexpr (R == 6) {
+    dft_pq<2, 3, INV>(a);
+  } else if constexpr (R == 2) {
     const float2 t = a[1];
     a[1] = csub(a[0], t);
     a[0] = cadd(a[0], t);
@@ -436,6 +523,9 @@ __device__ __forceinline__ void stage_b(float2* s, int L, int R, int LS, const f
   }
 }
 
+// Shared-memory two-stage plan for R in {1, 2, 4, 8, 16}.  The kernels run it only for
+// N = 64 (R = 1); longer lines take the global-stage variants below (fwd_a_global /
+// inv_a_global), which also serve R = 3, 5 and 6.
 template <bool INV>
 __device__ void transform_lines_2s(float2* s, int L, int N, const float2* tw, int tid, int nt) {
   const int R = N >> 6, LS = line_stride(N);
@@ -551,7 +641,9 @@ __device__ __forceinline__ void inv_a_global(float2* s, int L, int lgL, int LS, 
 // Whether the global-stage variants apply: two-stage plans with a radix-R stage.
 __host__ __device__ inline bool a_global(int N) { return two_stage(N) && N > 64; }
 
-// Runtime R = N / 64 dispatch (N in {128, 256, 512, 1024}).
+// Runtime R = N / 64 dispatch for the run-time-radix kernels (N = 1024 in practice; radices
+// 3, 5 and 6 have specialised kernels, and leaving them out here keeps the register use of
+// these kernels down).
 template <bool LFAST, class Ld>
 __device__ __forceinline__ void fwd_a_global_plan(float2* s, int L, int lgL, int LS, int N, const float2* tw,
                                                   int tid, int nt, Ld ld) {

@@ -70,6 +70,24 @@ __device__ __forceinline__ float plane_in(const Planes& a, int b, int m, size_t 
 
 __device__ __forceinline__ int even_up(int x) { return (x + 1) & ~1; }
 
+// Line l and element e of a flat index over lines of N elements: N = 64 RA is a compile-time
+// constant when RA > 0; otherwise shifts for a power of two, a division for the rest.
+template <int RA>
+__device__ __forceinline__ void line_elem(int idx, int N, int lgN, int& l, int& e) {
+  if constexpr (RA > 0) {
+    l = idx / (64 * RA);
+    e = idx - l * (64 * RA);
+  } else {
+    if ((N & (N - 1)) == 0) {
+      l = idx >> lgN;
+      e = idx & (N - 1);
+    } else {
+      l = idx / N;
+      e = idx - l * N;
+    }
+  }
+}
+
 // Variants of the transform kernels: RA = N / 64 (2, 4, 8) specialises the radix-R stage that
 // runs on global memory; RA = -1 chooses at run time between that stage (any R) and the
 // shared-memory plan (used for N = 1024: measured faster than the radix-16
@@ -113,7 +131,8 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_fwd_kernel(Pla
   } else {
 #pragma unroll 4
     for (int idx = tid; idx < nl * N; idx += nt) {
-      const int l = idx >> lgN, e = idx & (N - 1);
+      int l, e;
+      line_elem<RA>(idx, N, lgN, l, e);
       const int line = line0 + l;
       const int u = line / a.rows, r = line - u * a.rows;
       const int gs = u / a.ms, m = u - gs * a.ms;
@@ -130,7 +149,8 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_fwd_kernel(Pla
   }
 #pragma unroll 4
   for (int idx = tid; idx < nl * N; idx += nt) {
-    const int l = idx >> lgN, e = idx & (N - 1);
+    int l, e;
+    line_elem<RA>(idx, N, lgN, l, e);
     __stcs(&dst[(size_t)(line0 + l) * N + e], s[l * LS + pidx(e)]);   // read once
   }
 }
@@ -154,7 +174,8 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_inv_kernel(con
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
 #pragma unroll 4
   for (int idx = tid; idx < nl * N; idx += nt) {
-    const int l = idx >> lgN, e = idx & (N - 1);
+    int l, e;
+    line_elem<RA>(idx, N, lgN, l, e);
     s[l * LS + pidx(e)] = __ldcs(&src[(size_t)(line0 + l) * N + e]);   // last use
   }
   if (RA > 0 || (RA < 0 && fft::a_global(N))) {
@@ -355,8 +376,8 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA, MODE == 2)) cols_ker
 // acc[m][f] (+)= sum over pairs of x^[p][f] * conj(q^[p][m][f])  (fixed pair order).  A
 // thread takes two adjacent frequencies (16-byte accesses) of kDgM directions
 // (blockIdx.y), so x^ is read once per kDgM directions and the kDgM q^ loads of a pair are
-// independent.  NN is even (the planner's FFT sides are powers of two, at least 2) and the
-// spectra are 16-byte aligned.
+// independent.  NN is even (the planner's FFT sides are even: powers of two or multiples of
+// 64) and the spectra are 16-byte aligned.
 // dg_accum picks kDgM per grid size so that small grids still fill the GPU.
 template <int kDgM>
 __global__ void dg_accum_kernel(const float2* __restrict__ xhat, const float2* __restrict__ q,
@@ -908,10 +929,12 @@ nc_status smem_attr(const void* fn, size_t bytes) {
   return NC_OK;
 }
 
-// RA of the transform kernels for N-point lines (see fft_ctas).
+// RA of the transform kernels for N-point lines (see fft_ctas): a specialisation for
+// N = 128 ... 512, the run-time variant for 1024.
 int kernel_ra(int N) {
   if (!fft::a_global(N)) return 0;
-  return N >= 1024 ? -1 : N >> 6;
+  const int R = N >> 6;
+  return (R == 2 || R == 3 || R == 4 || R == 5 || R == 6 || R == 8) ? R : -1;
 }
 
 template <int RA>
@@ -937,7 +960,10 @@ nc_status rows_inv_ra(const float2* src, const Planes& a, int N, const float2* t
 nc_status rows_fwd(const Planes& a, float2* dst, int N, const float2* tw, cudaStream_t st) {
   switch (kernel_ra(N)) {
     case 2: return rows_fwd_ra<2>(a, dst, N, tw, st);
+    case 3: return rows_fwd_ra<3>(a, dst, N, tw, st);
     case 4: return rows_fwd_ra<4>(a, dst, N, tw, st);
+    case 5: return rows_fwd_ra<5>(a, dst, N, tw, st);
+    case 6: return rows_fwd_ra<6>(a, dst, N, tw, st);
     case 8: return rows_fwd_ra<8>(a, dst, N, tw, st);
     case -1: return rows_fwd_ra<-1>(a, dst, N, tw, st);
     default: return rows_fwd_ra<0>(a, dst, N, tw, st);
@@ -947,7 +973,10 @@ nc_status rows_fwd(const Planes& a, float2* dst, int N, const float2* tw, cudaSt
 nc_status rows_inv(const float2* src, const Planes& a, int N, const float2* tw, cudaStream_t st) {
   switch (kernel_ra(N)) {
     case 2: return rows_inv_ra<2>(src, a, N, tw, st);
+    case 3: return rows_inv_ra<3>(src, a, N, tw, st);
     case 4: return rows_inv_ra<4>(src, a, N, tw, st);
+    case 5: return rows_inv_ra<5>(src, a, N, tw, st);
+    case 6: return rows_inv_ra<6>(src, a, N, tw, st);
     case 8: return rows_inv_ra<8>(src, a, N, tw, st);
     case -1: return rows_inv_ra<-1>(src, a, N, tw, st);
     default: return rows_inv_ra<0>(src, a, N, tw, st);
@@ -967,7 +996,10 @@ template <int MODE>
 nc_status cols(const ColArgs& a, int units, const float2* tw, cudaStream_t st) {
   switch (kernel_ra(a.Nh)) {
     case 2: return cols_ra<MODE, 2>(a, units, tw, st);
+    case 3: return cols_ra<MODE, 3>(a, units, tw, st);
     case 4: return cols_ra<MODE, 4>(a, units, tw, st);
+    case 5: return cols_ra<MODE, 5>(a, units, tw, st);
+    case 6: return cols_ra<MODE, 6>(a, units, tw, st);
     case 8: return cols_ra<MODE, 8>(a, units, tw, st);
     case -1: return cols_ra<MODE, -1>(a, units, tw, st);
     default: return cols_ra<MODE, 0>(a, units, tw, st);

@@ -140,41 +140,69 @@ __device__ __forceinline__ void inv2d(float2* s, int nrows, const float2* tw, co
   __syncthreads();
 }
 
-// ROI pixels p = tid + 512 k of this thread: their plane offsets (r, c) -> at2(r, c), or -1.
-constexpr int kPixPerThread = kN * kN / kThreads;   // a ROI has at most 64 x 64 pixels
-__device__ __forceinline__ void pixel_offsets(const Geo& g, int tid, int poff[kPixPerThread]) {
+// The fused kernels run 1024 threads: two halves of 512, each laid out as 64 groups of
+// 8 lanes (fft64::lane_of), so one half transforms every row or column of one plane.  A
+// round of the d-step loop holds two direction pairs in two working planes; half h works on
+// plane h wherever a phase has one transform per line and plane.
+constexpr int kThreadsF = 1024;
+constexpr int kPosPerThread = kN * kN / kThreadsF;   // plane positions per thread (4)
+
+// ROI pixels p = tid + 1024 k of this thread: their plane offsets (r, c) -> at2(r, c), or -1.
+__device__ __forceinline__ void pixel_offsets(const Geo& g, int tid, int poff[kPosPerThread]) {
 #pragma unroll
-  for (int k = 0; k < kPixPerThread; ++k) {
-    const int p = tid + k * kThreads;
+  for (int k = 0; k < kPosPerThread; ++k) {
+    const int p = tid + k * kThreadsF;
     const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
     poff[k] = p < g.P ? at2(r, c) : -1;
   }
 }
 
-// Sum of four per-thread values over the CTA, broadcast to every thread, with ONE barrier:
-// warp partials go to half `par` of `red` (2 x 4 x 16 floats) and every thread adds the 16
-// partials in warp order (the same order everywhere, so all threads get identical sums).
-// Alternating halves makes a barrier before the writes unnecessary: a thread writes half
-// `par` again only after the barrier of the next call, which every thread reaches after
-// its reads of this call.  Callers flip `par` after each call, uniformly.
-__device__ __forceinline__ void block_sum4(float v[4], float* red, int& par) {
-  static_assert(kThreads / 32 == 16, "16 warp partials");
-#pragma unroll
-  for (int k = 0; k < 4; ++k) v[k] = warp_sum(v[k]);
-  float* h = red + par * 64;
+// Sum of eight per-thread values over the 1024-thread CTA, broadcast to every thread, in a
+// fixed order: each warp's sums go to half `par` of `red` (2 x (8 x 32 + 8) floats); after a
+// barrier warp k < 8 adds value k over the 32 warps; after a second barrier every thread
+// reads the eight sums.  Alternating halves make a barrier before the writes unnecessary:
+// a thread writes half `par` again only after the barriers of the next call, which every
+// thread reaches after its reads of this call.  Callers flip `par` after each call.
+constexpr int kRedHalf = 8 * 32 + 8;
+__device__ __forceinline__ void block_sum8(float v[8], float* red, int& par) {
+  static_assert(kThreadsF / 32 == 32, "32 warp partials");
+  float* h = red + par * kRedHalf;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = warp_sum(v[k]);
   if (lane == 0)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) h[k * 16 + w] = v[k];
+    for (int k = 0; k < 8; ++k) h[k * 32 + w] = v[k];
+  __syncthreads();
+  if (w < 8) {
+    const float t = warp_sum(h[w * 32 + lane]);
+    if (lane == 0) h[256 + w] = t;
+  }
   __syncthreads();
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float4* q = reinterpret_cast<const float4*>(h + k * 16);
-    const float4 a0 = q[0], a1 = q[1], a2 = q[2], a3 = q[3];
-    v[k] = ((((a0.x + a0.y) + (a0.z + a0.w)) + ((a1.x + a1.y) + (a1.z + a1.w))) +
-            (((a2.x + a2.y) + (a2.z + a2.w)) + ((a3.x + a3.y) + (a3.z + a3.w))));
-  }
+  for (int k = 0; k < 8; ++k) v[k] = h[256 + k];
   par ^= 1;
+}
+
+// Forward 2-D transform of rows [0, nrows) then all columns by the first half (one plane
+// has one transform per line); barriers on both sides for the whole CTA.
+__device__ __forceinline__ void fwd2d_h0(float2* s, int nrows, const float2* tw, const fft64::Lane& L,
+                                         int half) {
+  __syncthreads();
+  if (half == 0) fft64::pass64<false, false>(s, nrows, tw, L);
+  __syncthreads();
+  if (half == 0) fft64::pass64<true, false>(s, kN, tw, L);
+  __syncthreads();
+}
+
+// Inverse 2-D transform (all columns, then rows [0, nrows)) by the first half.
+__device__ __forceinline__ void inv2d_h0(float2* s, int nrows, const float2* tw, const fft64::Lane& L,
+                                         int half) {
+  __syncthreads();
+  if (half == 0) fft64::pass64<true, true>(s, kN, tw, L);
+  __syncthreads();
+  if (half == 0) fft64::pass64<false, true>(s, nrows, tw, L);
+  __syncthreads();
 }
 
 // Chan's pairwise merge of (count, mean, centred sum of squares): the two-stage variance of
@@ -191,62 +219,54 @@ __device__ __forceinline__ void chan_merge(float& n, float& mean, float& m2, flo
   n = nn;
 }
 
-// Inverse row pass of the ROI rows of two planes (re and im parts: four real planes) that
-// also leaves each row's centred statistics (mean, M2 over its `roi_w` columns) in
-// rowst[row * 4 + k], k = (Wp re, Wp im, Wq re, Wq im).  The 8 lanes of a row sum their
-// values with three xor shuffles, then sum the squared deviations from the row mean the
-// same way; the row values never leave registers for it.
-__device__ __forceinline__ void rows_inv_x2_stats(float2* s1, float2* s2, int nrows, int roi_w,
-                                                  const float2* tw64, const fft64::Lane& L, float2* rowst) {
+// Inverse row pass of the ROI rows of one plane that also leaves each row's centred
+// statistics (mean, M2 over its `roi_w` columns) of the re and im parts in
+// rowst[row * 4 + k0] and rowst[row * 4 + k0 + 1].  The 8 lanes of a row sum their values
+// with three xor shuffles, then sum the squared deviations from the row mean the same way;
+// the row values never leave registers for it.
+__device__ __forceinline__ void rows_inv_stats(float2* s, int nrows, int roi_w, const float2* tw64,
+                                               const fft64::Lane& L, float2* rowst, int k0) {
   const int line = L.row;
   const bool active = line < nrows;
   if (!__any_sync(0xffffffffu, active)) return;
-  float2 v[8], u[8];
+  float2 v[8];
 #pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    const int o = at2(line, L.j + 8 * n);
-    v[n] = active ? s1[o] : make_float2(0.f, 0.f);
-    u[n] = active ? s2[o] : make_float2(0.f, 0.f);
-  }
+  for (int n = 0; n < 8; ++n) v[n] = active ? s[at2(line, L.j + 8 * n)] : make_float2(0.f, 0.f);
   fft64::fft64_lanes<true>(v, L.j, tw64);
-  fft64::fft64_lanes<true>(u, L.j, tw64);
-  float sm[4] = {0.f, 0.f, 0.f, 0.f};
+  float sx = 0.f, sy = 0.f;
 #pragma unroll
   for (int n = 0; n < 8; ++n) {
     if (L.j + 8 * n < roi_w) {
-      sm[0] += v[n].x; sm[1] += v[n].y; sm[2] += u[n].x; sm[3] += u[n].y;
+      sx += v[n].x;
+      sy += v[n].y;
     }
   }
 #pragma unroll
-  for (int o = 1; o < 8; o <<= 1)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) sm[k] += __shfl_xor_sync(0xffffffffu, sm[k], o);
+  for (int o = 1; o < 8; o <<= 1) {
+    sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    sy += __shfl_xor_sync(0xffffffffu, sy, o);
+  }
   const float inv_w = 1.0f / (float)roi_w;
-  float mu[4], q[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int k = 0; k < 4; ++k) mu[k] = sm[k] * inv_w;
+  const float mx = sx * inv_w, my = sy * inv_w;
+  float qx = 0.f, qy = 0.f;
 #pragma unroll
   for (int n = 0; n < 8; ++n) {
     if (L.j + 8 * n < roi_w) {
-      const float d0 = v[n].x - mu[0], d1 = v[n].y - mu[1], d2 = u[n].x - mu[2], d3 = u[n].y - mu[3];
-      q[0] = fmaf(d0, d0, q[0]); q[1] = fmaf(d1, d1, q[1]);
-      q[2] = fmaf(d2, d2, q[2]); q[3] = fmaf(d3, d3, q[3]);
+      const float dx = v[n].x - mx, dy = v[n].y - my;
+      qx = fmaf(dx, dx, qx);
+      qy = fmaf(dy, dy, qy);
     }
   }
 #pragma unroll
-  for (int o = 1; o < 8; o <<= 1)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) q[k] += __shfl_xor_sync(0xffffffffu, q[k], o);
+  for (int o = 1; o < 8; o <<= 1) {
+    qx += __shfl_xor_sync(0xffffffffu, qx, o);
+    qy += __shfl_xor_sync(0xffffffffu, qy, o);
+  }
   if (active) {
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const int o = at2(line, L.j + 8 * n);
-      s1[o] = v[n];
-      s2[o] = u[n];
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k)       // lane k of the row writes plane k (no indexed registers)
-      if (L.j == k) rowst[line * 4 + k] = make_float2(mu[k], q[k]);
+    for (int n = 0; n < 8; ++n) s[at2(line, L.j + 8 * n)] = v[n];
+    if (L.j == 0) rowst[line * 4 + k0] = make_float2(mx, qx);
+    if (L.j == 1) rowst[line * 4 + k0 + 1] = make_float2(my, qy);
   }
 }
 
@@ -330,15 +350,14 @@ __device__ void load_field(const FftfArgs& a, float2* X, const float* roi_src, c
 constexpr int kActRuntime = -1;
 
 template <int ACT, int FACT>
-__global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
+__global__ void __launch_bounds__(kThreadsF, 1) fftf_fwd_kernel(FftfArgs a) {
   extern __shared__ float4 smem4[];
   uint64_t* hbar = reinterpret_cast<uint64_t*>(smem4);   // staging barrier (16 B slot)
   volatile int* abort_flag = reinterpret_cast<int*>(smem4) + 2;   // in the same slot
   float2* stw = reinterpret_cast<float2*>(smem4 + 1);
   float2* X = stw + kN;
-  float2* Wp = X + kPlane;
-  float2* Wq = Wp + kPlane;
-  float2* Hs = Wq + kPlane;                               // staged spectra of one round
+  float2* W = X + kPlane;                                 // the round's two working planes
+  float2* Hs = W + 2 * kPlane;                            // staged spectra of one round
   const bool stage = a.stage != 0;
   float2* rowst = Hs + (stage ? 2 * kPlane : 0);          // (64 rows, 4 planes) row statistics
   float2* pst = rowst + 4 * kN;                           // 4 plane statistics (8 slots)
@@ -346,11 +365,12 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
   float* acc = lin + a.g.P;
   const Geo& g = a.g;
   const int tid = threadIdx.x, nt = blockDim.x, b = blockIdx.x;
+  const int half = tid >> 9;                              // working plane of this thread
   const size_t P = (size_t)g.P, M = (size_t)g.M;
   const int pairs = g.M / 2;
   fft64::init_tw64(stw, tid);
-  const fft64::Lane Ln = fft64::lane_of(tid);
-  int poff[kPixPerThread];
+  const fft64::Lane Ln = fft64::lane_of(tid & 511);
+  int poff[kPosPerThread];
   pixel_offsets(g, tid, poff);
   // Spectra of round j0 (pairs j0, j0+1) -> Hs: the stored planes already have the on-chip
   // layout (row stride 66: the column pass reads them without bank conflicts), so they
@@ -382,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
     const bool last = (t == g.d - 1);
     load_field(a, X, t == 0 ? nullptr : lin, a.inputs + (size_t)b * g.n_in, tid, nt);
     FFTF_MARK(0, 0);
-    fwd2d(X, g.Fh, stw, Ln);
+    fwd2d_h0(X, g.Fh, stw, Ln, half);
     if (a.train && a.xspec) {          // the backward reuses this step's field spectrum
       float2* xo = a.xspec + ((size_t)b * g.d + t) * kPlane;
       for (int i = tid; i < kPlane; i += nt) xo[i] = X[i];
@@ -392,35 +412,28 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
     const float slope = last ? g.fslope : g.slope;
     for (int p = tid; p < g.P; p += nt) { lin[p] = 0.f; acc[p] = 0.f; }
 
-    // two direction pairs (four planes) per round: independent transforms interleave
+    // two direction pairs (four planes) per round: half h transforms plane h
     for (int j = 0; j < pairs; j += 2) {
       const bool two = j + 1 < pairs;
-      const float2* Ha = a.H + (size_t)j * kPlane;
-      const float2* Hb = two ? Ha + kPlane : Ha;
+      const bool mine = half == 0 || two;                 // uniform over each half
+      float2* Wh = W + half * kPlane;
       if (stage) {
         mbar_wait(hbar, huse & 1u, a.sp.status, abort_flag);
         ++huse;
       }
       FFTF_MARK(0, 7);
-      // inverse column passes of X^ . H_j and X^ . H_{j+1} (products taken at load time)
-      {
-        float2 va[8], vb[8];
+      // inverse column pass of X^ . H_{j+h} (product taken at load time)
+      if (mine) {
+        const float2* Hh = stage ? Hs + half * kPlane : a.H + (size_t)(j + half) * kPlane;
+        float2 v[8];
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
-          const int r = Ln.j + 8 * n;
-          const float2 x = X[at2(r, Ln.col)];
-          const float2 ha = stage ? Hs[at2(r, Ln.col)] : __ldg(&Ha[at2(r, Ln.col)]);
-          const float2 hb = stage ? Hs[(two ? kPlane : 0) + at2(r, Ln.col)] : __ldg(&Hb[at2(r, Ln.col)]);
-          va[n] = cmul(x, ha);
-          vb[n] = cmul(x, hb);
+          const int o = at2(Ln.j + 8 * n, Ln.col);
+          v[n] = cmul(X[o], stage ? Hh[o] : __ldg(&Hh[o]));
         }
-        fft64::fft64_lanes<true>(va, Ln.j, stw);
-        fft64::fft64_lanes<true>(vb, Ln.j, stw);
+        fft64::fft64_lanes<true>(v, Ln.j, stw);
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          Wp[at2(Ln.j + 8 * n, Ln.col)] = va[n];
-          Wq[at2(Ln.j + 8 * n, Ln.col)] = vb[n];
-        }
+        for (int n = 0; n < 8; ++n) Wh[at2(Ln.j + 8 * n, Ln.col)] = v[n];
       }
       __syncthreads();
       if (stage && *abort_flag) {        // uniform: set before the barrier above
@@ -432,14 +445,16 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
         if (nj >= 0) issue_h(nj);
       }
       FFTF_MARK(0, 2);
-      // inverse row passes of the ROI rows (warps beyond them skip); with the spatial norm
-      // the pass also leaves every row's centred statistics, merged per plane below
-      if (g.norm) rows_inv_x2_stats(Wp, Wq, g.roi_h, g.roi_w, stw, Ln, rowst);
-      else fft64::pass64x2<false, true>(Wp, Wq, g.roi_h, stw, Ln);
+      // inverse row pass of the ROI rows (warps beyond them skip); with the spatial norm the
+      // pass also leaves every row's centred statistics, merged per plane below
+      if (mine) {
+        if (g.norm) rows_inv_stats(Wh, g.roi_h, g.roi_w, stw, Ln, rowst, 2 * half);
+        else fft64::pass64<false, true>(Wh, g.roi_h, stw, Ln);
+      }
       __syncthreads();
       FFTF_MARK(0, 3);
-      // plane statistics of 2j, 2j+1 (Wp re, im) and 2j+2, 2j+3 (Wq): centred per row, merged
-      // over the rows with Chan's formula; thread tid owns pixels p = tid + 512 k
+      // plane statistics of 2j, 2j+1 (plane 0 re, im) and 2j+2, 2j+3 (plane 1): centred per
+      // row, merged over the rows with Chan's formula
       float mu[4] = {0.f, 0.f, 0.f, 0.f}, rs[4] = {1.f, 1.f, 1.f, 1.f};
       if (g.norm) {
         merge_row_stats(rowst, g.roi_h, g.roi_w, pst);
@@ -456,11 +471,13 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
       if (a.train && tid < np)           // pst holds them when norm is on (no indexed registers)
         a.rstd[((size_t)b * g.d + t) * M + 2 * j + tid] = g.norm ? pst[tid].y : 1.0f;
       float* zh = a.train ? a.zhat + (((size_t)b * g.d + t) * M + 2 * j) * P : nullptr;
+      const float2* W0 = W;
+      const float2* W1 = W + kPlane;
 #pragma unroll
-      for (int k = 0; k < kPixPerThread; ++k) {
+      for (int k = 0; k < kPosPerThread; ++k) {
         if (poff[k] < 0) continue;
-        const int p = tid + k * kThreads;
-        const float2 w = Wp[poff[k]], u = Wq[poff[k]];
+        const int p = tid + k * kThreadsF;
+        const float2 w = W0[poff[k]], u = W1[poff[k]];
         const float h0 = (w.x - mu[0]) * rs[0], h1 = (w.y - mu[1]) * rs[1];
         const float h2 = (u.x - mu[2]) * rs[2], h3 = (u.y - mu[3]) * rs[3];
         const float bb = a.sp.broi[p];
@@ -518,103 +535,63 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_fwd_kernel(FftfArgs a) {
 // ---------------------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------------------
+// Two direction pairs per round, as in the forward.  The field spectra X^ and the pair
+// spectra H come from global memory (L2) in the column pass, the standardised planes are
+// staged into shared memory four planes at a time; the field adjoint D = sum_j Q^_j .
+// conj(H_j) and the per-pixel parameter gradients stay on chip for the whole launch.
 template <int ACT, int FACT>
-__global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
+__global__ void __launch_bounds__(kThreadsF, 1) fftf_bwd_kernel(FftfArgs a) {
   extern __shared__ float4 smem4[];
   const Geo& g = a.g;
   const int tid = threadIdx.x, nt = blockDim.x, b = blockIdx.x;
+  const int half = tid >> 9, warp = tid >> 5, lane = tid & 31;
   const size_t P = (size_t)g.P, M = (size_t)g.M;
   const int pairs = g.M / 2;
   const int FF = g.Fh * g.Fw;
-  // staging barriers: [0] saved planes, [1] filter-pair spectrum, [2] field spectrum
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem4);
-  volatile int* abort_flag = reinterpret_cast<int*>(smem4) + 6;   // after the three barriers
-  float2* stw = reinterpret_cast<float2*>(smem4 + 2);
-  float2* X = stw + kN;
-  float2* Wp = X + kPlane;
-  float2* D = Wp + kPlane;
+  uint64_t* zbar = reinterpret_cast<uint64_t*>(smem4);   // staging barrier of the planes
+  volatile int* abort_flag = reinterpret_cast<int*>(smem4) + 2;
+  float2* stw = reinterpret_cast<float2*>(smem4 + 1);
+  float2* W = stw + kN;                                   // the round's two working planes
+  float2* D = W + 2 * kPlane;                             // field-adjoint spectrum of the step
+  float* red = reinterpret_cast<float*>(D + kPlane);      // block_sum8 halves
   const bool stage = a.stage != 0;
-  float2* Hs = D + kPlane;                                // staged spectrum H_j
-  float* red = reinterpret_cast<float*>(Hs + (stage ? kPlane : 0));  // 160, 16-B aligned
-  float* zs = red + 160;                                  // staged planes 2j, 2j+1
-  float* gy = zs + (stage ? 2 * g.P : 0);
+  float* zs = red + 2 * kRedHalf;                         // staged planes 2j .. 2j+3
+  float* gy = zs + (stage ? 4 * g.P : 0);
   float* gp0 = gy + g.P;
   float* gp1 = gp0 + g.P;
   float* gp2 = gp1 + g.P;
   float* dg = gp2 + g.P;                       // M*K
   float* gport = dg + M * g.K;                 // n_out * M
-  float* ring = gport + (size_t)g.n_out * M;   // Fh*Fw when a.gring
-  int16_t* pmap = reinterpret_cast<int16_t*>(ring + (a.gring ? FF : 0));   // P
+  int16_t* pmap = reinterpret_cast<int16_t*>(gport + (size_t)g.n_out * M);   // P
+  float* ring = a.gring ? a.gring + (size_t)b * FF : nullptr;                 // global, this sample
   fft64::init_tw64(stw, tid);
-  const fft64::Lane Ln = fft64::lane_of(tid);
+  const fft64::Lane Ln = fft64::lane_of(tid & 511);
   for (int p = tid; p < g.P; p += nt) { gp0[p] = 0.f; gp1[p] = 0.f; gp2[p] = 0.f; pmap[p] = -1; }
   for (int i = tid; i < (int)(M * g.K); i += nt) dg[i] = 0.f;
-  if (a.gring)
+  if (ring)
     for (int i = tid; i < FF; i += nt) ring[i] = 0.f;
   if (tid == 0) *abort_flag = 0;
-  if (stage && tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    mbar_init(&bars[2], 1);
-  }
+  if (stage && tid == 0) mbar_init(zbar, 1);
   __syncthreads();
-  // Saved planes 2j, 2j+1 of step t_ (8P contiguous bytes, P % 4 == 0) -> zs, and the
-  // spectrum H_j -> Hs (stored in the on-chip layout, four bulk copies).  Warp 0, after a barrier that ends the
-  // previous readers of the buffer.  Spectra are staged only for steps t > 0 (the field
-  // adjoint); step 0 needs none.
-  unsigned zuse = 0, huse = 0, ziss = 0, hiss = 0;
+  // Saved planes 2j .. 2j+3 of step t_ (4P contiguous floats, P % 4 == 0) -> zs.  Warp 0,
+  // after a barrier that ends the previous readers of zs.
+  unsigned zuse = 0, ziss = 0;
   auto issue_z = [&](int t_, int j_) {
     ++ziss;
     if (tid < 32) {
-      const unsigned bytes = (unsigned)(2 * P * sizeof(float));
-      if (tid == 0) mbar_expect_tx(&bars[0], bytes);
+      const int np = (j_ + 1 < pairs) ? 2 : 1;
+      const unsigned bytes = (unsigned)(2 * np * P * sizeof(float));
+      if (tid == 0) mbar_expect_tx(zbar, bytes);
       __syncwarp();
       fence_proxy_async();
       const char* src = reinterpret_cast<const char*>(a.zhat + (((size_t)b * g.d + t_) * M + 2 * j_) * P);
       constexpr unsigned kChunk = 4096;
       for (unsigned o = tid * kChunk; o < bytes; o += 32 * kChunk)
-        bulk_g2s(reinterpret_cast<char*>(zs) + o, src + o, min(kChunk, bytes - o), &bars[0]);
+        bulk_g2s(reinterpret_cast<char*>(zs) + o, src + o, min(kChunk, bytes - o), zbar);
     }
   };
-  auto issue_h = [&](int j_) {
-    ++hiss;
-    if (tid < 32) {
-      if (tid == 0) mbar_expect_tx(&bars[1], kPlaneBytes);
-      __syncwarp();
-      fence_proxy_async();
-      if (tid < 4)
-        bulk_g2s(reinterpret_cast<char*>(Hs) + tid * kPlaneChunk,
-                 reinterpret_cast<const char*>(a.H + (size_t)j_ * kPlane) + tid * kPlaneChunk,
-                 kPlaneChunk, &bars[1]);
-    }
-  };
-  // the forward's field spectrum of step t_ -> X (four bulk copies); X is free from the
-  // last column pass of the step before (the field adjoint uses D)
-  const bool xstage = stage && a.xspec != nullptr;
-  unsigned xuse = 0, xiss = 0;
-  auto issue_x = [&](int t_) {
-    ++xiss;
-    if (tid < 32) {
-      if (tid == 0) mbar_expect_tx(&bars[2], kPlaneBytes);
-      __syncwarp();
-      fence_proxy_async();
-      if (tid < 4)
-        bulk_g2s(reinterpret_cast<char*>(X) + tid * kPlaneChunk,
-                 reinterpret_cast<const char*>(a.xspec + ((size_t)b * g.d + t_) * kPlane) + tid * kPlaneChunk,
-                 kPlaneChunk, &bars[2]);
-    }
-  };
-  auto drain = [&]() {
-    mbar_drain(&bars[0], zuse, ziss);
-    mbar_drain(&bars[1], huse, hiss);
-    mbar_drain(&bars[2], xuse, xiss);
-  };
-  if (stage) {
-    issue_z(g.d - 1, 0);
-    if (g.d > 1) issue_h(0);
-    if (xstage) issue_x(g.d - 1);
-  }
-  int rpar = 0;                  // block_sum4 half
+  if (stage) issue_z(g.d - 1, 0);
+  int rpar = 0;                  // block_sum8 half
   FFTF_T0();
 
   // output step (t = d-1): the port cells' plane gradients and parameter gradients
@@ -660,147 +637,155 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   __syncthreads();
   FFTF_MARK(1, 0);
 
+  // column-pass lanes: warp w takes columns 2w, 2w+1 of both planes; lanes 0-15 plane 0,
+  // lanes 16-31 plane 1 (lane ^ 16 holds the same positions of the other plane)
+  const int cj = lane & 7, ccol = 2 * warp + ((lane >> 3) & 1), cpl = lane >> 4;
+
   for (int t = g.d - 1; t >= 0; --t) {
     const bool last = (t == g.d - 1);
-    if (xstage) {
-      mbar_wait(&bars[2], xuse & 1u, a.sp.status, abort_flag);
-      ++xuse;
-    } else {
-      const float* xs = t > 0 ? a.xsave + ((size_t)b * (g.d - 1) + (t - 1)) * P : nullptr;
-      load_field(a, X, xs, a.inputs + (size_t)b * g.n_in, tid, nt);
-      fwd2d(X, g.Fh, stw, Ln);
-    }
     if (t > 0)
       for (int i = tid; i < kPlane; i += nt) D[i] = make_float2(0.f, 0.f);
     FFTF_MARK(1, 1);
     const float* ZH = a.zhat + ((size_t)b * g.d + t) * M * P;
+    const float2* Xs = a.xspec + ((size_t)b * g.d + t) * kPlane;
     // universe mode runs the last step's ROI epilogue with the final activation
     const int act_id = last ? (FACT != kActRuntime ? FACT : g.fact) : (ACT != kActRuntime ? ACT : g.act);
     const float slope = last ? g.fslope : g.slope;
 
-    for (int j = 0; j < pairs; ++j) {
-      const int m1 = 2 * j, m2 = 2 * j + 1;
-      const float* z1 = ZH + (size_t)m1 * P;
-      const float* z2 = ZH + (size_t)m2 * P;
+    for (int j = 0; j < pairs; j += 2) {
+      const bool two = j + 1 < pairs;
+      const bool mine = half == 0 || two;
+      const float* zp = stage ? zs : ZH + (size_t)(2 * j) * P;   // planes 2j .. 2j+3
       if (stage) {
-        mbar_wait(&bars[0], zuse & 1u, a.sp.status, abort_flag);
+        mbar_wait(zbar, zuse & 1u, a.sp.status, abort_flag);
         ++zuse;
-        z1 = zs;
-        z2 = zs + P;
       }
       FFTF_MARK(1, 9);
-      const float rs1 = a.rstd[((size_t)b * g.d + t) * M + m1];
-      const float rs2 = a.rstd[((size_t)b * g.d + t) * M + m2];
       // plane gradients before the standardisation adjoint at plane positions
-      // i = tid + 512 k (row i / 64, column i % 64; zero outside the ROI), and their moments
-      float h1[kPixPerThread], h2[kPixPerThread];
-      float2 v[kPixPerThread];
-      float mo[4] = {0.f, 0.f, 0.f, 0.f};
+      // i = tid + 1024 k (row i / 64, column i % 64; zero outside the ROI) of both pairs,
+      // stored raw, and their moments
+      float mo[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < kPixPerThread; ++k) {
-        const int i = tid + k * kThreads, r = i >> 6, c = i & (kN - 1);
-        h1[k] = 0.f;
-        h2[k] = 0.f;
-        v[k] = make_float2(0.f, 0.f);
-        if (r >= g.roi_h || c >= g.roi_w) continue;
-        const int p = r * g.roi_w + c;
-        h1[k] = z1[p];
-        h2[k] = z2[p];
-        if (last && !a.guroi) {
-          const int jo = pmap[p];
-          if (jo >= 0) v[k] = make_float2(gport[jo * g.M + m1], gport[jo * g.M + m2]);
-        } else {
-          const float y = gy[p], bb = a.sp.broi[p], we = a.sp.weff[p], se = a.sp.seff[p];
-          float d1, d2;
-          const float a1 = act_fwd_deriv(act_id, h1[k] + bb, slope, &d1);
-          const float a2 = act_fwd_deriv(act_id, h2[k] + bb, slope, &d2);
-          v[k] = make_float2(we * y + se * y * d1, we * y + se * y * d2);
-          // pixel-parameter gradients, summed over directions pair by pair
-          gp0[p] += y * (h1[k] + h2[k]);
-          gp1[p] += y * (a1 + a2);
-          gp2[p] += se * y * (d1 + d2);
+      for (int k = 0; k < kPosPerThread; ++k) {
+        const int i = tid + k * kThreadsF, r = i >> 6, c = i & (kN - 1);
+        float2 v0 = make_float2(0.f, 0.f), v1 = v0;
+        if (r < g.roi_h && c < g.roi_w) {
+          const int p = r * g.roi_w + c;
+          const float h0 = zp[p], h1 = zp[P + p];
+          const float h2 = two ? zp[2 * P + p] : 0.f, h3 = two ? zp[3 * P + p] : 0.f;
+          if (last && !a.guroi) {
+            const int jo = pmap[p];
+            if (jo >= 0) {
+              const float* gq = gport + jo * g.M + 2 * j;
+              v0 = make_float2(gq[0], gq[1]);
+              if (two) v1 = make_float2(gq[2], gq[3]);
+            }
+          } else {
+            const float y = gy[p], bb = a.sp.broi[p], wy = a.sp.weff[p] * y, sy = a.sp.seff[p] * y;
+            float d0, d1, d2 = 0.f, d3 = 0.f;
+            float as = act_fwd_deriv(act_id, h0 + bb, slope, &d0) + act_fwd_deriv(act_id, h1 + bb, slope, &d1);
+            float hs = h0 + h1;
+            if (two) {
+              as += act_fwd_deriv(act_id, h2 + bb, slope, &d2) + act_fwd_deriv(act_id, h3 + bb, slope, &d3);
+              hs += h2 + h3;
+            }
+            v0 = make_float2(fmaf(sy, d0, wy), fmaf(sy, d1, wy));
+            v1 = make_float2(fmaf(sy, d2, wy), fmaf(sy, d3, wy));
+            // pixel-parameter gradients, summed over the round's directions
+            gp0[p] = fmaf(y, hs, gp0[p]);
+            gp1[p] = fmaf(y, as, gp1[p]);
+            gp2[p] = fmaf(sy, (d0 + d1) + (d2 + d3), gp2[p]);
+          }
+          mo[0] += v0.x; mo[1] = fmaf(v0.x, h0, mo[1]);
+          mo[2] += v0.y; mo[3] = fmaf(v0.y, h1, mo[3]);
+          mo[4] += v1.x; mo[5] = fmaf(v1.x, h2, mo[5]);
+          mo[6] += v1.y; mo[7] = fmaf(v1.y, h3, mo[7]);
         }
-        mo[0] += v[k].x;
-        mo[1] = fmaf(v[k].x, h1[k], mo[1]);
-        mo[2] += v[k].y;
-        mo[3] = fmaf(v[k].y, h2[k], mo[3]);
+        W[at2(r, c)] = v0;
+        W[kPlane + at2(r, c)] = v1;
       }
       FFTF_MARK(1, 2);
       if (g.norm) {
-        block_sum4(mo, red, rpar);
+        block_sum8(mo, red, rpar);       // its barriers also publish the raw stores
+        if (stage && *abort_flag) {      // uniform: set before the barriers above
+          mbar_drain(zbar, zuse, ziss);
+          return;
+        }
+        // the standardisation adjoint gz = rs (v - mean(v) - z^ mean(v z^)) per plane
         const float inv_n = 1.0f / (float)g.P;
-        const float c11 = mo[0] * inv_n, c21 = mo[1] * inv_n, c12 = mo[2] * inv_n, c22 = mo[3] * inv_n;
+        const size_t rb = ((size_t)b * g.d + t) * M + 2 * j;
+        const float r0 = a.rstd[rb], r1 = a.rstd[rb + 1];
+        const float r2 = two ? a.rstd[rb + 2] : 0.f, r3 = two ? a.rstd[rb + 3] : 0.f;
 #pragma unroll
-        for (int k = 0; k < kPixPerThread; ++k) {
-          const int i = tid + k * kThreads, r = i >> 6, c = i & (kN - 1);
+        for (int k = 0; k < kPosPerThread; ++k) {
+          const int i = tid + k * kThreadsF, r = i >> 6, c = i & (kN - 1);
           if (r >= g.roi_h || c >= g.roi_w) continue;
-          v[k].x = rs1 * (v[k].x - c11 - h1[k] * c21);
-          v[k].y = rs2 * (v[k].y - c12 - h2[k] * c22);
+          const int p = r * g.roi_w + c, o = at2(r, c);
+          const float2 v0 = W[o], v1 = W[kPlane + o];
+          W[o] = make_float2(r0 * (v0.x - mo[0] * inv_n - zp[p] * (mo[1] * inv_n)),
+                             r1 * (v0.y - mo[2] * inv_n - zp[P + p] * (mo[3] * inv_n)));
+          if (two)
+            W[kPlane + o] = make_float2(r2 * (v1.x - mo[4] * inv_n - zp[2 * P + p] * (mo[5] * inv_n)),
+                                        r3 * (v1.y - mo[6] * inv_n - zp[3 * P + p] * (mo[7] * inv_n)));
         }
-      }
-#pragma unroll
-      for (int k = 0; k < kPixPerThread; ++k) {
-        const int i = tid + k * kThreads;
-        Wp[at2(i >> 6, i & (kN - 1))] = v[k];
-      }
-      __syncthreads();
-      if (stage && *abort_flag) {        // uniform: set before the barrier above
-        drain();
-        return;
-      }
-      if (stage) {                       // the next pair's planes land during this pair
-        if (j + 1 < pairs) issue_z(t, j + 1);
-        else if (t > 0) issue_z(t - 1, 0);
-      }
-      FFTF_MARK(1, 3);
-      // Q^_j = FFT(gz_{2j} + i gz_{2j+1}): rows of the ROI, then the columns
-      fft64::pass64<false, false>(Wp, g.roi_h, stw, Ln);
-      __syncthreads();
-      FFTF_MARK(1, 4);
-      const float2* H = a.H + (size_t)j * kPlane;
-      if (stage && t > 0) {
-        mbar_wait(&bars[1], huse & 1u, a.sp.status, abort_flag);
-        ++huse;
-      }
-      FFTF_MARK(1, 10);
-      {
-        float2 q[8];
-#pragma unroll
-        for (int n = 0; n < 8; ++n) q[n] = Wp[at2(Ln.j + 8 * n, Ln.col)];
-        fft64::fft64_lanes<false>(q, Ln.j, stw);
-        // D += Q^ . conj(H_j) (field adjoint); X^ . conj(Q^) (filter adjoint)
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          const int r = Ln.j + 8 * n, o = at2(r, Ln.col);
-          if (t > 0) D[o] = cadd(D[o], cmulc(q[n], stage ? Hs[o] : __ldg(&H[o])));
-          q[n] = cmulc(X[o], q[n]);
-        }
-        // inverse column pass of the product, on the registers just formed
-        fft64::fft64_lanes<true>(q, Ln.j, stw);
-#pragma unroll
-        for (int n = 0; n < 8; ++n) Wp[at2(Ln.j + 8 * n, Ln.col)] = q[n];
       }
       __syncthreads();
       if (stage && *abort_flag) {
-        drain();
+        mbar_drain(zbar, zuse, ziss);
         return;
       }
-      if (stage) {                       // the next spectrum lands during this pair
-        if (t > 0 && j + 1 < pairs) issue_h(j + 1);
-        else if (j + 1 == pairs && t > 1) issue_h(0);
-        if (xstage && j + 1 == pairs && t > 0) issue_x(t - 1);
+      if (stage) {                       // the next round's planes land during this round
+        if (j + 2 < pairs) issue_z(t, j + 2);
+        else if (t > 0) issue_z(t - 1, 0);
       }
-      FFTF_MARK(1, 5);
-      // corr(X, gz_{2j}) - i corr(X, gz_{2j+1}) at lags [0, kh) x [0, kw): inverse row pass
-      // of the first kh rows (warps beyond them skip), kept in registers
+      FFTF_MARK(1, 3);
+      // Q^ = FFT(gz_{2(j+h)} + i gz_{2(j+h)+1}): rows of the ROI, then the columns
+      if (mine) fft64::pass64<false, false>(W + half * kPlane, g.roi_h, stw, Ln);
+      __syncthreads();
+      FFTF_MARK(1, 4);
       {
+        const bool cact = cpl == 0 || two;
+        float2* Wc = W + cpl * kPlane;
+        float2 q[8];
+#pragma unroll
+        for (int n = 0; n < 8; ++n) q[n] = cact ? Wc[at2(cj + 8 * n, ccol)] : make_float2(0.f, 0.f);
+        fft64::fft64_lanes<false>(q, cj, stw);
+        if (t > 0) {
+          // D += Q^_j . conj(H_j) + Q^_{j+1} . conj(H_{j+1}): plane-0 lanes add the partner's
+          // term (lane ^ 16) to their own and update D
+          const float2* Hc = a.H + (size_t)(j + cpl) * kPlane;
+#pragma unroll
+          for (int n = 0; n < 8; ++n) {
+            const int o = at2(cj + 8 * n, ccol);
+            const float2 dv = cact ? cmulc(q[n], __ldg(&Hc[o])) : make_float2(0.f, 0.f);
+            const float ox = __shfl_xor_sync(0xffffffffu, dv.x, 16);
+            const float oy = __shfl_xor_sync(0xffffffffu, dv.y, 16);
+            if (cpl == 0) D[o] = cadd(D[o], make_float2(dv.x + ox, dv.y + oy));
+          }
+        }
+        // X^ . conj(Q^) (filter adjoint), then the inverse column pass in registers
+#pragma unroll
+        for (int n = 0; n < 8; ++n) q[n] = cmulc(__ldg(&Xs[at2(cj + 8 * n, ccol)]), q[n]);
+        fft64::fft64_lanes<true>(q, cj, stw);
+        if (cact) {
+#pragma unroll
+          for (int n = 0; n < 8; ++n) Wc[at2(cj + 8 * n, ccol)] = q[n];
+        }
+      }
+      __syncthreads();
+      FFTF_MARK(1, 5);
+      // corr(X, gz_{2m}) - i corr(X, gz_{2m+1}) at lags [0, kh) x [0, kw) for pair m = j + h:
+      // inverse row pass of the first kh rows (warps beyond them skip), kept in registers
+      if (mine) {
         const bool lagok = Ln.row < g.kh;
         if (__any_sync(0xffffffffu, lagok)) {
+          const float2* Wh = W + half * kPlane;
           float2 w[8];
 #pragma unroll
-          for (int n = 0; n < 8; ++n) w[n] = lagok ? Wp[at2(Ln.row, Ln.j + 8 * n)] : make_float2(0.f, 0.f);
+          for (int n = 0; n < 8; ++n) w[n] = lagok ? Wh[at2(Ln.row, Ln.j + 8 * n)] : make_float2(0.f, 0.f);
           fft64::fft64_lanes<true>(w, Ln.j, stw);
           if (lagok) {
+            const int m1 = 2 * (j + half), m2 = m1 + 1;
 #pragma unroll
             for (int n = 0; n < 8; ++n) {
               const int vv = Ln.j + 8 * n;
@@ -818,7 +803,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
     if (t == 0) break;
 
     // field adjoint of step t: Re IFFT(D) on the field rows
-    inv2d(D, g.Fh, stw, Ln);
+    inv2d_h0(D, g.Fh, stw, Ln, half);
     for (int p = tid; p < g.P; p += nt) {
       const int r = p / g.roi_w, c = p - (p / g.roi_w) * g.roi_w;
       float s;
@@ -831,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
       }
       gy[p] = s;
     }
-    if (a.gring) {
+    if (ring) {
       for (int i = tid; i < FF; i += nt) {
         const int fr = i / g.Fw, fc = i - (i / g.Fw) * g.Fw;
         const int r = fr - g.oh, c = fc - g.ow;
@@ -848,10 +833,6 @@ __global__ void __launch_bounds__(kThreads, 1) fftf_bwd_kernel(FftfArgs a) {
   for (int p = tid; p < g.P; p += nt) { gpx[p] = gp0[p]; gpx[P + p] = gp1[p]; gpx[2 * P + p] = gp2[p]; }
   float* gd = a.gdpart + (size_t)b * M * g.K;
   for (int i = tid; i < (int)(M * g.K); i += nt) gd[i] = dg[i];
-  if (a.gring) {
-    float* gr = a.gring + (size_t)b * FF;
-    for (int i = tid; i < FF; i += nt) gr[i] = ring[i];
-  }
   FFTF_MARK(1, 8);
 }
 
@@ -917,18 +898,17 @@ size_t fftf_fwd_smem(const Geo& g, bool stage) {
          sizeof(float) * 2 * (size_t)g.P;
 }
 
-
+// The ring gradient accumulates in global memory, so `ring` does not change the size.
 size_t fftf_bwd_smem(const Geo& g, bool ring, bool stage) {
-  size_t f = 4 * (size_t)g.P + (size_t)g.M * g.K + (size_t)g.n_out * g.M + 160 +
-             (ring ? (size_t)g.Fh * g.Fw : 0) + (stage ? 2 * (size_t)g.P : 0);
-  return 32 + sizeof(float2) * (kN + (3 + (stage ? 1 : 0)) * (size_t)kPlane) + sizeof(float) * f +
-         sizeof(int16_t) * (size_t)g.P + 16;
+  (void)ring;
+  const size_t f = (size_t)2 * kRedHalf + (stage ? 4 * (size_t)g.P : 0) + 4 * (size_t)g.P +
+                   (size_t)g.M * g.K + (size_t)g.n_out * g.M;
+  return 16 + sizeof(float2) * (kN + 3 * (size_t)kPlane) + sizeof(float) * f + sizeof(int16_t) * (size_t)g.P + 16;
 }
 
 bool fftf_fits(const Geo& g) {
   if (g.Nh != kN || g.Nw != kN || g.M % 2 != 0 || g.P > 32767) return false;
-  const bool ring = g.padding == NC_PAD_VALID && g.d > 1;
-  return fftf_fwd_smem(g, false) <= kFftfSmemMax && fftf_bwd_smem(g, ring, false) <= kFftfSmemMax;
+  return fftf_fwd_smem(g, false) <= kFftfSmemMax && fftf_bwd_smem(g, false, false) <= kFftfSmemMax;
 }
 
 nc_status fftf_prestep_spectra(const Geo& g, const StepParams& sp, const float* cell, const float* filters,
@@ -951,7 +931,7 @@ nc_status fftf_forward(const FftfArgs& args, cudaStream_t st) {
                                    : (const void*)fftf_fwd_kernel<kActRuntime, kActRuntime>;
   NC_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* kargs[] = {&a};
-  NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(a.batch), dim3(kThreads), kargs, smem, st));
+  NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(a.batch), dim3(kThreadsF), kargs, smem, st));
   return launched("fftf_fwd_kernel launch");
 }
 
@@ -959,12 +939,13 @@ nc_status fftf_backward(const FftfArgs& args, cudaStream_t st) {
   FftfArgs a = args;
   const bool ring = a.gring != nullptr;
   a.stage = (a.g.P % 4 == 0 && fftf_bwd_smem(a.g, ring, true) <= kFftfSmemMax) ? 1 : 0;
+  if (!a.xspec || !a.zhat) return set_error(NC_ERR_INVALID, "fused FFT backward needs the forward's saved spectra and planes");
   const size_t smem = fftf_bwd_smem(a.g, ring, a.stage != 0);
   const void* fn = fixed_acts(a.g) ? (const void*)fftf_bwd_kernel<NC_ACT_TANH, NC_ACT_NONE>
                                    : (const void*)fftf_bwd_kernel<kActRuntime, kActRuntime>;
   NC_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* kargs[] = {&a};
-  NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(a.batch), dim3(kThreads), kargs, smem, st));
+  NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(a.batch), dim3(kThreadsF), kargs, smem, st));
   return launched("fftf_bwd_kernel launch");
 }
 

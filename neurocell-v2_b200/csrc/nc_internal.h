@@ -29,7 +29,7 @@ struct Geo {
   int norm, hard_pin, gated;
   int F_elems;             // floats of one field buffer (incl. slack rows)
   int algo;                // resolved nc_conv_algo: NC_CONV_DIRECT or NC_CONV_FFT
-  int Nh, Nw;              // FFT grid (next powers of two of Fh, Fw)
+  int Nh, Nw;              // FFT grid: sides >= Fh, Fw (powers of two to 64, then 64 R)
 };
 
 // Largest FFT side the on-chip line transforms handle.

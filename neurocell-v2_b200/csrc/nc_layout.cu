@@ -17,6 +17,17 @@ static int next_pow2(int x) {
   return n;
 }
 
+// FFT side for a field side F: a power of two up to 64 (radix-4 plans), else the smallest
+// N = 64 R >= F whose first-stage radix R the two-stage transforms have (nc_fft.cuh); a
+// size above 1024 is refused by the caller.  The result of the convolution does not depend
+// on the transform size as long as N >= F.
+static int fft_side(int F) {
+  if (F <= 64) return next_pow2(F);
+  for (int R = 2; R <= kFftMaxN / 64; ++R)
+    if (fft::stage_a_radix(R) && 64 * R >= F) return 64 * R;
+  return next_pow2(F);
+}
+
 nc_status make_geo(const nc_topo* t, Geo* g) {
   if (!t) return set_error(NC_ERR_INVALID, "topology pointer is null");
   if (t->H <= 0 || t->W <= 0) return set_error(NC_ERR_INVALID, "grid must be positive, got %dx%d", t->H, t->W);
@@ -55,8 +66,8 @@ nc_status make_geo(const nc_topo* t, Geo* g) {
   const double total_px = (double)g->M * (double)g->P;
   if (total_px > 2.0e9) return set_error(NC_ERR_UNSUPPORTED, "plane too large (%g values)", total_px);
   // Green's convolution algorithm (reference auto rule: propagator.py:68-85)
-  g->Nh = next_pow2(g->Fh);
-  g->Nw = next_pow2(g->Fw);
+  g->Nh = fft_side(g->Fh);
+  g->Nw = fft_side(g->Fw);
   const bool fft_fits = g->Nh <= kFftMaxN && g->Nw <= kFftMaxN;
   if (t->conv_algo < NC_CONV_AUTO || t->conv_algo > NC_CONV_FFT)
     return set_error(NC_ERR_INVALID, "unsupported conv_algo id %d", t->conv_algo);

@@ -586,11 +586,18 @@ def test_zz_workspace_status_was_read():
 
 
 # ---- two-stage line transforms of the FFT regime (N = 64 R: 128 .. 1024) ----------------
+# The planner takes the smallest N = 64 R >= the field side with R in {2, 3, 4, 5, 6, 8, 16}
+# (a power of two up to 64).  FFT grid (rows x columns of the transform) noted per case.
 @pytest.mark.parametrize("grid,kernel,mode", [
-    ((160, 160), (31, 31), "VALID"),     # N = 256 x 256 (R = 4)
-    ((300, 100), (9, 9), "VALID"),       # N = 512 x 128 (R = 8 rows, R = 2 columns)
-    ((280, 20), (17, 5), "SAME"),        # N = 512 x 32: two-stage rows, radix-4 columns
-    ((600, 60), (25, 5), "VALID"),       # N = 1024 x 64 (R = 16, R = 1)
+    ((160, 160), (31, 31), "VALID"),     # 192 x 192 (R = 3, 3)
+    ((220, 140), (9, 9), "VALID"),       # 256 x 192 (R = 4 columns, R = 3 rows)
+    ((300, 100), (9, 9), "VALID"),       # 320 x 128 (R = 5, R = 2)
+    ((280, 20), (17, 5), "SAME"),        # 320 x 32: two-stage columns, radix-4 rows
+    ((350, 70), (7, 7), "VALID"),        # 384 x 128 (R = 6, R = 2)
+    ((100, 350), (5, 9), "SAME"),        # 128 x 384 (R = 2, R = 6)
+    ((260, 40), (7, 7), "CIRCULAR"),     # 320 x 64 (R = 5, R = 1), wrapped halo
+    ((450, 64), (9, 9), "VALID"),        # 512 x 64 (R = 8, R = 1)
+    ((600, 60), (25, 5), "VALID"),       # 1024 x 64 (R = 16, R = 1)
 ])
 def test_fft_two_stage_line_transforms_parity(grid, kernel, mode):
     H, W = grid
@@ -604,8 +611,8 @@ def test_fft_two_stage_line_transforms_parity(grid, kernel, mode):
 
 # ---- direction blocks of the filter-gradient accumulation, odd direction counts ---------
 @pytest.mark.parametrize("grid,kernel,M", [
-    ((300, 150), (9, 9), 16),    # FFT 512 x 256: the accumulation holds 8 directions per thread
-    ((160, 160), (31, 31), 5),   # FFT 256 x 256, M odd: blocks of 2 with a partial last block,
+    ((300, 150), (9, 9), 16),    # FFT 320 x 192: the accumulation holds 8 directions per thread
+    ((160, 160), (31, 31), 5),   # FFT 192 x 192, M odd: blocks of 2 with a partial last block,
                                  # and the paired-direction reductions end on a single direction
 ])
 def test_fft_direction_blocks_parity(grid, kernel, M):
