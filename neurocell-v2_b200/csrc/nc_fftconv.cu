@@ -71,20 +71,16 @@ __device__ __forceinline__ float plane_in(const Planes& a, int b, int m, size_t 
 __device__ __forceinline__ int even_up(int x) { return (x + 1) & ~1; }
 
 // Line l and element e of a flat index over lines of N elements: N = 64 RA is a compile-time
-// constant when RA > 0; otherwise shifts for a power of two, a division for the rest.
+// constant when RA > 0; the other variants only see powers of two (N <= 64 for RA = 0,
+// N = 1024 for RA = -1, see kernel_ra), so shifts.
 template <int RA>
 __device__ __forceinline__ void line_elem(int idx, int N, int lgN, int& l, int& e) {
   if constexpr (RA > 0) {
     l = idx / (64 * RA);
     e = idx - l * (64 * RA);
   } else {
-    if ((N & (N - 1)) == 0) {
-      l = idx >> lgN;
-      e = idx & (N - 1);
-    } else {
-      l = idx / N;
-      e = idx - l * N;
-    }
+    l = idx >> lgN;
+    e = idx & (N - 1);
   }
 }
 

@@ -363,6 +363,7 @@ __global__ void __launch_bounds__(kThreadsF, 1) fftf_fwd_kernel(FftfArgs a) {
   float2* pst = rowst + 4 * kN;                           // 4 plane statistics (8 slots)
   float* lin = reinterpret_cast<float*>(pst + 8);
   float* acc = lin + a.g.P;
+  float* bsm = acc + a.g.P;                               // b on the ROI, read every round
   const Geo& g = a.g;
   const int tid = threadIdx.x, nt = blockDim.x, b = blockIdx.x;
   const int half = tid >> 9;                              // working plane of this thread
@@ -372,6 +373,7 @@ __global__ void __launch_bounds__(kThreadsF, 1) fftf_fwd_kernel(FftfArgs a) {
   const fft64::Lane Ln = fft64::lane_of(tid & 511);
   int poff[kPosPerThread];
   pixel_offsets(g, tid, poff);
+  for (int p = tid; p < g.P; p += nt) bsm[p] = a.sp.broi[p];   // published by the first barriers
   // Spectra of round j0 (pairs j0, j0+1) -> Hs: the stored planes already have the on-chip
   // layout (row stride 66: the column pass reads them without bank conflicts), so they
   // move as four bulk copies each.  Warp 0, after a barrier that ends the previous readers
@@ -480,7 +482,7 @@ __global__ void __launch_bounds__(kThreadsF, 1) fftf_fwd_kernel(FftfArgs a) {
         const float2 w = W0[poff[k]], u = W1[poff[k]];
         const float h0 = (w.x - mu[0]) * rs[0], h1 = (w.y - mu[1]) * rs[1];
         const float h2 = (u.x - mu[2]) * rs[2], h3 = (u.y - mu[3]) * rs[3];
-        const float bb = a.sp.broi[p];
+        const float bb = bsm[p];
         if (zh) { zh[p] = h0; zh[P + p] = h1; }
         float l = h0 + h1;
         float ac = (act_id != NC_ACT_NONE) ? act_fwd(act_id, h0 + bb, slope) + act_fwd(act_id, h1 + bb, slope) : 0.f;
@@ -560,13 +562,19 @@ __global__ void __launch_bounds__(kThreadsF, 1) fftf_bwd_kernel(FftfArgs a) {
   float* gp0 = gy + g.P;
   float* gp1 = gp0 + g.P;
   float* gp2 = gp1 + g.P;
-  float* dg = gp2 + g.P;                       // M*K
+  float* wsm = gp2 + g.P;                      // w_eff, s_eff, b on the ROI, read every round
+  float* ssm = wsm + g.P;
+  float* bsm = ssm + g.P;
+  float* dg = bsm + g.P;                       // M*K
   float* gport = dg + M * g.K;                 // n_out * M
   int16_t* pmap = reinterpret_cast<int16_t*>(gport + (size_t)g.n_out * M);   // P
   float* ring = a.gring ? a.gring + (size_t)b * FF : nullptr;                 // global, this sample
   fft64::init_tw64(stw, tid);
   const fft64::Lane Ln = fft64::lane_of(tid & 511);
-  for (int p = tid; p < g.P; p += nt) { gp0[p] = 0.f; gp1[p] = 0.f; gp2[p] = 0.f; pmap[p] = -1; }
+  for (int p = tid; p < g.P; p += nt) {
+    gp0[p] = 0.f; gp1[p] = 0.f; gp2[p] = 0.f; pmap[p] = -1;
+    wsm[p] = a.sp.weff[p]; ssm[p] = a.sp.seff[p]; bsm[p] = a.sp.broi[p];
+  }
   for (int i = tid; i < (int)(M * g.K); i += nt) dg[i] = 0.f;
   if (ring)
     for (int i = tid; i < FF; i += nt) ring[i] = 0.f;
@@ -681,7 +689,7 @@ __global__ void __launch_bounds__(kThreadsF, 1) fftf_bwd_kernel(FftfArgs a) {
               if (two) v1 = make_float2(gq[2], gq[3]);
             }
           } else {
-            const float y = gy[p], bb = a.sp.broi[p], wy = a.sp.weff[p] * y, sy = a.sp.seff[p] * y;
+            const float y = gy[p], bb = bsm[p], wy = wsm[p] * y, sy = ssm[p] * y;
             float d0, d1, d2 = 0.f, d3 = 0.f;
             float as = act_fwd_deriv(act_id, h0 + bb, slope, &d0) + act_fwd_deriv(act_id, h1 + bb, slope, &d1);
             float hs = h0 + h1;
@@ -895,13 +903,13 @@ nc_status launched(const char* what) {
 
 size_t fftf_fwd_smem(const Geo& g, bool stage) {
   return 16 + sizeof(float2) * (kN + (3 + (stage ? 2 : 0)) * (size_t)kPlane + 4 * kN + 8) +
-         sizeof(float) * 2 * (size_t)g.P;
+         sizeof(float) * 3 * (size_t)g.P;
 }
 
 // The ring gradient accumulates in global memory, so `ring` does not change the size.
 size_t fftf_bwd_smem(const Geo& g, bool ring, bool stage) {
   (void)ring;
-  const size_t f = (size_t)2 * kRedHalf + (stage ? 4 * (size_t)g.P : 0) + 4 * (size_t)g.P +
+  const size_t f = (size_t)2 * kRedHalf + (stage ? 4 * (size_t)g.P : 0) + 7 * (size_t)g.P +
                    (size_t)g.M * g.K + (size_t)g.n_out * g.M;
   return 16 + sizeof(float2) * (kN + 3 * (size_t)kPlane) + sizeof(float) * f + sizeof(int16_t) * (size_t)g.P + 16;
 }
