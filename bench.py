@@ -8,7 +8,8 @@
   (``--exchange nccl``: NCCL all-reduce + SGD kernel) -- data parallel, weak scaling:
   global batch = 128*N.  Prints ONE
   JSON line on rank 0: device-resident throughput (``value``), the end-to-end figure through
-  the public ``VNNTrainStep`` API with pinned host batches (``e2e``), the fused-kernel
+  the public ``VNNTrainStep`` API with page-locked host batches in and the loss out to
+  page-locked host memory inside the timed region (``e2e``), the fused-kernel
   roofline against a live-measured FP32 FFMA peak, the clocks seen during the timed region
   and a CPU baseline (the torch-CPU port of the same algorithm, rank 0, N=1 only).
 * ``--impl reference``: the reference's JAX path cannot be installed here, so rank 0 times
@@ -352,32 +353,46 @@ def run_b200(args) -> None:
     fwd_ms = statistics.median(e[0].elapsed_time(e[1]) for e in kev)
     bwd_ms = statistics.median(e[2].elapsed_time(e[3]) for e in kev)
 
-    # ---- end to end through the public API: pinned host batches, H2D + step + D2H loss
+    # ---- end to end through the public API: pinned host batches in, the loss out to pinned
+    # host memory, both inside the timed region.  A second train step with host_loss=True
+    # (same initial parameters): one staging kernel reads each page-locked batch
+    # (nc_stage_from_host), the loss kernel stores the loss into a page-locked host scalar.
     x_host = torch.tensor(xs.reshape(nb, BATCH, -1)).pin_memory()
     y_host = torch.tensor(ys).pin_memory()
-    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    e2e_runner = nc.trainer.VNNTrainStep(
+        topo, nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev)), BATCH,
+        lr=LR, in_shapes=((8, 1),) * 3, process_group=pg, exchange=args.exchange, conv=args.conv,
+        spatial_mask=spec, host_loss=True)
+    if not args.no_graph:
+        e2e_runner.load_batch(x_host[0], y_host[0])
+        e2e_runner.capture()
+    for i in range(args.warmup):
+        e2e_runner.step(x_host[i % nb], y_host[i % nb])
     eev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     for i in range(K):
         l2_flush.fill_(float(i))
         eev[i][0].record()
-        loss = runner.step(x_host[i % nb], y_host[i % nb])
-        loss_host.copy_(loss, non_blocking=True)
+        loss = e2e_runner.step(x_host[i % nb], y_host[i % nb])   # loss: page-locked host scalar
         eev[i][1].record()
     torch.cuda.synchronize()
     barrier()
+    assert float(loss) == float(loss)                             # read on the host after the sync
     e2e_sp = spread([a.elapsed_time(b) for a, b in eev])
     e2e_ms = e2e_sp["median"]
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if pg is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
-    bad = torch.tensor([runner.exchange_status()], dtype=torch.int32, device=dev)
+    bad = torch.tensor([max(runner.exchange_status(), e2e_runner.exchange_status())], dtype=torch.int32,
+                       device=dev)
     if pg is not None:
         dist.all_reduce(bad, op=dist.ReduceOp.MAX)    # every rank takes the same exit
     if int(bad.item()) != 0:
         runner.graph = None
+        e2e_runner.graph = None
         raise RuntimeError("NVLink gradient exchange: a peer timed out during the run")
     h2d = x_host[0].numel() * 4 + y_host[0].numel() * 4
 
@@ -443,6 +458,7 @@ def run_b200(args) -> None:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     runner.release()                # graphs holding NCCL calls and the IPC maps go first
+    e2e_runner.release()
     torch.cuda.synchronize()
     if pg is not None:
         dist.barrier()

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define NC_ABI_VERSION 6
+#define NC_ABI_VERSION 7
 
 typedef enum nc_status {
   NC_OK = 0,
@@ -238,13 +238,35 @@ nc_status nc_codd_states(const nc_topo* topo, const void* d_plan, const float* s
 
 /* ---- losses and update ----------------------------------------------------------------- */
 
-/* MSE over batch*n values: loss[0] = mean((out-y)^2); g_out = d loss / d out. */
+/* MSE over batch*n values: loss[0] = mean((out-y)^2); g_out = d loss / d out.
+   `loss` (both losses) may be device memory or page-locked host memory mapped for the
+   device, which the kernel then writes directly (no separate device-to-host copy);
+   pageable host memory is refused with NC_ERR_INVALID before any launch. */
 nc_status nc_mse_loss(const float* out, const float* targets, int32_t batch, int32_t n,
                       float* loss, float* g_out, void* stream);
 
 /* Mean softmax cross-entropy over `batch` rows of `n` logits with int32 labels. */
 nc_status nc_softmax_ce_loss(const float* logits, const int32_t* labels, int32_t batch,
                              int32_t n, float* loss, float* g_logits, void* stream);
+
+/*
+ * Batch staging without the copy engine (no counterpart in the reference): copies `nseg`
+ * (1..NC_MAX_STAGE_SEGS) byte ranges into device buffers with one kernel that reads the
+ * sources directly.  Every source must be page-locked host memory mapped for the device
+ * (cudaHostAlloc, or cudaHostRegister with mapping; device memory works too), checked with
+ * cudaPointerGetAttributes before the launch: pageable memory is refused with
+ * NC_ERR_INVALID.  Sizes and addresses are multiples of 4 bytes.  A training step's batch
+ * of a few KB costs about 9 us per cudaMemcpyAsync on the GPU timeline; one such kernel
+ * takes the place of the step's input copies.  Stream-ordered: the sources must stay
+ * unchanged until the stream has run the kernel.
+ */
+#define NC_MAX_STAGE_SEGS 4
+typedef struct nc_stage_seg {
+  void* dst;          /* device buffer                                   */
+  const void* src;    /* page-locked, device-mapped host memory (or device) */
+  size_t bytes;
+} nc_stage_seg;
+nc_status nc_stage_from_host(const nc_stage_seg* segs, int32_t nseg, void* stream);
 
 /* In-place SGD: params[i] -= lr * grads[i]  (lr read from host scalar). */
 nc_status nc_sgd_update(float* params, const float* grads, int64_t n, float lr, void* stream);

@@ -78,6 +78,7 @@ __global__ void universe_embed_bwd_ports_kernel(Geo g, UniWindow wn, const int32
                                                 const float* cell, const uint8_t* io, nc_codd codd,
                                                 const float* gout, float* guwin, float* gcell, int B);
 __global__ void mse_kernel(const float* o, const float* y, int n, float* loss, float* g);
+__global__ void stage_copy_kernel(StageSegs s);
 __global__ void softmax_ce_kernel(const float* x, const int32_t* lab, int batch, int n,
                                   float* loss, float* g);
 __global__ void sgd_kernel(float* p, const float* gr, int64_t n, float lr);
@@ -128,6 +129,30 @@ static nc_status check_codd(const nc_codd* c) {
   if (reinterpret_cast<uintptr_t>(c->temperature_dev) % 4 != 0)
     return set_error(NC_ERR_INVALID, "codd temperature_dev is not 4-byte aligned");
   return NC_OK;
+}
+
+// The device address of `p` when the device can access it: device memory, managed memory,
+// or page-locked host memory that is mapped into the device's address space (cudaHostAlloc,
+// cudaHostRegister with mapping; under unified addressing the same pointer).  Anything else
+// (pageable host memory, unknown pointers) is refused on the host, before any launch.
+static nc_status device_address(const void* p, const char* name, const void** dev) {
+  if (!p) return set_error(NC_ERR_INVALID, "%s is null", name);
+  cudaPointerAttributes at;
+  cudaError_t e = cudaPointerGetAttributes(&at, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(NC_ERR_INVALID, "%s: not an address CUDA knows (%s)", name, cudaGetErrorName(e));
+  }
+  if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) {
+    *dev = p;
+    return NC_OK;
+  }
+  if (at.type == cudaMemoryTypeHost && at.devicePointer) {
+    *dev = at.devicePointer;
+    return NC_OK;
+  }
+  return set_error(NC_ERR_INVALID, "%s is pageable host memory or not mapped for the device; "
+                   "pass device memory or page-locked host memory", name);
 }
 
 static nc_status check_ptr(const void* p, const char* name) {
@@ -800,7 +825,13 @@ nc_status nc_mse_loss(const float* out, const float* targets, int32_t batch, int
   NC_CHECK(check_ptr(targets, "targets"));
   const int64_t total = (int64_t)batch * n;
   if (total > 0x7fffffff) return set_error(NC_ERR_INVALID, "loss too large");
-  mse_kernel<<<1, 1024, 0, as_stream(stream)>>>(out, targets, (int)total, loss, g_out);
+  float* lossd = nullptr;
+  if (loss) {
+    const void* d = nullptr;
+    NC_CHECK(device_address(loss, "loss", &d));
+    lossd = const_cast<float*>(static_cast<const float*>(d));
+  }
+  mse_kernel<<<1, 1024, 0, as_stream(stream)>>>(out, targets, (int)total, lossd, g_out);
   NC_CHECK(launch_check("mse_kernel launch"));
   clear_error();
   return NC_OK;
@@ -811,8 +842,45 @@ nc_status nc_softmax_ce_loss(const float* logits, const int32_t* labels, int32_t
   if (batch <= 0 || n <= 0) return set_error(NC_ERR_INVALID, "bad loss shape (%d, %d)", batch, n);
   NC_CHECK(check_ptr(logits, "logits"));
   NC_CHECK(check_ptr(labels, "labels"));
-  softmax_ce_kernel<<<1, 1024, 0, as_stream(stream)>>>(logits, labels, batch, n, loss, g_logits);
+  float* lossd = nullptr;
+  if (loss) {
+    const void* d = nullptr;
+    NC_CHECK(device_address(loss, "loss", &d));
+    lossd = const_cast<float*>(static_cast<const float*>(d));
+  }
+  softmax_ce_kernel<<<1, 1024, 0, as_stream(stream)>>>(logits, labels, batch, n, lossd, g_logits);
   NC_CHECK(launch_check("softmax_ce_kernel launch"));
+  clear_error();
+  return NC_OK;
+}
+
+nc_status nc_stage_from_host(const nc_stage_seg* segs, int32_t nseg, void* stream) {
+  if (!segs || nseg < 1 || nseg > NC_MAX_STAGE_SEGS)
+    return set_error(NC_ERR_INVALID, "nc_stage_from_host takes 1..%d segments, got %d", NC_MAX_STAGE_SEGS, nseg);
+  StageSegs s;
+  memset(&s, 0, sizeof(s));
+  size_t most = 0;
+  for (int k = 0; k < nseg; ++k) {
+    const nc_stage_seg& g = segs[k];
+    if (g.bytes % 4 != 0 || reinterpret_cast<uintptr_t>(g.dst) % 4 != 0 ||
+        reinterpret_cast<uintptr_t>(g.src) % 4 != 0)
+      return set_error(NC_ERR_INVALID, "segment %d: sizes and addresses must be multiples of 4 bytes", k);
+    const void* dsrc = nullptr;
+    const void* ddst = nullptr;
+    NC_CHECK(device_address(g.src, "segment source", &dsrc));
+    NC_CHECK(device_address(g.dst, "segment destination", &ddst));
+    s.src[k] = dsrc;
+    s.dst[k] = const_cast<void*>(ddst);
+    s.bytes[k] = g.bytes;
+    if (g.bytes > most) most = g.bytes;
+  }
+  s.n = nseg;
+  if (most == 0) return NC_OK;
+  const size_t units = (most + 15) / 16;
+  unsigned bx = (unsigned)((units + 255) / 256);
+  if (bx > 64) bx = 64;
+  stage_copy_kernel<<<dim3(bx, nseg), 256, 0, as_stream(stream)>>>(s);
+  NC_CHECK(launch_check("stage_copy_kernel launch"));
   clear_error();
   return NC_OK;
 }

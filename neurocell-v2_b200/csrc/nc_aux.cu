@@ -216,6 +216,26 @@ __device__ float block_sum(float v, float* red) {
 }
 
 // MSE (trainer.py:57-61): loss = mean((o - y)^2), g = 2 (o - y) / n.  One CTA.
+// Batch staging: byte ranges from page-locked, device-mapped host memory into device
+// buffers, one segment per blockIdx.y; 16-byte accesses when a segment allows them.
+__global__ void stage_copy_kernel(StageSegs s) {
+  const int k = blockIdx.y;
+  if (k >= s.n) return;
+  const size_t nb = s.bytes[k];
+  const char* src = static_cast<const char*>(s.src[k]);
+  char* dst = static_cast<char*>(s.dst[k]);
+  const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x, step = (size_t)gridDim.x * blockDim.x;
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | nb) & 15) == 0) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    for (size_t i = i0; i < nb / 16; i += step) d4[i] = s4[i];
+  } else {
+    const uint32_t* s1 = reinterpret_cast<const uint32_t*>(src);
+    uint32_t* d1 = reinterpret_cast<uint32_t*>(dst);
+    for (size_t i = i0; i < nb / 4; i += step) d1[i] = s1[i];
+  }
+}
+
 __global__ void mse_kernel(const float* __restrict__ o, const float* __restrict__ y, int n,
                            float* __restrict__ loss, float* __restrict__ g) {
   __shared__ float red[32];

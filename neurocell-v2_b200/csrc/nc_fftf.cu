@@ -157,22 +157,44 @@ __device__ __forceinline__ void pixel_offsets(const Geo& g, int tid, int poff[kP
   }
 }
 
+// Warp sums of eight values by a reduce-scatter butterfly: exchanging half of the values
+// with lane ^ 16, then half of the rest with lane ^ 8, then one with lane ^ 4, leaves each
+// lane the sum over 8 lanes of value k = 4 b4 + 2 b3 + b2 (b_i = bit i of the lane); two
+// more xor steps (2, 1) complete it over the warp.  9 shuffles instead of 40, fixed order;
+// on return every lane of quad k (lanes 4k' .. 4k'+3 with those bits) holds warp sum k.
+__device__ __forceinline__ float warp_reduce8(const float v[8], int lane) {
+  const bool b4 = (lane & 16) != 0, b3 = (lane & 8) != 0, b2 = (lane & 4) != 0;
+  float a[4], c[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float keep = b4 ? v[i + 4] : v[i], send = b4 ? v[i] : v[i + 4];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float keep = b3 ? a[i + 2] : a[i], send = b3 ? a[i] : a[i + 2];
+    c[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float r = (b2 ? c[1] : c[0]) + __shfl_xor_sync(0xffffffffu, b2 ? c[0] : c[1], 4);
+  r += __shfl_xor_sync(0xffffffffu, r, 2);
+  r += __shfl_xor_sync(0xffffffffu, r, 1);
+  return r;
+}
+
 // Sum of eight per-thread values over the 1024-thread CTA, broadcast to every thread, in a
-// fixed order: each warp's sums go to half `par` of `red` (2 x (8 x 32 + 8) floats); after a
-// barrier warp k < 8 adds value k over the 32 warps; after a second barrier every thread
-// reads the eight sums.  Alternating halves make a barrier before the writes unnecessary:
-// a thread writes half `par` again only after the barriers of the next call, which every
-// thread reaches after its reads of this call.  Callers flip `par` after each call.
+// fixed order: each warp's sums (warp_reduce8) go to half `par` of `red` (2 x (8 x 32 + 8)
+// floats); after a barrier warp k < 8 adds value k over the 32 warps; after a second barrier
+// every thread reads the eight sums.  Alternating halves make a barrier before the writes
+// unnecessary: a thread writes half `par` again only after the barriers of the next call,
+// which every thread reaches after its reads of this call.  Callers flip `par` after each
+// call.
 constexpr int kRedHalf = 8 * 32 + 8;
 __device__ __forceinline__ void block_sum8(float v[8], float* red, int& par) {
   static_assert(kThreadsF / 32 == 32, "32 warp partials");
   float* h = red + par * kRedHalf;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) v[k] = warp_sum(v[k]);
-  if (lane == 0)
-#pragma unroll
-    for (int k = 0; k < 8; ++k) h[k * 32 + w] = v[k];
+  const float r = warp_reduce8(v, lane);
+  if ((lane & 3) == 0) h[(lane >> 2) * 32 + w] = r;   // lane 4k holds value k
   __syncthreads();
   if (w < 8) {
     const float t = warp_sum(h[w * 32 + lane]);

@@ -20,6 +20,14 @@ struct StepParams {           // pre-step fusion output (neurocell/params.py:104
                               // kernel, set to 1 when a kernel's bounded wait gives up
 };
 
+// Segments of one nc_stage_from_host call (device addresses).
+struct StageSegs {
+  void* dst[NC_MAX_STAGE_SEGS];
+  const void* src[NC_MAX_STAGE_SEGS];
+  size_t bytes[NC_MAX_STAGE_SEGS];
+  int n;
+};
+
 struct FwdArgs {
   Geo g;
   StepParams sp;

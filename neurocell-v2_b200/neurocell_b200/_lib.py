@@ -12,7 +12,7 @@ import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libneurocell_b200.so")
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 NC_OK, NC_ERR_INVALID, NC_ERR_WORKSPACE, NC_ERR_UNSUPPORTED, NC_ERR_CUDA = 0, 1, 2, 3, 4
 NC_PAD = {"VALID": 0, "SAME": 1, "CIRCULAR": 2}
@@ -30,7 +30,7 @@ EXPORTED = (
     "nc_dp_alloc", "nc_dp_free", "nc_ipc_get", "nc_ipc_open", "nc_ipc_close",
     "nc_dp_allreduce_sgd", "nc_dp_status", "nc_launch_count", "nc_conv_path",
     "nc_vnn_forward_universe", "nc_vnn_backward_universe", "nc_universe_embed_forward",
-    "nc_universe_embed_backward", "nc_workspace_status", "nc_dp_reset",
+    "nc_universe_embed_backward", "nc_workspace_status", "nc_dp_reset", "nc_stage_from_host",
 )
 NC_DP_MAX_RANKS = 8
 NC_IPC_HANDLE_BYTES = 64
@@ -53,6 +53,13 @@ class NcTopo(ctypes.Structure):
 class NcCodd(ctypes.Structure):
     _fields_ = [("mode", ctypes.c_int32), ("temperature", ctypes.c_float),
                 ("active_threshold", ctypes.c_float), ("temperature_dev", ctypes.c_void_p)]
+
+
+class NcStageSeg(ctypes.Structure):
+    _fields_ = [("dst", ctypes.c_void_p), ("src", ctypes.c_void_p), ("bytes", ctypes.c_size_t)]
+
+
+NC_MAX_STAGE_SEGS = 4
 
 
 _vp, _sz, _i32, _u32, _i64, _f32 = (ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32,
@@ -97,6 +104,7 @@ _SIGS = {
     "nc_conv_path": (_i32, [_TP]),
     "nc_workspace_status": (_i32, [_vp, ctypes.POINTER(_i32), _vp]),
     "nc_dp_reset": (_i32, [_vp, _vp, _sz, _vp]),
+    "nc_stage_from_host": (_i32, [ctypes.c_void_p, _i32, _vp]),
 }
 
 _lib = None

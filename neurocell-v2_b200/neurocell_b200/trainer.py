@@ -197,9 +197,14 @@ class VNNTrainStep:
     ``"nccl"`` all-reduces the packed gradient with the process group and then runs the SGD
     kernel; ``"nvlink"`` runs one kernel that sums the ranks' gradients over NVLink peer
     memory and applies SGD (:class:`NVLinkExchange`).  ``step(x, y)`` copies the batch into
-    the static input buffers (host tensors: from pinned memory, asynchronously) and returns
-    the device loss.  ``capture()`` records the launch sequence into a CUDA graph.  Every
-    kernel of the step except NCCL's comes from ``libneurocell_b200.so``.
+    the static input buffers and returns the loss.  Page-locked host batches are read by one
+    staging kernel (``nc_stage_from_host``) instead of two copy-engine transfers (each costs
+    about 9 us on the GPU timeline at these sizes); other host tensors go through
+    ``copy_``.  With ``host_loss=True`` the loss kernel writes the loss straight into a
+    page-locked host scalar, returned by ``step()`` and valid once the stream has reached
+    the end of the step (``torch.cuda.synchronize()`` or an event); otherwise ``step()``
+    returns the device loss.  ``capture()`` records the launch sequence into a CUDA graph.
+    Every kernel of the step except NCCL's comes from ``libneurocell_b200.so``.
     """
 
     def __init__(self, topology, params: VNNParams, batch_size: int, lr: float = 1e-2,
@@ -207,7 +212,8 @@ class VNNTrainStep:
                  hard_pin_io: bool = False, gated_filters: bool = False,
                  codd_mode: str = "continuous", state_temperature: float = 1.0,
                  active_threshold: float = 0.6, in_shapes=None, process_group=None,
-                 exchange: str = "nccl", conv: str = "auto", spatial_mask=None):
+                 exchange: str = "nccl", conv: str = "auto", spatial_mask=None,
+                 host_loss: bool = False):
         import ctypes
         from . import _lib
         from .params import check_codd_mode
@@ -272,6 +278,9 @@ class VNNTrainStep:
         self.out = torch.empty((self.B, self.plan.n_out), dtype=torch.float32, device=dev)
         self.g_out = torch.empty_like(self.out)
         self.loss = torch.zeros((), dtype=torch.float32, device=dev)
+        # host_loss: the loss kernel stores into this page-locked scalar (device-mapped)
+        self.loss_host = torch.zeros((), dtype=torch.float32).pin_memory() if host_loss else None
+        self._stage = (_lib.NcStageSeg * 2)()
         self.codd = ops._codd(codd_mode, state_temperature, active_threshold)
         # tau lives on the device so captured graphs replay with the current temperature
         self.tau_dev = torch.full((1,), float(state_temperature), dtype=torch.float32, device=dev)
@@ -308,7 +317,8 @@ class VNNTrainStep:
 
     def _launch(self, loss_out: torch.Tensor | None = None) -> None:
         c, lib, P = self.ctypes, self.lib, ops._ptr
-        loss_t = self.loss if loss_out is None else loss_out
+        loss_t = loss_out if loss_out is not None else (self.loss_host if self.loss_host is not None
+                                                          else self.loss)
         st = ops._stream(self.device)
         n0 = lib.nc_launch_count()
         t = c.byref(self.plan.topo)
@@ -342,6 +352,16 @@ class VNNTrainStep:
         self._launches = int(lib.nc_launch_count() - n0)
 
     def load_batch(self, x: torch.Tensor, y: torch.Tensor) -> None:
+        if (not x.is_cuda and not y.is_cuda and x.dtype == self.x.dtype and y.dtype == self.y.dtype
+                and x.numel() == self.x.numel() and y.numel() == self.y.numel()
+                and x.is_contiguous() and y.is_contiguous() and x.is_pinned() and y.is_pinned()):
+            # page-locked host batch: one staging kernel reads both tensors
+            sg = self._stage
+            sg[0].dst, sg[0].src, sg[0].bytes = self.x.data_ptr(), x.data_ptr(), 4 * x.numel()
+            sg[1].dst, sg[1].src, sg[1].bytes = self.y.data_ptr(), y.data_ptr(), 4 * y.numel()
+            self._lib.check(self.lib.nc_stage_from_host(sg, 2, ops._stream(self.device)),
+                            "nc_stage_from_host")
+            return
         self.x.copy_(x.reshape(self.B, -1), non_blocking=True)
         self.y.copy_(y.reshape(self.y.shape), non_blocking=True)
 
@@ -352,7 +372,7 @@ class VNNTrainStep:
             self.graph.replay()
         else:
             self._launch()
-        return self.loss
+        return self.loss if self.loss_host is None else self.loss_host
 
     def capture(self) -> None:
         """Records one step into a CUDA graph (the gradient exchange included when data

@@ -358,3 +358,58 @@ def test_five_step_sgd_trajectory_matches_oracle():
     rc = np.linalg.norm(q.cell_params.cpu().numpy() - c) / np.linalg.norm(c)
     rf = np.linalg.norm(q.greens_filters.cpu().numpy() - f) / np.linalg.norm(f)
     assert rc <= 1e-5 and rf <= 1e-5, (rc, rf)
+
+
+def test_stage_from_host_copies_pinned_batches_and_refuses_pageable_memory():
+    """nc_stage_from_host: page-locked host tensors land in device buffers bit for bit (16-
+    and 4-byte paths); a pageable source is refused on the host with NC_ERR_INVALID before
+    any launch."""
+    import ctypes
+    from neurocell_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    a = torch.randn(3072).pin_memory()
+    b = torch.arange(1001, dtype=torch.int32).pin_memory()        # 4004 bytes: 4-byte path
+    da = torch.empty(3072, device=dev)
+    db = torch.empty(1001, dtype=torch.int32, device=dev)
+    segs = (_lib.NcStageSeg * 2)()
+    segs[0].dst, segs[0].src, segs[0].bytes = da.data_ptr(), a.data_ptr(), 4 * a.numel()
+    segs[1].dst, segs[1].src, segs[1].bytes = db.data_ptr(), b.data_ptr(), 4 * b.numel()
+    st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(lib.nc_stage_from_host(segs, 2, st), "nc_stage_from_host")
+    torch.cuda.synchronize()
+    assert torch.equal(da.cpu(), a) and torch.equal(db.cpu(), b)
+    pageable = torch.randn(64)
+    assert not pageable.is_pinned()
+    bad = (_lib.NcStageSeg * 1)()
+    bad[0].dst, bad[0].src, bad[0].bytes = da.data_ptr(), pageable.data_ptr(), 256
+    assert lib.nc_stage_from_host(bad, 1, st) == _lib.NC_ERR_INVALID
+    assert b"pageable" in lib.nc_last_error()
+
+
+def test_host_loss_train_step_matches_device_loss_step():
+    """VNNTrainStep(host_loss=True) with page-locked batches (staging kernel, loss stored into
+    page-locked host memory) trains exactly like the device-loss step, eager and graph."""
+    cell, filt, xs, ys = _alu(3, 32, 12)
+    dev = torch.device("cuda:0")
+    topo = nc.ChipTopology2D.alu_chip()
+
+    def runner(host_loss):
+        p = nc.VNNParams(torch.tensor(cell, device=dev), torch.tensor(filt, device=dev))
+        return nc.trainer.VNNTrainStep(topo, p, 32, lr=1e-2, in_shapes=((8, 1),) * 3,
+                                       host_loss=host_loss)
+    xh = torch.tensor(xs).pin_memory()
+    yh = torch.tensor(ys).pin_memory()
+    xd, yd = xh.to(dev), yh.to(dev)
+    ref, hst, hg = runner(False), runner(True), runner(True)
+    hg.load_batch(xh[0], yh[0])
+    hg.capture()
+    for i in range(3):
+        l_ref = float(ref.step(xd[i], yd[i]))
+        l_h = hst.step(xh[i], yh[i])
+        l_g = hg.step(xh[i], yh[i])
+        assert not l_h.is_cuda and l_h.is_pinned()
+        torch.cuda.synchronize()
+        assert float(l_h) == l_ref and float(l_g) == l_ref
+    torch.cuda.synchronize()
+    assert torch.equal(hst.flat, ref.flat) and torch.equal(hg.flat, ref.flat)
