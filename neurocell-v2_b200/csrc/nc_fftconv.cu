@@ -24,6 +24,8 @@
 // (kernels_pallas.py:740-837).
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include "nc_common.cuh"
 #include "nc_errors.h"
 #include "nc_fft.cuh"
@@ -60,12 +62,52 @@ struct Planes {
   const float4* coef;
 };
 
-// Element `off` of plane (b, m) as the row pass reads it (see Planes::coef).
-__device__ __forceinline__ float plane_in(const Planes& a, int b, int m, size_t off) {
-  const float v = a.ptr[(size_t)b * a.sstride + off];
-  if (!a.coef) return v * a.scale;
-  const float4 k = a.coef[(size_t)b * a.ms + m];
-  return k.x * (v - k.y - a.zh[(size_t)b * a.zstride + off] * k.z) * a.scale;
+// Where one line of a row pass lives: the offsets of its row in a.ptr for sample 2g (or g)
+// and, on packed lines, sample 2g+1 (o[1] = -1 when that sample does not exist), the same
+// rows in a.zh, and the standardisation-adjoint coefficients of those planes (rows_fwd with
+// a.coef).  A CTA computes them once per line (line_refs), so its element loops do no
+// index divisions.
+struct LineRef {
+  long long o[2];
+  long long z[2];
+  float4 k[2];
+};
+constexpr int kLineRefF2 = sizeof(LineRef) / sizeof(float2);   // float2 words per LineRef
+
+__device__ __forceinline__ void line_refs(const Planes& a, int line0, int nl, LineRef* refs, int tid,
+                                          int nt) {
+  for (int l = tid; l < nl; l += nt) {
+    const int line = line0 + l;
+    const int u = line / a.rows, r = line - u * a.rows;
+    const int gs = u / a.ms, m = u - gs * a.ms;
+    const int b1 = a.pack ? 2 * gs : gs;
+    const size_t off = (size_t)m * a.plane + (size_t)r * a.rs;
+    LineRef R;
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int b = b1 + s;
+      const bool ok = s == 0 || (a.pack && b < a.nsamp);
+      R.o[s] = ok ? (long long)((size_t)b * a.sstride + off) : -1;
+      R.z[s] = (ok && a.coef) ? (long long)((size_t)b * a.zstride + off) : 0;
+      float4 k = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ok && a.coef) {
+        k = a.coef[(size_t)b * a.ms + m];
+        k.x *= a.scale;
+      }
+      R.k[s] = k;
+    }
+    refs[l] = R;
+  }
+}
+
+// Element e of sample s of a line as the row pass reads it (COEF: a.coef is set, see
+// Planes::coef; line_refs folds a.scale into k.x).
+template <bool COEF>
+__device__ __forceinline__ float line_in(const Planes& a, const LineRef& R, int s, int e) {
+  const float v = a.ptr[R.o[s] + e];
+  if (!COEF) return v * a.scale;
+  const float4 k = R.k[s];
+  return k.x * (v - k.y - a.zh[R.z[s] + e] * k.z);
 }
 
 __device__ __forceinline__ int even_up(int x) { return (x + 1) & ~1; }
@@ -84,6 +126,20 @@ __device__ __forceinline__ void line_elem(int idx, int N, int lgN, int& l, int& 
   }
 }
 
+// line_elem over element pairs (N even): idx runs over N / 2 pairs per line, e is even.
+// Elements e and e + 1 sit next to each other in a line's shared-memory layout
+// (pidx(e + 1) = pidx(e) + 1 for even e).
+template <int RA>
+__device__ __forceinline__ void line_pair(int idx, int N, int lgN, int& l, int& e) {
+  if constexpr (RA > 0) {
+    l = idx / (32 * RA);
+    e = 2 * (idx - l * (32 * RA));
+  } else {
+    l = idx >> (lgN - 1);
+    e = 2 * (idx & ((N >> 1) - 1));
+  }
+}
+
 // Variants of the transform kernels: RA = N / 64 (2, 4, 8) specialises the radix-R stage that
 // runs on global memory; RA = -1 chooses at run time between that stage (any R) and the
 // shared-memory plan (used for N = 1024: measured faster than the radix-16
@@ -94,99 +150,100 @@ __device__ __forceinline__ void line_elem(int idx, int N, int lgN, int& l, int& 
 constexpr int fft_ctas(int RA, bool heavy = false) { return RA == 0 ? 1 : (RA < 0 || heavy) ? 4 : 5; }
 
 // Forward row transforms of real planes -> dst (lines, N) complex.  For N > 64 (RA = N/64)
-// the radix-R stage reads the planes directly (fft::fwd_a_global).
+// the radix-R stage reads the planes directly (fft::fwd_a_global).  Dynamic shared memory:
+// L line references, the plan's twiddles, L lines (rows_smem).
 template <int RA>
 __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_fwd_kernel(Planes a, float2* __restrict__ dst,
                                                                 int N, const float2* __restrict__ tw,
                                                                 int L) {
-  extern __shared__ float2 sm[];
+  extern __shared__ __align__(16) float2 sm[];
   const int TN = fft::plan_twiddle_len(N);
-  float2* stw = sm;
-  float2* s = sm + even_up(TN);
+  LineRef* refs = reinterpret_cast<LineRef*>(sm);
+  float2* stw = sm + kLineRefF2 * L;
+  float2* s = stw + even_up(TN);
   const int LS = line_stride(N), lgN = fft::ilog2(N);
   const int total = a.units * a.rows;
   const int line0 = blockIdx.x * L;
   const int nl = min(L, total - line0);
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
-  if (RA > 0 || (RA < 0 && fft::a_global(N))) {
-    __syncthreads();
+  line_refs(a, line0, nl, refs, tid, nt);
+  __syncthreads();
+  // the transform, compiled once with and once without the standardisation adjoint on the
+  // loads (a.coef is the same for the whole launch)
+  auto run = [&](auto with_coef) {
+    constexpr bool kCoef = decltype(with_coef)::value;
     auto ld = [&](int l, int e) -> float2 {
       if (e >= a.cols) return make_float2(0.f, 0.f);
-      const int line = line0 + l;
-      const int u = line / a.rows, r = line - u * a.rows;
-      const int gs = u / a.ms, m = u - gs * a.ms;
-      const int b1 = a.pack ? 2 * gs : gs;
-      const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
-      const float re = plane_in(a, b1, m, off);
-      const float im = (a.pack && b1 + 1 < a.nsamp) ? plane_in(a, b1 + 1, m, off) : 0.f;
+      const LineRef& R = refs[l];
+      const float re = line_in<kCoef>(a, R, 0, e);
+      const float im = R.o[1] >= 0 ? line_in<kCoef>(a, R, 1, e) : 0.f;
       return make_float2(re, im);
     };
-    if constexpr (RA > 0) fft::fwd_a_global<RA, false>(s, nl, 0, LS, stw, tid, nt, ld);
-    else fft::fwd_a_global_plan<false>(s, nl, 0, LS, N, stw, tid, nt, ld);
-  } else {
+    if (RA > 0 || (RA < 0 && fft::a_global(N))) {
+      if constexpr (RA > 0) fft::fwd_a_global<RA, false>(s, nl, 0, LS, stw, tid, nt, ld);
+      else fft::fwd_a_global_plan<false>(s, nl, 0, LS, N, stw, tid, nt, ld);
+    } else {
 #pragma unroll 4
-    for (int idx = tid; idx < nl * N; idx += nt) {
-      int l, e;
-      line_elem<RA>(idx, N, lgN, l, e);
-      const int line = line0 + l;
-      const int u = line / a.rows, r = line - u * a.rows;
-      const int gs = u / a.ms, m = u - gs * a.ms;
-      float re = 0.f, im = 0.f;
-      if (e < a.cols) {
-        const int b1 = a.pack ? 2 * gs : gs;
-        const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
-        re = plane_in(a, b1, m, off);
-        if (a.pack && b1 + 1 < a.nsamp) im = plane_in(a, b1 + 1, m, off);
+      for (int idx = tid; idx < nl * N; idx += nt) {
+        int l, e;
+        line_elem<RA>(idx, N, lgN, l, e);
+        s[l * LS + pidx(e)] = ld(l, e);
       }
-      s[l * LS + pidx(e)] = make_float2(re, im);
+      fft::transform_lines_plan<false>(s, nl, N, stw, tid, nt);
     }
-    fft::transform_lines_plan<false>(s, nl, N, stw, tid, nt);
-  }
+  };
+  if (a.coef) run(std::true_type{});
+  else run(std::false_type{});
+  // two elements per 16-byte store (lines of even N, 16-byte aligned)
 #pragma unroll 4
-  for (int idx = tid; idx < nl * N; idx += nt) {
+  for (int idx = tid; idx < nl * (N >> 1); idx += nt) {
     int l, e;
-    line_elem<RA>(idx, N, lgN, l, e);
-    __stcs(&dst[(size_t)(line0 + l) * N + e], s[l * LS + pidx(e)]);   // read once
+    line_pair<RA>(idx, N, lgN, l, e);
+    const float2 v0 = s[l * LS + pidx(e)], v1 = s[l * LS + pidx(e) + 1];
+    __stcs(reinterpret_cast<float4*>(&dst[(size_t)(line0 + l) * N + e]), make_float4(v0.x, v0.y, v1.x, v1.y));   // read once
   }
 }
 
 // Inverse row transforms of src (lines, N) -> real planes (re -> sample 2g, im -> 2g+1).
 // For N > 64 (RA = N/64) the radix-R stage writes the planes directly (fft::inv_a_global).
+// Shared memory as rows_fwd_kernel.
 template <int RA>
 __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_inv_kernel(const float2* __restrict__ src,
                                                                 Planes a, int N,
                                                                 const float2* __restrict__ tw,
                                                                 int L) {
-  extern __shared__ float2 sm[];
+  extern __shared__ __align__(16) float2 sm[];
   const int TN = fft::plan_twiddle_len(N);
-  float2* stw = sm;
-  float2* s = sm + even_up(TN);
+  LineRef* refs = reinterpret_cast<LineRef*>(sm);
+  float2* stw = sm + kLineRefF2 * L;
+  float2* s = stw + even_up(TN);
   const int LS = line_stride(N), lgN = fft::ilog2(N);
   const int total = a.units * a.rows;
   const int line0 = blockIdx.x * L;
   const int nl = min(L, total - line0);
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
+  line_refs(a, line0, nl, refs, tid, nt);
+  // two elements per 16-byte load (lines of even N, 16-byte aligned)
 #pragma unroll 4
-  for (int idx = tid; idx < nl * N; idx += nt) {
+  for (int idx = tid; idx < nl * (N >> 1); idx += nt) {
     int l, e;
-    line_elem<RA>(idx, N, lgN, l, e);
-    s[l * LS + pidx(e)] = __ldcs(&src[(size_t)(line0 + l) * N + e]);   // last use
+    line_pair<RA>(idx, N, lgN, l, e);
+    const float4 v = __ldcs(reinterpret_cast<const float4*>(&src[(size_t)(line0 + l) * N + e]));   // last use
+    s[l * LS + pidx(e)] = make_float2(v.x, v.y);
+    s[l * LS + pidx(e) + 1] = make_float2(v.z, v.w);
   }
   if (RA > 0 || (RA < 0 && fft::a_global(N))) {
     __syncthreads();
     const bool keep = a.rowstats != nullptr;   // the row statistics read the lines back
     auto st = [&](int l, int e, float2 v) {
+      if (e < a.cols) {
+        const long long o0 = refs[l].o[0], o1 = refs[l].o[1];
+        a.ptr[o0 + e] = v.x * a.scale;
+        if (o1 >= 0) a.ptr[o1 + e] = v.y * a.scale;
+      }
       if (keep) s[l * LS + pidx(e)] = v;       // in place: the positions this thread read
-      if (e >= a.cols) return;
-      const int line = line0 + l;
-      const int u = line / a.rows, r = line - u * a.rows;
-      const int gs = u / a.ms, m = u - gs * a.ms;
-      const int b1 = a.pack ? 2 * gs : gs;
-      const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
-      a.ptr[(size_t)b1 * a.sstride + off] = v.x * a.scale;
-      if (a.pack && b1 + 1 < a.nsamp) a.ptr[(size_t)(b1 + 1) * a.sstride + off] = v.y * a.scale;
     };
     if constexpr (RA > 0) fft::inv_a_global<RA, false>(s, nl, 0, LS, stw, tid, nt, st);
     else fft::inv_a_global_plan<false>(s, nl, 0, LS, N, stw, tid, nt, st);
@@ -196,14 +253,10 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA)) rows_inv_kernel(con
 #pragma unroll 4
     for (int idx = tid; idx < nl * a.cols; idx += nt) {
       const int l = idx / a.cols, e = idx - l * a.cols;
-      const int line = line0 + l;
-      const int u = line / a.rows, r = line - u * a.rows;
-      const int gs = u / a.ms, m = u - gs * a.ms;
-      const int b1 = a.pack ? 2 * gs : gs;
-      const size_t off = (size_t)m * a.plane + (size_t)r * a.rs + e;
       const float2 v = s[l * LS + pidx(e)];
-      a.ptr[(size_t)b1 * a.sstride + off] = v.x * a.scale;
-      if (a.pack && b1 + 1 < a.nsamp) a.ptr[(size_t)(b1 + 1) * a.sstride + off] = v.y * a.scale;
+      const long long o0 = refs[l].o[0], o1 = refs[l].o[1];
+      a.ptr[o0 + e] = v.x * a.scale;
+      if (o1 >= 0) a.ptr[o1 + e] = v.y * a.scale;
     }
   }
   if (a.rowstats) {
@@ -262,14 +315,20 @@ __host__ __device__ inline int col_line_stride(int N) {
 template <int MODE, int RA>
 __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA, MODE == 2)) cols_kernel(ColArgs a, const float2* __restrict__ tw,
                                                             int C) {
-  extern __shared__ float2 sm[];
+  extern __shared__ __align__(16) float2 sm[];
   const int N = a.Nh;
   const int TN = fft::plan_twiddle_len(N);
   float2* stw = sm;
   float2* s = sm + even_up(TN);
   const int LS = col_line_stride(N), lgC = fft::ilog2(C);
   const int c0 = blockIdx.x * C;
-  const int u = blockIdx.y;
+  int u = blockIdx.y;
+  if (MODE == COL_INV_MULCONJ) {
+    // blockIdx.y runs over the pairs first, so the CTAs in flight share one filter spectrum
+    // (the M spectra together exceed L2); the unit (and output) order stays p * M + m
+    const int pairs = gridDim.y / a.M, m = u / pairs;
+    u = (u - m * pairs) * a.M + m;
+  }
   const int tid = threadIdx.x, nt = blockDim.x;
   const size_t NN = (size_t)a.Nh * a.Nw;
   for (int i = tid; i < TN; i += nt) stw[i] = tw[i];
@@ -904,7 +963,7 @@ int rows_per_cta(int N) {
 
 size_t rows_smem(int N, int L) {
   const int TN = fft::plan_twiddle_len(N);
-  return sizeof(float2) * ((size_t)((TN + 1) & ~1) + (size_t)L * line_stride(N));
+  return sizeof(float2) * ((size_t)kLineRefF2 * L + (size_t)((TN + 1) & ~1) + (size_t)L * line_stride(N));
 }
 
 // Columns per CTA: 8 from 512-point columns on (37 KB of lines at N = 512, six CTAs per
