@@ -265,6 +265,7 @@ static FftCall fft_call(const Prepared& pr, void* ws, const float* inputs, int b
   c.zscr = at<float>(ws, L.zscr);
   c.zhat = at<float>(ws, L.zhat);
   c.rstd_save = at<float>(ws, L.rstd);
+  c.mean_save = at<float>(ws, L.f_mean_save);
   c.xsave = at<float>(ws, L.xsave);
   c.q = at<float2>(ws, L.f_q);
   c.dgacc = at<float2>(ws, L.f_dgacc);

@@ -56,7 +56,8 @@ struct Planes {
   float2* rowstats;   // rows_inv: per stored row (mean, M2) of its `cols` values, or null
   // rows_fwd: with coef set, the pass reads the standardisation adjoint of the planes,
   // coef.x * (v - coef.y - zh * coef.z) per (sample, m) plane, from the planes v and the
-  // standardised planes zh (same layout, sample stride zstride)
+  // forward's raw planes zh (same layout, sample stride zstride; the coefficients fold in
+  // their standardisation, see norm_coef_kernel)
   const float* zh;
   size_t zstride;
   const float4* coef;
@@ -530,7 +531,8 @@ __global__ void field_ring_kernel(Geo g, float* __restrict__ field, const float*
 // the two-stage variance the reference uses for tiled planes (kernels_pallas.py:740-837).
 __global__ void __launch_bounds__(kEpiThreads) plane_stats_rows_kernel(Geo g, const float2* __restrict__ rowstats,
                                                                        float* mean, float* rstd,
-                                                                       float* rstd_save, int t) {
+                                                                       float* rstd_save, float* mean_save,
+                                                                       int t) {
   __shared__ float red[33];
   const int bm = blockIdx.x, b = bm / g.M, m = bm - b * g.M;
   const int rows = g.roi_h;
@@ -552,12 +554,10 @@ __global__ void __launch_bounds__(kEpiThreads) plane_stats_rows_kernel(Geo g, co
     mean[bm] = mu;
     rstd[bm] = rs;
     if (rstd_save) rstd_save[((size_t)b * g.d + t) * g.M + m] = rs;
+    if (mean_save) mean_save[((size_t)b * g.d + t) * g.M + m] = mu;
   }
 }
 
-// ROI epilogue (epilogue.py:28-56): standardise (in place when write_zhat), gate, write the
-// next field's interior and the training residual -- or, in universe mode (uroi != null),
-// the last step's ROI cells.
 // V consecutive floats (V = 4: one 16-byte access; callers guarantee the alignment).
 template <int V>
 __device__ __forceinline__ void ldv(const float* __restrict__ p, float* v) {
@@ -579,9 +579,13 @@ __device__ __forceinline__ void stv(float* __restrict__ p, const float* v) {
   }
 }
 
-// One thread per V consecutive pixels of one sample (V = 4 when P % 4 == 0).
+// ROI epilogue (epilogue.py:28-56): standardise, gate, write the next field's interior and
+// the training residual -- or, in universe mode (uroi != null), the last step's ROI cells.
+// The planes z are only read: a training call keeps them raw and the backward standardises
+// them again from the saved statistics.  One thread per V consecutive pixels of one sample
+// (V = 4 when P % 4 == 0).
 template <int V>
-__global__ void hidden_epi_kernel(Geo g, StepParams sp, float* z, size_t zs, int write_zhat,
+__global__ void hidden_epi_kernel(Geo g, StepParams sp, const float* __restrict__ z, size_t zs,
                                   const float* __restrict__ mean, const float* __restrict__ rstd,
                                   float* __restrict__ field, float* __restrict__ xsave, int t, int B,
                                   int act_id, float slope, float* __restrict__ uroi) {
@@ -593,7 +597,8 @@ __global__ void hidden_epi_kernel(Geo g, StepParams sp, float* z, size_t zs, int
   ldv<V>(sp.broi + p0, bb);
 #pragma unroll
   for (int v = 0; v < V; ++v) { lin[v] = 0.f; act[v] = 0.f; }
-  float* zb = z + (size_t)b * zs + p0;
+  const float* zb = z + (size_t)b * zs + p0;
+#pragma unroll 4
   for (int m = 0; m < g.M; ++m) {
     const float mu = mean[b * g.M + m], rs = rstd[b * g.M + m];
     float zv[V];
@@ -601,11 +606,9 @@ __global__ void hidden_epi_kernel(Geo g, StepParams sp, float* z, size_t zs, int
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       const float zh = (zv[v] - mu) * rs;
-      zv[v] = zh;
       lin[v] += zh;
       if (act_id != NC_ACT_NONE) act[v] += act_fwd(act_id, zh + bb[v], slope);
     }
-    if (write_zhat) stv<V>(zb + (size_t)m * g.P, zv);
   }
   float we[V], se[V], xn[V];
   ldv<V>(sp.weff + p0, we);
@@ -653,44 +656,44 @@ __global__ void port_out_kernel(Geo g, StepParams sp, const int32_t* __restrict_
                                    : act_fwd(g.fact, wo * lin + so * act, g.fslope);
 }
 
-// Training residual of the output step: planes standardised in place.
-__global__ void normalize_kernel(Geo g, float* z, size_t zs, const float* __restrict__ mean,
-                                 const float* __restrict__ rstd, int B) {
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const size_t MP = (size_t)g.M * g.P;
-  if (i >= (size_t)B * MP) return;
-  const int b = (int)(i / MP);
-  const size_t k = i - (size_t)b * MP;
-  const int m = (int)(k / g.P);
-  float* v = z + (size_t)b * zs + k;
-  *v = (*v - mean[b * g.M + m]) * rstd[b * g.M + m];
-}
-
 // ---------------------------------------------------------------------------------------
 // backward epilogues
 // ---------------------------------------------------------------------------------------
 
-// Output-step adjoint at the port cells (kernels_pallas.py:1378-1504): sparse plane
-// gradients (gz must be zero elsewhere) and the port cells' parameter gradients, summed
-// over the batch in sample order.
-__global__ void port_gz_kernel(Geo g, StepParams sp, const int32_t* __restrict__ out_index,
-                               const float* __restrict__ gout, const float* __restrict__ zh_t,
-                               size_t zs, float* __restrict__ gz, float* __restrict__ gsum, int B) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= g.n_out) return;
+// Plane pixel of output port j, or -1 for a border output (universe mode only).
+__device__ __forceinline__ int port_pixel(const Geo& g, const int32_t* __restrict__ out_index, int j) {
   const int idx = out_index[j];
   const int gr_ = idx / g.W, gc_ = idx - (idx / g.W) * g.W;
-  const int p = (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
-  if (gr_ < g.pad_h || gr_ >= g.pad_h + g.roi_h || gc_ < g.pad_w || gc_ >= g.pad_w + g.roi_w) return;
+  if (gr_ < g.pad_h || gr_ >= g.pad_h + g.roi_h || gc_ < g.pad_w || gc_ >= g.pad_w + g.roi_w) return -1;
+  return (gr_ - g.pad_h) * g.roi_w + (gc_ - g.pad_w);
+}
+
+// Output-step adjoint at the port cells (kernels_pallas.py:1378-1504): sparse plane
+// gradients (gz must be zero elsewhere) and the port cells' parameter gradients summed
+// over the batch.  One warp per port, lanes over the samples, then a fixed-order warp sum.
+// z_t: the raw planes of step t, standardised here with the saved statistics.
+__global__ void port_gz_kernel(Geo g, StepParams sp, const int32_t* __restrict__ out_index,
+                               const float* __restrict__ gout, const float* __restrict__ z_t,
+                               size_t zs, const float* __restrict__ mean_save,
+                               const float* __restrict__ rstd_save, int t, float* __restrict__ gz,
+                               float* __restrict__ gsum, int B) {
+  const int j = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (j >= g.n_out) return;                  // whole warps leave together
+  const int p = port_pixel(g, out_index, j);
+  if (p < 0) return;
   const size_t P = (size_t)g.P;
   const float wo = sp.weff[p], so = sp.seff[p], bo = sp.broi[p];
   float gp0 = 0.f, gp1 = 0.f, gp2 = 0.f;
-  for (int b = 0; b < B; ++b) {
+  for (int b = lane; b < B; b += 32) {
     const float go = gout[(size_t)b * g.n_out + j];
-    const float* ZH = zh_t + (size_t)b * zs + p;
+    const float* Z = z_t + (size_t)b * zs + p;
+    const float* mu = mean_save + ((size_t)b * g.d + t) * g.M;
+    const float* rs = rstd_save + ((size_t)b * g.d + t) * g.M;
+    auto zh = [&](int m) { return (Z[m * P] - mu[m]) * rs[m]; };
     float* GZ = gz + (size_t)b * g.M * P + p;
     float lin = 0.f;
-    for (int m = 0; m < g.M; ++m) lin += ZH[m * P];
+    for (int m = 0; m < g.M; ++m) lin += zh(m);
     if (g.fact == NC_ACT_NONE) {
       gp0 += go * lin;
       gp1 += go * (lin + (float)g.M * bo);
@@ -699,7 +702,7 @@ __global__ void port_gz_kernel(Geo g, StepParams sp, const int32_t* __restrict__
       for (int m = 0; m < g.M; ++m) GZ[m * P] = gzh;
     } else {
       float act = 0.f;
-      for (int m = 0; m < g.M; ++m) act += act_fwd(g.fact, ZH[m * P] + bo, g.fslope);
+      for (int m = 0; m < g.M; ++m) act += act_fwd(g.fact, zh(m) + bo, g.fslope);
       float dpre;
       act_fwd_deriv(g.fact, wo * lin + so * act, g.fslope, &dpre);
       const float gpre = go * dpre;
@@ -708,23 +711,66 @@ __global__ void port_gz_kernel(Geo g, StepParams sp, const int32_t* __restrict__
       float db = 0.f;
       for (int m = 0; m < g.M; ++m) {
         float dd;
-        act_fwd_deriv(g.fact, ZH[m * P] + bo, g.fslope, &dd);
+        act_fwd_deriv(g.fact, zh(m) + bo, g.fslope, &dd);
         GZ[m * P] = gpre * (wo + so * dd);
         db += gpre * so * dd;
       }
       gp2 += db;
     }
   }
-  gsum[p] += gp0;
-  gsum[P + p] += gp1;
-  gsum[2 * P + p] += gp2;
+  gp0 = warp_sum(gp0);
+  gp1 = warp_sum(gp1);
+  gp2 = warp_sum(gp2);
+  if (lane == 0) {
+    gsum[p] += gp0;
+    gsum[P + p] += gp1;
+    gsum[2 * P + p] += gp2;
+  }
 }
 
-// Standardisation adjoint per (b, m): gz <- rstd (gz - mean(gz) - zh mean(gz zh)).
-// gzpart (not null): the sums come from hidden_gz_kernel's per-CTA partials (ncta of them,
-// added in CTA order) and the planes are read once.
+// Coefficients of the standardisation adjoint of the output step (see norm_coef_kernel)
+// from the port cells alone: the plane gradients are zero elsewhere.  One warp per (b, m)
+// plane; each port cell counts once (a cell listed twice holds one gradient), lanes over
+// the ports, then a fixed-order warp sum.
+__global__ void port_coef_kernel(Geo g, const int32_t* __restrict__ out_index, const float* __restrict__ gz,
+                                 const float* __restrict__ z_t, size_t zs,
+                                 const float* __restrict__ mean_save, const float* __restrict__ rstd_save,
+                                 int t, int nplanes, float4* __restrict__ coef) {
+  const int bm = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (bm >= nplanes) return;                 // whole warps leave together
+  const int b = bm / g.M, m = bm - b * g.M;
+  const size_t st = ((size_t)b * g.d + t) * g.M + m;
+  const float mu = mean_save[st], rs = rstd_save[st];
+  const float* GZ = gz + (size_t)bm * g.P;
+  const float* Z = z_t + (size_t)b * zs + (size_t)m * g.P;
+  float s1 = 0.f, s2 = 0.f;
+  for (int j = lane; j < g.n_out; j += 32) {
+    const int p = port_pixel(g, out_index, j);
+    if (p < 0) continue;
+    bool first = true;
+    for (int i = 0; i < j && first; ++i) first = out_index[i] != out_index[j];
+    if (!first) continue;
+    const float v = GZ[p];
+    s1 += v;
+    s2 = fmaf(v, (Z[p] - mu) * rs, s2);
+  }
+  s1 = warp_sum(s1);
+  s2 = warp_sum(s2);
+  if (lane == 0) {
+    const float inv_n = 1.0f / (float)g.P;
+    const float c1 = s1 * inv_n, c2 = s2 * inv_n;
+    coef[bm] = make_float4(rs, c1 - mu * rs * c2, rs * c2, 0.f);
+  }
+}
+
+// Standardisation adjoint per (b, m): gz <- rstd (gz - mean(gz) - zh mean(gz zh)), zh the
+// raw planes z_t of step t standardised with the saved statistics.  gzpart (not null): the
+// sums come from hidden_gz_kernel's per-CTA partials (ncta of them, added in CTA order) and
+// the planes are read once.
 __global__ void __launch_bounds__(kStatThreads) norm_bwd_kernel(Geo g, float* __restrict__ gz,
-                                                                 const float* __restrict__ zh_t, size_t zs,
+                                                                 const float* __restrict__ z_t, size_t zs,
+                                                                 const float* __restrict__ mean_save,
                                                                  const float* __restrict__ rstd_save, int t,
                                                                  int nplanes, int vec,
                                                                  const float* __restrict__ gzpart, int ncta) {
@@ -733,7 +779,10 @@ __global__ void __launch_bounds__(kStatThreads) norm_bwd_kernel(Geo g, float* __
   for (int bm = blockIdx.x; bm < nplanes; bm += gridDim.x) {
     const int b = bm / g.M, m = bm - b * g.M;
     float* gp = gz + (size_t)bm * g.P;
-    const float* zp = zh_t + (size_t)b * zs + (size_t)m * g.P;
+    const float* zp = z_t + (size_t)b * zs + (size_t)m * g.P;
+    const float mu = mean_save[((size_t)b * g.d + t) * g.M + m];
+    const float rs = rstd_save[((size_t)b * g.d + t) * g.M + m];
+    auto zh = [&](float z) { return (z - mu) * rs; };
     float s1 = 0.f, s2 = 0.f, u1 = 0.f, u2 = 0.f;
     if (gzpart) {
       for (int k = threadIdx.x; k < ncta; k += blockDim.x) {
@@ -747,43 +796,45 @@ __global__ void __launch_bounds__(kStatThreads) norm_bwd_kernel(Geo g, float* __
         const float4 v = g4[i], w = z4[i];
         s1 += v.x + v.y;
         u1 += v.z + v.w;
-        s2 = fmaf(v.x, w.x, fmaf(v.y, w.y, s2));
-        u2 = fmaf(v.z, w.z, fmaf(v.w, w.w, u2));
+        s2 = fmaf(v.x, zh(w.x), fmaf(v.y, zh(w.y), s2));
+        u2 = fmaf(v.z, zh(w.z), fmaf(v.w, zh(w.w), u2));
       }
     } else {
       for (int p = threadIdx.x; p < g.P; p += blockDim.x) {
         const float v = gp[p];
         s1 += v;
-        s2 = fmaf(v, zp[p], s2);
+        s2 = fmaf(v, zh(zp[p]), s2);
       }
     }
     const float c1 = block_sum(s1 + u1, red) * inv_n;
     const float c2 = block_sum(s2 + u2, red) * inv_n;
-    const float rs = rstd_save[((size_t)b * g.d + t) * g.M + m];
     if (vec) {
       float4* g4 = reinterpret_cast<float4*>(gp);
       const float4* z4 = reinterpret_cast<const float4*>(zp);
       for (int i = threadIdx.x; i < g.P / 4; i += blockDim.x) {
         float4 v = g4[i];
         const float4 w = z4[i];
-        v.x = rs * (v.x - c1 - w.x * c2);
-        v.y = rs * (v.y - c1 - w.y * c2);
-        v.z = rs * (v.z - c1 - w.z * c2);
-        v.w = rs * (v.w - c1 - w.w * c2);
+        v.x = rs * (v.x - c1 - zh(w.x) * c2);
+        v.y = rs * (v.y - c1 - zh(w.y) * c2);
+        v.z = rs * (v.z - c1 - zh(w.z) * c2);
+        v.w = rs * (v.w - c1 - zh(w.w) * c2);
         g4[i] = v;
       }
     } else {
-      for (int p = threadIdx.x; p < g.P; p += blockDim.x) gp[p] = rs * (gp[p] - c1 - zp[p] * c2);
+      for (int p = threadIdx.x; p < g.P; p += blockDim.x) gp[p] = rs * (gp[p] - c1 - zh(zp[p]) * c2);
     }
   }
 }
 
 // Coefficients of the standardisation adjoint gz <- rstd (gz - mean(gz) - zhat mean(gz zhat))
 // from hidden_gz_kernel's per-CTA sums (ncta of them, one warp per plane, lanes over the
-// CTAs in a fixed order); the next row pass applies them while it reads the planes.
+// CTAs in a fixed order); the next row pass applies them while it reads the planes.  With
+// zhat = (z - mu) rstd of the raw planes z the row pass reads, the adjoint is
+// k.x (gz - k.y - z k.z) with k = (rstd, c1 - mu rstd c2, rstd c2), c1 = mean(gz),
+// c2 = mean(gz zhat).
 __global__ void norm_coef_kernel(Geo g, const float* __restrict__ gzpart, int ncta,
-                                 const float* __restrict__ rstd_save, int t, int nplanes,
-                                 float4* __restrict__ coef) {
+                                 const float* __restrict__ mean_save, const float* __restrict__ rstd_save,
+                                 int t, int nplanes, float4* __restrict__ coef) {
   const int bm = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   if (bm >= nplanes) return;                 // whole warps leave together
@@ -797,7 +848,10 @@ __global__ void norm_coef_kernel(Geo g, const float* __restrict__ gzpart, int nc
   if (lane == 0) {
     const float inv_n = 1.0f / (float)g.P;
     const int b = bm / g.M, m = bm - b * g.M;
-    coef[bm] = make_float4(rstd_save[((size_t)b * g.d + t) * g.M + m], s1 * inv_n, s2 * inv_n, 0.f);
+    const size_t st = ((size_t)b * g.d + t) * g.M + m;
+    const float mu = mean_save[st], rs = rstd_save[st];
+    const float c1 = s1 * inv_n, c2 = s2 * inv_n;
+    coef[bm] = make_float4(rs, c1 - mu * rs * c2, rs * c2, 0.f);
   }
 }
 
@@ -830,13 +884,16 @@ __device__ __forceinline__ float warp_sum4(float a, float b, float c, float d, i
   return z;
 }
 
+// z_t: the raw planes of step t, standardised here with the saved statistics.
 // gzpart (not null): the CTA's sums of gz and gz * zhat over its pixels per (b, m) of its
 // chunk, at gzpart[((blockIdx.x * B + b) * M + m) * 2 + {0, 1}] (warp_sum4 over directions
 // m, m+1, then the warps in order), so the standardisation adjoint needs one pass.  `red`
 // in dynamic shared memory holds bc * M * 2 values per warp.
 template <int V>
-__global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__ dx,
-                                 const float* __restrict__ zh_t, size_t zs, float* __restrict__ gz,
+__global__ void __launch_bounds__(256, 4) hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__ dx,
+                                 const float* __restrict__ z_t, size_t zs,
+                                 const float* __restrict__ mean_save, const float* __restrict__ rstd_save,
+                                 int t, float* __restrict__ gz,
                                  float* __restrict__ gpart, int B, int bc, int act_id, float slope,
                                  const float* __restrict__ gy_roi, float* __restrict__ gzpart) {
   extern __shared__ float red[];
@@ -861,7 +918,9 @@ __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__
       gy[v] = !on ? 0.f : gy_roi ? gy_roi[(size_t)b * P + p] : field_grad(g, dx + (size_t)b * FF, r, c);
       lin[v] = 0.f; act[v] = 0.f; dsum[v] = 0.f;
     }
-    const float* ZH = zh_t + (size_t)b * zs + p0;
+    const float* Z = z_t + (size_t)b * zs + p0;
+    const float* mu = mean_save + ((size_t)b * g.d + t) * g.M;
+    const float* rs = rstd_save + ((size_t)b * g.d + t) * g.M;
     float* GZ = gz + (size_t)b * g.M * P + p0;
     for (int m = 0; m < g.M; m += 2) {          // directions m, m+1 (m+1 < M or empty)
       float s[4] = {0.f, 0.f, 0.f, 0.f};
@@ -870,7 +929,10 @@ __global__ void hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__
         if (m + k >= g.M) break;
         float zv[V], gv[V];
         if (on) {
-          ldv<V>(ZH + (size_t)(m + k) * P, zv);
+          ldv<V>(Z + (size_t)(m + k) * P, zv);
+          const float mk = mu[m + k], rk = rs[m + k];
+#pragma unroll
+          for (int v = 0; v < V; ++v) zv[v] = (zv[v] - mk) * rk;
         } else {
 #pragma unroll
           for (int v = 0; v < V; ++v) zv[v] = 0.f;
@@ -1088,16 +1150,16 @@ int plane_vec(const Geo& g, size_t zs) { return (g.P % 4 == 0 && zs % 4 == 0) ? 
 
 // ROI epilogue over all samples (train: xsave; universe mode: uroi); 4 pixels per thread
 // when the planes allow 16-byte accesses.
-nc_status hidden_epi(const Geo& g, const FftCall& c, float* z, size_t zs, int t, int act_id, float slope,
+nc_status hidden_epi(const Geo& g, const FftCall& c, const float* z, size_t zs, int t, int act_id, float slope,
                      float* uroi, cudaStream_t st) {
   const size_t n = (size_t)c.batch * g.P;
   float* xs = (c.train && !uroi) ? c.xsave : nullptr;
   if (plane_vec(g, zs))
     hidden_epi_kernel<4><<<blocks_for(n / 4, kEpiThreads), kEpiThreads, 0, st>>>(
-        g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, xs, t, c.batch, act_id, slope, uroi);
+        g, c.sp, z, zs, c.mean, c.rstd, c.field, xs, t, c.batch, act_id, slope, uroi);
   else
     hidden_epi_kernel<1><<<blocks_for(n, kEpiThreads), kEpiThreads, 0, st>>>(
-        g, c.sp, z, zs, c.train ? 1 : 0, c.mean, c.rstd, c.field, xs, t, c.batch, act_id, slope, uroi);
+        g, c.sp, z, zs, c.mean, c.rstd, c.field, xs, t, c.batch, act_id, slope, uroi);
   return launched("hidden_epi_kernel launch");
 }
 
@@ -1105,8 +1167,8 @@ nc_status hidden_epi(const Geo& g, const FftCall& c, float* z, size_t zs, int t,
 // *ncta: the number of per-CTA sum partials written to c.gzpart for the standardisation
 // adjoint, or 0 when they did not fit the kernel's shared memory (norm_bwd then takes two
 // passes).
-nc_status hidden_gz(const Geo& g, const FftCall& c, const float* zh, size_t zs, int nch, int bc, int act_id,
-                    float slope, const float* gy_roi, int* ncta, cudaStream_t st) {
+nc_status hidden_gz(const Geo& g, const FftCall& c, const float* z, size_t zs, int tz, int nch, int bc,
+                    int act_id, float slope, const float* gy_roi, int* ncta, cudaStream_t st) {
   const size_t red = sizeof(float) * (size_t)bc * g.M * (256 / 32) * 2;
   const bool part = c.gzpart != nullptr && red <= 48 * 1024;
   float* gzp = part ? c.gzpart : nullptr;
@@ -1114,12 +1176,14 @@ nc_status hidden_gz(const Geo& g, const FftCall& c, const float* zh, size_t zs, 
   unsigned grid;
   if (plane_vec(g, zs)) {
     grid = blocks_for((size_t)g.P / 4, 256);
-    hidden_gz_kernel<4><<<dim3(grid, nch), 256, smem, st>>>(g, c.sp, c.dx, zh, zs, c.gz, c.gpart, c.batch,
-                                                            bc, act_id, slope, gy_roi, gzp);
+    hidden_gz_kernel<4><<<dim3(grid, nch), 256, smem, st>>>(g, c.sp, c.dx, z, zs, c.mean_save, c.rstd_save,
+                                                            tz, c.gz, c.gpart, c.batch, bc, act_id, slope,
+                                                            gy_roi, gzp);
   } else {
     grid = blocks_for((size_t)g.P, 256);
-    hidden_gz_kernel<1><<<dim3(grid, nch), 256, smem, st>>>(g, c.sp, c.dx, zh, zs, c.gz, c.gpart, c.batch,
-                                                            bc, act_id, slope, gy_roi, gzp);
+    hidden_gz_kernel<1><<<dim3(grid, nch), 256, smem, st>>>(g, c.sp, c.dx, z, zs, c.mean_save, c.rstd_save,
+                                                            tz, c.gz, c.gpart, c.batch, bc, act_id, slope,
+                                                            gy_roi, gzp);
   }
   *ncta = part ? (int)grid : 0;
   return launched("hidden_gz_kernel launch");
@@ -1222,7 +1286,8 @@ nc_status fft_forward(const FftCall& c, cudaStream_t st) {
     }
     // plane statistics from the row statistics the row pass wrote
     plane_stats_rows_kernel<<<B * g.M, kEpiThreads, 0, st>>>(g, c.rowstats, c.mean, c.rstd,
-                                                             c.train ? c.rstd_save : nullptr, t);
+                                                             c.train ? c.rstd_save : nullptr,
+                                                             c.train ? c.mean_save : nullptr, t);
     NC_CHECK(launched("plane_stats_rows_kernel launch"));
     if (t < g.d - 1) {
       NC_CHECK(hidden_epi(g, c, z, zs, t, g.act, g.slope, nullptr, st));
@@ -1233,11 +1298,6 @@ nc_status fft_forward(const FftCall& c, cudaStream_t st) {
       port_out_kernel<<<blocks_for((size_t)B * g.n_out, 128), 128, 0, st>>>(g, c.sp, c.out_index, z, zs,
                                                                              c.mean, c.rstd, c.out, B);
       NC_CHECK(launched("port_out_kernel launch"));
-      if (c.train) {
-        normalize_kernel<<<blocks_for((size_t)B * M * P, kEpiThreads), kEpiThreads, 0, st>>>(
-            g, z, zs, c.mean, c.rstd, B);
-        NC_CHECK(launched("normalize_kernel launch"));
-      }
     }
   }
   return NC_OK;
@@ -1249,19 +1309,19 @@ nc_status fft_forward(const FftCall& c, cudaStream_t st) {
 // Standardisation adjoint of step t's plane gradients in c.gz: deferred to the next row pass
 // (*pending = true, coefficients in c.ncoef) when hidden_gz_kernel wrote the per-CTA sums
 // (ncta > 0), else applied in place by norm_bwd_kernel (two passes over the planes).
-nc_status norm_adjoint(const FftCall& c, const float* zh, size_t zs, int t, int ncta, bool* pending,
+nc_status norm_adjoint(const FftCall& c, const float* z, size_t zs, int t, int ncta, bool* pending,
                        cudaStream_t st) {
   const Geo& g = c.g;
   const int nplanes = c.batch * g.M;
   if (ncta > 0 && c.ncoef) {
-    norm_coef_kernel<<<blocks_for((size_t)nplanes * 32, 256), 256, 0, st>>>(g, c.gzpart, ncta, c.rstd_save, t,
-                                                                           nplanes, c.ncoef);
+    norm_coef_kernel<<<blocks_for((size_t)nplanes * 32, 256), 256, 0, st>>>(g, c.gzpart, ncta, c.mean_save,
+                                                                           c.rstd_save, t, nplanes, c.ncoef);
     *pending = true;
     return launched("norm_coef_kernel launch");
   }
-  norm_bwd_kernel<<<stat_grid(nplanes), kStatThreads, 0, st>>>(g, c.gz, zh, zs, c.rstd_save, t, nplanes,
-                                                               plane_vec(g, zs), ncta ? c.gzpart : nullptr,
-                                                               ncta);
+  norm_bwd_kernel<<<stat_grid(nplanes), kStatThreads, 0, st>>>(g, c.gz, z, zs, c.mean_save, c.rstd_save, t,
+                                                               nplanes, plane_vec(g, zs),
+                                                               ncta ? c.gzpart : nullptr, ncta);
   *pending = false;
   return launched("norm_bwd_kernel launch");
 }
@@ -1280,27 +1340,37 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
   NC_CUDA_CHECK(cudaMemsetAsync(c.gz, 0, sizeof(float) * B * M * P, st));
 
   // The standardisation adjoint of the planes in c.gz is either applied in place
-  // (norm_bwd_kernel) or left `pending`: its coefficients are in c.ncoef and the row pass
-  // that reads c.gz next applies it (the corrected planes have no other reader).
+  // (norm_bwd_kernel) or left `pending`: its coefficients, folded for the raw planes, are in
+  // c.ncoef and the row pass that reads c.gz next applies it (the corrected planes have no
+  // other reader).
   bool pending = false;
   int pending_t = 0;
 
   // output step: sparse port adjoint (or the universe ROI adjoint), then the
-  // standardisation adjoint
+  // standardisation adjoint (the saved planes are raw; every reader standardises them)
   {
-    const float* zh = c.zhat + (size_t)(g.d - 1) * M * P;
-    int ncta_out = 0;   // the port adjoint writes no partial sums
+    const int tl = g.d - 1;
+    const float* z = c.zhat + (size_t)tl * M * P;
     if (c.guroi) {
-      NC_CHECK(hidden_gz(g, c, zh, zs, nch, bc, g.fact, g.fslope, c.guroi, &ncta_out, st));
+      int ncta_out = 0;
+      NC_CHECK(hidden_gz(g, c, z, zs, tl, nch, bc, g.fact, g.fslope, c.guroi, &ncta_out, st));
       gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
       NC_CHECK(launched("gsum_chunks_kernel launch"));
+      if (g.norm) NC_CHECK(norm_adjoint(c, z, zs, tl, ncta_out, &pending, st));
     } else {
-      port_gz_kernel<<<blocks_for(g.n_out, 128), 128, 0, st>>>(g, c.sp, c.out_index, c.gout, zh, zs, c.gz,
-                                                                c.gsum, B);
+      port_gz_kernel<<<blocks_for((size_t)g.n_out * 32, 128), 128, 0, st>>>(g, c.sp, c.out_index, c.gout, z, zs,
+                                                                c.mean_save, c.rstd_save, tl, c.gz, c.gsum, B);
       NC_CHECK(launched("port_gz_kernel launch"));
+      if (g.norm) {
+        // the plane gradients are zero off the ports: their sums come from the port cells
+        const int nplanes = B * g.M;
+        port_coef_kernel<<<blocks_for((size_t)nplanes * 32, 256), 256, 0, st>>>(
+            g, c.out_index, c.gz, z, zs, c.mean_save, c.rstd_save, tl, nplanes, c.ncoef);
+        NC_CHECK(launched("port_coef_kernel launch"));
+        pending = true;
+      }
     }
-    if (g.norm) NC_CHECK(norm_adjoint(c, zh, zs, g.d - 1, ncta_out, &pending, st));
-    pending_t = g.d - 1;
+    pending_t = tl;
   }
 
   for (int t = g.d - 1; t >= 0; --t) {
@@ -1333,14 +1403,14 @@ nc_status fft_backward(const FftCall& c, cudaStream_t st) {
       NC_CHECK(launched("ring_grad_kernel launch"));
     }
     // hidden-step adjoint of step t-1
-    const float* zh = c.zhat + (size_t)(t - 1) * M * P;
+    const float* z = c.zhat + (size_t)(t - 1) * M * P;
     int ncta = 0;
-    NC_CHECK(hidden_gz(g, c, zh, zs, nch, bc, g.act, g.slope, nullptr, &ncta, st));
+    NC_CHECK(hidden_gz(g, c, z, zs, t - 1, nch, bc, g.act, g.slope, nullptr, &ncta, st));
     gsum_chunks_kernel<<<blocks_for(3 * P, 256), 256, 0, st>>>(c.gpart, c.gsum, g.P, nch);
     NC_CHECK(launched("gsum_chunks_kernel launch"));
     pending = false;
     pending_t = t - 1;
-    if (g.norm) NC_CHECK(norm_adjoint(c, zh, zs, t - 1, ncta, &pending, st));
+    if (g.norm) NC_CHECK(norm_adjoint(c, z, zs, t - 1, ncta, &pending, st));
   }
 
   // filter gradient: Re IFFT(acc_m) / (Nh Nw) at lags [0, kh) x [0, kw)

@@ -29,8 +29,9 @@ struct FftCall {
   float* gzpart;              // train: (ceil(P/256), B, M, 2) per-CTA sums of gz, gz*zhat
   float4* ncoef;              // train: (B, M) standardisation-adjoint coefficients
   float* zscr;                // (B, M, P) inference planes
-  float* zhat;                // train: (B, d, M, P)
-  float* rstd_save;           // train: (B, d, M)
+  float* zhat;                // train: (B, d, M, P) raw planes z of every step
+  float* rstd_save;           // train: (B, d, M) their 1 / sqrt(var + eps)
+  float* mean_save;           // train: (B, d, M) their means (zhat = (z - mean) * rstd)
   float* xsave;               // train: (B, d-1, P)
   float2* q;                  // train: (B/2, M, Nh, Nw)
   float2* dgacc;              // train: (M, Nh, Nw)

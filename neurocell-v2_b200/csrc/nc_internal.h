@@ -66,6 +66,8 @@ struct WsLayout {
   size_t f_tmp;           // row-pass / column-pass intermediate lines
   size_t f_gspec;         // (M, Nh, Nw) filter spectra / (Nh*Nw)
   size_t f_mean, f_rstd;  // (B, M) plane statistics of the current step
+  size_t f_mean_save;     // train: (B, d, M) per-step plane means (the saved planes stay
+                          // raw; the backward standardises them on the fly)
   size_t f_rowstats;      // (B, M, roi_h) per-row (mean, M2) of the current step's planes
   size_t f_gzpart;        // train: (ceil(P/256), B, M, 2) per-CTA sums of gz and gz*zhat
   size_t f_ncoef;         // train: (B, M) float4 (rstd, mean gz, mean gz*zhat, 0) of the

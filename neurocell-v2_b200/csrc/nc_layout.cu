@@ -146,6 +146,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
   L.zhat = train ? take(fl * B * g.d * M * P) : SIZE_MAX;
   L.rstd = train ? take(fl * B * g.d * M) : SIZE_MAX;
   L.f_field = L.f_xhat = L.f_tmp = L.f_gspec = L.f_mean = L.f_rstd = L.f_rowstats = L.f_gzpart = L.f_ncoef = SIZE_MAX;
+  L.f_mean_save = SIZE_MAX;
   L.f_q = L.f_dgacc = L.f_gz = L.f_dx = L.f_gpart = L.f_h = L.f_gring = L.f_xspec = SIZE_MAX;
   if (g.algo == NC_CONV_FFT && fftf_fits(g)) {
     // fused per-sample FFT kernels: spectra tables + per-sample partials only
@@ -197,6 +198,7 @@ WsLayout ws_layout(const Geo& g, int batch, uint32_t flags, bool* f_smem, bool* 
       L.f_gpart = take(fl * kRedChunks * 3 * P);
       L.f_gzpart = take(fl * ((P + 255) / 256) * B * M * 2);
       L.f_ncoef = take(fl * 4 * B * M);
+      L.f_mean_save = take(fl * B * g.d * M);
       L.gsum = take(fl * 3 * P);
       L.gdsum = take(fl * M * g.K);
       L.gborder = take(fl * HW);
