@@ -149,6 +149,11 @@ __device__ __forceinline__ void line_pair(int idx, int N, int lgN, int& l, int& 
 // the run-time variant and the column pass that sums over the directions (`heavy`); the
 // shared-memory plans leave the choice to the compiler.
 constexpr int fft_ctas(int RA, bool heavy = false) { return RA == 0 ? 1 : (RA < 0 || heavy) ? 4 : 5; }
+// Threads of a column-pass CTA: the N = 1024 sum over the directions runs one CTA of 1024
+// threads per SM over 16 columns (shared memory holds 16 lines either way; one large CTA
+// keeps twice the warps, and loads in flight, of two 256-thread CTAs).
+constexpr bool cols_big(int MODE, int RA) { return RA < 0 && MODE == 2; }
+constexpr int cols_threads(int MODE, int RA) { return cols_big(MODE, RA) ? 1024 : kFftThreads; }
 
 // Forward row transforms of real planes -> dst (lines, N) complex.  For N > 64 (RA = N/64)
 // the radix-R stage reads the planes directly (fft::fwd_a_global).  Dynamic shared memory:
@@ -314,7 +319,7 @@ __host__ __device__ inline int col_line_stride(int N) {
 // Column transforms of C adjacent columns per CTA (blockIdx.y = unit).  For N > 64
 // (RA = N/64) the radix-R stage reads (forward) or writes (inverse) global memory directly.
 template <int MODE, int RA>
-__global__ void __launch_bounds__(kFftThreads, fft_ctas(RA, MODE == 2)) cols_kernel(ColArgs a, const float2* __restrict__ tw,
+__global__ void __launch_bounds__(cols_threads(MODE, RA), cols_big(MODE, RA) ? 1 : fft_ctas(RA, MODE == 2)) cols_kernel(ColArgs a, const float2* __restrict__ tw,
                                                             int C) {
   extern __shared__ __align__(16) float2 sm[];
   const int N = a.Nh;
@@ -363,6 +368,7 @@ __global__ void __launch_bounds__(kFftThreads, fft_ctas(RA, MODE == 2)) cols_ker
       } else {
         float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
         const float2* q = a.src + (size_t)u * a.M * NN + off;
+#pragma unroll 2
         for (int m = 0; m < a.M; ++m) {
           const float4 x = *reinterpret_cast<const float4*>(q + (size_t)m * NN);
           const float4 h = *reinterpret_cast<const float4*>(a.spec + (size_t)m * NN + off);
@@ -583,12 +589,14 @@ __device__ __forceinline__ void stv(float* __restrict__ p, const float* v) {
 // the training residual -- or, in universe mode (uroi != null), the last step's ROI cells.
 // The planes z are only read: a training call keeps them raw and the backward standardises
 // them again from the saved statistics.  One thread per V consecutive pixels of one sample
-// (V = 4 when P % 4 == 0).
-template <int V>
+// (V = 4 when P % 4 == 0).  ACT >= 0 compiles the activation in (tanh, the hidden default);
+// ACT = -1 reads it from act_rt.
+template <int V, int ACT>
 __global__ void hidden_epi_kernel(Geo g, StepParams sp, const float* __restrict__ z, size_t zs,
                                   const float* __restrict__ mean, const float* __restrict__ rstd,
                                   float* __restrict__ field, float* __restrict__ xsave, int t, int B,
-                                  int act_id, float slope, float* __restrict__ uroi) {
+                                  int act_rt, float slope, float* __restrict__ uroi) {
+  const int act_id = ACT >= 0 ? ACT : act_rt;
   const size_t gidx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (gidx * V >= (size_t)B * g.P) return;
   const size_t e0 = gidx * V;
@@ -888,15 +896,16 @@ __device__ __forceinline__ float warp_sum4(float a, float b, float c, float d, i
 // gzpart (not null): the CTA's sums of gz and gz * zhat over its pixels per (b, m) of its
 // chunk, at gzpart[((blockIdx.x * B + b) * M + m) * 2 + {0, 1}] (warp_sum4 over directions
 // m, m+1, then the warps in order), so the standardisation adjoint needs one pass.  `red`
-// in dynamic shared memory holds bc * M * 2 values per warp.
-template <int V>
-__global__ void __launch_bounds__(256, 4) hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__ dx,
+// in dynamic shared memory holds bc * M * 2 values per warp.  ACT as hidden_epi_kernel.
+template <int V, int ACT>
+__global__ void __launch_bounds__(256, ACT >= 0 ? 3 : 4) hidden_gz_kernel(Geo g, StepParams sp, const float* __restrict__ dx,
                                  const float* __restrict__ z_t, size_t zs,
                                  const float* __restrict__ mean_save, const float* __restrict__ rstd_save,
                                  int t, float* __restrict__ gz,
-                                 float* __restrict__ gpart, int B, int bc, int act_id, float slope,
+                                 float* __restrict__ gpart, int B, int bc, int act_rt, float slope,
                                  const float* __restrict__ gy_roi, float* __restrict__ gzpart) {
   extern __shared__ float red[];
+  const int act_id = ACT >= 0 ? ACT : act_rt;
   const int gi = blockIdx.x * blockDim.x + threadIdx.x;
   const bool on = gi * V < g.P;       // threads past the plane join the warp sums with zeros
   const int p0 = on ? gi * V : 0;
@@ -1029,9 +1038,10 @@ size_t rows_smem(int N, int L) {
 }
 
 // Columns per CTA: 8 from 512-point columns on (37 KB of lines at N = 512, six CTAs per
-// SM; measured faster than 16 at N = 512 and than 4 at N = 1024), 16 below.
-int cols_per_cta(int Nh, int Nw) {
-  int C = Nh >= 512 ? 8 : 16;
+// SM; measured faster than 16 at N = 512 and than 4 at N = 1024), 16 below, 16 for the
+// 1024-thread CTAs (cols_threads).
+int cols_per_cta(int Nh, int Nw, bool big) {
+  int C = (big || Nh < 512) ? 16 : 8;
   return C < Nw ? C : Nw;
 }
 
@@ -1102,10 +1112,10 @@ nc_status rows_inv(const float2* src, const Planes& a, int N, const float2* tw, 
 
 template <int MODE, int RA>
 nc_status cols_ra(const ColArgs& a, int units, const float2* tw, cudaStream_t st) {
-  const int C = cols_per_cta(a.Nh, a.Nw);
+  const int C = cols_per_cta(a.Nh, a.Nw, cols_big(MODE, RA));
   const size_t smem = cols_smem(a.Nh, C);
   NC_CHECK(smem_attr((const void*)cols_kernel<MODE, RA>, smem));
-  cols_kernel<MODE, RA><<<dim3(a.Nw / C, units), kFftThreads, smem, st>>>(a, tw, C);
+  cols_kernel<MODE, RA><<<dim3(a.Nw / C, units), cols_threads(MODE, RA), smem, st>>>(a, tw, C);
   return launched("cols_kernel launch");
 }
 
@@ -1154,12 +1164,15 @@ nc_status hidden_epi(const Geo& g, const FftCall& c, const float* z, size_t zs, 
                      float* uroi, cudaStream_t st) {
   const size_t n = (size_t)c.batch * g.P;
   float* xs = (c.train && !uroi) ? c.xsave : nullptr;
+  auto run = [&](auto kernel, int V) {
+    kernel<<<blocks_for(n / V, kEpiThreads), kEpiThreads, 0, st>>>(g, c.sp, z, zs, c.mean, c.rstd, c.field, xs,
+                                                                   t, c.batch, act_id, slope, uroi);
+  };
+  const bool tanh_act = act_id == NC_ACT_TANH;
   if (plane_vec(g, zs))
-    hidden_epi_kernel<4><<<blocks_for(n / 4, kEpiThreads), kEpiThreads, 0, st>>>(
-        g, c.sp, z, zs, c.mean, c.rstd, c.field, xs, t, c.batch, act_id, slope, uroi);
+    run(tanh_act ? hidden_epi_kernel<4, NC_ACT_TANH> : hidden_epi_kernel<4, -1>, 4);
   else
-    hidden_epi_kernel<1><<<blocks_for(n, kEpiThreads), kEpiThreads, 0, st>>>(
-        g, c.sp, z, zs, c.mean, c.rstd, c.field, xs, t, c.batch, act_id, slope, uroi);
+    run(tanh_act ? hidden_epi_kernel<1, NC_ACT_TANH> : hidden_epi_kernel<1, -1>, 1);
   return launched("hidden_epi_kernel launch");
 }
 
@@ -1173,18 +1186,17 @@ nc_status hidden_gz(const Geo& g, const FftCall& c, const float* z, size_t zs, i
   const bool part = c.gzpart != nullptr && red <= 48 * 1024;
   float* gzp = part ? c.gzpart : nullptr;
   const size_t smem = part ? red : 0;
-  unsigned grid;
-  if (plane_vec(g, zs)) {
-    grid = blocks_for((size_t)g.P / 4, 256);
-    hidden_gz_kernel<4><<<dim3(grid, nch), 256, smem, st>>>(g, c.sp, c.dx, z, zs, c.mean_save, c.rstd_save,
-                                                            tz, c.gz, c.gpart, c.batch, bc, act_id, slope,
-                                                            gy_roi, gzp);
-  } else {
-    grid = blocks_for((size_t)g.P, 256);
-    hidden_gz_kernel<1><<<dim3(grid, nch), 256, smem, st>>>(g, c.sp, c.dx, z, zs, c.mean_save, c.rstd_save,
-                                                            tz, c.gz, c.gpart, c.batch, bc, act_id, slope,
-                                                            gy_roi, gzp);
-  }
+  const int V = plane_vec(g, zs) ? 4 : 1;
+  const unsigned grid = blocks_for((size_t)g.P / V, 256);
+  auto run = [&](auto kernel) {
+    kernel<<<dim3(grid, nch), 256, smem, st>>>(g, c.sp, c.dx, z, zs, c.mean_save, c.rstd_save, tz, c.gz,
+                                               c.gpart, c.batch, bc, act_id, slope, gy_roi, gzp);
+  };
+  const bool tanh_act = act_id == NC_ACT_TANH;
+  if (V == 4)
+    run(tanh_act ? hidden_gz_kernel<4, NC_ACT_TANH> : hidden_gz_kernel<4, -1>);
+  else
+    run(tanh_act ? hidden_gz_kernel<1, NC_ACT_TANH> : hidden_gz_kernel<1, -1>);
   *ncta = part ? (int)grid : 0;
   return launched("hidden_gz_kernel launch");
 }
