@@ -164,6 +164,28 @@ class ClockSampler:
                 "source": self.source}
 
 
+def exchange_ms(runner, n: int, dev, pg):
+    """Device time of the gradient exchange (the NVLink kernel, or the NCCL all-reduce and
+    the SGD kernel): median over n eager steps taken after the timed region by every rank
+    (same collective steps), max over ranks.  None on one GPU."""
+    if pg is None or runner.world <= 1:
+        return None
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for a, b in evs:            # torch creates the CUDA event on first record
+        a.record()
+        b.record()
+    torch.cuda.synchronize()
+    for i in range(n):
+        runner.exchange_events = evs[i]
+        runner._launch()
+    runner.exchange_events = None
+    torch.cuda.synchronize()
+    med = statistics.median(a.elapsed_time(b) for a, b in evs)
+    t = torch.tensor([med], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def spread(ms: list) -> dict:
     """Median and 10th / 90th percentiles of per-step times (ms)."""
     q = np.percentile(np.asarray(ms, dtype=np.float64), [10, 50, 90])
@@ -351,6 +373,7 @@ def run_b200(args) -> None:
         torch.cuda.synchronize()
         kev = kev[:min(K, 10)]
     fwd_ms = statistics.median(e[0].elapsed_time(e[1]) for e in kev)
+    xch_ms = exchange_ms(runner, 10, dev, pg)
     bwd_ms = statistics.median(e[2].elapsed_time(e[3]) for e in kev)
 
     # ---- end to end through the public API: pinned host batches in, the loss out to pinned
@@ -426,6 +449,9 @@ def run_b200(args) -> None:
             "conv_path": {1: "direct per-sample kernels", 2: "FFT per-step kernels",
                           3: "fused per-sample FFT kernels"}.get(path, "?"),
             "kernels_ms": {names[0]: fwd_ms, names[1]: bwd_ms},
+            **({"grad_exchange_ms": {"median_max_over_ranks": xch_ms, "share_of_step": xch_ms / ms_max,
+                                     "how": "CUDA events around the exchange call, 10 eager steps "
+                                            "after the timed region"}} if xch_ms is not None else {}),
             "roofline": {"bound": "fp32", "kernel": dom, "achieved": ach, "peak": peak,
                          "unit": "TFLOP/s", "frac": ach / peak if peak else None,
                          "work": "effective direct-convolution FLOPs (2*M*P*K per pass) per the "
@@ -642,6 +668,7 @@ def run_config(args) -> None:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    xch_ms = exchange_ms(runner, 5, dev, pg) if meta["train"] else None
     M, P, Kk, d = meta["M"], meta["P"], meta["K"], meta["d"]
     passes = (3 * d - 1) if meta["train"] else d
     flops = 2.0 * M * P * Kk * passes * B
@@ -676,6 +703,10 @@ def run_config(args) -> None:
         "effective_tflops": flops / (ms * 1e-3) / 1e12, "roofline": roof, "clocks": clk,
         "gpu_launches_per_step": runner.launches_per_step() if meta["train"] else n_launch,
     }
+    if xch_ms is not None:
+        line["grad_exchange_ms"] = {"median_max_over_ranks": xch_ms, "share_of_step": xch_ms / ms,
+                                    "how": "CUDA events around the exchange call, 5 eager steps after "
+                                           "the timed region"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if meta["train"]:

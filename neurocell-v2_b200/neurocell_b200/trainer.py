@@ -287,6 +287,9 @@ class VNNTrainStep:
         self.codd.temperature_dev = self.tau_dev.data_ptr()
         self.graph = None
         self.epoch_graph = None
+        # (start, stop) torch.cuda.Event pair recorded around the gradient exchange of eager
+        # steps (timing only; a captured graph does not record them)
+        self.exchange_events = None
         self.exchange = None
         if exchange == "nvlink" and self.world > 1:
             self.exchange = NVLinkExchange(self.n_cell + self.n_filt, process_group, dev)
@@ -341,6 +344,9 @@ class VNNTrainStep:
                                             P(self.x), self.B, c.byref(self.codd), P(self.g_out),
                                             c.c_void_p(gcell), c.c_void_p(gfilt), P(self.ws),
                                             self.ws_bytes, st), "nc_vnn_backward")
+        timed = self.exchange_events is not None and not torch.cuda.is_current_stream_capturing()
+        if timed:
+            self.exchange_events[0].record()
         if self.exchange is not None:
             # sum over ranks + params -= lr / world * sum, in one kernel over NVLink
             self.exchange.allreduce_sgd(gcell, cell, self.lr, st)
@@ -349,6 +355,8 @@ class VNNTrainStep:
             lr = self.lr / world            # mean of the per-rank mean-loss gradients
             self._lib.check(lib.nc_sgd_update(c.c_void_p(cell), c.c_void_p(gcell),
                                               self.n_cell + self.n_filt, lr, st), "nc_sgd_update")
+        if timed:
+            self.exchange_events[1].record()
         self._launches = int(lib.nc_launch_count() - n0)
 
     def load_batch(self, x: torch.Tensor, y: torch.Tensor) -> None:
