@@ -34,6 +34,7 @@ for _p in (ROOT, os.path.join(ROOT, "neurocell-v2_b200")):
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
 
 BATCH = 128
 SEED = 0            # config index 0 -> seeds 0 (params), 1 (filters), 2 (inputs)
@@ -180,8 +181,12 @@ def exchange_ms(runner, n: int, dev, pg):
         runner._launch()
     runner.exchange_events = None
     torch.cuda.synchronize()
-    med = statistics.median(a.elapsed_time(b) for a, b in evs)
-    t = torch.tensor([med], dtype=torch.float64, device=dev)
+    return max_over_ranks(statistics.median(a.elapsed_time(b) for a, b in evs), dev)
+
+
+def max_over_ranks(v: float, dev) -> float:
+    """The largest v over the ranks of the default process group."""
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 

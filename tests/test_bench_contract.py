@@ -46,3 +46,34 @@ def test_reference_arm_other_ranks_print_nothing():
 
 def test_reference_arm_has_no_secondary_config_lines():
     assert _run(["--impl", "reference", "--config", "2"]) == []
+
+
+def _rank_max(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q.put((rank, bench.max_over_ranks(1.5 + rank, "cpu")))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_multi_gpu_helpers_on_gloo_ranks():
+    """The max-over-ranks reduction behind the multi-GPU timings (step time and gradient
+    exchange), run by two gloo ranks on the host; exchange_ms is None without a group."""
+    import multiprocessing as mp
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank_max, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got == {0: 2.5, 1: 2.5}
+    assert bench.exchange_ms(None, 3, "cpu", None) is None
