@@ -9,24 +9,26 @@
 // memory model makes single-copy atomic even inside a vector access, so a reader sees a
 // value together with the tag written with it -- never the current tag beside an older
 // value.  A receiver knows a value has arrived when its tag equals the current step, so no
-// fences and no separate flags are needed: block k polls the elements of its slice in its
-// OWN buffer (bounded), then sums the slice over ranks 0..world-1 in that order (its own
-// contribution straight from `grads`) and applies SGD.  Every rank adds the same values in
-// the same order and ends with bitwise identical parameters.  Double buffering makes the
+// fences and no separate flags are needed: for each line of its slice, a thread loads that
+// line of every peer's slot in its OWN buffer at once (bounded retries) and, once every tag
+// is the current step, sums the values that came with the tags over ranks 0..world-1 in
+// that order (its own contribution straight from `grads`) and applies SGD.  Every rank adds
+// the same values in the same order and ends with bitwise identical parameters.  The grid
+// grows with the gradient (one line per thread, at most kDpMaxBlocks blocks: four per SM,
+// all resident at once, so no block waits for a peer block that is not running).  Double buffering makes the
 // next step safe: a rank writes slot `parity` again only at step+2, after every peer has
 // published step+1, i.e. after every peer finished reading step's slot (its step kernel
 // ended before its step+1 kernel began).  Step counters are per block and live on the
 // device, so the launch can be captured in a CUDA graph.  No multicast, no TMA, no atomics
 // on peer memory: plain volatile stores and loads.
 //
-// Failure: a block whose peers do not arrive within max_wait polls sets the status word
-// and returns without touching its slice.  The status is terminal: every later call on
-// that state returns at once (no stores to peers, no update), so the peers of this rank
-// time out at their next step as well and the failure reaches every rank within one step.
-// Parameters of slices whose blocks did complete the failing step WERE updated, so after a
-// failure the ranks' parameters are no longer known to agree: restore them from a
-// consistent copy, then call nc_dp_reset on every rank (and a host barrier) before the
-// next exchange.
+// Failure: a thread whose peers do not arrive within max_wait polls of one line sets the
+// status word; its block stops updating and returns.  The status is terminal: every later
+// call on that state returns at once (no stores to peers, no update), so the peers of this
+// rank time out at their next step as well and the failure reaches every rank within one
+// step.  Lines that arrived before the failure WERE updated, so after a failure the ranks'
+// parameters are no longer known to agree: restore them from a consistent copy, then call
+// nc_dp_reset on every rank (and a host barrier) before the next exchange.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -38,7 +40,7 @@
 namespace nc {
 namespace {
 
-constexpr int kDpBlocks = 32;
+constexpr int kDpMaxBlocks = 592;   // 4 per SM of a B200; the state holds one counter each
 constexpr int kDpThreads = 128;
 
 struct Peers {
@@ -97,38 +99,35 @@ __global__ void __launch_bounds__(kDpThreads) dp_allreduce_sgd_kernel(
     for (int r = 0; r < world; ++r)
       if (r != rank) st_line(slot(r, rank) + l, line);
   }
-  // 2. wait until every peer's lines of this slice carry this step's tag (bounded)
-  int it = 0, bad = 0;
+  // 2. per line: every peer's copy with this step's tag (bounded), then the sum in rank
+  //    order of the values that came with those tags, and SGD
+  int bad = 0;
   for (long long l = l0 + threadIdx.x; l < l1 && !bad; l += blockDim.x) {
-    for (int r = 0; r < world && !bad; ++r) {
-      if (r == rank) continue;
-      const ulonglong2* q = slot(rank, r) + l;
-      for (;;) {
-        const ulonglong2 v = ld_line(q);
-        if ((unsigned)(v.x >> 32) == step && (unsigned)(v.y >> 32) == step) break;
-        if (++it > max_wait) { bad = 1; break; }
-        if (it > 64) __nanosleep(32);
+    ulonglong2 q[NC_DP_MAX_RANKS];
+#pragma unroll
+    for (int r = 0; r < NC_DP_MAX_RANKS; ++r) q[r] = make_ulonglong2(0ull, 0ull);
+    for (int it = 0;; ++it) {
+      bool ready = true;
+#pragma unroll
+      for (int r = 0; r < NC_DP_MAX_RANKS; ++r) {
+        if (r >= world || r == rank) continue;
+        q[r] = ld_line(slot(rank, r) + l);
+        ready = ready && (unsigned)(q[r].x >> 32) == step && (unsigned)(q[r].y >> 32) == step;
       }
+      if (ready) break;
+      if (it >= max_wait) { bad = 1; break; }
+      if (it > 64) __nanosleep(32);
     }
-  }
-  if (bad) s_bad = 1;
-  __syncthreads();
-  if (s_bad) {                            // a peer did not arrive: no update, status set
-    if (threadIdx.x == 0) atomicExch(status, 1);
-    return;
-  }
-  // 3. sum in rank order, SGD (the tags were checked above; the values came with them)
-  for (long long l = l0 + threadIdx.x; l < l1; l += blockDim.x) {
+    if (bad) break;
+    const float2 own = load_pair(grads, n, l);
     float2 s = make_float2(0.f, 0.f);
-    for (int r = 0; r < world; ++r) {
-      float2 v;
-      if (r == rank) {
-        v = load_pair(grads, n, l);
-      } else {
-        const ulonglong2 q = ld_line(slot(rank, r) + l);
-        v = make_float2(__uint_as_float((unsigned)q.x), __uint_as_float((unsigned)q.y));
+#pragma unroll
+    for (int r = 0; r < NC_DP_MAX_RANKS; ++r) {
+      if (r < world) {
+        const float2 v = r == rank ? own
+                                   : make_float2(__uint_as_float((unsigned)q[r].x), __uint_as_float((unsigned)q[r].y));
+        if (r == 0) s = v; else { s.x += v.x; s.y += v.y; }
       }
-      if (r == 0) s = v; else { s.x += v.x; s.y += v.y; }
     }
     const long long i = 2 * l;
     grads[i] = s.x;
@@ -138,8 +137,19 @@ __global__ void __launch_bounds__(kDpThreads) dp_allreduce_sgd_kernel(
       params[i + 1] -= lr_eff * s.y;
     }
   }
+  if (bad) s_bad = 1;
   __syncthreads();
+  if (s_bad) {                            // a peer did not arrive: status set, no counter
+    if (threadIdx.x == 0) atomicExch(status, 1);
+    return;
+  }
   if (threadIdx.x == 0) counters[k] = step;
+}
+
+// Blocks of the exchange for n elements: one 16-byte line per thread, at most kDpMaxBlocks.
+inline int dp_blocks(long long n) {
+  const long long b = (n_lines(n) + kDpThreads - 1) / kDpThreads;
+  return (int)(b < 1 ? 1 : b > kDpMaxBlocks ? kDpMaxBlocks : b);
 }
 
 }  // namespace
@@ -154,7 +164,7 @@ size_t nc_dp_shared_bytes(int64_t n, int32_t world) {
   return align256(sizeof(ulonglong2) * 2 * (size_t)world * (size_t)n_lines(n));
 }
 
-size_t nc_dp_state_bytes(void) { return align256(sizeof(unsigned) * kDpBlocks + sizeof(int)); }
+size_t nc_dp_state_bytes(void) { return align256(sizeof(unsigned) * kDpMaxBlocks + sizeof(int)); }
 
 nc_status nc_dp_alloc(size_t bytes, void** d_ptr) {
   if (!d_ptr || bytes == 0) return set_error(NC_ERR_INVALID, "bad nc_dp_alloc arguments");
@@ -207,8 +217,8 @@ nc_status nc_dp_allreduce_sgd(void* const* peers, int32_t world, int32_t rank, v
     pp.p[r] = static_cast<ulonglong2*>(peers[r]);
   }
   unsigned* counters = static_cast<unsigned*>(d_state);
-  int* status = reinterpret_cast<int*>(counters + kDpBlocks);
-  dp_allreduce_sgd_kernel<<<kDpBlocks, kDpThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  int* status = reinterpret_cast<int*>(counters + kDpMaxBlocks);
+  dp_allreduce_sgd_kernel<<<dp_blocks(n), kDpThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       pp, world, rank, (long long)n, counters, status, grads, params, lr / (float)world,
       max_wait_iters);
   cudaError_t e = cudaGetLastError();
@@ -220,7 +230,7 @@ nc_status nc_dp_allreduce_sgd(void* const* peers, int32_t world, int32_t rank, v
 
 nc_status nc_dp_status(const void* d_state, int32_t* status, void* stream) {
   if (!d_state || !status) return set_error(NC_ERR_INVALID, "bad nc_dp_status arguments");
-  const int* s = reinterpret_cast<const int*>(static_cast<const unsigned*>(d_state) + kDpBlocks);
+  const int* s = reinterpret_cast<const int*>(static_cast<const unsigned*>(d_state) + kDpMaxBlocks);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   NC_CUDA_CHECK(cudaMemcpyAsync(status, s, sizeof(int), cudaMemcpyDeviceToHost, st));
   NC_CUDA_CHECK(cudaStreamSynchronize(st));
