@@ -126,24 +126,35 @@ class ClockSampler:
         except Exception as e:   # noqa: BLE001 -- no NVML: nothing to sample
             self.source = f"unavailable ({type(e).__name__})"
 
-    def _poll(self):
+    def _sample(self):
         nv, h = self.nvml, self.h
         get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
                               getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+        try:
+            sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+            bits = int(get_reasons(h)) if get_reasons else 0
+            self.rows.append((time.perf_counter(), sm, bits))
+        except Exception:   # noqa: BLE001
+            pass
+
+    def _poll(self):
         while not self._stop.is_set():
-            try:
-                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
-                bits = int(get_reasons(h)) if get_reasons else 0
-                self.rows.append((time.perf_counter(), sm, bits))
-            except Exception:   # noqa: BLE001
-                pass
+            self._sample()
             time.sleep(0.002)
 
     def mark_start(self):
+        # the poller needs the interpreter lock while the timed loop launches: switch often
+        self._switch = sys.getswitchinterval()
+        sys.setswitchinterval(1e-4)
         self.t0 = time.perf_counter()
 
     def mark_stop(self):
+        # one sample taken here as well, at the end of the work, for windows of a few ms
+        if self.nvml is not None:
+            self._sample()
         self.t1 = time.perf_counter()
+        if getattr(self, "_switch", None):
+            sys.setswitchinterval(self._switch)
 
     def stop(self) -> dict:
         if self.nvml is None:

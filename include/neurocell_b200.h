@@ -305,10 +305,10 @@ nc_status nc_ipc_close(void* d_peer_ptr);
  * grads[n] (this rank's gradient of its mean loss) -> grads[n] = sum over ranks,
  * params[n] -= lr / world * grads[n].  peers[world] are the shared buffers of all ranks
  * (this rank's own at index rank).
- * Failure: a peer that does not arrive within max_wait_iters polls sets the status word
- * (read it with nc_dp_status: 0 = ok, 1 = a peer timed out).  The slices whose peers did
- * not arrive are left untouched; slices whose peers did arrive in that call were updated,
- * so the ranks' parameters no longer agree.  The status is terminal: every later call on
+ * Failure: a peer that does not arrive within max_wait_iters polls of one line sets the
+ * status word (read it with nc_dp_status: 0 = ok, 1 = a peer timed out).  The lines whose
+ * peers did not arrive are left untouched; lines whose peers did arrive in that call were
+ * updated, so the ranks' parameters no longer agree.  The status is terminal: every later call on
  * this state returns without storing to peers or updating, which makes every peer time out
  * at its next step too.  To go on, restore the parameters from a consistent copy, call
  * nc_dp_reset on every rank and pass a host barrier before the next exchange.
