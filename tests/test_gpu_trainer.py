@@ -249,19 +249,17 @@ def _tagged(values: np.ndarray, step: int) -> torch.Tensor:
 def test_exchange_timeout_is_terminal_until_reset():
     """Failure detection without a GPU fault.  Rank 0 of a two-rank exchange whose peer is
     a plain buffer on this GPU: rank 0's own receive buffer is pre-filled from the host with
-    the peer's step-1 values for the first half of the slices only.  Blocks whose slices
-    arrived sum and update them; the others time out, leave their slices untouched and set
-    the status word.  The status is terminal: a second call changes nothing.  After
-    nc_dp_reset and a complete pre-fill the exchange completes again."""
+    the peer's step-1 values for the first half of the lines only.  Lines that arrived are
+    summed and updated; the others time out, stay untouched and set the status word.  The
+    status is terminal: a second call changes nothing.  After nc_dp_reset and a complete
+    pre-fill the exchange completes again."""
     import ctypes
     from neurocell_b200 import _lib
     lib = _lib.load()
     dev = torch.device("cuda:0")
     n, world, lr = 1000, 2, 0.1
     L = (n + 1) // 2                       # 16-byte lines of two elements
-    blocks = 32
-    slice_lines = -(-L // blocks)
-    good_lines = 16 * slice_lines          # blocks 0..15 see their peer's values
+    good_lines = 256                       # lines 0..255 see their peer's values
     shared_bytes = lib.nc_dp_shared_bytes(n, world)
     assert shared_bytes >= 2 * world * L * 16
     own = torch.zeros(shared_bytes // 8, dtype=torch.int64, device=dev)
