@@ -182,11 +182,15 @@ __device__ __forceinline__ void line_pair(int idx, int N, int lgN, int& l, int& 
 // the run-time variant and the column pass that sums over the directions (`heavy`); the
 // shared-memory plans leave the choice to the compiler.
 constexpr int fft_ctas(int RA, bool heavy = false) { return RA == 0 ? 1 : (RA < 0 || heavy) ? 4 : 5; }
-// Threads of a column-pass CTA: the N = 1024 sum over the directions runs one CTA of 1024
-// threads per SM over 16 columns (shared memory holds 16 lines either way; one large CTA
-// keeps twice the warps, and loads in flight, of two 256-thread CTAs).
+// Threads of a column-pass CTA.  Shared memory holds 16 lines of N = 1024 per SM either
+// way; more threads per line keep more loads in flight: the sum over the directions runs
+// one CTA of 1024 threads per SM over 16 columns, the other N = 1024 passes two CTAs of
+// 512 threads over 8 columns each (one radix-16 task per thread; one 1024-thread CTA
+// measured slower for them: its barrier phases stall the whole SM).
 constexpr bool cols_big(int MODE, int RA) { return RA < 0 && MODE == 2; }
-constexpr int cols_threads(int MODE, int RA) { return cols_big(MODE, RA) ? 1024 : kFftThreads; }
+constexpr int cols_threads(int MODE, int RA) {
+  return cols_big(MODE, RA) ? 1024 : RA < 0 ? 512 : kFftThreads;
+}
 
 // Forward row transforms of real planes -> dst (lines, N) complex.  For N > 64 (RA = N/64)
 // the radix-R stage reads the planes directly (fft::fwd_a_global).  Dynamic shared memory:
@@ -354,7 +358,7 @@ __host__ __device__ inline int col_line_stride(int N) {
 // Column transforms of C adjacent columns per CTA (blockIdx.y = unit).  For N > 64
 // (RA = N/64) the radix-R stage reads (forward) or writes (inverse) global memory directly.
 template <int MODE, int RA>
-__global__ void __launch_bounds__(cols_threads(MODE, RA), cols_big(MODE, RA) ? 1 : fft_ctas(RA, MODE == 2)) cols_kernel(ColArgs a, const float2* __restrict__ tw,
+__global__ void __launch_bounds__(cols_threads(MODE, RA), cols_big(MODE, RA) ? 1 : RA < 0 ? 2 : fft_ctas(RA, MODE == 2)) cols_kernel(ColArgs a, const float2* __restrict__ tw,
                                                             int C) {
   extern __shared__ __align__(16) float2 sm[];
   const int N = a.Nh;
