@@ -182,12 +182,14 @@ __device__ __forceinline__ void line_pair(int idx, int N, int lgN, int& l, int& 
 // the run-time variant and the column pass that sums over the directions (`heavy`); the
 // shared-memory plans leave the choice to the compiler.
 constexpr int fft_ctas(int RA, bool heavy = false) { return RA == 0 ? 1 : (RA < 0 || heavy) ? 4 : 5; }
-// Threads of a column-pass CTA.  Shared memory holds 16 lines of N = 1024 per SM either
-// way; more threads per line keep more loads in flight: the sum over the directions runs
-// one CTA of 1024 threads per SM over 16 columns, the other N = 1024 passes two CTAs of
-// 512 threads over 8 columns each (one radix-16 task per thread; one 1024-thread CTA
-// measured slower for them: its barrier phases stall the whole SM).
-constexpr bool cols_big(int MODE, int RA) { return RA < 0 && MODE == 2; }
+// Threads of a column-pass CTA.  The sum over the directions (M loads per element) runs
+// one CTA of 1024 threads per SM over 16 columns for every two-stage size (config 2:
+// 12.24 -> 11.70 ms).  The other N = 1024 passes run two CTAs of 512 threads over 8
+// columns each (shared memory holds 16 lines of N = 1024 per SM either way; one radix-16
+// task per thread keeps more loads in flight; one 1024-thread CTA measured slower for
+// them: its barrier phases stall the whole SM); the other sizes keep 256 threads (512
+// measured slower).
+constexpr bool cols_big(int MODE, int RA) { return RA != 0 && MODE == 2; }
 constexpr int cols_threads(int MODE, int RA) {
   return cols_big(MODE, RA) ? 1024 : RA < 0 ? 512 : kFftThreads;
 }
