@@ -613,12 +613,19 @@ static nc_status vnn_backward(const nc_topo* topo, const void* d_plan, const flo
       const int chunks = batch < kRedChunks ? batch : kRedChunks;
       const int bc = (batch + chunks - 1) / chunks;
       float* part = at<float>(d_ws, L.redscr);
-      seg_batch_sum1_kernel<<<dim3((j.total + 255) / 256, chunks), 256, 0, st>>>(j, batch, bc, part);
-      NC_CHECK(launch_check("seg_batch_sum1_kernel launch"));
-      prestep_bwd_kernel<<<(HW + 255) / 256, 256, 0, st>>>(
-          g, pr.sp, cell_params, filters, pr.owm, pr.bmask, part, fa.gring ? part + P3 + MK : nullptr,
-          part + P3, gringf, g_cell_params, g_filters, chunks, (size_t)j.total);
-      NC_CHECK(launch_check("prestep_bwd_kernel launch"));
+      {
+        PdlLaunch l1(dim3((j.total + 255) / 256, chunks), dim3(256), 0, st);
+        NC_CUDA_CHECK(cudaLaunchKernelEx(&l1.cfg, seg_batch_sum1_kernel, j, batch, bc, part));
+        NC_CHECK(launch_check("seg_batch_sum1_kernel launch"));
+      }
+      {
+        float* gring_part = fa.gring ? part + P3 + MK : nullptr;
+        PdlLaunch l2(dim3((HW + 255) / 256), dim3(256), 0, st);
+        NC_CUDA_CHECK(cudaLaunchKernelEx(&l2.cfg, prestep_bwd_kernel, g, pr.sp, cell_params, filters, pr.owm,
+                                         pr.bmask, part, gring_part, part + P3, gringf, g_cell_params,
+                                         g_filters, chunks, (size_t)j.total));
+        NC_CHECK(launch_check("prestep_bwd_kernel launch"));
+      }
     }
     clear_error();
     return NC_OK;
@@ -832,7 +839,10 @@ nc_status nc_mse_loss(const float* out, const float* targets, int32_t batch, int
     NC_CHECK(device_address(loss, "loss", &d));
     lossd = const_cast<float*>(static_cast<const float*>(d));
   }
-  mse_kernel<<<1, 1024, 0, as_stream(stream)>>>(out, targets, (int)total, lossd, g_out);
+  {
+    PdlLaunch l(dim3(1), dim3(1024), 0, as_stream(stream));
+    NC_CUDA_CHECK(cudaLaunchKernelEx(&l.cfg, mse_kernel, out, targets, (int)total, lossd, g_out));
+  }
   NC_CHECK(launch_check("mse_kernel launch"));
   clear_error();
   return NC_OK;
@@ -849,7 +859,10 @@ nc_status nc_softmax_ce_loss(const float* logits, const int32_t* labels, int32_t
     NC_CHECK(device_address(loss, "loss", &d));
     lossd = const_cast<float*>(static_cast<const float*>(d));
   }
-  softmax_ce_kernel<<<1, 1024, 0, as_stream(stream)>>>(logits, labels, batch, n, lossd, g_logits);
+  {
+    PdlLaunch l(dim3(1), dim3(1024), 0, as_stream(stream));
+    NC_CUDA_CHECK(cudaLaunchKernelEx(&l.cfg, softmax_ce_kernel, logits, labels, batch, n, lossd, g_logits));
+  }
   NC_CHECK(launch_check("softmax_ce_kernel launch"));
   clear_error();
   return NC_OK;
@@ -892,7 +905,10 @@ nc_status nc_sgd_update(float* params, const float* grads, int64_t n, float lr, 
   NC_CHECK(check_ptr(grads, "grads"));
   const int64_t blocks64 = (n + 255) / 256;
   const int blocks = (int)(blocks64 < 4096 ? blocks64 : 4096);
-  sgd_kernel<<<blocks, 256, 0, as_stream(stream)>>>(params, grads, n, lr);
+  {
+    PdlLaunch l(dim3(blocks), dim3(256), 0, as_stream(stream));
+    NC_CUDA_CHECK(cudaLaunchKernelEx(&l.cfg, sgd_kernel, params, grads, n, lr));
+  }
   NC_CHECK(launch_check("sgd_kernel launch"));
   clear_error();
   return NC_OK;

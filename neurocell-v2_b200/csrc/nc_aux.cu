@@ -74,6 +74,7 @@ __device__ __forceinline__ int seg_of(const SegSum& j, int i, int* off) {
 }
 
 __global__ void seg_batch_sum1_kernel(SegSum j, int batch, int bc, float* __restrict__ part) {
+  pdl_enter();   // see pdl_wait
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= j.total) return;
   int off;
@@ -155,6 +156,7 @@ __global__ void prestep_bwd_kernel(Geo g, StepParams sp, const float* __restrict
                                    const float* __restrict__ gdsum, const float* __restrict__ gring_final,
                                    float* __restrict__ gcell, float* __restrict__ gfilt, int rows,
                                    size_t stride) {
+  pdl_enter();   // see pdl_wait
   const int HW = g.H * g.W;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < HW) {
@@ -238,6 +240,7 @@ __global__ void stage_copy_kernel(StageSegs s) {
 
 __global__ void mse_kernel(const float* __restrict__ o, const float* __restrict__ y, int n,
                            float* __restrict__ loss, float* __restrict__ g) {
+  pdl_enter();   // see pdl_wait
   __shared__ float red[32];
   const float inv_n = 1.0f / (float)n;
   float acc = 0.f;
@@ -253,6 +256,7 @@ __global__ void mse_kernel(const float* __restrict__ o, const float* __restrict_
 // Mean softmax cross-entropy with integer labels.  One CTA.
 __global__ void softmax_ce_kernel(const float* __restrict__ x, const int32_t* __restrict__ lab,
                                   int batch, int n, float* __restrict__ loss, float* __restrict__ g) {
+  pdl_enter();   // see pdl_wait
   __shared__ float red[32];
   const float inv_b = 1.0f / (float)batch;
   float acc = 0.f;
@@ -277,6 +281,7 @@ __global__ void softmax_ce_kernel(const float* __restrict__ x, const int32_t* __
 }
 
 __global__ void sgd_kernel(float* __restrict__ p, const float* __restrict__ gr, int64_t n, float lr) {
+  pdl_enter();   // see pdl_wait
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     p[i] -= lr * gr[i];

@@ -8,6 +8,17 @@
 
 namespace nc {
 
+// Programmatic dependent launch (PdlLaunch, nc_errors.h): pdl_wait() returns once the
+// kernels this grid follows on the stream have finished and their writes are visible;
+// pdl_trigger() lets the next kernel be scheduled.  Kernels call both at their start, so
+// at most one dependent grid waits at a time.  Both do nothing in an ordinary launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_trigger();
+}
+
 constexpr float kNormEps = 1e-5f;      // neurocell/kernels_pallas.py:204 (rsqrt(var + 1e-5))
 constexpr float kTauMin = 1e-4f;       // neurocell/params.py:63
 constexpr float kGeluC = 0.7978845608028654f;   // sqrt(2/pi), kernels_pallas.py:130

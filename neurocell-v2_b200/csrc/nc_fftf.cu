@@ -373,6 +373,7 @@ constexpr int kActRuntime = -1;
 
 template <int ACT, int FACT>
 __global__ void __launch_bounds__(kThreadsF, 1) fftf_fwd_kernel(FftfArgs a) {
+  pdl_enter();   // see pdl_wait
   extern __shared__ float4 smem4[];
   uint64_t* hbar = reinterpret_cast<uint64_t*>(smem4);   // staging barrier (16 B slot)
   volatile int* abort_flag = reinterpret_cast<int*>(smem4) + 2;   // in the same slot
@@ -565,6 +566,7 @@ __global__ void __launch_bounds__(kThreadsF, 1) fftf_fwd_kernel(FftfArgs a) {
 // conj(H_j) and the per-pixel parameter gradients stay on chip for the whole launch.
 template <int ACT, int FACT>
 __global__ void __launch_bounds__(kThreadsF, 1) fftf_bwd_kernel(FftfArgs a) {
+  pdl_enter();   // see pdl_wait
   extern __shared__ float4 smem4[];
   const Geo& g = a.g;
   const int tid = threadIdx.x, nt = blockDim.x, b = blockIdx.x;
@@ -961,7 +963,8 @@ nc_status fftf_forward(const FftfArgs& args, cudaStream_t st) {
                                    : (const void*)fftf_fwd_kernel<kActRuntime, kActRuntime>;
   NC_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* kargs[] = {&a};
-  NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(a.batch), dim3(kThreadsF), kargs, smem, st));
+  PdlLaunch l(dim3(a.batch), dim3(kThreadsF), smem, st);
+  NC_CUDA_CHECK(cudaLaunchKernelExC(&l.cfg, fn, kargs));
   return launched("fftf_fwd_kernel launch");
 }
 
@@ -975,7 +978,8 @@ nc_status fftf_backward(const FftfArgs& args, cudaStream_t st) {
                                    : (const void*)fftf_bwd_kernel<kActRuntime, kActRuntime>;
   NC_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* kargs[] = {&a};
-  NC_CUDA_CHECK(cudaLaunchKernel(fn, dim3(a.batch), dim3(kThreadsF), kargs, smem, st));
+  PdlLaunch l(dim3(a.batch), dim3(kThreadsF), smem, st);
+  NC_CUDA_CHECK(cudaLaunchKernelExC(&l.cfg, fn, kargs));
   return launched("fftf_bwd_kernel launch");
 }
 
