@@ -227,20 +227,6 @@ __device__ __forceinline__ void inv2d_h0(float2* s, int nrows, const float2* tw,
   __syncthreads();
 }
 
-// Chan's pairwise merge of (count, mean, centred sum of squares): the two-stage variance of
-// the reference's tiled epilogue (neurocell/kernels_pallas.py:740-837).
-__device__ __forceinline__ void chan_merge(float& n, float& mean, float& m2, float nb, float mb, float m2b) {
-  if (nb == 0.f) return;
-  if (n == 0.f) {
-    n = nb; mean = mb; m2 = m2b;
-    return;
-  }
-  const float nn = n + nb, delta = mb - mean, f = nb / nn;
-  mean = fmaf(delta, f, mean);
-  m2 += m2b + delta * delta * n * f;
-  n = nn;
-}
-
 // Inverse row pass of the ROI rows of one plane that also leaves each row's centred
 // statistics (mean, M2 over its `roi_w` columns) of the re and im parts in
 // rowst[row * 4 + k0] and rowst[row * 4 + k0 + 1].  The 8 lanes of a row sum their values
@@ -293,24 +279,27 @@ __device__ __forceinline__ void rows_inv_stats(float2* s, int nrows, int roi_w, 
 }
 
 // Plane statistics of the four real planes from the row statistics (after a barrier):
-// warp k < 4 merges the rows of plane k (lane l takes rows l, l + 32, ...), then the lanes
-// merge in a fixed butterfly; lane 0 writes (mean, 1 / sqrt(var + eps)) to st[k].
+// warp k < 4 takes plane k, lane l rows l and l + 32.  Every row holds roi_w cells, so the
+// plane mean is the mean of the row means and M2 = sum_r M2_r + roi_w sum_r (mean_r -
+// mean)^2 -- the reference's two-stage variance for tiled planes
+// (neurocell/kernels_pallas.py:740-837) -- in two fixed-order warp sums; lane 0 writes
+// (mean, 1 / sqrt(var + eps)) to st[k].
 __device__ __forceinline__ void merge_row_stats(const float2* rowst, int roi_h, int roi_w, float2* st) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (w >= 4) return;
-  float n = 0.f, mean = 0.f, m2 = 0.f;
-  for (int r = lane; r < roi_h; r += 32) {
-    const float2 rs = rowst[r * 4 + w];
-    chan_merge(n, mean, m2, (float)roi_w, rs.x, rs.y);
-  }
+  const bool h0 = lane < roi_h, h1 = lane + 32 < roi_h;
+  const float2 r0 = h0 ? rowst[lane * 4 + w] : make_float2(0.f, 0.f);
+  const float2 r1 = h1 ? rowst[(lane + 32) * 4 + w] : make_float2(0.f, 0.f);
+  const float mean = warp_sum(r0.x + r1.x) / (float)roi_h;
+  const float d0 = h0 ? r0.x - mean : 0.f, d1 = h1 ? r1.x - mean : 0.f;
+  float dev = fmaf(d0, d0, d1 * d1), m2 = r0.y + r1.y;
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) {
-    const float nb = __shfl_xor_sync(0xffffffffu, n, o);
-    const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
-    const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
-    chan_merge(n, mean, m2, nb, mb, m2b);
+    dev += __shfl_xor_sync(0xffffffffu, dev, o);
+    m2 += __shfl_xor_sync(0xffffffffu, m2, o);
   }
-  if (lane == 0) st[w] = make_float2(mean, 1.0f / sqrtf(m2 / n + kNormEps));
+  m2 = fmaf((float)roi_w, dev, m2);
+  if (lane == 0) st[w] = make_float2(mean, 1.0f / sqrtf(m2 / (float)(roi_h * roi_w) + kNormEps));
 }
 
 // Field of step t into X (real part; zero imaginary, zero beyond Fh x Fw).
