@@ -283,14 +283,16 @@ __device__ __forceinline__ void rows_inv_stats(float2* s, int nrows, int roi_w, 
 // plane mean is the mean of the row means and M2 = sum_r M2_r + roi_w sum_r (mean_r -
 // mean)^2 -- the reference's two-stage variance for tiled planes
 // (neurocell/kernels_pallas.py:740-837) -- in two fixed-order warp sums; lane 0 writes
-// (mean, 1 / sqrt(var + eps)) to st[k].
-__device__ __forceinline__ void merge_row_stats(const float2* rowst, int roi_h, int roi_w, float2* st) {
+// (mean, 1 / sqrt(var + eps)) to st[k].  inv_h = 1 / roi_h, inv_n = 1 / (roi_h roi_w) come
+// from the caller (no division on this path, which every warp of the CTA waits for).
+__device__ __forceinline__ void merge_row_stats(const float2* rowst, int roi_h, int roi_w, float inv_h,
+                                                float inv_n, float2* st) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (w >= 4) return;
   const bool h0 = lane < roi_h, h1 = lane + 32 < roi_h;
   const float2 r0 = h0 ? rowst[lane * 4 + w] : make_float2(0.f, 0.f);
   const float2 r1 = h1 ? rowst[(lane + 32) * 4 + w] : make_float2(0.f, 0.f);
-  const float mean = warp_sum(r0.x + r1.x) / (float)roi_h;
+  const float mean = warp_sum(r0.x + r1.x) * inv_h;
   const float d0 = h0 ? r0.x - mean : 0.f, d1 = h1 ? r1.x - mean : 0.f;
   float dev = fmaf(d0, d0, d1 * d1), m2 = r0.y + r1.y;
 #pragma unroll
@@ -299,7 +301,7 @@ __device__ __forceinline__ void merge_row_stats(const float2* rowst, int roi_h, 
     m2 += __shfl_xor_sync(0xffffffffu, m2, o);
   }
   m2 = fmaf((float)roi_w, dev, m2);
-  if (lane == 0) st[w] = make_float2(mean, 1.0f / sqrtf(m2 / (float)(roi_h * roi_w) + kNormEps));
+  if (lane == 0) st[w] = make_float2(mean, rsqrtf(fmaf(m2, inv_n, kNormEps)));
 }
 
 // Field of step t into X (real part; zero imaginary, zero beyond Fh x Fw).
@@ -381,6 +383,7 @@ __global__ void __launch_bounds__(kThreadsF, 1) fftf_fwd_kernel(FftfArgs a) {
   const int half = tid >> 9;                              // working plane of this thread
   const size_t P = (size_t)g.P, M = (size_t)g.M;
   const int pairs = g.M / 2;
+  const float inv_h = 1.0f / (float)g.roi_h, inv_n = 1.0f / (float)g.P;   // plane statistics
   fft64::init_tw64(stw, tid);
   const fft64::Lane Ln = fft64::lane_of(tid & 511);
   int poff[kPosPerThread];
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(kThreadsF, 1) fftf_fwd_kernel(FftfArgs a) {
       // row, merged over the rows with Chan's formula
       float mu[4] = {0.f, 0.f, 0.f, 0.f}, rs[4] = {1.f, 1.f, 1.f, 1.f};
       if (g.norm) {
-        merge_row_stats(rowst, g.roi_h, g.roi_w, pst);
+        merge_row_stats(rowst, g.roi_h, g.roi_w, inv_h, inv_n, pst);
         __syncthreads();
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
