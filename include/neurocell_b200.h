@@ -117,7 +117,9 @@ size_t nc_plan_bytes(const nc_topo* topo);
  *   in_index[n_in]    flat grid index r*W+c of each input value, -1 to drop it
  *                     (neurocell/propagator.py:103-191 injection order)
  *   out_index[n_out]  flat grid index r*W+c of each output cell, pairwise distinct
- *                     (neurocell/epilogue.py:82-128 gather order); cells outside the ROI
+ *                     (neurocell/epilogue.py:82-128 gather order; a repeated cell, which
+ *                     the reference's gather allows, is refused with NC_ERR_UNSUPPORTED);
+ *                     cells outside the ROI
  *                     (VALID border) are served by nc_vnn_forward_universe (the reference's
  *                     full-grid output path) -- nc_vnn_forward writes NaN for them
  *   io_mask[H*W]      io_state_mask      (neurocell/topology.py:241-253), 0/1 bytes

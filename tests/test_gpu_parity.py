@@ -642,3 +642,23 @@ def test_sharpen_option_of_the_model_facade():
     out = nc.VonNeumannNetwork(topo, sharpen=True).apply(p, xin)
     ref, _ = O.forward(cell, filt, x, geom, O.Config(sharpen=True))
     assert _rel(out.cpu().numpy(), ref) <= TOL
+
+
+# ---- an output cell listed twice ----------------------------------------------------------
+# Legal in the reference (CoordinatePortSpec does not require distinct coordinates,
+# topology.py:38-56; its gather gives such a cell the sum of its ports' gradients).  The
+# library's port kernels assume one port per cell, so the plan refuses the port list with
+# NC_ERR_UNSUPPORTED on every path instead of computing a wrong gradient.
+@pytest.mark.parametrize("backend,grid,ks", [
+    ("b200", 62, (23, 13)),          # fused per-sample FFT kernels (64 x 64 grid)
+    ("nchw_direct", 62, (23, 13)),   # direct kernels
+    ("pallas_sram", 96, (23, 23)),   # FFT regime (128-point lines)
+])
+def test_duplicate_output_cell_is_refused(backend, grid, ks):
+    c = grid // 2
+    inp = O.CoordPort(((c - 5, 12), (c, 12), (c + 5, 12)))
+    out = O.CoordPort(((c, grid - 14), (c + 3, grid - 14), (c, grid - 14), (c - 2, grid - 14)))
+    geom = O.make_geometry(grid, ks, 4, 3, (inp,), out)
+    cell, filt, ins, y = random_problem(geom, 6, 61)
+    with pytest.raises(NotImplementedError, match="duplicate output cell"):
+        run_gpu(geom, O.Config(), cell, filt, ins, y, backend=backend)
